@@ -1,0 +1,118 @@
+/*
+ * mle_engine.h -- C ABI of the B200 host runtime (libmle_engine.so).
+ *
+ * A "session" owns one training graph built with the reference-compatible
+ * C++ API (NodeBackProp / GraphOperations / AdamParameter / Linear, the
+ * replacement of Includes/engine.h) for one of the benchmark configurations,
+ * with its static graph-build allocation, a compute stream, pinned host
+ * staging buffers for the step's inputs and loss, an optional captured CUDA
+ * graph of the whole step, and an optional data-parallel NCCL communicator.
+ *
+ * One step is the reference training loop body
+ *   go.zero_grad(); go.forward(nullptr, true); go.backward();
+ *   [clip]; go.ParameterUpdate(nullptr, false, lr, adamw);
+ * (use_cases/mnist.cu:284-293, Engine/transformer.cu:852-871), with the clip
+ * being the reference's private accumulate/Sqrt_Scale/clipNorm sequence
+ * (Engine/engine.cu:3362-3368) generalised to a max norm.
+ *
+ * All functions return 0 or an mle_status code (include/mle_kernels.h).
+ */
+#ifndef MLE_ENGINE_H
+#define MLE_ENGINE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* mle_session_t;
+
+enum mle_config {
+    MLE_CFG_MLP = 1,      /* Linear-ReLU-Linear + SoftMaxCrossEntropy (use_cases/mnist.cu:252-273) */
+    MLE_CFG_ENCODER = 2,  /* pre-LN transformer encoder stack + projection + SMCE */
+    MLE_CFG_ENCDEC = 3    /* encoder-decoder (self, masked self, cross attention) + SMCE */
+};
+
+typedef struct mle_session_desc {
+    int config;          /* enum mle_config */
+    int batch;           /* local (per-rank) batch */
+    /* MLP */
+    int in_features, hidden, classes;
+    /* transformer */
+    int seq_len, d_model, heads, ffn, layers, vocab;
+    int fused_attention; /* 1: ScaledDotAttention node, 0: the reference's graph ops */
+    int key_grad_mode;   /* MLE_KEYGRAD_REFERENCE or MLE_KEYGRAD_TRUE */
+    /* optimizer */
+    float lr;
+    int adamw;
+    float clip_norm;     /* <= 0 disables the clip */
+    uint64_t seed;
+} mle_session_desc;
+
+/* Builds the graph and allocates everything the step needs. */
+int mle_session_create(const mle_session_desc* desc, mle_session_t* out);
+int mle_session_destroy(mle_session_t s);
+
+/* The session's compute stream (cudaStream_t as void*). */
+void* mle_session_stream(mle_session_t s);
+
+/* Step inputs.  Each input has a pinned host staging buffer (host_ptr) the
+ * caller fills before mle_session_step(..., upload=1, ...), and a device
+ * buffer (dev_ptr).  dtype: 0 = float32, 1 = int32. */
+int mle_session_input_count(mle_session_t s);
+int mle_session_input_info(mle_session_t s, int i, char* name, int name_len, int64_t* numel, int* dtype,
+                           void** host_ptr, void** dev_ptr);
+
+/* One training step on the session stream.  upload != 0 copies every input
+ * host -> device first (cudaMemcpyAsync from pinned memory); if loss_out is
+ * non-NULL the loss is copied device -> pinned host and the call waits for
+ * the stream.  Replays the captured graph when one was captured. */
+int mle_session_step(mle_session_t s, int upload, float* loss_out);
+
+/* Runs one phase of the step: 0 zero_grad, 1 forward (calc_loss),
+ * 2 backward, 3 data-parallel gradient reduction, 4 clip, 5 update. */
+int mle_session_phase(mle_session_t s, int phase);
+
+/* Captures the whole step (with the input upload and loss download) into a
+ * CUDA graph; later mle_session_step calls replay it. */
+int mle_session_capture(mle_session_t s);
+
+int mle_session_sync(mle_session_t s);
+
+/* Parameters in graph order (W1 then B1 per Linear). */
+int mle_session_param_count(mle_session_t s);
+int mle_session_param_info(mle_session_t s, int i, char* name, int name_len, int64_t* numel);
+/* which: 0 weights, 1 gradient, 2 first moment, 3 second moment. */
+int mle_session_param_read(mle_session_t s, int i, int which, float* host);
+int mle_session_param_write(mle_session_t s, int i, int which, const float* host);
+/* Step counter t of parameter i, read from its device mirror. */
+int mle_session_param_step(mle_session_t s, int i, int* t);
+
+/* Embedding tables (transformer configs; gather only, not trained). */
+int mle_session_embedding_count(mle_session_t s);
+int mle_session_embedding_write(mle_session_t s, int i, const float* host, int64_t numel);
+
+/* Total device bytes held by the session's arenas. */
+int mle_session_device_bytes(mle_session_t s, int64_t* bytes);
+
+/* Number of graph nodes and launches of the last non-captured step. */
+int mle_session_node_count(mle_session_t s);
+
+/* ---- data parallelism (one process per GPU, NCCL over NVLink) ---- */
+
+/* Writes a fresh NCCL unique id (128 bytes) for rank 0 to distribute. */
+int mle_dp_unique_id(uint8_t* out128);
+
+/* Joins a communicator of `world` ranks.  After backward, the parameter
+ * gradients are summed over ranks in buckets of `bucket_mb` MiB on a second
+ * stream, each bucket as soon as the backward pass has produced every
+ * gradient in it, and the update averages them (scale 1/world) before the
+ * clip norm and AdamW. */
+int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int world, int bucket_mb);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLE_ENGINE_H */

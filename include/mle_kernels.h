@@ -1,0 +1,372 @@
+/*
+ * mle_kernels.h -- C ABI of the B200 (sm_100a) kernels behind ML_Engine's
+ * training hot path.
+ *
+ * Every entry point replaces one group of `<<<>>>` launches that the
+ * reference issues from the backward lambdas in Engine/engine.cu, from the
+ * AdamParameter methods, or from the forward lambdas that produce the
+ * tensors those backward lambdas read.  Each declaration names the
+ * reference code it stands in for (path:line inside the ML_Engine tree).
+ *
+ * Conventions shared by all entry points
+ *   - pointers are device pointers to fp32 unless stated otherwise;
+ *   - sizes are int64_t element counts; shapes follow the reference's
+ *     [dim0, dim1, dim2, dim3] row-major layout;
+ *   - `stream` is a cudaStream_t passed as void*; NULL is the legacy default
+ *     stream, which keeps the reference's implicit ordering;
+ *   - the return value is 0 (MLE_OK) or an mle_status code; nothing here
+ *     allocates device memory, synchronises the device, or exits the
+ *     process -- the C++ shim maps a non-zero status onto the reference's
+ *     print-and-exit behaviour;
+ *   - "accumulate" outputs are `+=` exactly where the reference's kernel
+ *     uses `+=`/atomicAdd, and "assign" outputs are `=` where it assigns.
+ */
+#ifndef MLE_KERNELS_H
+#define MLE_KERNELS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* mle_stream_t;
+
+enum mle_status {
+    MLE_OK = 0,
+    MLE_ERR_ARG = 1,          /* invalid size, pointer or flag */
+    MLE_ERR_CUDA = 2,         /* a CUDA runtime call or launch failed */
+    MLE_ERR_UNSUPPORTED = 3,  /* shape/flag combination not implemented */
+    MLE_ERR_TIMEOUT = 4       /* a bounded device-side wait gave up */
+};
+
+enum mle_activation {
+    MLE_ACT_RELU = 0,
+    MLE_ACT_LEAKY_RELU = 1,
+    MLE_ACT_SILU = 2,
+    MLE_ACT_TANH = 3,
+    MLE_ACT_GELU = 4,
+    MLE_ACT_SIGMOID = 5
+};
+
+/* GEMM variants, named after the reference kernels they replace
+ * (Engine/kernels.cu:387-539):
+ *   MLE_GEMM_AB   bcmm     C[m,p] (op) A[m,n]   * B[n,p]
+ *   MLE_GEMM_ABT  bcmmABT  C[m,p] (op) A[m,n]   * B[p,n]^T
+ *   MLE_GEMM_ATB  bcmmATB  C[m,p] (op) A[n,m]^T * B[n,p]
+ *   MLE_GEMM_ATBT bcmmT    C[m,p] (op) A[n,m]^T * B[p,n]^T               */
+enum mle_gemm_variant {
+    MLE_GEMM_AB = 0,
+    MLE_GEMM_ABT = 1,
+    MLE_GEMM_ATB = 2,
+    MLE_GEMM_ATBT = 3
+};
+
+/* ------------------------------------------------------------------ */
+/* library / status                                                    */
+/* ------------------------------------------------------------------ */
+
+/* Human readable name of an mle_status value. */
+const char* mle_status_string(int status);
+
+/* Last CUDA error code recorded by a failing entry point (0 if none). */
+int mle_last_cuda_error(void);
+
+/* Reads and clears the device watchdog word that bounded waits inside the
+ * tensor-core kernels set when they give up (0 = no timeout).  Synchronises
+ * `stream`; call it outside the timed region. */
+int mle_watchdog_read(int* out_flag, mle_stream_t stream);
+
+/* Version of this ABI (incremented on incompatible change). */
+int mle_abi_version(void);
+
+/* ------------------------------------------------------------------ */
+/* elementwise glue (graph-op forward/backward lambdas)                */
+/* ------------------------------------------------------------------ */
+
+/* x[i] = value.  Replaces fillKernel (Includes/kernels.h:13-19) as launched
+ * by Zerograd (Engine/engine.cu:312-326). */
+int mle_fill(float* x, float value, int64_t n, mle_stream_t stream);
+
+/* y[i] = x[i].  Replaces Write (Engine/kernels.cu:1670-1675). */
+int mle_copy(const float* x, float* y, int64_t n, mle_stream_t stream);
+
+/* y[i] = (float)((double)y[i] + scale * x[i]) (the sum in double).  Replaces
+ * Accumulate (Engine/kernels.cu:1702-1708), the backward of Copy, Scale,
+ * MatrixPositionalEncoding, Bias_Add/Broadcast_Channel input A
+ * (Engine/engine.cu:696,2543,1287,1388,1433). */
+int mle_accumulate(const float* x, float* y, int64_t n, double scale, mle_stream_t stream);
+
+/* ga += g; gb += g in one pass.  Replaces the two Accumulate launches of
+ * GraphOperations::Add backward (Engine/engine.cu:1659-1667). */
+int mle_add_bwd(const float* g, float* ga, float* gb, int64_t n, mle_stream_t stream);
+
+/* y[i] = scale * x[i].  Replaces Scale_Write (Engine/kernels.cu:1677-1682),
+ * the forward of Scale (Engine/engine.cu:2533-2538). */
+int mle_scale_write(const float* x, float* y, int64_t n, float scale, mle_stream_t stream);
+
+/* z[i] = x[i] + scale * y[i].  Replaces ScaleAdd (Engine/kernels.cu:1718-1724),
+ * the forward of Add (Engine/engine.cu:1650-1655). */
+int mle_scale_add(const float* x, const float* y, float* z, float scale, int64_t n, mle_stream_t stream);
+
+/* Activation forward y = f(x).  Replaces ReLU/LeakyReLU/SiLU/TaNH/GeLU/Sigmoid
+ * (Engine/kernels.cu:1214-1319). */
+int mle_act_fwd(int kind, const float* x, float* y, int64_t n, mle_stream_t stream);
+
+/* Activation backward gx[i] += gy[i] * f'(x[i]) with x the activation INPUT,
+ * using the reference's derivative formulas (deriv_* in
+ * Engine/kernels.cu:1223-1328, lambdas Engine/engine.cu:2666-2842).
+ * If bias_grad is non-NULL the same pass also adds the column sums of the
+ * updated gx (a [rows, cols] matrix, rows*cols == n) into bias_grad[cols]; this fuses the BCompress launch of the producing Linear
+ * (Engine/kernels.cu:1562-1584) when the activation is that Linear's only
+ * consumer. */
+int mle_act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n,
+                float* bias_grad, int64_t rows, int64_t cols, mle_stream_t stream);
+
+/* y[r, c] = x[r, c] + bias[c].  Replaces BCumAdd (Engine/kernels.cu:1586-1592)
+ * as launched by Linear/Bias_Add forward.  y may alias x. */
+int mle_bias_add_fwd(const float* x, const float* bias, float* y, int64_t rows, int64_t cols,
+                     mle_stream_t stream);
+
+/* bias_grad[c] += scale * sum_r g[r, c].  Replaces BCompress
+ * (Engine/kernels.cu:1562-1584) in Linear and Bias_Add backward. */
+int mle_bias_grad(const float* g, float* bias_grad, int64_t rows, int64_t cols, float scale,
+                  mle_stream_t stream);
+
+/* Per-channel broadcast of a [1,1,1,C] vector over [B,C,H,W]:
+ * y = x + b[c].  Replaces broadcast_add (Engine/kernels.cu:1661-1668). */
+int mle_channel_bias_fwd(const float* x, const float* b, float* y, int batch, int channels,
+                         int64_t spatial, mle_stream_t stream);
+
+/* gb[c] += sum_{n,s} g[n,c,s]; if gx != NULL also gx += g.  Replaces
+ * Channel_Squeeze1D (Engine/kernels.cu:1734-1761) plus the Accumulate of
+ * Broadcast_Channel backward (Engine/engine.cu:1430-1438) and the dB part
+ * of Convolute2D/2DT backward (Engine/engine.cu:3768,3868). */
+int mle_channel_bias_bwd(const float* g, float* gx, float* gb, int batch, int channels,
+                         int64_t spatial, mle_stream_t stream);
+
+/* Sinusoidal matrix positional encoding, y = x + PE (sin even / cos odd
+ * columns).  Replaces MatPEncoding (Engine/kernels.cu:166-185). */
+int mle_matpe_fwd(const float* x, float* y, int batch, int rows, int cols, int start_idx,
+                  mle_stream_t stream);
+
+/* Timestep encoding (cos first half, sin second half).  Replaces PEncoding
+ * (Engine/kernels.cu:147-164). */
+int mle_timestep_pe(float* y, int t, int dim, mle_stream_t stream);
+
+/* Head split/merge between [B,1,S,H*hd] and [B,H,S,hd].  flag follows
+ * HeadifyColChannel (Engine/kernels.cu:1371-1406):
+ *   0: out[headified] = in[flat]      (Headify forward)
+ *   1: out[flat]     += in[headified] (Headify backward)
+ *   2: out[flat]      = in[headified] (DeHeadify forward)
+ *   3: out[headified]+= in[flat]      (DeHeadify backward)               */
+int mle_headify(const float* in, float* out, int batch, int heads, int seq, int head_dim,
+                int flag, mle_stream_t stream);
+
+/* Channel concat / split: Channel_Concat and Channel_Split
+ * (Engine/kernels.cu:1408-1432).  split accumulates (+=). */
+int mle_channel_concat(const float* a, const float* b, float* c, int batch, int c1, int c2,
+                       int64_t spatial, mle_stream_t stream);
+int mle_channel_split(float* ga, float* gb, const float* gc, int batch, int c1, int c2,
+                      int64_t spatial, mle_stream_t stream);
+
+/* Centre crop (a,b)->(c,d) and its adjoint (CopynCrop / PaddingCrop,
+ * Engine/kernels.cu:1330-1369).  pad_crop accumulates. */
+int mle_center_crop(const float* x, float* y, int batch, int depth, int a, int b, int c, int d,
+                    mle_stream_t stream);
+int mle_pad_crop(const float* x, float* y, int batch, int depth, int a, int b, int c, int d,
+                 mle_stream_t stream);
+
+/* Embedding gather out[i, :] = table[keys[i], :] (GatherEmbeddings,
+ * Engine/kernels.cu:2279-2296); keys < 0 leave the row untouched.
+ * one_hot writes out[i, keys[i]] = 1 into a zeroed [n, vocab] matrix
+ * (OneHotEmbeddings, Engine/kernels.cu:1551-1560). */
+int mle_embedding_gather(const int32_t* keys, const float* table, float* out, int64_t n_keys,
+                         int dim, mle_stream_t stream);
+int mle_one_hot(const int32_t* keys, float* out, int64_t n_keys, int vocab, mle_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* normalisation                                                        */
+/* ------------------------------------------------------------------ */
+
+/* LayerNorm over each dim0 index (N = channels*row*col elements), gamma=1,
+ * beta=0: writes y, mean[batch] and sqdev[batch] = sum (x-mean)^2.
+ * Replaces LayerMean+LayerStd+LNorm (Engine/kernels.cu:541-572,670-699,
+ * 794-804) as launched by LayerNorm forward (Engine/engine.cu:3099-3113). */
+int mle_layernorm_fwd(const float* x, float* y, float* mean, float* sqdev, int batch,
+                      int channels, int row, int col, float eps, mle_stream_t stream);
+
+/* LayerNorm backward gx += rstd*(gy - sum(gy)/N - y*sum(gy*y)/N), with the
+ * reference's index map (only the first batch*row*col elements, correct for
+ * channels == 1).  Replaces Scale_Write+mulKernel+2xLayerMean+LayerBackward
+ * (Engine/engine.cu:3116-3130, Engine/kernels.cu:849-862). */
+int mle_layernorm_bwd(const float* y, const float* gy, const float* sqdev, float* gx, int batch,
+                      int channels, int row, int col, float eps, mle_stream_t stream);
+
+/* GroupNorm forward/backward over (sample, group) blocks of
+ * (channels/groups)*row*col elements.  Replaces GroupMean/GroupStd/GNorm and
+ * GroupBackward (Engine/kernels.cu:607-639,732-763,818-834,877-896) as used by
+ * GroupNorm (Engine/engine.cu:3232-3270). */
+int mle_groupnorm_fwd(const float* x, float* y, float* mean, float* sqdev, int batch,
+                      int channels, int groups, int row, int col, float eps, mle_stream_t stream);
+int mle_groupnorm_bwd(const float* y, const float* gy, const float* sqdev, float* gx, int batch,
+                      int channels, int groups, int row, int col, float eps, mle_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* softmax and losses                                                   */
+/* ------------------------------------------------------------------ */
+
+/* Softmax over [bc, rows, cols].  axis 0 normalises each row over its
+ * columns, axis 1 normalises each column over its rows (the reference's
+ * "type 1", used by attention).  causal != 0 zeroes entries with col > row
+ * before normalising (SoftMask).  An all-zero line is divided by 1 as in
+ * SumRows/SumCols.  Replaces SoftMax/SoftMask (Engine/kernels.cu:2183-2235). */
+int mle_softmax_fwd(const float* x, float* y, int64_t bc, int rows, int cols, int axis,
+                    int causal, mle_stream_t stream);
+
+/* gx += y * (gy - sum_axis(gy*y)).  Replaces deriv_softmax
+ * (Engine/kernels.cu:2149-2181). */
+int mle_softmax_bwd(const float* y, const float* gy, float* gx, int64_t bc, int rows, int cols,
+                    int axis, mle_stream_t stream);
+
+/* Softmax cross-entropy forward over rows of `cols` logits with a dense
+ * target: probs = softmax_row(logits); *loss = sum(-t*log(p+1e-27)) / (rows*cols)
+ * (assigned).  If grad != NULL the same pass also writes the `last=true`
+ * backward grad[r,c] = (p - t) / batch_div (assign), which is what
+ * SoftMaxCrossEntropy backward computes (Engine/engine.cu:2090-2111,
+ * Engine/kernels.cu:1818-1826).  probs may be NULL when not needed. */
+int mle_softmax_ce_fwd(const float* logits, const float* target, float* probs, float* loss,
+                       float* grad, float batch_div, int64_t rows, int cols, mle_stream_t stream);
+
+/* SoftMaxCrossEntropy backward from stored probabilities:
+ * grad = (probs - target) [* upstream[0]] / batch_div (assign). */
+int mle_softmax_ce_bwd(const float* probs, const float* target, const float* upstream,
+                       float* grad, float batch_div, int64_t n, mle_stream_t stream);
+
+/* Mean squared error: *loss = sum (t-x)^2 / n (assigned);
+ * backward gx += 2 (x-t)/n [* upstream[0]].  Replaces scalar_mse_kernel and
+ * deriv_mse_kernel (Engine/kernels.cu:1808-1848). */
+int mle_mse_fwd(const float* x, const float* target, float* loss, int64_t n, mle_stream_t stream);
+int mle_mse_bwd(const float* x, const float* target, const float* upstream, float* gx, int64_t n,
+                mle_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* tensor-core GEMM (tcgen05 kind::tf32, TMEM accumulator, TMA operands) */
+/* ------------------------------------------------------------------ */
+
+/* Batched GEMM with the reference's broadcast flags.  Same argument meaning
+ * as bcmm/bcmmABT/bcmmATB/bcmmT (Engine/kernels.cu:387-539): `backward`!=0
+ * adds scale*product into C (the reference's atomicAdd), 0 assigns it.
+ * Flags A_case/B_case/C_case in {0,1,2,3}: bit 0 = has batch, bit 1 = has
+ * channel.  Whenever several (batch, channel) products map onto one C
+ * matrix they are summed, exactly as the reference's atomics do. */
+int mle_bcmm(int variant, const float* A, const float* B, float* C, int batch, int channels,
+             int m, int n, int p, int backward, int A_case, int B_case, int C_case, float scale,
+             mle_stream_t stream);
+
+/* Plain strided GEMM  C = alpha * op(A) * op(B) + beta * C  (+ bias[col]),
+ * row-major, op(A) is [M,K], op(B) is [K,N].  beta must be 0 or 1.
+ * trans_a: A stored [K,M]; trans_b: B stored [N,K].  lda/ldb/ldc are row
+ * strides in elements; batch strides may be 0 (broadcast). */
+int mle_gemm(const float* A, const float* B, float* C, const float* bias, int batch, int64_t M,
+             int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a,
+             int64_t stride_b, int64_t stride_c, int trans_a, int trans_b, float alpha, float beta,
+             mle_stream_t stream);
+
+/* Linear layer forward Y = X*W (+ bias), X [rows, in], W [in, out] ([1,1,in,out]
+ * AdamParameter), Y [rows, out].  Replaces bcmm(...,0,3,0,3) + BCumAdd in
+ * Linear::forward (Engine/engine.cu:3536-3548), with the batch*channel*m
+ * rows flattened into one GEMM. */
+int mle_linear_fwd(const float* X, const float* W, const float* bias, float* Y, int64_t rows,
+                   int in_features, int out_features, mle_stream_t stream);
+
+/* Linear layer backward: dX += dY*W^T (if dX != NULL), dW += X^T*dY as one
+ * GEMM with K = rows, dB += column sums of dY (if dB != NULL).  Replaces
+ * bcmmABT + bcmmATB + BCompress of the Linear backward lambda
+ * (Engine/engine.cu:3550-3563) without its two device synchronisations. */
+int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, float* dW,
+                   float* dB, int64_t rows, int in_features, int out_features,
+                   mle_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* fused attention backward                                             */
+/* ------------------------------------------------------------------ */
+
+/* Key-gradient semantics of mle_attention_bwd.
+ *   MLE_KEYGRAD_REFERENCE: what the reference's BMMABT backward computes,
+ *     bcmmT(Q, dScores, K.grad, n, m, p) (Engine/engine.cu:2307): dScores'
+ *     memory is read as a [Sk, Sq] matrix M and K.grad's memory receives
+ *     (M Q)^T laid out [hd, Sk].  This equals dScores^T Q only when
+ *     Sq == Sk == hd; it is the drop-in default because it is the
+ *     reference's result.
+ *   MLE_KEYGRAD_TRUE: dK += scale * dS^T Q, the mathematical gradient. */
+enum mle_keygrad_mode { MLE_KEYGRAD_REFERENCE = 0, MLE_KEYGRAD_TRUE = 1 };
+
+/* Backward of the attention sub-graph built by MultiHeadAttention::forward /
+ * cross_forward (Engine/transformer.cu:647-675):
+ *   S = Q K^T, Ssc = scale*S, P = softmax_axis(Ssc) [masked], O = P V.
+ * Inputs are [B,H,Sq,hd] (Q, dO), [B,H,Sk,hd] (K, V) and P [B,H,Sq,Sk].
+ * Accumulates dQ, dK, dV (+=); dP_out receives (+=) the softmax node's
+ * gradient dO V^T and dS_out (+=) the Scale node's gradient (the softmax
+ * backward), both [B,H,Sq,Sk] as the reference keeps them in node->grad.
+ * softmax_axis 1 is the reference's column-wise softmax.  Replaces
+ * bcmmABT/bcmmATB (BMM bwd), deriv_softmax, Accumulate (Scale bwd) and
+ * bcmm/bcmmT (BMMABT bwd) (Engine/engine.cu:2246-2253,2302-2309,2450-2455,
+ * 2488-2493,2540-2546). */
+int mle_attention_bwd(const float* Q, const float* K, const float* V, const float* P,
+                      const float* dO, float* dQ, float* dK, float* dV, float* dP_out,
+                      float* dS_out, int batch, int heads, int seq_q, int seq_k, int head_dim,
+                      float scale, int causal, int softmax_axis, int key_grad_mode,
+                      mle_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* gradient-norm clip + Adam/AdamW                                      */
+/* ------------------------------------------------------------------ */
+
+/* One parameter tensor as seen by the optimizer.  t points at the tensor's
+ * step counter in DEVICE memory (AdamParameter::t, Includes/engine.h:64);
+ * the update reads it and the same launch increments it, so a captured
+ * CUDA graph replays the reference's per-tensor t++ (Engine/engine.cu:291). */
+typedef struct mle_param_view {
+    float* w;
+    float* g;
+    float* m;
+    float* v;
+    int64_t n;
+    int32_t* t;
+    float b1, b2, eps, weight_decay;
+} mle_param_view;
+
+/* *norm_ws += scale^2 * sum over all tensors of g^2, accumulated in double.
+ * Replaces one SumSquared launch per tensor (AdamParameter::accumulate_grad,
+ * Engine/engine.cu:294-300; Engine/kernels.cu:1486-1506).  `params` is a
+ * HOST array; its contents travel as kernel parameters (no allocation). */
+int mle_grad_sumsq(const mle_param_view* params, int n_tensors, double* norm_ws, double scale,
+                   mle_stream_t stream);
+
+/* *norm_ws = max(sqrt(*norm_ws), max_norm) (a NaN is left unchanged).
+ * Replaces Sqrt_Scale<<<1,1>>>(ws, 1.0, 0) (Engine/kernels.cu:1763-1773)
+ * for max_norm = 1, as called by GraphOperations::accumulate
+ * (Engine/engine.cu:3364-3368). */
+int mle_clip_finalize(double* norm_ws, double max_norm, mle_stream_t stream);
+
+/* g /= (float)(*norm_ws) in place for every tensor.  Replaces the per-tensor
+ * SP launches of GraphOperations::clipNorm (Engine/engine.cu:3362,302). */
+int mle_clip_apply(const mle_param_view* params, int n_tensors, const double* norm_ws,
+                   mle_stream_t stream);
+
+/* Fused multi-tensor update.  For every tensor: g' = g * pre_scale, then if
+ * clip_ws != NULL g' = g' / (float)(*clip_ws) (written back to g when
+ * write_back_grad != 0), then AdamW (adamw != 0) or Adam with the
+ * reference's arithmetic (AdamWUpdate/AdamUpdate, Engine/kernels.cu:1508-1534),
+ * then *t += 1.  One launch replaces the per-tensor AdamParameter::update
+ * loop (Engine/engine.cu:283-292, 3370-3384). */
+int mle_adam_update(const mle_param_view* params, int n_tensors, const double* clip_ws,
+                    float pre_scale, float lr, int adamw, int write_back_grad,
+                    mle_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLE_KERNELS_H */

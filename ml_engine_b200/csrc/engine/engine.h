@@ -1,0 +1,249 @@
+// engine.h -- B200-native replacement for ML_Engine's Includes/engine.h
+// (training hot path).
+//
+// Declarations keep the reference's names, argument lists, default
+// arguments and public fields (Includes/engine.h:33-213) so programs written
+// against the reference compile and link unchanged for the ops on the path.
+// What differs is underneath:
+//   * every launch goes through the C ABI of include/mle_kernels.h on one
+//     compute stream (mle::stream(); the legacy default stream unless a
+//     session selects its own), with no device synchronisation in forward
+//     or backward;
+//   * node and parameter buffers are carved from static graph-build arenas
+//     (still allocated once, when the graph is built), so zero_grad clears
+//     coalesced ranges and the optimizer sees contiguous parameter storage;
+//   * GraphOperations::ParameterUpdate, accumulate and clipNorm gather the
+//     AdamParameters their lambdas touch and issue one fused multi-tensor
+//     launch instead of one launch per tensor;
+//   * AdamParameter::t is mirrored in device memory so a captured CUDA graph
+//     replays the per-tensor step counter.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <fstream>
+#include <functional>
+#include <iostream>
+#include <memory>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "mle_kernels.h"
+
+using str = std::string;
+
+// Includes/debugging_utils.h:10-14 and Includes/kernels.h:7-8
+static constexpr float XAVIER = 6.0f;
+static constexpr bool ADAMW = true;
+static constexpr float NORM = 1.0f;
+static constexpr float LEARNING_RATE = 1e-4f;
+static constexpr bool SHOULDNORM = false;
+static constexpr int BLOCK_SIZE = 32;
+static constexpr int THREADSPERBLOCK = 512;
+
+struct NodeBackProp;
+struct AdamParameter;
+using graph = std::shared_ptr<NodeBackProp>;
+using graph_tree = std::vector<graph>;
+using graphFn = std::function<graph(graph)>;
+
+namespace mle {
+
+// Compute stream used by every op (default: legacy stream 0).
+cudaStream_t stream();
+void set_stream(cudaStream_t s);
+
+// Maps a non-zero mle_status onto the reference's behaviour: print the
+// reason and exit(1) (Engine/debug.cu:15-25).
+void check(int status, const str& what);
+
+// Static graph-build arenas.  Memory is handed out in 256-byte aligned
+// slices of large cudaMalloc'ed chunks and only returned by release_all().
+enum Arena { ARENA_ACT = 0, ARENA_GRAD = 1, ARENA_PARAM = 2, ARENA_PARAM_GRAD = 3, ARENA_WS = 4, ARENA_COUNT = 5 };
+float* arena_alloc(Arena a, int64_t n_floats, const str& name);
+void* arena_alloc_bytes(Arena a, int64_t bytes, const str& name);
+double arena_gib(Arena a);
+void release_all_arenas();
+
+// Zeroing of many small ranges, coalesced into as few memsets as possible
+// while a ZeroBatch is alive (GraphOperations::zero_grad keeps one open).
+void zero_range(float* p, int64_t n);
+struct ZeroBatch {
+    ZeroBatch();
+    ~ZeroBatch();
+};
+
+// Every AdamParameter ever constructed, in construction order.
+std::vector<AdamParameter*>& all_parameters();
+
+// Seed for parameter initialisation (Standard_Weights draws from
+// std::random_device in the reference; a fixed seed makes runs repeatable).
+void set_seed(uint64_t seed);
+
+// Global gradient-norm workspace (one double) used by clip_grad_norm.
+double* clip_workspace();
+
+}  // namespace mle
+
+void CheckError(const str& reason);
+
+struct NodeBackProp {
+    str op_name;
+    graph_tree inputs;
+    float* output;
+    float* grad;
+    int dim[4];
+    long long total;
+    bool forward_called = false;
+    std::function<void()> forward;
+    std::function<void()> backward;
+    std::function<void()> free;
+    std::function<void()> zero_grad;
+    std::function<void()> serious_free;
+    std::function<void(const float lr, const bool adamw)> updateParams;
+    std::function<void(const double*)> clipnorm;
+    std::function<void(double*)> accumulate;
+    std::function<void(const bool full)> printparams;
+    virtual void update(const float lr = LEARNING_RATE, const bool W = ADAMW) {}
+    NodeBackProp(str name, int batch, int d1, int d2, int d3, int allocation);
+    virtual ~NodeBackProp() = default;
+    void clear();
+    void reshape(std::vector<int> new_dims);
+    void reshape(int arr[], const int size = 4);
+};
+
+float ReadValueAt(const graph& X, const int& idx, const bool flag = false);
+void WriteValueAt(const graph& X, const float value, const int& idx, const bool flag = false);
+
+struct AdamParameter : public NodeBackProp {
+    float *m, *v;
+    int t;
+    float b1, b2, epsilon;
+    int batch_size;
+    float group_norm;
+    float weight_decay;
+    int32_t* t_dev;  // device mirror of t, read and advanced by the fused update
+
+    AdamParameter(str n, int out, int in, int row, int col, double norm = NORM);
+    void save(std::ofstream& f) const;
+    void load(std::ifstream& f);
+    void update(const float lr = LEARNING_RATE, const bool W = ADAMW) override;
+    void accumulate_grad(double* global_scale);
+    void gradnorm(const double* global_scale);
+    void operator=(const AdamParameter& other);
+    // copies the device step counter back into t
+    void sync_step();
+};
+
+void Dimension(graph X);
+void Dimension(AdamParameter X);
+void Zerograd(AdamParameter X);
+void Zerograd(graph X);
+graph_tree topological_sort(const graph& root);
+
+class GraphOperations {
+   private:
+    static bool calculate_loss;
+    void clipNorm(double* global_scale);
+    void accumulate(double* global_scale);
+
+   public:
+    graph_tree nodes;
+
+    static double GB;
+    static float loss;
+
+    void ParameterUpdate(const graph& X = nullptr, const bool show = false, const float lr = LEARNING_RATE,
+                         const bool adamw = ADAMW);
+    void forward(const graph& X = nullptr, const bool calc_loss = false, const bool show = false,
+                 const bool time = false, const bool check_nan = false);
+    void backward(const graph& X = nullptr, const bool show = false, const bool time = false,
+                  const bool check_nan = false);
+    void zero_grad(const graph& X = nullptr, const bool show = false);
+    void printParams(const graph& X = nullptr, const bool show = false);
+    void printNodes(const graph& X = nullptr, const int show = 0);
+    void clear_graph(const graph& X = nullptr, const bool show = false);
+    void clean_clear_graph(const graph& X = nullptr, const bool show = false);
+
+    // Public gradient-norm clip (the reference keeps accumulate/clipNorm
+    // private and never calls them, Includes/engine.h:112-113).  Computes
+    // s = max(||g||_2 / max_norm, 1) over every parameter of `nodes`; the
+    // division g /= s is applied by the next ParameterUpdate inside the
+    // fused update (and written back to the gradients), or immediately by
+    // apply_clip().
+    void clip_grad_norm(const float max_norm = NORM);
+    void apply_clip();
+    // Multiplies every gradient by `scale` inside the next update and
+    // before the norm (data-parallel averaging).
+    void set_grad_prescale(float scale) { grad_prescale_ = scale; }
+
+    static graph Copy(const graph& X);
+    static graph identity(const graph& X);
+    static graph like(const graph& X, const str name = "");
+    static graph MatrixPositionalEncoding(const graph& X, const int start_idx = 0);
+    static graph PositionalEncoding(const int& t, const int d_model);
+    static graph HeadifytoChannel(const graph& X, const int new_channels);
+    static graph DeHeadify(const graph& X);
+    static graph Bias_Add(const graph& A, const graph& B);
+    static graph Broadcast_Channel(const graph& A, const graph& B);
+    static graph Scale(const graph& input, const float scale, const bool last = false);
+    static graph Add(const graph& A, const graph& B, const bool last = false);
+
+    static graph MeanSquaredError(const graph& prediction, const graph& target, const bool last);
+    static graph SoftMaxCrossEntropy(const graph& prediction, const graph& target, const bool last);
+
+    static graph BMM(const graph& A, const graph& B);     // m x n, n x p = m x p
+    static graph BMMABT(const graph& A, const graph& B);  // m x n, p x n = m x p
+    static graph BMMATB(const graph& A, const graph& B);  // n x m, n x p = m x p
+    static graph BMMT(const graph& A, const graph& B);    // n x m, p x n = m x p
+
+    static graph SOFTMAX(const graph& X, const int type = 0);
+    static graph SOFTMASK(const graph& X, const int type = 0);
+
+    static graph RELU(const graph& input);
+    static graph SILU(const graph& input);
+    static graph TANH(const graph& input);
+    static graph GELU(const graph& input);
+    static graph SIGMOID(const graph& input);
+    static graph LeakyRELU(const graph& input);
+
+    static graph CopyCrop(const graph& input1, const graph& input2);
+
+    static graph LayerNorm(const graph& X);
+    static graph GroupNorm(const graph& X, const int group = 8);
+
+    // Extension: the whole attention sub-graph of MultiHeadAttention
+    // (Headify x3, BMMABT, Scale, SOFTMAX/SOFTMASK type `axis`, BMM,
+    // DeHeadify; Engine/transformer.cu:647-675) as one node over the flat
+    // [B,1,S,H*hd] projections, forward on the tensor cores and backward
+    // through mle_attention_bwd.  key_grad_mode selects the reference's
+    // BMMABT key gradient (default) or the mathematical one.
+    static graph ScaledDotAttention(const graph& Q, const graph& K, const graph& V, const int heads, const float scale,
+                                    const bool mask, const int axis = 1,
+                                    const int key_grad_mode = MLE_KEYGRAD_REFERENCE);
+
+   private:
+    float grad_prescale_ = 1.0f;
+    bool clip_pending_ = false;
+    void collect_params(std::vector<AdamParameter*>& out);
+};
+
+inline graph operator+(const graph& A, const graph& B) { return GraphOperations::Add(A, B); }
+
+class Linear {
+   private:
+    int in, out;
+    const bool bias;
+
+   public:
+    AdamParameter W1;
+    AdamParameter B1;
+    str op_name = "Linear Layer";
+    Linear(const int input, const int output, const str name = "", const bool bias = true);
+    graph forward(const graph& X);
+    void save(std::ofstream& f) const;
+    void load(std::ifstream& f);
+    void operator=(const Linear& other);
+};

@@ -1,0 +1,59 @@
+// Internal plumbing shared by the runtime translation units.
+#pragma once
+
+#include <vector>
+
+#include "engine.h"
+
+namespace mle {
+
+void* st();                                    // compute stream as mle_stream_t
+void check_cuda(cudaError_t e, const str& what);
+
+// Parameters touched by per-node lambdas while one fused launch is built.
+struct ParamUpdate {
+    AdamParameter* p;
+    float lr;
+    bool adamw;
+};
+struct ParamCollector {
+    std::vector<ParamUpdate> update;
+    std::vector<AdamParameter*> sumsq;
+    std::vector<AdamParameter*> clip;
+};
+extern ParamCollector* g_collector;
+
+// SoftMaxCrossEntropy keeps its probabilities for a later forward without
+// calc_loss (the reference's softmax buffer); a session that always
+// computes the loss switches this off to save one tensor write per step.
+extern bool g_keep_softmax;
+// Loss nodes copy their value into GraphOperations::loss (a device sync)
+// when last, as the reference does; sessions read the loss themselves.
+extern bool g_loss_readback;
+void set_keep_softmax(bool keep);
+
+// Op tags used by the fusion pass.
+enum OpKind {
+    OP_GENERIC = 0,
+    OP_LINEAR = 1,
+    OP_ACTIVATION = 2,
+    OP_SMCE = 3,
+};
+
+// Per-node fusion state decided by prepare_fusions() before a backward pass.
+struct NodeExt {
+    int kind = OP_GENERIC;
+    float* linear_bias_grad = nullptr;   // Linear with bias: B1.grad
+    bool bias_grad_fused = false;        // Linear: the consumer adds the bias grad
+    float* fused_bias_target = nullptr;  // activation: bias grad to accumulate
+    long long fused_rows = 0, fused_cols = 0;
+};
+NodeExt& ext(const NodeBackProp* n);
+void forget_ext(const NodeBackProp* n);
+
+// Decides the Linear -> activation bias-gradient fusion for a node list:
+// an activation whose input is a biased Linear output consumed by nothing
+// else adds that Linear's BCompress (column sums) to its own backward pass.
+void prepare_fusions(const graph_tree& nodes);
+
+}  // namespace mle

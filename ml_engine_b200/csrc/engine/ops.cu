@@ -1,0 +1,660 @@
+// Graph-op builders on the hot path.  Each keeps the reference builder's
+// shape checks, allocation (output + grad at build time), and the exact
+// forward/backward semantics of its lambdas (cited per builder), while the
+// launches go through include/mle_kernels.h on mle::stream().
+//
+// Lambdas capture raw node pointers: a node is owned by whoever holds the
+// graph (its consumers' `inputs`), and capturing the node's own shared_ptr
+// inside its lambdas would keep it alive forever.
+#include <math.h>
+#include <stdio.h>
+
+#include <unordered_map>
+
+#include "engine.h"
+#include "engine_internal.h"
+
+using namespace mle;
+
+namespace mle {
+
+static std::unordered_map<const NodeBackProp*, NodeExt>& ext_map() {
+    static std::unordered_map<const NodeBackProp*, NodeExt> m;
+    return m;
+}
+NodeExt& ext(const NodeBackProp* n) { return ext_map()[n]; }
+void forget_ext(const NodeBackProp* n) { ext_map().erase(n); }
+
+void prepare_fusions(const graph_tree& nodes) {
+    std::unordered_map<const NodeBackProp*, int> consumers;
+    for (auto& n : nodes)
+        for (auto& in : n->inputs) consumers[in.get()]++;
+    for (auto& n : nodes) {
+        NodeExt& e = ext(n.get());
+        if (e.kind == OP_LINEAR) e.bias_grad_fused = false;
+        if (e.kind == OP_ACTIVATION) e.fused_bias_target = nullptr;
+    }
+    for (auto& n : nodes) {
+        NodeExt& e = ext(n.get());
+        if (e.kind != OP_ACTIVATION || n->inputs.size() != 1) continue;
+        const NodeBackProp* L = n->inputs[0].get();
+        NodeExt& le = ext(L);
+        if (le.kind == OP_LINEAR && le.linear_bias_grad && consumers[L] == 1) {
+            e.fused_bias_target = le.linear_bias_grad;
+            e.fused_rows = L->total / L->dim[3];
+            e.fused_cols = L->dim[3];
+            le.bias_grad_fused = true;
+        }
+    }
+}
+
+}  // namespace mle
+
+static void dims_mismatch(const char* what, const graph& A, const graph& B) {
+    std::cout << what << " \n";
+    Dimension(A);
+    Dimension(B);
+    std::exit(1);
+}
+
+// ---------------------------------------------------------------- Copy (:683)
+graph GraphOperations::Copy(const graph& X) {
+    auto node = std::make_shared<NodeBackProp>("Copy of " + X->op_name, X->dim[0], X->dim[1], X->dim[2], X->dim[3], 1);
+    node->inputs = {X};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    node->forward = [nd, xp]() { check(mle_copy(xp->output, nd->output, nd->total, st()), "Copy forward"); };
+    node->backward = [nd, xp]() {
+        check(mle_accumulate(nd->grad, xp->grad, nd->total, 1.0, st()), "Copy backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// ------------------------------------------------------------ identity (:701)
+graph GraphOperations::identity(const graph& X) {
+    auto node = std::make_shared<NodeBackProp>(X->op_name, X->dim[0], X->dim[1], X->dim[2], X->dim[3], 1);
+    node->inputs = {X};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    node->forward = [nd, xp]() { check(mle_copy(xp->output, nd->output, nd->total, st()), "identity forward"); };
+    node->backward = [nd, xp]() { check(mle_copy(nd->grad, xp->grad, nd->total, st()), "identity backward"); };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+graph GraphOperations::like(const graph& X, const str name) {
+    auto node = std::make_shared<NodeBackProp>(name, X->dim[0], X->dim[1], X->dim[2], X->dim[3], 1);
+    node->inputs = {X};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp* nd = node.get();
+    node->forward = []() {};
+    node->backward = []() {};
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// ------------------------------------------ HeadifytoChannel/DeHeadify (:1143-1176)
+graph GraphOperations::HeadifytoChannel(const graph& X, const int heads) {
+    if (X->dim[1] != 1 || X->dim[3] % heads != 0) {
+        std::cerr << "Headify: channel must be 1 and embed must be divisible by heads\n";
+        Dimension(X);
+        std::exit(1);
+    }
+    const int b = X->dim[0], seq = X->dim[2], embed = X->dim[3], hd = embed / heads;
+    auto node = std::make_shared<NodeBackProp>("Headified " + X->op_name, b, heads, seq, hd, 1);
+    node->inputs = {X};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    node->forward = [=]() { check(mle_headify(xp->output, nd->output, b, heads, seq, hd, 0, st()), "Headify fwd"); };
+    node->backward = [=]() { check(mle_headify(nd->grad, xp->grad, b, heads, seq, hd, 1, st()), "Headify bwd"); };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+graph GraphOperations::DeHeadify(const graph& X) {
+    const int b = X->dim[0], heads = X->dim[1], seq = X->dim[2], hd = X->dim[3];
+    auto node = std::make_shared<NodeBackProp>("Deheadified " + X->op_name, b, 1, seq, heads * hd, 1);
+    node->inputs = {X};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    node->forward = [=]() { check(mle_headify(xp->output, nd->output, b, heads, seq, hd, 2, st()), "DeHeadify fwd"); };
+    node->backward = [=]() { check(mle_headify(nd->grad, xp->grad, b, heads, seq, hd, 3, st()), "DeHeadify bwd"); };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// ------------------------------------------------- positional encodings (:1257-1295)
+graph GraphOperations::PositionalEncoding(const int& t, const int d_model) {
+    auto node = std::make_shared<NodeBackProp>("SinoSuodalPosEncoding", 1, 1, 1, d_model, 1);
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp* nd = node.get();
+    const int tt = t;
+    node->forward = [nd, tt, d_model]() { check(mle_timestep_pe(nd->output, tt, d_model, st()), "PositionalEncoding"); };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+graph GraphOperations::MatrixPositionalEncoding(const graph& X, const int start_idx) {
+    if (X->dim[1] != 1) {
+        std::cerr << "MatrixPositionalEncoding expects input with channel dimension of 1\n";
+        Dimension(X);
+        std::exit(1);
+    }
+    const int batch = X->dim[0], rows = X->dim[2], cols = X->dim[3];
+    auto node = std::make_shared<NodeBackProp>("MatrixSinoSuodalPosEncoding", batch, 1, rows, cols, 1);
+    node->inputs = {X};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    node->forward = [=]() { check(mle_matpe_fwd(xp->output, nd->output, batch, rows, cols, start_idx, st()), "MatPE"); };
+    node->backward = [=]() { check(mle_accumulate(nd->grad, xp->grad, nd->total, 1.0, st()), "MatPE backward"); };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// -------------------------------------------------------- Bias_Add (:1355-1395)
+graph GraphOperations::Bias_Add(const graph& A, const graph& B) {
+    if (B->dim[0] != 1 || B->dim[1] != 1 || B->dim[2] != 1 || B->dim[3] != A->dim[3]) {
+        std::cout << "Dimension mismatch in Bias_Add.. Bias must be a 1D vector matching at dim[3] \n";
+        Dimension(A);
+        Dimension(B);
+        std::exit(1);
+    }
+    const long long rows = (long long)A->dim[0] * A->dim[1] * A->dim[2], cols = A->dim[3];
+    auto node = std::make_shared<NodeBackProp>("Bias Add", A->dim[0], A->dim[1], A->dim[2], A->dim[3], 1);
+    node->inputs = {A, B};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *ap = A.get(), *bp = B.get();
+    node->forward = [=]() { check(mle_bias_add_fwd(ap->output, bp->output, nd->output, rows, cols, st()), "Bias_Add"); };
+    node->backward = [=]() {
+        check(mle_accumulate(nd->grad, ap->grad, nd->total, 1.0, st()), "Bias_Add backward A");
+        check(mle_bias_grad(nd->grad, bp->grad, rows, cols, 1.0f, st()), "Bias_Add backward B");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// ----------------------------------------------- Broadcast_Channel (:1398-1444)
+graph GraphOperations::Broadcast_Channel(const graph& A, const graph& B) {
+    if (A->dim[1] != B->dim[3] || B->dim[1] != 1 || B->dim[2] != 1) {
+        std::cout << "Channel mismatch in broadcast channel \n";
+        Dimension(A);
+        Dimension(B);
+        std::exit(1);
+    }
+    const int batch = A->dim[0], channels = A->dim[1], a = A->dim[2], b = A->dim[3];
+    auto node = std::make_shared<NodeBackProp>("Broadcast Channel", batch, channels, a, b, 1);
+    node->inputs = {A, B};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *ap = A.get(), *bp = B.get();
+    node->forward = [=]() {
+        check(mle_channel_bias_fwd(ap->output, bp->output, nd->output, batch, channels, (int64_t)a * b, st()),
+              "Broadcast_Channel");
+    };
+    // The reference reduces with Channel_Squeeze1D<<<b, tpb>>>: one block per
+    // index of dim[3], i.e. the first min(b, channels) channels receive their
+    // sums (Engine/engine.cu:1435).  The same channels are reduced here; the
+    // out-of-range blocks the reference launches when b > channels are not.
+    node->backward = [=]() {
+        check(mle_accumulate(nd->grad, ap->grad, nd->total, 1.0, st()), "Broadcast_Channel backward A");
+        const int reduced = b < channels ? b : channels;
+        if (reduced == channels) {
+            check(mle_channel_bias_bwd(nd->grad, nullptr, bp->grad, batch, channels, (int64_t)a * b, st()),
+                  "Broadcast_Channel backward B");
+        } else {
+            // reduce only channels [0, reduced): view the tensor per sample as
+            // [reduced channels] + rest by running one sample at a time
+            for (int n = 0; n < batch; ++n)
+                check(mle_channel_bias_bwd(nd->grad + (int64_t)n * channels * a * b, nullptr, bp->grad, 1, reduced,
+                                           (int64_t)a * b, st()),
+                      "Broadcast_Channel backward B");
+        }
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// -------------------------------------------------------------- Add (:1627-1670)
+graph GraphOperations::Add(const graph& A, const graph& B, const bool last) {
+    for (int i = 0; i < 4; ++i)
+        if (A->dim[i] != B->dim[i]) dims_mismatch("Dimension mismatch in Add", A, B);
+    auto node = std::make_shared<NodeBackProp>("Add", A->dim[0], A->dim[1], A->dim[2], A->dim[3], 1);
+    node->inputs = {A, B};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *ap = A.get(), *bp = B.get();
+    node->forward = [=]() {
+        check(mle_scale_add(ap->output, bp->output, nd->output, 1.0f, nd->total, st()), "Add forward");
+        if (last && g_loss_readback) {
+            check_cuda(cudaStreamSynchronize(stream()), "Add loss");
+            check_cuda(cudaMemcpy(&loss, nd->output, sizeof(float), cudaMemcpyDeviceToHost), "Add loss");
+        }
+    };
+    node->backward = [=]() {
+        if (last) check(mle_fill(nd->grad, 1.0f, nd->total, st()), "Add backward fill");
+        if (ap == bp) {  // x + x: two accumulations into the same gradient
+            check(mle_accumulate(nd->grad, ap->grad, nd->total, 1.0, st()), "Add backward A");
+            check(mle_accumulate(nd->grad, bp->grad, nd->total, 1.0, st()), "Add backward B");
+        } else {
+            check(mle_add_bwd(nd->grad, ap->grad, bp->grad, nd->total, st()), "Add backward");
+        }
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// ------------------------------------------------------------ Scale (:2521-2549)
+graph GraphOperations::Scale(const graph& input, const float scale, const bool last) {
+    auto node =
+        std::make_shared<NodeBackProp>("Scale", input->dim[0], input->dim[1], input->dim[2], input->dim[3], 1);
+    node->inputs = {input};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *ip = input.get();
+    node->forward = [=]() { check(mle_scale_write(ip->output, nd->output, nd->total, scale, st()), "Scale forward"); };
+    node->backward = [=]() {
+        if (last) check(mle_fill(nd->grad, 1.0f, nd->total, st()), "Scale backward fill");
+        check(mle_accumulate(nd->grad, ip->grad, nd->total, (double)scale, st()), "Scale backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// ------------------------------------------------ MeanSquaredError (:1895-1950)
+graph GraphOperations::MeanSquaredError(const graph& prediction, const graph& target, const bool last) {
+    for (int i = 0; i < 4; ++i)
+        if (prediction->dim[i] != target->dim[i]) dims_mismatch("Dimension mismatch \n MSE dimensions are:", prediction, target);
+    auto node = std::make_shared<NodeBackProp>("MSE", 1, 1, 1, 1, 1);
+    node->inputs = {prediction, target};
+    GB += (double)(prediction->total + target->total + 1) * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *pp = prediction.get(), *tp = target.get();
+    node->forward = [=]() {
+        if (calculate_loss || !last) {
+            check(mle_mse_fwd(pp->output, tp->output, nd->output, pp->total, st()), "Scalar MSE in MSE forward");
+            if (last && g_loss_readback) {
+                check_cuda(cudaStreamSynchronize(stream()), "MSE loss");
+                check_cuda(cudaMemcpy(&loss, nd->output, sizeof(float), cudaMemcpyDeviceToHost), "MSE loss");
+            }
+        }
+    };
+    node->backward = [=]() {
+        check(mle_mse_bwd(pp->output, tp->output, last ? nullptr : nd->grad, pp->grad, tp->total, st()),
+              "deriv_mse in MSE backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->output, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// ------------------------------------------ SoftMaxCrossEntropy (:2063-2124)
+// When `last`, the forward pass also writes the prediction gradient
+// (p - t)/batch, which is exactly what the backward lambda assigns from the
+// same probabilities; the backward then has nothing left to do.  A forward
+// that skipped the softmax (calc_loss false) leaves the backward to assign
+// from the kept probabilities, as the reference does with its stale buffer.
+graph GraphOperations::SoftMaxCrossEntropy(const graph& prediction, const graph& target, const bool last) {
+    for (int i = 0; i < 4; ++i)
+        if (prediction->dim[i] != target->dim[i])
+            dims_mismatch("Dimension mismatch \n CrossEntropy dimensions are:", prediction, target);
+    const int batch = target->dim[0], channels = target->dim[1], c = target->dim[2], d = target->dim[3];
+    auto node = std::make_shared<NodeBackProp>("SoftMaxCrossEntropy Loss", 1, 1, 1, 1, 1);
+    node->inputs = {prediction, target};
+    float* probs = arena_alloc(ARENA_ACT, prediction->total, "SoftMax");
+    GB += (double)(target->total + 1) * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *pp = prediction.get(), *tp = target.get();
+    ext(nd).kind = OP_SMCE;
+    const long long rows = (long long)batch * channels * c;
+    auto grad_written = std::make_shared<bool>(false);
+    node->forward = [=]() {
+        *grad_written = false;
+        if (calculate_loss || !last) {
+            float* gout = last ? pp->grad : nullptr;
+            check(mle_softmax_ce_fwd(pp->output, tp->output, (g_keep_softmax || !last) ? probs : nullptr, nd->output,
+                                     gout, (float)batch, rows, d, st()),
+                  "SoftMaxCrossEntropy");
+            *grad_written = (gout != nullptr);
+            if (last && g_loss_readback) {
+                check_cuda(cudaStreamSynchronize(stream()), "SMCE loss");
+                check_cuda(cudaMemcpy(&loss, nd->output, sizeof(float), cudaMemcpyDeviceToHost), "SMCE loss");
+            }
+        }
+    };
+    node->backward = [=]() {
+        if (*grad_written) return;
+        check(mle_softmax_ce_bwd(probs, tp->output, last ? nullptr : nd->grad, pp->grad, (float)batch, tp->total, st()),
+              "derivative of CE in CE backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->output, 1); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// --------------------------------------------- BMM family (:2196-2428)
+static int bcase(const graph& X) { return (X->dim[0] > 1) + 2 * (X->dim[1] > 1); }
+
+static void check_bc(const char* op, const graph& A, const graph& B) {
+    const bool bok = (A->dim[0] == B->dim[0]) || (A->dim[0] == 1) || (B->dim[0] == 1);
+    const bool cok = (A->dim[1] == B->dim[1]) || (A->dim[1] == 1) || (B->dim[1] == 1);
+    if (!(bok && cok)) {
+        std::cout << "Batch and Channel mismatch in " << op << "...\n";
+        Dimension(A);
+        Dimension(B);
+        std::exit(1);
+    }
+}
+
+// variant: forward kernel; the two backward calls follow the reference:
+//  BMM    : dA = bcmmABT(dZ, B), dB = bcmmATB(A, dZ)
+//  BMMABT : dA = bcmm(dZ, B),    dB = bcmmT(A, dZ)
+//  BMMATB : dA = bcmmT(dZ, B),   dB = bcmm(A, dZ)
+//  BMMT   : dA = bcmmATB(dZ, B), dB = bcmmABT(A, dZ)
+static graph bmm_node(const char* name, int variant, const graph& A, const graph& B, int m, int n, int p) {
+    check_bc(name, A, B);
+    const int Ac = bcase(A), Bc = bcase(B), Cc = Ac > Bc ? Ac : Bc;
+    const int batch = A->dim[0], channels = A->dim[1];
+    auto node = std::make_shared<NodeBackProp>(name, batch, channels, m, p, 1);
+    node->inputs = {A, B};
+    GraphOperations::GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *ap = A.get(), *bp = B.get();
+    node->forward = [=]() {
+        check(mle_bcmm(variant, ap->output, bp->output, nd->output, batch, channels, m, n, p, 0, Ac, Bc, Cc, 1.0f,
+                       st()),
+              str(name) + " forward");
+    };
+    int va, vb;  // backward variants for dA and dB
+    switch (variant) {
+        case MLE_GEMM_AB: va = MLE_GEMM_ABT; vb = MLE_GEMM_ATB; break;
+        case MLE_GEMM_ABT: va = MLE_GEMM_AB; vb = MLE_GEMM_ATBT; break;
+        case MLE_GEMM_ATB: va = MLE_GEMM_ATBT; vb = MLE_GEMM_AB; break;
+        default: va = MLE_GEMM_ATB; vb = MLE_GEMM_ABT; break;
+    }
+    node->backward = [=]() {
+        check(mle_bcmm(va, nd->grad, bp->output, ap->grad, batch, channels, m, p, n, 1, Cc, Bc, Ac, 1.0f, st()),
+              str(name) + " backward dA");
+        check(mle_bcmm(vb, ap->output, nd->grad, bp->grad, batch, channels, n, m, p, 1, Ac, Cc, Bc, 1.0f, st()),
+              str(name) + " backward dB");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+graph GraphOperations::BMM(const graph& A, const graph& B) {
+    if (A->dim[3] != B->dim[2]) dims_mismatch("Dimension mismatch in BMM", A, B);
+    return bmm_node("BMM", MLE_GEMM_AB, A, B, A->dim[2], A->dim[3], B->dim[3]);
+}
+graph GraphOperations::BMMABT(const graph& A, const graph& B) {
+    if (A->dim[3] != B->dim[3]) dims_mismatch("Dimension mismatch in BMMABT", A, B);
+    return bmm_node("BMMABT", MLE_GEMM_ABT, A, B, A->dim[2], A->dim[3], B->dim[2]);
+}
+graph GraphOperations::BMMATB(const graph& A, const graph& B) {
+    if (A->dim[2] != B->dim[2]) dims_mismatch("Dimension mismatch in BMM", A, B);
+    return bmm_node("BMMATB", MLE_GEMM_ATB, A, B, A->dim[3], A->dim[2], B->dim[3]);
+}
+graph GraphOperations::BMMT(const graph& A, const graph& B) {
+    if (A->dim[2] != B->dim[3]) dims_mismatch("Dimension mismatch in BMMT", A, B);
+    return bmm_node("BMMT", MLE_GEMM_ATBT, A, B, A->dim[3], A->dim[2], B->dim[2]);
+}
+
+// ------------------------------------------------ SOFTMAX / SOFTMASK (:2431-2497)
+static graph softmax_node(const char* name, const graph& X, int type, int mask) {
+    const int a = X->dim[0], b = X->dim[1], c = X->dim[2], d = X->dim[3];
+    auto node = std::make_shared<NodeBackProp>(name, a, b, c, d, 1);
+    node->inputs = {X};
+    const int lines = (type == 0) ? a * b * c : a * b * d;
+    GraphOperations::GB += (double)(node->total + 2 * lines) * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    node->forward = [=]() {
+        check(mle_softmax_fwd(xp->output, nd->output, (int64_t)a * b, c, d, type, mask, st()), str(name) + " forward");
+    };
+    node->backward = [=]() {
+        check(mle_softmax_bwd(nd->output, nd->grad, xp->grad, (int64_t)a * b, c, d, type, st()),
+              str(name) + " backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+graph GraphOperations::SOFTMAX(const graph& X, const int type) { return softmax_node("Softmax", X, type, 0); }
+graph GraphOperations::SOFTMASK(const graph& X, const int type) { return softmax_node("Softmask", X, type, 1); }
+
+// ---------------------------------------------------- activations (:2650-2850)
+static graph act_node(const char* name, int kind, const graph& input) {
+    auto node = std::make_shared<NodeBackProp>(name, input->dim[0], input->dim[1], input->dim[2], input->dim[3], 1);
+    node->inputs = {input};
+    GraphOperations::GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *ip = input.get();
+    ext(nd).kind = OP_ACTIVATION;
+    node->forward = [=]() { check(mle_act_fwd(kind, ip->output, nd->output, nd->total, st()), str(name) + " forward"); };
+    node->backward = [=]() {
+        const NodeExt& e = ext(nd);
+        check(mle_act_bwd(kind, ip->output, nd->grad, ip->grad, nd->total, e.fused_bias_target, e.fused_rows,
+                          e.fused_cols, st()),
+              str(name) + " backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+graph GraphOperations::RELU(const graph& input) { return act_node("ReLU", MLE_ACT_RELU, input); }
+graph GraphOperations::LeakyRELU(const graph& input) { return act_node("LeakyReLU", MLE_ACT_LEAKY_RELU, input); }
+graph GraphOperations::SILU(const graph& input) { return act_node("SiLU", MLE_ACT_SILU, input); }
+graph GraphOperations::TANH(const graph& input) { return act_node("TaNH", MLE_ACT_TANH, input); }
+graph GraphOperations::GELU(const graph& input) { return act_node("GeLU", MLE_ACT_GELU, input); }
+graph GraphOperations::SIGMOID(const graph& input) { return act_node("Sigmoid", MLE_ACT_SIGMOID, input); }
+
+// ------------------------------------------------------- CopyCrop (:2855-2915)
+// Channel concatenation when the spatial sizes agree.  With different sizes
+// the reference crops input1 into a buffer sized for input2's channels and
+// accumulates into a scratch gradient that is never cleared between steps
+// (Engine/engine.cu:2873-2898); that branch is not reproduced.
+graph GraphOperations::CopyCrop(const graph& input1, const graph& input2) {
+    const int batch = input2->dim[0], depth = input2->dim[1], d1 = input1->dim[1];
+    const int a = input2->dim[2], b = input2->dim[3];
+    if (input1->dim[2] != a || input1->dim[3] != b) {
+        std::cerr << "CopyCrop: cropping inputs of different spatial size is not supported by this runtime\n";
+        std::exit(1);
+    }
+    auto node = std::make_shared<NodeBackProp>("CopyNCrop", batch, d1 + depth, a, b, 1);
+    node->inputs = {input1, input2};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *p1 = input1.get(), *p2 = input2.get();
+    node->forward = [=]() {
+        check(mle_channel_concat(p1->output, p2->output, nd->output, batch, d1, depth, (int64_t)a * b, st()),
+              "CopyCrop forward");
+    };
+    node->backward = [=]() {
+        check(mle_channel_split(p1->grad, p2->grad, nd->grad, batch, d1, depth, (int64_t)a * b, st()),
+              "CopyCrop backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// -------------------------------------------------- LayerNorm (:3079-3135)
+graph GraphOperations::LayerNorm(const graph& X) {
+    const int a = X->dim[0], b = X->dim[1], c = X->dim[2], d = X->dim[3];
+    const float eps = 1e-5f;
+    auto node = std::make_shared<NodeBackProp>("LayerNorm", a, b, c, d, 1);
+    float* mean = arena_alloc(ARENA_ACT, a, "LayerNorm mean");
+    float* sq = arena_alloc(ARENA_ACT, a, "LayerNorm std");
+    GB += (double)(node->total + 2 * a) * sizeof(float) / (1ULL << 30);
+    node->inputs = {X};
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    node->forward = [=]() {
+        check(mle_layernorm_fwd(xp->output, nd->output, mean, sq, a, b, c, d, eps, st()), "LayerNorm forward");
+    };
+    node->backward = [=]() {
+        check(mle_layernorm_bwd(nd->output, nd->grad, sq, xp->grad, a, b, c, d, eps, st()), "LayerNorm backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// -------------------------------------------------- GroupNorm (:3200-3275)
+graph GraphOperations::GroupNorm(const graph& X, const int group) {
+    const int a = X->dim[0], b = X->dim[1], c = X->dim[2], d = X->dim[3];
+    if (b % group != 0) {
+        std::cout << "Groups cannot be cleanly split \n";
+        Dimension(X);
+        std::exit(1);
+    }
+    const float eps = 1e-5f;
+    auto node = std::make_shared<NodeBackProp>("GroupNorm", a, b, c, d, 1);
+    float* mean = arena_alloc(ARENA_ACT, (int64_t)a * group, "GroupNorm mean");
+    float* sq = arena_alloc(ARENA_ACT, (int64_t)a * group, "GroupNorm std");
+    GB += (double)(node->total + 2 * a * group) * sizeof(float) / (1ULL << 30);
+    node->inputs = {X};
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    node->forward = [=]() {
+        check(mle_groupnorm_fwd(xp->output, nd->output, mean, sq, a, b, group, c, d, eps, st()), "GroupNorm forward");
+    };
+    node->backward = [=]() {
+        check(mle_groupnorm_bwd(nd->output, nd->grad, sq, xp->grad, a, b, group, c, d, eps, st()),
+              "GroupNorm backward");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// -------------------------------------------- ScaledDotAttention (extension)
+graph GraphOperations::ScaledDotAttention(const graph& Q, const graph& K, const graph& V, const int heads,
+                                          const float scale, const bool mask, const int axis,
+                                          const int key_grad_mode) {
+    if (Q->dim[1] != 1 || K->dim[1] != 1 || V->dim[1] != 1 || Q->dim[3] % heads != 0 || K->dim[3] != Q->dim[3] ||
+        V->dim[3] != Q->dim[3] || K->dim[2] != V->dim[2] || K->dim[0] != Q->dim[0] || V->dim[0] != Q->dim[0]) {
+        std::cerr << "ScaledDotAttention: expects [B,1,S,H*hd] projections with matching shapes\n";
+        Dimension(Q);
+        Dimension(K);
+        Dimension(V);
+        std::exit(1);
+    }
+    const int B = Q->dim[0], Sq = Q->dim[2], Sk = K->dim[2], D = Q->dim[3], hd = D / heads;
+    auto node = std::make_shared<NodeBackProp>("Attention", B, 1, Sq, D, 1);
+    node->inputs = {Q, K, V};
+    // headified operands and their gradients, P and the score gradients
+    const int64_t nq = (int64_t)B * Sq * D, nk = (int64_t)B * Sk * D, ns = (int64_t)B * heads * Sq * Sk;
+    float* qh = arena_alloc(ARENA_ACT, nq, "Attention Qh");
+    float* kh = arena_alloc(ARENA_ACT, nk, "Attention Kh");
+    float* vh = arena_alloc(ARENA_ACT, nk, "Attention Vh");
+    float* oh = arena_alloc(ARENA_ACT, nq, "Attention Oh");
+    float* P = arena_alloc(ARENA_ACT, ns, "Attention P");
+    float* gqh = arena_alloc(ARENA_GRAD, nq, "Attention dQh");
+    float* gkh = arena_alloc(ARENA_GRAD, nk, "Attention dKh");
+    float* gvh = arena_alloc(ARENA_GRAD, nk, "Attention dVh");
+    float* goh = arena_alloc(ARENA_GRAD, nq, "Attention dOh");
+    float* dP = arena_alloc(ARENA_GRAD, ns, "Attention dP");
+    float* dS = arena_alloc(ARENA_GRAD, ns, "Attention dS");
+    GB += (double)(2 * (2 * nq + 2 * nk + 2 * ns) + nq) * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *qp = Q.get(), *kp = K.get(), *vp = V.get();
+    const int causal = (mask && Sq > 1) ? 1 : 0;
+    node->forward = [=]() {
+        check(mle_headify(qp->output, qh, B, heads, Sq, hd, 0, st()), "Attention headify Q");
+        check(mle_headify(kp->output, kh, B, heads, Sk, hd, 0, st()), "Attention headify K");
+        check(mle_headify(vp->output, vh, B, heads, Sk, hd, 0, st()), "Attention headify V");
+        // P = softmax(scale * Q K^T) along `axis`, in place
+        check(mle_bcmm(MLE_GEMM_ABT, qh, kh, P, B, heads, Sq, hd, Sk, 0, 3, 3, 3, scale, st()), "Attention scores");
+        check(mle_softmax_fwd(P, P, (int64_t)B * heads, Sq, Sk, axis, causal, st()), "Attention softmax");
+        check(mle_bcmm(MLE_GEMM_AB, P, vh, oh, B, heads, Sq, Sk, hd, 0, 3, 3, 3, 1.0f, st()), "Attention PV");
+        check(mle_headify(oh, nd->output, B, heads, Sq, hd, 2, st()), "Attention deheadify");
+    };
+    node->backward = [=]() {
+        check(mle_headify(nd->grad, goh, B, heads, Sq, hd, 3, st()), "Attention dO");
+        check(mle_attention_bwd(qh, kh, vh, P, goh, gqh, gkh, gvh, dP, dS, B, heads, Sq, Sk, hd, scale, causal, axis,
+                                key_grad_mode, st()),
+              "Attention backward");
+        check(mle_headify(gqh, qp->grad, B, heads, Sq, hd, 1, st()), "Attention dQ");
+        check(mle_headify(gkh, kp->grad, B, heads, Sk, hd, 1, st()), "Attention dK");
+        check(mle_headify(gvh, vp->grad, B, heads, Sk, hd, 1, st()), "Attention dV");
+    };
+    node->zero_grad = [=]() {
+        zero_range(nd->grad, nd->total);
+        zero_range(gqh, nq);
+        zero_range(gkh, nk);
+        zero_range(gvh, nk);
+        zero_range(goh, nq);
+        zero_range(dP, ns);
+        zero_range(dS, ns);
+    };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// ===================================================== Linear (:3496-3606)
+Linear::Linear(const int input, const int output, const str name, const bool bias)
+    : in(input), out(output), bias(bias), W1(name + " W1", 1, 1, input, output), B1(name + " B1", 1, 1, 1, output) {
+    if (name != "") op_name = name;
+}
+
+void Linear::save(std::ofstream& f) const {
+    W1.save(f);
+    if (bias) B1.save(f);
+}
+void Linear::load(std::ifstream& f) {
+    W1.load(f);
+    if (bias) B1.load(f);
+}
+void Linear::operator=(const Linear& other) {
+    W1 = other.W1;
+    if (bias) B1 = other.B1;
+}
+
+graph Linear::forward(const graph& X) {
+    if (X->dim[3] != W1.dim[2]) {
+        std::cout << "Shape Mismatch in Linear Layer of " << X->op_name << ": \n";
+        std::exit(1);
+    }
+    const int batch = X->dim[0], channels = X->dim[1], m = X->dim[2], n = X->dim[3], p = out;
+    auto node = std::make_shared<NodeBackProp>(op_name, batch, channels, m, p, 1);
+    node->inputs = {X};
+    const long long rows = (long long)batch * channels * m;
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    AdamParameter* W = &W1;
+    AdamParameter* Bp = bias ? &B1 : nullptr;
+    NodeExt& e = ext(nd);
+    e.kind = OP_LINEAR;
+    e.linear_bias_grad = bias ? B1.grad : nullptr;
+    node->forward = [=]() {
+        check(mle_linear_fwd(xp->output, W->output, Bp ? Bp->output : nullptr, nd->output, rows, n, p, st()),
+              "Linear forward");
+    };
+    node->backward = [=]() {
+        const bool fused = ext(nd).bias_grad_fused;
+        check(mle_linear_bwd(xp->output, W->output, nd->grad, xp->grad, W->grad, (Bp && !fused) ? Bp->grad : nullptr,
+                             rows, n, p, st()),
+              "MatMul... in " + nd->op_name + " backward");
+    };
+    node->free = [nd]() { nd->clear(); };
+    node->zero_grad = [=]() {
+        zero_range(nd->grad, nd->total);
+        zero_range(W->grad, W->total);
+        if (Bp) zero_range(Bp->grad, Bp->total);
+    };
+    node->accumulate = [=](double* gs) {
+        W->accumulate_grad(gs);
+        if (Bp) Bp->accumulate_grad(gs);
+    };
+    node->clipnorm = [=](const double* gs) {
+        W->gradnorm(gs);
+        if (Bp) Bp->gradnorm(gs);
+    };
+    node->updateParams = [=](const float lr, const bool adamw) {
+        W->update(lr, adamw);
+        if (Bp) Bp->update(lr, adamw);
+    };
+    return node;
+}

@@ -1,0 +1,499 @@
+// Benchmark/test sessions: the configuration graphs built with the
+// reference-compatible API, their step, CUDA-graph capture and the C ABI of
+// include/mle_engine.h.
+//
+// Graph shapes follow the benchmark configurations:
+//   MLP      use_cases/mnist.cu:252-273 (Linear 784->256, ReLU, Linear 256->10,
+//            SoftMaxCrossEntropy with a one-hot target built on the device)
+//   ENCODER  embedding gather -> MatrixPositionalEncoding -> N x pre-LN blocks
+//            [LayerNorm per token, MultiHeadAttention (column softmax, scale
+//            1/sqrt(head_dim), Engine/transformer.cu:647-661), Add, LayerNorm,
+//            Linear-GELU-Linear, Add] -> Linear projection -> SMCE
+//   ENCDEC   encoder as above; decoder blocks add masked self-attention and
+//            cross attention (scale 1/sqrt(d_model), masked whenever the query
+//            length exceeds 1, Engine/transformer.cu:662-675)
+// LayerNorm per token uses the reference's own mechanism: the token matrix
+// is reshaped to [B*S,1,1,D] while the LayerNorm node is built
+// (NodeBackProp::reshape, Engine/engine.cu:82-124).
+#include <math.h>
+#include <string.h>
+
+#include <cstring>
+#include <memory>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "engine_internal.h"
+#include "mle_engine.h"
+#include "session_dp.h"
+
+using namespace mle;
+
+namespace mle {
+bool g_loss_readback = true;
+}
+
+namespace {
+
+struct Input {
+    std::string name;
+    int dtype;  // 0 f32, 1 i32
+    int64_t numel;
+    void* host = nullptr;
+    void* dev = nullptr;
+};
+
+struct Session {
+    mle_session_desc d{};
+    cudaStream_t stream = nullptr;
+    GraphOperations go;
+    graph loss;
+    std::vector<std::unique_ptr<Linear>> linears;
+    std::vector<AdamParameter*> params;
+    std::vector<Input> inputs;
+    std::vector<std::function<void()>> prep;
+    std::vector<std::pair<float*, int64_t>> emb;
+    float* loss_host = nullptr;
+    cudaGraph_t graph_ = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    std::unique_ptr<DataParallel> dp;
+    size_t param_first = 0;
+};
+
+int status_of(cudaError_t e) {
+    if (e != cudaSuccess) {
+        fprintf(stderr, "mle_session: CUDA error %s\n", cudaGetErrorString(e));
+        return MLE_ERR_CUDA;
+    }
+    return MLE_OK;
+}
+
+struct StreamScope {  // routes every op of this session to its stream
+    cudaStream_t prev;
+    explicit StreamScope(cudaStream_t s) : prev(mle::stream()) { mle::set_stream(s); }
+    ~StreamScope() { mle::set_stream(prev); }
+};
+
+Linear* new_linear(Session& S, int in, int out, const std::string& name) {
+    S.linears.emplace_back(new Linear(in, out, name));
+    return S.linears.back().get();
+}
+
+Input& add_input(Session& S, const std::string& name, int dtype, int64_t numel, void* dev) {
+    Input in;
+    in.name = name;
+    in.dtype = dtype;
+    in.numel = numel;
+    in.dev = dev;
+    mle::check_cuda(cudaHostAlloc(&in.host, (size_t)numel * 4, cudaHostAllocDefault), "pinned input " + name);
+    std::memset(in.host, 0, (size_t)numel * 4);
+    S.inputs.push_back(in);
+    return S.inputs.back();
+}
+
+// Token matrix [B,1,S,D] normalised per token.
+graph ln_tokens(const graph& x, int B, int Sq, int D) {
+    x->reshape({B * Sq, 1, 1, D});
+    graph h = GraphOperations::LayerNorm(x);
+    x->reshape({B, 1, Sq, D});
+    h->reshape({B, 1, Sq, D});
+    return h;
+}
+
+graph attention(Session& S, const graph& xq, const graph& xkv, bool mask, float scale, const std::string& name) {
+    const int D = S.d.d_model, H = S.d.heads;
+    Linear* q = new_linear(S, D, D, name + " Query");
+    Linear* k = new_linear(S, D, D, name + " Key");
+    Linear* v = new_linear(S, D, D, name + " Value");
+    Linear* o = new_linear(S, D, D, name + " Output");
+    graph Qp = q->forward(xq), Kp = k->forward(xkv), Vp = v->forward(xkv);
+    graph att;
+    if (S.d.fused_attention) {
+        att = GraphOperations::ScaledDotAttention(Qp, Kp, Vp, H, scale, mask, 1, S.d.key_grad_mode);
+    } else {
+        graph Q = GraphOperations::HeadifytoChannel(Qp, H);
+        graph K = GraphOperations::HeadifytoChannel(Kp, H);
+        graph V = GraphOperations::HeadifytoChannel(Vp, H);
+        graph scores = GraphOperations::BMMABT(Q, K);
+        graph scaled = GraphOperations::Scale(scores, scale);
+        graph w = (mask && scaled->dim[2] > 1) ? GraphOperations::SOFTMASK(scaled, 1) : GraphOperations::SOFTMAX(scaled, 1);
+        att = GraphOperations::DeHeadify(GraphOperations::BMM(w, V));
+    }
+    graph out = o->forward(att);
+    out->op_name = name + " Output";
+    return out;
+}
+
+graph ffn(Session& S, const graph& h, const std::string& name) {
+    Linear* l1 = new_linear(S, S.d.d_model, S.d.ffn, name + " FFN1");
+    Linear* l2 = new_linear(S, S.d.ffn, S.d.d_model, name + " FFN2");
+    return l2->forward(GraphOperations::GELU(l1->forward(h)));
+}
+
+graph encoder_block(Session& S, graph x, int Sq, const std::string& name) {
+    const int B = S.d.batch, D = S.d.d_model, hd = D / S.d.heads;
+    graph h = ln_tokens(x, B, Sq, D);
+    x = GraphOperations::Add(x, attention(S, h, h, false, 1.0f / sqrtf((float)hd), name + " SelfAttn"));
+    graph h2 = ln_tokens(x, B, Sq, D);
+    return GraphOperations::Add(x, ffn(S, h2, name));
+}
+
+graph decoder_block(Session& S, graph x, const graph& enc, int Sq, const std::string& name) {
+    const int B = S.d.batch, D = S.d.d_model, hd = D / S.d.heads;
+    graph h = ln_tokens(x, B, Sq, D);
+    x = GraphOperations::Add(x, attention(S, h, h, true, 1.0f / sqrtf((float)hd), name + " MaskedSelfAttn"));
+    graph h2 = ln_tokens(x, B, Sq, D);
+    x = GraphOperations::Add(x, attention(S, h2, enc, true, 1.0f / sqrtf((float)D), name + " CrossAttn"));
+    graph h3 = ln_tokens(x, B, Sq, D);
+    return GraphOperations::Add(x, ffn(S, h3, name));
+}
+
+// token ids -> embedding node (gather) and target ids -> one-hot node
+graph token_input(Session& S, const std::string& name, int vocab) {
+    const int B = S.d.batch, Sq = S.d.seq_len, D = S.d.d_model;
+    auto node = std::make_shared<NodeBackProp>(name + " Embeddings", B, 1, Sq, D, 1);
+    float* table = arena_alloc(ARENA_PARAM, (int64_t)vocab * D, name + " embedding table");
+    S.emb.push_back({table, (int64_t)vocab * D});
+    int32_t* keys = (int32_t*)arena_alloc_bytes(ARENA_WS, (int64_t)B * Sq * 4, name + " keys");
+    add_input(S, name, 1, (int64_t)B * Sq, keys);
+    NodeBackProp* nd = node.get();
+    const int64_t nk = (int64_t)B * Sq;
+    S.prep.push_back([=]() { check(mle_embedding_gather(keys, table, nd->output, nk, D, st()), "GatherEmbeddings"); });
+    return node;
+}
+
+graph onehot_target(Session& S, const std::string& name, int rows_b, int rows_s, int classes) {
+    auto node = std::make_shared<NodeBackProp>(name, rows_b, 1, rows_s, classes, 1);
+    int32_t* keys = (int32_t*)arena_alloc_bytes(ARENA_WS, (int64_t)rows_b * rows_s * 4, name + " keys");
+    add_input(S, name, 1, (int64_t)rows_b * rows_s, keys);
+    NodeBackProp* nd = node.get();
+    const int64_t nk = (int64_t)rows_b * rows_s;
+    S.prep.push_back([=]() {
+        check_cuda(cudaMemsetAsync(nd->output, 0, (size_t)nd->total * 4, stream()), "one-hot clear");
+        check(mle_one_hot(keys, nd->output, nk, classes, st()), "OneHotEmbeddings");
+    });
+    return node;
+}
+
+void build(Session& S) {
+    const mle_session_desc& d = S.d;
+    if (d.config == MLE_CFG_MLP) {
+        auto x = std::make_shared<NodeBackProp>("MNIST input", d.batch, 1, 1, d.in_features, 1);
+        add_input(S, "x", 0, (int64_t)d.batch * d.in_features, x->output);
+        graph target = onehot_target(S, "labels", d.batch, 1, d.classes);
+        Linear* l1 = new_linear(S, d.in_features, d.hidden, "Linear1");
+        Linear* l2 = new_linear(S, d.hidden, d.classes, "Linear2");
+        graph logits = l2->forward(GraphOperations::RELU(l1->forward(x)));
+        S.loss = GraphOperations::SoftMaxCrossEntropy(logits, target, true);
+    } else if (d.config == MLE_CFG_ENCODER) {
+        graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tokens", d.vocab));
+        graph target = onehot_target(S, "targets", d.batch, d.seq_len, d.vocab);
+        for (int l = 0; l < d.layers; ++l) x = encoder_block(S, x, d.seq_len, "Enc" + std::to_string(l));
+        Linear* proj = new_linear(S, d.d_model, d.vocab, "Projection");
+        S.loss = GraphOperations::SoftMaxCrossEntropy(proj->forward(x), target, true);
+    } else if (d.config == MLE_CFG_ENCDEC) {
+        graph e = GraphOperations::MatrixPositionalEncoding(token_input(S, "src", d.vocab));
+        for (int l = 0; l < d.layers; ++l) e = encoder_block(S, e, d.seq_len, "Enc" + std::to_string(l));
+        graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tgt_in", d.vocab));
+        graph target = onehot_target(S, "tgt_out", d.batch, d.seq_len, d.vocab);
+        for (int l = 0; l < d.layers; ++l) x = decoder_block(S, x, e, d.seq_len, "Dec" + std::to_string(l));
+        Linear* proj = new_linear(S, d.d_model, d.vocab, "Projection");
+        S.loss = GraphOperations::SoftMaxCrossEntropy(proj->forward(x), target, true);
+    }
+    S.go.nodes = topological_sort(S.loss);
+}
+
+// He init for the MLP (N(0, 2/fan_in)), N(0, 0.02) for transformers; biases 0.
+void init_params(Session& S) {
+    std::mt19937_64 gen(S.d.seed * 0x2545F4914F6CDD1Dull + 17);
+    for (AdamParameter* p : S.params) {
+        std::vector<float> h((size_t)p->total, 0.0f);
+        const bool is_bias = p->dim[2] == 1;
+        if (!is_bias) {
+            const double stdv = (S.d.config == MLE_CFG_MLP) ? sqrt(2.0 / p->dim[2]) : 0.02;
+            std::normal_distribution<double> nd(0.0, stdv);
+            for (auto& x : h) x = (float)nd(gen);
+        }
+        check_cuda(cudaMemcpy(p->output, h.data(), h.size() * 4, cudaMemcpyHostToDevice), "param init");
+    }
+    std::normal_distribution<double> ne(0.0, 0.02);
+    for (auto& e : S.emb) {
+        std::vector<float> h((size_t)e.second);
+        for (auto& x : h) x = (float)ne(gen);
+        check_cuda(cudaMemcpy(e.first, h.data(), h.size() * 4, cudaMemcpyHostToDevice), "embedding init");
+    }
+}
+
+void run_phase(Session& S, int phase) {
+    switch (phase) {
+        case 0:
+            S.go.zero_grad();
+            break;
+        case 1:
+            for (auto& f : S.prep) f();
+            S.go.forward(nullptr, true);
+            break;
+        case 2:
+            S.go.backward();
+            break;
+        case 3:
+            if (S.dp) S.dp->reduce_remaining(stream());
+            break;
+        case 4:
+            if (S.d.clip_norm > 0) S.go.clip_grad_norm(S.d.clip_norm);
+            break;
+        case 5:
+            S.go.ParameterUpdate(nullptr, false, S.d.lr, S.d.adamw != 0);
+            break;
+    }
+}
+
+void step_body(Session& S, int upload) {
+    if (upload)
+        for (auto& in : S.inputs)
+            check_cuda(cudaMemcpyAsync(in.dev, in.host, (size_t)in.numel * 4, cudaMemcpyHostToDevice, S.stream),
+                       "input upload");
+    for (int ph = 0; ph <= 5; ++ph) run_phase(S, ph);
+    check_cuda(cudaMemcpyAsync(S.loss_host, S.loss->output, sizeof(float), cudaMemcpyDeviceToHost, S.stream),
+               "loss download");
+}
+
+Session* as_session(mle_session_t s) { return reinterpret_cast<Session*>(s); }
+
+}  // namespace
+
+extern "C" {
+
+int mle_session_create(const mle_session_desc* desc, mle_session_t* out) {
+    if (!desc || !out) return MLE_ERR_ARG;
+    const mle_session_desc& d = *desc;
+    if (d.batch <= 0) return MLE_ERR_ARG;
+    if (d.config == MLE_CFG_MLP) {
+        if (d.in_features <= 0 || d.hidden <= 0 || d.classes <= 0) return MLE_ERR_ARG;
+    } else if (d.config == MLE_CFG_ENCODER || d.config == MLE_CFG_ENCDEC) {
+        if (d.seq_len <= 0 || d.d_model <= 0 || d.heads <= 0 || d.d_model % d.heads || d.ffn <= 0 || d.layers <= 0 ||
+            d.vocab <= 0)
+            return MLE_ERR_ARG;
+    } else {
+        return MLE_ERR_ARG;
+    }
+    auto* S = new Session();
+    S->d = d;
+    if (cudaStreamCreateWithFlags(&S->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete S;
+        return MLE_ERR_CUDA;
+    }
+    mle::set_seed(d.seed);
+    mle::set_keep_softmax(false);
+    mle::g_loss_readback = false;
+    S->param_first = all_parameters().size();
+    {
+        StreamScope sc(S->stream);
+        build(*S);
+    }
+    // parameters in graph order (the order ParameterUpdate visits them)
+    {
+        std::vector<AdamParameter*> ordered;
+        for (auto& l : S->linears) {
+            ordered.push_back(&l->W1);
+            ordered.push_back(&l->B1);
+        }
+        S->params = ordered;
+    }
+    init_params(*S);
+    mle::check_cuda(cudaHostAlloc((void**)&S->loss_host, sizeof(float) * 4, cudaHostAllocDefault), "pinned loss");
+    mle::check_cuda(cudaDeviceSynchronize(), "session build");
+    *out = S;
+    return MLE_OK;
+}
+
+int mle_session_destroy(mle_session_t s) {
+    Session* S = as_session(s);
+    if (!S) return MLE_ERR_ARG;
+    cudaStreamSynchronize(S->stream);
+    if (S->exec) cudaGraphExecDestroy(S->exec);
+    if (S->graph_) cudaGraphDestroy(S->graph_);
+    S->dp.reset();
+    for (auto& in : S->inputs) cudaFreeHost(in.host);
+    cudaFreeHost(S->loss_host);
+    cudaStreamDestroy(S->stream);
+    // parameters are owned by the session's Linear layers
+    auto& all = all_parameters();
+    for (AdamParameter* p : S->params) all.erase(std::remove(all.begin(), all.end(), p), all.end());
+    S->go.nodes.clear();
+    S->loss.reset();
+    delete S;
+    return MLE_OK;
+}
+
+void* mle_session_stream(mle_session_t s) { return s ? (void*)as_session(s)->stream : nullptr; }
+
+int mle_session_input_count(mle_session_t s) { return s ? (int)as_session(s)->inputs.size() : -1; }
+
+int mle_session_input_info(mle_session_t s, int i, char* name, int name_len, int64_t* numel, int* dtype,
+                           void** host_ptr, void** dev_ptr) {
+    Session* S = as_session(s);
+    if (!S || i < 0 || i >= (int)S->inputs.size()) return MLE_ERR_ARG;
+    const Input& in = S->inputs[i];
+    if (name && name_len > 0) {
+        std::strncpy(name, in.name.c_str(), (size_t)name_len - 1);
+        name[name_len - 1] = 0;
+    }
+    if (numel) *numel = in.numel;
+    if (dtype) *dtype = in.dtype;
+    if (host_ptr) *host_ptr = in.host;
+    if (dev_ptr) *dev_ptr = in.dev;
+    return MLE_OK;
+}
+
+int mle_session_step(mle_session_t s, int upload, float* loss_out) {
+    Session* S = as_session(s);
+    if (!S) return MLE_ERR_ARG;
+    StreamScope sc(S->stream);
+    if (S->exec) {
+        if (!upload) return MLE_ERR_UNSUPPORTED;  // the captured step includes the upload
+        if (cudaGraphLaunch(S->exec, S->stream) != cudaSuccess) return status_of(cudaGetLastError());
+    } else {
+        step_body(*S, upload);
+    }
+    if (loss_out) {
+        const cudaError_t e = cudaStreamSynchronize(S->stream);
+        if (e != cudaSuccess) return status_of(e);
+        *loss_out = *S->loss_host;
+    }
+    return status_of(cudaGetLastError());
+}
+
+int mle_session_phase(mle_session_t s, int phase) {
+    Session* S = as_session(s);
+    if (!S || phase < 0 || phase > 5) return MLE_ERR_ARG;
+    StreamScope sc(S->stream);
+    if (phase == 1)
+        for (auto& in : S->inputs)
+            check_cuda(cudaMemcpyAsync(in.dev, in.host, (size_t)in.numel * 4, cudaMemcpyHostToDevice, S->stream),
+                       "input upload");
+    run_phase(*S, phase);
+    if (phase == 1)
+        check_cuda(cudaMemcpyAsync(S->loss_host, S->loss->output, sizeof(float), cudaMemcpyDeviceToHost, S->stream),
+                   "loss download");
+    return status_of(cudaGetLastError());
+}
+
+int mle_session_capture(mle_session_t s) {
+    Session* S = as_session(s);
+    if (!S) return MLE_ERR_ARG;
+    StreamScope sc(S->stream);
+    if (S->exec) {
+        cudaGraphExecDestroy(S->exec);
+        S->exec = nullptr;
+    }
+    if (S->graph_) {
+        cudaGraphDestroy(S->graph_);
+        S->graph_ = nullptr;
+    }
+    cudaError_t e = cudaStreamSynchronize(S->stream);
+    if (e != cudaSuccess) return status_of(e);
+    e = cudaStreamBeginCapture(S->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return status_of(e);
+    step_body(*S, 1);
+    e = cudaStreamEndCapture(S->stream, &S->graph_);
+    if (e != cudaSuccess) return status_of(e);
+    e = cudaGraphInstantiate(&S->exec, S->graph_, 0);
+    return status_of(e);
+}
+
+int mle_session_sync(mle_session_t s) {
+    Session* S = as_session(s);
+    if (!S) return MLE_ERR_ARG;
+    return status_of(cudaStreamSynchronize(S->stream));
+}
+
+int mle_session_param_count(mle_session_t s) { return s ? (int)as_session(s)->params.size() : -1; }
+
+int mle_session_param_info(mle_session_t s, int i, char* name, int name_len, int64_t* numel) {
+    Session* S = as_session(s);
+    if (!S || i < 0 || i >= (int)S->params.size()) return MLE_ERR_ARG;
+    AdamParameter* p = S->params[i];
+    if (name && name_len > 0) {
+        std::strncpy(name, p->op_name.c_str(), (size_t)name_len - 1);
+        name[name_len - 1] = 0;
+    }
+    if (numel) *numel = p->total;
+    return MLE_OK;
+}
+
+static float* param_buf(AdamParameter* p, int which) {
+    switch (which) {
+        case 0: return p->output;
+        case 1: return p->grad;
+        case 2: return p->m;
+        case 3: return p->v;
+        default: return nullptr;
+    }
+}
+
+int mle_session_param_read(mle_session_t s, int i, int which, float* host) {
+    Session* S = as_session(s);
+    if (!S || i < 0 || i >= (int)S->params.size() || !host) return MLE_ERR_ARG;
+    float* src = param_buf(S->params[i], which);
+    if (!src) return MLE_ERR_ARG;
+    cudaError_t e = cudaStreamSynchronize(S->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(host, src, (size_t)S->params[i]->total * 4, cudaMemcpyDeviceToHost);
+    return status_of(e);
+}
+
+int mle_session_param_write(mle_session_t s, int i, int which, const float* host) {
+    Session* S = as_session(s);
+    if (!S || i < 0 || i >= (int)S->params.size() || !host) return MLE_ERR_ARG;
+    float* dst = param_buf(S->params[i], which);
+    if (!dst) return MLE_ERR_ARG;
+    cudaError_t e = cudaStreamSynchronize(S->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(dst, host, (size_t)S->params[i]->total * 4, cudaMemcpyHostToDevice);
+    return status_of(e);
+}
+
+int mle_session_param_step(mle_session_t s, int i, int* t) {
+    Session* S = as_session(s);
+    if (!S || i < 0 || i >= (int)S->params.size() || !t) return MLE_ERR_ARG;
+    StreamScope sc(S->stream);
+    S->params[i]->sync_step();
+    *t = S->params[i]->t;
+    return MLE_OK;
+}
+
+int mle_session_embedding_count(mle_session_t s) { return s ? (int)as_session(s)->emb.size() : -1; }
+
+int mle_session_embedding_write(mle_session_t s, int i, const float* host, int64_t numel) {
+    Session* S = as_session(s);
+    if (!S || i < 0 || i >= (int)S->emb.size() || !host || numel != S->emb[i].second) return MLE_ERR_ARG;
+    cudaError_t e = cudaStreamSynchronize(S->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(S->emb[i].first, host, (size_t)numel * 4, cudaMemcpyHostToDevice);
+    return status_of(e);
+}
+
+int mle_session_device_bytes(mle_session_t s, int64_t* bytes) {
+    if (!s || !bytes) return MLE_ERR_ARG;
+    double gib = 0;
+    for (int a = 0; a < ARENA_COUNT; ++a) gib += arena_gib((Arena)a);
+    *bytes = (int64_t)(gib * (double)(1ull << 30));
+    return MLE_OK;
+}
+
+int mle_session_node_count(mle_session_t s) { return s ? (int)as_session(s)->go.nodes.size() : -1; }
+
+int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int world, int bucket_mb) {
+    Session* S = as_session(s);
+    if (!S || !id128 || world <= 0 || rank < 0 || rank >= world) return MLE_ERR_ARG;
+    std::vector<std::pair<float*, int64_t>> grads;
+    for (AdamParameter* p : S->params) grads.push_back({p->grad, p->total});
+    std::unique_ptr<DataParallel> dp(new DataParallel());
+    const int st_ = dp->init(id128, rank, world, grads, bucket_mb, S->stream);
+    if (st_ != MLE_OK) return st_;
+    S->dp = std::move(dp);
+    S->go.set_grad_prescale(1.0f / (float)world);
+    return MLE_OK;
+}
+
+}  // extern "C"

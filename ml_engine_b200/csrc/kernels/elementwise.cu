@@ -1,0 +1,708 @@
+// Elementwise and gather/scatter kernels of the graph-op lambdas.
+//
+// All kernels are grid-stride loops sized to whole waves of the 148 SMs and
+// use 128-bit accesses whenever every pointer is 16-byte aligned.  The
+// arithmetic of each op follows the reference kernel named at its entry
+// point in include/mle_kernels.h, operation for operation, so results are
+// bitwise those of the reference for the elementwise ops.
+#include <math.h>
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace mle {
+
+static cudaError_t g_last_cuda_error = cudaSuccess;
+
+void record_cuda_error(cudaError_t e) { g_last_cuda_error = e; }
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr float kPi = 3.14159265359f;  // the reference's float PI constant
+
+// ---------------------------------------------------------------------------
+// activation formulas (Engine/kernels.cu:1214-1328)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float act_forward(int kind, float x) {
+    switch (kind) {
+        case MLE_ACT_RELU: return (x < 0.f) ? 0.0f : x;
+        case MLE_ACT_LEAKY_RELU: return (x < 0.f) ? 0.01f * x : x;
+        case MLE_ACT_SILU: return x * (1.0f / (1.0f + expf(-x)));
+        case MLE_ACT_TANH: return tanhf(x);
+        case MLE_ACT_GELU: {
+            const float val = sqrtf(2.0f / kPi) * (x + 0.044715f * x * x * x);
+            const float th = tanhf(val);
+            return 0.5f * x * (1.0f + th);
+        }
+        default: {  // sigmoid
+            const float negexp = expf(-1.0f * x);
+            return 1.0f / (1.0f + negexp);
+        }
+    }
+}
+
+// gx + gy * f'(x), with the reference's derivative expressions.
+__device__ __forceinline__ float act_backward(int kind, float x, float gy, float gx) {
+    switch (kind) {
+        case MLE_ACT_RELU: {
+            const float mask = (x > 0.0f) ? 1.0f : 0.0f;
+            return gx + gy * mask;
+        }
+        case MLE_ACT_LEAKY_RELU: {
+            const float mask = (x < 0.0f) ? 0.01f : 1.0f;
+            return gx + gy * mask;
+        }
+        case MLE_ACT_SILU: {
+            const float e = expf(x);
+            const float ne = 1.0f / e;
+            const float sigma = 1.0f / (1.0f + ne);
+            const float d = sigma + (x / (e + ne + 2.0f));
+            return gx + gy * d;
+        }
+        case MLE_ACT_TANH: {
+            const float e2 = expf(2.0f * x);
+            const float ne2 = 1.0f / e2;
+            const float d = 4.0f / (e2 + ne2 + 2.0f);
+            return gx + gy * d;
+        }
+        case MLE_ACT_GELU: {
+            const float root = sqrtf(2.0f / kPi);
+            const float u = root * (x + 0.044715f * x * x * x);
+            const float du = root * (1.0f + 0.134145f * x * x);
+            const float t = tanhf(u);
+            return gx + (0.5f + 0.5f * t + 0.5f * x * (1.0f - t * t) * du) * gy;
+        }
+        default: {  // sigmoid
+            const float e = expf(x);
+            const float ne = 1.0f / e;
+            const float d = 1.0f / (e + ne + 2.0f);
+            return gx + gy * d;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// generic vectorised map kernels
+// ---------------------------------------------------------------------------
+__global__ void fill_kernel(float* __restrict__ x, float v, int64_t n) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t n4 = n >> 2;
+    float4* x4 = reinterpret_cast<float4*>(x);
+    for (int64_t j = i; j < n4; j += stride) x4[j] = make_float4(v, v, v, v);
+    for (int64_t j = (n4 << 2) + i; j < n; j += stride) x[j] = v;
+}
+
+__global__ void fill_kernel_scalar(float* __restrict__ x, float v, int64_t n) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) x[i] = v;
+}
+
+// op codes for the binary map kernel
+enum MapOp { OP_COPY = 0, OP_ACCUM = 1, OP_SCALE_WRITE = 2, OP_SCALE_ADD = 3 };
+
+template <int OP>
+__device__ __forceinline__ float map1(float x, float y_old, float other, float fscale, double dscale) {
+    if (OP == OP_COPY) return x;
+    if (OP == OP_ACCUM) return (float)((double)y_old + dscale * (double)x);  // Y += scale*X in double
+    if (OP == OP_SCALE_WRITE) return fscale * x;
+    return x + fscale * other;  // OP_SCALE_ADD: z = x + scale*y
+}
+
+template <int OP, bool VEC>
+__global__ void map_kernel(const float* __restrict__ x, const float* __restrict__ other,
+                           float* __restrict__ y, int64_t n, float fscale, double dscale) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t tail = 0;
+    if (VEC) {
+        const int64_t n4 = n >> 2;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        const float4* o4 = reinterpret_cast<const float4*>(other);
+        float4* y4 = reinterpret_cast<float4*>(y);
+        for (int64_t j = i0; j < n4; j += stride) {
+            const float4 a = x4[j];
+            float4 yo = make_float4(0.f, 0.f, 0.f, 0.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (OP == OP_ACCUM) yo = y4[j];
+            if (OP == OP_SCALE_ADD) b = o4[j];
+            float4 r;
+            r.x = map1<OP>(a.x, yo.x, b.x, fscale, dscale);
+            r.y = map1<OP>(a.y, yo.y, b.y, fscale, dscale);
+            r.z = map1<OP>(a.z, yo.z, b.z, fscale, dscale);
+            r.w = map1<OP>(a.w, yo.w, b.w, fscale, dscale);
+            y4[j] = r;
+        }
+        tail = n4 << 2;
+    }
+    for (int64_t j = tail + i0; j < n; j += stride) {
+        const float yo = (OP == OP_ACCUM) ? y[j] : 0.f;
+        const float b = (OP == OP_SCALE_ADD) ? other[j] : 0.f;
+        y[j] = map1<OP>(x[j], yo, b, fscale, dscale);
+    }
+}
+
+template <bool VEC>
+__global__ void add_bwd_kernel(const float* __restrict__ g, float* __restrict__ ga,
+                               float* __restrict__ gb, int64_t n) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t tail = 0;
+    if (VEC) {
+        const int64_t n4 = n >> 2;
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        float4* a4 = reinterpret_cast<float4*>(ga);
+        float4* b4 = reinterpret_cast<float4*>(gb);
+        for (int64_t j = i0; j < n4; j += stride) {
+            const float4 v = g4[j];
+            float4 a = a4[j];
+            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+            a4[j] = a;
+            float4 b = b4[j];
+            b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
+            b4[j] = b;
+        }
+        tail = n4 << 2;
+    }
+    for (int64_t j = tail + i0; j < n; j += stride) {
+        const float v = g[j];
+        ga[j] += v;
+        gb[j] += v;
+    }
+}
+
+template <bool VEC>
+__global__ void act_fwd_kernel(int kind, const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t tail = 0;
+    if (VEC) {
+        const int64_t n4 = n >> 2;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        float4* y4 = reinterpret_cast<float4*>(y);
+        for (int64_t j = i0; j < n4; j += stride) {
+            const float4 a = x4[j];
+            y4[j] = make_float4(act_forward(kind, a.x), act_forward(kind, a.y), act_forward(kind, a.z),
+                                act_forward(kind, a.w));
+        }
+        tail = n4 << 2;
+    }
+    for (int64_t j = tail + i0; j < n; j += stride) y[j] = act_forward(kind, x[j]);
+}
+
+template <bool VEC>
+__global__ void act_bwd_kernel(int kind, const float* __restrict__ x, const float* __restrict__ gy,
+                               float* __restrict__ gx, int64_t n) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t tail = 0;
+    if (VEC) {
+        const int64_t n4 = n >> 2;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        const float4* g4 = reinterpret_cast<const float4*>(gy);
+        float4* o4 = reinterpret_cast<float4*>(gx);
+        for (int64_t j = i0; j < n4; j += stride) {
+            const float4 a = x4[j], g = g4[j];
+            float4 o = o4[j];
+            o.x = act_backward(kind, a.x, g.x, o.x);
+            o.y = act_backward(kind, a.y, g.y, o.y);
+            o.z = act_backward(kind, a.z, g.z, o.z);
+            o.w = act_backward(kind, a.w, g.w, o.w);
+            o4[j] = o;
+        }
+        tail = n4 << 2;
+    }
+    for (int64_t j = tail + i0; j < n; j += stride) gx[j] = act_backward(kind, x[j], gy[j], gx[j]);
+}
+
+// Activation backward fused with the column sums of the updated gradient.
+// Block (kThreads) covers kThreads*4 columns (4 per thread, float4) of a
+// chunk of rows; each thread keeps 4 column partials and adds them with one
+// atomicAdd per column per block.
+template <bool VEC>
+__global__ void act_bwd_bias_kernel(int kind, const float* __restrict__ x, const float* __restrict__ gy,
+                                    float* __restrict__ gx, float* __restrict__ bias_grad, int64_t rows,
+                                    int64_t cols, int64_t rows_per_block) {
+    const int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const int64_t r_begin = (int64_t)blockIdx.y * rows_per_block;
+    int64_t r_end = r_begin + rows_per_block;
+    if (r_end > rows) r_end = rows;
+    if (c0 >= cols) return;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    if (VEC) {  // cols % 4 == 0 and aligned
+        for (int64_t r = r_begin; r < r_end; ++r) {
+            const int64_t idx = r * cols + c0;
+            const float4 a = *reinterpret_cast<const float4*>(x + idx);
+            const float4 g = *reinterpret_cast<const float4*>(gy + idx);
+            float4 o = *reinterpret_cast<float4*>(gx + idx);
+            o.x = act_backward(kind, a.x, g.x, o.x);
+            o.y = act_backward(kind, a.y, g.y, o.y);
+            o.z = act_backward(kind, a.z, g.z, o.z);
+            o.w = act_backward(kind, a.w, g.w, o.w);
+            *reinterpret_cast<float4*>(gx + idx) = o;
+            s0 += o.x; s1 += o.y; s2 += o.z; s3 += o.w;
+        }
+        atomicAdd(bias_grad + c0 + 0, s0);
+        atomicAdd(bias_grad + c0 + 1, s1);
+        atomicAdd(bias_grad + c0 + 2, s2);
+        atomicAdd(bias_grad + c0 + 3, s3);
+    } else {
+        const int nc = (int)((cols - c0) < 4 ? (cols - c0) : 4);
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int64_t r = r_begin; r < r_end; ++r) {
+            for (int k = 0; k < nc; ++k) {
+                const int64_t idx = r * cols + c0 + k;
+                const float o = act_backward(kind, x[idx], gy[idx], gx[idx]);
+                gx[idx] = o;
+                s[k] += o;
+            }
+        }
+        for (int k = 0; k < nc; ++k) atomicAdd(bias_grad + c0 + k, s[k]);
+    }
+}
+
+// y[r,c] = x[r,c] + b[c]
+template <bool VEC>
+__global__ void bias_add_kernel(const float* __restrict__ x, const float* __restrict__ b, float* __restrict__ y,
+                                int64_t rows, int64_t cols) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (VEC) {
+        const int64_t c4 = cols >> 2;
+        const int64_t n4 = rows * c4;
+        for (int64_t j = i0; j < n4; j += stride) {
+            const int64_t c = (j % c4) << 2;
+            float4 a = reinterpret_cast<const float4*>(x)[j];
+            const float4 bb = *reinterpret_cast<const float4*>(b + c);
+            a.x += bb.x; a.y += bb.y; a.z += bb.z; a.w += bb.w;
+            reinterpret_cast<float4*>(y)[j] = a;
+        }
+    } else {
+        const int64_t n = rows * cols;
+        for (int64_t j = i0; j < n; j += stride) y[j] = x[j] + b[j % cols];
+    }
+}
+
+// Column sums: one block per (column strip of 4*kThreads, row chunk).
+template <bool VEC>
+__global__ void col_sum_kernel(const float* __restrict__ g, float* __restrict__ out, int64_t rows, int64_t cols,
+                               int64_t rows_per_block, float scale) {
+    const int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const int64_t r_begin = (int64_t)blockIdx.y * rows_per_block;
+    int64_t r_end = r_begin + rows_per_block;
+    if (r_end > rows) r_end = rows;
+    if (c0 >= cols) return;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    if (VEC) {
+        for (int64_t r = r_begin; r < r_end; ++r) {
+            const float4 v = *reinterpret_cast<const float4*>(g + r * cols + c0);
+            s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
+        }
+        for (int k = 0; k < 4; ++k) atomicAdd(out + c0 + k, s[k] * scale);
+    } else {
+        const int nc = (int)((cols - c0) < 4 ? (cols - c0) : 4);
+        for (int64_t r = r_begin; r < r_end; ++r)
+            for (int k = 0; k < nc; ++k) s[k] += g[r * cols + c0 + k];
+        for (int k = 0; k < nc; ++k) atomicAdd(out + c0 + k, s[k] * scale);
+    }
+}
+
+// y[n,c,s] = x[n,c,s] + b[c]
+__global__ void channel_bias_fwd_kernel(const float* __restrict__ x, const float* __restrict__ b,
+                                        float* __restrict__ y, int channels, int64_t spatial, int64_t total) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int c = (int)((i / spatial) % channels);
+        y[i] = x[i] + b[c];
+    }
+}
+
+// One block per (channel, batch chunk): gb[c] += sum; optional gx += g.
+__global__ void channel_bias_bwd_kernel(const float* __restrict__ g, float* __restrict__ gx,
+                                        float* __restrict__ gb, int batch, int channels, int64_t spatial,
+                                        int batch_per_block) {
+    __shared__ float scratch[32];
+    const int c = blockIdx.x;
+    const int n0 = blockIdx.y * batch_per_block;
+    int n1 = n0 + batch_per_block;
+    if (n1 > batch) n1 = batch;
+    float s = 0.f;
+    for (int n = n0; n < n1; ++n) {
+        const int64_t base = ((int64_t)n * channels + c) * spatial;
+        for (int64_t k = threadIdx.x; k < spatial; k += blockDim.x) {
+            const float v = g[base + k];
+            s += v;
+            if (gx) gx[base + k] += v;
+        }
+    }
+    s = block_sum(s, scratch);
+    if (threadIdx.x == 0) atomicAdd(gb + c, s);
+}
+
+// MatPEncoding (Engine/kernels.cu:166-185): double-precision angle.
+__global__ void matpe_kernel(const float* __restrict__ x, float* __restrict__ y, int rows, int cols,
+                             int64_t total, int start_idx) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int pos = (int)((i % ((int64_t)rows * cols)) / cols) + start_idx;
+        const int d = (int)(i % cols);
+        const int half = d / 2;
+        const double exponent = (2.0 * half) / cols;
+        const double freq = 1.0 / pow(10000.0, exponent);
+        const double angle = (double)pos * freq;
+        y[i] = (d % 2 == 0) ? x[i] + (float)sin(angle) : x[i] + (float)cos(angle);
+    }
+}
+
+// PEncoding (Engine/kernels.cu:147-164)
+__global__ void timestep_pe_kernel(float* __restrict__ y, int t, int dim) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= dim) return;
+    const int half = dim / 2;
+    const int f = (i < half) ? i : i - half;
+    const double exponent = -(double)f * log(10000.0) / (half - 1);
+    const double freq = exp(exponent);
+    const double angle = (double)t * freq;
+    y[i] = (i < half) ? (float)cos(angle) : (float)sin(angle);
+}
+
+// HeadifyColChannel (Engine/kernels.cu:1371-1406); the += forms touch each
+// element once, so plain read-modify-write replaces the atomics.
+__global__ void headify_kernel(const float* __restrict__ in, float* __restrict__ out, int heads, int seq,
+                               int head_dim, int64_t total, int flag) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int embed = heads * head_dim;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+        const int d = (int)(idx % head_dim);
+        const int s = (int)((idx / head_dim) % seq);
+        const int h = (int)((idx / ((int64_t)head_dim * seq)) % heads);
+        const int64_t b = idx / ((int64_t)head_dim * seq * heads);
+        const int64_t hidx = idx;
+        const int64_t fidx = b * ((int64_t)seq * embed) + (int64_t)s * embed + (int64_t)h * head_dim + d;
+        if (flag == 0) out[hidx] = in[fidx];
+        else if (flag == 1) out[fidx] += in[hidx];
+        else if (flag == 2) out[fidx] = in[hidx];
+        else out[hidx] += in[fidx];
+    }
+}
+
+__global__ void channel_concat_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                      float* __restrict__ c, int c1, int c2, int64_t spatial, int64_t total) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int cc = c1 + c2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t n = i / ((int64_t)cc * spatial);
+        const int ch = (int)((i / spatial) % cc);
+        const int64_t s = i % spatial;
+        c[i] = (ch < c1) ? a[(n * c1 + ch) * spatial + s] : b[(n * c2 + (ch - c1)) * spatial + s];
+    }
+}
+
+__global__ void channel_split_kernel(float* __restrict__ ga, float* __restrict__ gb, const float* __restrict__ gc,
+                                     int c1, int c2, int64_t spatial, int64_t total) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int cc = c1 + c2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t n = i / ((int64_t)cc * spatial);
+        const int ch = (int)((i / spatial) % cc);
+        const int64_t s = i % spatial;
+        if (ch < c1) ga[(n * c1 + ch) * spatial + s] += gc[i];
+        else gb[(n * c2 + (ch - c1)) * spatial + s] += gc[i];
+    }
+}
+
+// CopynCrop: (a,b) -> (c,d) centre crop
+__global__ void center_crop_kernel(const float* __restrict__ x, float* __restrict__ y, int depth, int a, int b,
+                                   int c, int d, int64_t total) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int dr = (a - c) / 2, dc = (b - d) / 2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t nb = i / ((int64_t)depth * c * d);
+        const int ch = (int)((i / ((int64_t)c * d)) % depth);
+        const int t = (int)(i % ((int64_t)c * d));
+        const int r = t / d, col = t % d;
+        y[i] = x[nb * depth * (int64_t)a * b + (int64_t)ch * a * b + (int64_t)(r + dr) * b + col + dc];
+    }
+}
+
+// PaddingCrop: (c,d) -> (a,b), accumulate
+__global__ void pad_crop_kernel(const float* __restrict__ x, float* __restrict__ y, int depth, int a, int b,
+                                int c, int d, int64_t total) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int dr = (a - c) / 2, dc = (b - d) / 2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t nb = i / ((int64_t)depth * a * b);
+        const int ch = (int)((i / ((int64_t)a * b)) % depth);
+        const int t = (int)(i % ((int64_t)a * b));
+        const int xr = t / b - dr, xc = t % b - dc;
+        if (xr >= 0 && xr < c && xc >= 0 && xc < d)
+            y[i] += x[nb * depth * (int64_t)c * d + (int64_t)ch * c * d + (int64_t)xr * d + xc];
+    }
+}
+
+__global__ void gather_kernel(const int32_t* __restrict__ keys, const float* __restrict__ table,
+                              float* __restrict__ out, int64_t total, int dim) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t row = i / dim;
+        const int k = keys[row];
+        out[i] = (k < 0) ? 0.0f : table[(int64_t)k * dim + (i % dim)];
+    }
+}
+
+__global__ void one_hot_kernel(const int32_t* __restrict__ keys, float* __restrict__ out, int64_t n, int vocab) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const int k = keys[i];
+        if (k >= 0 && k < vocab) out[i * vocab + k] = 1.0f;
+    }
+}
+
+inline bool vec_ok(int64_t n, const void* a, const void* b = nullptr, const void* c = nullptr) {
+    (void)n;
+    return aligned16(a) && (b == nullptr || aligned16(b)) && (c == nullptr || aligned16(c));
+}
+
+}  // namespace
+}  // namespace mle
+
+using namespace mle;
+
+extern "C" {
+
+const char* mle_status_string(int status) {
+    switch (status) {
+        case MLE_OK: return "ok";
+        case MLE_ERR_ARG: return "invalid argument";
+        case MLE_ERR_CUDA: return "CUDA error";
+        case MLE_ERR_UNSUPPORTED: return "unsupported shape or flag";
+        case MLE_ERR_TIMEOUT: return "device-side wait timed out";
+        default: return "unknown status";
+    }
+}
+
+int mle_last_cuda_error(void) { return (int)g_last_cuda_error; }
+
+int mle_abi_version(void) { return 1; }
+
+int mle_fill(float* x, float value, int64_t n, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && !x)) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    if (aligned16(x)) fill_kernel<<<grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>(x, value, n);
+    else fill_kernel_scalar<<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(x, value, n);
+    return launch_status();
+}
+
+#define MLE_MAP_LAUNCH(OP, X, O, Y, N, FS, DS)                                                        \
+    do {                                                                                          \
+        if (vec_ok(N, X, O, Y))                                                                   \
+            map_kernel<OP, true><<<grid_for((N) / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>( \
+                X, O, Y, N, FS, DS);                                                              \
+        else                                                                                      \
+            map_kernel<OP, false><<<grid_for(N, kThreads), kThreads, 0, as_stream(stream)>>>(X, O, Y, N, \
+                                                                                        FS, DS);  \
+    } while (0)
+
+int mle_copy(const float* x, float* y, int64_t n, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && (!x || !y))) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    MLE_MAP_LAUNCH(OP_COPY, x, (const float*)nullptr, y, n, 1.f, 1.0);
+    return launch_status();
+}
+
+int mle_accumulate(const float* x, float* y, int64_t n, double scale, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && (!x || !y))) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    MLE_MAP_LAUNCH(OP_ACCUM, x, (const float*)nullptr, y, n, 1.f, scale);
+    return launch_status();
+}
+
+int mle_scale_write(const float* x, float* y, int64_t n, float scale, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && (!x || !y))) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    MLE_MAP_LAUNCH(OP_SCALE_WRITE, x, (const float*)nullptr, y, n, scale, 1.0);
+    return launch_status();
+}
+
+int mle_scale_add(const float* x, const float* y, float* z, float scale, int64_t n, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && (!x || !y || !z))) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    MLE_MAP_LAUNCH(OP_SCALE_ADD, x, y, z, n, scale, 1.0);
+    return launch_status();
+}
+
+int mle_add_bwd(const float* g, float* ga, float* gb, int64_t n, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && (!g || !ga || !gb))) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    if (vec_ok(n, g, ga, gb))
+        add_bwd_kernel<true><<<grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>(g, ga, gb, n);
+    else
+        add_bwd_kernel<false><<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(g, ga, gb, n);
+    return launch_status();
+}
+
+int mle_act_fwd(int kind, const float* x, float* y, int64_t n, mle_stream_t stream) {
+    if (kind < 0 || kind > MLE_ACT_SIGMOID || n < 0 || (n > 0 && (!x || !y))) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    if (vec_ok(n, x, y))
+        act_fwd_kernel<true><<<grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>(kind, x, y, n);
+    else
+        act_fwd_kernel<false><<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(kind, x, y, n);
+    return launch_status();
+}
+
+int mle_act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n, float* bias_grad, int64_t rows,
+                int64_t cols, mle_stream_t stream) {
+    if (kind < 0 || kind > MLE_ACT_SIGMOID || n < 0 || (n > 0 && (!x || !gy || !gx))) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    if (!bias_grad) {
+        if (vec_ok(n, x, gy, gx))
+            act_bwd_kernel<true><<<grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>(kind, x, gy, gx, n);
+        else
+            act_bwd_kernel<false><<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(kind, x, gy, gx, n);
+        return launch_status();
+    }
+    if (rows <= 0 || cols <= 0 || rows * cols != n) return MLE_ERR_ARG;
+    const int64_t col_blocks = (cols + 4 * kThreads - 1) / (4 * kThreads);
+    int64_t row_blocks = (2 * kSMs + col_blocks - 1) / col_blocks;
+    if (row_blocks > rows) row_blocks = rows;
+    const int64_t rpb = (rows + row_blocks - 1) / row_blocks;
+    row_blocks = (rows + rpb - 1) / rpb;
+    dim3 grid((unsigned)col_blocks, (unsigned)row_blocks);
+    const bool vec = (cols % 4 == 0) && vec_ok(n, x, gy, gx) && aligned16(bias_grad);
+    if (vec)
+        act_bwd_bias_kernel<true><<<grid, kThreads, 0, as_stream(stream)>>>(kind, x, gy, gx, bias_grad, rows, cols, rpb);
+    else
+        act_bwd_bias_kernel<false><<<grid, kThreads, 0, as_stream(stream)>>>(kind, x, gy, gx, bias_grad, rows, cols, rpb);
+    return launch_status();
+}
+
+int mle_bias_add_fwd(const float* x, const float* bias, float* y, int64_t rows, int64_t cols, mle_stream_t stream) {
+    if (rows < 0 || cols <= 0 || !x || !bias || !y) return MLE_ERR_ARG;
+    if (rows == 0) return MLE_OK;
+    const int64_t n = rows * cols;
+    if (cols % 4 == 0 && vec_ok(n, x, bias, y))
+        bias_add_kernel<true><<<grid_for(n / 4, kThreads), kThreads, 0, as_stream(stream)>>>(x, bias, y, rows, cols);
+    else
+        bias_add_kernel<false><<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(x, bias, y, rows, cols);
+    return launch_status();
+}
+
+int mle_bias_grad(const float* g, float* bias_grad, int64_t rows, int64_t cols, float scale, mle_stream_t stream) {
+    if (rows < 0 || cols <= 0 || !g || !bias_grad) return MLE_ERR_ARG;
+    if (rows == 0) return MLE_OK;
+    const int64_t col_blocks = (cols + 4 * kThreads - 1) / (4 * kThreads);
+    int64_t row_blocks = (2 * kSMs + col_blocks - 1) / col_blocks;
+    if (row_blocks > rows) row_blocks = rows;
+    const int64_t rpb = (rows + row_blocks - 1) / row_blocks;
+    row_blocks = (rows + rpb - 1) / rpb;
+    dim3 grid((unsigned)col_blocks, (unsigned)row_blocks);
+    if (cols % 4 == 0 && aligned16(g) && aligned16(bias_grad))
+        col_sum_kernel<true><<<grid, kThreads, 0, as_stream(stream)>>>(g, bias_grad, rows, cols, rpb, scale);
+    else
+        col_sum_kernel<false><<<grid, kThreads, 0, as_stream(stream)>>>(g, bias_grad, rows, cols, rpb, scale);
+    return launch_status();
+}
+
+int mle_channel_bias_fwd(const float* x, const float* b, float* y, int batch, int channels, int64_t spatial,
+                         mle_stream_t stream) {
+    if (batch < 0 || channels <= 0 || spatial <= 0 || !x || !b || !y) return MLE_ERR_ARG;
+    const int64_t total = (int64_t)batch * channels * spatial;
+    if (total == 0) return MLE_OK;
+    channel_bias_fwd_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, b, y, channels, spatial,
+                                                                                           total);
+    return launch_status();
+}
+
+int mle_channel_bias_bwd(const float* g, float* gx, float* gb, int batch, int channels, int64_t spatial,
+                         mle_stream_t stream) {
+    if (batch < 0 || channels <= 0 || spatial <= 0 || !g || !gb) return MLE_ERR_ARG;
+    if (batch == 0) return MLE_OK;
+    int chunks = (2 * kSMs + channels - 1) / channels;
+    if (chunks > batch) chunks = batch;
+    const int bpb = (batch + chunks - 1) / chunks;
+    chunks = (batch + bpb - 1) / bpb;
+    dim3 grid((unsigned)channels, (unsigned)chunks);
+    channel_bias_bwd_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(g, gx, gb, batch, channels, spatial, bpb);
+    return launch_status();
+}
+
+int mle_matpe_fwd(const float* x, float* y, int batch, int rows, int cols, int start_idx, mle_stream_t stream) {
+    if (batch < 0 || rows <= 0 || cols <= 0 || !x || !y) return MLE_ERR_ARG;
+    const int64_t total = (int64_t)batch * rows * cols;
+    if (total == 0) return MLE_OK;
+    matpe_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, y, rows, cols, total, start_idx);
+    return launch_status();
+}
+
+int mle_timestep_pe(float* y, int t, int dim, mle_stream_t stream) {
+    if (dim <= 2 || !y) return MLE_ERR_ARG;
+    timestep_pe_kernel<<<(dim + kThreads - 1) / kThreads, kThreads, 0, as_stream(stream)>>>(y, t, dim);
+    return launch_status();
+}
+
+int mle_headify(const float* in, float* out, int batch, int heads, int seq, int head_dim, int flag,
+                mle_stream_t stream) {
+    if (batch < 0 || heads <= 0 || seq <= 0 || head_dim <= 0 || flag < 0 || flag > 3 || !in || !out)
+        return MLE_ERR_ARG;
+    const int64_t total = (int64_t)batch * heads * seq * head_dim;
+    if (total == 0) return MLE_OK;
+    headify_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(in, out, heads, seq, head_dim, total,
+                                                                                  flag);
+    return launch_status();
+}
+
+int mle_channel_concat(const float* a, const float* b, float* c, int batch, int c1, int c2, int64_t spatial,
+                       mle_stream_t stream) {
+    if (batch < 0 || c1 < 0 || c2 < 0 || spatial <= 0 || !a || !b || !c) return MLE_ERR_ARG;
+    const int64_t total = (int64_t)batch * (c1 + c2) * spatial;
+    if (total == 0) return MLE_OK;
+    channel_concat_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(a, b, c, c1, c2, spatial,
+                                                                                         total);
+    return launch_status();
+}
+
+int mle_channel_split(float* ga, float* gb, const float* gc, int batch, int c1, int c2, int64_t spatial,
+                      mle_stream_t stream) {
+    if (batch < 0 || c1 < 0 || c2 < 0 || spatial <= 0 || !ga || !gb || !gc) return MLE_ERR_ARG;
+    const int64_t total = (int64_t)batch * (c1 + c2) * spatial;
+    if (total == 0) return MLE_OK;
+    channel_split_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(ga, gb, gc, c1, c2, spatial,
+                                                                                        total);
+    return launch_status();
+}
+
+int mle_center_crop(const float* x, float* y, int batch, int depth, int a, int b, int c, int d,
+                    mle_stream_t stream) {
+    if (batch < 0 || depth <= 0 || c <= 0 || d <= 0 || c > a || d > b || !x || !y) return MLE_ERR_ARG;
+    const int64_t total = (int64_t)batch * depth * c * d;
+    if (total == 0) return MLE_OK;
+    center_crop_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, y, depth, a, b, c, d, total);
+    return launch_status();
+}
+
+int mle_pad_crop(const float* x, float* y, int batch, int depth, int a, int b, int c, int d, mle_stream_t stream) {
+    if (batch < 0 || depth <= 0 || a <= 0 || b <= 0 || !x || !y) return MLE_ERR_ARG;
+    const int64_t total = (int64_t)batch * depth * a * b;
+    if (total == 0) return MLE_OK;
+    pad_crop_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, y, depth, a, b, c, d, total);
+    return launch_status();
+}
+
+int mle_embedding_gather(const int32_t* keys, const float* table, float* out, int64_t n_keys, int dim,
+                         mle_stream_t stream) {
+    if (n_keys < 0 || dim <= 0 || !keys || !table || !out) return MLE_ERR_ARG;
+    const int64_t total = n_keys * dim;
+    if (total == 0) return MLE_OK;
+    gather_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(keys, table, out, total, dim);
+    return launch_status();
+}
+
+int mle_one_hot(const int32_t* keys, float* out, int64_t n_keys, int vocab, mle_stream_t stream) {
+    if (n_keys < 0 || vocab <= 0 || !keys || !out) return MLE_ERR_ARG;
+    if (n_keys == 0) return MLE_OK;
+    one_hot_kernel<<<grid_for(n_keys, kThreads), kThreads, 0, as_stream(stream)>>>(keys, out, n_keys, vocab);
+    return launch_status();
+}
+
+}  // extern "C"

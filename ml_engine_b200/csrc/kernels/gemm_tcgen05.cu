@@ -1,0 +1,697 @@
+// fp32-in / fp32-out GEMM on the 5th-generation tensor cores (sm_100a).
+//
+// The reference multiplies with 32x32 shared-memory tiles, one output per
+// thread, and atomics for every `backward` output (bcmm*,
+// Engine/kernels.cu:387-539).  This kernel computes the same products with
+// tcgen05.mma kind::tf32:
+//   * operand tiles stream through a STAGES-deep shared-memory ring, loaded
+//     by TMA (cp.async.bulk.tensor, 128-byte swizzle) and tracked by
+//     mbarriers (full: TMA bytes landed; empty: the MMAs reading the slot
+//     retired, signalled by tcgen05.commit);
+//   * one thread issues 128 x BN x 8 MMAs into a TMEM accumulator;
+//   * four warps drain TMEM with tcgen05.ld and apply the epilogue
+//     (assign, += or atomic add, alpha, optional bias).
+// Both K-major and MN-major operands are read straight from their row-major
+// storage (instruction-descriptor transpose bits), so dX = dY*W^T and
+// dW = X^T*dY need no transposed copies.
+//
+// Every mbarrier wait is bounded by %globaltimer; on timeout the kernel sets
+// the watchdog word, stops issuing work, lets issued copies and MMAs retire,
+// frees its TMEM and returns.
+#include <cuda.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "gemm.cuh"
+
+namespace mle {
+
+__device__ unsigned int g_tc_watchdog = 0;
+
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 32;                   // fp32 elements per k-block = one 128-byte swizzle row
+constexpr int kThreads = 128;
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s
+
+enum EpiMode { EPI_ASSIGN = 0, EPI_ACCUM = 1, EPI_ATOMIC = 2 };
+
+struct EpiParams {
+    float* C;
+    const float* bias;
+    int64_t ldc;
+    int64_t c_stride_b, c_stride_c;  // element offsets per batch / channel index (0 = broadcast)
+    int M, N, K;
+    int channels;                     // z = (b * channels + c) * splits + split
+    int splits, kb_per_split;
+    int a_has_b, a_has_c, b_has_b, b_has_c;
+    float alpha;
+    int mode;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait.  Returns false if the CTA-wide abort flag is (or becomes) set.
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 127u) == 127u) {
+            if (*abort_flag) return false;
+            const uint64_t now = gtimer();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > kTimeoutNs) {
+                *abort_flag = 1;
+                atomicOr(&g_tc_watchdog, 1u);
+                return false;
+            }
+        }
+    }
+}
+
+// Wait that ignores the abort flag (used to drain issued work), still bounded.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (gtimer() - t0 > kTimeoutNs) {
+            atomicOr(&g_tc_watchdog, 2u);
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+// UMMA shared-memory descriptor (sm100 version bits).  Layout types:
+// 2 = 128-byte swizzle with 16-byte atoms (K-major operands),
+// 1 = 128-byte swizzle with 32-byte atoms, the only MN-major layout the
+//     tensor cores accept for 32-bit (tf32) elements.
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Atom32 = 1;
+
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                               uint32_t layout = kLayoutSW128) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version (sm100)
+    d |= (uint64_t)(layout & 7u) << 61;
+    return d;
+}
+
+// Operand tile descriptors for k-step kk (8 tf32 of K) of a stage:
+//  K-major : rows of 128 B (32 K-values), 8-row swizzle atoms 1024 B apart;
+//            a k-step advances 32 B along the row.
+//  MN-major: per TMA box 32 K-rows x 128 B (32 MN-values), boxes 4096 B
+//            apart along MN (LBO); 32-byte-atom swizzle repeats every 4 rows
+//            (SBO = 512 B); a k-step advances 8 rows = 1024 B.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) { return make_sdesc(base + kk * 32, 16, 1024); }
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
+    return make_sdesc(base + kk * 1024, 4096, 512, kLayoutSW128Atom32);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN, int STAGES>
+struct Smem {
+    static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
+    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+    static constexpr int TOTAL = BAR_OFFSET + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
+};
+
+// A_MN: A is stored MN-major ([K][M]); B_MN: B is stored MN-major ([K][N]).
+template <bool A_MN, bool B_MN, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const EpiParams ep) {
+    using L = Smem<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tmem_full = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN;
+    const int m0 = blockIdx.y * BM;
+    int z = blockIdx.z;
+    const int split = z % ep.splits;
+    z /= ep.splits;
+    const int cidx = z % ep.channels;
+    const int bidx = z / ep.channels;
+    const int kb_total = (ep.K + BK - 1) / BK;
+    const int kb_begin = split * ep.kb_per_split;
+    int kb_end = kb_begin + ep.kb_per_split;
+    if (kb_end > kb_total) kb_end = kb_total;
+    const int nkb = kb_end > kb_begin ? kb_end - kb_begin : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tmem_full, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int a_c = ep.a_has_c ? cidx : 0, a_b = ep.a_has_b ? bidx : 0;
+    const int b_c = ep.b_has_c ? cidx : 0, b_b = ep.b_has_b ? bidx : 0;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        uint32_t last_parity[STAGES];
+        bool issued[STAGES];
+        for (int s = 0; s < STAGES; ++s) issued[s] = false;
+        int s = 0;
+        uint32_t ph = 0;
+        for (int i = 0; i < nkb; ++i) {
+            if (!wait_bounded(&empty[s], ph ^ 1u, abort_flag)) break;
+            uint8_t* sa = smem + s * L::STAGE_BYTES;
+            uint8_t* sb = sa + L::A_BYTES;
+            const int k0 = (kb_begin + i) * BK;
+            mbar_arrive_expect_tx(&full[s], (uint32_t)L::STAGE_BYTES);
+            if (A_MN) {
+#pragma unroll
+                for (int j = 0; j < BM / 32; ++j) tma_load_4d(&tmA, &full[s], sa + j * 4096, m0 + 32 * j, k0, a_c, a_b);
+            } else {
+                tma_load_4d(&tmA, &full[s], sa, k0, m0, a_c, a_b);
+            }
+            if (B_MN) {
+#pragma unroll
+                for (int j = 0; j < BN / 32; ++j) tma_load_4d(&tmB, &full[s], sb + j * 4096, n0 + 32 * j, k0, b_c, b_b);
+            } else {
+                tma_load_4d(&tmB, &full[s], sb, k0, n0, b_c, b_b);
+            }
+            issued[s] = true;
+            last_parity[s] = ph;
+            if (++s == STAGES) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        if (*abort_flag) {
+            for (int t = 0; t < STAGES; ++t)
+                if (issued[t]) drain_wait(&full[t], last_parity[t]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------- MMA issuer -------------------------------
+        // instruction descriptor: D=f32, A=B=tf32, transpose bits, N>>3, M>>4
+        const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                               ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+        int s = 0;
+        uint32_t ph = 0;
+        for (int i = 0; i < nkb; ++i) {
+            if (!wait_bounded(&full[s], ph, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
+            const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk) {
+                const uint64_t ad = A_MN ? mnmajor_desc(sa, kk) : kmajor_desc(sa, kk);
+                const uint64_t bd = B_MN ? mnmajor_desc(sb, kk) : kmajor_desc(sb, kk);
+                mma_tf32(tmem_base, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(&empty[s]);
+            if (++s == STAGES) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        mma_commit(tmem_full);  // arrives once every MMA issued above retired
+    }
+    __syncwarp();
+
+    // --------------------------------- epilogue ---------------------------------
+    drain_wait(tmem_full, 0);
+    tc_fence_after();
+    const bool skip = (*abort_flag != 0) || nkb == 0;
+    const int row = m0 + warp * 32 + lane;
+    float* Cbase = ep.C + (int64_t)bidx * ep.c_stride_b + (int64_t)cidx * ep.c_stride_c;
+    const bool row_ok = row < ep.M;
+    float* crow = Cbase + (int64_t)(row_ok ? row : 0) * ep.ldc;
+    const bool vec_ok = ((ep.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(Cbase) & 15u) == 0);
+#pragma unroll 1
+    for (int cc = 0; cc < BN / 32; ++cc) {
+        const int col0 = n0 + cc * 32;
+        if (col0 >= ep.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cc * 32), r);
+        if (skip || !row_ok) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
+        if (ep.bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < ep.N) v[j] += ep.bias[col0 + j];
+        }
+        if (vec_ok && col0 + 32 <= ep.N) {
+            float4* dst = reinterpret_cast<float4*>(crow + col0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                float4 val = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                if (ep.mode == EPI_ASSIGN) {
+                    dst[q] = val;
+                } else if (ep.mode == EPI_ACCUM) {
+                    float4 o = dst[q];
+                    o.x += val.x; o.y += val.y; o.z += val.z; o.w += val.w;
+                    dst[q] = o;
+                } else {
+                    atomicAdd(dst + q, val);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int col = col0 + j;
+                if (col < ep.N) {
+                    if (ep.mode == EPI_ASSIGN) crow[col] = v[j];
+                    else if (ep.mode == EPI_ACCUM) crow[col] += v[j];
+                    else atomicAdd(crow + col, v[j]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)BN)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps through the driver entry point (no libcuda link)
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Operand view: element (inner i, outer o, channel c, batch b) lives at
+// base + i + o*ld + c*sc + b*sb.  Extents of broadcast dims are 1.
+struct OperandView {
+    const float* base;
+    int64_t inner, outer, nc, nb;
+    int64_t ld, sc, sb;  // elements
+};
+
+// K-major tiles use the 16-byte-atom 128-byte swizzle; MN-major tiles the
+// 32-byte-atom one, matching the UMMA layout types above.
+static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner, int box_outer,
+                           bool mn_major = false) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)v.inner, (cuuint64_t)v.outer, (cuuint64_t)v.nc, (cuuint64_t)v.nb};
+    // byte strides of dims 1..3 (must be multiples of 16 and non-zero)
+    int64_t sc = v.sc, sb = v.sb;
+    if (v.nc == 1) sc = v.ld * v.outer;
+    if (v.nb == 1) sb = (v.nc == 1 ? v.ld * v.outer : sc * v.nc);
+    cuuint64_t strides[3] = {(cuuint64_t)(v.ld * 4), (cuuint64_t)(sc * 4), (cuuint64_t)(sb * 4)};
+    cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(v.base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <bool A_MN, bool B_MN, int BN, int STAGES>
+static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& ep, int grid_x, int grid_y,
+                     int grid_z, cudaStream_t st) {
+    using L = Smem<BN, STAGES>;
+    auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, STAGES>;
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
+            return launch_status();
+        configured = true;
+    }
+    kern<<<dim3(grid_x, grid_y, grid_z), kThreads, L::TOTAL, st>>>(ma, mb, ep);
+    return launch_status();
+}
+
+}  // namespace tc
+
+static bool tc_eligible(const GemmProblem& p) {
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (!al(p.A) || !al(p.B)) return false;
+    if ((p.lda & 3) || (p.ldb & 3)) return false;
+    if ((p.a_sb & 3) || (p.a_sc & 3) || (p.b_sb & 3) || (p.b_sc & 3)) return false;
+    // N tiles of >= 64 columns: tiny N (e.g. 10 logits) goes to the SIMT path.
+    if (p.N < 32 || p.M < 16) return false;
+    if (tc::get_encode() == nullptr) return false;
+    return true;
+}
+
+int run_gemm(const GemmProblem& p, cudaStream_t st) {
+    if (p.M <= 0 || p.N <= 0 || p.nbatch <= 0 || p.channels <= 0) return MLE_OK;
+    if (p.K <= 0) {
+        // empty reduction: assign writes alpha*0 (+bias); accumulate is a no-op
+        if (p.mode != tc::EPI_ASSIGN) return MLE_OK;
+    }
+    if (p.K <= 0 || !tc_eligible(p)) return simt_gemm(p, st);
+
+    using namespace tc;
+    const bool A_MN = p.trans_a != 0;  // A stored [K][M]: M contiguous
+    const bool B_MN = p.trans_b == 0;  // B stored [K][N]: N contiguous
+    const int64_t z_count = (int64_t)p.nbatch * p.channels;
+    const int m_tiles = (p.M + BM - 1) / BM;
+    const int kb_total = (p.K + BK - 1) / BK;
+
+    int BN = 128;
+    {
+        const int64_t t256 = (int64_t)m_tiles * ((p.N + 255) / 256) * z_count;
+        const int64_t t128 = (int64_t)m_tiles * ((p.N + 127) / 128) * z_count;
+        if (p.N >= 256 && t256 >= 2 * kSMs) BN = 256;
+        else if (p.N > 64 && t128 >= kSMs) BN = 128;
+        else if (p.N <= 64) BN = 64;
+        else BN = (t128 >= kSMs / 2) ? 128 : 64;
+    }
+    const int n_tiles = (p.N + BN - 1) / BN;
+    const int64_t tiles = (int64_t)m_tiles * n_tiles * z_count;
+    int splits = 1;
+    if (p.mode != EPI_ASSIGN && tiles < kSMs && kb_total >= 8) {
+        splits = (int)((2 * kSMs + tiles - 1) / tiles);
+        if (splits > kb_total / 4) splits = kb_total / 4;
+        if (splits < 1) splits = 1;
+    }
+    const int kb_per_split = (kb_total + splits - 1) / splits;
+    splits = (kb_total + kb_per_split - 1) / kb_per_split;
+    if (z_count * splits > 65535 || m_tiles > 65535) return simt_gemm(p, st);
+
+    EpiParams ep;
+    ep.C = p.C;
+    ep.bias = p.bias;
+    ep.ldc = p.ldc;
+    ep.c_stride_b = p.c_sb;
+    ep.c_stride_c = p.c_sc;
+    ep.M = p.M;
+    ep.N = p.N;
+    ep.K = p.K;
+    ep.channels = p.channels;
+    ep.splits = splits;
+    ep.kb_per_split = kb_per_split;
+    ep.a_has_b = (p.a_sb != 0 && p.nbatch > 1);
+    ep.a_has_c = (p.a_sc != 0 && p.channels > 1);
+    ep.b_has_b = (p.b_sb != 0 && p.nbatch > 1);
+    ep.b_has_c = (p.b_sc != 0 && p.channels > 1);
+    if (p.nbatch == 1) ep.c_stride_b = 0;
+    if (p.channels == 1) ep.c_stride_c = 0;
+    ep.alpha = p.alpha;
+    ep.mode = (splits > 1) ? EPI_ATOMIC : p.mode;
+    if (splits > 1 && p.bias) return simt_gemm(p, st);  // bias with split-K would be added per split
+
+    OperandView va, vb;
+    va.base = p.A;
+    va.inner = A_MN ? p.M : p.K;
+    va.outer = A_MN ? p.K : p.M;
+    va.ld = p.lda;
+    va.nc = ep.a_has_c ? p.channels : 1;
+    va.nb = ep.a_has_b ? p.nbatch : 1;
+    va.sc = p.a_sc;
+    va.sb = p.a_sb;
+    vb.base = p.B;
+    vb.inner = B_MN ? p.N : p.K;
+    vb.outer = B_MN ? p.K : p.N;
+    vb.ld = p.ldb;
+    vb.nc = ep.b_has_c ? p.channels : 1;
+    vb.nb = ep.b_has_b ? p.nbatch : 1;
+    vb.sc = p.b_sc;
+    vb.sb = p.b_sb;
+    CUtensorMap ma, mb;
+    memset(&ma, 0, sizeof(ma));
+    memset(&mb, 0, sizeof(mb));
+    if (!encode_operand(&ma, va, 32, A_MN ? BK : BM, A_MN)) return simt_gemm(p, st);
+    if (!encode_operand(&mb, vb, 32, B_MN ? BK : BN, B_MN)) return simt_gemm(p, st);
+
+    const int gx = n_tiles, gy = m_tiles, gz = (int)(z_count * splits);
+#define MLE_TC(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST>(ma, mb, ep, gx, gy, gz, st)
+    if (BN == 256) {
+        if (A_MN) { if (B_MN) MLE_TC(true, true, 256, 4); else MLE_TC(true, false, 256, 4); }
+        else { if (B_MN) MLE_TC(false, true, 256, 4); else MLE_TC(false, false, 256, 4); }
+    } else if (BN == 128) {
+        if (A_MN) { if (B_MN) MLE_TC(true, true, 128, 6); else MLE_TC(true, false, 128, 6); }
+        else { if (B_MN) MLE_TC(false, true, 128, 6); else MLE_TC(false, false, 128, 6); }
+    } else {
+        if (A_MN) { if (B_MN) MLE_TC(true, true, 64, 8); else MLE_TC(true, false, 64, 8); }
+        else { if (B_MN) MLE_TC(false, true, 64, 8); else MLE_TC(false, false, 64, 8); }
+    }
+#undef MLE_TC
+}
+
+}  // namespace mle
+
+using namespace mle;
+
+extern "C" {
+
+int mle_watchdog_read(int* out_flag, mle_stream_t stream) {
+    if (!out_flag) return MLE_ERR_ARG;
+    unsigned int v = 0, zero = 0;
+    cudaStream_t st = as_stream(stream);
+    if (cudaMemcpyFromSymbolAsync(&v, g_tc_watchdog, sizeof(v), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return launch_status();
+    if (cudaMemcpyToSymbolAsync(g_tc_watchdog, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return launch_status();
+    if (cudaStreamSynchronize(st) != cudaSuccess) return launch_status();
+    *out_flag = (int)v;
+    return MLE_OK;
+}
+
+int mle_gemm(const float* A, const float* B, float* C, const float* bias, int batch, int64_t M, int64_t N, int64_t K,
+             int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a, int64_t stride_b, int64_t stride_c, int trans_a,
+             int trans_b, float alpha, float beta, mle_stream_t stream) {
+    if (!A || !B || !C || batch <= 0 || M < 0 || N < 0 || K < 0) return MLE_ERR_ARG;
+    if (beta != 0.0f && beta != 1.0f) return MLE_ERR_UNSUPPORTED;
+    if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return MLE_ERR_UNSUPPORTED;
+    GemmProblem p;
+    p.A = A;
+    p.B = B;
+    p.C = C;
+    p.bias = bias;
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.lda = lda;
+    p.ldb = ldb;
+    p.ldc = ldc;
+    p.trans_a = trans_a;
+    p.trans_b = trans_b;
+    p.nbatch = batch;
+    p.channels = 1;
+    p.a_sb = (batch > 1) ? stride_a : 0;
+    p.b_sb = (batch > 1) ? stride_b : 0;
+    p.c_sb = (batch > 1) ? stride_c : 0;
+    p.a_sc = p.b_sc = p.c_sc = 0;
+    p.alpha = alpha;
+    p.mode = (beta == 0.0f) ? tc::EPI_ASSIGN : tc::EPI_ACCUM;
+    if (batch > 1 && stride_c == 0) {
+        if (beta == 0.0f) return MLE_ERR_UNSUPPORTED;
+        p.mode = tc::EPI_ATOMIC;
+    }
+    return run_gemm(p, as_stream(stream));
+}
+
+int mle_bcmm(int variant, const float* A, const float* B, float* C, int batch, int channels, int m, int n, int p,
+             int backward, int A_case, int B_case, int C_case, float scale, mle_stream_t stream) {
+    if (!A || !B || !C || batch <= 0 || channels <= 0 || m <= 0 || n <= 0 || p <= 0) return MLE_ERR_ARG;
+    if (variant < 0 || variant > 3 || A_case < 0 || A_case > 3 || B_case < 0 || B_case > 3 || C_case < 0 ||
+        C_case > 3)
+        return MLE_ERR_ARG;
+    // Per-operand element strides for batch and channel, as batch_chan_offset
+    // (Engine/kernels.cu:371-385) computes them.
+    auto strides = [&](int flag, int64_t inner, int64_t& sb, int64_t& sc) {
+        const int hb = flag & 1, hc = (flag >> 1) & 1;
+        sc = hc ? inner : 0;
+        sb = hb ? (hc ? (int64_t)channels * inner : inner) : 0;
+    };
+    const bool a_t = (variant == MLE_GEMM_ATB || variant == MLE_GEMM_ATBT);
+    const bool b_t = (variant == MLE_GEMM_ABT || variant == MLE_GEMM_ATBT);
+    GemmProblem q;
+    q.A = A;
+    q.B = B;
+    q.C = C;
+    q.bias = nullptr;
+    q.M = m;
+    q.N = p;
+    q.K = n;
+    q.lda = a_t ? m : n;  // A stored [n][m] when transposed
+    q.ldb = b_t ? n : p;  // B stored [p][n] when transposed
+    q.ldc = p;
+    q.trans_a = a_t;
+    q.trans_b = b_t;
+    strides(A_case, (int64_t)m * n, q.a_sb, q.a_sc);
+    strides(B_case, (int64_t)n * p, q.b_sb, q.b_sc);
+    strides(C_case, (int64_t)m * p, q.c_sb, q.c_sc);
+    // Which of the grid's (batch, channel) axes some operand actually varies
+    // over; axes no operand varies over only repeat the same product.
+    const bool any_b = (A_case & 1) || (B_case & 1) || (C_case & 1);
+    const bool any_c = (A_case & 2) || (B_case & 2) || (C_case & 2);
+    q.nbatch = any_b ? batch : 1;
+    q.channels = any_c ? channels : 1;
+    float mult = 1.0f;
+    if (!any_b) mult *= (float)batch;
+    if (!any_c) mult *= (float)channels;
+    // C receives several products when an axis is iterated but C does not
+    // vary over it: those are summed (the reference's atomicAdd).
+    const bool c_reduces = (q.nbatch > 1 && !(C_case & 1)) || (q.channels > 1 && !(C_case & 2));
+    q.alpha = scale * (backward ? mult : 1.0f);
+    if (!backward) {
+        q.mode = tc::EPI_ASSIGN;
+        if (c_reduces) return MLE_ERR_UNSUPPORTED;  // racing assignments in the reference
+    } else {
+        q.mode = c_reduces ? tc::EPI_ATOMIC : tc::EPI_ACCUM;
+    }
+    // A reduction over batch rows that are contiguous in both operands folds
+    // into K: C[m,p] += sum_z A_z^T B_z with A,B [z][n][*] row-major is one
+    // GEMM with K = z*n (the Linear dW case of Engine/engine.cu:3558).
+    if (backward && variant == MLE_GEMM_ATB && C_case == 0 && A_case == 3 && B_case == 3) {
+        q.K = (int)((int64_t)batch * channels * n);
+        q.nbatch = 1;
+        q.channels = 1;
+        q.a_sb = q.a_sc = q.b_sb = q.b_sc = q.c_sb = q.c_sc = 0;
+        q.mode = tc::EPI_ACCUM;
+        q.alpha = scale;
+        return run_gemm(q, as_stream(stream));
+    }
+    // Broadcast B with full A and C folds the batch into M (Linear forward /
+    // dX: Engine/engine.cu:3538,3552).
+    if (!a_t && A_case == 3 && B_case == 0 && C_case == 3) {
+        q.M = (int)((int64_t)batch * channels * m);
+        q.nbatch = 1;
+        q.channels = 1;
+        q.a_sb = q.a_sc = q.b_sb = q.b_sc = q.c_sb = q.c_sc = 0;
+        q.mode = backward ? tc::EPI_ACCUM : tc::EPI_ASSIGN;
+        q.alpha = scale;
+        return run_gemm(q, as_stream(stream));
+    }
+    return run_gemm(q, as_stream(stream));
+}
+
+int mle_linear_fwd(const float* X, const float* W, const float* bias, float* Y, int64_t rows, int in_features,
+                   int out_features, mle_stream_t stream) {
+    if (!X || !W || !Y || rows < 0 || in_features <= 0 || out_features <= 0) return MLE_ERR_ARG;
+    if (rows == 0) return MLE_OK;
+    return mle_gemm(X, W, Y, bias, 1, rows, out_features, in_features, in_features, out_features, out_features, 0, 0, 0,
+                    0, 0, 1.0f, 0.0f, stream);
+}
+
+int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, float* dW, float* dB, int64_t rows,
+                   int in_features, int out_features, mle_stream_t stream) {
+    if (!X || !W || !dY || !dW || rows < 0 || in_features <= 0 || out_features <= 0) return MLE_ERR_ARG;
+    if (rows == 0) return MLE_OK;
+    int s;
+    if (dX) {
+        // dX[rows, in] += dY[rows, out] * W[in, out]^T
+        s = mle_gemm(dY, W, dX, nullptr, 1, rows, in_features, out_features, out_features, out_features, in_features, 0,
+                     0, 0, 0, 1, 1.0f, 1.0f, stream);
+        if (s) return s;
+    }
+    // dW[in, out] += X[rows, in]^T * dY[rows, out]
+    s = mle_gemm(X, dY, dW, nullptr, 1, in_features, out_features, rows, in_features, out_features, out_features, 0, 0,
+                 0, 1, 0, 1.0f, 1.0f, stream);
+    if (s) return s;
+    if (dB) return mle_bias_grad(dY, dB, rows, out_features, 1.0f, stream);
+    return MLE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,228 @@
+"""Python face of the sm_100a kernels (include/mle_kernels.h).
+
+Thin wrappers over the C ABI for torch CUDA tensors: every function checks
+dtype/contiguity/device, passes raw pointers and the current torch stream,
+and raises MLEError on a non-zero status.  Argument names and the
+accumulate/assign behaviour follow the reference kernels each entry point
+replaces (cited in the header).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import MLEError, kernels, mle_param_view
+
+RELU, LEAKY_RELU, SILU, TANH, GELU, SIGMOID = range(6)
+GEMM_AB, GEMM_ABT, GEMM_ATB, GEMM_ATBT = range(4)
+
+
+def _p(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise MLEError("ml_engine_b200 kernels need CUDA tensors")
+    if t.dtype not in (torch.float32, torch.int32, torch.float64):
+        raise MLEError(f"unsupported dtype {t.dtype}")
+    if not t.is_contiguous():
+        raise MLEError("ml_engine_b200 kernels need contiguous tensors")
+    return t.data_ptr()
+
+
+def _s():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _call(name, *args):
+    kernels().call(name, *args)
+
+
+def fill(x, value):
+    _call("mle_fill", _p(x), value, x.numel(), _s())
+
+
+def copy(x, y):
+    _call("mle_copy", _p(x), _p(y), x.numel(), _s())
+
+
+def accumulate(x, y, scale=1.0):
+    _call("mle_accumulate", _p(x), _p(y), y.numel(), scale, _s())
+
+
+def add_bwd(g, ga, gb):
+    _call("mle_add_bwd", _p(g), _p(ga), _p(gb), g.numel(), _s())
+
+
+def scale_write(x, y, scale):
+    _call("mle_scale_write", _p(x), _p(y), x.numel(), scale, _s())
+
+
+def scale_add(x, y, z, scale):
+    _call("mle_scale_add", _p(x), _p(y), _p(z), scale, x.numel(), _s())
+
+
+def act_fwd(kind, x, y):
+    _call("mle_act_fwd", kind, _p(x), _p(y), x.numel(), _s())
+
+
+def act_bwd(kind, x, gy, gx, bias_grad=None):
+    cols = bias_grad.numel() if bias_grad is not None else 0
+    rows = x.numel() // cols if cols else 0
+    _call("mle_act_bwd", kind, _p(x), _p(gy), _p(gx), x.numel(), _p(bias_grad), rows, cols, _s())
+
+
+def bias_add_fwd(x, bias, y):
+    _call("mle_bias_add_fwd", _p(x), _p(bias), _p(y), x.numel() // bias.numel(), bias.numel(), _s())
+
+
+def bias_grad(g, db, scale=1.0):
+    _call("mle_bias_grad", _p(g), _p(db), g.numel() // db.numel(), db.numel(), scale, _s())
+
+
+def channel_bias_fwd(x, b, y, batch, channels, spatial):
+    _call("mle_channel_bias_fwd", _p(x), _p(b), _p(y), batch, channels, spatial, _s())
+
+
+def channel_bias_bwd(g, gx, gb, batch, channels, spatial):
+    _call("mle_channel_bias_bwd", _p(g), _p(gx), _p(gb), batch, channels, spatial, _s())
+
+
+def matpe_fwd(x, y, batch, rows, cols, start_idx=0):
+    _call("mle_matpe_fwd", _p(x), _p(y), batch, rows, cols, start_idx, _s())
+
+
+def timestep_pe(y, t):
+    _call("mle_timestep_pe", _p(y), t, y.numel(), _s())
+
+
+def headify(inp, out, batch, heads, seq, head_dim, flag):
+    _call("mle_headify", _p(inp), _p(out), batch, heads, seq, head_dim, flag, _s())
+
+
+def channel_concat(a, b, c, batch, c1, c2, spatial):
+    _call("mle_channel_concat", _p(a), _p(b), _p(c), batch, c1, c2, spatial, _s())
+
+
+def channel_split(ga, gb, gc, batch, c1, c2, spatial):
+    _call("mle_channel_split", _p(ga), _p(gb), _p(gc), batch, c1, c2, spatial, _s())
+
+
+def embedding_gather(keys, table, out):
+    _call("mle_embedding_gather", _p(keys), _p(table), _p(out), keys.numel(), table.shape[-1], _s())
+
+
+def one_hot(keys, out, vocab):
+    _call("mle_one_hot", _p(keys), _p(out), keys.numel(), vocab, _s())
+
+
+def layernorm_fwd(x, y, mean, sqdev, batch, channels, row, col, eps=1e-5):
+    _call("mle_layernorm_fwd", _p(x), _p(y), _p(mean), _p(sqdev), batch, channels, row, col, eps, _s())
+
+
+def layernorm_bwd(y, gy, sqdev, gx, batch, channels, row, col, eps=1e-5):
+    _call("mle_layernorm_bwd", _p(y), _p(gy), _p(sqdev), _p(gx), batch, channels, row, col, eps, _s())
+
+
+def groupnorm_fwd(x, y, mean, sqdev, batch, channels, groups, row, col, eps=1e-5):
+    _call("mle_groupnorm_fwd", _p(x), _p(y), _p(mean), _p(sqdev), batch, channels, groups, row, col, eps, _s())
+
+
+def groupnorm_bwd(y, gy, sqdev, gx, batch, channels, groups, row, col, eps=1e-5):
+    _call("mle_groupnorm_bwd", _p(y), _p(gy), _p(sqdev), _p(gx), batch, channels, groups, row, col, eps, _s())
+
+
+def softmax_fwd(x, y, bc, rows, cols, axis, causal=0):
+    _call("mle_softmax_fwd", _p(x), _p(y), bc, rows, cols, axis, causal, _s())
+
+
+def softmax_bwd(y, gy, gx, bc, rows, cols, axis):
+    _call("mle_softmax_bwd", _p(y), _p(gy), _p(gx), bc, rows, cols, axis, _s())
+
+
+def softmax_ce_fwd(logits, target, probs, loss, grad, batch_div, rows, cols):
+    _call("mle_softmax_ce_fwd", _p(logits), _p(target), _p(probs), _p(loss), _p(grad), batch_div, rows, cols, _s())
+
+
+def softmax_ce_bwd(probs, target, grad, batch_div, upstream=None):
+    _call("mle_softmax_ce_bwd", _p(probs), _p(target), _p(upstream), _p(grad), batch_div, probs.numel(), _s())
+
+
+def mse_fwd(x, target, loss):
+    _call("mle_mse_fwd", _p(x), _p(target), _p(loss), x.numel(), _s())
+
+
+def mse_bwd(x, target, gx, upstream=None):
+    _call("mle_mse_bwd", _p(x), _p(target), _p(upstream), _p(gx), x.numel(), _s())
+
+
+def bcmm(variant, A, B, C, batch, channels, m, n, p, backward, A_case, B_case, C_case, scale=1.0):
+    _call("mle_bcmm", variant, _p(A), _p(B), _p(C), batch, channels, m, n, p, backward, A_case, B_case, C_case,
+          scale, _s())
+
+
+def gemm(A, B, C, M, N, K, trans_a=0, trans_b=0, alpha=1.0, beta=0.0, bias=None, batch=1, lda=None, ldb=None,
+         ldc=None, stride_a=0, stride_b=0, stride_c=0):
+    lda = lda if lda is not None else (M if trans_a else K)
+    ldb = ldb if ldb is not None else (K if trans_b else N)
+    ldc = ldc if ldc is not None else N
+    _call("mle_gemm", _p(A), _p(B), _p(C), _p(bias), batch, M, N, K, lda, ldb, ldc, stride_a, stride_b, stride_c,
+          trans_a, trans_b, alpha, beta, _s())
+
+
+def linear_fwd(X, W, bias, Y, rows, in_features, out_features):
+    _call("mle_linear_fwd", _p(X), _p(W), _p(bias), _p(Y), rows, in_features, out_features, _s())
+
+
+def linear_bwd(X, W, dY, dX, dW, dB, rows, in_features, out_features):
+    _call("mle_linear_bwd", _p(X), _p(W), _p(dY), _p(dX), _p(dW), _p(dB), rows, in_features, out_features, _s())
+
+
+KEYGRAD_REFERENCE, KEYGRAD_TRUE = 0, 1
+
+
+def attention_bwd(Q, K, V, P, dO, dQ, dK, dV, dP, dS, batch, heads, seq_q, seq_k, head_dim, scale, causal=0,
+                  softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE):
+    _call("mle_attention_bwd", _p(Q), _p(K), _p(V), _p(P), _p(dO), _p(dQ), _p(dK), _p(dV), _p(dP), _p(dS), batch,
+          heads, seq_q, seq_k, head_dim, scale, causal, softmax_axis, key_grad_mode, _s())
+
+
+def param_views(params):
+    """params: list of dicts with w, g, m, v (float32 CUDA tensors), t (int32
+    CUDA tensor of one element) and optional b1, b2, eps, weight_decay."""
+    arr = (mle_param_view * len(params))()
+    for i, p in enumerate(params):
+        arr[i].w, arr[i].g, arr[i].m, arr[i].v = _p(p["w"]), _p(p["g"]), _p(p["m"]), _p(p["v"])
+        arr[i].n = p["w"].numel()
+        arr[i].t = _p(p["t"])
+        arr[i].b1 = p.get("b1", 0.9)
+        arr[i].b2 = p.get("b2", 0.999)
+        arr[i].eps = p.get("eps", 1e-8)
+        arr[i].weight_decay = p.get("weight_decay", 0.01)
+    return arr
+
+
+def grad_sumsq(params, norm_ws, scale=1.0):
+    views = param_views(params)
+    _call("mle_grad_sumsq", ctypes.cast(views, ctypes.c_void_p), len(params), _p(norm_ws), scale, _s())
+
+
+def clip_finalize(norm_ws, max_norm=1.0):
+    _call("mle_clip_finalize", _p(norm_ws), max_norm, _s())
+
+
+def clip_apply(params, norm_ws):
+    views = param_views(params)
+    _call("mle_clip_apply", ctypes.cast(views, ctypes.c_void_p), len(params), _p(norm_ws), _s())
+
+
+def adam_update(params, lr, adamw=True, clip_ws=None, pre_scale=1.0, write_back_grad=True):
+    views = param_views(params)
+    _call("mle_adam_update", ctypes.cast(views, ctypes.c_void_p), len(params), _p(clip_ws), pre_scale, lr,
+          int(adamw), int(write_back_grad), _s())
+
+
+def watchdog():
+    flag = ctypes.c_int(0)
+    _call("mle_watchdog_read", ctypes.addressof(flag), _s())
+    return flag.value

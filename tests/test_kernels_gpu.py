@@ -1,0 +1,455 @@
+"""Parity of every sm_100a kernel (C ABI, include/mle_kernels.h) with the CPU
+oracle on seeded inputs, including ragged, unaligned and edge sizes.
+
+Tolerances (see conftest): 1e-5 for elementwise / reduction / Adam paths,
+2e-3 per tensor for the TF32 tensor-core GEMMs.
+"""
+import numpy as np
+import pytest
+
+from conftest import RTOL_EXACT, RTOL_TC, rel_err
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def T(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def H(t):
+    torch.cuda.synchronize()
+    return t.detach().cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from ml_engine_b200 import ops as o
+    return o
+
+
+@pytest.fixture(scope="module")
+def orc():
+    from oracle import ops as o
+    return o
+
+
+# ---------------------------------------------------------------- elementwise
+@pytest.mark.parametrize("n", [1, 7, 1024, 4099, 1 << 20])
+def test_glue_ops(cuda, ops, orc, rng, n):
+    x = rng.standard_normal(n).astype(np.float32)
+    y = rng.standard_normal(n).astype(np.float32)
+    gx, gy = T(x, cuda), T(y, cuda)
+    out = torch.empty_like(gx)
+    ops.fill(out, 3.5)
+    assert np.all(H(out) == 3.5)
+    ops.copy(gx, out)
+    assert np.array_equal(H(out), x)
+    acc = gy.clone()
+    ops.accumulate(gx, acc, 0.125)
+    assert rel_err(H(acc), orc.accumulate(x, y.copy(), 0.125)) <= 1e-7
+    ops.scale_write(gx, out, 0.3)
+    assert np.array_equal(H(out), orc.scale_write(x, 0.3))
+    ops.scale_add(gx, gy, out, -1.0)
+    assert np.array_equal(H(out), orc.scale_add(x, y, -1.0))
+    a, b = gy.clone(), gx.clone()
+    ops.add_bwd(gx, a, b)
+    assert np.array_equal(H(a), y + x) and np.array_equal(H(b), x + x)
+
+
+def test_unaligned_pointers(cuda, ops, orc, rng):
+    """Views starting one element in take the scalar path."""
+    x = rng.standard_normal(1001).astype(np.float32)
+    base = T(x, cuda)
+    v = base[1:]
+    out = torch.zeros(1000, device=cuda)[0:]
+    out2 = torch.zeros(1001, device=cuda)[1:]
+    ops.act_fwd(ops.GELU, v, out2)
+    assert rel_err(H(out2), orc.act_fwd(4, x[1:])) <= RTOL_EXACT
+    ops.copy(v, out)
+    assert np.array_equal(H(out), x[1:])
+
+
+@pytest.mark.parametrize("kind", range(6))
+def test_activation_fwd_bwd(cuda, ops, orc, rng, kind):
+    n = 3 * 1024 + 5
+    x = (rng.standard_normal(n) * 3).astype(np.float32)
+    g = rng.standard_normal(n).astype(np.float32)
+    gx0 = rng.standard_normal(n).astype(np.float32)
+    y = torch.empty(n, device=cuda)
+    ops.act_fwd(kind, T(x, cuda), y)
+    assert rel_err(H(y), orc.act_fwd(kind, x)) <= RTOL_EXACT
+    gx = T(gx0, cuda)
+    ops.act_bwd(kind, T(x, cuda), T(g, cuda), gx)
+    assert rel_err(H(gx), orc.act_bwd(kind, x, g, gx0.copy())) <= RTOL_EXACT
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 256), (4096, 1024), (33, 10), (5, 1027)])
+def test_activation_bwd_fused_bias(cuda, ops, orc, rng, rows, cols):
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    g = rng.standard_normal((rows, cols)).astype(np.float32)
+    gx0 = np.zeros((rows, cols), np.float32)
+    db0 = rng.standard_normal(cols).astype(np.float32)
+    gx, db = T(gx0, cuda), T(db0, cuda)
+    ops.act_bwd(ops.GELU, T(x, cuda), T(g, cuda), gx, bias_grad=db)
+    ref_gx = orc.act_bwd(4, x, g, gx0.copy())
+    ref_db = orc.bias_grad(ref_gx, db0.copy())
+    assert rel_err(H(gx), ref_gx) <= RTOL_EXACT
+    assert rel_err(H(db), ref_db) <= 1e-4  # column sums over up to 4096 rows, reordered
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 256), (1000, 10), (7, 4096)])
+def test_bias_add_and_grad(cuda, ops, orc, rng, rows, cols):
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    b = rng.standard_normal(cols).astype(np.float32)
+    y = torch.empty(rows, cols, device=cuda)
+    ops.bias_add_fwd(T(x, cuda), T(b, cuda), y)
+    assert np.array_equal(H(y), orc.bias_add(x, b))
+    db0 = rng.standard_normal(cols).astype(np.float32)
+    db = T(db0, cuda)
+    ops.bias_grad(T(x, cuda), db)
+    assert rel_err(H(db), orc.bias_grad(x, db0.copy())) <= 1e-5 * max(1, rows / 64)
+
+
+def test_channel_bias(cuda, ops, orc, rng):
+    B, C, S = 4, 6, 35
+    x = rng.standard_normal(B * C * S).astype(np.float32)
+    b = rng.standard_normal(C).astype(np.float32)
+    y = torch.empty(B * C * S, device=cuda)
+    ops.channel_bias_fwd(T(x, cuda), T(b, cuda), y, B, C, S)
+    assert np.array_equal(H(y), orc.channel_bias_fwd(x, b, B, C, S))
+    gx0 = rng.standard_normal(B * C * S).astype(np.float32)
+    gb0 = rng.standard_normal(C).astype(np.float32)
+    gx, gb = T(gx0, cuda), T(gb0, cuda)
+    ops.channel_bias_bwd(T(x, cuda), gx, gb, B, C, S)
+    rgx, rgb = gx0.copy(), gb0.copy()
+    orc.channel_bias_bwd(x, rgx, rgb, B, C, S)
+    assert np.array_equal(H(gx), rgx)
+    assert rel_err(H(gb), rgb) <= RTOL_EXACT
+
+
+@pytest.mark.parametrize("flag", [0, 1, 2, 3])
+def test_headify(cuda, ops, orc, rng, flag):
+    B, Hh, S, D = 3, 4, 5, 8
+    n = B * Hh * S * D
+    inp = rng.standard_normal(n).astype(np.float32)
+    out0 = rng.standard_normal(n).astype(np.float32)
+    out = T(out0, cuda)
+    ops.headify(T(inp, cuda), out, B, Hh, S, D, flag)
+    assert np.array_equal(H(out), orc.headify(inp, out0.copy(), B, Hh, S, D, flag))
+
+
+def test_matpe(cuda, ops, orc, rng):
+    B, S, D = 2, 17, 24
+    x = rng.standard_normal(B * S * D).astype(np.float32)
+    y = torch.empty(B * S * D, device=cuda)
+    ops.matpe_fwd(T(x, cuda), y, B, S, D, 3)
+    assert rel_err(H(y), orc.matpe(x, B, S, D, 3)) <= RTOL_EXACT
+
+
+# -------------------------------------------------------------- normalisation
+@pytest.mark.parametrize("batch,channels,row,col", [(64, 1, 1, 256), (33, 1, 1, 1000), (7, 1, 4, 1024),
+                                                    (5, 1, 1, 8192), (4, 3, 5, 8)])
+def test_layernorm(cuda, ops, orc, rng, batch, channels, row, col):
+    n = batch * channels * row * col
+    x = (rng.standard_normal(n) * 2 + 0.5).astype(np.float32)
+    gy = rng.standard_normal(n).astype(np.float32)
+    y, mean, sq = torch.empty(n, device=cuda), torch.empty(batch, device=cuda), torch.empty(batch, device=cuda)
+    ops.layernorm_fwd(T(x, cuda), y, mean, sq, batch, channels, row, col)
+    ry, rmean, rsq = orc.layernorm_fwd(x, batch, channels, row, col)
+    assert rel_err(H(y), ry) <= RTOL_EXACT
+    assert rel_err(H(sq), rsq) <= RTOL_EXACT
+    gx0 = rng.standard_normal(n).astype(np.float32)
+    gx = T(gx0, cuda)
+    ops.layernorm_bwd(y, T(gy, cuda), sq, gx, batch, channels, row, col)
+    assert rel_err(H(gx), orc.layernorm_bwd(ry, gy, rsq, gx0.copy(), batch, channels, row, col)) <= RTOL_EXACT
+
+
+@pytest.mark.parametrize("batch,channels,groups,row,col", [(4, 64, 8, 16, 16), (2, 24, 8, 3, 5)])
+def test_groupnorm(cuda, ops, orc, rng, batch, channels, groups, row, col):
+    n = batch * channels * row * col
+    x = (rng.standard_normal(n) * 2 + 0.5).astype(np.float32)
+    gy = rng.standard_normal(n).astype(np.float32)
+    y = torch.empty(n, device=cuda)
+    mean, sq = torch.empty(batch * groups, device=cuda), torch.empty(batch * groups, device=cuda)
+    ops.groupnorm_fwd(T(x, cuda), y, mean, sq, batch, channels, groups, row, col)
+    ry, _, rsq = orc.groupnorm_fwd(x, batch, channels, groups, row, col)
+    assert rel_err(H(y), ry) <= RTOL_EXACT
+    gx0 = rng.standard_normal(n).astype(np.float32)
+    gx = T(gx0, cuda)
+    ops.groupnorm_bwd(y, T(gy, cuda), sq, gx, batch, channels, groups, row, col)
+    assert rel_err(H(gx), orc.groupnorm_bwd(ry, gy, rsq, gx0.copy(), batch, channels, groups, row, col)) <= RTOL_EXACT
+
+
+# --------------------------------------------------------- softmax and losses
+@pytest.mark.parametrize("axis,causal", [(0, 0), (1, 0), (1, 1), (0, 1)])
+@pytest.mark.parametrize("bc,rows,cols", [(6, 128, 128), (3, 17, 33), (2, 5, 4096)])
+def test_softmax(cuda, ops, orc, rng, axis, causal, bc, rows, cols):
+    n = bc * rows * cols
+    x = (rng.standard_normal(n) * 3).astype(np.float32)
+    y = torch.empty(n, device=cuda)
+    ops.softmax_fwd(T(x, cuda), y, bc, rows, cols, axis, causal)
+    ry = orc.softmax_fwd(x, bc, rows, cols, axis, causal)
+    assert rel_err(H(y), ry) <= RTOL_EXACT
+    gy = rng.standard_normal(n).astype(np.float32)
+    gx0 = rng.standard_normal(n).astype(np.float32)
+    gx = T(gx0, cuda)
+    ops.softmax_bwd(y, T(gy, cuda), gx, bc, rows, cols, axis)
+    assert rel_err(H(gx), orc.softmax_bwd(ry, gy, gx0.copy(), bc, rows, cols, axis)) <= RTOL_EXACT
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 10), (256, 4096), (3, 8192 + 4), (9, 1001)])
+def test_softmax_cross_entropy(cuda, ops, orc, rng, rows, cols):
+    logits = (rng.standard_normal((rows, cols)) * 2).astype(np.float32)
+    labels = rng.integers(0, cols, rows)
+    target = np.zeros((rows, cols), np.float32)
+    target[np.arange(rows), labels] = 1.0
+    probs = torch.empty(rows, cols, device=cuda)
+    grad = torch.empty(rows, cols, device=cuda)
+    loss = torch.empty(1, device=cuda)
+    batch = 4.0
+    ops.softmax_ce_fwd(T(logits, cuda), T(target, cuda), probs, loss, grad, batch, rows, cols)
+    rp, rloss = orc.smce_fwd(logits, target, rows, cols)
+    assert rel_err(H(probs), rp) <= RTOL_EXACT
+    assert abs(float(H(loss)[0]) - rloss) <= RTOL_EXACT * abs(rloss)
+    assert rel_err(H(grad), orc.smce_bwd(rp, target, batch)) <= RTOL_EXACT
+    g2 = torch.empty(rows, cols, device=cuda)
+    ops.softmax_ce_bwd(probs, T(target, cuda), g2, batch)
+    assert rel_err(H(g2), orc.smce_bwd(rp, target, batch)) <= RTOL_EXACT
+
+
+def test_mse(cuda, ops, orc, rng):
+    n = 32 * 3 * 64 * 64
+    x = rng.standard_normal(n).astype(np.float32)
+    t = rng.standard_normal(n).astype(np.float32)
+    loss = torch.empty(1, device=cuda)
+    ops.mse_fwd(T(x, cuda), T(t, cuda), loss)
+    assert abs(float(H(loss)[0]) - orc.mse_fwd(x, t)) <= 1e-5 * orc.mse_fwd(x, t)
+    gx0 = rng.standard_normal(n).astype(np.float32)
+    gx = T(gx0, cuda)
+    ops.mse_bwd(T(x, cuda), T(t, cuda), gx)
+    assert rel_err(H(gx), orc.mse_bwd(x, t, gx0.copy())) <= RTOL_EXACT
+
+
+# ----------------------------------------------------------------------- GEMM
+GEMM_SHAPES = [(128, 128, 32), (256, 512, 384), (200, 130, 70), (64, 256, 784), (784, 256, 64), (1000, 96, 8),
+               (4096, 256, 256), (256, 256, 4096), (33, 1024, 129)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+def test_gemm_tf32(cuda, ops, orc, rng, M, N, K, ta, tb, beta):
+    A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    C = T(C0, cuda)
+    ops.gemm(T(A, cuda), T(B, cuda), C, M, N, K, ta, tb, alpha=0.5, beta=beta)
+    ref = C0.copy() if beta else np.zeros_like(C0)
+    prod = np.zeros((M, N), np.float32)
+    orc.gemm(A, B, prod, M, N, K, ta, tb)
+    ref = ref + 0.5 * prod
+    # relative to the product's scale: C0 can dominate the sum
+    err = np.max(np.abs(H(C) - ref)) / max(np.max(np.abs(0.5 * prod)), 1e-30)
+    assert err <= RTOL_TC, err
+
+
+def test_gemm_fallback_exact(cuda, ops, orc, rng):
+    """N = 10 (MNIST logits) has a 40-byte row stride: CUDA-core path, fp32."""
+    M, N, K = 64, 10, 256
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    C = torch.empty(M, N, device=cuda)
+    ops.gemm(T(A, cuda), T(B, cuda), C, M, N, K)
+    prod = np.zeros((M, N), np.float32)
+    orc.gemm(A, B, prod, M, N, K)
+    assert rel_err(H(C), prod) <= RTOL_EXACT
+
+
+def test_gemm_bias_and_batch(cuda, ops, orc, rng):
+    batch, M, N, K = 3, 130, 96, 40
+    A = rng.standard_normal((batch, M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)  # broadcast over batch
+    bias = rng.standard_normal(N).astype(np.float32)
+    C = torch.empty(batch, M, N, device=cuda)
+    ops.gemm(T(A, cuda), T(B, cuda), C, M, N, K, bias=T(bias, cuda), batch=batch, stride_a=M * K, stride_b=0,
+             stride_c=M * N)
+    for b in range(batch):
+        prod = np.zeros((M, N), np.float32)
+        orc.gemm(A[b].copy(), B, prod, M, N, K)
+        assert rel_err(H(C)[b], prod + bias) <= RTOL_TC
+
+
+BCMM_CASES = [
+    # variant, batch, channels, m, n, p, backward, A_case, B_case, C_case
+    (0, 4, 1, 128, 64, 96, 0, 3, 0, 3),    # Linear forward (W broadcast)
+    (1, 4, 1, 128, 96, 64, 1, 3, 0, 3),    # Linear dX
+    (2, 4, 1, 64, 128, 96, 1, 3, 3, 0),    # Linear dW (batch reduction folded into K)
+    (1, 2, 8, 128, 32, 128, 0, 3, 3, 3),   # attention scores Q K^T
+    (0, 2, 8, 128, 128, 32, 0, 3, 3, 3),   # P V
+    (3, 2, 8, 32, 128, 128, 1, 3, 3, 3),   # bcmmT (BMMABT dK)
+    (2, 2, 3, 40, 50, 60, 1, 1, 3, 2),     # mixed broadcast with C reduction over batch
+    (0, 3, 2, 20, 30, 10, 1, 0, 0, 0),     # everything broadcast: product counted batch*channels times
+]
+
+
+@pytest.mark.parametrize("case", BCMM_CASES)
+def test_bcmm_broadcast_semantics(cuda, ops, orc, rng, case):
+    variant, batch, ch, m, n, p, bwd, ac, bc, cc = case
+
+    def size(flag, inner):
+        return (batch if flag & 1 else 1) * (ch if flag & 2 else 1) * inner
+
+    A = rng.standard_normal(size(ac, m * n)).astype(np.float32)
+    B = rng.standard_normal(size(bc, n * p)).astype(np.float32)
+    C0 = rng.standard_normal(size(cc, m * p)).astype(np.float32) if bwd else np.zeros(size(cc, m * p), np.float32)
+    C = T(C0, cuda)
+    ops.bcmm(variant, T(A, cuda), T(B, cuda), C, batch, ch, m, n, p, bwd, ac, bc, cc, 0.75)
+    ref = orc.bcmm(variant, A, B, C0.copy(), batch, ch, m, n, p, bwd, ac, bc, cc, 0.75)
+    delta = ref - C0 if bwd else ref
+    err = np.max(np.abs(H(C) - ref)) / max(np.max(np.abs(delta)), 1e-30)
+    assert err <= RTOL_TC, err
+
+
+@pytest.mark.parametrize("rows,fin,fout", [(64, 784, 256), (4096, 256, 1024), (4096, 1024, 256), (100, 40, 72)])
+def test_linear_fwd_bwd(cuda, ops, orc, rng, rows, fin, fout):
+    X = rng.random((rows, fin)).astype(np.float32)
+    W = (rng.standard_normal((fin, fout)) * np.sqrt(2.0 / fin)).astype(np.float32)
+    b = rng.standard_normal(fout).astype(np.float32) * 0.1
+    Y = torch.empty(rows, fout, device=cuda)
+    ops.linear_fwd(T(X, cuda), T(W, cuda), T(b, cuda), Y, rows, fin, fout)
+    ry = np.zeros((rows, fout), np.float32)
+    orc.gemm(X, W, ry, rows, fout, fin)
+    ry = orc.bias_add(ry, b)
+    assert rel_err(H(Y), ry) <= RTOL_TC
+    dY = rng.standard_normal((rows, fout)).astype(np.float32)
+    dX0 = rng.standard_normal((rows, fin)).astype(np.float32)
+    dX, dW, dB = T(dX0, cuda), torch.zeros(fin, fout, device=cuda), torch.zeros(fout, device=cuda)
+    ops.linear_bwd(T(X, cuda), T(W, cuda), T(dY, cuda), dX, dW, dB, rows, fin, fout)
+    rdx = dX0.copy()
+    orc.gemm(dY, W, rdx, rows, fin, fout, 0, 1, accumulate=True)
+    rdw = np.zeros((fin, fout), np.float32)
+    orc.gemm(X, dY, rdw, fin, fout, rows, 1, 0)
+    rdb = orc.bias_grad(dY, np.zeros(fout, np.float32))
+    assert np.max(np.abs(H(dX) - rdx)) / np.max(np.abs(rdx - dX0)) <= RTOL_TC
+    assert rel_err(H(dW), rdw) <= RTOL_TC
+    assert rel_err(H(dB), rdb) <= 1e-4
+
+
+# ------------------------------------------------------------------ attention
+@pytest.mark.parametrize("key_mode", [0, 1])
+@pytest.mark.parametrize("B,Hh,Sq,Sk,D,axis,causal", [(2, 8, 128, 128, 32, 1, 0), (2, 4, 64, 64, 64, 1, 1),
+                                                     (1, 2, 40, 72, 16, 0, 0)])
+def test_attention_bwd(cuda, ops, orc, rng, B, Hh, Sq, Sk, D, axis, causal, key_mode):
+    bh = B * Hh
+    Q = rng.standard_normal((bh, Sq, D)).astype(np.float32)
+    K = rng.standard_normal((bh, Sk, D)).astype(np.float32)
+    V = rng.standard_normal((bh, Sk, D)).astype(np.float32)
+    dO = rng.standard_normal((bh, Sq, D)).astype(np.float32)
+    scale = 1.0 / np.sqrt(D)
+    S = np.zeros((bh, Sq, Sk), np.float32)
+    orc.bcmm(1, Q, K, S, B, Hh, Sq, D, Sk, 0, 3, 3, 3)
+    P = orc.softmax_fwd(orc.scale_write(S, scale), bh, Sq, Sk, axis, causal)
+    dQ, dK, dV = (torch.zeros(bh, s, D, device=cuda) for s in (Sq, Sk, Sk))
+    dP, dS = torch.zeros(bh, Sq, Sk, device=cuda), torch.zeros(bh, Sq, Sk, device=cuda)
+    ops.attention_bwd(T(Q, cuda), T(K, cuda), T(V, cuda), T(P, cuda), T(dO, cuda), dQ, dK, dV, dP, dS, B, Hh, Sq, Sk,
+                      D, float(scale), causal, axis, key_mode)
+    # reference chain (Engine/engine.cu:2246-2253, 2450-2455, 2540-2546, 2302-2309)
+    rdP = orc.bcmm(1, dO, V, np.zeros((bh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 1, 3, 3, 3)
+    rdV = orc.bcmm(2, P, dO, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
+    rdSc = orc.softmax_bwd(P, rdP, np.zeros_like(P), bh, Sq, Sk, axis)
+    rdS = orc.accumulate(rdSc, np.zeros_like(P), scale)
+    rdQ = orc.bcmm(0, rdS, K, np.zeros((bh, Sq, D), np.float32), B, Hh, Sq, Sk, D, 1, 3, 3, 3)
+    if key_mode == 0:  # bcmmT(Q, dScores, K.grad, hd, Sq, Sk): the reference's own call
+        rdK = orc.bcmm(3, Q, rdS, np.zeros((bh, Sk, D), np.float32), B, Hh, D, Sq, Sk, 1, 3, 3, 3)
+    else:              # the mathematical gradient dS^T Q
+        rdK = orc.bcmm(2, rdS, Q, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
+    assert rel_err(H(dP), rdP) <= RTOL_TC
+    assert rel_err(H(dV), rdV) <= RTOL_TC
+    assert rel_err(H(dS), rdSc) <= RTOL_TC
+    assert rel_err(H(dQ), rdQ) <= RTOL_TC
+    assert rel_err(H(dK), rdK) <= RTOL_TC
+
+
+# ------------------------------------------------------------------ optimizer
+def _make_params(rng, sizes, dev):
+    ps, host = [], []
+    for n in sizes:
+        w = (rng.standard_normal(n) * 0.02).astype(np.float32)
+        g = (rng.standard_normal(n) * 0.5).astype(np.float32)
+        m = (rng.standard_normal(n) * 0.01).astype(np.float32)
+        v = np.abs(rng.standard_normal(n) * 0.001).astype(np.float32)
+        host.append(dict(w=w, g=g, m=m, v=v))
+        ps.append(dict(w=T(w, dev), g=T(g, dev), m=T(m, dev), v=T(v, dev),
+                       t=torch.tensor([3], dtype=torch.int32, device=dev)))
+    return ps, host
+
+
+@pytest.mark.parametrize("adamw", [True, False])
+@pytest.mark.parametrize("clip", [True, False])
+def test_clip_adam_multi_tensor(cuda, ops, orc, rng, adamw, clip):
+    sizes = [784 * 256, 256, 2560, 10, 1, 5000, 4096 * 3 + 1]
+    ps, host = _make_params(rng, sizes, cuda)
+    ws = torch.zeros(1, dtype=torch.float64, device=cuda)
+    if clip:
+        ops.grad_sumsq(ps, ws)
+        ops.clip_finalize(ws)
+    ops.adam_update(ps, lr=1e-3, adamw=adamw, clip_ws=ws if clip else None)
+    acc = np.zeros(1, np.float64)
+    if clip:
+        for h in host:
+            orc.sumsq(acc, h["g"])
+        orc.clip_finalize(acc)
+        assert abs(H(ws)[0] - acc[0]) <= 1e-12 * acc[0]
+    for p, h in zip(ps, host):
+        g = h["g"].copy()
+        if clip:
+            orc.clip_apply(g, acc)
+        w, m, v = h["w"].copy(), h["m"].copy(), h["v"].copy()
+        orc.adam(w, g, m, v, 3, 1e-3, adamw)
+        assert rel_err(H(p["m"]), m) <= RTOL_EXACT
+        assert rel_err(H(p["v"]), v) <= RTOL_EXACT
+        assert rel_err(H(p["w"]), w) <= RTOL_EXACT
+        if clip:
+            assert rel_err(H(p["g"]), g) <= RTOL_EXACT
+        assert int(H(p["t"])[0]) == 4
+
+
+def test_clip_apply_and_nan(cuda, ops, orc, rng):
+    ps, host = _make_params(rng, [1000, 33], cuda)
+    ws = torch.zeros(1, dtype=torch.float64, device=cuda)
+    ops.grad_sumsq(ps, ws)
+    ops.clip_finalize(ws)
+    ops.clip_apply(ps, ws)
+    acc = np.zeros(1, np.float64)
+    for h in host:
+        orc.sumsq(acc, h["g"])
+    orc.clip_finalize(acc)
+    for p, h in zip(ps, host):
+        assert rel_err(H(p["g"]), orc.clip_apply(h["g"].copy(), acc)) <= RTOL_EXACT
+    nan_ws = torch.tensor([float("nan")], dtype=torch.float64, device=cuda)
+    ops.clip_finalize(nan_ws)
+    assert np.isnan(H(nan_ws)[0])
+
+
+def test_small_norm_is_not_scaled(cuda, ops, rng):
+    ps, _ = _make_params(rng, [10], cuda)
+    ps[0]["g"].mul_(1e-3)
+    ws = torch.zeros(1, dtype=torch.float64, device=cuda)
+    ops.grad_sumsq(ps, ws)
+    ops.clip_finalize(ws)
+    assert H(ws)[0] == 1.0
+
+
+def test_argument_errors(cuda, ops):
+    from ml_engine_b200 import MLEError
+    x = torch.zeros(4, device=cuda)
+    with pytest.raises(MLEError):
+        ops.act_fwd(17, x, x)
+    with pytest.raises(MLEError):
+        ops.gemm(x, x, x, 2, 2, 2, beta=0.5)
+
+
+def test_watchdog_clear(cuda, ops):
+    assert ops.watchdog() == 0
