@@ -48,6 +48,7 @@ typedef struct mle_session_desc {
     int adamw;
     float clip_norm;     /* <= 0 disables the clip */
     uint64_t seed;
+    int gemm_mode;       /* MLE_GEMM_MODE_TF32 or MLE_GEMM_MODE_FP32 for every GEMM of the step */
 } mle_session_desc;
 
 /* Builds the graph and allocates everything the step needs. */
@@ -74,9 +75,14 @@ int mle_session_step(mle_session_t s, int upload, float* loss_out);
  * 2 backward, 3 data-parallel gradient reduction, 4 clip, 5 update. */
 int mle_session_phase(mle_session_t s, int phase);
 
-/* Captures the whole step (with the input upload and loss download) into a
- * CUDA graph; later mle_session_step calls replay it. */
+/* Captures the whole step into two CUDA graphs, one device-resident and one
+ * that also uploads the inputs and downloads the loss; later
+ * mle_session_step calls replay the one matching `upload`. */
 int mle_session_capture(mle_session_t s);
+
+/* Kernel, memset and memcpy nodes of the captured device-resident step
+ * (the launches one replay issues). */
+int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* copies);
 
 int mle_session_sync(mle_session_t s);
 

@@ -254,6 +254,17 @@ int mle_mse_bwd(const float* x, const float* target, const float* upstream, floa
 /* tensor-core GEMM (tcgen05 kind::tf32, TMEM accumulator, TMA operands) */
 /* ------------------------------------------------------------------ */
 
+/* How the GEMM entry points below multiply, per host thread:
+ *   MLE_GEMM_MODE_TF32: tcgen05 kind::tf32 tensor cores with fp32
+ *     accumulation wherever TMA can describe the operands (default);
+ *   MLE_GEMM_MODE_FP32: CUDA-core fp32 FMA chains in k order, the
+ *     reference's own product arithmetic (for graphs whose forward feeds a
+ *     discontinuous derivative, e.g. ReLU masks, where TF32 rounding of a
+ *     pre-activation near zero flips the mask). */
+enum mle_gemm_mode { MLE_GEMM_MODE_TF32 = 0, MLE_GEMM_MODE_FP32 = 1 };
+int mle_set_gemm_mode(int mode);
+int mle_get_gemm_mode(void);
+
 /* Batched GEMM with the reference's broadcast flags.  Same argument meaning
  * as bcmm/bcmmABT/bcmmATB/bcmmT (Engine/kernels.cu:387-539): `backward`!=0
  * adds scale*product into C (the reference's atomicAdd), 0 assigns it.
@@ -302,22 +313,51 @@ int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, f
  *   MLE_KEYGRAD_TRUE: dK += scale * dS^T Q, the mathematical gradient. */
 enum mle_keygrad_mode { MLE_KEYGRAD_REFERENCE = 0, MLE_KEYGRAD_TRUE = 1 };
 
-/* Backward of the attention sub-graph built by MultiHeadAttention::forward /
- * cross_forward (Engine/transformer.cu:647-675):
- *   S = Q K^T, Ssc = scale*S, P = softmax_axis(Ssc) [masked], O = P V.
- * Inputs are [B,H,Sq,hd] (Q, dO), [B,H,Sk,hd] (K, V) and P [B,H,Sq,Sk].
- * Accumulates dQ, dK, dV (+=); dP_out receives (+=) the softmax node's
- * gradient dO V^T and dS_out (+=) the Scale node's gradient (the softmax
- * backward), both [B,H,Sq,Sk] as the reference keeps them in node->grad.
- * softmax_axis 1 is the reference's column-wise softmax.  Replaces
- * bcmmABT/bcmmATB (BMM bwd), deriv_softmax, Accumulate (Scale bwd) and
- * bcmm/bcmmT (BMMABT bwd) (Engine/engine.cu:2246-2253,2302-2309,2450-2455,
- * 2488-2493,2540-2546). */
+/* Layout of Q, K, V, O and their gradients in the attention entry points:
+ *   MLE_ATTN_HEAD_MAJOR : [B, H, S, hd] (the Headify nodes' tensors);
+ *   MLE_ATTN_TOKEN_MAJOR: [B, S, H*hd] (the q/k/v Linear outputs and the
+ *                         DeHeadify output), so no head copies are needed.
+ * P and the score gradients are always [B, H, Sq, Sk]. */
+enum mle_attn_layout { MLE_ATTN_HEAD_MAJOR = 0, MLE_ATTN_TOKEN_MAJOR = 1 };
+
+/* Forward of the attention sub-graph built by MultiHeadAttention::forward /
+ * cross_forward (Engine/transformer.cu:647-675): P = softmax_axis(scale *
+ * Q K^T) [causal: entries with key > query zeroed before normalising],
+ * O = P V (assigned).  Replaces bcmmABT (BMMABT), Scale_Write, SoftMax /
+ * SoftMask and bcmm (BMM) plus the Headify/DeHeadify copies.  The column-
+ * wise softmax (axis 1) runs as one fused kernel per (batch, head) whose
+ * sums follow the reference kernels' order, so P and O are bitwise the
+ * reference's; other shapes run the composed path (head-major only). */
+int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, float* O,
+                      int batch, int heads, int seq_q, int seq_k, int head_dim, float scale,
+                      int causal, int softmax_axis, int layout, mle_stream_t stream);
+
+/* Backward of the same sub-graph.  Inputs Q, K, V, dO in `layout`, P as
+ * written by the forward.  Accumulates dQ, dK, dV (+=) in `layout`; if
+ * dP_out / dS_out are non-NULL they receive (+=) the softmax node's
+ * gradient dO V^T and the Scale node's gradient (the softmax backward), as
+ * the reference keeps them in node->grad.  Replaces bcmmABT/bcmmATB (BMM
+ * bwd), deriv_softmax, Accumulate (Scale bwd), bcmm/bcmmT (BMMABT bwd) and
+ * the Headify backward copies (Engine/engine.cu:2246-2253,2302-2309,
+ * 2450-2455,2488-2493,2540-2546).  The fused column-softmax kernel keeps the
+ * reference's summation order for every product. */
 int mle_attention_bwd(const float* Q, const float* K, const float* V, const float* P,
                       const float* dO, float* dQ, float* dK, float* dV, float* dP_out,
                       float* dS_out, int batch, int heads, int seq_q, int seq_k, int head_dim,
-                      float scale, int causal, int softmax_axis, int key_grad_mode,
+                      float scale, int causal, int softmax_axis, int key_grad_mode, int layout,
                       mle_stream_t stream);
+
+/* 1 if mle_attention_fwd/bwd take the fused path for these sizes (any
+ * layout), 0 if they need the head-major composed path. */
+int mle_attention_fused_supported(int seq_q, int seq_k, int head_dim, int softmax_axis, int key_grad_mode);
+
+/* Positional table of MatPEncoding alone, table[r, c] = (float)sin/cos of
+ * the angle for position r + start_idx (Engine/kernels.cu:166-185), and its
+ * broadcast add y[b, i] = x[b, i] + table[i]: together bitwise equal to
+ * mle_matpe_fwd, with the trigonometry done once at graph build. */
+int mle_matpe_table(float* table, int rows, int cols, int start_idx, mle_stream_t stream);
+int mle_rows_add_table(const float* x, const float* table, float* y, int64_t batch, int64_t row_elems,
+                       mle_stream_t stream);
 
 /* ------------------------------------------------------------------ */
 /* gradient-norm clip + Adam/AdamW                                      */

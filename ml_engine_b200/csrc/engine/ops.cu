@@ -152,7 +152,13 @@ graph GraphOperations::MatrixPositionalEncoding(const graph& X, const int start_
     node->inputs = {X};
     GB += (double)node->total * sizeof(float) / (1ULL << 30);
     NodeBackProp *nd = node.get(), *xp = X.get();
-    node->forward = [=]() { check(mle_matpe_fwd(xp->output, nd->output, batch, rows, cols, start_idx, st()), "MatPE"); };
+    // the positional term depends on (row, col) only: computed once here
+    float* table = arena_alloc(ARENA_ACT, (int64_t)rows * cols, "MatPE table");
+    check(mle_matpe_table(table, rows, cols, start_idx, st()), "MatPE table");
+    const int64_t row_elems = (int64_t)rows * cols;
+    node->forward = [=]() {
+        check(mle_rows_add_table(xp->output, table, nd->output, batch, row_elems, st()), "MatPE");
+    };
     node->backward = [=]() { check(mle_accumulate(nd->grad, xp->grad, nd->total, 1.0, st()), "MatPE backward"); };
     node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
     node->free = [nd]() { nd->clear(); };
@@ -546,8 +552,29 @@ graph GraphOperations::ScaledDotAttention(const graph& Q, const graph& K, const 
     const int B = Q->dim[0], Sq = Q->dim[2], Sk = K->dim[2], D = Q->dim[3], hd = D / heads;
     auto node = std::make_shared<NodeBackProp>("Attention", B, 1, Sq, D, 1);
     node->inputs = {Q, K, V};
-    // headified operands and their gradients, P and the score gradients
     const int64_t nq = (int64_t)B * Sq * D, nk = (int64_t)B * Sk * D, ns = (int64_t)B * heads * Sq * Sk;
+    NodeBackProp *nd = node.get(), *qp = Q.get(), *kp = K.get(), *vp = V.get();
+    const int causal = (mask && Sq > 1) ? 1 : 0;
+    if (mle_attention_fused_supported(Sq, Sk, hd, axis, key_grad_mode)) {
+        // fused kernels read and write the Linear layout directly; only P is kept
+        float* P = arena_alloc(ARENA_ACT, ns, "Attention P");
+        GB += (double)(2 * nq + ns) * sizeof(float) / (1ULL << 30);
+        node->forward = [=]() {
+            check(mle_attention_fwd(qp->output, kp->output, vp->output, P, nd->output, B, heads, Sq, Sk, hd, scale,
+                                    causal, axis, MLE_ATTN_TOKEN_MAJOR, st()),
+                  "Attention forward");
+        };
+        node->backward = [=]() {
+            check(mle_attention_bwd(qp->output, kp->output, vp->output, P, nd->grad, qp->grad, kp->grad, vp->grad,
+                                    nullptr, nullptr, B, heads, Sq, Sk, hd, scale, causal, axis, key_grad_mode,
+                                    MLE_ATTN_TOKEN_MAJOR, st()),
+                  "Attention backward");
+        };
+        node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+        node->free = [nd]() { nd->clear(); };
+        return node;
+    }
+    // composed path: headified operands and their gradients, P and the score gradients
     float* qh = arena_alloc(ARENA_ACT, nq, "Attention Qh");
     float* kh = arena_alloc(ARENA_ACT, nk, "Attention Kh");
     float* vh = arena_alloc(ARENA_ACT, nk, "Attention Vh");
@@ -560,22 +587,19 @@ graph GraphOperations::ScaledDotAttention(const graph& Q, const graph& K, const 
     float* dP = arena_alloc(ARENA_GRAD, ns, "Attention dP");
     float* dS = arena_alloc(ARENA_GRAD, ns, "Attention dS");
     GB += (double)(2 * (2 * nq + 2 * nk + 2 * ns) + nq) * sizeof(float) / (1ULL << 30);
-    NodeBackProp *nd = node.get(), *qp = Q.get(), *kp = K.get(), *vp = V.get();
-    const int causal = (mask && Sq > 1) ? 1 : 0;
     node->forward = [=]() {
         check(mle_headify(qp->output, qh, B, heads, Sq, hd, 0, st()), "Attention headify Q");
         check(mle_headify(kp->output, kh, B, heads, Sk, hd, 0, st()), "Attention headify K");
         check(mle_headify(vp->output, vh, B, heads, Sk, hd, 0, st()), "Attention headify V");
-        // P = softmax(scale * Q K^T) along `axis`, in place
-        check(mle_bcmm(MLE_GEMM_ABT, qh, kh, P, B, heads, Sq, hd, Sk, 0, 3, 3, 3, scale, st()), "Attention scores");
-        check(mle_softmax_fwd(P, P, (int64_t)B * heads, Sq, Sk, axis, causal, st()), "Attention softmax");
-        check(mle_bcmm(MLE_GEMM_AB, P, vh, oh, B, heads, Sq, Sk, hd, 0, 3, 3, 3, 1.0f, st()), "Attention PV");
+        check(mle_attention_fwd(qh, kh, vh, P, oh, B, heads, Sq, Sk, hd, scale, causal, axis, MLE_ATTN_HEAD_MAJOR,
+                                st()),
+              "Attention forward");
         check(mle_headify(oh, nd->output, B, heads, Sq, hd, 2, st()), "Attention deheadify");
     };
     node->backward = [=]() {
         check(mle_headify(nd->grad, goh, B, heads, Sq, hd, 3, st()), "Attention dO");
         check(mle_attention_bwd(qh, kh, vh, P, goh, gqh, gkh, gvh, dP, dS, B, heads, Sq, Sk, hd, scale, causal, axis,
-                                key_grad_mode, st()),
+                                key_grad_mode, MLE_ATTN_HEAD_MAJOR, st()),
               "Attention backward");
         check(mle_headify(gqh, qp->grad, B, heads, Sq, hd, 1, st()), "Attention dQ");
         check(mle_headify(gkh, kp->grad, B, heads, Sk, hd, 1, st()), "Attention dK");

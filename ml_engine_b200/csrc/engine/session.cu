@@ -56,8 +56,10 @@ struct Session {
     std::vector<std::function<void()>> prep;
     std::vector<std::pair<float*, int64_t>> emb;
     float* loss_host = nullptr;
-    cudaGraph_t graph_ = nullptr;
-    cudaGraphExec_t exec = nullptr;
+    // captured steps: [0] device-resident (no host copies), [1] with the
+    // input upload and the loss download
+    cudaGraph_t graph_[2] = {nullptr, nullptr};
+    cudaGraphExec_t exec[2] = {nullptr, nullptr};
     std::unique_ptr<DataParallel> dp;
     size_t param_first = 0;
 };
@@ -70,10 +72,17 @@ int status_of(cudaError_t e) {
     return MLE_OK;
 }
 
-struct StreamScope {  // routes every op of this session to its stream
+struct StreamScope {  // routes every op of this session to its stream and GEMM mode
     cudaStream_t prev;
-    explicit StreamScope(cudaStream_t s) : prev(mle::stream()) { mle::set_stream(s); }
-    ~StreamScope() { mle::set_stream(prev); }
+    int prev_mode;
+    explicit StreamScope(cudaStream_t s, int gemm_mode = -1) : prev(mle::stream()), prev_mode(mle_get_gemm_mode()) {
+        mle::set_stream(s);
+        if (gemm_mode >= 0) mle_set_gemm_mode(gemm_mode);
+    }
+    ~StreamScope() {
+        mle::set_stream(prev);
+        mle_set_gemm_mode(prev_mode);
+    }
 };
 
 Linear* new_linear(Session& S, int in, int out, const std::string& name) {
@@ -250,14 +259,24 @@ void run_phase(Session& S, int phase) {
     }
 }
 
-void step_body(Session& S, int upload) {
+void step_body(Session& S, int upload, int download) {
     if (upload)
         for (auto& in : S.inputs)
             check_cuda(cudaMemcpyAsync(in.dev, in.host, (size_t)in.numel * 4, cudaMemcpyHostToDevice, S.stream),
                        "input upload");
     for (int ph = 0; ph <= 5; ++ph) run_phase(S, ph);
-    check_cuda(cudaMemcpyAsync(S.loss_host, S.loss->output, sizeof(float), cudaMemcpyDeviceToHost, S.stream),
-               "loss download");
+    if (download)
+        check_cuda(cudaMemcpyAsync(S.loss_host, S.loss->output, sizeof(float), cudaMemcpyDeviceToHost, S.stream),
+                   "loss download");
+}
+
+void drop_graphs(Session& S) {
+    for (int i = 0; i < 2; ++i) {
+        if (S.exec[i]) cudaGraphExecDestroy(S.exec[i]);
+        if (S.graph_[i]) cudaGraphDestroy(S.graph_[i]);
+        S.exec[i] = nullptr;
+        S.graph_[i] = nullptr;
+    }
 }
 
 Session* as_session(mle_session_t s) { return reinterpret_cast<Session*>(s); }
@@ -269,7 +288,7 @@ extern "C" {
 int mle_session_create(const mle_session_desc* desc, mle_session_t* out) {
     if (!desc || !out) return MLE_ERR_ARG;
     const mle_session_desc& d = *desc;
-    if (d.batch <= 0) return MLE_ERR_ARG;
+    if (d.batch <= 0 || (d.gemm_mode != MLE_GEMM_MODE_TF32 && d.gemm_mode != MLE_GEMM_MODE_FP32)) return MLE_ERR_ARG;
     if (d.config == MLE_CFG_MLP) {
         if (d.in_features <= 0 || d.hidden <= 0 || d.classes <= 0) return MLE_ERR_ARG;
     } else if (d.config == MLE_CFG_ENCODER || d.config == MLE_CFG_ENCDEC) {
@@ -290,7 +309,7 @@ int mle_session_create(const mle_session_desc* desc, mle_session_t* out) {
     mle::g_loss_readback = false;
     S->param_first = all_parameters().size();
     {
-        StreamScope sc(S->stream);
+        StreamScope sc(S->stream, S->d.gemm_mode);
         build(*S);
     }
     // parameters in graph order (the order ParameterUpdate visits them)
@@ -313,8 +332,7 @@ int mle_session_destroy(mle_session_t s) {
     Session* S = as_session(s);
     if (!S) return MLE_ERR_ARG;
     cudaStreamSynchronize(S->stream);
-    if (S->exec) cudaGraphExecDestroy(S->exec);
-    if (S->graph_) cudaGraphDestroy(S->graph_);
+    drop_graphs(*S);
     S->dp.reset();
     for (auto& in : S->inputs) cudaFreeHost(in.host);
     cudaFreeHost(S->loss_host);
@@ -351,12 +369,16 @@ int mle_session_input_info(mle_session_t s, int i, char* name, int name_len, int
 int mle_session_step(mle_session_t s, int upload, float* loss_out) {
     Session* S = as_session(s);
     if (!S) return MLE_ERR_ARG;
-    StreamScope sc(S->stream);
-    if (S->exec) {
-        if (!upload) return MLE_ERR_UNSUPPORTED;  // the captured step includes the upload
-        if (cudaGraphLaunch(S->exec, S->stream) != cudaSuccess) return status_of(cudaGetLastError());
+    StreamScope sc(S->stream, S->d.gemm_mode);
+    const int g = upload ? 1 : 0;
+    if (S->exec[g]) {
+        if (cudaGraphLaunch(S->exec[g], S->stream) != cudaSuccess) return status_of(cudaGetLastError());
+        if (loss_out && !upload)
+            check_cuda(cudaMemcpyAsync(S->loss_host, S->loss->output, sizeof(float), cudaMemcpyDeviceToHost,
+                                       S->stream),
+                       "loss download");
     } else {
-        step_body(*S, upload);
+        step_body(*S, upload, loss_out != nullptr || upload);
     }
     if (loss_out) {
         const cudaError_t e = cudaStreamSynchronize(S->stream);
@@ -369,7 +391,7 @@ int mle_session_step(mle_session_t s, int upload, float* loss_out) {
 int mle_session_phase(mle_session_t s, int phase) {
     Session* S = as_session(s);
     if (!S || phase < 0 || phase > 5) return MLE_ERR_ARG;
-    StreamScope sc(S->stream);
+    StreamScope sc(S->stream, S->d.gemm_mode);
     if (phase == 1)
         for (auto& in : S->inputs)
             check_cuda(cudaMemcpyAsync(in.dev, in.host, (size_t)in.numel * 4, cudaMemcpyHostToDevice, S->stream),
@@ -384,24 +406,20 @@ int mle_session_phase(mle_session_t s, int phase) {
 int mle_session_capture(mle_session_t s) {
     Session* S = as_session(s);
     if (!S) return MLE_ERR_ARG;
-    StreamScope sc(S->stream);
-    if (S->exec) {
-        cudaGraphExecDestroy(S->exec);
-        S->exec = nullptr;
-    }
-    if (S->graph_) {
-        cudaGraphDestroy(S->graph_);
-        S->graph_ = nullptr;
-    }
+    StreamScope sc(S->stream, S->d.gemm_mode);
+    drop_graphs(*S);
     cudaError_t e = cudaStreamSynchronize(S->stream);
     if (e != cudaSuccess) return status_of(e);
-    e = cudaStreamBeginCapture(S->stream, cudaStreamCaptureModeThreadLocal);
-    if (e != cudaSuccess) return status_of(e);
-    step_body(*S, 1);
-    e = cudaStreamEndCapture(S->stream, &S->graph_);
-    if (e != cudaSuccess) return status_of(e);
-    e = cudaGraphInstantiate(&S->exec, S->graph_, 0);
-    return status_of(e);
+    for (int g = 0; g < 2; ++g) {
+        e = cudaStreamBeginCapture(S->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return status_of(e);
+        step_body(*S, g, g);
+        e = cudaStreamEndCapture(S->stream, &S->graph_[g]);
+        if (e != cudaSuccess) return status_of(e);
+        e = cudaGraphInstantiate(&S->exec[g], S->graph_[g], 0);
+        if (e != cudaSuccess) return status_of(e);
+    }
+    return MLE_OK;
 }
 
 int mle_session_sync(mle_session_t s) {
@@ -457,7 +475,7 @@ int mle_session_param_write(mle_session_t s, int i, int which, const float* host
 int mle_session_param_step(mle_session_t s, int i, int* t) {
     Session* S = as_session(s);
     if (!S || i < 0 || i >= (int)S->params.size() || !t) return MLE_ERR_ARG;
-    StreamScope sc(S->stream);
+    StreamScope sc(S->stream, S->d.gemm_mode);
     S->params[i]->sync_step();
     *t = S->params[i]->t;
     return MLE_OK;
@@ -482,6 +500,25 @@ int mle_session_device_bytes(mle_session_t s, int64_t* bytes) {
 }
 
 int mle_session_node_count(mle_session_t s) { return s ? (int)as_session(s)->go.nodes.size() : -1; }
+
+int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* copies) {
+    Session* S = as_session(s);
+    if (!S || !kernels || !memsets || !copies) return MLE_ERR_ARG;
+    *kernels = *memsets = *copies = 0;
+    if (!S->graph_[0]) return MLE_ERR_UNSUPPORTED;
+    size_t n = 0;
+    if (cudaGraphGetNodes(S->graph_[0], nullptr, &n) != cudaSuccess) return MLE_ERR_CUDA;
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (cudaGraphGetNodes(S->graph_[0], nodes.data(), &n) != cudaSuccess) return MLE_ERR_CUDA;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        cudaGraphNodeGetType(nd, &t);
+        if (t == cudaGraphNodeTypeKernel) ++*kernels;
+        else if (t == cudaGraphNodeTypeMemset) ++*memsets;
+        else if (t == cudaGraphNodeTypeMemcpy) ++*copies;
+    }
+    return MLE_OK;
+}
 
 int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int world, int bucket_mb) {
     Session* S = as_session(s);

@@ -215,50 +215,88 @@ __global__ void act_bwd_kernel(int kind, const float* __restrict__ x, const floa
     for (int64_t j = tail + i0; j < n; j += stride) gx[j] = act_backward(kind, x[j], gy[j], gx[j]);
 }
 
-// Activation backward fused with the column sums of the updated gradient.
-// Block (kThreads) covers kThreads*4 columns (4 per thread, float4) of a
-// chunk of rows; each thread keeps 4 column partials and adds them with one
-// atomicAdd per column per block.
-template <bool VEC>
-__global__ void act_bwd_bias_kernel(int kind, const float* __restrict__ x, const float* __restrict__ gy,
-                                    float* __restrict__ gx, float* __restrict__ bias_grad, int64_t rows,
-                                    int64_t cols, int64_t rows_per_block) {
-    const int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+// Column sums of a [rows, cols] matrix, optionally fused with the activation
+// backward that produces it (gx = gx + gy*f'(x), summing the updated gx).
+// A 256-thread block owns a strip of 128 columns (4 per lane, float4) or 32
+// columns (1 per lane) and a chunk of rows; its 8 warps take rows
+// round-robin, the partials meet in shared memory, and one atomicAdd per
+// column per block publishes them -- the grid is sized so a column sees at
+// most a few dozen atomics.
+constexpr int kColWarps = 8;
+
+template <bool ACT, bool VEC>
+__global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __restrict__ x,
+                                                     const float* __restrict__ gy, float* __restrict__ g,
+                                                     float* __restrict__ out, int64_t rows, int64_t cols,
+                                                     int64_t rows_per_block, float scale) {
+    constexpr int W = VEC ? 4 : 1;  // columns per lane
+    __shared__ float part[kColWarps][32 * W];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t c0 = (int64_t)blockIdx.x * (32 * W) + (int64_t)lane * W;
     const int64_t r_begin = (int64_t)blockIdx.y * rows_per_block;
-    int64_t r_end = r_begin + rows_per_block;
-    if (r_end > rows) r_end = rows;
-    if (c0 >= cols) return;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    if (VEC) {  // cols % 4 == 0 and aligned
-        for (int64_t r = r_begin; r < r_end; ++r) {
+    const int64_t r_end = (r_begin + rows_per_block < rows) ? r_begin + rows_per_block : rows;
+    float s[W];
+#pragma unroll
+    for (int k = 0; k < W; ++k) s[k] = 0.f;
+    if (c0 < cols) {
+        for (int64_t r = r_begin + warp; r < r_end; r += kColWarps) {
             const int64_t idx = r * cols + c0;
-            const float4 a = *reinterpret_cast<const float4*>(x + idx);
-            const float4 g = *reinterpret_cast<const float4*>(gy + idx);
-            float4 o = *reinterpret_cast<float4*>(gx + idx);
-            o.x = act_backward(kind, a.x, g.x, o.x);
-            o.y = act_backward(kind, a.y, g.y, o.y);
-            o.z = act_backward(kind, a.z, g.z, o.z);
-            o.w = act_backward(kind, a.w, g.w, o.w);
-            *reinterpret_cast<float4*>(gx + idx) = o;
-            s0 += o.x; s1 += o.y; s2 += o.z; s3 += o.w;
-        }
-        atomicAdd(bias_grad + c0 + 0, s0);
-        atomicAdd(bias_grad + c0 + 1, s1);
-        atomicAdd(bias_grad + c0 + 2, s2);
-        atomicAdd(bias_grad + c0 + 3, s3);
-    } else {
-        const int nc = (int)((cols - c0) < 4 ? (cols - c0) : 4);
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int64_t r = r_begin; r < r_end; ++r) {
-            for (int k = 0; k < nc; ++k) {
-                const int64_t idx = r * cols + c0 + k;
-                const float o = act_backward(kind, x[idx], gy[idx], gx[idx]);
-                gx[idx] = o;
-                s[k] += o;
+            if constexpr (VEC) {
+                float4 o = *reinterpret_cast<float4*>(g + idx);
+                if (ACT) {
+                    const float4 a = *reinterpret_cast<const float4*>(x + idx);
+                    const float4 d = *reinterpret_cast<const float4*>(gy + idx);
+                    o.x = act_backward(kind, a.x, d.x, o.x);
+                    o.y = act_backward(kind, a.y, d.y, o.y);
+                    o.z = act_backward(kind, a.z, d.z, o.z);
+                    o.w = act_backward(kind, a.w, d.w, o.w);
+                    *reinterpret_cast<float4*>(g + idx) = o;
+                }
+                s[0] += o.x;
+                s[1] += o.y;
+                s[2] += o.z;
+                s[3] += o.w;
+            } else {
+                float o = g[idx];
+                if (ACT) {
+                    o = act_backward(kind, x[idx], gy[idx], o);
+                    g[idx] = o;
+                }
+                s[0] += o;
             }
         }
-        for (int k = 0; k < nc; ++k) atomicAdd(bias_grad + c0 + k, s[k]);
     }
+#pragma unroll
+    for (int k = 0; k < W; ++k) part[warp][lane * W + k] = s[k];
+    __syncthreads();
+    for (int t = threadIdx.x; t < 32 * W; t += blockDim.x) {
+        const int64_t c = (int64_t)blockIdx.x * (32 * W) + t;
+        if (c < cols) {
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kColWarps; ++w) tot += part[w][t];
+            atomicAdd(out + c, tot * scale);
+        }
+    }
+}
+
+// Launch shape for colsum_kernel: column strips x row chunks, about two
+// waves of blocks, each chunk at least 32 rows.
+struct ColsumShape {
+    dim3 grid;
+    int64_t rpb;
+};
+
+inline ColsumShape colsum_shape(int64_t rows, int64_t cols, bool vec) {
+    const int64_t strip = vec ? 128 : 32;
+    const int64_t col_blocks = (cols + strip - 1) / strip;
+    int64_t row_blocks = (2 * kSMs + col_blocks - 1) / col_blocks;
+    const int64_t max_rb = (rows + 31) / 32;
+    if (row_blocks > max_rb) row_blocks = max_rb;
+    if (row_blocks < 1) row_blocks = 1;
+    const int64_t rpb = (rows + row_blocks - 1) / row_blocks;
+    row_blocks = (rows + rpb - 1) / rpb;
+    return {dim3((unsigned)col_blocks, (unsigned)row_blocks), rpb};
 }
 
 // y[r,c] = x[r,c] + b[c]
@@ -280,30 +318,6 @@ __global__ void bias_add_kernel(const float* __restrict__ x, const float* __rest
     } else {
         const int64_t n = rows * cols;
         for (int64_t j = i0; j < n; j += stride) y[j] = x[j] + b[j % cols];
-    }
-}
-
-// Column sums: one block per (column strip of 4*kThreads, row chunk).
-template <bool VEC>
-__global__ void col_sum_kernel(const float* __restrict__ g, float* __restrict__ out, int64_t rows, int64_t cols,
-                               int64_t rows_per_block, float scale) {
-    const int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    const int64_t r_begin = (int64_t)blockIdx.y * rows_per_block;
-    int64_t r_end = r_begin + rows_per_block;
-    if (r_end > rows) r_end = rows;
-    if (c0 >= cols) return;
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-    if (VEC) {
-        for (int64_t r = r_begin; r < r_end; ++r) {
-            const float4 v = *reinterpret_cast<const float4*>(g + r * cols + c0);
-            s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
-        }
-        for (int k = 0; k < 4; ++k) atomicAdd(out + c0 + k, s[k] * scale);
-    } else {
-        const int nc = (int)((cols - c0) < 4 ? (cols - c0) : 4);
-        for (int64_t r = r_begin; r < r_end; ++r)
-            for (int k = 0; k < nc; ++k) s[k] += g[r * cols + c0 + k];
-        for (int k = 0; k < nc; ++k) atomicAdd(out + c0 + k, s[k] * scale);
     }
 }
 
@@ -354,6 +368,38 @@ __global__ void matpe_kernel(const float* __restrict__ x, float* __restrict__ y,
     }
 }
 
+// The positional term of MatPEncoding alone (x = 0): table[r, c].
+__global__ void matpe_table_kernel(float* __restrict__ t, int rows, int cols, int start_idx) {
+    const int64_t total = (int64_t)rows * cols;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int pos = (int)(i / cols) + start_idx;
+        const int d = (int)(i % cols);
+        const double freq = 1.0 / pow(10000.0, (2.0 * (d / 2)) / cols);
+        const double angle = (double)pos * freq;
+        t[i] = (d % 2 == 0) ? (float)sin(angle) : (float)cos(angle);
+    }
+}
+
+// y[b, i] = x[b, i] + table[i]
+__global__ void rows_add_table_kernel(const float4* __restrict__ x, const float4* __restrict__ table,
+                                      float4* __restrict__ y, int64_t total4, int64_t row4) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += stride) {
+        float4 a = x[i];
+        const float4 t = table[i % row4];
+        a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
+        y[i] = a;
+    }
+}
+
+__global__ void rows_add_table_scalar(const float* __restrict__ x, const float* __restrict__ table,
+                                      float* __restrict__ y, int64_t total, int64_t row) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride)
+        y[i] = x[i] + table[i % row];
+}
+
 // PEncoding (Engine/kernels.cu:147-164)
 __global__ void timestep_pe_kernel(float* __restrict__ y, int t, int dim) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -383,6 +429,39 @@ __global__ void headify_kernel(const float* __restrict__ in, float* __restrict__
         else if (flag == 1) out[fidx] += in[hidx];
         else if (flag == 2) out[fidx] = in[hidx];
         else out[hidx] += in[fidx];
+    }
+}
+
+// float4 form of headify_kernel for head_dim % 4 == 0: thread i moves the
+// 4-vector i of the head-major tensor; 32-bit index math (the entry point
+// checks that the element count fits).
+__global__ void headify4_kernel(const float4* __restrict__ in, float4* __restrict__ out, int heads, int seq, int hd4,
+                                int total4, int flag) {
+    const int stride = gridDim.x * blockDim.x;
+    const int row4 = heads * hd4;  // 4-vectors per token row
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += stride) {
+        const int d4 = i % hd4;
+        int t = i / hd4;
+        const int s = t % seq;
+        t /= seq;
+        const int h = t % heads;
+        const int b = t / heads;
+        const int f = (b * seq + s) * row4 + h * hd4 + d4;
+        if (flag == 0) {
+            out[i] = in[f];
+        } else if (flag == 2) {
+            out[f] = in[i];
+        } else if (flag == 1) {
+            float4 o = out[f];
+            const float4 v = in[i];
+            o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
+            out[f] = o;
+        } else {
+            float4 o = out[i];
+            const float4 v = in[f];
+            o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
+            out[i] = o;
+        }
     }
 }
 
@@ -563,17 +642,14 @@ int mle_act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n,
         return launch_status();
     }
     if (rows <= 0 || cols <= 0 || rows * cols != n) return MLE_ERR_ARG;
-    const int64_t col_blocks = (cols + 4 * kThreads - 1) / (4 * kThreads);
-    int64_t row_blocks = (2 * kSMs + col_blocks - 1) / col_blocks;
-    if (row_blocks > rows) row_blocks = rows;
-    const int64_t rpb = (rows + row_blocks - 1) / row_blocks;
-    row_blocks = (rows + rpb - 1) / rpb;
-    dim3 grid((unsigned)col_blocks, (unsigned)row_blocks);
-    const bool vec = (cols % 4 == 0) && vec_ok(n, x, gy, gx) && aligned16(bias_grad);
+    const bool vec = (cols % 4 == 0) && vec_ok(n, x, gy, gx);
+    const ColsumShape sh = colsum_shape(rows, cols, vec);
     if (vec)
-        act_bwd_bias_kernel<true><<<grid, kThreads, 0, as_stream(stream)>>>(kind, x, gy, gx, bias_grad, rows, cols, rpb);
+        colsum_kernel<true, true><<<sh.grid, 256, 0, as_stream(stream)>>>(kind, x, gy, gx, bias_grad, rows, cols,
+                                                                          sh.rpb, 1.0f);
     else
-        act_bwd_bias_kernel<false><<<grid, kThreads, 0, as_stream(stream)>>>(kind, x, gy, gx, bias_grad, rows, cols, rpb);
+        colsum_kernel<true, false><<<sh.grid, 256, 0, as_stream(stream)>>>(kind, x, gy, gx, bias_grad, rows, cols,
+                                                                           sh.rpb, 1.0f);
     return launch_status();
 }
 
@@ -591,16 +667,15 @@ int mle_bias_add_fwd(const float* x, const float* bias, float* y, int64_t rows, 
 int mle_bias_grad(const float* g, float* bias_grad, int64_t rows, int64_t cols, float scale, mle_stream_t stream) {
     if (rows < 0 || cols <= 0 || !g || !bias_grad) return MLE_ERR_ARG;
     if (rows == 0) return MLE_OK;
-    const int64_t col_blocks = (cols + 4 * kThreads - 1) / (4 * kThreads);
-    int64_t row_blocks = (2 * kSMs + col_blocks - 1) / col_blocks;
-    if (row_blocks > rows) row_blocks = rows;
-    const int64_t rpb = (rows + row_blocks - 1) / row_blocks;
-    row_blocks = (rows + rpb - 1) / rpb;
-    dim3 grid((unsigned)col_blocks, (unsigned)row_blocks);
-    if (cols % 4 == 0 && aligned16(g) && aligned16(bias_grad))
-        col_sum_kernel<true><<<grid, kThreads, 0, as_stream(stream)>>>(g, bias_grad, rows, cols, rpb, scale);
+    const bool vec = cols % 4 == 0 && aligned16(g);
+    const ColsumShape sh = colsum_shape(rows, cols, vec);
+    float* gm = const_cast<float*>(g);  // read-only when ACT == false
+    if (vec)
+        colsum_kernel<false, true><<<sh.grid, 256, 0, as_stream(stream)>>>(0, nullptr, nullptr, gm, bias_grad, rows,
+                                                                           cols, sh.rpb, scale);
     else
-        col_sum_kernel<false><<<grid, kThreads, 0, as_stream(stream)>>>(g, bias_grad, rows, cols, rpb, scale);
+        colsum_kernel<false, false><<<sh.grid, 256, 0, as_stream(stream)>>>(0, nullptr, nullptr, gm, bias_grad, rows,
+                                                                            cols, sh.rpb, scale);
     return launch_status();
 }
 
@@ -635,6 +710,28 @@ int mle_matpe_fwd(const float* x, float* y, int batch, int rows, int cols, int s
     return launch_status();
 }
 
+int mle_matpe_table(float* table, int rows, int cols, int start_idx, mle_stream_t stream) {
+    if (rows <= 0 || cols <= 0 || !table) return MLE_ERR_ARG;
+    matpe_table_kernel<<<grid_for((int64_t)rows * cols, kThreads), kThreads, 0, as_stream(stream)>>>(table, rows, cols,
+                                                                                                     start_idx);
+    return launch_status();
+}
+
+int mle_rows_add_table(const float* x, const float* table, float* y, int64_t batch, int64_t row_elems,
+                       mle_stream_t stream) {
+    if (batch < 0 || row_elems <= 0 || !x || !table || !y) return MLE_ERR_ARG;
+    const int64_t total = batch * row_elems;
+    if (total == 0) return MLE_OK;
+    if (row_elems % 4 == 0 && aligned16(x) && aligned16(table) && aligned16(y))
+        rows_add_table_kernel<<<grid_for(total / 4, kThreads), kThreads, 0, as_stream(stream)>>>(
+            reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(table), reinterpret_cast<float4*>(y),
+            total / 4, row_elems / 4);
+    else
+        rows_add_table_scalar<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, table, y, total,
+                                                                                             row_elems);
+    return launch_status();
+}
+
 int mle_timestep_pe(float* y, int t, int dim, mle_stream_t stream) {
     if (dim <= 2 || !y) return MLE_ERR_ARG;
     timestep_pe_kernel<<<(dim + kThreads - 1) / kThreads, kThreads, 0, as_stream(stream)>>>(y, t, dim);
@@ -647,8 +744,15 @@ int mle_headify(const float* in, float* out, int batch, int heads, int seq, int 
         return MLE_ERR_ARG;
     const int64_t total = (int64_t)batch * heads * seq * head_dim;
     if (total == 0) return MLE_OK;
-    headify_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(in, out, heads, seq, head_dim, total,
-                                                                                  flag);
+    if (head_dim % 4 == 0 && aligned16(in) && aligned16(out) && total / 4 < (1ll << 31)) {
+        const int total4 = (int)(total / 4);
+        headify4_kernel<<<grid_for(total4, kThreads), kThreads, 0, as_stream(stream)>>>(
+            reinterpret_cast<const float4*>(in), reinterpret_cast<float4*>(out), heads, seq, head_dim / 4, total4,
+            flag);
+    } else {
+        headify_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(in, out, heads, seq, head_dim,
+                                                                                      total, flag);
+    }
     return launch_status();
 }
 

@@ -442,13 +442,15 @@ static bool tc_eligible(const GemmProblem& p) {
     return true;
 }
 
+static thread_local int g_gemm_mode = MLE_GEMM_MODE_TF32;
+
 int run_gemm(const GemmProblem& p, cudaStream_t st) {
     if (p.M <= 0 || p.N <= 0 || p.nbatch <= 0 || p.channels <= 0) return MLE_OK;
     if (p.K <= 0) {
         // empty reduction: assign writes alpha*0 (+bias); accumulate is a no-op
         if (p.mode != tc::EPI_ASSIGN) return MLE_OK;
     }
-    if (p.K <= 0 || !tc_eligible(p)) return simt_gemm(p, st);
+    if (p.K <= 0 || g_gemm_mode == MLE_GEMM_MODE_FP32 || !tc_eligible(p)) return simt_gemm(p, st);
 
     using namespace tc;
     const bool A_MN = p.trans_a != 0;  // A stored [K][M]: M contiguous
@@ -543,6 +545,14 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
 using namespace mle;
 
 extern "C" {
+
+int mle_set_gemm_mode(int mode) {
+    if (mode != MLE_GEMM_MODE_TF32 && mode != MLE_GEMM_MODE_FP32) return MLE_ERR_ARG;
+    g_gemm_mode = mode;
+    return MLE_OK;
+}
+
+int mle_get_gemm_mode(void) { return g_gemm_mode; }
 
 int mle_watchdog_read(int* out_flag, mle_stream_t stream) {
     if (!out_flag) return MLE_ERR_ARG;

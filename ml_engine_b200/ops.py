@@ -179,12 +179,31 @@ def linear_bwd(X, W, dY, dX, dW, dB, rows, in_features, out_features):
 
 
 KEYGRAD_REFERENCE, KEYGRAD_TRUE = 0, 1
+HEAD_MAJOR, TOKEN_MAJOR = 0, 1
+
+
+def attention_fwd(Q, K, V, P, O, batch, heads, seq_q, seq_k, head_dim, scale, causal=0, softmax_axis=1,
+                  layout=HEAD_MAJOR):
+    _call("mle_attention_fwd", _p(Q), _p(K), _p(V), _p(P), _p(O), batch, heads, seq_q, seq_k, head_dim, scale, causal,
+          softmax_axis, layout, _s())
 
 
 def attention_bwd(Q, K, V, P, dO, dQ, dK, dV, dP, dS, batch, heads, seq_q, seq_k, head_dim, scale, causal=0,
-                  softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE):
+                  softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE, layout=HEAD_MAJOR):
     _call("mle_attention_bwd", _p(Q), _p(K), _p(V), _p(P), _p(dO), _p(dQ), _p(dK), _p(dV), _p(dP), _p(dS), batch,
-          heads, seq_q, seq_k, head_dim, scale, causal, softmax_axis, key_grad_mode, _s())
+          heads, seq_q, seq_k, head_dim, scale, causal, softmax_axis, key_grad_mode, layout, _s())
+
+
+def attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE):
+    return bool(kernels().mle_attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis, key_grad_mode))
+
+
+def matpe_table(table, rows, cols, start_idx=0):
+    _call("mle_matpe_table", _p(table), rows, cols, start_idx, _s())
+
+
+def rows_add_table(x, table, y, batch):
+    _call("mle_rows_add_table", _p(x), _p(table), _p(y), batch, table.numel(), _s())
 
 
 def param_views(params):

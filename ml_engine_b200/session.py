@@ -30,7 +30,11 @@ class SessionDesc(ctypes.Structure):
         ("fused_attention", ctypes.c_int), ("key_grad_mode", ctypes.c_int),
         ("lr", ctypes.c_float), ("adamw", ctypes.c_int), ("clip_norm", ctypes.c_float),
         ("seed", ctypes.c_uint64),
+        ("gemm_mode", ctypes.c_int),
     ]
+
+
+GEMM_TF32, GEMM_FP32 = 0, 1
 
 
 class Session:
@@ -69,6 +73,9 @@ class Session:
     # ------------------------------------------------------------ builders
     @classmethod
     def mlp(cls, batch=64, in_features=784, hidden=256, classes=10, **kw):
+        # ReLU masks follow the pre-activation's sign: fp32 products keep
+        # them identical to the reference's (the GEMMs here are tiny)
+        kw.setdefault("gemm_mode", GEMM_FP32)
         return cls(config=MLP, batch=batch, in_features=in_features, hidden=hidden, classes=classes, **kw)
 
     @classmethod

@@ -1,0 +1,234 @@
+"""Whole training steps of the benchmark graphs on the CPU oracle.
+
+TEST INFRASTRUCTURE: every step below is the reference's graph executed node
+by node with the oracle ops (oracle/mle_oracle.c), forward in topological
+order and backward in reverse, with the reference's accumulate/assign
+conventions:
+
+  * Linear (Engine/engine.cu:3534-3563): Y = X W + b; dX += dY W^T,
+    dW += X^T dY, db += colsum(dY)
+  * MultiHeadAttention::forward (Engine/transformer.cu:647-661): Headify,
+    BMMABT, Scale(1/sqrt(hd)), SOFTMAX(type 1), BMM, DeHeadify; its backward
+    keeps BMMABT's key gradient as the reference computes it, bcmmT(Q, dS)
+    (Engine/engine.cu:2307)
+  * LayerNorm per token via the [B*S,1,1,D] reshape (Engine/engine.cu:3079-3130)
+  * SoftMaxCrossEntropy, last=true (Engine/engine.cu:2063-2111)
+  * clip = accumulate + Sqrt_Scale + clipNorm (Engine/engine.cu:3362-3368)
+  * AdamW per tensor with its own step counter (Engine/engine.cu:283-292)
+
+Parameters are lists of float32 arrays in the order the native session
+reports them (W then b for each Linear, in construction order).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from . import ops as o
+
+
+def _lin_fwd(X, W, b):
+    rows, fin = X.shape
+    Y = np.zeros((rows, W.shape[1]), np.float32)
+    o.gemm(X, W, Y, rows, W.shape[1], fin)
+    return o.bias_add(Y, b)
+
+
+def _lin_bwd(X, W, dY, dX, dW, db):
+    rows, fin = X.shape
+    fout = W.shape[1]
+    if dX is not None:
+        o.gemm(dY, W, dX, rows, fin, fout, 0, 1, accumulate=True)
+    o.gemm(X, dY, dW, fin, fout, rows, 1, 0, accumulate=True)
+    o.bias_grad(dY, db)
+
+
+def clip_and_update(params, grads, steps, lr, clip_norm=1.0, adamw=True, moments=None):
+    """Clip (if clip_norm > 0) then AdamW/Adam.  Returns (clip factor,
+    new params, m, v); grads are clipped in place."""
+    acc = np.zeros(1, np.float64)
+    if clip_norm > 0:
+        for g in grads:
+            o.sumsq(acc, g)
+        x = acc[0]
+        if x == x:
+            s = math.sqrt(x)
+            acc[0] = s / clip_norm if s > clip_norm else 1.0
+        for g in grads:
+            o.clip_apply(g, acc)
+    new_p, ms, vs = [], [], []
+    for i, (p, g) in enumerate(zip(params, grads)):
+        w = p.copy()
+        m = np.zeros_like(w) if moments is None else moments[0][i].copy()
+        v = np.zeros_like(w) if moments is None else moments[1][i].copy()
+        o.adam(w, g, m, v, steps[i], lr, adamw)
+        new_p.append(w)
+        ms.append(m)
+        vs.append(v)
+    return float(acc[0]), new_p, ms, vs
+
+
+# ============================================================== MLP (config 1)
+def mlp_step(params, x, labels, classes=10, lr=1e-3, clip_norm=1.0, steps=None):
+    W1, b1, W2, b2 = [p.reshape(s) for p, s in zip(params, [(x.shape[1], -1), (-1,), (-1, classes), (-1,)])]
+    B = x.shape[0]
+    h = _lin_fwd(x, W1, b1)
+    a = o.act_fwd(0, h)
+    logits = _lin_fwd(a, W2, b2)
+    target = o.one_hot(labels, classes)
+    probs, loss = o.smce_fwd(logits, target, B, classes)
+    dlogits = o.smce_bwd(probs, target, float(B)).reshape(B, classes)
+    da = np.zeros_like(a)
+    gW2, gb2 = np.zeros_like(W2), np.zeros_like(b2)
+    _lin_bwd(a, W2, dlogits, da, gW2, gb2)
+    dh = o.act_bwd(0, h, da, np.zeros_like(h))
+    gW1, gb1 = np.zeros_like(W1), np.zeros_like(b1)
+    _lin_bwd(x, W1, dh, np.zeros_like(x), gW1, gb1)
+    grads = [g.ravel().copy() for g in (gW1, gb1, gW2, gb2)]
+    raw = [g.copy() for g in grads]
+    steps = steps or [1] * 4
+    clip, new_p, m, v = clip_and_update([p.ravel() for p in params], grads, steps, lr, clip_norm)
+    return dict(loss=loss, grads=raw, clipped=grads, clip=clip, params=new_p, m=m, v=v)
+
+
+# ======================================================== transformer blocks
+class _Tape:
+    """Records backward closures in forward order; replays them reversed."""
+
+    def __init__(self):
+        self.ops = []
+
+    def add(self, fn):
+        self.ops.append(fn)
+
+    def backward(self):
+        for fn in reversed(self.ops):
+            fn()
+
+
+def _layernorm_tokens(tape, x, dx, rows, D):
+    y, _, sq = o.layernorm_fwd(x, rows, 1, 1, D)
+    y = y.reshape(rows, D)
+    dy = np.zeros_like(y)
+
+    def bwd():
+        o.layernorm_bwd(y, dy, sq, dx, rows, 1, 1, D)
+
+    tape.add(bwd)
+    return y, dy
+
+
+def _linear(tape, X, dX, W, b, gW, gb):
+    Y = _lin_fwd(X, W, b)
+    dY = np.zeros_like(Y)
+
+    def bwd():
+        _lin_bwd(X, W, dY, dX, gW, gb)
+
+    tape.add(bwd)
+    return Y, dY
+
+
+def _attention(tape, hq, dhq, hkv, dhkv, P_, G_, B, Sq, Sk, D, H, scale, mask):
+    """q/k/v/o Linears around the reference's attention ops.  P_/G_ are the
+    four (W, b) parameter and gradient pairs."""
+    hd = D // H
+    (Wq, bq, Wk, bk, Wv, bv, Wo, bo) = P_
+    (gWq, gbq, gWk, gbk, gWv, gbv, gWo, gbo) = G_
+    q, dq = _linear(tape, hq, dhq, Wq, bq, gWq, gbq)
+    k, dk = _linear(tape, hkv, dhkv, Wk, bk, gWk, gbk)
+    v, dv = _linear(tape, hkv, dhkv, Wv, bv, gWv, gbv)
+    Qh = o.headify(q, np.zeros(B * Sq * D, np.float32), B, H, Sq, hd, 0)
+    Kh = o.headify(k, np.zeros(B * Sk * D, np.float32), B, H, Sk, hd, 0)
+    Vh = o.headify(v, np.zeros(B * Sk * D, np.float32), B, H, Sk, hd, 0)
+    scores = o.bcmm(1, Qh, Kh, np.zeros(B * H * Sq * Sk, np.float32), B, H, Sq, hd, Sk, 0, 3, 3, 3)
+    scaled = o.scale_write(scores, scale)
+    P = o.softmax_fwd(scaled, B * H, Sq, Sk, 1, 1 if (mask and Sq > 1) else 0)
+    Oh = o.bcmm(0, P, Vh, np.zeros(B * H * Sq * hd, np.float32), B, H, Sq, Sk, hd, 0, 3, 3, 3)
+    c = o.headify(Oh, np.zeros(B * Sq * D, np.float32), B, H, Sq, hd, 2).reshape(B * Sq, D)
+    dc = np.zeros_like(c)
+    dQh, dKh, dVh = (np.zeros(n, np.float32) for n in (B * Sq * D, B * Sk * D, B * Sk * D))
+
+    def attn_bwd():
+        dOh = o.headify(dc, np.zeros(B * Sq * D, np.float32), B, H, Sq, hd, 3)
+        dP = o.bcmm(1, dOh, Vh, np.zeros(B * H * Sq * Sk, np.float32), B, H, Sq, hd, Sk, 1, 3, 3, 3)
+        o.bcmm(2, P, dOh, dVh, B, H, Sk, Sq, hd, 1, 3, 3, 3)
+        dsc = o.softmax_bwd(P, dP, np.zeros(B * H * Sq * Sk, np.float32), B * H, Sq, Sk, 1)
+        dS = o.accumulate(dsc, np.zeros_like(dsc), scale)
+        o.bcmm(0, dS, Kh, dQh, B, H, Sq, Sk, hd, 1, 3, 3, 3)
+        o.bcmm(3, Qh, dS, dKh, B, H, hd, Sq, Sk, 1, 3, 3, 3)  # the reference's bcmmT key gradient
+        o.headify(dQh, dq, B, H, Sq, hd, 1)
+        o.headify(dKh, dk, B, H, Sk, hd, 1)
+        o.headify(dVh, dv, B, H, Sk, hd, 1)
+
+    tape.add(attn_bwd)
+    a, da = _linear(tape, c, dc, Wo, bo, gWo, gbo)
+    return a, da
+
+
+def _add(tape, a, da, b, db):
+    y = o.scale_add(a, b, 1.0)
+    dy = np.zeros_like(y)
+
+    def bwd():
+        np.add(da, dy, out=da)
+        np.add(db, dy, out=db)
+
+    tape.add(bwd)
+    return y, dy
+
+
+def _ffn(tape, h, dh, W1, b1, W2, b2, g):
+    f1, df1 = _linear(tape, h, dh, W1, b1, g[0], g[1])
+    a = o.act_fwd(4, f1)
+    da = np.zeros_like(a)
+
+    def gelu_bwd():
+        o.act_bwd(4, f1, da, df1)
+
+    tape.add(gelu_bwd)
+    f2, df2 = _linear(tape, a, da, W2, b2, g[2], g[3])
+    return f2, df2
+
+
+def encoder_step(params, table, tokens, targets, batch, seq, d_model, heads, ffn, layers, vocab, lr=1e-3,
+                 clip_norm=1.0, steps=None):
+    """One step of the ENCODER session graph on the oracle."""
+    B, S, D, H = batch, seq, d_model, heads
+    rows = B * S
+    shapes = []
+    for _ in range(layers):
+        shapes += [(D, D), (D,)] * 4 + [(D, ffn), (ffn,), (ffn, D), (D,)]
+    shapes += [(D, vocab), (vocab,)]
+    P = [p.reshape(s) for p, s in zip(params, shapes)]
+    G = [np.zeros_like(p) for p in P]
+    tape = _Tape()
+    emb = o.embedding_gather(tokens.ravel(), table.reshape(vocab, D))
+    x = o.matpe(emb, B, S, D).reshape(rows, D)
+    dx = np.zeros_like(x)
+    demb = np.zeros_like(x)
+
+    def pe_bwd(dx0=dx):  # bound now: `dx` is rebound per layer below
+        np.add(demb, dx0, out=demb)
+
+    tape.add(pe_bwd)
+    for layer in range(layers):
+        base = layer * 12
+        h, dh = _layernorm_tokens(tape, x, dx, rows, D)
+        a, da = _attention(tape, h, dh, h, dh, P[base:base + 8], G[base:base + 8], B, S, S, D, H,
+                           1.0 / math.sqrt(D // H), False)
+        x1, dx1 = _add(tape, x, dx, a, da)
+        h2, dh2 = _layernorm_tokens(tape, x1, dx1, rows, D)
+        f, df = _ffn(tape, h2, dh2, P[base + 8], P[base + 9], P[base + 10], P[base + 11], G[base + 8:base + 12])
+        x, dx = _add(tape, x1, dx1, f, df)
+    logits, dlogits = _linear(tape, x, dx, P[-2], P[-1], G[-2], G[-1])
+    target = o.one_hot(targets.ravel(), vocab)
+    probs, loss = o.smce_fwd(logits, target, rows, vocab)
+    dlogits[:] = o.smce_bwd(probs, target, float(B)).reshape(rows, vocab)
+    tape.backward()
+    grads = [g.ravel().copy() for g in G]
+    raw = [g.copy() for g in grads]
+    steps = steps or [1] * len(grads)
+    clip, new_p, m, v = clip_and_update([p.ravel() for p in P], grads, steps, lr, clip_norm)
+    return dict(loss=loss, grads=raw, clipped=grads, clip=clip, params=new_p, m=m, v=v)

@@ -21,6 +21,7 @@ _SIGS = {
     "ref_act_fwd": [I, P, P, I],
     "ref_act_bwd": [I, P, P, P, I],
     "ref_accumulate": [P, P, L, D],
+    "ref_scale_write": [P, P, L, F],
     "ref_bcompress": [P, P, I, I, I, I],
     "ref_headify": [P, P, I, I, I, I, I],
     "ref_matpe": [P, P, I, I, I, I],

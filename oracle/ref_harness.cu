@@ -91,6 +91,12 @@ int ref_accumulate(const float* x, float* y, long long n, double scale) {
     return (int)cudaGetLastError();
 }
 
+/* Scale forward (Engine/engine.cu:2533-2538) */
+int ref_scale_write(const float* x, float* y, long long n, float scale) {
+    Scale_Write<<<blocks(n, THREADSPERBLOCK), THREADSPERBLOCK>>>(x, y, (unsigned long long)n, scale);
+    return (int)cudaGetLastError();
+}
+
 int ref_bcompress(const float* g, float* db, int batch, int channels, int rows, int cols) {
     BCompress<<<cols, THREADSPERBLOCK>>>(g, db, batch, channels, rows, cols);
     return (int)cudaGetLastError();

@@ -338,23 +338,75 @@ def test_linear_fwd_bwd(cuda, ops, orc, rng, rows, fin, fout):
 
 
 # ------------------------------------------------------------------ attention
-@pytest.mark.parametrize("key_mode", [0, 1])
-@pytest.mark.parametrize("B,Hh,Sq,Sk,D,axis,causal", [(2, 8, 128, 128, 32, 1, 0), (2, 4, 64, 64, 64, 1, 1),
-                                                     (1, 2, 40, 72, 16, 0, 0)])
-def test_attention_bwd(cuda, ops, orc, rng, B, Hh, Sq, Sk, D, axis, causal, key_mode):
+ATTN_CASES = [  # B, H, Sq, Sk, hd, axis, causal
+    (2, 8, 128, 128, 32, 1, 0),   # configs[1] shape per head: fused
+    (2, 4, 64, 64, 64, 1, 1),     # masked (SoftMask): fused
+    (1, 2, 256, 256, 64, 1, 1),   # configs[2] head shape: fused
+    (1, 2, 40, 72, 16, 1, 0),     # Sq != Sk: fused for the true key gradient, composed for the reference one
+    (1, 2, 40, 72, 16, 0, 0),     # row-wise softmax: composed (tensor cores)
+]
+
+
+def _attn_inputs(rng, B, Hh, Sq, Sk, D):
     bh = B * Hh
-    Q = rng.standard_normal((bh, Sq, D)).astype(np.float32)
-    K = rng.standard_normal((bh, Sk, D)).astype(np.float32)
-    V = rng.standard_normal((bh, Sk, D)).astype(np.float32)
-    dO = rng.standard_normal((bh, Sq, D)).astype(np.float32)
-    scale = 1.0 / np.sqrt(D)
-    S = np.zeros((bh, Sq, Sk), np.float32)
-    orc.bcmm(1, Q, K, S, B, Hh, Sq, D, Sk, 0, 3, 3, 3)
+    return [rng.standard_normal((bh, s, D)).astype(np.float32) for s in (Sq, Sk, Sk, Sq)]
+
+
+def _to_token_major(x, B, Hh):
+    bh, S, D = x.shape
+    return np.ascontiguousarray(x.reshape(B, Hh, S, D).transpose(0, 2, 1, 3).reshape(B, S, Hh * D))
+
+
+def _from_token_major(x, B, Hh, D):
+    S = x.shape[1]
+    return np.ascontiguousarray(x.reshape(B, S, Hh, D).transpose(0, 2, 1, 3).reshape(B * Hh, S, D))
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_attention_fwd(cuda, ops, orc, rng, case, layout):
+    B, Hh, Sq, Sk, D, axis, causal = case
+    fused = ops.attention_fused_supported(Sq, Sk, D, axis, 1)
+    if layout == 1 and not fused:
+        pytest.skip("token-major layout is served by the fused kernels only")
+    Q, K, V, _ = _attn_inputs(rng, B, Hh, Sq, Sk, D)
+    scale = float(1.0 / np.sqrt(D))
+    conv = (lambda x: _to_token_major(x, B, Hh)) if layout else (lambda x: x)
+    P = torch.zeros(B * Hh, Sq, Sk, device=cuda)
+    O = torch.zeros(*conv(np.zeros((B * Hh, Sq, D), np.float32)).shape, device=cuda)
+    ops.attention_fwd(T(conv(Q), cuda), T(conv(K), cuda), T(conv(V), cuda), P, O, B, Hh, Sq, Sk, D, scale, causal,
+                      axis, layout)
+    S = orc.bcmm(1, Q, K, np.zeros((B * Hh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 0, 3, 3, 3)
+    rP = orc.softmax_fwd(orc.scale_write(S, scale), B * Hh, Sq, Sk, axis, causal)
+    rO = orc.bcmm(0, rP, V, np.zeros((B * Hh, Sq, D), np.float32), B, Hh, Sq, Sk, D, 0, 3, 3, 3)
+    tol = 1e-5 if fused else RTOL_TC
+    o = H(O)
+    if layout:
+        o = _from_token_major(o, B, Hh, D)
+    assert rel_err(H(P), rP) <= tol
+    assert rel_err(o, rO) <= tol
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+@pytest.mark.parametrize("key_mode", [0, 1])
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_attention_bwd(cuda, ops, orc, rng, case, key_mode, layout):
+    B, Hh, Sq, Sk, D, axis, causal = case
+    fused = ops.attention_fused_supported(Sq, Sk, D, axis, key_mode)
+    if layout == 1 and not fused:
+        pytest.skip("token-major layout is served by the fused kernels only")
+    bh = B * Hh
+    Q, K, V, dO = _attn_inputs(rng, B, Hh, Sq, Sk, D)
+    scale = float(1.0 / np.sqrt(D))
+    S = orc.bcmm(1, Q, K, np.zeros((bh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 0, 3, 3, 3)
     P = orc.softmax_fwd(orc.scale_write(S, scale), bh, Sq, Sk, axis, causal)
-    dQ, dK, dV = (torch.zeros(bh, s, D, device=cuda) for s in (Sq, Sk, Sk))
+    conv = (lambda x: _to_token_major(x, B, Hh)) if layout else (lambda x: x)
+    back = (lambda x: _from_token_major(x, B, Hh, D)) if layout else (lambda x: x)
+    dQ0, dK0, dV0 = (rng.standard_normal((bh, s, D)).astype(np.float32) for s in (Sq, Sk, Sk))
+    dQ, dK, dV = T(conv(dQ0), cuda), T(conv(dK0), cuda), T(conv(dV0), cuda)
     dP, dS = torch.zeros(bh, Sq, Sk, device=cuda), torch.zeros(bh, Sq, Sk, device=cuda)
-    ops.attention_bwd(T(Q, cuda), T(K, cuda), T(V, cuda), T(P, cuda), T(dO, cuda), dQ, dK, dV, dP, dS, B, Hh, Sq, Sk,
-                      D, float(scale), causal, axis, key_mode)
+    ops.attention_bwd(T(conv(Q), cuda), T(conv(K), cuda), T(conv(V), cuda), T(P, cuda), T(conv(dO), cuda), dQ, dK,
+                      dV, dP, dS, B, Hh, Sq, Sk, D, scale, causal, axis, key_mode, layout)
     # reference chain (Engine/engine.cu:2246-2253, 2450-2455, 2540-2546, 2302-2309)
     rdP = orc.bcmm(1, dO, V, np.zeros((bh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 1, 3, 3, 3)
     rdV = orc.bcmm(2, P, dO, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
@@ -365,11 +417,23 @@ def test_attention_bwd(cuda, ops, orc, rng, B, Hh, Sq, Sk, D, axis, causal, key_
         rdK = orc.bcmm(3, Q, rdS, np.zeros((bh, Sk, D), np.float32), B, Hh, D, Sq, Sk, 1, 3, 3, 3)
     else:              # the mathematical gradient dS^T Q
         rdK = orc.bcmm(2, rdS, Q, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
-    assert rel_err(H(dP), rdP) <= RTOL_TC
-    assert rel_err(H(dV), rdV) <= RTOL_TC
-    assert rel_err(H(dS), rdSc) <= RTOL_TC
-    assert rel_err(H(dQ), rdQ) <= RTOL_TC
-    assert rel_err(H(dK), rdK) <= RTOL_TC
+    tol = 1e-5 if fused else RTOL_TC
+    assert rel_err(H(dP), rdP) <= tol
+    assert rel_err(H(dS), rdSc) <= tol
+    assert rel_err(back(H(dV)) - dV0, rdV) <= tol
+    assert rel_err(back(H(dQ)) - dQ0, rdQ) <= tol
+    assert rel_err(back(H(dK)) - dK0, rdK) <= tol
+
+
+def test_matpe_table_matches_direct(cuda, ops, rng):
+    B, S, D = 3, 50, 64
+    x = rng.standard_normal(B * S * D).astype(np.float32)
+    y1, y2 = torch.empty(B * S * D, device=cuda), torch.empty(B * S * D, device=cuda)
+    table = torch.empty(S * D, device=cuda)
+    ops.matpe_fwd(T(x, cuda), y1, B, S, D, 2)
+    ops.matpe_table(table, S, D, 2)
+    ops.rows_add_table(T(x, cuda), table, y2, B)
+    assert np.array_equal(H(y1), H(y2))
 
 
 # ------------------------------------------------------------------ optimizer

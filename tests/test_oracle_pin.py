@@ -177,3 +177,43 @@ def test_smce_reference(cuda, ref, ops, orc, rng):
     assert rel_err(H(gm), H(grad)) <= RTOL_EXACT
     _, oloss = orc.smce_fwd(logits, target, rows, V)
     assert abs(oloss - H(loss)[0]) <= RTOL_EXACT * abs(oloss)
+
+
+@pytest.mark.parametrize("mask", [0, 1])
+def test_fused_attention_bitwise_vs_reference_chain(cuda, ref, ops, rng, mask):
+    """The fused attention kernels against the reference's own kernel chain
+    (bcmmABT, Scale_Write, SoftMax/SoftMask type 1, bcmm; then bcmmABT,
+    bcmmATB, deriv_softmax, Accumulate, bcmm, bcmmT) run through oracle/_ref:
+    P, O, dQ, dK (reference key gradient) and dV are bitwise equal."""
+    B, Hh, S, D = 2, 4, 128, 32
+    bh, n_s = B * Hh, B * Hh * S * S
+    Q, K, V, dO = (rng.standard_normal((bh, S, D)).astype(np.float32) for _ in range(4))
+    scale = float(1.0 / np.sqrt(D))
+    tQ, tK, tV, tdO = (T(a, cuda) for a in (Q, K, V, dO))
+    # reference forward
+    scores, scaled, rP = (torch.zeros(n_s, device=cuda) for _ in range(3))
+    ref.call("ref_bcmm", 1, ref.ptr(tQ), ref.ptr(tK), ref.ptr(scores), B, Hh, S, D, S, 0, 3, 3, 3, 1.0)
+    ref.call("ref_scale_write", ref.ptr(scores), ref.ptr(scaled), n_s, scale)
+    arr, mx = torch.empty(bh * S, device=cuda), torch.empty(bh * S, device=cuda)
+    ref.call("ref_softmax_fwd", ref.ptr(scaled), ref.ptr(arr), ref.ptr(rP), ref.ptr(mx), B, Hh, S, S, 1, mask)
+    rO = torch.zeros(bh * S * D, device=cuda)
+    ref.call("ref_bcmm", 0, ref.ptr(rP), ref.ptr(tV), ref.ptr(rO), B, Hh, S, S, D, 0, 3, 3, 3, 1.0)
+    # fused forward (head-major)
+    P, O = torch.zeros(n_s, device=cuda), torch.zeros(bh * S * D, device=cuda)
+    ops.attention_fwd(tQ, tK, tV, P, O, B, Hh, S, S, D, scale, mask, 1, 0)
+    assert np.array_equal(H(P), H(rP))
+    assert np.array_equal(H(O), H(rO))
+    # reference backward
+    rdP, rdSc, rdS = (torch.zeros(n_s, device=cuda) for _ in range(3))
+    rdQ, rdK, rdV = (torch.zeros(bh * S * D, device=cuda) for _ in range(3))
+    ref.call("ref_bcmm", 1, ref.ptr(tdO), ref.ptr(tV), ref.ptr(rdP), B, Hh, S, D, S, 1, 3, 3, 3, 1.0)
+    ref.call("ref_bcmm", 2, ref.ptr(rP), ref.ptr(tdO), ref.ptr(rdV), B, Hh, S, S, D, 1, 3, 3, 3, 1.0)
+    ref.call("ref_softmax_bwd", ref.ptr(rP), ref.ptr(rdP), ref.ptr(rdSc), B, Hh, S, S, 1)
+    ref.call("ref_accumulate", ref.ptr(rdSc), ref.ptr(rdS), n_s, scale)
+    ref.call("ref_bcmm", 0, ref.ptr(rdS), ref.ptr(tK), ref.ptr(rdQ), B, Hh, S, S, D, 1, 3, 3, 3, 1.0)
+    ref.call("ref_bcmm", 3, ref.ptr(tQ), ref.ptr(rdS), ref.ptr(rdK), B, Hh, D, S, S, 1, 3, 3, 3, 1.0)
+    dQ, dK, dV = (torch.zeros(bh * S * D, device=cuda) for _ in range(3))
+    dP, dS = torch.zeros(n_s, device=cuda), torch.zeros(n_s, device=cuda)
+    ops.attention_bwd(tQ, tK, tV, P, tdO, dQ, dK, dV, dP, dS, B, Hh, S, S, D, scale, mask, 1, 0, 0)
+    for mine, theirs in ((dP, rdP), (dS, rdSc), (dV, rdV), (dQ, rdQ), (dK, rdK)):
+        assert np.array_equal(H(mine), H(theirs))
