@@ -325,9 +325,10 @@ enum mle_attn_layout { MLE_ATTN_HEAD_MAJOR = 0, MLE_ATTN_TOKEN_MAJOR = 1 };
  * Q K^T) [causal: entries with key > query zeroed before normalising],
  * O = P V (assigned).  Replaces bcmmABT (BMMABT), Scale_Write, SoftMax /
  * SoftMask and bcmm (BMM) plus the Headify/DeHeadify copies.  The column-
- * wise softmax (axis 1) runs as one fused kernel per (batch, head) whose
- * sums follow the reference kernels' order, so P and O are bitwise the
- * reference's; other shapes run the composed path (head-major only). */
+ * wise softmax (axis 1) runs as two fused kernels (P by key blocks, O by
+ * query blocks) whose sums follow the reference kernels' order, so P and O
+ * are bitwise the reference's; other shapes run the composed path
+ * (head-major only).  Q, K, V must be 16-byte aligned for the fused path. */
 int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, float* O,
                       int batch, int heads, int seq_q, int seq_k, int head_dim, float scale,
                       int causal, int softmax_axis, int layout, mle_stream_t stream);
@@ -336,16 +337,19 @@ int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, 
  * written by the forward.  Accumulates dQ, dK, dV (+=) in `layout`; if
  * dP_out / dS_out are non-NULL they receive (+=) the softmax node's
  * gradient dO V^T and the Scale node's gradient (the softmax backward), as
- * the reference keeps them in node->grad.  Replaces bcmmABT/bcmmATB (BMM
- * bwd), deriv_softmax, Accumulate (Scale bwd), bcmm/bcmmT (BMMABT bwd) and
- * the Headify backward copies (Engine/engine.cu:2246-2253,2302-2309,
- * 2450-2455,2488-2493,2540-2546).  The fused column-softmax kernel keeps the
- * reference's summation order for every product. */
+ * the reference keeps them in node->grad.  The fused path needs
+ * `workspace`, batch*heads*seq_q*seq_k floats of scratch (left holding
+ * the score gradients); the composed path ignores it and needs dP_out and
+ * dS_out instead.  Replaces bcmmABT/bcmmATB (BMM bwd), deriv_softmax,
+ * Accumulate (Scale bwd), bcmm/bcmmT (BMMABT bwd) and the Headify backward
+ * copies (Engine/engine.cu:2246-2253,2302-2309,2450-2455,2488-2493,
+ * 2540-2546).  The fused kernels keep the reference's summation order for
+ * every product. */
 int mle_attention_bwd(const float* Q, const float* K, const float* V, const float* P,
                       const float* dO, float* dQ, float* dK, float* dV, float* dP_out,
-                      float* dS_out, int batch, int heads, int seq_q, int seq_k, int head_dim,
-                      float scale, int causal, int softmax_axis, int key_grad_mode, int layout,
-                      mle_stream_t stream);
+                      float* dS_out, float* workspace, int batch, int heads, int seq_q, int seq_k,
+                      int head_dim, float scale, int causal, int softmax_axis, int key_grad_mode,
+                      int layout, mle_stream_t stream);
 
 /* 1 if mle_attention_fwd/bwd take the fused path for these sizes (any
  * layout), 0 if they need the head-major composed path. */

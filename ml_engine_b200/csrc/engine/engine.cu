@@ -243,7 +243,10 @@ NodeBackProp::NodeBackProp(str name, int batch, int d1, int d2, int d3, int allo
         output = nullptr;
         grad = nullptr;
     }
+    forget_ext(this);
 }
+
+NodeBackProp::~NodeBackProp() { forget_ext(this); }
 
 void NodeBackProp::clear() {
     // Arena memory is released with the arenas; the reference cudaFrees here.

@@ -108,7 +108,7 @@ struct NodeBackProp {
     std::function<void(const bool full)> printparams;
     virtual void update(const float lr = LEARNING_RATE, const bool W = ADAMW) {}
     NodeBackProp(str name, int batch, int d1, int d2, int d3, int allocation);
-    virtual ~NodeBackProp() = default;
+    virtual ~NodeBackProp();
     void clear();
     void reshape(std::vector<int> new_dims);
     void reshape(int arr[], const int size = 4);

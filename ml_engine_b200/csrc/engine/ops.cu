@@ -18,9 +18,12 @@ using namespace mle;
 
 namespace mle {
 
+// Keyed by node address: a node drops its entry when it is constructed and
+// destroyed, so a later node at a recycled address starts from defaults.
+// Never destroyed, so nodes outliving static destruction can still erase.
 static std::unordered_map<const NodeBackProp*, NodeExt>& ext_map() {
-    static std::unordered_map<const NodeBackProp*, NodeExt> m;
-    return m;
+    static auto* m = new std::unordered_map<const NodeBackProp*, NodeExt>();
+    return *m;
 }
 NodeExt& ext(const NodeBackProp* n) { return ext_map()[n]; }
 void forget_ext(const NodeBackProp* n) { ext_map().erase(n); }
@@ -558,7 +561,8 @@ graph GraphOperations::ScaledDotAttention(const graph& Q, const graph& K, const 
     if (mle_attention_fused_supported(Sq, Sk, hd, axis, key_grad_mode)) {
         // fused kernels read and write the Linear layout directly; only P is kept
         float* P = arena_alloc(ARENA_ACT, ns, "Attention P");
-        GB += (double)(2 * nq + ns) * sizeof(float) / (1ULL << 30);
+        float* ws = arena_alloc(ARENA_WS, ns, "Attention dScores");
+        GB += (double)(2 * nq + 2 * ns) * sizeof(float) / (1ULL << 30);
         node->forward = [=]() {
             check(mle_attention_fwd(qp->output, kp->output, vp->output, P, nd->output, B, heads, Sq, Sk, hd, scale,
                                     causal, axis, MLE_ATTN_TOKEN_MAJOR, st()),
@@ -566,7 +570,7 @@ graph GraphOperations::ScaledDotAttention(const graph& Q, const graph& K, const 
         };
         node->backward = [=]() {
             check(mle_attention_bwd(qp->output, kp->output, vp->output, P, nd->grad, qp->grad, kp->grad, vp->grad,
-                                    nullptr, nullptr, B, heads, Sq, Sk, hd, scale, causal, axis, key_grad_mode,
+                                    nullptr, nullptr, ws, B, heads, Sq, Sk, hd, scale, causal, axis, key_grad_mode,
                                     MLE_ATTN_TOKEN_MAJOR, st()),
                   "Attention backward");
         };
@@ -598,8 +602,8 @@ graph GraphOperations::ScaledDotAttention(const graph& Q, const graph& K, const 
     };
     node->backward = [=]() {
         check(mle_headify(nd->grad, goh, B, heads, Sq, hd, 3, st()), "Attention dO");
-        check(mle_attention_bwd(qh, kh, vh, P, goh, gqh, gkh, gvh, dP, dS, B, heads, Sq, Sk, hd, scale, causal, axis,
-                                key_grad_mode, MLE_ATTN_HEAD_MAJOR, st()),
+        check(mle_attention_bwd(qh, kh, vh, P, goh, gqh, gkh, gvh, dP, dS, nullptr, B, heads, Sq, Sk, hd, scale,
+                                causal, axis, key_grad_mode, MLE_ATTN_HEAD_MAJOR, st()),
               "Attention backward");
         check(mle_headify(gqh, qp->grad, B, heads, Sq, hd, 1, st()), "Attention dQ");
         check(mle_headify(gkh, kp->grad, B, heads, Sk, hd, 1, st()), "Attention dK");

@@ -2,20 +2,28 @@
 //   scores = Q K^T, scaled = scale*scores, P = softmax_axis(scaled), O = P V.
 //
 // Fused path (column-wise softmax, the reference's "type 1", head_dim 16/32/64,
-// Sq <= 256): one 256-thread CTA per (batch, head) keeps Q (and dO) in shared
-// memory and walks the key axis in blocks of 32 columns.  A column of the
-// softmax needs every query row, which the CTA holds, so each key block is
-// finished inside the block loop; products that sum over keys (O, dQ and the
-// reference's key gradient) accumulate in registers across blocks in key
-// order.  Every sum is one FMA chain in the order the reference kernels use
-// (bcmm*: k ascending; SumRows / deriv_softmax: rows ascending), so P, O and
-// the gradients are bitwise those of the reference's kernel chain.  Q, K, V,
-// O and the gradients are read and written token-major ([B, S, H*hd], the
+// Sq, Sk <= 256).  A column of that softmax runs over every query row, a
+// row of O, dQ or of the reference's key gradient over every key, so each
+// direction is two kernels, one per axis:
+//   forward : probs  — CTA per (batch*head, 32 keys): scaled scores of all
+//                      query rows, the column softmax, P stored;
+//             pv     — CTA per (batch*head, 32 queries): O = P V;
+//   backward: cols   — CTA per (batch*head, 32 keys): dP = dO V^T, the column
+//                      dot, dScores = scale * P (dP - dot) into a workspace,
+//                      dV (and the true dK), complete for these keys;
+//             rows   — CTA per (batch*head, 32 queries): dQ = dScores K and
+//                      the reference's key gradient dScores Q.
+// Every sum is one FMA chain in the order the reference kernels use (bcmm*:
+// k ascending; SumRows / deriv_softmax: rows ascending), so P, O and the
+// gradients are bitwise those of the reference's kernel chain.  Q, K, V, O
+// and the gradients are read and written token-major ([B, S, H*hd], the
 // Linear layout) or head-major through strides, so no head copies are made.
 //
 // Other shapes run the composed path on the tensor-core GEMM (head-major).
 #include <float.h>
 
+#include <algorithm>
+#include <initializer_list>
 #include <type_traits>
 
 #include "common.cuh"
@@ -23,12 +31,16 @@
 namespace mle {
 namespace {
 
-constexpr int kNT = 256;  // threads per CTA
-constexpr int kTC = 32;   // key columns per block
+constexpr int kNT = 256;     // threads per CTA
+constexpr int kTC = 32;      // key columns per column-block CTA
+constexpr int kTR = 64;      // query rows per row-block CTA
+constexpr int kWarps = kNT / 32;
+constexpr int kMaxSeq = 256;
 
 struct AttnArgs {
     const float *Q, *K, *V, *P, *dO;
     float *Pout, *O, *dQ, *dK, *dV, *dPout, *dSout;
+    float* dScores;  // [B*H, Sq, Sk] workspace of the backward
     int B, H, Sq, Sk;
     float scale;
     int causal, key_mode;
@@ -49,262 +61,411 @@ inline void strides_for(int layout, int H, int S, int hd, int64_t& sb, int64_t& 
     }
 }
 
+// rows [0, rows) of a [*, HD] operand (row stride rs) into padded shared
+// rows of HD + 1 floats; rows >= valid are zero-filled
 template <int HD>
-__device__ __forceinline__ void load_rows(float* dst, const float* __restrict__ src, int rows, int64_t rs) {
-    for (int i = threadIdx.x; i < rows * HD; i += kNT) {
-        const int r = i / HD, d = i % HD;
-        dst[r * (HD + 1) + d] = src[(int64_t)r * rs + d];
+__device__ __forceinline__ void load_rows(float* dst, const float* __restrict__ src, int rows, int valid, int64_t rs) {
+    for (int i = threadIdx.x; i < rows * (HD / 4); i += kNT) {
+        const int r = i / (HD / 4), d4 = (i % (HD / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < valid) v = *reinterpret_cast<const float4*>(src + (int64_t)r * rs + d4);
+        float* o = dst + r * (HD + 1) + d4;
+        o[0] = v.x;
+        o[1] = v.y;
+        o[2] = v.z;
+        o[3] = v.w;
     }
 }
 
-// ------------------------------------------------------------------ forward
-template <int HD>
-__global__ void __launch_bounds__(kNT) attn_fwd_col_kernel(const AttnArgs a) {
-    extern __shared__ float sm[];
-    const int Sq = a.Sq, Sk = a.Sk;
-    float* Qs = sm;                        // [Sq][HD+1]
-    float* Ks = Qs + Sq * (HD + 1);        // [TC][HD+1]
-    float* Vs = Ks + kTC * (HD + 1);       // [TC][HD+1]
-    float* Ss = Vs + kTC * (HD + 1);       // [Sq][TC+1]
-    float* csum = Ss + Sq * (kTC + 1);     // [TC]
-    const int b = blockIdx.x / a.H, h = blockIdx.x % a.H, t = threadIdx.x;
-    const float* Qg = a.Q + b * a.qb + h * a.qh;
-    const float* Kg = a.K + b * a.kb + h * a.kh;
-    const float* Vg = a.V + b * a.kb + h * a.kh;
-    float* Pg = a.Pout + ((int64_t)b * a.H + h) * Sq * Sk;
-    float* Og = a.O + b * a.qb + h * a.qh;
-    load_rows<HD>(Qs, Qg, Sq, a.qs);
+// [rows, kTC] tile of a head's [Sq, Sk] matrix (column offset c0) into
+// shared rows of kTC + 1 floats, zero beyond Sk
+__device__ __forceinline__ void load_col_tile(float* dst, const float* __restrict__ src, int rows, int Sk, int c0) {
+    for (int i = threadIdx.x; i < rows * kTC; i += kNT) {
+        const int r = i / kTC, c = i % kTC;
+        dst[r * (kTC + 1) + c] = (c0 + c < Sk) ? src[(int64_t)r * Sk + c0 + c] : 0.f;
+    }
+}
 
-    // O accumulators: thread owns column d and rows r0, r0 + kNT/HD, ...
-    constexpr int RSTEP = kNT / HD;
-    constexpr int MAXJ = 256 / RSTEP;
-    const int d = t % HD, r0 = t / HD;
-    float acc[MAXJ];
-#pragma unroll
-    for (int j = 0; j < MAXJ; ++j) acc[j] = 0.f;
+// Register-tiled products.  Every output is one FMA chain over its
+// reduction index in ascending order (the reference kernels' order); a
+// thread keeps several such chains so each shared-memory load feeds more
+// than one FMA.
 
-    for (int c0 = 0; c0 < Sk; c0 += kTC) {
-        const int tc = min(kTC, Sk - c0);
-        __syncthreads();
-        for (int i = t; i < kTC * HD; i += kNT) {
-            const int c = i / HD, dd = i % HD;
-            const bool in = c < tc;
-            Ks[c * (HD + 1) + dd] = in ? Kg[(int64_t)(c0 + c) * a.ks + dd] : 0.f;
-            Vs[c * (HD + 1) + dd] = in ? Vg[(int64_t)(c0 + c) * a.ks + dd] : 0.f;
-        }
-        __syncthreads();
-        // scaled scores: one k-ordered FMA chain per entry, then Scale_Write
-        for (int i = t; i < Sq * kTC; i += kNT) {
-            const int r = i / kTC, c = i % kTC;
-            float s = 0.f;
+// out[r][c] = sum_k A[r][k] * B[c][k] (k < HD) for every query row r < Sq
+// and the kTC columns c of a block (A: [Sq][HD+1], B: [kTC][HD+1]).
+// Thread: columns c = t%8 + 8j, rows r = t/8 + 32i (4 x 4 chains per pass
+// of 128 rows).
+template <int HD, typename Epi>
+__device__ __forceinline__ void rows_times_cols(const float* As, const float* Bs, int Sq, Epi&& epi) {
+    const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;
+    for (int rb = 0; rb < Sq; rb += 128) {
+        float acc[4][4];
+        int ra[4];
 #pragma unroll
-            for (int k = 0; k < HD; ++k) s = fmaf(Qs[r * (HD + 1) + k], Ks[c * (HD + 1) + k], s);
-            Ss[r * (kTC + 1) + c] = a.scale * s;
-        }
-        __syncthreads();
-        // column softmax: max over every row (masked ones too, as FindMax),
-        // exp, rows summed in order (SumRows), all-zero column divided by 1
-        if (t < tc) {
-            float m = -FLT_MAX;
-            for (int r = 0; r < Sq; ++r) m = fmaxf(m, Ss[r * (kTC + 1) + t]);
-            float s = 0.f;
-            for (int r = 0; r < Sq; ++r) {
-                const float e = (a.causal && c0 + t > r) ? 0.0f : expf(Ss[r * (kTC + 1) + t] - m);
-                Ss[r * (kTC + 1) + t] = e;
-                s += e;
-            }
-            if (s < 1e-45f) s = 1.0f;
-            csum[t] = s;
-        }
-        __syncthreads();
-        for (int i = t; i < Sq * kTC; i += kNT) {
-            const int r = i / kTC, c = i % kTC;
-            if (c < tc) {
-                const float p = Ss[r * (kTC + 1) + c] / csum[c];
-                Ss[r * (kTC + 1) + c] = p;
-                Pg[(int64_t)r * Sk + c0 + c] = p;
-            } else {
-                Ss[r * (kTC + 1) + c] = 0.f;
-            }
-        }
-        __syncthreads();
-        // O += P_blk V_blk, keys in order
+        for (int i = 0; i < 4; ++i) {
+            ra[i] = min(rb + ty + 32 * i, Sq - 1) * (HD + 1);
 #pragma unroll
-        for (int j = 0; j < MAXJ; ++j) {
-            const int r = r0 + j * RSTEP;
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+        }
+#pragma unroll 8
+        for (int k = 0; k < HD; ++k) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[ra[i] + k];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[(tx + 8 * j) * (HD + 1) + k];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = rb + ty + 32 * i;
             if (r < Sq) {
-                float o = acc[j];
-                for (int c = 0; c < tc; ++c) o = fmaf(Ss[r * (kTC + 1) + c], Vs[c * (HD + 1) + d], o);
-                acc[j] = o;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) epi(r, tx + 8 * j, acc[i][j]);
             }
         }
     }
+}
+
+// out[x][d] = sum_y M[y][x] * R[y][d] (y < ny) for the kTC columns x of a
+// block (M: [ny][kTC+1], R: [ny][HD+1]).  Thread: x = t%16 + 16i (i < 2),
+// d = t/16 + 16j (j < HD/16).
+template <int HD, typename Epi>
+__device__ __forceinline__ void cols_t_times_rows(const float* Ms, const float* Rs, int ny, int nx, Epi&& epi) {
+    constexpr int JD = HD / 16;
+    const int tx = threadIdx.x & 15, td = threadIdx.x >> 4;
+    float acc[2][JD];
 #pragma unroll
-    for (int j = 0; j < MAXJ; ++j) {
-        const int r = r0 + j * RSTEP;
-        if (r < Sq) Og[(int64_t)r * a.qs + d] = acc[j];
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < JD; ++j) acc[i][j] = 0.f;
+#pragma unroll 4
+    for (int y = 0; y < ny; ++y) {
+        float m[2], r[JD];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) m[i] = Ms[y * (kTC + 1) + tx + 16 * i];
+#pragma unroll
+        for (int j = 0; j < JD; ++j) r[j] = Rs[y * (HD + 1) + td + 16 * j];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int j = 0; j < JD; ++j) acc[i][j] = fmaf(m[i], r[j], acc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int x = tx + 16 * i;
+        if (x < nx) {
+#pragma unroll
+            for (int j = 0; j < JD; ++j) epi(x, td + 16 * j, acc[i][j]);
+        }
+    }
+}
+
+// out_p[r][d] = sum_c M[r][c] * R_p[c][d] (c < nc) for the kTR rows r of a
+// block and one or two right operands R_p ([nc][HD+1]); M: [kTR][ldm].
+// Thread: r = t%16 + 16i (i < kTR/16), d = t/16 + 16j (j < HD/16); results
+// land in shared tiles O_p[kTR][HD+1], which may overlay M (the block
+// synchronises before writing them).
+template <int HD, int NP>
+__device__ __forceinline__ void rows_times_rows(const float* Ms, int ldm, const float* R0, const float* R1, int nc,
+                                                float* O0, float* O1) {
+    constexpr int JD = HD / 16, IR = kTR / 16;
+    const int tr = threadIdx.x & 15, td = threadIdx.x >> 4;
+    float acc[NP][IR][JD];
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int i = 0; i < IR; ++i)
+#pragma unroll
+            for (int j = 0; j < JD; ++j) acc[p][i][j] = 0.f;
+#pragma unroll 2
+    for (int c = 0; c < nc; ++c) {
+        float m[IR], r0[JD], r1[JD];
+#pragma unroll
+        for (int i = 0; i < IR; ++i) m[i] = Ms[(tr + 16 * i) * ldm + c];
+#pragma unroll
+        for (int j = 0; j < JD; ++j) {
+            r0[j] = R0[c * (HD + 1) + td + 16 * j];
+            if (NP > 1) r1[j] = R1[c * (HD + 1) + td + 16 * j];
+        }
+#pragma unroll
+        for (int i = 0; i < IR; ++i)
+#pragma unroll
+            for (int j = 0; j < JD; ++j) {
+                acc[0][i][j] = fmaf(m[i], r0[j], acc[0][i][j]);
+                if (NP > 1) acc[NP - 1][i][j] = fmaf(m[i], r1[j], acc[NP - 1][i][j]);
+            }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < IR; ++i)
+#pragma unroll
+        for (int j = 0; j < JD; ++j) {
+            const int o = (tr + 16 * i) * (HD + 1) + td + 16 * j;
+            O0[o] = acc[0][i][j];
+            if (NP > 1) O1[o] = acc[NP - 1][i][j];
+        }
+}
+
+// ------------------------------------------------------------------ forward
+// grid (B*H, ceil(Sk / kTC)): P[:, c0:c0+kTC] of one head
+template <int HD>
+__global__ void __launch_bounds__(kNT) attn_probs_kernel(const AttnArgs a) {
+    extern __shared__ float sm[];
+    const int Sq = a.Sq, Sk = a.Sk, c0 = blockIdx.y * kTC, tc = min(kTC, Sk - c0);
+    float* Qs = sm;                      // [Sq][HD+1]
+    float* Ks = Qs + Sq * (HD + 1);      // [kTC][HD+1]
+    float* Ss = Ks + kTC * (HD + 1);     // [Sq][kTC+1]
+    float* cred = Ss + Sq * (kTC + 1);   // [kWarps][kTC]
+    const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H, t = threadIdx.x;
+    load_rows<HD>(Qs, a.Q + b * a.qb + h * a.qh, Sq, Sq, a.qs);
+    load_rows<HD>(Ks, a.K + b * a.kb + h * a.kh + (int64_t)c0 * a.ks, kTC, tc, a.ks);
+    __syncthreads();
+    // scaled scores (bcmmABT chain, then Scale_Write's product)
+    const float scale = a.scale;
+    rows_times_cols<HD>(Qs, Ks, Sq, [&](int r, int c, float s) { Ss[r * (kTC + 1) + c] = scale * s; });
+    __syncthreads();
+    // column max over every row, masked ones included (FindMax); max is
+    // exact in any order
+    const int lane = t & 31, w = t >> 5;
+    {
+        float m = -FLT_MAX;
+        for (int r = w; r < Sq; r += kWarps) m = fmaxf(m, Ss[r * (kTC + 1) + lane]);
+        cred[w * kTC + lane] = m;
+    }
+    __syncthreads();
+    {
+        float m = cred[lane];
+#pragma unroll
+        for (int i = 1; i < kWarps; ++i) m = fmaxf(m, cred[i * kTC + lane]);
+        for (int r = w; r < Sq; r += kWarps) {
+            float* e = &Ss[r * (kTC + 1) + lane];
+            *e = (a.causal && c0 + lane > r) ? 0.0f : expf(*e - m);
+        }
+    }
+    __syncthreads();
+    // rows summed in order (SumRows); an all-zero column is divided by 1
+    if (t < kTC) {
+        float s = 0.f;
+#pragma unroll 8
+        for (int r = 0; r < Sq; ++r) s += Ss[r * (kTC + 1) + t];
+        if (s < 1e-45f) s = 1.0f;
+        cred[t] = s;
+    }
+    __syncthreads();
+    float* Pg = a.Pout + (int64_t)bh * Sq * Sk + c0;
+    for (int i = t; i < Sq * kTC; i += kNT) {
+        const int r = i / kTC, c = i % kTC;
+        if (c < tc) Pg[(int64_t)r * Sk + c] = Ss[r * (kTC + 1) + c] / cred[c];
+    }
+}
+
+// [kTR][Sk] rows r0.. of a head's [Sq][Sk] matrix into shared rows of
+// Sk + 1 floats, zero beyond Sq
+__device__ __forceinline__ void load_row_tile(float* dst, const float* __restrict__ src, int tr, int Sk) {
+    const int ldm = Sk + 1;
+    for (int i = threadIdx.x; i < kTR * Sk; i += kNT) {
+        const int r = i / Sk, c = i % Sk;
+        dst[r * ldm + c] = r < tr ? src[(int64_t)r * Sk + c] : 0.f;
+    }
+}
+
+// grid (B*H, ceil(Sq / kTR)): O[r0:r0+kTR] = P V
+template <int HD>
+__global__ void __launch_bounds__(kNT) attn_pv_kernel(const AttnArgs a) {
+    extern __shared__ float sm[];
+    const int Sq = a.Sq, Sk = a.Sk, r0 = blockIdx.y * kTR, tr = min(kTR, Sq - r0);
+    const int ldp = Sk + 1;
+    float* Ps = sm;                                   // [kTR][Sk+1]
+    float* Os = sm;                                   // [kTR][HD+1], overlays Ps
+    float* Vs = Ps + kTR * max(ldp, HD + 1);          // [Sk][HD+1]
+    const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+    load_row_tile(Ps, a.Pout + ((int64_t)bh * Sq + r0) * Sk, tr, Sk);
+    load_rows<HD>(Vs, a.V + b * a.kb + h * a.kh, Sk, Sk, a.ks);
+    __syncthreads();
+    rows_times_rows<HD, 1>(Ps, ldp, Vs, nullptr, Sk, Os, nullptr);
+    __syncthreads();
+    float* Og = a.O + b * a.qb + h * a.qh + (int64_t)r0 * a.qs;
+    for (int i = threadIdx.x; i < tr * HD; i += kNT) {
+        const int r = i / HD, d = i % HD;
+        Og[(int64_t)r * a.qs + d] = Os[r * (HD + 1) + d];
     }
 }
 
 // ----------------------------------------------------------------- backward
+// grid (B*H, ceil(Sk / kTC)): everything that sums over query rows for the
+// keys c0 .. c0+kTC
 template <int HD>
-__global__ void __launch_bounds__(kNT) attn_bwd_col_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kNT) attn_bwd_cols_kernel(const AttnArgs a) {
     extern __shared__ float sm[];
-    const int Sq = a.Sq, Sk = a.Sk;
-    float* Qs = sm;                        // [Sq][HD+1]
-    float* dOs = Qs + Sq * (HD + 1);       // [Sq][HD+1]
-    float* Ks = dOs + Sq * (HD + 1);       // [TC][HD+1]
-    float* Vs = Ks + kTC * (HD + 1);       // [TC][HD+1]
-    float* Ps = Vs + kTC * (HD + 1);       // [Sq][TC+1]
-    float* Ds = Ps + Sq * (kTC + 1);       // [Sq][TC+1]  dP, then dScores
-    float* dot = Ds + Sq * (kTC + 1);      // [TC]
-    const int b = blockIdx.x / a.H, h = blockIdx.x % a.H, t = threadIdx.x;
-    const int64_t qoff = b * a.qb + h * a.qh, koff = b * a.kb + h * a.kh;
-    const float* Pg = a.P + ((int64_t)b * a.H + h) * Sq * Sk;
-    const int64_t soff = ((int64_t)b * a.H + h) * Sq * Sk;
-    load_rows<HD>(Qs, a.Q + qoff, Sq, a.qs);
-    load_rows<HD>(dOs, a.dO + qoff, Sq, a.qs);
-
-    constexpr int RSTEP = kNT / HD;
-    constexpr int MAXJ = 256 / RSTEP;
-    const int d = t % HD, r0 = t / HD;
-    float accq[MAXJ], acck[MAXJ];
-#pragma unroll
-    for (int j = 0; j < MAXJ; ++j) accq[j] = acck[j] = 0.f;
+    const int Sq = a.Sq, Sk = a.Sk, c0 = blockIdx.y * kTC, tc = min(kTC, Sk - c0);
+    const bool true_dk = a.key_mode == MLE_KEYGRAD_TRUE;
+    float* dOs = sm;                      // [Sq][HD+1]
+    float* Vs = dOs + Sq * (HD + 1);      // [kTC][HD+1]
+    float* Ps = Vs + kTC * (HD + 1);      // [Sq][kTC+1]
+    float* Ds = Ps + Sq * (kTC + 1);      // [Sq][kTC+1]  dP, then dScores
+    float* dot = Ds + Sq * (kTC + 1);     // [kTC]
+    float* Qs = dot + kTC;                // [Sq][HD+1]  (true key gradient only)
+    const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H, t = threadIdx.x;
+    const int64_t qoff = b * a.qb + h * a.qh, koff = b * a.kb + h * a.kh + (int64_t)c0 * a.ks;
+    const int64_t soff = (int64_t)bh * Sq * Sk + c0;
+    load_rows<HD>(dOs, a.dO + qoff, Sq, Sq, a.qs);
+    load_rows<HD>(Vs, a.V + koff, kTC, tc, a.ks);
+    if (true_dk) load_rows<HD>(Qs, a.Q + qoff, Sq, Sq, a.qs);
+    load_col_tile(Ps, a.P + (int64_t)bh * Sq * Sk, Sq, Sk, c0);
+    __syncthreads();
+    // dP = dO V^T (bcmmABT: k = head_dim ascending)
+    rows_times_cols<HD>(dOs, Vs, Sq, [&](int r, int c, float s) { Ds[r * (kTC + 1) + c] = s; });
+    __syncthreads();
+    // deriv_softmax type 1: per column dot over rows in order
+    if (t < kTC) {
+        float s = 0.f;
+#pragma unroll 8
+        for (int r = 0; r < Sq; ++r) s = fmaf(Ds[r * (kTC + 1) + t], Ps[r * (kTC + 1) + t], s);
+        dot[t] = s;
+    }
+    __syncthreads();
+    // dScaled = P (dP - dot); dScores = (float)(scale * dScaled) as Accumulate
     const double dscale = (double)a.scale;
-
-    for (int c0 = 0; c0 < Sk; c0 += kTC) {
-        const int tc = min(kTC, Sk - c0);
-        __syncthreads();
-        for (int i = t; i < kTC * HD; i += kNT) {
-            const int c = i / HD, dd = i % HD;
-            const bool in = c < tc;
-            Ks[c * (HD + 1) + dd] = in ? a.K[koff + (int64_t)(c0 + c) * a.ks + dd] : 0.f;
-            Vs[c * (HD + 1) + dd] = in ? a.V[koff + (int64_t)(c0 + c) * a.ks + dd] : 0.f;
+    for (int i = t; i < Sq * kTC; i += kNT) {
+        const int r = i / kTC, c = i % kTC;
+        float v = 0.f;
+        if (c < tc) {
+            const float dp = Ds[r * (kTC + 1) + c];
+            if (a.dPout) a.dPout[soff + (int64_t)r * Sk + c] += dp;
+            const float ds = Ps[r * (kTC + 1) + c] * (dp - dot[c]);
+            if (a.dSout) a.dSout[soff + (int64_t)r * Sk + c] += ds;
+            v = (float)(0.0 + dscale * (double)ds);
+            a.dScores[soff + (int64_t)r * Sk + c] = v;
         }
-        for (int i = t; i < Sq * kTC; i += kNT) {
-            const int r = i / kTC, c = i % kTC;
-            Ps[r * (kTC + 1) + c] = (c < tc) ? Pg[(int64_t)r * Sk + c0 + c] : 0.f;
-        }
-        __syncthreads();
-        // dP = dO V^T (bcmmABT: k = head_dim ascending)
-        for (int i = t; i < Sq * kTC; i += kNT) {
-            const int r = i / kTC, c = i % kTC;
-            float s = 0.f;
-#pragma unroll
-            for (int k = 0; k < HD; ++k) s = fmaf(dOs[r * (HD + 1) + k], Vs[c * (HD + 1) + k], s);
-            Ds[r * (kTC + 1) + c] = s;
-            if (a.dPout && c < tc) a.dPout[soff + (int64_t)r * Sk + c0 + c] += s;
-        }
-        __syncthreads();
-        // deriv_softmax type 1: per column dot over rows in order
-        if (t < tc) {
-            float s = 0.f;
-            for (int r = 0; r < Sq; ++r) s = fmaf(Ds[r * (kTC + 1) + t], Ps[r * (kTC + 1) + t], s);
-            dot[t] = s;
-        }
-        __syncthreads();
-        // dScaled = P (dP - dot); dScores = (float)(scale * dScaled) as Accumulate
-        for (int i = t; i < Sq * kTC; i += kNT) {
-            const int r = i / kTC, c = i % kTC;
-            if (c < tc) {
-                const float ds = Ps[r * (kTC + 1) + c] * (Ds[r * (kTC + 1) + c] - dot[c]);
-                if (a.dSout) a.dSout[soff + (int64_t)r * Sk + c0 + c] += ds;
-                Ds[r * (kTC + 1) + c] = (float)(0.0 + dscale * (double)ds);
-            } else {
-                Ds[r * (kTC + 1) + c] = 0.f;
-            }
-        }
-        __syncthreads();
-        // per-key products of this block: dV = P^T dO, true dK = dS^T Q
-        // (bcmmATB: k = query row ascending)
-        for (int i = t; i < tc * HD; i += kNT) {
-            const int c = i / HD, dd = i % HD;
-            float sv = 0.f;
-            for (int r = 0; r < Sq; ++r) sv = fmaf(Ps[r * (kTC + 1) + c], dOs[r * (HD + 1) + dd], sv);
-            a.dV[koff + (int64_t)(c0 + c) * a.ks + dd] += sv;
-            if (a.key_mode == MLE_KEYGRAD_TRUE) {
-                float sk = 0.f;
-                for (int r = 0; r < Sq; ++r) sk = fmaf(Ds[r * (kTC + 1) + c], Qs[r * (HD + 1) + dd], sk);
-                a.dK[koff + (int64_t)(c0 + c) * a.ks + dd] += sk;
-            }
-        }
-        // sums over keys, continued across blocks in key order:
-        //   dQ = dScores K (bcmm), reference key gradient (dScores Q) of bcmmT
-#pragma unroll
-        for (int j = 0; j < MAXJ; ++j) {
-            const int r = r0 + j * RSTEP;
-            if (r < Sq) {
-                float q = accq[j], kr = acck[j];
-                for (int c = 0; c < tc; ++c) {
-                    const float ds = Ds[r * (kTC + 1) + c];
-                    q = fmaf(ds, Ks[c * (HD + 1) + d], q);
-                    if (a.key_mode == MLE_KEYGRAD_REFERENCE) kr = fmaf(ds, Qs[(c0 + c) * (HD + 1) + d], kr);
-                }
-                accq[j] = q;
-                acck[j] = kr;
-            }
-        }
+        Ds[r * (kTC + 1) + c] = v;
     }
-#pragma unroll
-    for (int j = 0; j < MAXJ; ++j) {
-        const int r = r0 + j * RSTEP;
-        if (r < Sq) {
-            a.dQ[qoff + (int64_t)r * a.qs + d] += accq[j];
-            if (a.key_mode == MLE_KEYGRAD_REFERENCE) {
-                // bcmmT(Q, dScores, Kh.grad, hd, Sq, Sk) writes element
-                // (row d, col r) of its [hd, Sk] result at d*Sk + r of the
-                // head's [Sk, hd] gradient block (Sq == Sk here)
-                const int pos = d * Sk + r;
-                a.dK[koff + (int64_t)(pos / HD) * a.ks + pos % HD] += acck[j];
-            }
+    __syncthreads();
+    // dV = P^T dO and the true dK = dScores^T Q for these keys
+    // (bcmmATB: k = query row ascending)
+    float* dVg = a.dV + koff;
+    const int64_t ks = a.ks;
+    cols_t_times_rows<HD>(Ps, dOs, Sq, tc, [&](int x, int d, float v) { dVg[(int64_t)x * ks + d] += v; });
+    if (true_dk) {
+        float* dKg = a.dK + koff;
+        cols_t_times_rows<HD>(Ds, Qs, Sq, tc, [&](int x, int d, float v) { dKg[(int64_t)x * ks + d] += v; });
+    }
+}
+
+// grid (B*H, ceil(Sq / kTR)): sums over keys for the query rows r0 ..
+// r0+kTR: dQ = dScores K (bcmm) and the reference key gradient
+// dScores Q (bcmmT)
+template <int HD>
+__global__ void __launch_bounds__(kNT) attn_bwd_rows_kernel(const AttnArgs a) {
+    extern __shared__ float sm[];
+    const int Sq = a.Sq, Sk = a.Sk, r0 = blockIdx.y * kTR, tr = min(kTR, Sq - r0);
+    const bool ref_dk = a.key_mode == MLE_KEYGRAD_REFERENCE;
+    const int ldm = Sk + 1;
+    float* Ms = sm;                                    // [kTR][Sk+1] dScores rows
+    float* Oq = sm;                                    // [kTR][HD+1] dQ rows, overlays Ms
+    float* Ok = Oq + kTR * (HD + 1);                   // [kTR][HD+1] reference key gradient
+    float* Ks = Ms + kTR * max(ldm, 2 * (HD + 1));     // [Sk][HD+1]
+    float* Qs = Ks + Sk * (HD + 1);                    // [Sk][HD+1]  (reference key gradient; Sq == Sk)
+    const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+    load_row_tile(Ms, a.dScores + ((int64_t)bh * Sq + r0) * Sk, tr, Sk);
+    const int64_t qoff = b * a.qb + h * a.qh, koff = b * a.kb + h * a.kh;
+    load_rows<HD>(Ks, a.K + koff, Sk, Sk, a.ks);
+    if (ref_dk) load_rows<HD>(Qs, a.Q + qoff, Sk, Sk, a.qs);
+    __syncthreads();
+    if (ref_dk) rows_times_rows<HD, 2>(Ms, ldm, Ks, Qs, Sk, Oq, Ok);
+    else rows_times_rows<HD, 1>(Ms, ldm, Ks, nullptr, Sk, Oq, nullptr);
+    __syncthreads();
+    float* dQg = a.dQ + qoff + (int64_t)r0 * a.qs;
+    for (int i = threadIdx.x; i < tr * HD; i += kNT) {
+        const int r = i / HD, d = i % HD;
+        dQg[(int64_t)r * a.qs + d] += Oq[r * (HD + 1) + d];
+    }
+    if (ref_dk) {
+        // bcmmT(Q, dScores, Kh.grad, hd, Sq, Sk) writes element (row d, col
+        // r) of its [hd, Sk] result at d*Sk + r of the head's [Sk, hd]
+        // gradient block: consecutive r are consecutive there
+        float* dKg = a.dK + koff;
+        for (int i = threadIdx.x; i < tr * HD; i += kNT) {
+            const int d = i / tr, r = i % tr;
+            const int pos = d * Sk + r0 + r;
+            dKg[(int64_t)(pos / HD) * a.ks + pos % HD] += Ok[r * (HD + 1) + d];
         }
     }
 }
 
 template <int HD>
-size_t fwd_smem(int Sq) {
-    return sizeof(float) * ((size_t)Sq * (HD + 1) + 2 * kTC * (HD + 1) + (size_t)Sq * (kTC + 1) + kTC);
+size_t probs_smem(int Sq) {
+    return sizeof(float) * ((size_t)Sq * (HD + 1) + kTC * (HD + 1) + (size_t)Sq * (kTC + 1) + kWarps * kTC);
 }
 template <int HD>
-size_t bwd_smem(int Sq) {
-    return sizeof(float) * (2 * (size_t)Sq * (HD + 1) + 2 * kTC * (HD + 1) + 2 * (size_t)Sq * (kTC + 1) + kTC);
+size_t pv_smem(int Sk) {
+    return sizeof(float) * ((size_t)kTR * std::max(Sk + 1, HD + 1) + (size_t)Sk * (HD + 1));
+}
+template <int HD>
+size_t bwd_cols_smem(int Sq, bool true_dk) {
+    return sizeof(float) * ((size_t)Sq * (HD + 1) * (true_dk ? 2 : 1) + kTC * (HD + 1) + 2 * (size_t)Sq * (kTC + 1) +
+                            kTC);
+}
+template <int HD>
+size_t bwd_rows_smem(int Sk, bool ref_dk) {
+    return sizeof(float) * ((size_t)kTR * std::max(Sk + 1, 2 * (HD + 1)) + (size_t)Sk * (HD + 1) * (ref_dk ? 2 : 1));
 }
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
+template <typename K>
+int set_smem(K kern, bool& done) {
+    if (!done) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem) != cudaSuccess)
+            return launch_status();
+        done = true;
+    }
+    return MLE_OK;
+}
+
 template <int HD>
 int launch_fwd(const AttnArgs& a, cudaStream_t st) {
-    const size_t smem = fwd_smem<HD>(a.Sq);
-    if (smem > kMaxSmem) return MLE_ERR_UNSUPPORTED;
-    static bool cfg = false;
-    if (!cfg) {
-        if (cudaFuncSetAttribute(attn_fwd_col_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem) !=
-            cudaSuccess)
-            return launch_status();
-        cfg = true;
-    }
-    attn_fwd_col_kernel<HD><<<a.B * a.H, kNT, smem, st>>>(a);
+    const size_t s1 = probs_smem<HD>(a.Sq), s2 = pv_smem<HD>(a.Sk);
+    if (s1 > kMaxSmem || s2 > kMaxSmem) return MLE_ERR_UNSUPPORTED;
+    static bool c1 = false, c2 = false;
+    int s = set_smem(attn_probs_kernel<HD>, c1);
+    if (s == MLE_OK) s = set_smem(attn_pv_kernel<HD>, c2);
+    if (s) return s;
+    attn_probs_kernel<HD><<<dim3(a.B * a.H, (a.Sk + kTC - 1) / kTC), kNT, s1, st>>>(a);
+    s = launch_status();
+    if (s) return s;
+    attn_pv_kernel<HD><<<dim3(a.B * a.H, (a.Sq + kTR - 1) / kTR), kNT, s2, st>>>(a);
     return launch_status();
 }
 
 template <int HD>
 int launch_bwd(const AttnArgs& a, cudaStream_t st) {
-    const size_t smem = bwd_smem<HD>(a.Sq);
-    if (smem > kMaxSmem) return MLE_ERR_UNSUPPORTED;
-    static bool cfg = false;
-    if (!cfg) {
-        if (cudaFuncSetAttribute(attn_bwd_col_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem) !=
-            cudaSuccess)
-            return launch_status();
-        cfg = true;
-    }
-    attn_bwd_col_kernel<HD><<<a.B * a.H, kNT, smem, st>>>(a);
+    const bool true_dk = a.key_mode == MLE_KEYGRAD_TRUE;
+    const size_t s1 = bwd_cols_smem<HD>(a.Sq, true_dk), s2 = bwd_rows_smem<HD>(a.Sk, !true_dk);
+    if (s1 > kMaxSmem || s2 > kMaxSmem) return MLE_ERR_UNSUPPORTED;
+    static bool c1 = false, c2 = false;
+    int s = set_smem(attn_bwd_cols_kernel<HD>, c1);
+    if (s == MLE_OK) s = set_smem(attn_bwd_rows_kernel<HD>, c2);
+    if (s) return s;
+    attn_bwd_cols_kernel<HD><<<dim3(a.B * a.H, (a.Sk + kTC - 1) / kTC), kNT, s1, st>>>(a);
+    s = launch_status();
+    if (s) return s;
+    attn_bwd_rows_kernel<HD><<<dim3(a.B * a.H, (a.Sq + kTR - 1) / kTR), kNT, s2, st>>>(a);
     return launch_status();
 }
 
-bool fused_ok(int axis, int Sq, int hd, int B, int H) {
-    return axis == 1 && Sq >= 1 && Sq <= 256 && (hd == 16 || hd == 32 || hd == 64) && (int64_t)B * H < (1ll << 31);
+bool fused_ok(int axis, int Sq, int Sk, int hd, int B, int H) {
+    return axis == 1 && Sq >= 1 && Sq <= kMaxSeq && Sk >= 1 && Sk <= kMaxSeq && (hd == 16 || hd == 32 || hd == 64) &&
+           (int64_t)B * H < (1ll << 31);
+}
+
+bool ptrs_aligned(std::initializer_list<const float*> ps) {
+    for (const float* q : ps)
+        if (!aligned16(q)) return false;
+    return true;
 }
 
 template <typename F>
@@ -324,10 +485,15 @@ using namespace mle;
 extern "C" {
 
 int mle_attention_fused_supported(int seq_q, int seq_k, int head_dim, int softmax_axis, int key_grad_mode) {
-    if (seq_k <= 0 || !fused_ok(softmax_axis, seq_q, head_dim, 1, 1)) return 0;
+    if (!fused_ok(softmax_axis, seq_q, seq_k, head_dim, 1, 1)) return 0;
     if (key_grad_mode == MLE_KEYGRAD_REFERENCE && seq_q != seq_k) return 0;
-    const size_t smem = head_dim == 16 ? bwd_smem<16>(seq_q) : head_dim == 32 ? bwd_smem<32>(seq_q) : bwd_smem<64>(seq_q);
-    return smem <= kMaxSmem ? 1 : 0;
+    const bool t = key_grad_mode == MLE_KEYGRAD_TRUE;
+    const int ok = dispatch_hd(head_dim, [&](auto hd) {
+        constexpr int HD = decltype(hd)::value;
+        return (int)(probs_smem<HD>(seq_q) <= kMaxSmem && pv_smem<HD>(seq_k) <= kMaxSmem &&
+                     bwd_cols_smem<HD>(seq_q, t) <= kMaxSmem && bwd_rows_smem<HD>(seq_k, !t) <= kMaxSmem);
+    });
+    return ok;
 }
 
 int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, float* O, int batch, int heads,
@@ -338,7 +504,7 @@ int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, 
     if ((softmax_axis != 0 && softmax_axis != 1) || (layout != MLE_ATTN_HEAD_MAJOR && layout != MLE_ATTN_TOKEN_MAJOR))
         return MLE_ERR_ARG;
     cudaStream_t st = as_stream(stream);
-    if (fused_ok(softmax_axis, seq_q, head_dim, batch, heads)) {
+    if (fused_ok(softmax_axis, seq_q, seq_k, head_dim, batch, heads) && ptrs_aligned({Q, K, V})) {
         AttnArgs a{};
         a.Q = Q;
         a.K = K;
@@ -366,9 +532,9 @@ int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, 
 }
 
 int mle_attention_bwd(const float* Q, const float* K, const float* V, const float* P, const float* dO, float* dQ,
-                      float* dK, float* dV, float* dP_out, float* dS_out, int batch, int heads, int seq_q, int seq_k,
-                      int head_dim, float scale, int causal, int softmax_axis, int key_grad_mode, int layout,
-                      mle_stream_t stream) {
+                      float* dK, float* dV, float* dP_out, float* dS_out, float* workspace, int batch, int heads,
+                      int seq_q, int seq_k, int head_dim, float scale, int causal, int softmax_axis,
+                      int key_grad_mode, int layout, mle_stream_t stream) {
     (void)causal;  // P is exactly zero where the mask applied, so dS is too
     if (!Q || !K || !V || !P || !dO || !dQ || !dK || !dV) return MLE_ERR_ARG;
     if (batch <= 0 || heads <= 0 || seq_q <= 0 || seq_k <= 0 || head_dim <= 0) return MLE_ERR_ARG;
@@ -377,7 +543,9 @@ int mle_attention_bwd(const float* Q, const float* K, const float* V, const floa
     if (key_grad_mode != MLE_KEYGRAD_REFERENCE && key_grad_mode != MLE_KEYGRAD_TRUE) return MLE_ERR_ARG;
     cudaStream_t st = as_stream(stream);
     const bool ref_shape_ok = key_grad_mode == MLE_KEYGRAD_TRUE || seq_q == seq_k;
-    if (fused_ok(softmax_axis, seq_q, head_dim, batch, heads) && ref_shape_ok) {
+    if (fused_ok(softmax_axis, seq_q, seq_k, head_dim, batch, heads) && ref_shape_ok &&
+        ptrs_aligned({Q, K, V, dO})) {
+        if (!workspace) return MLE_ERR_ARG;
         AttnArgs a{};
         a.Q = Q;
         a.K = K;
@@ -389,6 +557,7 @@ int mle_attention_bwd(const float* Q, const float* K, const float* V, const floa
         a.dV = dV;
         a.dPout = dP_out;
         a.dSout = dS_out;
+        a.dScores = workspace;
         a.B = batch;
         a.H = heads;
         a.Sq = seq_q;

@@ -3,14 +3,17 @@
 // The reference multiplies with 32x32 shared-memory tiles, one output per
 // thread, and atomics for every `backward` output (bcmm*,
 // Engine/kernels.cu:387-539).  This kernel computes the same products with
-// tcgen05.mma kind::tf32:
-//   * operand tiles stream through a STAGES-deep shared-memory ring, loaded
-//     by TMA (cp.async.bulk.tensor, 128-byte swizzle) and tracked by
-//     mbarriers (full: TMA bytes landed; empty: the MMAs reading the slot
+// tcgen05.mma kind::tf32 as a persistent, warp-specialised kernel (one CTA
+// per SM walking the 128 x BN output tiles):
+//   * warp 0 (one lane) streams operand tiles through a STAGES-deep shared-
+//     memory ring with TMA (cp.async.bulk.tensor, 128-byte swizzle), tracked
+//     by mbarriers (full: bytes landed; empty: the MMAs reading the slot
 //     retired, signalled by tcgen05.commit);
-//   * one thread issues 128 x BN x 8 MMAs into a TMEM accumulator;
-//   * four warps drain TMEM with tcgen05.ld and apply the epilogue
-//     (assign, += or atomic add, alpha, optional bias).
+//   * warp 1 (one lane) issues 128 x BN x 8 MMAs into one of two TMEM
+//     accumulators, so a tile's epilogue overlaps the next tile's MMAs;
+//   * warps 2-5 drain TMEM with tcgen05.ld, transpose each 32 x 32 block
+//     through shared memory and apply the epilogue (assign, += or atomic
+//     add, alpha, optional bias) with row-contiguous 128-byte accesses.
 // Both K-major and MN-major operands are read straight from their row-major
 // storage (instruction-descriptor transpose bits), so dX = dY*W^T and
 // dW = X^T*dY need no transposed copies.
@@ -32,7 +35,9 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 32;                   // fp32 elements per k-block = one 128-byte swizzle row
-constexpr int kThreads = 128;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA, 4 epilogue warps
+constexpr int kEpiLd = 36;                      // staging row pitch (floats): float4-aligned, conflict-free
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s
 
 enum EpiMode { EPI_ASSIGN = 0, EPI_ACCUM = 1, EPI_ATOMIC = 2 };
@@ -46,9 +51,40 @@ struct EpiParams {
     int channels;                     // z = (b * channels + c) * splits + split
     int splits, kb_per_split;
     int a_has_b, a_has_c, b_has_b, b_has_c;
+    int m_tiles, n_tiles;
+    int64_t tiles;                    // m_tiles * n_tiles * batch * channels * splits
     float alpha;
     int mode;
+    int vec;                          // C rows (and bias) 16-byte aligned
+    int tma_epi;                      // C leaves through bulk tensor stores / reduce-adds (tmC)
+    int c_has_b, c_has_c;             // C varies over batch / channel (tensor-map coordinates)
 };
+
+// Output tile `t` of the persistent walk: n fastest, then m, then (batch,
+// channel, split).
+struct Tile {
+    int m0, n0, bidx, cidx, kb_begin, nkb;
+};
+
+__device__ __forceinline__ Tile tile_at(const EpiParams& ep, int64_t t, int BN) {
+    Tile x;
+    const int n = (int)(t % ep.n_tiles);
+    t /= ep.n_tiles;
+    const int m = (int)(t % ep.m_tiles);
+    int64_t z = t / ep.m_tiles;
+    const int split = (int)(z % ep.splits);
+    z /= ep.splits;
+    x.cidx = (int)(z % ep.channels);
+    x.bidx = (int)(z / ep.channels);
+    x.m0 = m * 128;
+    x.n0 = n * BN;
+    const int kb_total = (ep.K + 31) / 32;
+    x.kb_begin = split * ep.kb_per_split;
+    int kb_end = x.kb_begin + ep.kb_per_split;
+    if (kb_end > kb_total) kb_end = kb_total;
+    x.nkb = kb_end > x.kb_begin ? kb_end - x.kb_begin : 0;
+    return x;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -65,6 +101,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
@@ -117,6 +157,40 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
+
+// Epilogue stores: a 32 x 32 fp32 block staged in shared memory (128-byte
+// swizzle) leaves with one bulk tensor store, or a bulk tensor reduce-add
+// (C += block) for the accumulate and split-K modes.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                                  int c3) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most N committed bulk groups may still be reading shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Programmatic dependent launch: wait for the preceding kernel's writes,
+// then let the following kernel start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // UMMA shared-memory descriptor (sm100 version bits).  Layout types:
 // 2 = 128-byte swizzle with 16-byte atoms (K-major operands),
@@ -183,52 +257,53 @@ struct Smem {
     static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
     static constexpr int B_BYTES = BN * BK * 4;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
-    static constexpr int TOTAL = BAR_OFFSET + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
+    static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
+    static constexpr int EPI_WARP_BYTES = 2 * 32 * 32 * 4;  // two 4 KB blocks (>= 32 x kEpiLd floats)
+    static constexpr int BAR_OFFSET = EPI_OFFSET + kEpiWarps * EPI_WARP_BYTES;
+    // full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], drain
+    static constexpr int N_BARS = 2 * STAGES + 5;
+    static constexpr int TOTAL = BAR_OFFSET + N_BARS * 8 + 16 + 1024;  // + TMEM slot, abort flag, alignment
 };
 
 // A_MN: A is stored MN-major ([K][M]); B_MN: B is stored MN-major ([K][N]).
 template <bool A_MN, bool B_MN, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const EpiParams ep) {
+                     const __grid_constant__ CUtensorMap tmC, const EpiParams ep) {
     using L = Smem<BN, STAGES>;
+    static_assert(L::EPI_WARP_BYTES >= 32 * kEpiLd * 4, "staging");
+    constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
     uint64_t* empty = full + STAGES;
     uint64_t* tmem_full = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint64_t* drain = tmem_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN;
-    const int m0 = blockIdx.y * BM;
-    int z = blockIdx.z;
-    const int split = z % ep.splits;
-    z /= ep.splits;
-    const int cidx = z % ep.channels;
-    const int bidx = z / ep.channels;
-    const int kb_total = (ep.K + BK - 1) / BK;
-    const int kb_begin = split * ep.kb_per_split;
-    int kb_end = kb_begin + ep.kb_per_split;
-    if (kb_end > kb_total) kb_end = kb_total;
-    const int nkb = kb_end > kb_begin ? kb_end - kb_begin : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(tmem_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], kEpiWarps);
+        }
+        mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+        if (ep.tma_epi) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmC)) : "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"((uint32_t)BN)
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -236,130 +311,246 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // everything above overlapped the previous kernel; its outputs are read
+    // (and C written) only from here on
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
 
-    const int a_c = ep.a_has_c ? cidx : 0, a_b = ep.a_has_b ? bidx : 0;
-    const int b_c = ep.b_has_c ? cidx : 0, b_b = ep.b_has_b ? bidx : 0;
-
-    if (warp == 0 && lane == 0) {
-        // ------------------------------ TMA producer ------------------------------
-        uint32_t last_parity[STAGES];
-        bool issued[STAGES];
-        for (int s = 0; s < STAGES; ++s) issued[s] = false;
-        int s = 0;
-        uint32_t ph = 0;
-        for (int i = 0; i < nkb; ++i) {
-            if (!wait_bounded(&empty[s], ph ^ 1u, abort_flag)) break;
-            uint8_t* sa = smem + s * L::STAGE_BYTES;
-            uint8_t* sb = sa + L::A_BYTES;
-            const int k0 = (kb_begin + i) * BK;
-            mbar_arrive_expect_tx(&full[s], (uint32_t)L::STAGE_BYTES);
-            if (A_MN) {
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------ TMA producer ------------------------------
+            uint32_t last_parity[STAGES];
+            bool issued[STAGES];
+            for (int s = 0; s < STAGES; ++s) issued[s] = false;
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; ok && t < ep.tiles; t += gridDim.x) {
+                const Tile x = tile_at(ep, t, BN);
+                const int a_c = ep.a_has_c ? x.cidx : 0, a_b = ep.a_has_b ? x.bidx : 0;
+                const int b_c = ep.b_has_c ? x.cidx : 0, b_b = ep.b_has_b ? x.bidx : 0;
+                for (int i = 0; i < x.nkb; ++i) {
+                    if (!wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + s * L::STAGE_BYTES;
+                    uint8_t* sb = sa + L::A_BYTES;
+                    const int k0 = (x.kb_begin + i) * BK;
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)L::STAGE_BYTES);
+                    if (A_MN) {
 #pragma unroll
-                for (int j = 0; j < BM / 32; ++j) tma_load_4d(&tmA, &full[s], sa + j * 4096, m0 + 32 * j, k0, a_c, a_b);
-            } else {
-                tma_load_4d(&tmA, &full[s], sa, k0, m0, a_c, a_b);
-            }
-            if (B_MN) {
+                        for (int j = 0; j < BM / 32; ++j)
+                            tma_load_4d(&tmA, &full[s], sa + j * 4096, x.m0 + 32 * j, k0, a_c, a_b);
+                    } else {
+                        tma_load_4d(&tmA, &full[s], sa, k0, x.m0, a_c, a_b);
+                    }
+                    if (B_MN) {
 #pragma unroll
-                for (int j = 0; j < BN / 32; ++j) tma_load_4d(&tmB, &full[s], sb + j * 4096, n0 + 32 * j, k0, b_c, b_b);
-            } else {
-                tma_load_4d(&tmB, &full[s], sb, k0, n0, b_c, b_b);
+                        for (int j = 0; j < BN / 32; ++j)
+                            tma_load_4d(&tmB, &full[s], sb + j * 4096, x.n0 + 32 * j, k0, b_c, b_b);
+                    } else {
+                        tma_load_4d(&tmB, &full[s], sb, k0, x.n0, b_c, b_b);
+                    }
+                    issued[s] = true;
+                    last_parity[s] = ph;
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
             }
-            issued[s] = true;
-            last_parity[s] = ph;
-            if (++s == STAGES) {
-                s = 0;
-                ph ^= 1u;
+            if (*abort_flag) {
+                for (int u = 0; u < STAGES; ++u)
+                    if (issued[u]) drain_wait(&full[u], last_parity[u]);
             }
         }
-        if (*abort_flag) {
-            for (int t = 0; t < STAGES; ++t)
-                if (issued[t]) drain_wait(&full[t], last_parity[t]);
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------- MMA issuer -------------------------------
+            // instruction descriptor: D=f32, A=B=tf32, transpose bits, N>>3, M>>4
+            const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                                   ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                                   ((uint32_t)(BM >> 4) << 24);
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int acc = 0;
+            for (int64_t t = blockIdx.x; ok && t < ep.tiles; t += gridDim.x, ++acc) {
+                const Tile x = tile_at(ep, t, BN);
+                const int buf = acc & 1;
+                const uint32_t use = (uint32_t)(acc >> 1);
+                if (!wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
+                for (int i = 0; i < x.nkb; ++i) {
+                    if (!wait_bounded(&full[s], ph, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
+                    const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        const uint64_t ad = A_MN ? mnmajor_desc(sa, kk) : kmajor_desc(sa, kk);
+                        const uint64_t bd = B_MN ? mnmajor_desc(sb, kk) : kmajor_desc(sb, kk);
+                        mma_tf32(tmem_d, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(&tmem_full[buf]);  // arrives once every MMA of this tile retired
+            }
+            // every MMA issued above retires before TMEM is released
+            mma_commit(drain);
+            drain_wait(drain, 0);
         }
-    } else if (warp == 1 && lane == 0) {
-        // ------------------------------- MMA issuer -------------------------------
-        // instruction descriptor: D=f32, A=B=tf32, transpose bits, N>>3, M>>4
-        const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
-                               ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-        int s = 0;
-        uint32_t ph = 0;
-        for (int i = 0; i < nkb; ++i) {
-            if (!wait_bounded(&full[s], ph, abort_flag)) break;
+        __syncwarp();
+    } else {
+        // --------------------------------- epilogue ---------------------------------
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        float* stage = reinterpret_cast<float*>(smem + L::EPI_OFFSET + (warp - 2) * L::EPI_WARP_BYTES);
+        const int rsub = lane >> 3, c4 = (lane & 7) * 4;
+        int acc = 0;
+        uint32_t blocks_out = 0;  // bulk groups this warp committed
+        for (int64_t t = blockIdx.x; t < ep.tiles; t += gridDim.x, ++acc) {
+            const Tile x = tile_at(ep, t, BN);
+            const int buf = acc & 1;
+            const uint32_t use = (uint32_t)(acc >> 1);
+            // the tcgen05.ld below is warp-collective: leave the loop together
+            const bool ready = wait_bounded(&tmem_full[buf], use & 1u, abort_flag);
+            if (!__all_sync(0xffffffffu, ready)) break;
             tc_fence_after();
-            const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
-            const uint32_t sb = sa + L::A_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < BK / 8; ++kk) {
-                const uint64_t ad = A_MN ? mnmajor_desc(sa, kk) : kmajor_desc(sa, kk);
-                const uint64_t bd = B_MN ? mnmajor_desc(sb, kk) : kmajor_desc(sb, kk);
-                mma_tf32(tmem_base, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-            }
-            mma_commit(&empty[s]);
-            if (++s == STAGES) {
-                s = 0;
-                ph ^= 1u;
-            }
-        }
-        mma_commit(tmem_full);  // arrives once every MMA issued above retired
-    }
-    __syncwarp();
-
-    // --------------------------------- epilogue ---------------------------------
-    drain_wait(tmem_full, 0);
-    tc_fence_after();
-    const bool skip = (*abort_flag != 0) || nkb == 0;
-    const int row = m0 + warp * 32 + lane;
-    float* Cbase = ep.C + (int64_t)bidx * ep.c_stride_b + (int64_t)cidx * ep.c_stride_c;
-    const bool row_ok = row < ep.M;
-    float* crow = Cbase + (int64_t)(row_ok ? row : 0) * ep.ldc;
-    const bool vec_ok = ((ep.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(Cbase) & 15u) == 0);
+            float* Cbase = ep.C + (int64_t)x.bidx * ep.c_stride_b + (int64_t)x.cidx * ep.c_stride_c;
+            const bool live = x.nkb > 0;
 #pragma unroll 1
-    for (int cc = 0; cc < BN / 32; ++cc) {
-        const int col0 = n0 + cc * 32;
-        if (col0 >= ep.N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cc * 32), r);
-        if (skip || !row_ok) continue;
-        float v[32];
+            for (int cc = 0; cc < BN / 32; ++cc) {
+                const int col0 = x.n0 + cc * 32;
+                if (col0 >= ep.N) break;  // warp-uniform
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + cc * 32), r);
+                if (!live) continue;
+                if (ep.tma_epi) {
+                    const int row0 = x.m0 + q * 32;
+                    if (row0 >= ep.M) continue;  // warp-uniform: this quarter lies below the matrix
+                    float* blk = stage + (blocks_out & 1u) * 1024;
+                    if (blocks_out >= 2) {
+                        if (lane == 0) bulk_wait_read<1>();
+                        __syncwarp();
+                    }
+                    // row `lane` of the block: alpha * acc + bias, 16-byte chunk j
+                    // stored at chunk j ^ (row % 8) (128-byte swizzle)
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
-        if (ep.bias) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < ep.N) v[j] += ep.bias[col0 + j];
-        }
-        if (vec_ok && col0 + 32 <= ep.N) {
-            float4* dst = reinterpret_cast<float4*>(crow + col0);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                float4 val = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                if (ep.mode == EPI_ASSIGN) {
-                    dst[q] = val;
-                } else if (ep.mode == EPI_ACCUM) {
-                    float4 o = dst[q];
-                    o.x += val.x; o.y += val.y; o.z += val.z; o.w += val.w;
-                    dst[q] = o;
-                } else {
-                    atomicAdd(dst + q, val);
+                    for (int j = 0; j < 8; ++j) {
+                        float4 v = make_float4(ep.alpha * __uint_as_float(r[4 * j]),
+                                               ep.alpha * __uint_as_float(r[4 * j + 1]),
+                                               ep.alpha * __uint_as_float(r[4 * j + 2]),
+                                               ep.alpha * __uint_as_float(r[4 * j + 3]));
+                        if (ep.bias) {
+                            const int cb = col0 + 4 * j;
+                            if (ep.vec && cb + 4 <= ep.N) {
+                                const float4 b = *reinterpret_cast<const float4*>(ep.bias + cb);
+                                v.x += b.x;
+                                v.y += b.y;
+                                v.z += b.z;
+                                v.w += b.w;
+                            } else {
+                                if (cb < ep.N) v.x += ep.bias[cb];
+                                if (cb + 1 < ep.N) v.y += ep.bias[cb + 1];
+                                if (cb + 2 < ep.N) v.z += ep.bias[cb + 2];
+                                if (cb + 3 < ep.N) v.w += ep.bias[cb + 3];
+                            }
+                        }
+                        *reinterpret_cast<float4*>(blk + lane * 32 + ((j ^ (lane & 7)) * 4)) = v;
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int cz = ep.c_has_c ? x.cidx : 0, bz = ep.c_has_b ? x.bidx : 0;
+                        if (ep.mode == EPI_ASSIGN) tma_store_4d(&tmC, blk, col0, row0, cz, bz);
+                        else tma_reduce_add_4d(&tmC, blk, col0, row0, cz, bz);
+                        bulk_commit();
+                    }
+                    ++blocks_out;
+                    continue;
                 }
-            }
-        } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int col = col0 + j;
-                if (col < ep.N) {
-                    if (ep.mode == EPI_ASSIGN) crow[col] = v[j];
-                    else if (ep.mode == EPI_ACCUM) crow[col] += v[j];
-                    else atomicAdd(crow + col, v[j]);
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<float4*>(stage + lane * kEpiLd + 4 * j) =
+                        make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                    __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+                __syncwarp();
+                const int col = col0 + c4;
+                const bool vec = ep.vec && col + 4 <= ep.N;
+                float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (ep.bias) {
+                    if (vec) {
+                        bv = *reinterpret_cast<const float4*>(ep.bias + col);
+                    } else {
+                        if (col < ep.N) bv.x = ep.bias[col];
+                        if (col + 1 < ep.N) bv.y = ep.bias[col + 1];
+                        if (col + 2 < ep.N) bv.z = ep.bias[col + 2];
+                        if (col + 3 < ep.N) bv.w = ep.bias[col + 3];
+                    }
                 }
+#pragma unroll 4
+                for (int it = 0; it < 8; ++it) {
+                    const int rr = it * 4 + rsub;
+                    const int row = x.m0 + q * 32 + rr;
+                    if (row >= ep.M || col >= ep.N) continue;
+                    float4 v = *reinterpret_cast<const float4*>(stage + rr * kEpiLd + c4);
+                    v.x = ep.alpha * v.x + bv.x;
+                    v.y = ep.alpha * v.y + bv.y;
+                    v.z = ep.alpha * v.z + bv.z;
+                    v.w = ep.alpha * v.w + bv.w;
+                    float* crow = Cbase + (int64_t)row * ep.ldc;
+                    if (vec) {
+                        float4* dst = reinterpret_cast<float4*>(crow + col);
+                        if (ep.mode == EPI_ASSIGN) {
+                            *dst = v;
+                        } else if (ep.mode == EPI_ACCUM) {
+                            float4 o = *dst;
+                            o.x += v.x;
+                            o.y += v.y;
+                            o.z += v.z;
+                            o.w += v.w;
+                            *dst = o;
+                        } else {
+                            atomicAdd(dst, v);
+                        }
+                    } else {
+                        const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (col + u >= ep.N) break;
+                            if (ep.mode == EPI_ASSIGN) crow[col + u] = e[u];
+                            else if (ep.mode == EPI_ACCUM) crow[col + u] += e[u];
+                            else atomicAdd(crow + col + u, e[u]);
+                        }
+                    }
+                }
+                __syncwarp();
             }
+            // this accumulator may be overwritten once every lane's loads retired
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[buf]);
         }
+        // bulk stores must finish reading shared memory (and land) before exit
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)BN)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
                      : "memory");
     }
 }
@@ -415,9 +606,10 @@ static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
-static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& ep, int grid_x, int grid_y,
-                     int grid_z, cudaStream_t st) {
+static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const EpiParams& ep,
+                     cudaStream_t st) {
     using L = Smem<BN, STAGES>;
+    static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
     auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, STAGES>;
     static bool configured = false;
     if (!configured) {
@@ -425,7 +617,20 @@ static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const EpiPara
             return launch_status();
         configured = true;
     }
-    kern<<<dim3(grid_x, grid_y, grid_z), kThreads, L::TOTAL, st>>>(ma, mb, ep);
+    // persistent: one CTA per SM (the shared-memory ring admits one); the
+    // prologue may overlap the previous kernel (programmatic dependent launch)
+    const int grid = (int)(ep.tiles < kSMs ? ep.tiles : kSMs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, ep) != cudaSuccess) return launch_status();
     return launch_status();
 }
 
@@ -459,26 +664,25 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     const int m_tiles = (p.M + BM - 1) / BM;
     const int kb_total = (p.K + BK - 1) / BK;
 
-    int BN = 128;
-    {
-        const int64_t t256 = (int64_t)m_tiles * ((p.N + 255) / 256) * z_count;
-        const int64_t t128 = (int64_t)m_tiles * ((p.N + 127) / 128) * z_count;
-        if (p.N >= 256 && t256 >= 2 * kSMs) BN = 256;
-        else if (p.N > 64 && t128 >= kSMs) BN = 128;
-        else if (p.N <= 64) BN = 64;
-        else BN = (t128 >= kSMs / 2) ? 128 : 64;
+    // Widest tile that still gives every SM a tile; narrow tiles otherwise.
+    int BN = 64;
+    for (int cand : {256, 128}) {
+        const int64_t t = (int64_t)m_tiles * ((p.N + cand - 1) / cand) * z_count;
+        if (p.N >= cand && t >= kSMs) {
+            BN = cand;
+            break;
+        }
     }
     const int n_tiles = (p.N + BN - 1) / BN;
     const int64_t tiles = (int64_t)m_tiles * n_tiles * z_count;
     int splits = 1;
     if (p.mode != EPI_ASSIGN && tiles < kSMs && kb_total >= 8) {
-        splits = (int)((2 * kSMs + tiles - 1) / tiles);
+        splits = (int)((kSMs + tiles - 1) / tiles);
         if (splits > kb_total / 4) splits = kb_total / 4;
         if (splits < 1) splits = 1;
     }
     const int kb_per_split = (kb_total + splits - 1) / splits;
     splits = (kb_total + kb_per_split - 1) / kb_per_split;
-    if (z_count * splits > 65535 || m_tiles > 65535) return simt_gemm(p, st);
 
     EpiParams ep;
     ep.C = p.C;
@@ -498,8 +702,13 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     ep.b_has_c = (p.b_sc != 0 && p.channels > 1);
     if (p.nbatch == 1) ep.c_stride_b = 0;
     if (p.channels == 1) ep.c_stride_c = 0;
+    ep.m_tiles = m_tiles;
+    ep.n_tiles = n_tiles;
+    ep.tiles = tiles * splits;
     ep.alpha = p.alpha;
     ep.mode = (splits > 1) ? EPI_ATOMIC : p.mode;
+    ep.vec = ((p.ldc & 3) == 0) && aligned16(p.C) && ((ep.c_stride_b & 3) == 0) && ((ep.c_stride_c & 3) == 0) &&
+             (p.bias == nullptr || aligned16(p.bias));
     if (splits > 1 && p.bias) return simt_gemm(p, st);  // bias with split-K would be added per split
 
     OperandView va, vb;
@@ -524,18 +733,35 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     memset(&mb, 0, sizeof(mb));
     if (!encode_operand(&ma, va, 32, A_MN ? BK : BM, A_MN)) return simt_gemm(p, st);
     if (!encode_operand(&mb, vb, 32, B_MN ? BK : BN, B_MN)) return simt_gemm(p, st);
+    // C through bulk tensor stores when its rows and strides allow TMA
+    CUtensorMap mc;
+    memset(&mc, 0, sizeof(mc));
+    ep.c_has_b = (ep.c_stride_b != 0);
+    ep.c_has_c = (ep.c_stride_c != 0);
+    ep.tma_epi = 0;
+    if (aligned16(p.C) && (p.ldc & 3) == 0 && (ep.c_stride_b & 3) == 0 && (ep.c_stride_c & 3) == 0) {
+        OperandView vc;
+        vc.base = p.C;
+        vc.inner = p.N;
+        vc.outer = p.M;
+        vc.ld = p.ldc;
+        vc.nc = ep.c_has_c ? p.channels : 1;
+        vc.nb = ep.c_has_b ? p.nbatch : 1;
+        vc.sc = ep.c_stride_c;
+        vc.sb = ep.c_stride_b;
+        ep.tma_epi = encode_operand(&mc, vc, 32, 32) ? 1 : 0;
+    }
 
-    const int gx = n_tiles, gy = m_tiles, gz = (int)(z_count * splits);
-#define MLE_TC(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST>(ma, mb, ep, gx, gy, gz, st)
+#define MLE_TC(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST>(ma, mb, mc, ep, st)
     if (BN == 256) {
         if (A_MN) { if (B_MN) MLE_TC(true, true, 256, 4); else MLE_TC(true, false, 256, 4); }
         else { if (B_MN) MLE_TC(false, true, 256, 4); else MLE_TC(false, false, 256, 4); }
     } else if (BN == 128) {
-        if (A_MN) { if (B_MN) MLE_TC(true, true, 128, 6); else MLE_TC(true, false, 128, 6); }
-        else { if (B_MN) MLE_TC(false, true, 128, 6); else MLE_TC(false, false, 128, 6); }
+        if (A_MN) { if (B_MN) MLE_TC(true, true, 128, 5); else MLE_TC(true, false, 128, 5); }
+        else { if (B_MN) MLE_TC(false, true, 128, 5); else MLE_TC(false, false, 128, 5); }
     } else {
-        if (A_MN) { if (B_MN) MLE_TC(true, true, 64, 8); else MLE_TC(true, false, 64, 8); }
-        else { if (B_MN) MLE_TC(false, true, 64, 8); else MLE_TC(false, false, 64, 8); }
+        if (A_MN) { if (B_MN) MLE_TC(true, true, 64, 6); else MLE_TC(true, false, 64, 6); }
+        else { if (B_MN) MLE_TC(false, true, 64, 6); else MLE_TC(false, false, 64, 6); }
     }
 #undef MLE_TC
 }

@@ -189,9 +189,14 @@ def attention_fwd(Q, K, V, P, O, batch, heads, seq_q, seq_k, head_dim, scale, ca
 
 
 def attention_bwd(Q, K, V, P, dO, dQ, dK, dV, dP, dS, batch, heads, seq_q, seq_k, head_dim, scale, causal=0,
-                  softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE, layout=HEAD_MAJOR):
-    _call("mle_attention_bwd", _p(Q), _p(K), _p(V), _p(P), _p(dO), _p(dQ), _p(dK), _p(dV), _p(dP), _p(dS), batch,
-          heads, seq_q, seq_k, head_dim, scale, causal, softmax_axis, key_grad_mode, layout, _s())
+                  softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE, layout=HEAD_MAJOR, workspace=None):
+    """workspace: batch*heads*seq_q*seq_k floats for the fused path; made
+    here when not given."""
+    if workspace is None and attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis, key_grad_mode):
+        workspace = torch.empty(batch * heads * seq_q * seq_k, device=Q.device, dtype=torch.float32)
+    _call("mle_attention_bwd", _p(Q), _p(K), _p(V), _p(P), _p(dO), _p(dQ), _p(dK), _p(dV), _p(dP), _p(dS),
+          _p(workspace), batch, heads, seq_q, seq_k, head_dim, scale, causal, softmax_axis, key_grad_mode, layout,
+          _s())
 
 
 def attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE):

@@ -343,6 +343,7 @@ ATTN_CASES = [  # B, H, Sq, Sk, hd, axis, causal
     (2, 4, 64, 64, 64, 1, 1),     # masked (SoftMask): fused
     (1, 2, 256, 256, 64, 1, 1),   # configs[2] head shape: fused
     (1, 2, 40, 72, 16, 1, 0),     # Sq != Sk: fused for the true key gradient, composed for the reference one
+    (2, 3, 37, 37, 32, 1, 1),     # ragged row and key blocks, masked: fused
     (1, 2, 40, 72, 16, 0, 0),     # row-wise softmax: composed (tensor cores)
 ]
 

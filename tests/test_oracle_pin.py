@@ -188,7 +188,7 @@ def test_fused_attention_bitwise_vs_reference_chain(cuda, ref, ops, rng, mask):
     B, Hh, S, D = 2, 4, 128, 32
     bh, n_s = B * Hh, B * Hh * S * S
     Q, K, V, dO = (rng.standard_normal((bh, S, D)).astype(np.float32) for _ in range(4))
-    scale = float(1.0 / np.sqrt(D))
+    scale = float(np.float32(1.0 / np.sqrt(D)))  # GraphOperations::Scale holds a float
     tQ, tK, tV, tdO = (T(a, cuda) for a in (Q, K, V, dO))
     # reference forward
     scores, scaled, rP = (torch.zeros(n_s, device=cuda) for _ in range(3))
