@@ -409,6 +409,34 @@ int mle_adam_update(const mle_param_view* params, int n_tensors, const double* c
                     float pre_scale, float lr, int adamw, int write_back_grad,
                     mle_stream_t stream);
 
+/* No counterpart in the reference: a gradient-norm clip that needs no
+ * workspace from the caller.  It computes what mle_grad_sumsq (scale 1),
+ * mle_clip_finalize and mle_clip_apply compute together -- g /= c with
+ * c = max(||g||, max_norm) / max_norm over all tensors -- but keeps its
+ * scratch (one double per 4096-element block of gradients plus the
+ * coefficient) in a static device array of the library, so a caller that
+ * owns no device memory of its own (a host binding only this C ABI, or a
+ * training loop whose memory is planned once at graph build and must not
+ * call cudaMalloc, which can synchronise the device, in the middle of a
+ * step) can still clip.  The per-block sums are added in a fixed order,
+ * so the coefficient does not depend on block scheduling.
+ *   - Limit: the tensors may span at most MLE_CLIP_STATIC_MAX_BLOCKS blocks
+ *     of 4096 elements (each tensor rounded up to whole blocks, an empty
+ *     tensor counting as one), about 33.5 million gradient elements; larger
+ *     sets return MLE_ERR_ARG before anything is launched.
+ *   - If coef_out != NULL (device pointer) it receives c, the value
+ *     mle_clip_finalize leaves in norm_ws.
+ *   - Nothing in the scratch has to start at zero: every slot read is
+ *     written earlier in the same call.
+ *   - The scratch is one array per device: calls that overlap in time
+ *     (several streams or host threads on one device) race on it.
+ *   - The first call on each device resolves the scratch's address with
+ *     cudaGetSymbolAddress (with that device current); make that first
+ *     call before any stream capture on the device. */
+#define MLE_CLIP_STATIC_MAX_BLOCKS 8192
+int mle_clip_grad_norm_static(const mle_param_view* params, int n_tensors, double max_norm,
+                              double* coef_out, mle_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

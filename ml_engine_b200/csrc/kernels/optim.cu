@@ -17,6 +17,8 @@
 // and the clip divides by (float)norm as SP does.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mle {
@@ -197,10 +199,74 @@ int64_t build_table(TensorTable& tt, const mle_param_view* params, int first, in
     return blocks;
 }
 
+// ------------------------- clip without a caller workspace -------------------------
+// Scratch of mle_clip_grad_norm_static: slots [0, blocks) hold the per-block
+// sums of squares of one call, slot MLE_CLIP_STATIC_MAX_BLOCKS the clip
+// coefficient.
+static __device__ __align__(256) double g_clip_static[MLE_CLIP_STATIC_MAX_BLOCKS + 1];
+
+__global__ void __launch_bounds__(kThreads) sumsq_partial_kernel(const __grid_constant__ TensorTable tt,
+                                                                 double* __restrict__ partial) {
+    __shared__ double scratch[32];
+    const int ti = find_tensor(tt, blockIdx.x);
+    const mle_param_view& P = tt.p[ti];
+    const int64_t begin = (int64_t)(blockIdx.x - tt.block_start[ti]) * kChunk;
+    int64_t end = begin + kChunk;
+    if (end > P.n) end = P.n;
+    double acc = 0.0;
+    for (int64_t i = begin + threadIdx.x; i < end; i += kThreads) acc += (double)P.g[i] * (double)P.g[i];
+    acc = block_sum(acc, scratch);
+    if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+}
+
+// One block: thread i adds partials i, i + 256, ... in order, then a fixed
+// shuffle tree; the coefficient follows clip_finalize_kernel.
+__global__ void __launch_bounds__(kThreads) clip_finalize_static_kernel(double* __restrict__ scratch, int nblocks,
+                                                                        double max_norm, double* coef_out) {
+    __shared__ double red[32];
+    double acc = 0.0;
+    for (int i = threadIdx.x; i < nblocks; i += kThreads) acc += scratch[i];
+    acc = block_sum(acc, red);
+    if (threadIdx.x == 0) {
+        double c = acc;  // a NaN sum is left as it is
+        if (acc == acc) {
+            const double curr = sqrt(acc);
+            c = (curr > max_norm) ? curr / max_norm : 1.0;
+        }
+        scratch[MLE_CLIP_STATIC_MAX_BLOCKS] = c;
+        if (coef_out) *coef_out = c;
+    }
+}
+
 }  // namespace
 }  // namespace mle
 
 using namespace mle;
+
+namespace {
+// Device address of g_clip_static, resolved once per device.
+double* clip_static_scratch(int& status) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static double* addr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        status = MLE_ERR_CUDA;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_clip_static) != cudaSuccess || !p) {
+            status = MLE_ERR_CUDA;
+            return nullptr;
+        }
+        addr[dev] = static_cast<double*>(p);
+    }
+    status = MLE_OK;
+    return addr[dev];
+}
+}  // namespace
 
 extern "C" {
 
@@ -275,6 +341,47 @@ int mle_adam_update(const mle_param_view* params, int n_tensors, const double* c
         }
         step_increment_kernel<<<(count + 127) / 128, 128, 0, st>>>(tt);
         const int s = launch_status();
+        if (s) return s;
+    }
+    return MLE_OK;
+}
+
+int mle_clip_grad_norm_static(const mle_param_view* params, int n_tensors, double max_norm, double* coef_out,
+                              mle_stream_t stream) {
+    if (n_tensors < 0 || (n_tensors > 0 && !params) || !(max_norm > 0.0)) return MLE_ERR_ARG;
+    // size check first: the whole set must fit the static scratch
+    int64_t total_blocks = 0;
+    for (int i = 0; i < n_tensors; ++i) {
+        if (params[i].n < 0 || (params[i].n > 0 && !params[i].g)) return MLE_ERR_ARG;
+        total_blocks += params[i].n > 0 ? (params[i].n + kChunk - 1) / kChunk : 1;
+    }
+    if (total_blocks > MLE_CLIP_STATIC_MAX_BLOCKS) return MLE_ERR_ARG;
+    int status = MLE_OK;
+    double* scratch = clip_static_scratch(status);
+    if (!scratch) return status;
+    cudaStream_t st = as_stream(stream);
+    int64_t offset = 0;
+    for (int first = 0; first < n_tensors; first += kMaxTensors) {
+        const int count = (n_tensors - first < kMaxTensors) ? n_tensors - first : kMaxTensors;
+        TensorTable tt;
+        const int64_t blocks = build_table(tt, params, first, count);
+        if (blocks < 0) return MLE_ERR_ARG;
+        if (blocks == 0) continue;
+        sumsq_partial_kernel<<<(unsigned)blocks, kThreads, 0, st>>>(tt, scratch + offset);
+        const int s = launch_status();
+        if (s) return s;
+        offset += blocks;
+    }
+    clip_finalize_static_kernel<<<1, kThreads, 0, st>>>(scratch, (int)offset, max_norm, coef_out);
+    int s = launch_status();
+    if (s) return s;
+    for (int first = 0; first < n_tensors; first += kMaxTensors) {
+        const int count = (n_tensors - first < kMaxTensors) ? n_tensors - first : kMaxTensors;
+        TensorTable tt;
+        const int64_t blocks = build_table(tt, params, first, count);
+        if (blocks <= 0) continue;
+        clip_apply_kernel<<<(unsigned)blocks, kThreads, 0, st>>>(tt, scratch + MLE_CLIP_STATIC_MAX_BLOCKS);
+        s = launch_status();
         if (s) return s;
     }
     return MLE_OK;
