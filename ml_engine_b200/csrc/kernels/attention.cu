@@ -214,6 +214,7 @@ __device__ __forceinline__ void rows_times_rows(const float* Ms, int ldm, const 
 // grid (B*H, ceil(Sk / kTC)): P[:, c0:c0+kTC] of one head
 template <int HD>
 __global__ void __launch_bounds__(kNT) attn_probs_kernel(const AttnArgs a) {
+    pdl_entry();
     extern __shared__ float sm[];
     const int Sq = a.Sq, Sk = a.Sk, c0 = blockIdx.y * kTC, tc = min(kTC, Sk - c0);
     float* Qs = sm;                      // [Sq][HD+1]
@@ -276,6 +277,7 @@ __device__ __forceinline__ void load_row_tile(float* dst, const float* __restric
 // grid (B*H, ceil(Sq / kTR)): O[r0:r0+kTR] = P V
 template <int HD>
 __global__ void __launch_bounds__(kNT) attn_pv_kernel(const AttnArgs a) {
+    pdl_entry();
     extern __shared__ float sm[];
     const int Sq = a.Sq, Sk = a.Sk, r0 = blockIdx.y * kTR, tr = min(kTR, Sq - r0);
     const int ldp = Sk + 1;
@@ -300,6 +302,7 @@ __global__ void __launch_bounds__(kNT) attn_pv_kernel(const AttnArgs a) {
 // keys c0 .. c0+kTC
 template <int HD>
 __global__ void __launch_bounds__(kNT) attn_bwd_cols_kernel(const AttnArgs a) {
+    pdl_entry();
     extern __shared__ float sm[];
     const int Sq = a.Sq, Sk = a.Sk, c0 = blockIdx.y * kTC, tc = min(kTC, Sk - c0);
     const bool true_dk = a.key_mode == MLE_KEYGRAD_TRUE;
@@ -360,6 +363,7 @@ __global__ void __launch_bounds__(kNT) attn_bwd_cols_kernel(const AttnArgs a) {
 // dScores Q (bcmmT)
 template <int HD>
 __global__ void __launch_bounds__(kNT) attn_bwd_rows_kernel(const AttnArgs a) {
+    pdl_entry();
     extern __shared__ float sm[];
     const int Sq = a.Sq, Sk = a.Sk, r0 = blockIdx.y * kTR, tr = min(kTR, Sq - r0);
     const bool ref_dk = a.key_mode == MLE_KEYGRAD_REFERENCE;
@@ -434,10 +438,10 @@ int launch_fwd(const AttnArgs& a, cudaStream_t st) {
     int s = set_smem(attn_probs_kernel<HD>, c1);
     if (s == MLE_OK) s = set_smem(attn_pv_kernel<HD>, c2);
     if (s) return s;
-    attn_probs_kernel<HD><<<dim3(a.B * a.H, (a.Sk + kTC - 1) / kTC), kNT, s1, st>>>(a);
+    launch_k(attn_probs_kernel<HD>, dim3(a.B * a.H, (a.Sk + kTC - 1) / kTC), kNT, s1, st, a);
     s = launch_status();
     if (s) return s;
-    attn_pv_kernel<HD><<<dim3(a.B * a.H, (a.Sq + kTR - 1) / kTR), kNT, s2, st>>>(a);
+    launch_k(attn_pv_kernel<HD>, dim3(a.B * a.H, (a.Sq + kTR - 1) / kTR), kNT, s2, st, a);
     return launch_status();
 }
 
@@ -450,10 +454,10 @@ int launch_bwd(const AttnArgs& a, cudaStream_t st) {
     int s = set_smem(attn_bwd_cols_kernel<HD>, c1);
     if (s == MLE_OK) s = set_smem(attn_bwd_rows_kernel<HD>, c2);
     if (s) return s;
-    attn_bwd_cols_kernel<HD><<<dim3(a.B * a.H, (a.Sk + kTC - 1) / kTC), kNT, s1, st>>>(a);
+    launch_k(attn_bwd_cols_kernel<HD>, dim3(a.B * a.H, (a.Sk + kTC - 1) / kTC), kNT, s1, st, a);
     s = launch_status();
     if (s) return s;
-    attn_bwd_rows_kernel<HD><<<dim3(a.B * a.H, (a.Sq + kTR - 1) / kTR), kNT, s2, st>>>(a);
+    launch_k(attn_bwd_rows_kernel<HD>, dim3(a.B * a.H, (a.Sq + kTR - 1) / kTR), kNT, s2, st, a);
     return launch_status();
 }
 

@@ -4,6 +4,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <unordered_set>
+#include <utility>
+
 #include "mle_kernels.h"
 
 namespace mle {
@@ -29,6 +33,44 @@ constexpr int kSMs = 148;  // B200: 2 dies x 74 SMs
 
 // Grid size for a grid-stride elementwise kernel of `n` work items with
 // `per_block` items per block and pass, capped at a whole number of waves.
+// Every kernel of the library is launched through launch_k:
+//  * programmatic dependent launch -- the kernel may be scheduled while the
+//    previous kernel on the stream finishes; every kernel therefore starts
+//    with pdl_entry(), which waits for that kernel's writes before any
+//    global memory is touched and lets the next kernel be scheduled;
+//  * the maximum shared-memory carveout for every kernel, so the SMs keep
+//    one L1/shared split across a step instead of switching between the
+//    tensor-core GEMM (which needs it) and the streaming kernels.
+__device__ __forceinline__ void pdl_entry() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+inline void prefer_max_shared(const void* fn) {
+    static std::mutex mu;
+    static std::unordered_set<const void*> done;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.insert(fn).second)
+        cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+    prefer_max_shared(reinterpret_cast<const void*>(kern));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 inline unsigned grid_for(int64_t n, int per_block, int max_waves = 16) {
     int64_t blocks = (n + per_block - 1) / per_block;
     int64_t cap = (int64_t)kSMs * max_waves;

@@ -86,6 +86,7 @@ __device__ __forceinline__ float act_backward(int kind, float x, float gy, float
 // generic vectorised map kernels
 // ---------------------------------------------------------------------------
 __global__ void fill_kernel(float* __restrict__ x, float v, int64_t n) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t n4 = n >> 2;
@@ -95,6 +96,7 @@ __global__ void fill_kernel(float* __restrict__ x, float v, int64_t n) {
 }
 
 __global__ void fill_kernel_scalar(float* __restrict__ x, float v, int64_t n) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) x[i] = v;
 }
@@ -113,6 +115,7 @@ __device__ __forceinline__ float map1(float x, float y_old, float other, float f
 template <int OP, bool VEC>
 __global__ void map_kernel(const float* __restrict__ x, const float* __restrict__ other,
                            float* __restrict__ y, int64_t n, float fscale, double dscale) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int64_t tail = 0;
@@ -145,6 +148,7 @@ __global__ void map_kernel(const float* __restrict__ x, const float* __restrict_
 template <bool VEC>
 __global__ void add_bwd_kernel(const float* __restrict__ g, float* __restrict__ ga,
                                float* __restrict__ gb, int64_t n) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int64_t tail = 0;
@@ -173,6 +177,7 @@ __global__ void add_bwd_kernel(const float* __restrict__ g, float* __restrict__ 
 
 template <bool VEC>
 __global__ void act_fwd_kernel(int kind, const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int64_t tail = 0;
@@ -193,6 +198,7 @@ __global__ void act_fwd_kernel(int kind, const float* __restrict__ x, float* __r
 template <bool VEC>
 __global__ void act_bwd_kernel(int kind, const float* __restrict__ x, const float* __restrict__ gy,
                                float* __restrict__ gx, int64_t n) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int64_t tail = 0;
@@ -229,6 +235,7 @@ __global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __re
                                                      const float* __restrict__ gy, float* __restrict__ g,
                                                      float* __restrict__ out, int64_t rows, int64_t cols,
                                                      int64_t rows_per_block, float scale) {
+    pdl_entry();
     constexpr int W = VEC ? 4 : 1;  // columns per lane
     __shared__ float part[kColWarps][32 * W];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -303,6 +310,7 @@ inline ColsumShape colsum_shape(int64_t rows, int64_t cols, bool vec) {
 template <bool VEC>
 __global__ void bias_add_kernel(const float* __restrict__ x, const float* __restrict__ b, float* __restrict__ y,
                                 int64_t rows, int64_t cols) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (VEC) {
@@ -324,6 +332,7 @@ __global__ void bias_add_kernel(const float* __restrict__ x, const float* __rest
 // y[n,c,s] = x[n,c,s] + b[c]
 __global__ void channel_bias_fwd_kernel(const float* __restrict__ x, const float* __restrict__ b,
                                         float* __restrict__ y, int channels, int64_t spatial, int64_t total) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
         const int c = (int)((i / spatial) % channels);
@@ -335,6 +344,7 @@ __global__ void channel_bias_fwd_kernel(const float* __restrict__ x, const float
 __global__ void channel_bias_bwd_kernel(const float* __restrict__ g, float* __restrict__ gx,
                                         float* __restrict__ gb, int batch, int channels, int64_t spatial,
                                         int batch_per_block) {
+    pdl_entry();
     __shared__ float scratch[32];
     const int c = blockIdx.x;
     const int n0 = blockIdx.y * batch_per_block;
@@ -356,6 +366,7 @@ __global__ void channel_bias_bwd_kernel(const float* __restrict__ g, float* __re
 // MatPEncoding (Engine/kernels.cu:166-185): double-precision angle.
 __global__ void matpe_kernel(const float* __restrict__ x, float* __restrict__ y, int rows, int cols,
                              int64_t total, int start_idx) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
         const int pos = (int)((i % ((int64_t)rows * cols)) / cols) + start_idx;
@@ -370,6 +381,7 @@ __global__ void matpe_kernel(const float* __restrict__ x, float* __restrict__ y,
 
 // The positional term of MatPEncoding alone (x = 0): table[r, c].
 __global__ void matpe_table_kernel(float* __restrict__ t, int rows, int cols, int start_idx) {
+    pdl_entry();
     const int64_t total = (int64_t)rows * cols;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -384,6 +396,7 @@ __global__ void matpe_table_kernel(float* __restrict__ t, int rows, int cols, in
 // y[b, i] = x[b, i] + table[i]
 __global__ void rows_add_table_kernel(const float4* __restrict__ x, const float4* __restrict__ table,
                                       float4* __restrict__ y, int64_t total4, int64_t row4) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += stride) {
         float4 a = x[i];
@@ -395,6 +408,7 @@ __global__ void rows_add_table_kernel(const float4* __restrict__ x, const float4
 
 __global__ void rows_add_table_scalar(const float* __restrict__ x, const float* __restrict__ table,
                                       float* __restrict__ y, int64_t total, int64_t row) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride)
         y[i] = x[i] + table[i % row];
@@ -402,6 +416,7 @@ __global__ void rows_add_table_scalar(const float* __restrict__ x, const float* 
 
 // PEncoding (Engine/kernels.cu:147-164)
 __global__ void timestep_pe_kernel(float* __restrict__ y, int t, int dim) {
+    pdl_entry();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= dim) return;
     const int half = dim / 2;
@@ -416,6 +431,7 @@ __global__ void timestep_pe_kernel(float* __restrict__ y, int t, int dim) {
 // element once, so plain read-modify-write replaces the atomics.
 __global__ void headify_kernel(const float* __restrict__ in, float* __restrict__ out, int heads, int seq,
                                int head_dim, int64_t total, int flag) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int embed = heads * head_dim;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
@@ -437,6 +453,7 @@ __global__ void headify_kernel(const float* __restrict__ in, float* __restrict__
 // checks that the element count fits).
 __global__ void headify4_kernel(const float4* __restrict__ in, float4* __restrict__ out, int heads, int seq, int hd4,
                                 int total4, int flag) {
+    pdl_entry();
     const int stride = gridDim.x * blockDim.x;
     const int row4 = heads * hd4;  // 4-vectors per token row
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += stride) {
@@ -467,6 +484,7 @@ __global__ void headify4_kernel(const float4* __restrict__ in, float4* __restric
 
 __global__ void channel_concat_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                       float* __restrict__ c, int c1, int c2, int64_t spatial, int64_t total) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int cc = c1 + c2;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -479,6 +497,7 @@ __global__ void channel_concat_kernel(const float* __restrict__ a, const float* 
 
 __global__ void channel_split_kernel(float* __restrict__ ga, float* __restrict__ gb, const float* __restrict__ gc,
                                      int c1, int c2, int64_t spatial, int64_t total) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int cc = c1 + c2;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -493,6 +512,7 @@ __global__ void channel_split_kernel(float* __restrict__ ga, float* __restrict__
 // CopynCrop: (a,b) -> (c,d) centre crop
 __global__ void center_crop_kernel(const float* __restrict__ x, float* __restrict__ y, int depth, int a, int b,
                                    int c, int d, int64_t total) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int dr = (a - c) / 2, dc = (b - d) / 2;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -507,6 +527,7 @@ __global__ void center_crop_kernel(const float* __restrict__ x, float* __restric
 // PaddingCrop: (c,d) -> (a,b), accumulate
 __global__ void pad_crop_kernel(const float* __restrict__ x, float* __restrict__ y, int depth, int a, int b,
                                 int c, int d, int64_t total) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int dr = (a - c) / 2, dc = (b - d) / 2;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -521,6 +542,7 @@ __global__ void pad_crop_kernel(const float* __restrict__ x, float* __restrict__
 
 __global__ void gather_kernel(const int32_t* __restrict__ keys, const float* __restrict__ table,
                               float* __restrict__ out, int64_t total, int dim) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
         const int64_t row = i / dim;
@@ -530,6 +552,7 @@ __global__ void gather_kernel(const int32_t* __restrict__ keys, const float* __r
 }
 
 __global__ void one_hot_kernel(const int32_t* __restrict__ keys, float* __restrict__ out, int64_t n, int vocab) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
         const int k = keys[i];
@@ -567,18 +590,18 @@ int mle_abi_version(void) { return 1; }
 int mle_fill(float* x, float value, int64_t n, mle_stream_t stream) {
     if (n < 0 || (n > 0 && !x)) return MLE_ERR_ARG;
     if (n == 0) return MLE_OK;
-    if (aligned16(x)) fill_kernel<<<grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>(x, value, n);
-    else fill_kernel_scalar<<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(x, value, n);
+    if (aligned16(x)) launch_k(fill_kernel, grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream), x, value, n);
+    else launch_k(fill_kernel_scalar, grid_for(n, kThreads), kThreads, 0, as_stream(stream), x, value, n);
     return launch_status();
 }
 
 #define MLE_MAP_LAUNCH(OP, X, O, Y, N, FS, DS)                                                        \
     do {                                                                                          \
         if (vec_ok(N, X, O, Y))                                                                   \
-            map_kernel<OP, true><<<grid_for((N) / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>( \
+            launch_k(map_kernel<OP, true>, grid_for((N) / 4 + 1, kThreads), kThreads, 0, as_stream(stream),  \
                 X, O, Y, N, FS, DS);                                                              \
         else                                                                                      \
-            map_kernel<OP, false><<<grid_for(N, kThreads), kThreads, 0, as_stream(stream)>>>(X, O, Y, N, \
+            launch_k(map_kernel<OP, false>, grid_for(N, kThreads), kThreads, 0, as_stream(stream), X, O, Y, N, \
                                                                                         FS, DS);  \
     } while (0)
 
@@ -614,9 +637,9 @@ int mle_add_bwd(const float* g, float* ga, float* gb, int64_t n, mle_stream_t st
     if (n < 0 || (n > 0 && (!g || !ga || !gb))) return MLE_ERR_ARG;
     if (n == 0) return MLE_OK;
     if (vec_ok(n, g, ga, gb))
-        add_bwd_kernel<true><<<grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>(g, ga, gb, n);
+        launch_k(add_bwd_kernel<true>, grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream), g, ga, gb, n);
     else
-        add_bwd_kernel<false><<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(g, ga, gb, n);
+        launch_k(add_bwd_kernel<false>, grid_for(n, kThreads), kThreads, 0, as_stream(stream), g, ga, gb, n);
     return launch_status();
 }
 
@@ -624,9 +647,9 @@ int mle_act_fwd(int kind, const float* x, float* y, int64_t n, mle_stream_t stre
     if (kind < 0 || kind > MLE_ACT_SIGMOID || n < 0 || (n > 0 && (!x || !y))) return MLE_ERR_ARG;
     if (n == 0) return MLE_OK;
     if (vec_ok(n, x, y))
-        act_fwd_kernel<true><<<grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>(kind, x, y, n);
+        launch_k(act_fwd_kernel<true>, grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream), kind, x, y, n);
     else
-        act_fwd_kernel<false><<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(kind, x, y, n);
+        launch_k(act_fwd_kernel<false>, grid_for(n, kThreads), kThreads, 0, as_stream(stream), kind, x, y, n);
     return launch_status();
 }
 
@@ -636,19 +659,19 @@ int mle_act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n,
     if (n == 0) return MLE_OK;
     if (!bias_grad) {
         if (vec_ok(n, x, gy, gx))
-            act_bwd_kernel<true><<<grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream)>>>(kind, x, gy, gx, n);
+            launch_k(act_bwd_kernel<true>, grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream), kind, x, gy, gx, n);
         else
-            act_bwd_kernel<false><<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(kind, x, gy, gx, n);
+            launch_k(act_bwd_kernel<false>, grid_for(n, kThreads), kThreads, 0, as_stream(stream), kind, x, gy, gx, n);
         return launch_status();
     }
     if (rows <= 0 || cols <= 0 || rows * cols != n) return MLE_ERR_ARG;
     const bool vec = (cols % 4 == 0) && vec_ok(n, x, gy, gx);
     const ColsumShape sh = colsum_shape(rows, cols, vec);
     if (vec)
-        colsum_kernel<true, true><<<sh.grid, 256, 0, as_stream(stream)>>>(kind, x, gy, gx, bias_grad, rows, cols,
+        launch_k(colsum_kernel<true, true>, sh.grid, 256, 0, as_stream(stream), kind, x, gy, gx, bias_grad, rows, cols,
                                                                           sh.rpb, 1.0f);
     else
-        colsum_kernel<true, false><<<sh.grid, 256, 0, as_stream(stream)>>>(kind, x, gy, gx, bias_grad, rows, cols,
+        launch_k(colsum_kernel<true, false>, sh.grid, 256, 0, as_stream(stream), kind, x, gy, gx, bias_grad, rows, cols,
                                                                            sh.rpb, 1.0f);
     return launch_status();
 }
@@ -658,9 +681,9 @@ int mle_bias_add_fwd(const float* x, const float* bias, float* y, int64_t rows, 
     if (rows == 0) return MLE_OK;
     const int64_t n = rows * cols;
     if (cols % 4 == 0 && vec_ok(n, x, bias, y))
-        bias_add_kernel<true><<<grid_for(n / 4, kThreads), kThreads, 0, as_stream(stream)>>>(x, bias, y, rows, cols);
+        launch_k(bias_add_kernel<true>, grid_for(n / 4, kThreads), kThreads, 0, as_stream(stream), x, bias, y, rows, cols);
     else
-        bias_add_kernel<false><<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(x, bias, y, rows, cols);
+        launch_k(bias_add_kernel<false>, grid_for(n, kThreads), kThreads, 0, as_stream(stream), x, bias, y, rows, cols);
     return launch_status();
 }
 
@@ -671,10 +694,10 @@ int mle_bias_grad(const float* g, float* bias_grad, int64_t rows, int64_t cols, 
     const ColsumShape sh = colsum_shape(rows, cols, vec);
     float* gm = const_cast<float*>(g);  // read-only when ACT == false
     if (vec)
-        colsum_kernel<false, true><<<sh.grid, 256, 0, as_stream(stream)>>>(0, nullptr, nullptr, gm, bias_grad, rows,
+        launch_k(colsum_kernel<false, true>, sh.grid, 256, 0, as_stream(stream), 0, nullptr, nullptr, gm, bias_grad, rows,
                                                                            cols, sh.rpb, scale);
     else
-        colsum_kernel<false, false><<<sh.grid, 256, 0, as_stream(stream)>>>(0, nullptr, nullptr, gm, bias_grad, rows,
+        launch_k(colsum_kernel<false, false>, sh.grid, 256, 0, as_stream(stream), 0, nullptr, nullptr, gm, bias_grad, rows,
                                                                             cols, sh.rpb, scale);
     return launch_status();
 }
@@ -684,7 +707,7 @@ int mle_channel_bias_fwd(const float* x, const float* b, float* y, int batch, in
     if (batch < 0 || channels <= 0 || spatial <= 0 || !x || !b || !y) return MLE_ERR_ARG;
     const int64_t total = (int64_t)batch * channels * spatial;
     if (total == 0) return MLE_OK;
-    channel_bias_fwd_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, b, y, channels, spatial,
+    launch_k(channel_bias_fwd_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), x, b, y, channels, spatial,
                                                                                            total);
     return launch_status();
 }
@@ -698,7 +721,7 @@ int mle_channel_bias_bwd(const float* g, float* gx, float* gb, int batch, int ch
     const int bpb = (batch + chunks - 1) / chunks;
     chunks = (batch + bpb - 1) / bpb;
     dim3 grid((unsigned)channels, (unsigned)chunks);
-    channel_bias_bwd_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(g, gx, gb, batch, channels, spatial, bpb);
+    launch_k(channel_bias_bwd_kernel, grid, kThreads, 0, as_stream(stream), g, gx, gb, batch, channels, spatial, bpb);
     return launch_status();
 }
 
@@ -706,13 +729,13 @@ int mle_matpe_fwd(const float* x, float* y, int batch, int rows, int cols, int s
     if (batch < 0 || rows <= 0 || cols <= 0 || !x || !y) return MLE_ERR_ARG;
     const int64_t total = (int64_t)batch * rows * cols;
     if (total == 0) return MLE_OK;
-    matpe_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, y, rows, cols, total, start_idx);
+    launch_k(matpe_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), x, y, rows, cols, total, start_idx);
     return launch_status();
 }
 
 int mle_matpe_table(float* table, int rows, int cols, int start_idx, mle_stream_t stream) {
     if (rows <= 0 || cols <= 0 || !table) return MLE_ERR_ARG;
-    matpe_table_kernel<<<grid_for((int64_t)rows * cols, kThreads), kThreads, 0, as_stream(stream)>>>(table, rows, cols,
+    launch_k(matpe_table_kernel, grid_for((int64_t)rows * cols, kThreads), kThreads, 0, as_stream(stream), table, rows, cols,
                                                                                                      start_idx);
     return launch_status();
 }
@@ -723,18 +746,18 @@ int mle_rows_add_table(const float* x, const float* table, float* y, int64_t bat
     const int64_t total = batch * row_elems;
     if (total == 0) return MLE_OK;
     if (row_elems % 4 == 0 && aligned16(x) && aligned16(table) && aligned16(y))
-        rows_add_table_kernel<<<grid_for(total / 4, kThreads), kThreads, 0, as_stream(stream)>>>(
+        launch_k(rows_add_table_kernel, grid_for(total / 4, kThreads), kThreads, 0, as_stream(stream), 
             reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(table), reinterpret_cast<float4*>(y),
             total / 4, row_elems / 4);
     else
-        rows_add_table_scalar<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, table, y, total,
+        launch_k(rows_add_table_scalar, grid_for(total, kThreads), kThreads, 0, as_stream(stream), x, table, y, total,
                                                                                              row_elems);
     return launch_status();
 }
 
 int mle_timestep_pe(float* y, int t, int dim, mle_stream_t stream) {
     if (dim <= 2 || !y) return MLE_ERR_ARG;
-    timestep_pe_kernel<<<(dim + kThreads - 1) / kThreads, kThreads, 0, as_stream(stream)>>>(y, t, dim);
+    launch_k(timestep_pe_kernel, (dim + kThreads - 1) / kThreads, kThreads, 0, as_stream(stream), y, t, dim);
     return launch_status();
 }
 
@@ -746,11 +769,11 @@ int mle_headify(const float* in, float* out, int batch, int heads, int seq, int 
     if (total == 0) return MLE_OK;
     if (head_dim % 4 == 0 && aligned16(in) && aligned16(out) && total / 4 < (1ll << 31)) {
         const int total4 = (int)(total / 4);
-        headify4_kernel<<<grid_for(total4, kThreads), kThreads, 0, as_stream(stream)>>>(
+        launch_k(headify4_kernel, grid_for(total4, kThreads), kThreads, 0, as_stream(stream), 
             reinterpret_cast<const float4*>(in), reinterpret_cast<float4*>(out), heads, seq, head_dim / 4, total4,
             flag);
     } else {
-        headify_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(in, out, heads, seq, head_dim,
+        launch_k(headify_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), in, out, heads, seq, head_dim,
                                                                                       total, flag);
     }
     return launch_status();
@@ -761,7 +784,7 @@ int mle_channel_concat(const float* a, const float* b, float* c, int batch, int 
     if (batch < 0 || c1 < 0 || c2 < 0 || spatial <= 0 || !a || !b || !c) return MLE_ERR_ARG;
     const int64_t total = (int64_t)batch * (c1 + c2) * spatial;
     if (total == 0) return MLE_OK;
-    channel_concat_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(a, b, c, c1, c2, spatial,
+    launch_k(channel_concat_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), a, b, c, c1, c2, spatial,
                                                                                          total);
     return launch_status();
 }
@@ -771,7 +794,7 @@ int mle_channel_split(float* ga, float* gb, const float* gc, int batch, int c1, 
     if (batch < 0 || c1 < 0 || c2 < 0 || spatial <= 0 || !ga || !gb || !gc) return MLE_ERR_ARG;
     const int64_t total = (int64_t)batch * (c1 + c2) * spatial;
     if (total == 0) return MLE_OK;
-    channel_split_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(ga, gb, gc, c1, c2, spatial,
+    launch_k(channel_split_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), ga, gb, gc, c1, c2, spatial,
                                                                                         total);
     return launch_status();
 }
@@ -781,7 +804,7 @@ int mle_center_crop(const float* x, float* y, int batch, int depth, int a, int b
     if (batch < 0 || depth <= 0 || c <= 0 || d <= 0 || c > a || d > b || !x || !y) return MLE_ERR_ARG;
     const int64_t total = (int64_t)batch * depth * c * d;
     if (total == 0) return MLE_OK;
-    center_crop_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, y, depth, a, b, c, d, total);
+    launch_k(center_crop_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), x, y, depth, a, b, c, d, total);
     return launch_status();
 }
 
@@ -789,7 +812,7 @@ int mle_pad_crop(const float* x, float* y, int batch, int depth, int a, int b, i
     if (batch < 0 || depth <= 0 || a <= 0 || b <= 0 || !x || !y) return MLE_ERR_ARG;
     const int64_t total = (int64_t)batch * depth * a * b;
     if (total == 0) return MLE_OK;
-    pad_crop_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(x, y, depth, a, b, c, d, total);
+    launch_k(pad_crop_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), x, y, depth, a, b, c, d, total);
     return launch_status();
 }
 
@@ -798,14 +821,14 @@ int mle_embedding_gather(const int32_t* keys, const float* table, float* out, in
     if (n_keys < 0 || dim <= 0 || !keys || !table || !out) return MLE_ERR_ARG;
     const int64_t total = n_keys * dim;
     if (total == 0) return MLE_OK;
-    gather_kernel<<<grid_for(total, kThreads), kThreads, 0, as_stream(stream)>>>(keys, table, out, total, dim);
+    launch_k(gather_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), keys, table, out, total, dim);
     return launch_status();
 }
 
 int mle_one_hot(const int32_t* keys, float* out, int64_t n_keys, int vocab, mle_stream_t stream) {
     if (n_keys < 0 || vocab <= 0 || !keys || !out) return MLE_ERR_ARG;
     if (n_keys == 0) return MLE_OK;
-    one_hot_kernel<<<grid_for(n_keys, kThreads), kThreads, 0, as_stream(stream)>>>(keys, out, n_keys, vocab);
+    launch_k(one_hot_kernel, grid_for(n_keys, kThreads), kThreads, 0, as_stream(stream), keys, out, n_keys, vocab);
     return launch_status();
 }
 

@@ -13,6 +13,7 @@ namespace {
 constexpr int TM = 64, TN = 64, TK = 16;
 
 __global__ void __launch_bounds__(256) simt_gemm_kernel(const GemmProblem p) {
+    pdl_entry();
     __shared__ float As[TK][TM + 4];
     __shared__ float Bs[TK][TN + 4];
     const int z = blockIdx.z;
@@ -86,7 +87,7 @@ int simt_gemm(const GemmProblem& p, cudaStream_t st) {
     if (z > 65535) return MLE_ERR_UNSUPPORTED;
     dim3 grid((p.N + TN - 1) / TN, (p.M + TM - 1) / TM, (unsigned)z);
     if (grid.y > 65535) return MLE_ERR_UNSUPPORTED;
-    simt_gemm_kernel<<<grid, 256, 0, st>>>(p);
+    launch_k(simt_gemm_kernel, grid, 256, 0, st, p);
     return launch_status();
 }
 

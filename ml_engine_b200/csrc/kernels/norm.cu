@@ -22,6 +22,7 @@ constexpr int kBlock = 256;
 template <int V>  // V float4 per lane -> N <= 128 * V
 __global__ void seg_norm_fwd_warp(const float* __restrict__ x, float* __restrict__ y, float* __restrict__ mean,
                                   float* __restrict__ sqdev, int64_t segs, int N, float eps) {
+    pdl_entry();
     const int lane = threadIdx.x & 31;
     const int64_t seg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (seg >= segs) return;
@@ -74,6 +75,7 @@ template <int V>
 __global__ void seg_norm_bwd_warp(const float* __restrict__ y, const float* __restrict__ gy,
                                   const float* __restrict__ sqdev, float* __restrict__ gx, int64_t segs, int N,
                                   float eps) {
+    pdl_entry();
     const int lane = threadIdx.x & 31;
     const int64_t seg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (seg >= segs) return;
@@ -115,6 +117,7 @@ __global__ void seg_norm_bwd_warp(const float* __restrict__ y, const float* __re
 // ----------------------------- block per segment --------------------------
 __global__ void seg_norm_fwd_block(const float* __restrict__ x, float* __restrict__ y, float* __restrict__ mean,
                                    float* __restrict__ sqdev, int N, float eps) {
+    pdl_entry();
     __shared__ float scratch[32];
     const int64_t seg = blockIdx.x;
     const float* xs = x + seg * N;
@@ -139,6 +142,7 @@ __global__ void seg_norm_fwd_block(const float* __restrict__ x, float* __restric
 
 __global__ void seg_norm_bwd_block(const float* __restrict__ y, const float* __restrict__ gy,
                                    const float* __restrict__ sqdev, float* __restrict__ gx, int N, float eps) {
+    pdl_entry();
     __shared__ float scratch[32];
     const int64_t seg = blockIdx.x;
     const float* ys = y + seg * N;
@@ -167,6 +171,7 @@ __global__ void seg_norm_bwd_block(const float* __restrict__ y, const float* __r
 __global__ void ln_bwd_channels_block(const float* __restrict__ y, const float* __restrict__ gy,
                                       const float* __restrict__ sqdev, float* __restrict__ gx, int64_t N, int64_t rc,
                                       float eps) {
+    pdl_entry();
     __shared__ float scratch[32];
     const int64_t b = blockIdx.x;
     float sg = 0.f, sgy = 0.f;
@@ -191,13 +196,13 @@ static int seg_norm_fwd(const float* x, float* y, float* mean, float* sqdev, int
     if (N % 4 == 0 && N <= 2048 && aligned16(x) && aligned16(y)) {
         const int wpb = 8;  // warps per block
         const unsigned grid = (unsigned)((segs + wpb - 1) / wpb);
-        if (N <= 128) seg_norm_fwd_warp<1><<<grid, 32 * wpb, 0, st>>>(x, y, mean, sqdev, segs, N, eps);
-        else if (N <= 256) seg_norm_fwd_warp<2><<<grid, 32 * wpb, 0, st>>>(x, y, mean, sqdev, segs, N, eps);
-        else if (N <= 512) seg_norm_fwd_warp<4><<<grid, 32 * wpb, 0, st>>>(x, y, mean, sqdev, segs, N, eps);
-        else if (N <= 1024) seg_norm_fwd_warp<8><<<grid, 32 * wpb, 0, st>>>(x, y, mean, sqdev, segs, N, eps);
-        else seg_norm_fwd_warp<16><<<grid, 32 * wpb, 0, st>>>(x, y, mean, sqdev, segs, N, eps);
+        if (N <= 128) launch_k(seg_norm_fwd_warp<1>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
+        else if (N <= 256) launch_k(seg_norm_fwd_warp<2>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
+        else if (N <= 512) launch_k(seg_norm_fwd_warp<4>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
+        else if (N <= 1024) launch_k(seg_norm_fwd_warp<8>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
+        else launch_k(seg_norm_fwd_warp<16>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
     } else {
-        seg_norm_fwd_block<<<(unsigned)segs, kBlock, 0, st>>>(x, y, mean, sqdev, N, eps);
+        launch_k(seg_norm_fwd_block, (unsigned)segs, kBlock, 0, st, x, y, mean, sqdev, N, eps);
     }
     return launch_status();
 }
@@ -208,13 +213,13 @@ static int seg_norm_bwd(const float* y, const float* gy, const float* sqdev, flo
     if (N % 4 == 0 && N <= 2048 && aligned16(y) && aligned16(gy) && aligned16(gx)) {
         const int wpb = 8;
         const unsigned grid = (unsigned)((segs + wpb - 1) / wpb);
-        if (N <= 128) seg_norm_bwd_warp<1><<<grid, 32 * wpb, 0, st>>>(y, gy, sqdev, gx, segs, N, eps);
-        else if (N <= 256) seg_norm_bwd_warp<2><<<grid, 32 * wpb, 0, st>>>(y, gy, sqdev, gx, segs, N, eps);
-        else if (N <= 512) seg_norm_bwd_warp<4><<<grid, 32 * wpb, 0, st>>>(y, gy, sqdev, gx, segs, N, eps);
-        else if (N <= 1024) seg_norm_bwd_warp<8><<<grid, 32 * wpb, 0, st>>>(y, gy, sqdev, gx, segs, N, eps);
-        else seg_norm_bwd_warp<16><<<grid, 32 * wpb, 0, st>>>(y, gy, sqdev, gx, segs, N, eps);
+        if (N <= 128) launch_k(seg_norm_bwd_warp<1>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
+        else if (N <= 256) launch_k(seg_norm_bwd_warp<2>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
+        else if (N <= 512) launch_k(seg_norm_bwd_warp<4>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
+        else if (N <= 1024) launch_k(seg_norm_bwd_warp<8>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
+        else launch_k(seg_norm_bwd_warp<16>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
     } else {
-        seg_norm_bwd_block<<<(unsigned)segs, kBlock, 0, st>>>(y, gy, sqdev, gx, N, eps);
+        launch_k(seg_norm_bwd_block, (unsigned)segs, kBlock, 0, st, y, gy, sqdev, gx, N, eps);
     }
     return launch_status();
 }
@@ -240,7 +245,7 @@ int mle_layernorm_bwd(const float* y, const float* gy, const float* sqdev, float
     if (N > (1ll << 30)) return MLE_ERR_UNSUPPORTED;
     if (channels == 1) return seg_norm_bwd(y, gy, sqdev, gx, batch, (int)N, eps, as_stream(stream));
     if (batch == 0) return MLE_OK;
-    ln_bwd_channels_block<<<(unsigned)batch, kBlock, 0, as_stream(stream)>>>(y, gy, sqdev, gx, N,
+    launch_k(ln_bwd_channels_block, (unsigned)batch, kBlock, 0, as_stream(stream), y, gy, sqdev, gx, N,
                                                                              (int64_t)row * col, eps);
     return launch_status();
 }

@@ -48,6 +48,7 @@ __device__ __forceinline__ int find_tensor(const TensorTable& tt, int64_t block)
 // ------------------------------- sum of squares -----------------------------
 __global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__ TensorTable tt,
                                                          double* __restrict__ ws, double scale2) {
+    pdl_entry();
     __shared__ double scratch[32];
     const int ti = find_tensor(tt, blockIdx.x);
     const mle_param_view& P = tt.p[ti];
@@ -78,6 +79,7 @@ __global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__
 // ws = (sqrt(ws) > max_norm) ? sqrt(ws)/max_norm : 1; with max_norm == 1 this
 // is the reference's (curr > 1.0) ? curr * 1.0 : 1.0.  A NaN stays NaN.
 __global__ void clip_finalize_kernel(double* ws, double max_norm) {
+    pdl_entry();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     const double x = ws[0];
     if (x != x) return;
@@ -88,6 +90,7 @@ __global__ void clip_finalize_kernel(double* ws, double max_norm) {
 // ---------------------------------- clip -----------------------------------
 __global__ void __launch_bounds__(kThreads) clip_apply_kernel(const __grid_constant__ TensorTable tt,
                                                               const double* __restrict__ ws) {
+    pdl_entry();
     const int ti = find_tensor(tt, blockIdx.x);
     const mle_param_view& P = tt.p[ti];
     const int64_t begin = (int64_t)(blockIdx.x - tt.block_start[ti]) * kChunk;
@@ -114,6 +117,7 @@ template <bool ADAMW, bool CLIP, bool PRESCALE>
 __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ TensorTable tt,
                                                         const double* __restrict__ clip_ws, float pre_scale,
                                                         float lr, int write_back) {
+    pdl_entry();
     const int ti = find_tensor(tt, blockIdx.x);
     const mle_param_view& P = tt.p[ti];
     const int64_t chunk = blockIdx.x - tt.block_start[ti];
@@ -178,6 +182,7 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
 // t += 1 for every tensor of the table (run after the update; stream order
 // makes every block of the update see the old value).
 __global__ void step_increment_kernel(const __grid_constant__ TensorTable tt) {
+    pdl_entry();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < tt.n) *tt.p[i].t += 1;
 }
@@ -207,6 +212,7 @@ static __device__ __align__(256) double g_clip_static[MLE_CLIP_STATIC_MAX_BLOCKS
 
 __global__ void __launch_bounds__(kThreads) sumsq_partial_kernel(const __grid_constant__ TensorTable tt,
                                                                  double* __restrict__ partial) {
+    pdl_entry();
     __shared__ double scratch[32];
     const int ti = find_tensor(tt, blockIdx.x);
     const mle_param_view& P = tt.p[ti];
@@ -223,6 +229,7 @@ __global__ void __launch_bounds__(kThreads) sumsq_partial_kernel(const __grid_co
 // shuffle tree; the coefficient follows clip_finalize_kernel.
 __global__ void __launch_bounds__(kThreads) clip_finalize_static_kernel(double* __restrict__ scratch, int nblocks,
                                                                         double max_norm, double* coef_out) {
+    pdl_entry();
     __shared__ double red[32];
     double acc = 0.0;
     for (int i = threadIdx.x; i < nblocks; i += kThreads) acc += scratch[i];
@@ -280,7 +287,7 @@ int mle_grad_sumsq(const mle_param_view* params, int n_tensors, double* norm_ws,
         if (blocks < 0) return MLE_ERR_ARG;
         if (blocks == 0) continue;
         if (blocks > 0x7fffffffLL) return MLE_ERR_UNSUPPORTED;
-        sumsq_kernel<<<(unsigned)blocks, kThreads, 0, st>>>(tt, norm_ws, scale * scale);
+        launch_k(sumsq_kernel, (unsigned)blocks, kThreads, 0, st, tt, norm_ws, scale * scale);
         const int s = launch_status();
         if (s) return s;
     }
@@ -289,7 +296,7 @@ int mle_grad_sumsq(const mle_param_view* params, int n_tensors, double* norm_ws,
 
 int mle_clip_finalize(double* norm_ws, double max_norm, mle_stream_t stream) {
     if (!norm_ws || !(max_norm > 0.0)) return MLE_ERR_ARG;
-    clip_finalize_kernel<<<1, 32, 0, as_stream(stream)>>>(norm_ws, max_norm);
+    launch_k(clip_finalize_kernel, 1, 32, 0, as_stream(stream), norm_ws, max_norm);
     return launch_status();
 }
 
@@ -302,7 +309,7 @@ int mle_clip_apply(const mle_param_view* params, int n_tensors, const double* no
         const int64_t blocks = build_table(tt, params, first, count);
         if (blocks < 0) return MLE_ERR_ARG;
         if (blocks == 0) continue;
-        clip_apply_kernel<<<(unsigned)blocks, kThreads, 0, st>>>(tt, norm_ws);
+        launch_k(clip_apply_kernel, (unsigned)blocks, kThreads, 0, st, tt, norm_ws);
         const int s = launch_status();
         if (s) return s;
     }
@@ -327,7 +334,7 @@ int mle_adam_update(const mle_param_view* params, int n_tensors, const double* c
         if (blocks < 0) return MLE_ERR_ARG;
         if (blocks > 0) {
 #define MLE_ADAM_LAUNCH(AW, CL, PS) \
-    adam_kernel<AW, CL, PS><<<(unsigned)blocks, kThreads, 0, st>>>(tt, clip_ws, pre_scale, lr, write_back_grad)
+    launch_k(adam_kernel<AW, CL, PS>, (unsigned)blocks, kThreads, 0, st, tt, clip_ws, pre_scale, lr, write_back_grad)
             if (adamw) {
                 if (clip) { if (pres) MLE_ADAM_LAUNCH(true, true, true); else MLE_ADAM_LAUNCH(true, true, false); }
                 else { if (pres) MLE_ADAM_LAUNCH(true, false, true); else MLE_ADAM_LAUNCH(true, false, false); }
@@ -339,7 +346,7 @@ int mle_adam_update(const mle_param_view* params, int n_tensors, const double* c
             int s = launch_status();
             if (s) return s;
         }
-        step_increment_kernel<<<(count + 127) / 128, 128, 0, st>>>(tt);
+        launch_k(step_increment_kernel, (count + 127) / 128, 128, 0, st, tt);
         const int s = launch_status();
         if (s) return s;
     }
@@ -367,12 +374,12 @@ int mle_clip_grad_norm_static(const mle_param_view* params, int n_tensors, doubl
         const int64_t blocks = build_table(tt, params, first, count);
         if (blocks < 0) return MLE_ERR_ARG;
         if (blocks == 0) continue;
-        sumsq_partial_kernel<<<(unsigned)blocks, kThreads, 0, st>>>(tt, scratch + offset);
+        launch_k(sumsq_partial_kernel, (unsigned)blocks, kThreads, 0, st, tt, scratch + offset);
         const int s = launch_status();
         if (s) return s;
         offset += blocks;
     }
-    clip_finalize_static_kernel<<<1, kThreads, 0, st>>>(scratch, (int)offset, max_norm, coef_out);
+    launch_k(clip_finalize_static_kernel, 1, kThreads, 0, st, scratch, (int)offset, max_norm, coef_out);
     int s = launch_status();
     if (s) return s;
     for (int first = 0; first < n_tensors; first += kMaxTensors) {
@@ -380,7 +387,7 @@ int mle_clip_grad_norm_static(const mle_param_view* params, int n_tensors, doubl
         TensorTable tt;
         const int64_t blocks = build_table(tt, params, first, count);
         if (blocks <= 0) continue;
-        clip_apply_kernel<<<(unsigned)blocks, kThreads, 0, st>>>(tt, scratch + MLE_CLIP_STATIC_MAX_BLOCKS);
+        launch_k(clip_apply_kernel, (unsigned)blocks, kThreads, 0, st, tt, scratch + MLE_CLIP_STATIC_MAX_BLOCKS);
         s = launch_status();
         if (s) return s;
     }

@@ -20,6 +20,7 @@ constexpr int kRowThreads = 256;
 
 // ------------------------------ column-wise --------------------------------
 __global__ void softmax_col_fwd(const float* __restrict__ x, float* __restrict__ y, int rows, int cols, int causal) {
+    pdl_entry();
     const int64_t mat = blockIdx.y;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= cols) return;
@@ -39,6 +40,7 @@ __global__ void softmax_col_fwd(const float* __restrict__ x, float* __restrict__
 
 __global__ void softmax_col_bwd(const float* __restrict__ y, const float* __restrict__ gy, float* __restrict__ gx,
                                 int rows, int cols) {
+    pdl_entry();
     const int64_t mat = blockIdx.y;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= cols) return;
@@ -102,6 +104,7 @@ __device__ __forceinline__ float row_softmax_regs(float (&v)[EPT], int cols, int
 template <int EPT>
 __global__ void softmax_row_fwd_cached(const float* __restrict__ x, float* __restrict__ y, int rows, int cols,
                                        int causal) {
+    pdl_entry();
     __shared__ float scratch[32];
     const int64_t row = blockIdx.x;
     float v[EPT];
@@ -119,6 +122,7 @@ __global__ void softmax_row_fwd_cached(const float* __restrict__ x, float* __res
 
 __global__ void softmax_row_fwd_generic(const float* __restrict__ x, float* __restrict__ y, int rows, int cols,
                                         int causal) {
+    pdl_entry();
     __shared__ float scratch[32];
     const int64_t row = blockIdx.x;
     const int r_in = (int)(row % rows);
@@ -148,6 +152,7 @@ __global__ void softmax_row_fwd_generic(const float* __restrict__ x, float* __re
 
 __global__ void softmax_row_bwd(const float* __restrict__ y, const float* __restrict__ gy, float* __restrict__ gx,
                                 int cols) {
+    pdl_entry();
     __shared__ float scratch[32];
     const int64_t row = blockIdx.x;
     const float* yr = y + row * cols;
@@ -164,6 +169,7 @@ template <int EPT>
 __global__ void smce_fwd_cached(const float* __restrict__ logits, const float* __restrict__ target,
                                 float* __restrict__ probs, float* __restrict__ loss, float* __restrict__ grad,
                                 float batch_div, int cols, double total) {
+    pdl_entry();
     __shared__ float scratch[32];
     __shared__ double dscratch[32];
     const int64_t row = blockIdx.x;
@@ -197,6 +203,7 @@ __global__ void smce_fwd_cached(const float* __restrict__ logits, const float* _
 __global__ void smce_fwd_generic(const float* __restrict__ logits, const float* __restrict__ target,
                                  float* __restrict__ probs, float* __restrict__ loss, float* __restrict__ grad,
                                  float batch_div, int cols, double total) {
+    pdl_entry();
     __shared__ float scratch[32];
     __shared__ double dscratch[32];
     const int64_t row = blockIdx.x;
@@ -232,6 +239,7 @@ __global__ void smce_fwd_generic(const float* __restrict__ logits, const float* 
 __global__ void smce_bwd_kernel(const float* __restrict__ probs, const float* __restrict__ target,
                                 const float* __restrict__ upstream, float* __restrict__ grad, float batch_div,
                                 int64_t n) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
         float g = probs[i] + (-1.0f) * target[i];
@@ -243,6 +251,7 @@ __global__ void smce_bwd_kernel(const float* __restrict__ probs, const float* __
 // ------------------------------------ MSE -----------------------------------
 __global__ void mse_fwd_kernel(const float* __restrict__ x, const float* __restrict__ t, float* __restrict__ loss,
                                int64_t n) {
+    pdl_entry();
     __shared__ double dscratch[32];
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     double part = 0.0;
@@ -256,6 +265,7 @@ __global__ void mse_fwd_kernel(const float* __restrict__ x, const float* __restr
 
 __global__ void mse_bwd_kernel(const float* __restrict__ x, const float* __restrict__ t,
                                const float* __restrict__ upstream, float* __restrict__ gx, int64_t n) {
+    pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const float nf = (float)n;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -279,19 +289,19 @@ int mle_softmax_fwd(const float* x, float* y, int64_t bc, int rows, int cols, in
     if (axis == 1) {
         if (bc > 65535) return MLE_ERR_UNSUPPORTED;
         dim3 grid((cols + kColThreads - 1) / kColThreads, (unsigned)bc);
-        softmax_col_fwd<<<grid, kColThreads, 0, st>>>(x, y, rows, cols, causal);
+        launch_k(softmax_col_fwd, grid, kColThreads, 0, st, x, y, rows, cols, causal);
         return launch_status();
     }
     const int64_t nrows = bc * rows;
     if (cols % 4 == 0 && cols <= 4 * kRowThreads * 4 && aligned16(x) && aligned16(y)) {
         if (cols <= 4 * kRowThreads)
-            softmax_row_fwd_cached<4><<<(unsigned)nrows, kRowThreads, 0, st>>>(x, y, rows, cols, causal);
+            launch_k(softmax_row_fwd_cached<4>, (unsigned)nrows, kRowThreads, 0, st, x, y, rows, cols, causal);
         else if (cols <= 8 * kRowThreads)
-            softmax_row_fwd_cached<8><<<(unsigned)nrows, kRowThreads, 0, st>>>(x, y, rows, cols, causal);
+            launch_k(softmax_row_fwd_cached<8>, (unsigned)nrows, kRowThreads, 0, st, x, y, rows, cols, causal);
         else
-            softmax_row_fwd_cached<16><<<(unsigned)nrows, kRowThreads, 0, st>>>(x, y, rows, cols, causal);
+            launch_k(softmax_row_fwd_cached<16>, (unsigned)nrows, kRowThreads, 0, st, x, y, rows, cols, causal);
     } else {
-        softmax_row_fwd_generic<<<(unsigned)nrows, kRowThreads, 0, st>>>(x, y, rows, cols, causal);
+        launch_k(softmax_row_fwd_generic, (unsigned)nrows, kRowThreads, 0, st, x, y, rows, cols, causal);
     }
     return launch_status();
 }
@@ -304,9 +314,9 @@ int mle_softmax_bwd(const float* y, const float* gy, float* gx, int64_t bc, int 
     if (axis == 1) {
         if (bc > 65535) return MLE_ERR_UNSUPPORTED;
         dim3 grid((cols + kColThreads - 1) / kColThreads, (unsigned)bc);
-        softmax_col_bwd<<<grid, kColThreads, 0, st>>>(y, gy, gx, rows, cols);
+        launch_k(softmax_col_bwd, grid, kColThreads, 0, st, y, gy, gx, rows, cols);
     } else {
-        softmax_row_bwd<<<(unsigned)(bc * rows), kRowThreads, 0, st>>>(y, gy, gx, cols);
+        launch_k(softmax_row_bwd, (unsigned)(bc * rows), kRowThreads, 0, st, y, gy, gx, cols);
     }
     return launch_status();
 }
@@ -321,16 +331,16 @@ int mle_softmax_ce_fwd(const float* logits, const float* target, float* probs, f
     const bool vec = cols % 4 == 0 && aligned16(logits) && aligned16(target) && (!probs || aligned16(probs)) &&
                      (!grad || aligned16(grad));
     if (vec && cols <= 4 * kRowThreads)
-        smce_fwd_cached<4><<<(unsigned)rows, kRowThreads, 0, st>>>(logits, target, probs, loss, grad, batch_div, cols,
+        launch_k(smce_fwd_cached<4>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, cols,
                                                                   total);
     else if (vec && cols <= 8 * kRowThreads)
-        smce_fwd_cached<8><<<(unsigned)rows, kRowThreads, 0, st>>>(logits, target, probs, loss, grad, batch_div, cols,
+        launch_k(smce_fwd_cached<8>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, cols,
                                                                   total);
     else if (vec && cols <= 16 * kRowThreads)
-        smce_fwd_cached<16><<<(unsigned)rows, kRowThreads, 0, st>>>(logits, target, probs, loss, grad, batch_div,
+        launch_k(smce_fwd_cached<16>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div,
                                                                    cols, total);
     else
-        smce_fwd_generic<<<(unsigned)rows, kRowThreads, 0, st>>>(logits, target, probs, loss, grad, batch_div, cols,
+        launch_k(smce_fwd_generic, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, cols,
                                                                  total);
     return launch_status();
 }
@@ -339,7 +349,7 @@ int mle_softmax_ce_bwd(const float* probs, const float* target, const float* ups
                        int64_t n, mle_stream_t stream) {
     if (n < 0 || !probs || !target || !grad || batch_div == 0.0f) return MLE_ERR_ARG;
     if (n == 0) return MLE_OK;
-    smce_bwd_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(probs, target, upstream, grad, batch_div, n);
+    launch_k(smce_bwd_kernel, grid_for(n, 256), 256, 0, as_stream(stream), probs, target, upstream, grad, batch_div, n);
     return launch_status();
 }
 
@@ -347,14 +357,14 @@ int mle_mse_fwd(const float* x, const float* target, float* loss, int64_t n, mle
     if (n <= 0 || !x || !target || !loss) return MLE_ERR_ARG;
     cudaStream_t st = as_stream(stream);
     if (cudaMemsetAsync(loss, 0, sizeof(float), st) != cudaSuccess) return launch_status();
-    mse_fwd_kernel<<<grid_for(n, 256, 4), 256, 0, st>>>(x, target, loss, n);
+    launch_k(mse_fwd_kernel, grid_for(n, 256, 4), 256, 0, st, x, target, loss, n);
     return launch_status();
 }
 
 int mle_mse_bwd(const float* x, const float* target, const float* upstream, float* gx, int64_t n,
                 mle_stream_t stream) {
     if (n <= 0 || !x || !target || !gx) return MLE_ERR_ARG;
-    mse_bwd_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(x, target, upstream, gx, n);
+    launch_k(mse_bwd_kernel, grid_for(n, 256), 256, 0, as_stream(stream), x, target, upstream, gx, n);
     return launch_status();
 }
 
