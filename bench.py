@@ -103,6 +103,42 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
+# ------------------------------------------------------------ ranks
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    """Largest value of x over the ranks (every rank gets it)."""
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def init_ranks():
+    """(world, rank, local_rank) from the torchrun environment; joins the
+    process group (NCCL on GPUs, gloo without) with a short timeout."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local_rank))
+        else:
+            dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+    return world, rank, local_rank
+
+
 # ------------------------------------------------------------ CPU baseline
 def cpu_sample(seconds=10.0, max_steps=None):
     """The oracle's encoder step (OpenMP C restatement) on one sequence of
@@ -190,19 +226,6 @@ def run_native(args, rank, world, local_rank):
         s.inputs["tokens"][:] = tok
         s.inputs["targets"][:] = tgt
 
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-
-    def max_over_ranks(x):
-        if world > 1:
-            import torch.distributed as dist
-            t = torch.tensor([x], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            return float(t.item())
-        return x
-
     feed(0)
     s.step()                 # eager step: builds tensor maps, configures kernels
     s.capture()
@@ -219,7 +242,7 @@ def run_native(args, rank, world, local_rank):
         if "CUDA_VISIBLE_DEVICES" in os.environ else str(local_rank)
     # ---------------------------------------------------------------- value
     with ClockSampler(smi_index) as clocks:
-        barrier()
+        barrier(world)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -227,11 +250,11 @@ def run_native(args, rank, world, local_rank):
             s.step(upload=False, read_loss=False)
         e1.record(stream)
         torch.cuda.synchronize()
-        barrier()
-        dev_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        barrier(world)
+        dev_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
 
         # ------------------------------------------------------------- e2e
-        barrier()
+        barrier(world)
         torch.cuda.synchronize()
         e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e2.record(stream)
@@ -241,8 +264,8 @@ def run_native(args, rank, world, local_rank):
             losses.append(s.step(upload=True, read_loss=True))
         e3.record(stream)
         torch.cuda.synchronize()
-        barrier()
-        e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps)
+        barrier(world)
+        e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps, world, dev)
     clk = clocks.summary()
 
     # ---------------------------------------------------- roofline kernel
@@ -310,15 +333,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
+    world, rank, local_rank = init_ranks()
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)

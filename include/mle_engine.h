@@ -110,6 +110,15 @@ int mle_session_node_count(mle_session_t s);
 /* Writes a fresh NCCL unique id (128 bytes) for rank 0 to distribute. */
 int mle_dp_unique_id(uint8_t* out128);
 
+/* Host-side bucket plan of data parallelism (what mle_session_enable_dp
+ * uses): gradient tensors (device addresses and float counts) sorted by
+ * address and merged while contiguous (gaps up to 64 floats bridged) within
+ * bucket_mb MiB.  Writes up to max_out buckets (base address, float count)
+ * and their number to *out_n; MLE_ERR_ARG if more than max_out are needed.
+ * Touches no device. */
+int mle_dp_plan_buckets(const uint64_t* addrs, const int64_t* counts, int n, int bucket_mb,
+                        uint64_t* out_base, int64_t* out_count, int max_out, int* out_n);
+
 /* Joins a communicator of `world` ranks.  After backward, the parameter
  * gradients are summed over ranks in buckets of `bucket_mb` MiB on a second
  * stream, each bucket as soon as the backward pass has produced every

@@ -97,9 +97,9 @@ class _Lib:
     def call(self, name: str, *args):
         st = getattr(self.dll, name)(*args)
         if st != 0:
-            err = self.dll.mle_last_cuda_error() if hasattr(self.dll, "mle_last_cuda_error") else 0
-            msg = self.dll.mle_status_string(st).decode() if hasattr(self.dll, "mle_status_string") else str(st)
-            raise MLEError(f"{name} -> status {st} ({msg}), cuda error {err}")
+            k = kernels()   # status strings and the CUDA error live in the kernel library
+            raise MLEError(f"{name} -> status {st} ({k.dll.mle_status_string(st).decode()}), "
+                           f"cuda error {k.dll.mle_last_cuda_error()}")
         return st
 
 

@@ -595,6 +595,7 @@ void GraphOperations::backward(const graph& X, const bool show, const bool time,
             if (check_nan) host_nan_check((*it)->grad, (*it)->total, "IsNan of " + (*it)->op_name);
             if (show) print_head((*it)->grad, (*it)->total, (*it)->op_name);
         }
+        if (on_backward_done) on_backward_done(it->get());
         if (time) {
             CheckError("After " + (*it)->op_name + " backward");
             auto t1 = std::chrono::high_resolution_clock::now();

@@ -178,6 +178,10 @@ class GraphOperations {
     // Multiplies every gradient by `scale` inside the next update and
     // before the norm (data-parallel averaging).
     void set_grad_prescale(float scale) { grad_prescale_ = scale; }
+    // Called after each node's backward lambda has been issued (data
+    // parallelism starts a bucket's reduction as soon as its last gradient
+    // is complete).
+    std::function<void(const NodeBackProp*)> on_backward_done;
 
     static graph Copy(const graph& X);
     static graph identity(const graph& X);

@@ -47,6 +47,7 @@ struct NodeExt {
     bool bias_grad_fused = false;        // Linear: the consumer adds the bias grad
     float* fused_bias_target = nullptr;  // activation: bias grad to accumulate
     long long fused_rows = 0, fused_cols = 0;
+    std::vector<float*> param_grads;     // parameter gradients complete once this node's backward ran
 };
 NodeExt& ext(const NodeBackProp* n);
 void forget_ext(const NodeBackProp* n);

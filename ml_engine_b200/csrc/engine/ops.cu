@@ -656,6 +656,8 @@ graph Linear::forward(const graph& X) {
     NodeExt& e = ext(nd);
     e.kind = OP_LINEAR;
     e.linear_bias_grad = bias ? B1.grad : nullptr;
+    e.param_grads = {W1.grad};
+    if (bias) e.param_grads.push_back(B1.grad);
     node->forward = [=]() {
         check(mle_linear_fwd(xp->output, W->output, Bp ? Bp->output : nullptr, nd->output, rows, n, p, st()),
               "Linear forward");

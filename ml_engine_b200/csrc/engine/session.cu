@@ -245,6 +245,7 @@ void run_phase(Session& S, int phase) {
             S.go.forward(nullptr, true);
             break;
         case 2:
+            if (S.dp) S.dp->begin_backward();
             S.go.backward();
             break;
         case 3:
@@ -530,6 +531,11 @@ int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int w
     if (st_ != MLE_OK) return st_;
     S->dp = std::move(dp);
     S->go.set_grad_prescale(1.0f / (float)world);
+    DataParallel* d = S->dp.get();
+    S->go.on_backward_done = [d](const NodeBackProp* n) {
+        const std::vector<float*>& g = ext(n).param_grads;
+        if (!g.empty()) d->grads_done(g, stream());
+    };
     return MLE_OK;
 }
 

@@ -12,28 +12,46 @@
 
 namespace mle {
 
+struct GradBucket {
+    float* base;
+    int64_t count;  // floats, from base
+};
+
+// Buckets over the parameter gradients: (pointer, element count) pairs are
+// sorted by address and merged while they are contiguous (a gap of at most
+// 64 floats -- one 256-byte arena pad, which belongs to no tensor -- is
+// bridged) and the bucket stays within bucket_mb MiB; a tensor larger than
+// that forms a bucket of its own.
+std::vector<GradBucket> plan_buckets(std::vector<std::pair<float*, int64_t>> grads, int bucket_mb);
+
 class DataParallel {
    public:
     DataParallel() = default;
     ~DataParallel();
-    // grads: (pointer, element count) of every parameter gradient, in the
-    // order the backward pass finishes them last.
     int init(const uint8_t* id128, int rank, int world, const std::vector<std::pair<float*, int64_t>>& grads,
              int bucket_mb, cudaStream_t compute);
-    // Sums every bucket over the ranks (on the comm stream, ordered after the
-    // work already queued on `compute`) and makes `compute` wait for it.
+    // Backward of one step starts: every bucket waits for all its tensors.
+    void begin_backward();
+    // `grads` are complete once the work queued on `compute` so far has run:
+    // each bucket whose last tensor this was is summed over the ranks on the
+    // comm stream, overlapping the rest of the backward.
+    void grads_done(const std::vector<float*>& grads, cudaStream_t compute);
+    // Sums the buckets not started yet and makes `compute` wait for every
+    // reduction (before clip and update).
     void reduce_remaining(cudaStream_t compute);
     int world() const { return world_; }
+    int bucket_count() const { return (int)buckets_.size(); }
 
    private:
-    struct Bucket {
-        float* base;
-        int64_t count;
-    };
-    std::vector<Bucket> buckets_;
+    void issue(int b, cudaStream_t compute);
+    std::vector<GradBucket> buckets_;
+    std::vector<int> members_, pending_;
+    std::vector<char> issued_;
+    std::vector<cudaEvent_t> ready_;
+    std::vector<std::pair<float*, int>> bucket_of_;  // grad pointer -> bucket, sorted
     void* comm_ = nullptr;
     cudaStream_t comm_stream_ = nullptr;
-    cudaEvent_t ready_ = nullptr, done_ = nullptr;
+    cudaEvent_t done_ = nullptr;
     int rank_ = 0, world_ = 1;
 };
 
