@@ -197,12 +197,38 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------ roofline kernel
+def roofline_pair(dev, stream, reps=50):
+    """The projection layer's backward GEMMs (dX = dY W^T, dW = X^T dY),
+    2 * 2 * 4096 * 256 * 4096 FLOP per pair, on `stream`: 3 untimed pairs,
+    then `reps` pairs between CUDA events.  Returns (ms per pair, FLOP)."""
+    import torch
+
+    from ml_engine_b200 import ops
+    M, K, N = TOKENS_PER_STEP, CFG["d_model"], CFG["vocab"]
+    g = torch.Generator(device=dev).manual_seed(0)
+    X = torch.randn(M, K, device=dev, generator=g)
+    W = torch.randn(K, N, device=dev, generator=g) * 0.02
+    dY = torch.randn(M, N, device=dev, generator=g) * 1e-3
+    dX, dW = torch.zeros(M, K, device=dev), torch.zeros(K, N, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            ops.linear_bwd(X, W, dY, dX, dW, None, M, K, N)
+        torch.cuda.synchronize()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(reps):
+            ops.linear_bwd(X, W, dY, dX, dW, None, M, K, N)
+        k1.record(stream)
+        torch.cuda.synchronize()
+    return k0.elapsed_time(k1) / reps, 2 * 2.0 * M * K * N
+
+
 # ------------------------------------------------------------ native arm
 def run_native(args, rank, world, local_rank):
     import numpy as np
     import torch
 
-    from ml_engine_b200 import ops
     from ml_engine_b200.session import Session
 
     dev = torch.device("cuda", local_rank)
@@ -268,28 +294,7 @@ def run_native(args, rank, world, local_rank):
         e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps, world, dev)
     clk = clocks.summary()
 
-    # ---------------------------------------------------- roofline kernel
-    # the projection layer's backward GEMMs (dX = dY W^T, dW = X^T dY),
-    # 2 * 2 * 4096 * 256 * 4096 FLOP per pair, on the same stream
-    M, K, N = TOKENS_PER_STEP, CFG["d_model"], CFG["vocab"]
-    g = torch.Generator(device=dev).manual_seed(0)
-    X = torch.randn(M, K, device=dev, generator=g)
-    W = torch.randn(K, N, device=dev, generator=g) * 0.02
-    dY = torch.randn(M, N, device=dev, generator=g) * 1e-3
-    dX, dW = torch.zeros(M, K, device=dev), torch.zeros(K, N, device=dev)
-    flops_pair = 2 * 2.0 * M * K * N
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            ops.linear_bwd(X, W, dY, dX, dW, None, M, K, N)
-        torch.cuda.synchronize()
-        reps = 50
-        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        k0.record(stream)
-        for _ in range(reps):
-            ops.linear_bwd(X, W, dY, dX, dW, None, M, K, N)
-        k1.record(stream)
-        torch.cuda.synchronize()
-    kern_ms = k0.elapsed_time(k1) / reps
+    kern_ms, flops_pair = roofline_pair(dev, stream)
     achieved_tf = flops_pair / (kern_ms * 1e-3) / 1e12
     traffic = None
     prof = ROOT / "profiles" / "traffic.json"
@@ -332,7 +337,15 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--roofline-only", action="store_true",
+                    help="run only the roofline kernel pair (3 + 2 pairs; for a profiler capture)")
     args = ap.parse_args()
+    if args.roofline_only:
+        import torch
+        dev = torch.device("cuda", 0)
+        ms, flops = roofline_pair(dev, torch.cuda.current_stream(dev), reps=2)
+        print(json.dumps({"roofline_pair_ms": ms, "flop": flops}))
+        return
     world, rank, local_rank = init_ranks()
     try:
         if args.impl == "reference":

@@ -84,6 +84,11 @@ int mle_session_capture(mle_session_t s);
  * (the launches one replay issues). */
 int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* copies);
 
+/* Dependency edges of the same graph: all of them, and those of the
+ * programmatic kind (a kernel that may start its prologue while the
+ * previous kernel finishes). */
+int mle_session_graph_edges(mle_session_t s, int* edges, int* programmatic);
+
 int mle_session_sync(mle_session_t s);
 
 /* Parameters in graph order (W1 then B1 per Linear). */

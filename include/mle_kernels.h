@@ -364,6 +364,59 @@ int mle_rows_add_table(const float* x, const float* table, float* y, int64_t bat
                        mle_stream_t stream);
 
 /* ------------------------------------------------------------------ */
+/* 2-D convolution and transposed convolution (NCHW, fp32)              */
+/* ------------------------------------------------------------------ */
+
+/* Output size of Convolute2D, (in + 2*pad - k)/stride + 1 (-1 if the
+ * kernel does not fit), and of Convolute2DT, (in - 1)*stride - 2*pad + k
+ * (Engine/engine.cu:3744-3745,3842-3843). */
+int mle_conv_out_size(int in, int k, int pad, int stride);
+int mle_convT_out_size(int in, int k, int pad, int stride);
+
+/* cols[n][(c*kh + i)*kw + j][oy*OW + ox] = x[n][c][oy*stride - pad + i][ox*stride - pad + j]
+ * (0 outside the image), OH/OW from mle_conv_out_size; and the gather
+ * adjoint x[n][c][y][x] (= or +=) sum of the columns entries that read it. */
+int mle_im2col(const float* x, float* cols, int batch, int channels, int h, int w, int kh, int kw,
+               int pad, int stride, mle_stream_t stream);
+int mle_col2im(const float* cols, float* x, int batch, int channels, int h, int w, int kh, int kw,
+               int pad, int stride, int accumulate, mle_stream_t stream);
+/* out = in with two of its three dimensions exchanged: mode 0
+ * [a][b][c] -> [b][a][c], mode 1 [a][b][c] -> [a][c][b]. */
+int mle_swap_dims(const float* in, float* out, int a, int b, int c, int mode, mle_stream_t stream);
+
+/* Convolute2D (Engine/engine.cu:3732-3817): weights [cout][cin][kh][kw],
+ * x [batch][cin][h][w], y [batch][cout][OH][OW].
+ *   forward : y = conv(x) (+ bias) (assigned, CV2D Engine/kernels.cu:985-1019);
+ *             ws receives the im2col columns of x
+ *             (mle_conv2d_workspace_floats floats) and must still hold them
+ *             when the backward runs;
+ *   backward: dw = sum over the batch (assigned, GV2D :1021-1051), db +=
+ *             channel sums (Channel_Squeeze1D :1734-1761), dx += (CV2D_GradInput
+ *             :1053-1089); any of dx, dw, db may be NULL; ws is consumed. */
+int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int kh, int kw, int pad, int stride);
+int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y, float* ws, int batch,
+                   int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
+                   mle_stream_t stream);
+int mle_conv2d_bwd(const float* wgt, const float* dy, float* dx, float* dw, float* db, float* ws,
+                   int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
+                   mle_stream_t stream);
+
+/* Convolute2DT (Engine/engine.cu:3828-3912): weights [cout][cin][kh][kw],
+ * x [batch][cin][h][w], y [batch][cout][OH][OW] with OH from
+ * mle_convT_out_size.  forward y = (assigned, CVT2D :1091-1135) (+ bias);
+ * backward dw = (assigned, GVT2D :1137-1176), db += , dx = (assigned,
+ * CVT2D_GradInput :1178-1212).  ws: mle_convT2d_workspace_floats floats,
+ * scratch for each call. */
+int64_t mle_convT2d_workspace_floats(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad,
+                                     int stride);
+int mle_convT2d_fwd(const float* x, const float* wgt, const float* bias, float* y, float* ws, int batch,
+                    int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
+                    mle_stream_t stream);
+int mle_convT2d_bwd(const float* x, const float* wgt, const float* dy, float* dx, float* dw, float* db,
+                    float* ws, int batch, int cin, int h, int w, int cout, int kh, int kw, int pad,
+                    int stride, mle_stream_t stream);
+
+/* ------------------------------------------------------------------ */
 /* gradient-norm clip + Adam/AdamW                                      */
 /* ------------------------------------------------------------------ */
 

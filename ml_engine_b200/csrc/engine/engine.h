@@ -251,3 +251,30 @@ class Linear {
     void load(std::ifstream& f);
     void operator=(const Linear& other);
 };
+
+// Convolute2D (Includes/engine.h:235-255): weights [out][inp][C][D], NCHW.
+class Convolute2D {
+   public:
+    int inp, out, c, d, pad, stride;
+    str name;
+    AdamParameter W1, B1;
+    Convolute2D(int Input, int Output, int C = 3, int D = 3, int stride = 1, int padding = 1, str param = "");
+    void save(std::ofstream& f) const;
+    void load(std::ifstream& f);
+    graph forward(const graph& X);
+};
+
+// Convolute2DT (Includes/engine.h:257-280): weights [out][inp][C][D].
+class Convolute2DT {
+   private:
+    graph T_node;
+    int inp, out, c, d, pad, stride;
+
+   public:
+    str name;
+    AdamParameter W1, B1;
+    Convolute2DT(int Input, int Output, int C = 2, int D = 2, int stride = 2, int padding = 0, str param = "");
+    void save(std::ofstream& f) const;
+    void load(std::ifstream& f);
+    graph forward(const graph& X);
+};

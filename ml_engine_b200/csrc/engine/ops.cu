@@ -688,3 +688,131 @@ graph Linear::forward(const graph& X) {
     };
     return node;
 }
+
+// --------------------------------------------- Convolute2D (Engine/engine.cu:3723-3817)
+Convolute2D::Convolute2D(int Input, int Output, int C, int D, int stride_, int padding, str param)
+    : inp(Input), out(Output), c(C), d(D), pad(padding), stride(stride_), name(param),
+      W1(name + " Weight ", Output, Input, C, D), B1(name + " Bias ", 1, Output, 1, 1) {}
+
+void Convolute2D::save(std::ofstream& f) const {
+    W1.save(f);
+    B1.save(f);
+}
+void Convolute2D::load(std::ifstream& f) {
+    W1.load(f);
+    B1.load(f);
+}
+
+namespace {
+// the parameter-side lambdas every convolution layer shares with Linear
+void conv_param_lambdas(const graph& node, AdamParameter* W, AdamParameter* B) {
+    NodeBackProp* nd = node.get();
+    node->zero_grad = [=]() {
+        zero_range(nd->grad, nd->total);
+        zero_range(W->grad, W->total);
+        zero_range(B->grad, B->total);
+    };
+    node->free = [nd]() { nd->clear(); };
+    node->accumulate = [=](double* gs) {
+        W->accumulate_grad(gs);
+        B->accumulate_grad(gs);
+    };
+    node->clipnorm = [=](const double* gs) {
+        W->gradnorm(gs);
+        B->gradnorm(gs);
+    };
+    node->updateParams = [=](const float lr, const bool adamw) {
+        W->update(lr, adamw);
+        B->update(lr, adamw);
+    };
+    ext(nd).param_grads = {W->grad, B->grad};
+}
+}  // namespace
+
+graph Convolute2D::forward(const graph& X) {
+    if (X->dim[1] != inp) {
+        std::cout << "Dimension Mismatch! in " << name << ": \n";
+        Dimension(X);
+        std::cout << "Actual input (Batch x depth): (" << X->dim[0] << "x" << X->dim[1] << ") \n";
+        std::cout << "Expected input (Batch x depth): (" << X->dim[0] << "x" << inp << ") \n";
+        std::exit(1);
+    }
+    const int batch = X->dim[0], a = X->dim[2], b = X->dim[3];
+    const int outR = mle_conv_out_size(a, c, pad, stride), outC = mle_conv_out_size(b, d, pad, stride);
+    if (outR <= 0 || outC <= 0) {
+        std::cout << "Kernel larger than the padded input in " << name << "\n";
+        std::exit(1);
+    }
+    auto node = std::make_shared<NodeBackProp>(name, batch, out, outR, outC, 1);
+    node->inputs = {X};
+    GraphOperations::GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    const int64_t wsn = mle_conv2d_workspace_floats(batch, inp, a, b, c, d, pad, stride);
+    float* ws = arena_alloc(ARENA_WS, wsn, name + " columns");
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    AdamParameter *W = &W1, *B = &B1;
+    const int ci = inp, co = out, kh = c, kw = d, p = pad, s = stride;
+    node->forward = [=]() {
+        check(mle_conv2d_fwd(xp->output, W->output, B->output, nd->output, ws, batch, ci, a, b, co, kh, kw, p, s, st()),
+              "Forward Convolution in " + nd->op_name);
+    };
+    node->backward = [=]() {
+        // dW assigned (GV2D), dB += (Channel_Squeeze1D), dX += (CV2D_GradInput)
+        check(mle_conv2d_bwd(W->output, nd->grad, xp->grad, W->grad, B->grad, ws, batch, ci, a, b, co, kh, kw, p, s,
+                             st()),
+              "Weight + Bias + Input Gradient in " + nd->op_name);
+    };
+    conv_param_lambdas(node, W, B);
+    return node;
+}
+
+// -------------------------------------------- Convolute2DT (Engine/engine.cu:3819-3912)
+Convolute2DT::Convolute2DT(int Input, int Output, int C, int D, int stride_, int padding, str param)
+    : inp(Input), out(Output), c(C), d(D), pad(padding), stride(stride_), name(param),
+      W1(name + " Weight ", Output, Input, C, D), B1(name + " Bias ", 1, Output, 1, 1) {}
+
+void Convolute2DT::save(std::ofstream& f) const {
+    W1.save(f);
+    B1.save(f);
+}
+void Convolute2DT::load(std::ifstream& f) {
+    W1.load(f);
+    B1.load(f);
+}
+
+graph Convolute2DT::forward(const graph& X) {
+    if (X->dim[1] != inp) {
+        std::cout << "Dimension Mismatch! in " << name << ": \n";
+        Dimension(X);
+        std::cout << "Actual input (Batch x depth): (" << X->dim[0] << "x" << X->dim[1] << ") \n";
+        std::cout << "Expected input (Batch x depth): (" << X->dim[0] << "x" << inp << ") \n";
+        std::exit(1);
+    }
+    const int batch = X->dim[0], ih = X->dim[2], iw = X->dim[3];
+    const int oh = mle_convT_out_size(ih, c, pad, stride), ow = mle_convT_out_size(iw, d, pad, stride);
+    auto node = std::make_shared<NodeBackProp>(name, batch, out, oh, ow, 1);
+    node->inputs = {X};
+    T_node = node;
+    GraphOperations::GB += (double)(node->total + W1.total + B1.total) * sizeof(float) / (1ULL << 30);
+    const int64_t wsn = mle_convT2d_workspace_floats(batch, inp, ih, iw, out, c, d, pad, stride);
+    if (wsn < 0) {
+        std::cout << "Unsupported transposed-convolution geometry in " << name << "\n";
+        std::exit(1);
+    }
+    float* ws = arena_alloc(ARENA_WS, wsn, name + " workspace");
+    NodeBackProp *nd = node.get(), *xp = X.get();
+    AdamParameter *W = &W1, *B = &B1;
+    const int ci = inp, co = out, kh = c, kw = d, p = pad, s = stride;
+    node->forward = [=]() {
+        check(mle_convT2d_fwd(xp->output, W->output, B->output, nd->output, ws, batch, ci, ih, iw, co, kh, kw, p, s,
+                              st()),
+              "ConvTranspose2D Forward Kernel");
+    };
+    node->backward = [=]() {
+        // dW assigned (GVT2D), dB += (Channel_Squeeze1D), dX assigned (CVT2D_GradInput)
+        check(mle_convT2d_bwd(xp->output, W->output, nd->grad, xp->grad, W->grad, B->grad, ws, batch, ci, ih, iw, co,
+                              kh, kw, p, s, st()),
+              "Gradient w.r.t W, B1 and input for ConvTranspose2D");
+    };
+    conv_param_lambdas(node, W, B);
+    return node;
+}

@@ -521,6 +521,23 @@ int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* c
     return MLE_OK;
 }
 
+int mle_session_graph_edges(mle_session_t s, int* edges, int* programmatic) {
+    Session* S = as_session(s);
+    if (!S || !edges || !programmatic) return MLE_ERR_ARG;
+    *edges = *programmatic = 0;
+    if (!S->graph_[0]) return MLE_ERR_UNSUPPORTED;
+    size_t n = 0;
+    if (cudaGraphGetEdges_v2(S->graph_[0], nullptr, nullptr, nullptr, &n) != cudaSuccess) return MLE_ERR_CUDA;
+    std::vector<cudaGraphNode_t> from(n), to(n);
+    std::vector<cudaGraphEdgeData> data(n);
+    if (n && cudaGraphGetEdges_v2(S->graph_[0], from.data(), to.data(), data.data(), &n) != cudaSuccess)
+        return MLE_ERR_CUDA;
+    *edges = (int)n;
+    for (size_t i = 0; i < n; ++i)
+        if (data[i].type == cudaGraphDependencyTypeProgrammatic) ++*programmatic;
+    return MLE_OK;
+}
+
 int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int world, int bucket_mb) {
     Session* S = as_session(s);
     if (!S || !id128 || world <= 0 || rank < 0 || rank >= world) return MLE_ERR_ARG;

@@ -1,0 +1,276 @@
+// 2-D convolution and transposed convolution (Convolute2D / Convolute2DT,
+// Engine/engine.cu:3723-3912) on the tensor-core GEMM.
+//
+// The reference computes every output with one thread looping over
+// (channel, kh, kw) or over the whole batch (CV2D, GV2D, CV2D_GradInput,
+// CVT2D, GVT2D, CVT2D_GradInput, Engine/kernels.cu:985-1212).  Here each of
+// them is a GEMM over an im2col matrix:
+//   cols[n][(c, kh, kw)][(oy, ox)] = x[n][c][oy*s - p + kh][ox*s - p + kw]
+// (zero outside the image), so for a convolution with weights
+// W[Cout][Cin][KH][KW]
+//   forward  y[n]  = W · cols(x)[n]                  (M=Cout, N=OH*OW, K=Cin*KH*KW)
+//   dW            = sum_n dy[n] · cols(x)[n]^T         (assigned, as GV2D)
+//   dx      += col2im(W^T · dy[n])                     (gather, as CV2D_GradInput)
+// and the transposed convolution (weights W[Cout][Cin][KH][KW] with Cin the
+// input channels) is the adjoint geometry: its forward is col2im of
+// W'^T · x with W' = W with its first two dimensions swapped, its input
+// gradient a convolution of dy, its weight gradient a reduction over the
+// batch.  The column index k = c*KH*KW + kh*KW + kw ascends in the
+// reference's loop order, so the fp32 GEMM mode sums the forward in the
+// reference's order.
+#include <string.h>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace mle {
+namespace {
+
+constexpr int kT = 256;
+
+// cols[n][(c,kh,kw)][(oy,ox)]; one thread per column entry, (oy,ox) fastest
+__global__ void im2col_kernel(const float* __restrict__ x, float* __restrict__ cols, int C, int H, int W, int KH,
+                              int KW, int OH, int OW, int pad, int stride, int64_t total) {
+    pdl_entry();
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    const int64_t P = (int64_t)OH * OW, KK = (int64_t)KH * KW;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        const int64_t p = i % P;
+        int64_t r = i / P;
+        const int64_t k = r % (C * KK);
+        const int64_t n = r / (C * KK);
+        const int c = (int)(k / KK), kh = (int)((k % KK) / KW), kw = (int)(k % KW);
+        const int oy = (int)(p / OW), ox = (int)(p % OW);
+        const int iy = oy * stride - pad + kh, ix = ox * stride - pad + kw;
+        float v = 0.f;
+        if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = x[((n * C + c) * H + iy) * (int64_t)W + ix];
+        cols[i] = v;
+    }
+}
+
+// x[n][c][h][w] (=|+=) sum over the (kh, kw) taps that reach (h, w) of
+// cols[n][(c,kh,kw)][(oy,ox)], with h = oy*s - p + kh, w = ox*s - p + kw
+__global__ void col2im_kernel(const float* __restrict__ cols, float* __restrict__ x, int C, int H, int W, int KH,
+                              int KW, int OH, int OW, int pad, int stride, int accumulate, int64_t total) {
+    pdl_entry();
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    const int64_t P = (int64_t)OH * OW, KK = (int64_t)KH * KW;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        const int w = (int)(i % W);
+        const int h = (int)((i / W) % H);
+        const int64_t nc = i / ((int64_t)H * W);
+        const int c = (int)(nc % C);
+        const int64_t n = nc / C;
+        const float* base = cols + (n * C + c) * KK * P;
+        float s = 0.f;
+        for (int kh = 0; kh < KH; ++kh) {
+            const int ry = h + pad - kh;
+            if (ry < 0 || ry % stride != 0) continue;
+            const int oy = ry / stride;
+            if (oy >= OH) continue;
+            for (int kw = 0; kw < KW; ++kw) {
+                const int rx = w + pad - kw;
+                if (rx < 0 || rx % stride != 0) continue;
+                const int ox = rx / stride;
+                if (ox >= OW) continue;
+                s += base[((int64_t)kh * KW + kw) * P + (int64_t)oy * OW + ox];
+            }
+        }
+        x[i] = accumulate ? x[i] + s : s;
+    }
+}
+
+// out = in with two of its three dimensions exchanged:
+//   mode 0: [A][B][C] -> [B][A][C];  mode 1: [A][B][C] -> [A][C][B]
+__global__ void swap_dims_kernel(const float* __restrict__ in, float* __restrict__ out, int A, int B, int C, int mode,
+                                 int64_t total) {
+    pdl_entry();
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        const int c = (int)(i % C);
+        const int b = (int)((i / C) % B);
+        const int a = (int)(i / ((int64_t)B * C));
+        const int64_t o = mode == 0 ? ((int64_t)b * A + a) * C + c : ((int64_t)a * C + c) * B + b;
+        out[o] = in[i];
+    }
+}
+
+int im2col(const float* x, float* cols, int n, int c, int h, int w, int kh, int kw, int oh, int ow, int pad,
+           int stride, cudaStream_t st) {
+    const int64_t total = (int64_t)n * c * kh * kw * oh * ow;
+    if (total == 0) return MLE_OK;
+    launch_k(im2col_kernel, grid_for(total, kT), kT, 0, st, x, cols, c, h, w, kh, kw, oh, ow, pad, stride, total);
+    return launch_status();
+}
+
+int col2im(const float* cols, float* x, int n, int c, int h, int w, int kh, int kw, int oh, int ow, int pad,
+           int stride, int accumulate, cudaStream_t st) {
+    const int64_t total = (int64_t)n * c * h * w;
+    if (total == 0) return MLE_OK;
+    launch_k(col2im_kernel, grid_for(total, kT), kT, 0, st, cols, x, c, h, w, kh, kw, oh, ow, pad, stride, accumulate,
+             total);
+    return launch_status();
+}
+
+int swap_dims(const float* in, float* out, int a, int b, int c, int mode, cudaStream_t st) {
+    const int64_t total = (int64_t)a * b * c;
+    if (total == 0) return MLE_OK;
+    launch_k(swap_dims_kernel, grid_for(total, kT), kT, 0, st, in, out, a, b, c, mode, total);
+    return launch_status();
+}
+
+bool conv_shape_ok(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride) {
+    return batch > 0 && cin > 0 && h > 0 && w > 0 && cout > 0 && kh > 0 && kw > 0 && pad >= 0 && stride > 0;
+}
+
+}  // namespace
+}  // namespace mle
+
+using namespace mle;
+
+extern "C" {
+
+int mle_conv_out_size(int in, int k, int pad, int stride) {
+    if (stride <= 0 || in + 2 * pad < k) return -1;
+    return (in + 2 * pad - k) / stride + 1;
+}
+
+int mle_convT_out_size(int in, int k, int pad, int stride) { return (in - 1) * stride - 2 * pad + k; }
+
+int mle_im2col(const float* x, float* cols, int batch, int channels, int h, int w, int kh, int kw, int pad, int stride,
+               mle_stream_t stream) {
+    if (!x || !cols || batch < 0 || channels <= 0 || kh <= 0 || kw <= 0 || stride <= 0 || pad < 0) return MLE_ERR_ARG;
+    const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
+    if (oh <= 0 || ow <= 0) return MLE_ERR_ARG;
+    return im2col(x, cols, batch, channels, h, w, kh, kw, oh, ow, pad, stride, as_stream(stream));
+}
+
+int mle_col2im(const float* cols, float* x, int batch, int channels, int h, int w, int kh, int kw, int pad, int stride,
+               int accumulate, mle_stream_t stream) {
+    if (!x || !cols || batch < 0 || channels <= 0 || kh <= 0 || kw <= 0 || stride <= 0 || pad < 0) return MLE_ERR_ARG;
+    const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
+    if (oh <= 0 || ow <= 0) return MLE_ERR_ARG;
+    return col2im(cols, x, batch, channels, h, w, kh, kw, oh, ow, pad, stride, accumulate, as_stream(stream));
+}
+
+int mle_swap_dims(const float* in, float* out, int a, int b, int c, int mode, mle_stream_t stream) {
+    if (!in || !out || a < 0 || b < 0 || c < 0 || (mode != 0 && mode != 1) || in == out) return MLE_ERR_ARG;
+    return swap_dims(in, out, a, b, c, mode, as_stream(stream));
+}
+
+int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int kh, int kw, int pad, int stride) {
+    const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
+    if (batch <= 0 || cin <= 0 || oh <= 0 || ow <= 0) return -1;
+    return (int64_t)batch * cin * kh * kw * oh * ow;
+}
+
+int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y, float* ws, int batch, int cin,
+                   int h, int w, int cout, int kh, int kw, int pad, int stride, mle_stream_t stream) {
+    if (!x || !wgt || !y || !ws || !conv_shape_ok(batch, cin, h, w, cout, kh, kw, pad, stride)) return MLE_ERR_ARG;
+    const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
+    if (oh <= 0 || ow <= 0) return MLE_ERR_ARG;
+    cudaStream_t st = as_stream(stream);
+    const int64_t P = (int64_t)oh * ow, K = (int64_t)cin * kh * kw;
+    int s = im2col(x, ws, batch, cin, h, w, kh, kw, oh, ow, pad, stride, st);
+    if (s) return s;
+    // y[n][Cout][P] = W[Cout][K] * cols[n][K][P]
+    s = mle_gemm(wgt, ws, y, nullptr, batch, cout, P, K, K, P, P, 0, K * P, cout * P, 0, 0, 1.0f, 0.0f, stream);
+    if (s || !bias) return s;
+    return mle_channel_bias_fwd(y, bias, y, batch, cout, P, stream);
+}
+
+int mle_conv2d_bwd(const float* wgt, const float* dy, float* dx, float* dw, float* db, float* ws, int batch, int cin,
+                   int h, int w, int cout, int kh, int kw, int pad, int stride, mle_stream_t stream) {
+    if (!wgt || !dy || !ws || !conv_shape_ok(batch, cin, h, w, cout, kh, kw, pad, stride)) return MLE_ERR_ARG;
+    const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
+    if (oh <= 0 || ow <= 0) return MLE_ERR_ARG;
+    cudaStream_t st = as_stream(stream);
+    const int64_t P = (int64_t)oh * ow, K = (int64_t)cin * kh * kw;
+    int s;
+    if (dw) {
+        // dW[Cout][K] = sum_n dy[n][Cout][P] * cols[n][K][P]^T  (assigned, as GV2D)
+        if (cudaMemsetAsync(dw, 0, sizeof(float) * (size_t)(cout * K), st) != cudaSuccess) return launch_status();
+        s = mle_gemm(dy, ws, dw, nullptr, batch, cout, K, P, P, P, K, cout * P, K * P, 0, 0, 1, 1.0f, 1.0f, stream);
+        if (s) return s;
+    }
+    if (db) {
+        s = mle_channel_bias_bwd(dy, nullptr, db, batch, cout, P, stream);
+        if (s) return s;
+    }
+    if (dx) {
+        // the forward's columns are consumed: ws[n][K][P] = W^T * dy[n], then dx += col2im
+        s = mle_gemm(wgt, dy, ws, nullptr, batch, K, P, cout, K, P, P, 0, cout * P, K * P, 1, 0, 1.0f, 0.0f, stream);
+        if (s) return s;
+        return col2im(ws, dx, batch, cin, h, w, kh, kw, oh, ow, pad, stride, 1, st);
+    }
+    return MLE_OK;
+}
+
+int64_t mle_convT2d_workspace_floats(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride) {
+    const int oh = mle_convT_out_size(h, kh, pad, stride), ow = mle_convT_out_size(w, kw, pad, stride);
+    if (batch <= 0 || cin <= 0 || cout <= 0 || oh <= 0 || ow <= 0 || stride <= 0) return -1;
+    const int64_t KK = (int64_t)cout * kh * kw;
+    return 2 * KK * cin + (int64_t)batch * KK * h * w;
+}
+
+int mle_convT2d_fwd(const float* x, const float* wgt, const float* bias, float* y, float* ws, int batch, int cin,
+                    int h, int w, int cout, int kh, int kw, int pad, int stride, mle_stream_t stream) {
+    if (!x || !wgt || !y || !ws || !conv_shape_ok(batch, cin, h, w, cout, kh, kw, pad, stride)) return MLE_ERR_ARG;
+    const int oh = mle_convT_out_size(h, kh, pad, stride), ow = mle_convT_out_size(w, kw, pad, stride);
+    if (oh <= 0 || ow <= 0 || mle_conv_out_size(oh, kh, pad, stride) != h || mle_conv_out_size(ow, kw, pad, stride) != w)
+        return MLE_ERR_ARG;
+    cudaStream_t st = as_stream(stream);
+    const int64_t P = (int64_t)h * w, KK = (int64_t)cout * kh * kw;
+    float* wswap = ws;                 // [Cin][Cout][KH][KW]
+    float* cols = ws + 2 * KK * cin;   // [n][Cout*KH*KW][h*w]
+    int s = swap_dims(wgt, wswap, cout, cin, kh * kw, 0, st);
+    if (s) return s;
+    // cols[n][(oc,kh,kw)][p] = sum_ic W[oc][ic][kh][kw] x[n][ic][p]
+    s = mle_gemm(wswap, x, cols, nullptr, batch, KK, P, cin, KK, P, P, 0, (int64_t)cin * P, KK * P, 1, 0, 1.0f, 0.0f,
+                 stream);
+    if (s) return s;
+    // the output image is the "input" of the adjoint convolution geometry
+    s = col2im(cols, y, batch, cout, oh, ow, kh, kw, h, w, pad, stride, 0, st);
+    if (s || !bias) return s;
+    return mle_channel_bias_fwd(y, bias, y, batch, cout, (int64_t)oh * ow, stream);
+}
+
+int mle_convT2d_bwd(const float* x, const float* wgt, const float* dy, float* dx, float* dw, float* db, float* ws,
+                    int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
+                    mle_stream_t stream) {
+    if (!x || !wgt || !dy || !ws || !conv_shape_ok(batch, cin, h, w, cout, kh, kw, pad, stride)) return MLE_ERR_ARG;
+    const int oh = mle_convT_out_size(h, kh, pad, stride), ow = mle_convT_out_size(w, kw, pad, stride);
+    if (oh <= 0 || ow <= 0 || mle_conv_out_size(oh, kh, pad, stride) != h || mle_conv_out_size(ow, kw, pad, stride) != w)
+        return MLE_ERR_ARG;
+    cudaStream_t st = as_stream(stream);
+    const int64_t P = (int64_t)h * w, KK = (int64_t)cout * kh * kw;
+    float* wswap = ws;
+    float* tmp = ws + KK * cin;        // [(oc,kh,kw)][ic]
+    float* cols = ws + 2 * KK * cin;   // im2col of dy over the input positions
+    int s = im2col(dy, cols, batch, cout, oh, ow, kh, kw, h, w, pad, stride, st);
+    if (s) return s;
+    if (dw) {
+        // tmp[(oc,kh,kw)][ic] = sum_n cols[n][(oc,kh,kw)][p] x[n][ic][p]; dW = tmp
+        // with its last two dimensions exchanged (assigned, as GVT2D)
+        if (cudaMemsetAsync(tmp, 0, sizeof(float) * (size_t)(KK * cin), st) != cudaSuccess) return launch_status();
+        s = mle_gemm(cols, x, tmp, nullptr, batch, KK, cin, P, P, P, cin, KK * P, (int64_t)cin * P, 0, 0, 1, 1.0f, 1.0f,
+                     stream);
+        if (s) return s;
+        s = swap_dims(tmp, dw, cout, kh * kw, cin, 1, st);
+        if (s) return s;
+    }
+    if (db) {
+        s = mle_channel_bias_bwd(dy, nullptr, db, batch, cout, (int64_t)oh * ow, stream);
+        if (s) return s;
+    }
+    if (dx) {
+        // dx[n][ic][p] = sum_(oc,kh,kw) W[oc][ic][kh][kw] cols[n][(oc,kh,kw)][p]  (assigned, as CVT2D_GradInput)
+        s = swap_dims(wgt, wswap, cout, cin, kh * kw, 0, st);
+        if (s) return s;
+        return mle_gemm(wswap, cols, dx, nullptr, batch, cin, P, KK, KK, P, P, 0, KK * P, (int64_t)cin * P, 0, 0, 1.0f,
+                        0.0f, stream);
+    }
+    return MLE_OK;
+}
+
+}  // extern "C"

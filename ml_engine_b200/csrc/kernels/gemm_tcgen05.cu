@@ -22,6 +22,8 @@
 // the watchdog word, stops issuing work, lets issued copies and MMAs retire,
 // frees its TMEM and returns.
 #include <cuda.h>
+
+#include <algorithm>
 #include <stdio.h>
 #include <string.h>
 
@@ -452,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                ep.alpha * __uint_as_float(r[4 * j + 1]),
                                                ep.alpha * __uint_as_float(r[4 * j + 2]),
                                                ep.alpha * __uint_as_float(r[4 * j + 3]));
-                        if (ep.bias) {
+                        if (ep.bias && x.kb_begin == 0) {  // split 0 adds the bias
                             const int cb = col0 + 4 * j;
                             if (ep.vec && cb + 4 <= ep.N) {
                                 const float4 b = *reinterpret_cast<const float4*>(ep.bias + cb);
@@ -489,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int col = col0 + c4;
                 const bool vec = ep.vec && col + 4 <= ep.N;
                 float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (ep.bias) {
+                if (ep.bias && x.kb_begin == 0) {  // split 0 adds the bias
                     if (vec) {
                         bv = *reinterpret_cast<const float4*>(ep.bias + col);
                     } else {
@@ -664,25 +666,46 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     const int m_tiles = (p.M + BM - 1) / BM;
     const int kb_total = (p.K + BK - 1) / BK;
 
-    // Widest tile that still gives every SM a tile; narrow tiles otherwise.
-    int BN = 64;
-    for (int cand : {256, 128}) {
-        const int64_t t = (int64_t)m_tiles * ((p.N + cand - 1) / cand) * z_count;
-        if (p.N >= cand && t >= kSMs) {
-            BN = cand;
-            break;
+    // Tile width and split-K from a fill-time model.  Operand tiles reach
+    // shared memory at ~90 GB/s per SM, so the mainloop costs
+    // M*N*K*4*(1/BN + 1/BM) bytes spread over the SMs in use; splitting K
+    // adds one reduce-add of C per split (and, for an assigned C, a memset
+    // first).  An assigned C may be split only when it is one dense block.
+    const bool c_dense = p.ldc == p.N && (z_count == 1 || (p.c_sb == (int64_t)p.M * p.N && p.channels == 1));
+    const bool may_split = p.mode != EPI_ASSIGN || c_dense;
+    int BN = 64, splits = 1;
+    double best = 1e30;
+    for (int cand : {256, 128, 64}) {
+        if (cand > 64 && p.N < cand / 2 + 1) continue;
+        const int64_t nt = (p.N + cand - 1) / cand;
+        const int64_t units = (int64_t)m_tiles * nt * z_count;
+        const int max_split = may_split ? std::max(1, kb_total / 4) : 1;
+        for (int sp = 1; sp <= max_split; sp = (sp < 4 ? sp + 1 : sp * 2)) {
+            const int64_t work = units * sp;
+            const double active = (double)std::min<int64_t>(work, kSMs);
+            const double fill = (double)units * (BM + cand) * (double)kb_total * BK * 4.0;
+            double t = fill / (active * 90e9) + 0.3e-6 * (double)((work + kSMs - 1) / kSMs);
+            if (sp > 1) {
+                t += (double)sp * p.M * p.N * z_count * 4.0 / 3e12;
+                if (p.mode == EPI_ASSIGN) t += (double)p.M * p.N * z_count * 4.0 / 5e12;
+            }
+            if (t < best * 0.98) {
+                best = t;
+                BN = cand;
+                splits = sp;
+            }
+            if (work >= kSMs) break;
         }
     }
     const int n_tiles = (p.N + BN - 1) / BN;
     const int64_t tiles = (int64_t)m_tiles * n_tiles * z_count;
-    int splits = 1;
-    if (p.mode != EPI_ASSIGN && tiles < kSMs && kb_total >= 8) {
-        splits = (int)((kSMs + tiles - 1) / tiles);
-        if (splits > kb_total / 4) splits = kb_total / 4;
-        if (splits < 1) splits = 1;
-    }
     const int kb_per_split = (kb_total + splits - 1) / splits;
     splits = (kb_total + kb_per_split - 1) / kb_per_split;
+    if (splits > 1 && p.mode == EPI_ASSIGN) {
+        // split partial products are reduce-added into a zeroed C
+        const size_t bytes = sizeof(float) * (size_t)p.M * p.N * (size_t)z_count;
+        if (cudaMemsetAsync(p.C, 0, bytes, st) != cudaSuccess) return launch_status();
+    }
 
     EpiParams ep;
     ep.C = p.C;
@@ -709,7 +732,6 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     ep.mode = (splits > 1) ? EPI_ATOMIC : p.mode;
     ep.vec = ((p.ldc & 3) == 0) && aligned16(p.C) && ((ep.c_stride_b & 3) == 0) && ((ep.c_stride_c & 3) == 0) &&
              (p.bias == nullptr || aligned16(p.bias));
-    if (splits > 1 && p.bias) return simt_gemm(p, st);  // bias with split-K would be added per split
 
     OperandView va, vb;
     va.base = p.A;

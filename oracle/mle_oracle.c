@@ -479,3 +479,147 @@ void oracle_adam(float* w, const float* g, float* m, float* v, int64_t n, int t,
         else w[i] -= lr * m_hat / (vs + eps);
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* 2-D convolution and transposed convolution (NCHW); weights [O][I][KH][KW] */
+/* ------------------------------------------------------------------------ */
+/* CV2D (Engine/kernels.cu:985-1019): y = sum_{ci,kh,kw} x*k (+ bias), assigned */
+void oracle_conv2d_fwd(const float* x, const float* k, const float* bias, float* y, int N, int Cout, int Cin, int H,
+                       int W, int KH, int KW, int pad, int stride) {
+    const int OH = (2 * pad + H - KH) / stride + 1, OW = (2 * pad + W - KW) / stride + 1;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int n = 0; n < N; ++n)
+        for (int co = 0; co < Cout; ++co)
+            for (int oy = 0; oy < OH; ++oy)
+                for (int ox = 0; ox < OW; ++ox) {
+                    double s = 0.0;
+                    for (int ci = 0; ci < Cin; ++ci)
+                        for (int kh = 0; kh < KH; ++kh)
+                            for (int kw = 0; kw < KW; ++kw) {
+                                const int iy = oy * stride - pad + kh, ix = ox * stride - pad + kw;
+                                if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+                                s += (double)x[(((int64_t)n * Cin + ci) * H + iy) * W + ix] *
+                                     (double)k[(((int64_t)co * Cin + ci) * KH + kh) * KW + kw];
+                            }
+                    const float v = (float)s;
+                    y[(((int64_t)n * Cout + co) * OH + oy) * OW + ox] = bias ? v + bias[co] : v;
+                }
+}
+
+/* GV2D (Engine/kernels.cu:1021-1051): dK = sum_{n,oy,ox} x*dZ, assigned */
+void oracle_conv2d_bwd_k(const float* x, const float* dz, float* dk, int N, int Cout, int Cin, int H, int W, int KH,
+                         int KW, int pad, int stride) {
+    const int OH = (2 * pad + H - KH) / stride + 1, OW = (2 * pad + W - KW) / stride + 1;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int co = 0; co < Cout; ++co)
+        for (int ci = 0; ci < Cin; ++ci)
+            for (int kh = 0; kh < KH; ++kh)
+                for (int kw = 0; kw < KW; ++kw) {
+                    double s = 0.0;
+                    for (int n = 0; n < N; ++n)
+                        for (int oy = 0; oy < OH; ++oy)
+                            for (int ox = 0; ox < OW; ++ox) {
+                                const int iy = oy * stride - pad + kh, ix = ox * stride - pad + kw;
+                                if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+                                s += (double)x[(((int64_t)n * Cin + ci) * H + iy) * W + ix] *
+                                     (double)dz[(((int64_t)n * Cout + co) * OH + oy) * OW + ox];
+                            }
+                    dk[(((int64_t)co * Cin + ci) * KH + kh) * KW + kw] = (float)s;
+                }
+}
+
+/* CV2D_GradInput (Engine/kernels.cu:1053-1089): dX += sum_{oc,kh,kw} dY*K */
+void oracle_conv2d_bwd_x(const float* dy, const float* k, float* dx, int N, int Cout, int Cin, int H, int W, int KH,
+                         int KW, int pad, int stride) {
+    const int OH = (2 * pad + H - KH) / stride + 1, OW = (2 * pad + W - KW) / stride + 1;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int n = 0; n < N; ++n)
+        for (int ci = 0; ci < Cin; ++ci)
+            for (int ih = 0; ih < H; ++ih)
+                for (int iw = 0; iw < W; ++iw) {
+                    double s = 0.0;
+                    for (int oc = 0; oc < Cout; ++oc)
+                        for (int kh = 0; kh < KH; ++kh) {
+                            const int ry = ih + pad - kh;
+                            if (ry < 0 || ry % stride != 0 || ry / stride >= OH) continue;
+                            for (int kw = 0; kw < KW; ++kw) {
+                                const int rx = iw + pad - kw;
+                                if (rx < 0 || rx % stride != 0 || rx / stride >= OW) continue;
+                                s += (double)dy[(((int64_t)n * Cout + oc) * OH + ry / stride) * OW + rx / stride] *
+                                     (double)k[(((int64_t)oc * Cin + ci) * KH + kh) * KW + kw];
+                            }
+                        }
+                    float* o = &dx[(((int64_t)n * Cin + ci) * H + ih) * W + iw];
+                    *o += (float)s;
+                }
+}
+
+/* CVT2D (Engine/kernels.cu:1091-1135): transposed conv forward, assigned */
+void oracle_convT2d_fwd(const float* x, const float* w, const float* bias, float* y, int N, int Cout, int Cin, int H,
+                        int W, int KH, int KW, int pad, int stride) {
+    const int OH = (H - 1) * stride - 2 * pad + KH, OW = (W - 1) * stride - 2 * pad + KW;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int n = 0; n < N; ++n)
+        for (int oc = 0; oc < Cout; ++oc)
+            for (int row = 0; row < OH; ++row)
+                for (int col = 0; col < OW; ++col) {
+                    double s = 0.0;
+                    for (int ic = 0; ic < Cin; ++ic)
+                        for (int kh = 0; kh < KH; ++kh)
+                            for (int kw = 0; kw < KW; ++kw) {
+                                int r = row + pad - kh, c = col + pad - kw;
+                                if (r % stride != 0 || c % stride != 0) continue;
+                                r /= stride;
+                                c /= stride;
+                                if (r < 0 || r >= H || c < 0 || c >= W) continue;
+                                s += (double)x[(((int64_t)n * Cin + ic) * H + r) * W + c] *
+                                     (double)w[(((int64_t)oc * Cin + ic) * KH + kh) * KW + kw];
+                            }
+                    const float v = (float)s;
+                    y[(((int64_t)n * Cout + oc) * OH + row) * OW + col] = bias ? v + bias[oc] : v;
+                }
+}
+
+/* GVT2D (Engine/kernels.cu:1137-1176): transposed conv weight grad, assigned */
+void oracle_convT2d_bwd_w(const float* x, const float* gout, float* gw, int N, int Cout, int Cin, int H, int W, int KH,
+                          int KW, int pad, int stride) {
+    const int OH = (H - 1) * stride - 2 * pad + KH, OW = (W - 1) * stride - 2 * pad + KW;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int oc = 0; oc < Cout; ++oc)
+        for (int ic = 0; ic < Cin; ++ic)
+            for (int kh = 0; kh < KH; ++kh)
+                for (int kw = 0; kw < KW; ++kw) {
+                    double s = 0.0;
+                    for (int n = 0; n < N; ++n)
+                        for (int r = 0; r < H; ++r)
+                            for (int c = 0; c < W; ++c) {
+                                const int orow = r * stride - pad + kh, ocol = c * stride - pad + kw;
+                                if (orow < 0 || orow >= OH || ocol < 0 || ocol >= OW) continue;
+                                s += (double)x[(((int64_t)n * Cin + ic) * H + r) * W + c] *
+                                     (double)gout[(((int64_t)n * Cout + oc) * OH + orow) * OW + ocol];
+                            }
+                    gw[(((int64_t)oc * Cin + ic) * KH + kh) * KW + kw] = (float)s;
+                }
+}
+
+/* CVT2D_GradInput (Engine/kernels.cu:1178-1212): assigned */
+void oracle_convT2d_bwd_x(const float* gout, const float* w, float* gx, int N, int Cout, int Cin, int H, int W,
+                          int KH, int KW, int pad, int stride) {
+    const int OH = (H - 1) * stride - 2 * pad + KH, OW = (W - 1) * stride - 2 * pad + KW;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int n = 0; n < N; ++n)
+        for (int ic = 0; ic < Cin; ++ic)
+            for (int r = 0; r < H; ++r)
+                for (int c = 0; c < W; ++c) {
+                    double s = 0.0;
+                    for (int oc = 0; oc < Cout; ++oc)
+                        for (int kh = 0; kh < KH; ++kh)
+                            for (int kw = 0; kw < KW; ++kw) {
+                                const int orow = r * stride - pad + kh, ocol = c * stride - pad + kw;
+                                if (orow < 0 || orow >= OH || ocol < 0 || ocol >= OW) continue;
+                                s += (double)gout[(((int64_t)n * Cout + oc) * OH + orow) * OW + ocol] *
+                                     (double)w[(((int64_t)oc * Cin + ic) * KH + kh) * KW + kw];
+                            }
+                    gx[(((int64_t)n * Cin + ic) * H + r) * W + c] = (float)s;
+                }
+}

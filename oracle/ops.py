@@ -21,6 +21,12 @@ L = ctypes.c_int64
 P = ctypes.c_void_p
 
 _SIGS = {
+    "oracle_conv2d_fwd": (None, [P, P, P, P, I, I, I, I, I, I, I, I, I]),
+    "oracle_conv2d_bwd_k": (None, [P, P, P, I, I, I, I, I, I, I, I, I]),
+    "oracle_conv2d_bwd_x": (None, [P, P, P, I, I, I, I, I, I, I, I, I]),
+    "oracle_convT2d_fwd": (None, [P, P, P, P, I, I, I, I, I, I, I, I, I]),
+    "oracle_convT2d_bwd_w": (None, [P, P, P, I, I, I, I, I, I, I, I, I]),
+    "oracle_convT2d_bwd_x": (None, [P, P, P, I, I, I, I, I, I, I, I, I]),
     "oracle_act_fwd": (None, [I, P, P, L]),
     "oracle_act_bwd": (None, [I, P, P, P, L]),
     "oracle_accumulate": (None, [P, P, L, D]),
@@ -276,3 +282,58 @@ def clip_apply(g, acc):
 def adam(w, g, m, v, t, lr, adamw=True, b1=0.9, b2=0.999, eps=1e-8, wd=0.01):
     lib().oracle_adam(_p(w), _p(f32(g)), _p(m), _p(v), w.size, t, b1, b2, eps, wd, lr, int(adamw))
     return w, m, v
+
+
+def _cgeom(x, k):
+    N, Cin, H, W = x.shape
+    Cout, _, KH, KW = k.shape
+    return N, Cout, Cin, H, W, KH, KW
+
+
+def conv2d_fwd(x, k, bias, pad, stride):
+    N, Cout, Cin, H, W, KH, KW = _cgeom(x, k)
+    OH, OW = (2 * pad + H - KH) // stride + 1, (2 * pad + W - KW) // stride + 1
+    y = np.zeros((N, Cout, OH, OW), np.float32)
+    lib().oracle_conv2d_fwd(_p(f32(x)), _p(f32(k)), _p(None if bias is None else f32(bias)), _p(y), N, Cout, Cin, H,
+                            W, KH, KW, pad, stride)
+    return y
+
+
+def conv2d_bwd_k(x, dz, kshape, pad, stride):
+    Cout, Cin, KH, KW = kshape
+    N, _, H, W = x.shape
+    dk = np.zeros(kshape, np.float32)
+    lib().oracle_conv2d_bwd_k(_p(f32(x)), _p(f32(dz)), _p(dk), N, Cout, Cin, H, W, KH, KW, pad, stride)
+    return dk
+
+
+def conv2d_bwd_x(dy, k, dx, pad, stride):
+    N, Cin, H, W = dx.shape
+    Cout, _, KH, KW = k.shape
+    lib().oracle_conv2d_bwd_x(_p(f32(dy)), _p(f32(k)), _p(dx), N, Cout, Cin, H, W, KH, KW, pad, stride)
+    return dx
+
+
+def convT2d_fwd(x, w, bias, pad, stride):
+    N, Cout, Cin, H, W, KH, KW = _cgeom(x, w)
+    OH, OW = (H - 1) * stride - 2 * pad + KH, (W - 1) * stride - 2 * pad + KW
+    y = np.zeros((N, Cout, OH, OW), np.float32)
+    lib().oracle_convT2d_fwd(_p(f32(x)), _p(f32(w)), _p(None if bias is None else f32(bias)), _p(y), N, Cout, Cin,
+                             H, W, KH, KW, pad, stride)
+    return y
+
+
+def convT2d_bwd_w(x, gout, wshape, pad, stride):
+    Cout, Cin, KH, KW = wshape
+    N, _, H, W = x.shape
+    gw = np.zeros(wshape, np.float32)
+    lib().oracle_convT2d_bwd_w(_p(f32(x)), _p(f32(gout)), _p(gw), N, Cout, Cin, H, W, KH, KW, pad, stride)
+    return gw
+
+
+def convT2d_bwd_x(gout, w, xshape, pad, stride):
+    N, Cin, H, W = xshape
+    Cout, _, KH, KW = w.shape
+    gx = np.zeros(xshape, np.float32)
+    lib().oracle_convT2d_bwd_x(_p(f32(gout)), _p(f32(w)), _p(gx), N, Cout, Cin, H, W, KH, KW, pad, stride)
+    return gx

@@ -40,6 +40,12 @@ _SIGS = {
     "ref_clip_finalize": [P],
     "ref_clip_apply": [P, P, L],
     "ref_adam": [P, P, I, I, P, P, F, F, F, F, F, I],
+    "ref_conv2d_fwd": [P, P, P, P, I, I, I, I, I, I, I, I, I],
+    "ref_conv2d_bwd_k": [P, P, P, I, I, I, I, I, I, I, I, I],
+    "ref_conv2d_bwd_x": [P, P, P, I, I, I, I, I, I, I, I, I],
+    "ref_convT2d_fwd": [P, P, P, P, I, I, I, I, I, I, I, I, I],
+    "ref_convT2d_bwd_w": [P, P, P, I, I, I, I, I, I, I, I, I],
+    "ref_convT2d_bwd_x": [P, P, P, I, I, I, I, I, I, I, I, I],
     "ref_sync": [],
 }
 

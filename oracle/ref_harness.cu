@@ -241,4 +241,56 @@ int ref_adam(float* w, const float* g, int n, int t, float* m, float* v, float b
 
 int ref_sync(void) { return (int)cudaDeviceSynchronize(); }
 
+
+/* Convolute2D / Convolute2DT kernels with the launch shapes of their
+ * lambdas (Engine/engine.cu:3751-3773, 3850-3874). */
+int ref_conv2d_fwd(const float* x, const float* k, const float* bias, float* y, int n, int cout, int cin, int h, int w,
+                   int kh, int kw, int pad, int stride) {
+    const int oh = (2 * pad + h - kh) / stride + 1, ow = (2 * pad + w - kw) / stride + 1;
+    dim3 block(8, 8, 16);
+    dim3 grid((ow + block.x - 1) / block.x, (oh + block.y - 1) / block.y, (n * cout + block.z - 1) / block.z);
+    CV2D<<<grid, block>>>(x, k, bias, y, n, cout, cin, h, w, kh, kw, pad, stride);
+    return (int)cudaGetLastError();
+}
+
+int ref_conv2d_bwd_k(const float* x, const float* dz, float* dk, int n, int cout, int cin, int h, int w, int kh,
+                     int kw, int pad, int stride) {
+    dim3 block(16, 16, 4);
+    dim3 grid((cout + block.x - 1) / block.x, (cin + block.y - 1) / block.y, (kh * kw + block.z - 1) / block.z);
+    GV2D<<<grid, block>>>(x, dz, dk, n, cout, cin, h, w, kh, kw, pad, stride);
+    return (int)cudaGetLastError();
+}
+
+int ref_conv2d_bwd_x(const float* dy, const float* k, float* dx, int n, int cout, int cin, int h, int w, int kh,
+                     int kw, int pad, int stride) {
+    const int oh = (2 * pad + h - kh) / stride + 1, ow = (2 * pad + w - kw) / stride + 1;
+    dim3 block(8, 8, 16);
+    dim3 grid((w + block.x - 1) / block.x, (h + block.y - 1) / block.y, (n * cin + block.z - 1) / block.z);
+    CV2D_GradInput<<<grid, block>>>(dy, k, dx, n, cout, cin, h, w, kh, kw, oh, ow, pad, stride);
+    return (int)cudaGetLastError();
+}
+
+int ref_convT2d_fwd(const float* x, const float* wt, const float* bias, float* y, int n, int cout, int cin, int h,
+                    int w, int kh, int kw, int pad, int stride) {
+    const int oh = (h - 1) * stride - 2 * pad + kh, ow = (w - 1) * stride - 2 * pad + kw;
+    dim3 block(8, 8, 16);
+    dim3 grid((ow + block.x - 1) / block.x, (oh + block.y - 1) / block.y, (n * cout + block.z - 1) / block.z);
+    CVT2D<<<grid, block>>>(x, wt, bias, y, n, cout, cin, h, w, kh, kw, pad, stride);
+    return (int)cudaGetLastError();
+}
+
+int ref_convT2d_bwd_w(const float* x, const float* gout, float* gw, int n, int cout, int cin, int h, int w, int kh,
+                      int kw, int pad, int stride) {
+    GVT2D<<<cout, THREADSPERBLOCK>>>(x, gout, gw, n, cout, cin, h, w, kh, kw, pad, stride);
+    return (int)cudaGetLastError();
+}
+
+int ref_convT2d_bwd_x(const float* gout, const float* wt, float* gx, int n, int cout, int cin, int h, int w, int kh,
+                      int kw, int pad, int stride) {
+    dim3 block(8, 8, 16);
+    dim3 grid((w + block.x - 1) / block.x, (h + block.y - 1) / block.y, (n * cin + block.z - 1) / block.z);
+    CVT2D_GradInput<<<grid, block>>>(gout, wt, gx, n, cout, cin, h, w, kh, kw, pad, stride);
+    return (int)cudaGetLastError();
+}
+
 }  // extern "C"

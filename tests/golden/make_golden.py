@@ -214,11 +214,50 @@ def linear_cases(rng):
                 dims=np.array([batch, ch, m, n, p], np.int64))
 
 
+def conv_cases(rng):
+    """CV2D / GV2D / CV2D_GradInput and CVT2D / GVT2D / CVT2D_GradInput with
+    the reference lambdas' launch shapes, small enough for the CPU oracle."""
+    out = {}
+    convs = [(2, 3, 9, 7, 4, 3, 1, 1), (2, 4, 9, 10, 3, 3, 1, 2), (1, 5, 6, 6, 2, 1, 0, 1)]
+    for i, (N, Cin, Hh, W, Cout, K, pad, s) in enumerate(convs):
+        OH, OW = (2 * pad + Hh - K) // s + 1, (2 * pad + W - K) // s + 1
+        x = rng.standard_normal((N, Cin, Hh, W)).astype(np.float32)
+        w = rng.standard_normal((Cout, Cin, K, K)).astype(np.float32)
+        b = rng.standard_normal(Cout).astype(np.float32)
+        dy = rng.standard_normal((N, Cout, OH, OW)).astype(np.float32)
+        dx0 = rng.standard_normal(x.shape).astype(np.float32)
+        y, dk, dx = torch.empty(N, Cout, OH, OW, device=DEV), torch.empty(w.shape, device=DEV), T(dx0)
+        ref.call("ref_conv2d_fwd", ref.ptr(T(x)), ref.ptr(T(w)), ref.ptr(T(b)), ref.ptr(y), N, Cout, Cin, Hh, W, K, K,
+                 pad, s)
+        ref.call("ref_conv2d_bwd_k", ref.ptr(T(x)), ref.ptr(T(dy)), ref.ptr(dk), N, Cout, Cin, Hh, W, K, K, pad, s)
+        ref.call("ref_conv2d_bwd_x", ref.ptr(T(dy)), ref.ptr(T(w)), ref.ptr(dx), N, Cout, Cin, Hh, W, K, K, pad, s)
+        out.update({f"c{i}_args": np.array([N, Cin, Hh, W, Cout, K, pad, s], np.int64), f"c{i}_x": x, f"c{i}_w": w,
+                    f"c{i}_b": b, f"c{i}_dy": dy, f"c{i}_dx0": dx0, f"c{i}_y": H(y), f"c{i}_dk": H(dk),
+                    f"c{i}_dx": H(dx)})
+    convts = [(2, 4, 4, 5, 3, 2, 0, 2), (1, 3, 5, 4, 2, 3, 1, 2), (2, 2, 6, 6, 3, 3, 1, 1)]
+    for i, (N, Cin, Hh, W, Cout, K, pad, s) in enumerate(convts):
+        OH, OW = (Hh - 1) * s - 2 * pad + K, (W - 1) * s - 2 * pad + K
+        x = rng.standard_normal((N, Cin, Hh, W)).astype(np.float32)
+        w = rng.standard_normal((Cout, Cin, K, K)).astype(np.float32)
+        b = rng.standard_normal(Cout).astype(np.float32)
+        dy = rng.standard_normal((N, Cout, OH, OW)).astype(np.float32)
+        y, gw, gx = torch.empty(N, Cout, OH, OW, device=DEV), torch.empty(w.shape, device=DEV), torch.empty(x.shape,
+                                                                                                          device=DEV)
+        ref.call("ref_convT2d_fwd", ref.ptr(T(x)), ref.ptr(T(w)), ref.ptr(T(b)), ref.ptr(y), N, Cout, Cin, Hh, W, K,
+                 K, pad, s)
+        ref.call("ref_convT2d_bwd_w", ref.ptr(T(x)), ref.ptr(T(dy)), ref.ptr(gw), N, Cout, Cin, Hh, W, K, K, pad, s)
+        ref.call("ref_convT2d_bwd_x", ref.ptr(T(dy)), ref.ptr(T(w)), ref.ptr(gx), N, Cout, Cin, Hh, W, K, K, pad, s)
+        out.update({f"t{i}_args": np.array([N, Cin, Hh, W, Cout, K, pad, s], np.int64), f"t{i}_x": x, f"t{i}_w": w,
+                    f"t{i}_b": b, f"t{i}_dy": dy, f"t{i}_y": H(y), f"t{i}_gw": H(gw), f"t{i}_gx": H(gx)})
+    return out
+
+
 def main(outdir: Path):
     outdir.mkdir(parents=True, exist_ok=True)
     rng = np.random.default_rng(20261201)
     for name, fn in [("bcmm", bcmm_cases), ("act", act_cases), ("norm", norm_cases), ("softmax", softmax_cases),
-                     ("loss", loss_cases), ("optim", optim_cases), ("glue", glue_cases), ("linear", linear_cases)]:
+                     ("loss", loss_cases), ("optim", optim_cases), ("glue", glue_cases), ("linear", linear_cases),
+                     ("conv", conv_cases)]:
         data = fn(rng)
         np.savez_compressed(outdir / f"ref_{name}.npz", **data)
         print("wrote", outdir / f"ref_{name}.npz")

@@ -1,0 +1,151 @@
+"""Convolute2D / Convolute2DT on the tensor-core GEMM against the CPU
+oracle's restatement of CV2D, GV2D, CV2D_GradInput, CVT2D, GVT2D and
+CVT2D_GradInput (and, where oracle/_ref is built, the reference kernels
+themselves).  TF32 products: <= 2e-3 normwise per tensor; fp32 GEMM mode:
+<= 1e-5 normwise."""
+import numpy as np
+import pytest
+
+from conftest import RTOL_EXACT, RTOL_TC, norm_err
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+CONV = [  # N, Cin, H, W, Cout, K, pad, stride
+    (2, 3, 16, 16, 8, 3, 1, 1),      # first layer of a U-Net: K = 27 (CUDA-core GEMM)
+    (4, 16, 32, 32, 32, 3, 1, 1),    # 3x3, tensor cores
+    (2, 32, 17, 13, 16, 3, 1, 2),    # stride-2 downsampling, odd sizes
+    (2, 64, 8, 8, 32, 1, 0, 1),      # 1x1 skip projection
+]
+CONVT = [  # N, Cin, H, W, Cout, K, pad, stride
+    (2, 32, 8, 8, 16, 2, 0, 2),      # 2x2 stride-2 upsampling
+    (2, 16, 7, 9, 8, 3, 1, 2),
+    (2, 8, 10, 10, 8, 3, 1, 1),
+]
+
+
+def T(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def H(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+@pytest.fixture(params=[0, 1], ids=["tf32", "fp32"])
+def gemm_mode(request):
+    from ml_engine_b200._lib import kernels
+    k = kernels()
+    old = k.mle_get_gemm_mode()
+    k.mle_set_gemm_mode(request.param)
+    yield request.param
+    k.mle_set_gemm_mode(old)
+
+
+@pytest.mark.parametrize("case", CONV)
+def test_conv2d(cuda, rng, gemm_mode, case):
+    from ml_engine_b200 import ops
+    from oracle import ops as orc
+    N, Cin, Hh, W, Cout, K, pad, stride = case
+    x = rng.standard_normal((N, Cin, Hh, W)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, K, K)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(Cout).astype(np.float32)
+    OH, OW = ops.conv_out_size(Hh, K, pad, stride), ops.conv_out_size(W, K, pad, stride)
+    dy = rng.standard_normal((N, Cout, OH, OW)).astype(np.float32)
+    dx0 = rng.standard_normal(x.shape).astype(np.float32)
+    db0 = rng.standard_normal(Cout).astype(np.float32)
+    tx, tw, tb = T(x, cuda), T(w, cuda), T(b, cuda)
+    y = torch.empty(N, Cout, OH, OW, device=cuda)
+    ws = ops.conv2d_workspace(tx, tw, pad, stride)
+    ops.conv2d_fwd(tx, tw, tb, y, ws, pad, stride)
+    dx, dw, db = T(dx0, cuda), torch.full((Cout, Cin, K, K), 7.0, device=cuda), T(db0, cuda)
+    ops.conv2d_bwd(tw, T(dy, cuda), dx, dw, db, ws, x.shape, pad, stride)
+    tol = RTOL_TC if gemm_mode == 0 else 1e-5
+    assert norm_err(H(y), orc.conv2d_fwd(x, w, b, pad, stride)) <= tol
+    assert norm_err(H(dw), orc.conv2d_bwd_k(x, dy, w.shape, pad, stride)) <= tol      # assigned
+    assert norm_err(H(dx) - dx0, orc.conv2d_bwd_x(dy, w, np.zeros_like(x), pad, stride)) <= tol
+    rdb = db0.copy()
+    orc.channel_bias_bwd(dy, None, rdb, N, Cout, OH * OW)
+    assert norm_err(H(db), rdb) <= 1e-5
+
+
+@pytest.mark.parametrize("case", CONVT)
+def test_convT2d(cuda, rng, gemm_mode, case):
+    from ml_engine_b200 import ops
+    from oracle import ops as orc
+    N, Cin, Hh, W, Cout, K, pad, stride = case
+    x = rng.standard_normal((N, Cin, Hh, W)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, K, K)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(Cout).astype(np.float32)
+    OH, OW = ops.convT_out_size(Hh, K, pad, stride), ops.convT_out_size(W, K, pad, stride)
+    dy = rng.standard_normal((N, Cout, OH, OW)).astype(np.float32)
+    tx, tw = T(x, cuda), T(w, cuda)
+    y = torch.empty(N, Cout, OH, OW, device=cuda)
+    ws = ops.convT2d_workspace(tx, tw, pad, stride)
+    ops.convT2d_fwd(tx, tw, T(b, cuda), y, ws, pad, stride)
+    dx = torch.full(x.shape, 3.0, device=cuda)
+    dw = torch.full(w.shape, 5.0, device=cuda)
+    db = torch.zeros(Cout, device=cuda)
+    ops.convT2d_bwd(tx, tw, T(dy, cuda), dx, dw, db, ws, pad, stride)
+    tol = RTOL_TC if gemm_mode == 0 else 1e-5
+    assert norm_err(H(y), orc.convT2d_fwd(x, w, b, pad, stride)) <= tol
+    assert norm_err(H(dw), orc.convT2d_bwd_w(x, dy, w.shape, pad, stride)) <= tol     # assigned
+    assert norm_err(H(dx), orc.convT2d_bwd_x(dy, w, x.shape, pad, stride)) <= tol     # assigned
+    rdb = np.zeros(Cout, np.float32)
+    orc.channel_bias_bwd(dy, None, rdb, N, Cout, OH * OW)
+    assert norm_err(H(db), rdb) <= 1e-5
+
+
+@pytest.mark.parametrize("case", CONV[1:3])
+def test_conv2d_reference_kernels(cuda, rng, case):
+    """Oracle vs the reference's own CV2D / GV2D / CV2D_GradInput."""
+    from oracle import ops as orc
+    from oracle import ref
+    if not ref.available():
+        pytest.skip("oracle/_ref not built")
+    N, Cin, Hh, W, Cout, K, pad, stride = case
+    x = rng.standard_normal((N, Cin, Hh, W)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, K, K)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(Cout).astype(np.float32)
+    OH, OW = (2 * pad + Hh - K) // stride + 1, (2 * pad + W - K) // stride + 1
+    dy = rng.standard_normal((N, Cout, OH, OW)).astype(np.float32)
+    y = torch.empty(N, Cout, OH, OW, device=cuda)
+    ref.call("ref_conv2d_fwd", ref.ptr(T(x, cuda)), ref.ptr(T(w, cuda)), ref.ptr(T(b, cuda)), ref.ptr(y), N, Cout,
+             Cin, Hh, W, K, K, pad, stride)
+    dk = torch.empty(w.shape, device=cuda)
+    ref.call("ref_conv2d_bwd_k", ref.ptr(T(x, cuda)), ref.ptr(T(dy, cuda)), ref.ptr(dk), N, Cout, Cin, Hh, W, K, K,
+             pad, stride)
+    dx = torch.zeros(x.shape, device=cuda)
+    ref.call("ref_conv2d_bwd_x", ref.ptr(T(dy, cuda)), ref.ptr(T(w, cuda)), ref.ptr(dx), N, Cout, Cin, Hh, W, K, K,
+             pad, stride)
+    assert norm_err(H(y), orc.conv2d_fwd(x, w, b, pad, stride)) <= RTOL_EXACT
+    assert norm_err(H(dk), orc.conv2d_bwd_k(x, dy, w.shape, pad, stride)) <= RTOL_EXACT
+    assert norm_err(H(dx), orc.conv2d_bwd_x(dy, w, np.zeros_like(x), pad, stride)) <= RTOL_EXACT
+
+
+@pytest.mark.parametrize("case", CONVT[:2])
+def test_convT2d_reference_kernels(cuda, rng, case):
+    """Oracle vs the reference's own CVT2D / GVT2D / CVT2D_GradInput."""
+    from oracle import ops as orc
+    from oracle import ref
+    if not ref.available():
+        pytest.skip("oracle/_ref not built")
+    N, Cin, Hh, W, Cout, K, pad, stride = case
+    x = rng.standard_normal((N, Cin, Hh, W)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, K, K)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(Cout).astype(np.float32)
+    OH, OW = (Hh - 1) * stride - 2 * pad + K, (W - 1) * stride - 2 * pad + K
+    dy = rng.standard_normal((N, Cout, OH, OW)).astype(np.float32)
+    y = torch.empty(N, Cout, OH, OW, device=cuda)
+    ref.call("ref_convT2d_fwd", ref.ptr(T(x, cuda)), ref.ptr(T(w, cuda)), ref.ptr(T(b, cuda)), ref.ptr(y), N, Cout,
+             Cin, Hh, W, K, K, pad, stride)
+    gw = torch.empty(w.shape, device=cuda)
+    ref.call("ref_convT2d_bwd_w", ref.ptr(T(x, cuda)), ref.ptr(T(dy, cuda)), ref.ptr(gw), N, Cout, Cin, Hh, W, K, K,
+             pad, stride)
+    gx = torch.empty(x.shape, device=cuda)
+    ref.call("ref_convT2d_bwd_x", ref.ptr(T(dy, cuda)), ref.ptr(T(w, cuda)), ref.ptr(gx), N, Cout, Cin, Hh, W, K, K,
+             pad, stride)
+    assert norm_err(H(y), orc.convT2d_fwd(x, w, b, pad, stride)) <= RTOL_EXACT
+    assert norm_err(H(gw), orc.convT2d_bwd_w(x, dy, w.shape, pad, stride)) <= RTOL_EXACT
+    assert norm_err(H(gx), orc.convT2d_bwd_x(dy, w, x.shape, pad, stride)) <= RTOL_EXACT

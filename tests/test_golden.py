@@ -119,3 +119,19 @@ def test_golden_linear():
     orc.gemm(d["X"], d["dY"], dw, n, p, rows, 1, 0)
     assert rel_err(dw, d["dW"].reshape(n, p)) <= RTOL_EXACT
     assert rel_err(orc.bias_grad(d["dY"], np.zeros(p, np.float32)), d["dB"]) <= RTOL_EXACT
+
+
+def test_golden_conv():
+    d = load("conv")
+    for i in range(3):
+        N, Cin, Hh, W, Cout, K, pad, s = (int(v) for v in d[f"c{i}_args"])
+        x, w, b, dy = d[f"c{i}_x"], d[f"c{i}_w"], d[f"c{i}_b"], d[f"c{i}_dy"]
+        assert rel_err(orc.conv2d_fwd(x, w, b, pad, s), d[f"c{i}_y"]) <= RTOL_EXACT
+        assert rel_err(orc.conv2d_bwd_k(x, dy, w.shape, pad, s), d[f"c{i}_dk"]) <= RTOL_EXACT
+        assert rel_err(orc.conv2d_bwd_x(dy, w, d[f"c{i}_dx0"].copy(), pad, s), d[f"c{i}_dx"]) <= RTOL_EXACT
+    for i in range(3):
+        N, Cin, Hh, W, Cout, K, pad, s = (int(v) for v in d[f"t{i}_args"])
+        x, w, b, dy = d[f"t{i}_x"], d[f"t{i}_w"], d[f"t{i}_b"], d[f"t{i}_dy"]
+        assert rel_err(orc.convT2d_fwd(x, w, b, pad, s), d[f"t{i}_y"]) <= RTOL_EXACT
+        assert rel_err(orc.convT2d_bwd_w(x, dy, w.shape, pad, s), d[f"t{i}_gw"]) <= RTOL_EXACT
+        assert rel_err(orc.convT2d_bwd_x(dy, w, x.shape, pad, s), d[f"t{i}_gx"]) <= RTOL_EXACT
