@@ -224,6 +224,80 @@ def roofline_pair(dev, stream, reps=50):
     return k0.elapsed_time(k1) / reps, 2 * 2.0 * M * K * N
 
 
+# ------------------------------------------------------------ kernel sweep
+def run_sweep(args):
+    """linear backward (dX = dY W^T, dW = X^T dY) at M=N=K = n,
+    LayerNorm backward over 65536 rows of width w, and the fused clip +
+    AdamW over 256 tensors totalling 1e8 parameters.  One JSON line per
+    case with achieved FLOP/s or bytes/s against the measured peaks (CUDA
+    events around `reps` launches, after warm-up; inputs larger than L2
+    except the two smallest GEMMs)."""
+    import numpy as np
+    import torch
+
+    from ml_engine_b200 import ops
+    dev = torch.device("cuda", 0)
+    hbm_peak, bf16_peak, kind = load_peaks()
+    tf32_peak = bf16_peak / 2
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    for n in (512, 1024, 2048, 4096, 8192):
+        X = torch.randn(n, n, device=dev, generator=g)
+        W = torch.randn(n, n, device=dev, generator=g)
+        dY = torch.randn(n, n, device=dev, generator=g)
+        dX, dW = torch.zeros(n, n, device=dev), torch.zeros(n, n, device=dev)
+        ms = timed(lambda: ops.linear_bwd(X, W, dY, dX, dW, None, n, n, n), 20 if n >= 4096 else 100)
+        tf = 4.0 * n ** 3 / (ms * 1e-3) / 1e12
+        print(json.dumps({"sweep": "linear_bwd", "n": n, "ms": ms, "tflops": tf, "frac_of_tf32": tf / tf32_peak,
+                          "frac_of_bf16": tf / bf16_peak, "peak_kind": kind}), flush=True)
+        del X, W, dY, dX, dW
+    rows = 65536
+    for w in (1024, 2048, 4096, 8192):
+        x = torch.randn(rows * w, device=dev, generator=g)
+        y, mean, sq = torch.empty_like(x), torch.empty(rows, device=dev), torch.empty(rows, device=dev)
+        ops.layernorm_fwd(x, y, mean, sq, rows, 1, 1, w)
+        gy, gx = torch.randn_like(x), torch.zeros_like(x)
+        ms = timed(lambda: ops.layernorm_bwd(y, gy, sq, gx, rows, 1, 1, w), 20)
+        gbs = 16.0 * rows * w / (ms * 1e-3) / 1e9   # y, gy, gx read; gx written
+        print(json.dumps({"sweep": "layernorm_bwd", "rows": rows, "width": w, "ms": ms, "gbs": gbs,
+                          "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
+        del x, y, gy, gx
+    total, nt = 100_000_000, 256
+    sizes = np.random.default_rng(0).integers(1, 1000, nt).astype(np.float64)
+    sizes = np.maximum(1, (sizes / sizes.sum() * total).astype(np.int64))
+    params = []
+    for sz in sizes:
+        params.append(dict(w=torch.randn(int(sz), device=dev, generator=g) * 0.02,
+                           g=torch.randn(int(sz), device=dev, generator=g) * 1e-2,
+                           m=torch.zeros(int(sz), device=dev), v=torch.zeros(int(sz), device=dev),
+                           t=torch.ones(1, dtype=torch.int32, device=dev)))
+    ws = torch.zeros(1, dtype=torch.float64, device=dev)
+    views = ops.param_views(params)   # built once, as the engine's optimizer does
+
+    def clip_adam():
+        ws.zero_()
+        ops.grad_sumsq(views, ws)
+        ops.clip_finalize(ws, 1.0)
+        ops.adam_update(views, lr=1e-3, adamw=True, clip_ws=ws, write_back_grad=False)
+    ms = timed(clip_adam, 10)
+    nparam = int(sizes.sum())
+    gbs = 32.0 * nparam / (ms * 1e-3) / 1e9   # g read (norm); w, g, m, v read; w, m, v written
+    print(json.dumps({"sweep": "clip_adamw", "params": nparam, "tensors": nt, "ms": ms, "gbs": gbs,
+                      "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
+
+
 # ------------------------------------------------------------ native arm
 def run_native(args, rank, world, local_rank):
     import numpy as np
@@ -337,9 +411,13 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="configs[4] kernel sweep, one JSON line per case")
     ap.add_argument("--roofline-only", action="store_true",
                     help="run only the roofline kernel pair (3 + 2 pairs; for a profiler capture)")
     args = ap.parse_args()
+    if args.sweep:
+        run_sweep(args)
+        return
     if args.roofline_only:
         import torch
         dev = torch.device("cuda", 0)

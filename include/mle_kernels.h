@@ -328,7 +328,8 @@ enum mle_attn_layout { MLE_ATTN_HEAD_MAJOR = 0, MLE_ATTN_TOKEN_MAJOR = 1 };
  * wise softmax (axis 1) runs as two fused kernels (P by key blocks, O by
  * query blocks) whose sums follow the reference kernels' order, so P and O
  * are bitwise the reference's; other shapes run the composed path
- * (head-major only).  Q, K, V must be 16-byte aligned for the fused path. */
+ * (head-major only).  Q, K, V, O (and, backward, dO, dQ, dK, dV) must be
+ * 16-byte aligned for the fused path. */
 int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, float* O,
                       int batch, int heads, int seq_q, int seq_k, int head_dim, float scale,
                       int causal, int softmax_axis, int layout, mle_stream_t stream);

@@ -61,63 +61,86 @@ inline void strides_for(int layout, int H, int S, int hd, int64_t& sb, int64_t& 
     }
 }
 
-// rows [0, rows) of a [*, HD] operand (row stride rs) into padded shared
-// rows of HD + 1 floats; rows >= valid are zero-filled
+// Shared-memory tiles are row-major with rows padded to a multiple of four
+// floats plus four (so every row starts 16-byte aligned and consecutive rows
+// start four banks apart): operand products read 128-bit vectors along the
+// contiguous axis.
+template <int HD>
+__host__ __device__ constexpr int hd_pitch() { return HD + 4; }
+constexpr int kColPitch = kTC + 4;
+__host__ __device__ inline int seq_pitch(int S) { return ((S + 3) & ~3) + 4; }
+
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float f4(const float4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// rows [0, rows) of a [*, HD] operand (row stride rs) into shared rows of
+// hd_pitch<HD>() floats; rows >= valid are zero-filled
 template <int HD>
 __device__ __forceinline__ void load_rows(float* dst, const float* __restrict__ src, int rows, int valid, int64_t rs) {
+    constexpr int P = hd_pitch<HD>();
     for (int i = threadIdx.x; i < rows * (HD / 4); i += kNT) {
         const int r = i / (HD / 4), d4 = (i % (HD / 4)) * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (r < valid) v = *reinterpret_cast<const float4*>(src + (int64_t)r * rs + d4);
-        float* o = dst + r * (HD + 1) + d4;
-        o[0] = v.x;
-        o[1] = v.y;
-        o[2] = v.z;
-        o[3] = v.w;
+        *reinterpret_cast<float4*>(dst + r * P + d4) = v;
     }
 }
 
 // [rows, kTC] tile of a head's [Sq, Sk] matrix (column offset c0) into
-// shared rows of kTC + 1 floats, zero beyond Sk
+// shared rows of kColPitch floats, zero beyond Sk
 __device__ __forceinline__ void load_col_tile(float* dst, const float* __restrict__ src, int rows, int Sk, int c0) {
     for (int i = threadIdx.x; i < rows * kTC; i += kNT) {
         const int r = i / kTC, c = i % kTC;
-        dst[r * (kTC + 1) + c] = (c0 + c < Sk) ? src[(int64_t)r * Sk + c0 + c] : 0.f;
+        dst[r * kColPitch + c] = (c0 + c < Sk) ? src[(int64_t)r * Sk + c0 + c] : 0.f;
+    }
+}
+
+// [kTR, Sk] rows r0.. of a head's [Sq, Sk] matrix into shared rows of
+// seq_pitch(Sk) floats, zero beyond Sk and below the tr valid rows
+__device__ __forceinline__ void load_row_tile(float* dst, const float* __restrict__ src, int tr, int Sk) {
+    const int ld = seq_pitch(Sk), w = ld - 4;
+    for (int i = threadIdx.x; i < kTR * w; i += kNT) {
+        const int r = i / w, c = i % w;
+        dst[r * ld + c] = (r < tr && c < Sk) ? src[(int64_t)r * Sk + c] : 0.f;
     }
 }
 
 // Register-tiled products.  Every output is one FMA chain over its
 // reduction index in ascending order (the reference kernels' order); a
-// thread keeps several such chains so each shared-memory load feeds more
-// than one FMA.
+// thread keeps several such chains, and zero-padded tails only add exact
+// zero products.
 
 // out[r][c] = sum_k A[r][k] * B[c][k] (k < HD) for every query row r < Sq
-// and the kTC columns c of a block (A: [Sq][HD+1], B: [kTC][HD+1]).
-// Thread: columns c = t%8 + 8j, rows r = t/8 + 32i (4 x 4 chains per pass
-// of 128 rows).
+// and the kTC columns c of a block (A: [Sq] rows, B: [kTC] rows, both of
+// hd_pitch).  Thread: columns c = t%8 + 8j, rows r = t/8 + 32i (4 x 4
+// chains per pass of 128 rows); k advances four at a time with 128-bit
+// loads.
 template <int HD, typename Epi>
 __device__ __forceinline__ void rows_times_cols(const float* As, const float* Bs, int Sq, Epi&& epi) {
+    constexpr int P = hd_pitch<HD>();
     const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;
     for (int rb = 0; rb < Sq; rb += 128) {
         float acc[4][4];
         int ra[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            ra[i] = min(rb + ty + 32 * i, Sq - 1) * (HD + 1);
+            ra[i] = min(rb + ty + 32 * i, Sq - 1) * P;
 #pragma unroll
             for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
         }
-#pragma unroll 8
-        for (int k = 0; k < HD; ++k) {
-            float a[4], b[4];
+#pragma unroll 2
+        for (int k = 0; k < HD; k += 4) {
+            float4 a[4], b[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = As[ra[i] + k];
+            for (int i = 0; i < 4; ++i) a[i] = lds4(As + ra[i] + k);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) b[j] = Bs[(tx + 8 * j) * (HD + 1) + k];
+            for (int j = 0; j < 4; ++j) b[j] = lds4(Bs + (tx + 8 * j) * P + k);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(f4(a[i], kk), f4(b[j], kk), acc[i][j]);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -131,83 +154,103 @@ __device__ __forceinline__ void rows_times_cols(const float* As, const float* Bs
 }
 
 // out[x][d] = sum_y M[y][x] * R[y][d] (y < ny) for the kTC columns x of a
-// block (M: [ny][kTC+1], R: [ny][HD+1]).  Thread: x = t%16 + 16i (i < 2),
-// d = t/16 + 16j (j < HD/16).
+// block (M: [ny] rows of kColPitch, R: [ny] rows of hd_pitch).  Thread:
+// XV consecutive x (one vector load of M) by DV d's, XV * DV = HD / 8.
 template <int HD, typename Epi>
 __device__ __forceinline__ void cols_t_times_rows(const float* Ms, const float* Rs, int ny, int nx, Epi&& epi) {
-    constexpr int JD = HD / 16;
-    const int tx = threadIdx.x & 15, td = threadIdx.x >> 4;
-    float acc[2][JD];
+    constexpr int P = hd_pitch<HD>();
+    constexpr int XV = HD >= 32 ? 4 : 2, DV = HD / 8 / XV;
+    constexpr int XG = kTC / XV;                       // x groups
+    const int xg = threadIdx.x % XG, dg = threadIdx.x / XG;
+    const int x0 = xg * XV;
+    float acc[XV][DV];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int u = 0; u < XV; ++u)
 #pragma unroll
-        for (int j = 0; j < JD; ++j) acc[i][j] = 0.f;
+        for (int v = 0; v < DV; ++v) acc[u][v] = 0.f;
 #pragma unroll 4
     for (int y = 0; y < ny; ++y) {
-        float m[2], r[JD];
+        float m[XV];
+        if (XV == 4) {
+            const float4 q = lds4(Ms + y * kColPitch + x0);
+            m[0] = q.x;
+            m[1] = q.y;
+            m[XV > 2 ? 2 : 0] = q.z;
+            m[XV > 3 ? 3 : 1] = q.w;
+        } else {
+            const float2 q = *reinterpret_cast<const float2*>(Ms + y * kColPitch + x0);
+            m[0] = q.x;
+            m[1] = q.y;
+        }
+        float r[DV];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) m[i] = Ms[y * (kTC + 1) + tx + 16 * i];
+        for (int v = 0; v < DV; ++v) r[v] = Rs[y * P + dg + (kNT / XG) * v];
 #pragma unroll
-        for (int j = 0; j < JD; ++j) r[j] = Rs[y * (HD + 1) + td + 16 * j];
+        for (int u = 0; u < XV; ++u)
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-            for (int j = 0; j < JD; ++j) acc[i][j] = fmaf(m[i], r[j], acc[i][j]);
+            for (int v = 0; v < DV; ++v) acc[u][v] = fmaf(m[u], r[v], acc[u][v]);
     }
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int x = tx + 16 * i;
+    for (int u = 0; u < XV; ++u) {
+        const int x = x0 + u;
         if (x < nx) {
 #pragma unroll
-            for (int j = 0; j < JD; ++j) epi(x, td + 16 * j, acc[i][j]);
+            for (int v = 0; v < DV; ++v) epi(x, dg + (kNT / XG) * v, acc[u][v]);
         }
     }
 }
 
 // out_p[r][d] = sum_c M[r][c] * R_p[c][d] (c < nc) for the kTR rows r of a
-// block and one or two right operands R_p ([nc][HD+1]); M: [kTR][ldm].
-// Thread: r = t%16 + 16i (i < kTR/16), d = t/16 + 16j (j < HD/16); results
-// land in shared tiles O_p[kTR][HD+1], which may overlay M (the block
-// synchronises before writing them).
+// block and one or two right operands R_p ([nc] rows of hd_pitch); M:
+// [kTR] rows of ldm (a multiple of 4).  Thread: four consecutive d (one
+// vector load of each R_p row) by RI rows; c advances four at a time (one
+// vector load of each M row).  Results land in shared tiles O_p [kTR] rows
+// of hd_pitch, which may overlay M (the block synchronises first).
 template <int HD, int NP>
 __device__ __forceinline__ void rows_times_rows(const float* Ms, int ldm, const float* R0, const float* R1, int nc,
                                                 float* O0, float* O1) {
-    constexpr int JD = HD / 16, IR = kTR / 16;
-    const int tr = threadIdx.x & 15, td = threadIdx.x >> 4;
-    float acc[NP][IR][JD];
+    constexpr int P = hd_pitch<HD>();
+    constexpr int DG = HD / 4, RG = kNT / DG, RI = kTR / RG;
+    const int dg = threadIdx.x % DG, rg = threadIdx.x / DG;
+    const int d0 = dg * 4;
+    float acc[NP][RI][4];
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
-        for (int i = 0; i < IR; ++i)
+        for (int i = 0; i < RI; ++i)
 #pragma unroll
-            for (int j = 0; j < JD; ++j) acc[p][i][j] = 0.f;
-#pragma unroll 2
-    for (int c = 0; c < nc; ++c) {
-        float m[IR], r0[JD], r1[JD];
+            for (int v = 0; v < 4; ++v) acc[p][i][v] = 0.f;
+    const int nc4 = (nc + 3) & ~3;
+#pragma unroll 1
+    for (int c = 0; c < nc4; c += 4) {
+        float4 m[RI];
 #pragma unroll
-        for (int i = 0; i < IR; ++i) m[i] = Ms[(tr + 16 * i) * ldm + c];
+        for (int i = 0; i < RI; ++i) m[i] = lds4(Ms + (rg + RG * i) * ldm + c);
 #pragma unroll
-        for (int j = 0; j < JD; ++j) {
-            r0[j] = R0[c * (HD + 1) + td + 16 * j];
-            if (NP > 1) r1[j] = R1[c * (HD + 1) + td + 16 * j];
-        }
+        for (int cc = 0; cc < 4; ++cc) {
+            const float4 r0 = lds4(R0 + (c + cc) * P + d0);
+            float4 r1 = r0;
+            if (NP > 1) r1 = lds4(R1 + (c + cc) * P + d0);
 #pragma unroll
-        for (int i = 0; i < IR; ++i)
+            for (int i = 0; i < RI; ++i) {
+                const float mv = f4(m[i], cc);
 #pragma unroll
-            for (int j = 0; j < JD; ++j) {
-                acc[0][i][j] = fmaf(m[i], r0[j], acc[0][i][j]);
-                if (NP > 1) acc[NP - 1][i][j] = fmaf(m[i], r1[j], acc[NP - 1][i][j]);
+                for (int v = 0; v < 4; ++v) {
+                    acc[0][i][v] = fmaf(mv, f4(r0, v), acc[0][i][v]);
+                    if (NP > 1) acc[NP - 1][i][v] = fmaf(mv, f4(r1, v), acc[NP - 1][i][v]);
+                }
             }
+        }
     }
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < IR; ++i)
-#pragma unroll
-        for (int j = 0; j < JD; ++j) {
-            const int o = (tr + 16 * i) * (HD + 1) + td + 16 * j;
-            O0[o] = acc[0][i][j];
-            if (NP > 1) O1[o] = acc[NP - 1][i][j];
-        }
+    for (int i = 0; i < RI; ++i) {
+        const int o = (rg + RG * i) * P + d0;
+        *reinterpret_cast<float4*>(O0 + o) = make_float4(acc[0][i][0], acc[0][i][1], acc[0][i][2], acc[0][i][3]);
+        if (NP > 1)
+            *reinterpret_cast<float4*>(O1 + o) =
+                make_float4(acc[NP - 1][i][0], acc[NP - 1][i][1], acc[NP - 1][i][2], acc[NP - 1][i][3]);
+    }
 }
 
 // ------------------------------------------------------------------ forward
@@ -215,26 +258,27 @@ __device__ __forceinline__ void rows_times_rows(const float* Ms, int ldm, const 
 template <int HD>
 __global__ void __launch_bounds__(kNT) attn_probs_kernel(const AttnArgs a) {
     pdl_entry();
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
+    constexpr int P = hd_pitch<HD>();
     const int Sq = a.Sq, Sk = a.Sk, c0 = blockIdx.y * kTC, tc = min(kTC, Sk - c0);
-    float* Qs = sm;                      // [Sq][HD+1]
-    float* Ks = Qs + Sq * (HD + 1);      // [kTC][HD+1]
-    float* Ss = Ks + kTC * (HD + 1);     // [Sq][kTC+1]
-    float* cred = Ss + Sq * (kTC + 1);   // [kWarps][kTC]
+    float* Qs = sm;                      // [Sq][P]
+    float* Ks = Qs + Sq * P;             // [kTC][P]
+    float* Ss = Ks + kTC * P;            // [Sq][kColPitch]
+    float* cred = Ss + Sq * kColPitch;   // [kWarps][kTC]
     const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H, t = threadIdx.x;
     load_rows<HD>(Qs, a.Q + b * a.qb + h * a.qh, Sq, Sq, a.qs);
     load_rows<HD>(Ks, a.K + b * a.kb + h * a.kh + (int64_t)c0 * a.ks, kTC, tc, a.ks);
     __syncthreads();
     // scaled scores (bcmmABT chain, then Scale_Write's product)
     const float scale = a.scale;
-    rows_times_cols<HD>(Qs, Ks, Sq, [&](int r, int c, float s) { Ss[r * (kTC + 1) + c] = scale * s; });
+    rows_times_cols<HD>(Qs, Ks, Sq, [&](int r, int c, float s) { Ss[r * kColPitch + c] = scale * s; });
     __syncthreads();
     // column max over every row, masked ones included (FindMax); max is
     // exact in any order
     const int lane = t & 31, w = t >> 5;
     {
         float m = -FLT_MAX;
-        for (int r = w; r < Sq; r += kWarps) m = fmaxf(m, Ss[r * (kTC + 1) + lane]);
+        for (int r = w; r < Sq; r += kWarps) m = fmaxf(m, Ss[r * kColPitch + lane]);
         cred[w * kTC + lane] = m;
     }
     __syncthreads();
@@ -243,7 +287,7 @@ __global__ void __launch_bounds__(kNT) attn_probs_kernel(const AttnArgs a) {
 #pragma unroll
         for (int i = 1; i < kWarps; ++i) m = fmaxf(m, cred[i * kTC + lane]);
         for (int r = w; r < Sq; r += kWarps) {
-            float* e = &Ss[r * (kTC + 1) + lane];
+            float* e = &Ss[r * kColPitch + lane];
             *e = (a.causal && c0 + lane > r) ? 0.0f : expf(*e - m);
         }
     }
@@ -252,7 +296,7 @@ __global__ void __launch_bounds__(kNT) attn_probs_kernel(const AttnArgs a) {
     if (t < kTC) {
         float s = 0.f;
 #pragma unroll 8
-        for (int r = 0; r < Sq; ++r) s += Ss[r * (kTC + 1) + t];
+        for (int r = 0; r < Sq; ++r) s += Ss[r * kColPitch + t];
         if (s < 1e-45f) s = 1.0f;
         cred[t] = s;
     }
@@ -260,17 +304,7 @@ __global__ void __launch_bounds__(kNT) attn_probs_kernel(const AttnArgs a) {
     float* Pg = a.Pout + (int64_t)bh * Sq * Sk + c0;
     for (int i = t; i < Sq * kTC; i += kNT) {
         const int r = i / kTC, c = i % kTC;
-        if (c < tc) Pg[(int64_t)r * Sk + c] = Ss[r * (kTC + 1) + c] / cred[c];
-    }
-}
-
-// [kTR][Sk] rows r0.. of a head's [Sq][Sk] matrix into shared rows of
-// Sk + 1 floats, zero beyond Sq
-__device__ __forceinline__ void load_row_tile(float* dst, const float* __restrict__ src, int tr, int Sk) {
-    const int ldm = Sk + 1;
-    for (int i = threadIdx.x; i < kTR * Sk; i += kNT) {
-        const int r = i / Sk, c = i % Sk;
-        dst[r * ldm + c] = r < tr ? src[(int64_t)r * Sk + c] : 0.f;
+        if (c < tc) Pg[(int64_t)r * Sk + c] = Ss[r * kColPitch + c] / cred[c];
     }
 }
 
@@ -278,22 +312,23 @@ __device__ __forceinline__ void load_row_tile(float* dst, const float* __restric
 template <int HD>
 __global__ void __launch_bounds__(kNT) attn_pv_kernel(const AttnArgs a) {
     pdl_entry();
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
+    constexpr int P = hd_pitch<HD>();
     const int Sq = a.Sq, Sk = a.Sk, r0 = blockIdx.y * kTR, tr = min(kTR, Sq - r0);
-    const int ldp = Sk + 1;
-    float* Ps = sm;                                   // [kTR][Sk+1]
-    float* Os = sm;                                   // [kTR][HD+1], overlays Ps
-    float* Vs = Ps + kTR * max(ldp, HD + 1);          // [Sk][HD+1]
+    const int ldp = seq_pitch(Sk), nk4 = (Sk + 3) & ~3;
+    float* Ps = sm;                                   // [kTR][ldp]
+    float* Os = sm;                                   // [kTR][P], overlays Ps
+    float* Vs = Ps + kTR * max(ldp, P);               // [nk4][P], rows >= Sk zero
     const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
     load_row_tile(Ps, a.Pout + ((int64_t)bh * Sq + r0) * Sk, tr, Sk);
-    load_rows<HD>(Vs, a.V + b * a.kb + h * a.kh, Sk, Sk, a.ks);
+    load_rows<HD>(Vs, a.V + b * a.kb + h * a.kh, nk4, Sk, a.ks);
     __syncthreads();
     rows_times_rows<HD, 1>(Ps, ldp, Vs, nullptr, Sk, Os, nullptr);
     __syncthreads();
     float* Og = a.O + b * a.qb + h * a.qh + (int64_t)r0 * a.qs;
-    for (int i = threadIdx.x; i < tr * HD; i += kNT) {
-        const int r = i / HD, d = i % HD;
-        Og[(int64_t)r * a.qs + d] = Os[r * (HD + 1) + d];
+    for (int i = threadIdx.x; i < tr * (HD / 4); i += kNT) {
+        const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
+        *reinterpret_cast<float4*>(Og + (int64_t)r * a.qs + d) = lds4(Os + r * P + d);
     }
 }
 
@@ -303,15 +338,16 @@ __global__ void __launch_bounds__(kNT) attn_pv_kernel(const AttnArgs a) {
 template <int HD>
 __global__ void __launch_bounds__(kNT) attn_bwd_cols_kernel(const AttnArgs a) {
     pdl_entry();
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
+    constexpr int P = hd_pitch<HD>();
     const int Sq = a.Sq, Sk = a.Sk, c0 = blockIdx.y * kTC, tc = min(kTC, Sk - c0);
     const bool true_dk = a.key_mode == MLE_KEYGRAD_TRUE;
-    float* dOs = sm;                      // [Sq][HD+1]
-    float* Vs = dOs + Sq * (HD + 1);      // [kTC][HD+1]
-    float* Ps = Vs + kTC * (HD + 1);      // [Sq][kTC+1]
-    float* Ds = Ps + Sq * (kTC + 1);      // [Sq][kTC+1]  dP, then dScores
-    float* dot = Ds + Sq * (kTC + 1);     // [kTC]
-    float* Qs = dot + kTC;                // [Sq][HD+1]  (true key gradient only)
+    float* dOs = sm;                        // [Sq][P]
+    float* Vs = dOs + Sq * P;               // [kTC][P]
+    float* Ps = Vs + kTC * P;               // [Sq][kColPitch]
+    float* Ds = Ps + Sq * kColPitch;        // [Sq][kColPitch]  dP, then dScores
+    float* Qs = Ds + Sq * kColPitch;        // [Sq][P]  (true key gradient only)
+    float* dot = Qs + (true_dk ? Sq * P : 0);   // [kTC]
     const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H, t = threadIdx.x;
     const int64_t qoff = b * a.qb + h * a.qh, koff = b * a.kb + h * a.kh + (int64_t)c0 * a.ks;
     const int64_t soff = (int64_t)bh * Sq * Sk + c0;
@@ -321,13 +357,13 @@ __global__ void __launch_bounds__(kNT) attn_bwd_cols_kernel(const AttnArgs a) {
     load_col_tile(Ps, a.P + (int64_t)bh * Sq * Sk, Sq, Sk, c0);
     __syncthreads();
     // dP = dO V^T (bcmmABT: k = head_dim ascending)
-    rows_times_cols<HD>(dOs, Vs, Sq, [&](int r, int c, float s) { Ds[r * (kTC + 1) + c] = s; });
+    rows_times_cols<HD>(dOs, Vs, Sq, [&](int r, int c, float s) { Ds[r * kColPitch + c] = s; });
     __syncthreads();
     // deriv_softmax type 1: per column dot over rows in order
     if (t < kTC) {
         float s = 0.f;
 #pragma unroll 8
-        for (int r = 0; r < Sq; ++r) s = fmaf(Ds[r * (kTC + 1) + t], Ps[r * (kTC + 1) + t], s);
+        for (int r = 0; r < Sq; ++r) s = fmaf(Ds[r * kColPitch + t], Ps[r * kColPitch + t], s);
         dot[t] = s;
     }
     __syncthreads();
@@ -337,14 +373,14 @@ __global__ void __launch_bounds__(kNT) attn_bwd_cols_kernel(const AttnArgs a) {
         const int r = i / kTC, c = i % kTC;
         float v = 0.f;
         if (c < tc) {
-            const float dp = Ds[r * (kTC + 1) + c];
+            const float dp = Ds[r * kColPitch + c];
             if (a.dPout) a.dPout[soff + (int64_t)r * Sk + c] += dp;
-            const float ds = Ps[r * (kTC + 1) + c] * (dp - dot[c]);
+            const float ds = Ps[r * kColPitch + c] * (dp - dot[c]);
             if (a.dSout) a.dSout[soff + (int64_t)r * Sk + c] += ds;
             v = (float)(0.0 + dscale * (double)ds);
             a.dScores[soff + (int64_t)r * Sk + c] = v;
         }
-        Ds[r * (kTC + 1) + c] = v;
+        Ds[r * kColPitch + c] = v;
     }
     __syncthreads();
     // dV = P^T dO and the true dK = dScores^T Q for these keys
@@ -364,28 +400,36 @@ __global__ void __launch_bounds__(kNT) attn_bwd_cols_kernel(const AttnArgs a) {
 template <int HD>
 __global__ void __launch_bounds__(kNT) attn_bwd_rows_kernel(const AttnArgs a) {
     pdl_entry();
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
+    constexpr int P = hd_pitch<HD>();
     const int Sq = a.Sq, Sk = a.Sk, r0 = blockIdx.y * kTR, tr = min(kTR, Sq - r0);
     const bool ref_dk = a.key_mode == MLE_KEYGRAD_REFERENCE;
-    const int ldm = Sk + 1;
-    float* Ms = sm;                                    // [kTR][Sk+1] dScores rows
-    float* Oq = sm;                                    // [kTR][HD+1] dQ rows, overlays Ms
-    float* Ok = Oq + kTR * (HD + 1);                   // [kTR][HD+1] reference key gradient
-    float* Ks = Ms + kTR * max(ldm, 2 * (HD + 1));     // [Sk][HD+1]
-    float* Qs = Ks + Sk * (HD + 1);                    // [Sk][HD+1]  (reference key gradient; Sq == Sk)
+    const int ldm = seq_pitch(Sk), nk4 = (Sk + 3) & ~3;
+    float* Ms = sm;                                    // [kTR][ldm] dScores rows
+    float* Oq = sm;                                    // [kTR][P] dQ rows, overlays Ms
+    float* Ok = Oq + kTR * P;                          // [kTR][P] reference key gradient
+    float* Ks = Ms + kTR * max(ldm, 2 * P);            // [nk4][P]
+    float* Qs = Ks + nk4 * P;                          // [nk4][P]  (reference key gradient; Sq == Sk)
     const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
     load_row_tile(Ms, a.dScores + ((int64_t)bh * Sq + r0) * Sk, tr, Sk);
     const int64_t qoff = b * a.qb + h * a.qh, koff = b * a.kb + h * a.kh;
-    load_rows<HD>(Ks, a.K + koff, Sk, Sk, a.ks);
-    if (ref_dk) load_rows<HD>(Qs, a.Q + qoff, Sk, Sk, a.qs);
+    load_rows<HD>(Ks, a.K + koff, nk4, Sk, a.ks);
+    if (ref_dk) load_rows<HD>(Qs, a.Q + qoff, nk4, Sk, a.qs);
     __syncthreads();
     if (ref_dk) rows_times_rows<HD, 2>(Ms, ldm, Ks, Qs, Sk, Oq, Ok);
     else rows_times_rows<HD, 1>(Ms, ldm, Ks, nullptr, Sk, Oq, nullptr);
     __syncthreads();
     float* dQg = a.dQ + qoff + (int64_t)r0 * a.qs;
-    for (int i = threadIdx.x; i < tr * HD; i += kNT) {
-        const int r = i / HD, d = i % HD;
-        dQg[(int64_t)r * a.qs + d] += Oq[r * (HD + 1) + d];
+    for (int i = threadIdx.x; i < tr * (HD / 4); i += kNT) {
+        const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
+        float4* g = reinterpret_cast<float4*>(dQg + (int64_t)r * a.qs + d);
+        float4 o = *g;
+        const float4 v = lds4(Oq + r * P + d);
+        o.x += v.x;
+        o.y += v.y;
+        o.z += v.z;
+        o.w += v.w;
+        *g = o;
     }
     if (ref_dk) {
         // bcmmT(Q, dScores, Kh.grad, hd, Sq, Sk) writes element (row d, col
@@ -395,27 +439,30 @@ __global__ void __launch_bounds__(kNT) attn_bwd_rows_kernel(const AttnArgs a) {
         for (int i = threadIdx.x; i < tr * HD; i += kNT) {
             const int d = i / tr, r = i % tr;
             const int pos = d * Sk + r0 + r;
-            dKg[(int64_t)(pos / HD) * a.ks + pos % HD] += Ok[r * (HD + 1) + d];
+            dKg[(int64_t)(pos / HD) * a.ks + pos % HD] += Ok[r * P + d];
         }
     }
 }
 
 template <int HD>
 size_t probs_smem(int Sq) {
-    return sizeof(float) * ((size_t)Sq * (HD + 1) + kTC * (HD + 1) + (size_t)Sq * (kTC + 1) + kWarps * kTC);
+    return sizeof(float) * ((size_t)Sq * hd_pitch<HD>() + kTC * hd_pitch<HD>() + (size_t)Sq * kColPitch + kWarps * kTC);
 }
 template <int HD>
 size_t pv_smem(int Sk) {
-    return sizeof(float) * ((size_t)kTR * std::max(Sk + 1, HD + 1) + (size_t)Sk * (HD + 1));
+    const size_t nk4 = (size_t)((Sk + 3) & ~3);
+    return sizeof(float) * ((size_t)kTR * std::max(seq_pitch(Sk), hd_pitch<HD>()) + nk4 * hd_pitch<HD>());
 }
 template <int HD>
 size_t bwd_cols_smem(int Sq, bool true_dk) {
-    return sizeof(float) * ((size_t)Sq * (HD + 1) * (true_dk ? 2 : 1) + kTC * (HD + 1) + 2 * (size_t)Sq * (kTC + 1) +
-                            kTC);
+    return sizeof(float) * ((size_t)Sq * hd_pitch<HD>() * (true_dk ? 2 : 1) + kTC * hd_pitch<HD>() +
+                            2 * (size_t)Sq * kColPitch + kTC);
 }
 template <int HD>
 size_t bwd_rows_smem(int Sk, bool ref_dk) {
-    return sizeof(float) * ((size_t)kTR * std::max(Sk + 1, 2 * (HD + 1)) + (size_t)Sk * (HD + 1) * (ref_dk ? 2 : 1));
+    const size_t nk4 = (size_t)((Sk + 3) & ~3);
+    return sizeof(float) * ((size_t)kTR * std::max(seq_pitch(Sk), 2 * hd_pitch<HD>()) +
+                            nk4 * hd_pitch<HD>() * (ref_dk ? 2 : 1));
 }
 
 constexpr size_t kMaxSmem = 227 * 1024;
@@ -508,7 +555,7 @@ int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, 
     if ((softmax_axis != 0 && softmax_axis != 1) || (layout != MLE_ATTN_HEAD_MAJOR && layout != MLE_ATTN_TOKEN_MAJOR))
         return MLE_ERR_ARG;
     cudaStream_t st = as_stream(stream);
-    if (fused_ok(softmax_axis, seq_q, seq_k, head_dim, batch, heads) && ptrs_aligned({Q, K, V})) {
+    if (fused_ok(softmax_axis, seq_q, seq_k, head_dim, batch, heads) && ptrs_aligned({Q, K, V, O})) {
         AttnArgs a{};
         a.Q = Q;
         a.K = K;
@@ -548,7 +595,7 @@ int mle_attention_bwd(const float* Q, const float* K, const float* V, const floa
     cudaStream_t st = as_stream(stream);
     const bool ref_shape_ok = key_grad_mode == MLE_KEYGRAD_TRUE || seq_q == seq_k;
     if (fused_ok(softmax_axis, seq_q, seq_k, head_dim, batch, heads) && ref_shape_ok &&
-        ptrs_aligned({Q, K, V, dO})) {
+        ptrs_aligned({Q, K, V, dO, dQ, dK, dV})) {
         if (!workspace) return MLE_ERR_ARG;
         AttnArgs a{};
         a.Q = Q;

@@ -124,16 +124,22 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
     const int64_t begin = chunk * kChunk;
     int64_t end = begin + kChunk;
     if (end > P.n) end = P.n;
-    const int t = *P.t;
     const float b1 = P.b1, b2 = P.b2, eps = P.eps, wd = P.weight_decay;
-    double bc1, bc2;
-    if (ADAMW) {
-        bc1 = 1.0 - pow(b1, t);   // pow(float, int) as in AdamWUpdate
-        bc2 = 1.0 - pow(b2, t);
-    } else {
-        bc1 = 1.0 - powf(b1, (float)t);
-        bc2 = 1.0 - powf(b2, (float)t);
+    // bias corrections: one thread per block evaluates the powers (the
+    // same values every thread would compute)
+    __shared__ double bc[2];
+    if (threadIdx.x == 0) {
+        const int t = *P.t;
+        if (ADAMW) {
+            bc[0] = 1.0 - pow(b1, t);   // pow(float, int) as in AdamWUpdate
+            bc[1] = 1.0 - pow(b2, t);
+        } else {
+            bc[0] = 1.0 - powf(b1, (float)t);
+            bc[1] = 1.0 - powf(b2, (float)t);
+        }
     }
+    __syncthreads();
+    const double bc1 = bc[0], bc2 = bc[1];
     const float clip_f = CLIP ? (float)clip_ws[0] : 1.0f;
     float* __restrict__ W = P.w;
     float* __restrict__ G = P.g;

@@ -226,9 +226,15 @@ def param_views(params):
     return arr
 
 
+# `params` below is a list of dicts (see param_views) or an array already
+# made by param_views, which callers that repeat the update can keep.
+def _views(params):
+    return params if isinstance(params, ctypes.Array) else param_views(params)
+
+
 def grad_sumsq(params, norm_ws, scale=1.0):
-    views = param_views(params)
-    _call("mle_grad_sumsq", ctypes.cast(views, ctypes.c_void_p), len(params), _p(norm_ws), scale, _s())
+    views = _views(params)
+    _call("mle_grad_sumsq", ctypes.cast(views, ctypes.c_void_p), len(views), _p(norm_ws), scale, _s())
 
 
 def clip_finalize(norm_ws, max_norm=1.0):
@@ -236,13 +242,13 @@ def clip_finalize(norm_ws, max_norm=1.0):
 
 
 def clip_apply(params, norm_ws):
-    views = param_views(params)
-    _call("mle_clip_apply", ctypes.cast(views, ctypes.c_void_p), len(params), _p(norm_ws), _s())
+    views = _views(params)
+    _call("mle_clip_apply", ctypes.cast(views, ctypes.c_void_p), len(views), _p(norm_ws), _s())
 
 
 def adam_update(params, lr, adamw=True, clip_ws=None, pre_scale=1.0, write_back_grad=True):
-    views = param_views(params)
-    _call("mle_adam_update", ctypes.cast(views, ctypes.c_void_p), len(params), _p(clip_ws), pre_scale, lr,
+    views = _views(params)
+    _call("mle_adam_update", ctypes.cast(views, ctypes.c_void_p), len(views), _p(clip_ws), pre_scale, lr,
           int(adamw), int(write_back_grad), _s())
 
 
