@@ -301,6 +301,22 @@ int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, f
 
 /* ------------------------------------------------------------------ */
 /* fused attention backward                                             */
+/* Up to three Linear layers that read the same input X -- the query, key
+ * and value projections of MultiHeadAttention::forward
+ * (Engine/transformer.cu:647-650) -- in one persistent tensor-core launch
+ * each way, with the semantics of n separate mle_linear_fwd / _bwd calls:
+ *   forward : Y_i = X W_i (+ b_i) (assigned), W_i [in, out_i];
+ *   backward: dX += sum_i dY_i W_i^T (one launch, reduce-added), dW_i +=
+ *             X^T dY_i (one launch), dB_i += column sums of dY_i;
+ *             dX, bias and dB (or any dB[i]) may be NULL.
+ * Pointer arrays are HOST arrays of n device pointers. */
+int mle_linear_group_fwd(const float* X, const float* const* W, const float* const* bias, float* const* Y,
+                         int n, int64_t rows, int in_features, const int* out_features,
+                         mle_stream_t stream);
+int mle_linear_group_bwd(const float* X, const float* const* W, const float* const* dY, float* dX,
+                         float* const* dW, float* const* dB, int n, int64_t rows, int in_features,
+                         const int* out_features, mle_stream_t stream);
+
 /* ------------------------------------------------------------------ */
 
 /* Key-gradient semantics of mle_attention_bwd.

@@ -143,6 +143,8 @@ void Zerograd(AdamParameter X);
 void Zerograd(graph X);
 graph_tree topological_sort(const graph& root);
 
+class Linear;
+
 class GraphOperations {
    private:
     static bool calculate_loss;
@@ -228,6 +230,12 @@ class GraphOperations {
                                     const bool mask, const int axis = 1,
                                     const int key_grad_mode = MLE_KEYGRAD_REFERENCE);
 
+    // Extension: several Linear layers that read the same input X (the
+    // query/key/value projections of MultiHeadAttention) with one tensor-core
+    // launch for their forward and one each for their dX and dW; returns one
+    // node per layer with Linear::forward's semantics.
+    static std::vector<graph> LinearGroup(const graph& X, const std::vector<Linear*>& layers);
+
    private:
     float grad_prescale_ = 1.0f;
     bool clip_pending_ = false;
@@ -250,6 +258,9 @@ class Linear {
     void save(std::ofstream& f) const;
     void load(std::ifstream& f);
     void operator=(const Linear& other);
+    int inputs() const { return in; }
+    int outputs() const { return out; }
+    bool has_bias() const { return bias; }
 };
 
 // Convolute2D (Includes/engine.h:235-255): weights [out][inp][C][D], NCHW.

@@ -816,3 +816,96 @@ graph Convolute2DT::forward(const graph& X) {
     conv_param_lambdas(node, W, B);
     return node;
 }
+
+// ------------------------------------------- LinearGroup (extension)
+std::vector<graph> GraphOperations::LinearGroup(const graph& X, const std::vector<Linear*>& layers) {
+    const int n = (int)layers.size();
+    if (n < 1 || n > 3) {
+        std::cerr << "LinearGroup: 1 to 3 layers\n";
+        std::exit(1);
+    }
+    const int batch = X->dim[0], channels = X->dim[1], m = X->dim[2], in = X->dim[3];
+    const long long rows = (long long)batch * channels * m;
+    struct Shared {
+        const float* W[3];
+        const float* bias[3];
+        float* Y[3];
+        const float* dY[3];
+        float* dW[3];
+        float* dB[3];
+        int out[3];
+        int n;
+        int backward_seen = 0;
+    };
+    auto sh = std::make_shared<Shared>();
+    sh->n = n;
+    std::vector<graph> nodes;
+    for (int i = 0; i < n; ++i) {
+        Linear* L = layers[i];
+        if (L->inputs() != in) {
+            std::cout << "Shape Mismatch in Linear Layer of " << X->op_name << ": \n";
+            std::exit(1);
+        }
+        auto node = std::make_shared<NodeBackProp>(L->op_name, batch, channels, m, L->outputs(), 1);
+        node->inputs = {X};
+        sh->W[i] = L->W1.output;
+        sh->bias[i] = L->has_bias() ? L->B1.output : nullptr;
+        sh->Y[i] = node->output;
+        sh->dY[i] = node->grad;
+        sh->dW[i] = L->W1.grad;
+        sh->dB[i] = L->has_bias() ? L->B1.grad : nullptr;
+        sh->out[i] = L->outputs();
+        nodes.push_back(node);
+    }
+    NodeBackProp* xp = X.get();
+    for (int i = 0; i < n; ++i) {
+        NodeBackProp* nd = nodes[i].get();
+        AdamParameter* W = &layers[i]->W1;
+        AdamParameter* Bp = layers[i]->has_bias() ? &layers[i]->B1 : nullptr;
+        if (i == 0) {
+            nd->forward = [=]() {
+                check(mle_linear_group_fwd(xp->output, sh->W, sh->bias, sh->Y, sh->n, rows, in, sh->out, st()),
+                      "Linear group forward");
+            };
+        } else {
+            nd->forward = []() {};  // computed with the first layer of the group
+        }
+        // the output gradients of all layers are complete once the reverse
+        // walk has reached every one of them
+        nd->backward = [=]() {
+            // the node that issues the group's backward reports every
+            // layer's parameter gradients (data-parallel buckets)
+            std::vector<float*>& done = ext(nd).param_grads;
+            done.clear();
+            if (++sh->backward_seen < sh->n) return;
+            sh->backward_seen = 0;
+            check(mle_linear_group_bwd(xp->output, sh->W, sh->dY, xp->grad, sh->dW, sh->dB, sh->n, rows, in, sh->out,
+                                       st()),
+                  "Linear group backward");
+            for (int j = 0; j < sh->n; ++j) {
+                done.push_back(sh->dW[j]);
+                if (sh->dB[j]) done.push_back(sh->dB[j]);
+            }
+        };
+        nd->free = [nd]() { nd->clear(); };
+        nd->zero_grad = [=]() {
+            zero_range(nd->grad, nd->total);
+            zero_range(W->grad, W->total);
+            if (Bp) zero_range(Bp->grad, Bp->total);
+        };
+        nd->accumulate = [=](double* gs) {
+            W->accumulate_grad(gs);
+            if (Bp) Bp->accumulate_grad(gs);
+        };
+        nd->clipnorm = [=](const double* gs) {
+            W->gradnorm(gs);
+            if (Bp) Bp->gradnorm(gs);
+        };
+        nd->updateParams = [=](const float lr, const bool adamw) {
+            W->update(lr, adamw);
+            if (Bp) Bp->update(lr, adamw);
+        };
+        ext(nd).param_grads.clear();
+    }
+    return nodes;
+}

@@ -117,7 +117,24 @@ graph attention(Session& S, const graph& xq, const graph& xkv, bool mask, float 
     Linear* k = new_linear(S, D, D, name + " Key");
     Linear* v = new_linear(S, D, D, name + " Value");
     Linear* o = new_linear(S, D, D, name + " Output");
-    graph Qp = q->forward(xq), Kp = k->forward(xkv), Vp = v->forward(xkv);
+    graph Qp, Kp, Vp;
+    if (S.d.fused_attention && xq.get() == xkv.get()) {
+        // self-attention: the three projections read the same input
+        std::vector<graph> p = GraphOperations::LinearGroup(xq, {q, k, v});
+        Qp = p[0];
+        Kp = p[1];
+        Vp = p[2];
+    } else if (S.d.fused_attention) {
+        // cross-attention: keys and values read the encoder output
+        Qp = q->forward(xq);
+        std::vector<graph> p = GraphOperations::LinearGroup(xkv, {k, v});
+        Kp = p[0];
+        Vp = p[1];
+    } else {
+        Qp = q->forward(xq);
+        Kp = k->forward(xkv);
+        Vp = v->forward(xkv);
+    }
     graph att;
     if (S.d.fused_attention) {
         att = GraphOperations::ScaledDotAttention(Qp, Kp, Vp, H, scale, mask, 1, S.d.key_grad_mode);

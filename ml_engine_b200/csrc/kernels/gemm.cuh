@@ -23,5 +23,6 @@ struct GemmProblem {
 
 int simt_gemm(const GemmProblem& p, cudaStream_t st);
 int run_gemm(const GemmProblem& p, cudaStream_t st);
+int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st);
 
 }  // namespace mle

@@ -68,6 +68,22 @@ struct Tile {
     int m0, n0, bidx, cidx, kb_begin, nkb;
 };
 
+// Up to kMaxGroup problems of one layout class share a launch; their tiles
+// are numbered consecutively (tile_start is the prefix of ep[g].tiles).
+constexpr int kMaxGroup = 3;
+struct GemmGroup {
+    CUtensorMap a[kMaxGroup], b[kMaxGroup], c[kMaxGroup];
+    EpiParams ep[kMaxGroup];
+    int64_t tile_start[kMaxGroup + 1];
+    int n;
+};
+
+__device__ __forceinline__ int group_of(const GemmGroup& G, int64_t t) {
+    int g = 0;
+    while (g + 1 < G.n && t >= G.tile_start[g + 1]) ++g;
+    return g;
+}
+
 __device__ __forceinline__ Tile tile_at(const EpiParams& ep, int64_t t, int BN) {
     Tile x;
     const int n = (int)(t % ep.n_tiles);
@@ -270,8 +286,7 @@ struct Smem {
 // A_MN: A is stored MN-major ([K][M]); B_MN: B is stored MN-major ([K][N]).
 template <bool A_MN, bool B_MN, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, const EpiParams ep) {
+    gemm_tf32_kernel(const __grid_constant__ GemmGroup grp) {
     using L = Smem<BN, STAGES>;
     static_assert(L::EPI_WARP_BYTES >= 32 * kEpiLd * 4, "staging");
     constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
@@ -286,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t total_tiles = grp.tile_start[grp.n];
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -299,9 +315,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
-        if (ep.tma_epi) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmC)) : "memory");
+        for (int g = 0; g < grp.n; ++g) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&grp.a[g])) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&grp.b[g])) : "memory");
+            if (grp.ep[g].tma_epi)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&grp.c[g])) : "memory");
+        }
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -327,8 +346,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; ok && t < ep.tiles; t += gridDim.x) {
-                const Tile x = tile_at(ep, t, BN);
+            for (int64_t t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+                const int g = group_of(grp, t);
+                const EpiParams& ep = grp.ep[g];
+                const CUtensorMap* tmA = &grp.a[g];
+                const CUtensorMap* tmB = &grp.b[g];
+                const Tile x = tile_at(ep, t - grp.tile_start[g], BN);
                 const int a_c = ep.a_has_c ? x.cidx : 0, a_b = ep.a_has_b ? x.bidx : 0;
                 const int b_c = ep.b_has_c ? x.cidx : 0, b_b = ep.b_has_b ? x.bidx : 0;
                 for (int i = 0; i < x.nkb; ++i) {
@@ -343,16 +366,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (A_MN) {
 #pragma unroll
                         for (int j = 0; j < BM / 32; ++j)
-                            tma_load_4d(&tmA, &full[s], sa + j * 4096, x.m0 + 32 * j, k0, a_c, a_b);
+                            tma_load_4d(tmA, &full[s], sa + j * 4096, x.m0 + 32 * j, k0, a_c, a_b);
                     } else {
-                        tma_load_4d(&tmA, &full[s], sa, k0, x.m0, a_c, a_b);
+                        tma_load_4d(tmA, &full[s], sa, k0, x.m0, a_c, a_b);
                     }
                     if (B_MN) {
 #pragma unroll
                         for (int j = 0; j < BN / 32; ++j)
-                            tma_load_4d(&tmB, &full[s], sb + j * 4096, x.n0 + 32 * j, k0, b_c, b_b);
+                            tma_load_4d(tmB, &full[s], sb + j * 4096, x.n0 + 32 * j, k0, b_c, b_b);
                     } else {
-                        tma_load_4d(&tmB, &full[s], sb, k0, x.n0, b_c, b_b);
+                        tma_load_4d(tmB, &full[s], sb, k0, x.n0, b_c, b_b);
                     }
                     issued[s] = true;
                     last_parity[s] = ph;
@@ -379,8 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             int acc = 0;
-            for (int64_t t = blockIdx.x; ok && t < ep.tiles; t += gridDim.x, ++acc) {
-                const Tile x = tile_at(ep, t, BN);
+            for (int64_t t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++acc) {
+                const int g = group_of(grp, t);
+                const Tile x = tile_at(grp.ep[g], t - grp.tile_start[g], BN);
                 const int buf = acc & 1;
                 const uint32_t use = (uint32_t)(acc >> 1);
                 if (!wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) break;
@@ -421,8 +445,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rsub = lane >> 3, c4 = (lane & 7) * 4;
         int acc = 0;
         uint32_t blocks_out = 0;  // bulk groups this warp committed
-        for (int64_t t = blockIdx.x; t < ep.tiles; t += gridDim.x, ++acc) {
-            const Tile x = tile_at(ep, t, BN);
+        for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++acc) {
+            const int g = group_of(grp, t);
+            const EpiParams& ep = grp.ep[g];
+            const CUtensorMap* tmC = &grp.c[g];
+            const Tile x = tile_at(ep, t - grp.tile_start[g], BN);
             const int buf = acc & 1;
             const uint32_t use = (uint32_t)(acc >> 1);
             // the tcgen05.ld below is warp-collective: leave the loop together
@@ -475,8 +502,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) {
                         const int cz = ep.c_has_c ? x.cidx : 0, bz = ep.c_has_b ? x.bidx : 0;
-                        if (ep.mode == EPI_ASSIGN) tma_store_4d(&tmC, blk, col0, row0, cz, bz);
-                        else tma_reduce_add_4d(&tmC, blk, col0, row0, cz, bz);
+                        if (ep.mode == EPI_ASSIGN) tma_store_4d(tmC, blk, col0, row0, cz, bz);
+                        else tma_reduce_add_4d(tmC, blk, col0, row0, cz, bz);
                         bulk_commit();
                     }
                     ++blocks_out;
@@ -608,10 +635,10 @@ static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
-static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const EpiParams& ep,
-                     cudaStream_t st) {
+static int launch_tc(const GemmGroup& grp, cudaStream_t st) {
     using L = Smem<BN, STAGES>;
     static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
+    static_assert(sizeof(GemmGroup) <= 4000, "kernel parameter space");
     auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, STAGES>;
     static bool configured = false;
     if (!configured) {
@@ -621,7 +648,8 @@ static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
     }
     // persistent: one CTA per SM (the shared-memory ring admits one); the
     // prologue may overlap the previous kernel (programmatic dependent launch)
-    const int grid = (int)(ep.tiles < kSMs ? ep.tiles : kSMs);
+    const int64_t tiles = grp.tile_start[grp.n];
+    const int grid = (int)(tiles < kSMs ? tiles : kSMs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -632,7 +660,7 @@ static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, ep) != cudaSuccess) return launch_status();
+    if (cudaLaunchKernelEx(&cfg, kern, grp) != cudaSuccess) return launch_status();
     return launch_status();
 }
 
@@ -651,44 +679,80 @@ static bool tc_eligible(const GemmProblem& p) {
 
 static thread_local int g_gemm_mode = MLE_GEMM_MODE_TF32;
 
-int run_gemm(const GemmProblem& p, cudaStream_t st) {
-    if (p.M <= 0 || p.N <= 0 || p.nbatch <= 0 || p.channels <= 0) return MLE_OK;
-    if (p.K <= 0) {
-        // empty reduction: assign writes alpha*0 (+bias); accumulate is a no-op
-        if (p.mode != tc::EPI_ASSIGN) return MLE_OK;
-    }
-    if (p.K <= 0 || g_gemm_mode == MLE_GEMM_MODE_FP32 || !tc_eligible(p)) return simt_gemm(p, st);
+namespace {
 
+struct Shape {
+    bool A_MN, B_MN;
+    int m_tiles, kb_total;
+    int64_t z;
+};
+
+Shape shape_of(const GemmProblem& p) {
+    Shape s;
+    s.A_MN = p.trans_a != 0;  // A stored [K][M]: M contiguous
+    s.B_MN = p.trans_b == 0;  // B stored [K][N]: N contiguous
+    s.z = (int64_t)p.nbatch * p.channels;
+    s.m_tiles = (p.M + tc::BM - 1) / tc::BM;
+    s.kb_total = (p.K + tc::BK - 1) / tc::BK;
+    return s;
+}
+
+bool may_split(const GemmProblem& p) {
+    const int64_t z = (int64_t)p.nbatch * p.channels;
+    const bool c_dense = p.ldc == p.N && (z == 1 || (p.c_sb == (int64_t)p.M * p.N && p.channels == 1));
+    return p.mode != tc::EPI_ASSIGN || c_dense;
+}
+
+// Tile width and split-K for a set of problems launched together.  For
+// accumulated outputs, a fill-time model: operand tiles reach shared memory
+// at ~90 GB/s per SM, so the mainloop costs sum M*N*K*4*(1/BN + 1/BM) bytes
+// spread over the SMs in use, and splitting K adds one reduce-add of C per
+// split.  Its choices match the best measured (BN, splits) within ~5 % for
+// the transformer's backward GEMMs.
+void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits) {
     using namespace tc;
-    const bool A_MN = p.trans_a != 0;  // A stored [K][M]: M contiguous
-    const bool B_MN = p.trans_b == 0;  // B stored [K][N]: N contiguous
-    const int64_t z_count = (int64_t)p.nbatch * p.channels;
-    const int m_tiles = (p.M + BM - 1) / BM;
-    const int kb_total = (p.K + BK - 1) / BK;
-
-    // Tile width and split-K from a fill-time model.  Operand tiles reach
-    // shared memory at ~90 GB/s per SM, so the mainloop costs
-    // M*N*K*4*(1/BN + 1/BM) bytes spread over the SMs in use; splitting K
-    // adds one reduce-add of C per split (and, for an assigned C, a memset
-    // first).  An assigned C may be split only when it is one dense block.
-    const bool c_dense = p.ldc == p.N && (z_count == 1 || (p.c_sb == (int64_t)p.M * p.N && p.channels == 1));
-    const bool may_split = p.mode != EPI_ASSIGN || c_dense;
-    int BN = 64, splits = 1;
+    BN = 64;
+    splits = 1;
+    // Assigned outputs never split (the memset and reduce-adds cost more
+    // than they save, measured on B200); narrow tiles keep enough of them
+    // in flight for these small-K products.
+    bool any_assign = false;
+    int max_n = 0;
+    for (int i = 0; i < n; ++i) {
+        any_assign = any_assign || ps[i].mode == EPI_ASSIGN;
+        max_n = std::max(max_n, ps[i].N);
+    }
+    if (any_assign) {
+        BN = max_n <= 256 ? 64 : 128;
+        return;
+    }
     double best = 1e30;
+    int min_n = ps[0].N, kb_min = 1 << 30;
+    bool split_ok = true;
+    for (int i = 0; i < n; ++i) {
+        min_n = std::min(min_n, ps[i].N);
+        kb_min = std::min(kb_min, shape_of(ps[i]).kb_total);
+        split_ok = split_ok && may_split(ps[i]);
+    }
     for (int cand : {256, 128, 64}) {
-        if (cand > 64 && p.N < cand / 2 + 1) continue;
-        const int64_t nt = (p.N + cand - 1) / cand;
-        const int64_t units = (int64_t)m_tiles * nt * z_count;
-        const int max_split = may_split ? std::max(1, kb_total / 4) : 1;
+        if (cand > 64 && min_n < cand / 2 + 1) continue;
+        int64_t units = 0;
+        double fill = 0, cbytes = 0, assign_bytes = 0;
+        for (int i = 0; i < n; ++i) {
+            const GemmProblem& p = ps[i];
+            const Shape sh = shape_of(p);
+            const int64_t u = (int64_t)sh.m_tiles * ((p.N + cand - 1) / cand) * sh.z;
+            units += u;
+            fill += (double)u * (BM + cand) * (double)sh.kb_total * BK * 4.0;
+            cbytes += (double)p.M * p.N * sh.z * 4.0;
+            if (p.mode == EPI_ASSIGN) assign_bytes += (double)p.M * p.N * sh.z * 4.0;
+        }
+        const int max_split = split_ok ? std::max(1, kb_min / 4) : 1;
         for (int sp = 1; sp <= max_split; sp = (sp < 4 ? sp + 1 : sp * 2)) {
             const int64_t work = units * sp;
             const double active = (double)std::min<int64_t>(work, kSMs);
-            const double fill = (double)units * (BM + cand) * (double)kb_total * BK * 4.0;
             double t = fill / (active * 90e9) + 0.3e-6 * (double)((work + kSMs - 1) / kSMs);
-            if (sp > 1) {
-                t += (double)sp * p.M * p.N * z_count * 4.0 / 3e12;
-                if (p.mode == EPI_ASSIGN) t += (double)p.M * p.N * z_count * 4.0 / 5e12;
-            }
+            if (sp > 1) t += (double)sp * cbytes / 3e12 + assign_bytes / 5e12;
             if (t < best * 0.98) {
                 best = t;
                 BN = cand;
@@ -697,22 +761,27 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
             if (work >= kSMs) break;
         }
     }
-    const int n_tiles = (p.N + BN - 1) / BN;
-    const int64_t tiles = (int64_t)m_tiles * n_tiles * z_count;
-    const int kb_per_split = (kb_total + splits - 1) / splits;
-    splits = (kb_total + kb_per_split - 1) / kb_per_split;
-    if (splits > 1 && p.mode == EPI_ASSIGN) {
-        // split partial products are reduce-added into a zeroed C
-        const size_t bytes = sizeof(float) * (size_t)p.M * p.N * (size_t)z_count;
-        if (cudaMemsetAsync(p.C, 0, bytes, st) != cudaSuccess) return launch_status();
-    }
+}
 
-    EpiParams ep;
+// Fills slot g of a launch group for problem p (tensor maps and epilogue
+// parameters); an assigned C that is split is zeroed first.  False if TMA
+// cannot describe an operand.
+int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc::GemmGroup& grp, int g,
+            cudaStream_t st, bool& ok) {
+    using namespace tc;
+    ok = false;
+    const Shape sh = shape_of(p);
+    const int n_tiles = (p.N + BN - 1) / BN;
+    const int64_t tiles = (int64_t)sh.m_tiles * n_tiles * sh.z;
+    const int kb_per_split = (sh.kb_total + splits_req - 1) / splits_req;
+    const int splits = (sh.kb_total + kb_per_split - 1) / kb_per_split;
+    EpiParams& ep = grp.ep[g];
+    memset(&ep, 0, sizeof(ep));
     ep.C = p.C;
     ep.bias = p.bias;
     ep.ldc = p.ldc;
-    ep.c_stride_b = p.c_sb;
-    ep.c_stride_c = p.c_sc;
+    ep.c_stride_b = p.nbatch == 1 ? 0 : p.c_sb;
+    ep.c_stride_c = p.channels == 1 ? 0 : p.c_sc;
     ep.M = p.M;
     ep.N = p.N;
     ep.K = p.K;
@@ -723,41 +792,37 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     ep.a_has_c = (p.a_sc != 0 && p.channels > 1);
     ep.b_has_b = (p.b_sb != 0 && p.nbatch > 1);
     ep.b_has_c = (p.b_sc != 0 && p.channels > 1);
-    if (p.nbatch == 1) ep.c_stride_b = 0;
-    if (p.channels == 1) ep.c_stride_c = 0;
-    ep.m_tiles = m_tiles;
+    ep.m_tiles = sh.m_tiles;
     ep.n_tiles = n_tiles;
     ep.tiles = tiles * splits;
     ep.alpha = p.alpha;
-    ep.mode = (splits > 1) ? EPI_ATOMIC : p.mode;
+    ep.mode = (splits > 1 || force_atomic) ? EPI_ATOMIC : p.mode;
     ep.vec = ((p.ldc & 3) == 0) && aligned16(p.C) && ((ep.c_stride_b & 3) == 0) && ((ep.c_stride_c & 3) == 0) &&
              (p.bias == nullptr || aligned16(p.bias));
 
     OperandView va, vb;
     va.base = p.A;
-    va.inner = A_MN ? p.M : p.K;
-    va.outer = A_MN ? p.K : p.M;
+    va.inner = sh.A_MN ? p.M : p.K;
+    va.outer = sh.A_MN ? p.K : p.M;
     va.ld = p.lda;
     va.nc = ep.a_has_c ? p.channels : 1;
     va.nb = ep.a_has_b ? p.nbatch : 1;
     va.sc = p.a_sc;
     va.sb = p.a_sb;
     vb.base = p.B;
-    vb.inner = B_MN ? p.N : p.K;
-    vb.outer = B_MN ? p.K : p.N;
+    vb.inner = sh.B_MN ? p.N : p.K;
+    vb.outer = sh.B_MN ? p.K : p.N;
     vb.ld = p.ldb;
     vb.nc = ep.b_has_c ? p.channels : 1;
     vb.nb = ep.b_has_b ? p.nbatch : 1;
     vb.sc = p.b_sc;
     vb.sb = p.b_sb;
-    CUtensorMap ma, mb;
-    memset(&ma, 0, sizeof(ma));
-    memset(&mb, 0, sizeof(mb));
-    if (!encode_operand(&ma, va, 32, A_MN ? BK : BM, A_MN)) return simt_gemm(p, st);
-    if (!encode_operand(&mb, vb, 32, B_MN ? BK : BN, B_MN)) return simt_gemm(p, st);
+    memset(&grp.a[g], 0, sizeof(CUtensorMap));
+    memset(&grp.b[g], 0, sizeof(CUtensorMap));
+    memset(&grp.c[g], 0, sizeof(CUtensorMap));
+    if (!encode_operand(&grp.a[g], va, 32, sh.A_MN ? BK : BM, sh.A_MN)) return MLE_OK;
+    if (!encode_operand(&grp.b[g], vb, 32, sh.B_MN ? BK : BN, sh.B_MN)) return MLE_OK;
     // C through bulk tensor stores when its rows and strides allow TMA
-    CUtensorMap mc;
-    memset(&mc, 0, sizeof(mc));
     ep.c_has_b = (ep.c_stride_b != 0);
     ep.c_has_c = (ep.c_stride_c != 0);
     ep.tma_epi = 0;
@@ -771,10 +836,20 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
         vc.nb = ep.c_has_b ? p.nbatch : 1;
         vc.sc = ep.c_stride_c;
         vc.sb = ep.c_stride_b;
-        ep.tma_epi = encode_operand(&mc, vc, 32, 32) ? 1 : 0;
+        ep.tma_epi = encode_operand(&grp.c[g], vc, 32, 32) ? 1 : 0;
     }
+    if (splits > 1 && p.mode == EPI_ASSIGN) {
+        // split partial products are reduce-added into a zeroed C
+        const size_t bytes = sizeof(float) * (size_t)p.M * p.N * (size_t)sh.z;
+        if (cudaMemsetAsync(p.C, 0, bytes, st) != cudaSuccess) return launch_status();
+    }
+    ok = true;
+    return MLE_OK;
+}
 
-#define MLE_TC(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST>(ma, mb, mc, ep, st)
+int dispatch(const tc::GemmGroup& grp, bool A_MN, bool B_MN, int BN, cudaStream_t st) {
+    using namespace tc;
+#define MLE_TC(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST>(grp, st)
     if (BN == 256) {
         if (A_MN) { if (B_MN) MLE_TC(true, true, 256, 4); else MLE_TC(true, false, 256, 4); }
         else { if (B_MN) MLE_TC(false, true, 256, 4); else MLE_TC(false, false, 256, 4); }
@@ -786,6 +861,72 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
         else { if (B_MN) MLE_TC(false, true, 64, 6); else MLE_TC(false, false, 64, 6); }
     }
 #undef MLE_TC
+}
+
+bool tc_path(const GemmProblem& p) { return p.K > 0 && g_gemm_mode == MLE_GEMM_MODE_TF32 && tc_eligible(p); }
+
+}  // namespace
+
+int run_gemm(const GemmProblem& p, cudaStream_t st) {
+    if (p.M <= 0 || p.N <= 0 || p.nbatch <= 0 || p.channels <= 0) return MLE_OK;
+    if (p.K <= 0) {
+        // empty reduction: assign writes alpha*0 (+bias); accumulate is a no-op
+        if (p.mode != tc::EPI_ASSIGN) return MLE_OK;
+    }
+    if (!tc_path(p)) return simt_gemm(p, st);
+    int BN, splits;
+    choose_tiles(&p, 1, BN, splits);
+    tc::GemmGroup grp;
+    memset(&grp, 0, sizeof(grp));
+    bool ok = false;
+    const int s = prepare(p, BN, splits, false, grp, 0, st, ok);
+    if (s) return s;
+    if (!ok) return simt_gemm(p, st);
+    grp.n = 1;
+    grp.tile_start[0] = 0;
+    grp.tile_start[1] = grp.ep[0].tiles;
+    const Shape sh = shape_of(p);
+    return dispatch(grp, sh.A_MN, sh.B_MN, BN, st);
+}
+
+// Problems of one layout class in one persistent launch.  `shared_c`: all
+// write the same C (their results are summed with reduce-adds).  Falls back
+// to one launch per problem when the set cannot share a launch.
+int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st) {
+    if (n <= 0) return MLE_OK;
+    bool same = n <= tc::kMaxGroup;
+    for (int i = 0; i < n && same; ++i) {
+        same = tc_path(ps[i]) && ps[i].M > 0 && ps[i].N > 0 && ps[i].nbatch > 0 && ps[i].channels > 0 &&
+               shape_of(ps[i]).A_MN == shape_of(ps[0]).A_MN && shape_of(ps[i]).B_MN == shape_of(ps[0]).B_MN;
+        if (shared_c && ps[i].mode == tc::EPI_ASSIGN) same = false;
+    }
+    if (!same) {
+        for (int i = 0; i < n; ++i) {
+            const int s = run_gemm(ps[i], st);
+            if (s) return s;
+        }
+        return MLE_OK;
+    }
+    int BN, splits;
+    choose_tiles(ps, n, BN, splits);
+    tc::GemmGroup grp;
+    memset(&grp, 0, sizeof(grp));
+    grp.n = n;
+    grp.tile_start[0] = 0;
+    for (int i = 0; i < n; ++i) {
+        bool ok = false;
+        const int s = prepare(ps[i], BN, splits, shared_c, grp, i, st, ok);
+        if (s) return s;
+        if (!ok) {  // an operand TMA cannot describe: separate launches
+            for (int j = 0; j < n; ++j) {
+                const int s2 = run_gemm(ps[j], st);
+                if (s2) return s2;
+            }
+            return MLE_OK;
+        }
+        grp.tile_start[i + 1] = grp.tile_start[i] + grp.ep[i].tiles;
+    }
+    return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st);
 }
 
 }  // namespace mle
@@ -847,6 +988,85 @@ int mle_gemm(const float* A, const float* B, float* C, const float* bias, int ba
         p.mode = tc::EPI_ATOMIC;
     }
     return run_gemm(p, as_stream(stream));
+}
+
+namespace {
+// A single (unbatched) row-major product as the Linear entry points use it.
+GemmProblem linear_problem(const float* A, const float* B, float* C, const float* bias, int64_t M, int64_t N,
+                           int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int trans_a, int trans_b, int mode) {
+    GemmProblem p;
+    memset(&p, 0, sizeof(p));
+    p.A = A;
+    p.B = B;
+    p.C = C;
+    p.bias = bias;
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.lda = lda;
+    p.ldb = ldb;
+    p.ldc = ldc;
+    p.trans_a = trans_a;
+    p.trans_b = trans_b;
+    p.nbatch = 1;
+    p.channels = 1;
+    p.alpha = 1.0f;
+    p.mode = mode;
+    return p;
+}
+}  // namespace
+
+int mle_linear_group_fwd(const float* X, const float* const* W, const float* const* bias, float* const* Y, int n,
+                         int64_t rows, int in_features, const int* out_features, mle_stream_t stream) {
+    if (!X || !W || !Y || !out_features || n <= 0 || n > tc::kMaxGroup || rows < 0 || in_features <= 0)
+        return MLE_ERR_ARG;
+    if (rows == 0) return MLE_OK;
+    if (rows > 0x7fffffff) return MLE_ERR_UNSUPPORTED;
+    GemmProblem ps[tc::kMaxGroup];
+    for (int i = 0; i < n; ++i) {
+        if (!W[i] || !Y[i] || out_features[i] <= 0) return MLE_ERR_ARG;
+        ps[i] = linear_problem(X, W[i], Y[i], bias ? bias[i] : nullptr, rows, out_features[i], in_features,
+                               in_features, out_features[i], out_features[i], 0, 0, tc::EPI_ASSIGN);
+    }
+    return run_gemm_group(ps, n, false, as_stream(stream));
+}
+
+int mle_linear_group_bwd(const float* X, const float* const* W, const float* const* dY, float* dX,
+                         float* const* dW, float* const* dB, int n, int64_t rows, int in_features,
+                         const int* out_features, mle_stream_t stream) {
+    if (!X || !W || !dY || !dW || !out_features || n <= 0 || n > tc::kMaxGroup || rows < 0 || in_features <= 0)
+        return MLE_ERR_ARG;
+    if (rows == 0) return MLE_OK;
+    if (rows > 0x7fffffff) return MLE_ERR_UNSUPPORTED;
+    cudaStream_t st = as_stream(stream);
+    GemmProblem ps[tc::kMaxGroup];
+    int s;
+    if (dX) {
+        // dX += sum_i dY_i W_i^T: every product reduce-adds into dX
+        for (int i = 0; i < n; ++i) {
+            if (!W[i] || !dY[i] || out_features[i] <= 0) return MLE_ERR_ARG;
+            ps[i] = linear_problem(dY[i], W[i], dX, nullptr, rows, in_features, out_features[i], out_features[i],
+                                   out_features[i], in_features, 0, 1, tc::EPI_ACCUM);
+        }
+        s = run_gemm_group(ps, n, true, st);
+        if (s) return s;
+    }
+    // dW_i += X^T dY_i
+    for (int i = 0; i < n; ++i) {
+        if (!dW[i] || !dY[i]) return MLE_ERR_ARG;
+        ps[i] = linear_problem(X, dY[i], dW[i], nullptr, in_features, out_features[i], rows, in_features,
+                               out_features[i], out_features[i], 1, 0, tc::EPI_ACCUM);
+    }
+    s = run_gemm_group(ps, n, false, st);
+    if (s) return s;
+    if (dB) {
+        for (int i = 0; i < n; ++i) {
+            if (!dB[i]) continue;
+            s = mle_bias_grad(dY[i], dB[i], rows, out_features[i], 1.0f, stream);
+            if (s) return s;
+        }
+    }
+    return MLE_OK;
 }
 
 int mle_bcmm(int variant, const float* A, const float* B, float* C, int batch, int channels, int m, int n, int p,

@@ -7,7 +7,7 @@ Tolerances (see conftest): 1e-5 for elementwise / reduction / Adam paths,
 import numpy as np
 import pytest
 
-from conftest import RTOL_EXACT, RTOL_TC, rel_err
+from conftest import RTOL_EXACT, RTOL_TC, norm_err, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -518,3 +518,38 @@ def test_argument_errors(cuda, ops):
 
 def test_watchdog_clear(cuda, ops):
     assert ops.watchdog() == 0
+
+
+@pytest.mark.parametrize("n", [1, 2, 3])
+def test_linear_group_matches_separate_linears(cuda, ops, rng, n):
+    """mle_linear_group_fwd/_bwd against n separate mle_linear_fwd/_bwd
+    calls (TF32 products; dX sums the n products with reduce-adds)."""
+    import ctypes
+    from ml_engine_b200._lib import kernels
+    rows, din = 1024, 256
+    outs = [256, 128, 512][:n]
+    X = T(rng.standard_normal((rows, din)).astype(np.float32), cuda)
+    Ws = [T((rng.standard_normal((din, o)) * 0.05).astype(np.float32), cuda) for o in outs]
+    Bs = [T(rng.standard_normal(o).astype(np.float32), cuda) for o in outs]
+    dYs = [T(rng.standard_normal((rows, o)).astype(np.float32), cuda) for o in outs]
+    dX0 = rng.standard_normal((rows, din)).astype(np.float32)
+    arr = lambda ts: (ctypes.c_void_p * n)(*[t.data_ptr() for t in ts])
+    Ys = [torch.empty(rows, o, device=cuda) for o in outs]
+    out_arr = (ctypes.c_int * n)(*outs)
+    st = torch.cuda.current_stream().cuda_stream
+    kernels().call("mle_linear_group_fwd", X.data_ptr(), arr(Ws), arr(Bs), arr(Ys), n, rows, din, out_arr, st)
+    dX = T(dX0, cuda)
+    dWs = [torch.zeros(din, o, device=cuda) for o in outs]
+    dBs = [torch.zeros(o, device=cuda) for o in outs]
+    kernels().call("mle_linear_group_bwd", X.data_ptr(), arr(Ws), arr(dYs), dX.data_ptr(), arr(dWs), arr(dBs), n,
+                   rows, din, out_arr, st)
+    rX = T(dX0, cuda)
+    for i, o in enumerate(outs):
+        y = torch.empty(rows, o, device=cuda)
+        ops.linear_fwd(X, Ws[i], Bs[i], y, rows, din, o)
+        assert norm_err(H(Ys[i]), H(y)) <= RTOL_TC
+        dw, db = torch.zeros(din, o, device=cuda), torch.zeros(o, device=cuda)
+        ops.linear_bwd(X, Ws[i], dYs[i], rX, dw, db, rows, din, o)
+        assert norm_err(H(dWs[i]), H(dw)) <= RTOL_TC
+        assert norm_err(H(dBs[i]), H(db)) <= 1e-6
+    assert norm_err(H(dX) - dX0, H(rX) - dX0) <= RTOL_TC
