@@ -232,3 +232,67 @@ def encoder_step(params, table, tokens, targets, batch, seq, d_model, heads, ffn
     steps = steps or [1] * len(grads)
     clip, new_p, m, v = clip_and_update([p.ravel() for p in P], grads, steps, lr, clip_norm)
     return dict(loss=loss, grads=raw, clipped=grads, clip=clip, params=new_p, m=m, v=v)
+
+
+def encdec_step(params, tables, src, tgt_in, tgt_out, batch, seq, d_model, heads, ffn, layers, vocab, lr=1e-3,
+                clip_norm=1.0, steps=None):
+    """One step of the ENCDEC session graph on the oracle: `layers` encoder
+    blocks over the source, `layers` decoder blocks (pre-LN masked
+    self-attention scaled by 1/sqrt(head_dim), cross-attention to the raw
+    encoder output as MultiHeadAttention::cross_forward does it -- masked,
+    scaled by 1/sqrt(d_model), Engine/transformer.cu:662-675 -- and a GELU
+    FFN), projection, softmax cross-entropy."""
+    B, S, D, H = batch, seq, d_model, heads
+    rows = B * S
+    enc_shapes, dec_shapes = [], []
+    for _ in range(layers):
+        enc_shapes += [(D, D), (D,)] * 4 + [(D, ffn), (ffn,), (ffn, D), (D,)]
+    for _ in range(layers):
+        dec_shapes += [(D, D), (D,)] * 8 + [(D, ffn), (ffn,), (ffn, D), (D,)]
+    shapes = enc_shapes + dec_shapes + [(D, vocab), (vocab,)]
+    P = [p.reshape(s) for p, s in zip(params, shapes)]
+    G = [np.zeros_like(p) for p in P]
+    tape = _Tape()
+
+    def embed(tokens, table):
+        emb = o.embedding_gather(tokens.ravel(), table.reshape(vocab, D))
+        return o.matpe(emb, B, S, D).reshape(rows, D)
+
+    e = embed(src, tables[0])
+    de = np.zeros_like(e)
+    for layer in range(layers):
+        base = layer * 12
+        h, dh = _layernorm_tokens(tape, e, de, rows, D)
+        a, da = _attention(tape, h, dh, h, dh, P[base:base + 8], G[base:base + 8], B, S, S, D, H,
+                           1.0 / math.sqrt(D // H), False)
+        e1, de1 = _add(tape, e, de, a, da)
+        h2, dh2 = _layernorm_tokens(tape, e1, de1, rows, D)
+        f, df = _ffn(tape, h2, dh2, P[base + 8], P[base + 9], P[base + 10], P[base + 11], G[base + 8:base + 12])
+        e, de = _add(tape, e1, de1, f, df)
+    x = embed(tgt_in, tables[1])
+    dx = np.zeros_like(x)
+    off = 12 * layers
+    for layer in range(layers):
+        base = off + layer * 20
+        h, dh = _layernorm_tokens(tape, x, dx, rows, D)
+        a, da = _attention(tape, h, dh, h, dh, P[base:base + 8], G[base:base + 8], B, S, S, D, H,
+                           1.0 / math.sqrt(D // H), True)
+        x1, dx1 = _add(tape, x, dx, a, da)
+        h2, dh2 = _layernorm_tokens(tape, x1, dx1, rows, D)
+        c, dc = _attention(tape, h2, dh2, e, de, P[base + 8:base + 16], G[base + 8:base + 16], B, S, S, D, H,
+                           1.0 / math.sqrt(D), True)
+        x2, dx2 = _add(tape, x1, dx1, c, dc)
+        h3, dh3 = _layernorm_tokens(tape, x2, dx2, rows, D)
+        f, df = _ffn(tape, h3, dh3, P[base + 16], P[base + 17], P[base + 18], P[base + 19],
+                     G[base + 16:base + 20])
+        x, dx = _add(tape, x2, dx2, f, df)
+    logits, dlogits = _linear(tape, x, dx, P[-2], P[-1], G[-2], G[-1])
+    target = o.one_hot(tgt_out.ravel(), vocab)
+    probs, loss = o.smce_fwd(logits, target, rows, vocab)
+    dlogits[:] = o.smce_bwd(probs, target, float(B)).reshape(rows, vocab)
+    tape.backward()
+    grads = [g.ravel().copy() for g in G]
+    raw = [g.copy() for g in grads]
+    steps = steps or [1] * len(grads)
+    clip, new_p, m, v = clip_and_update([p.ravel() for p in P], grads, steps, lr, clip_norm)
+    return dict(loss=loss, grads=raw, clipped=grads, clip=clip, params=new_p, m=m, v=v)

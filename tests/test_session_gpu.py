@@ -111,6 +111,35 @@ def test_encoder_step_matches_oracle(cuda, rng, fused):
     _check_step(s, ref, p0, lr, exact=False)
 
 
+@pytest.mark.parametrize("fused", [1, 0])
+def test_encdec_step_matches_oracle(cuda, rng, fused):
+    """configs[2] structure at a small size: encoder stack, decoder stack
+    with masked self-attention and masked cross-attention to the encoder
+    output (scale 1/sqrt(d_model)), projection, SMCE, clip, AdamW."""
+    from oracle import graphs
+    cfg = dict(batch=2, seq=32, d_model=64, heads=4, ffn=128, layers=2, vocab=256)
+    lr = 1e-3
+    s = _session(config=3, batch=cfg["batch"], seq_len=cfg["seq"], d_model=cfg["d_model"], heads=cfg["heads"],
+                 ffn=cfg["ffn"], layers=cfg["layers"], vocab=cfg["vocab"], lr=lr, clip_norm=1.0,
+                 fused_attention=fused, seed=7)
+    p0 = [(rng.standard_normal(n) * 0.05).astype(np.float32) for n in s.param_sizes]
+    for i, p in enumerate(p0):
+        s.write_param(i, p)
+    tables = [(rng.standard_normal(cfg["vocab"] * cfg["d_model"]) * 0.5).astype(np.float32) for _ in range(2)]
+    s.write_embedding(0, tables[0])
+    s.write_embedding(1, tables[1])
+    shape = (cfg["batch"], cfg["seq"])
+    src, tgt_in, tgt_out = (rng.integers(0, cfg["vocab"], shape).astype(np.int32) for _ in range(3))
+    s.inputs["src"][:] = src.ravel()
+    s.inputs["tgt_in"][:] = tgt_in.ravel()
+    s.inputs["tgt_out"][:] = tgt_out.ravel()
+    loss = s.step()
+    ref = graphs.encdec_step(p0, tables, src, tgt_in, tgt_out, cfg["batch"], cfg["seq"], cfg["d_model"],
+                             cfg["heads"], cfg["ffn"], cfg["layers"], cfg["vocab"], lr=lr)
+    assert abs(loss - ref["loss"]) <= 1e-4 * abs(ref["loss"]), (loss, ref["loss"])
+    _check_step(s, ref, p0, lr, exact=False)
+
+
 def test_graph_replay_equals_eager(cuda, rng):
     """A captured CUDA graph of the step gives the same parameters as eager
     steps on the same inputs (device step counters advance in both).  The
