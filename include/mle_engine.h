@@ -31,7 +31,8 @@ typedef void* mle_session_t;
 enum mle_config {
     MLE_CFG_MLP = 1,      /* Linear-ReLU-Linear + SoftMaxCrossEntropy (use_cases/mnist.cu:252-273) */
     MLE_CFG_ENCODER = 2,  /* pre-LN transformer encoder stack + projection + SMCE */
-    MLE_CFG_ENCDEC = 3    /* encoder-decoder (self, masked self, cross attention) + SMCE */
+    MLE_CFG_ENCDEC = 3,   /* encoder-decoder (self, masked self, cross attention) + SMCE */
+    MLE_CFG_UNET = 4      /* DDPM noise-prediction U-Net (ResidualBlocks, Conv2D/Conv2DT, GroupNorm, MSE) */
 };
 
 typedef struct mle_session_desc {
@@ -49,6 +50,11 @@ typedef struct mle_session_desc {
     float clip_norm;     /* <= 0 disables the clip */
     uint64_t seed;
     int gemm_mode;       /* MLE_GEMM_MODE_TF32 or MLE_GEMM_MODE_FP32 for every GEMM of the step */
+    /* U-Net: images [batch, channels, image_size, image_size]; levels of
+     * base_width, 2x and 4x channels; sinusoidal time embedding of t_embed
+     * features for the timestep `timestep` (fixed when the graph is built,
+     * as the reference's PositionalEncoding node captures it) */
+    int channels, image_size, base_width, t_embed, timestep;
 } mle_session_desc;
 
 /* Builds the graph and allocates everything the step needs. */

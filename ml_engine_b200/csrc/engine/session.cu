@@ -51,6 +51,11 @@ struct Session {
     GraphOperations go;
     graph loss;
     std::vector<std::unique_ptr<Linear>> linears;
+    std::vector<std::unique_ptr<Convolute2D>> convs;
+    std::vector<std::unique_ptr<Convolute2DT>> convts;
+    // (weight, bias) of every layer in construction order: the parameter
+    // order the session reports and the reference's layers update in
+    std::vector<std::pair<AdamParameter*, AdamParameter*>> layer_params;
     std::vector<AdamParameter*> params;
     std::vector<Input> inputs;
     std::vector<std::function<void()>> prep;
@@ -87,7 +92,39 @@ struct StreamScope {  // routes every op of this session to its stream and GEMM 
 
 Linear* new_linear(Session& S, int in, int out, const std::string& name) {
     S.linears.emplace_back(new Linear(in, out, name));
-    return S.linears.back().get();
+    Linear* l = S.linears.back().get();
+    S.layer_params.push_back({&l->W1, &l->B1});
+    return l;
+}
+
+Convolute2D* new_conv(Session& S, int in, int out, int k, int stride, int pad, const std::string& name) {
+    S.convs.emplace_back(new Convolute2D(in, out, k, k, stride, pad, name));
+    Convolute2D* c = S.convs.back().get();
+    S.layer_params.push_back({&c->W1, &c->B1});
+    return c;
+}
+
+Convolute2DT* new_convT(Session& S, int in, int out, int k, int stride, int pad, const std::string& name) {
+    S.convts.emplace_back(new Convolute2DT(in, out, k, k, stride, pad, name));
+    Convolute2DT* c = S.convts.back().get();
+    S.layer_params.push_back({&c->W1, &c->B1});
+    return c;
+}
+
+// ResidualBlock::forward (Engine/diffusion.cu:109-137): conv-GroupNorm-SiLU,
+// time MLP broadcast per channel, conv-GroupNorm, skip (a strided 1x1 conv
+// when the shape changes), Add, SiLU.  The skip convolution is built only
+// when it is used (the reference also constructs an unused one).
+graph residual_block(Session& S, const graph& x, const graph& t, int in, int out, int stride, const std::string& name) {
+    Convolute2D* c1 = new_conv(S, in, out, 3, stride, 1, name + " Conv1");
+    Convolute2D* c2 = new_conv(S, out, out, 3, 1, 1, name + " Conv2");
+    Linear* tm = new_linear(S, t->dim[3], out, name + " Time MLP");
+    Convolute2D* sk = (in != out || stride != 1) ? new_conv(S, in, out, 1, stride, 0, name + " SkipConv") : nullptr;
+    graph h = GraphOperations::SILU(GraphOperations::GroupNorm(c1->forward(x)));
+    h = GraphOperations::Broadcast_Channel(h, tm->forward(t));
+    h = GraphOperations::GroupNorm(c2->forward(h));
+    graph skip = sk ? sk->forward(x) : x;
+    return GraphOperations::SILU(GraphOperations::Add(h, skip));
 }
 
 Input& add_input(Session& S, const std::string& name, int dtype, int64_t numel, void* dev) {
@@ -219,6 +256,29 @@ void build(Session& S) {
         for (int l = 0; l < d.layers; ++l) x = encoder_block(S, x, d.seq_len, "Enc" + std::to_string(l));
         Linear* proj = new_linear(S, d.d_model, d.vocab, "Projection");
         S.loss = GraphOperations::SoftMaxCrossEntropy(proj->forward(x), target, true);
+    } else if (d.config == MLE_CFG_UNET) {
+        // U_NET::build_train (Engine/diffusion.cu:271-294) with three levels
+        const int B = d.batch, C = d.channels, HW = d.image_size, w = d.base_width;
+        auto x = std::make_shared<NodeBackProp>("x_t", B, C, HW, HW, 1);
+        add_input(S, "x_t", 0, (int64_t)B * C * HW * HW, x->output);
+        auto target = std::make_shared<NodeBackProp>("noise", B, C, HW, HW, 1);
+        add_input(S, "noise", 0, (int64_t)B * C * HW * HW, target->output);
+        // TimeMLPBlock (Engine/engine.cu:3914-3922): Linear, SiLU, Linear
+        graph t_emb = GraphOperations::PositionalEncoding(d.timestep, d.t_embed);
+        Linear* t0 = new_linear(S, d.t_embed, d.t_embed / 2, "Time MLP L0");
+        Linear* t1 = new_linear(S, d.t_embed / 2, d.t_embed / 2, "Time MLP L1");
+        graph t = t1->forward(GraphOperations::SILU(t0->forward(t_emb)));
+        graph e1 = residual_block(S, x, t, C, w, 1, "Enc1");
+        graph e2 = residual_block(S, e1, t, w, 2 * w, 2, "Enc2");
+        graph e3 = residual_block(S, e2, t, 2 * w, 4 * w, 2, "Enc3");
+        graph b0 = residual_block(S, e3, t, 4 * w, 4 * w, 1, "Bottleneck0");
+        graph b1 = residual_block(S, b0, t, 4 * w, 4 * w, 1, "Bottleneck1");
+        graph u1 = new_convT(S, 4 * w, 4 * w, 2, 2, 0, "UpConv 1")->forward(b1);
+        graph d1 = residual_block(S, GraphOperations::CopyCrop(u1, e2), t, 6 * w, 2 * w, 1, "Dec1");
+        graph u2 = new_convT(S, 2 * w, 2 * w, 2, 2, 0, "UpConv 2")->forward(d1);
+        graph d2 = residual_block(S, GraphOperations::CopyCrop(u2, e1), t, 3 * w, w, 1, "Dec2");
+        graph y = new_conv(S, w, C, 1, 1, 0, "Output Convolution")->forward(d2);
+        S.loss = GraphOperations::MeanSquaredError(y, target, true);
     } else if (d.config == MLE_CFG_ENCDEC) {
         graph e = GraphOperations::MatrixPositionalEncoding(token_input(S, "src", d.vocab));
         for (int l = 0; l < d.layers; ++l) e = encoder_block(S, e, d.seq_len, "Enc" + std::to_string(l));
@@ -236,7 +296,7 @@ void init_params(Session& S) {
     std::mt19937_64 gen(S.d.seed * 0x2545F4914F6CDD1Dull + 17);
     for (AdamParameter* p : S.params) {
         std::vector<float> h((size_t)p->total, 0.0f);
-        const bool is_bias = p->dim[2] == 1;
+        const bool is_bias = p->dim[0] == 1 && p->dim[2] == 1;  // [1,1,1,out] or [1,out,1,1]
         if (!is_bias) {
             const double stdv = (S.d.config == MLE_CFG_MLP) ? sqrt(2.0 / p->dim[2]) : 0.02;
             std::normal_distribution<double> nd(0.0, stdv);
@@ -313,6 +373,12 @@ int mle_session_create(const mle_session_desc* desc, mle_session_t* out) {
         if (d.seq_len <= 0 || d.d_model <= 0 || d.heads <= 0 || d.d_model % d.heads || d.ffn <= 0 || d.layers <= 0 ||
             d.vocab <= 0)
             return MLE_ERR_ARG;
+    } else if (d.config == MLE_CFG_UNET) {
+        // widths w, 2w, 3w (a concatenation), 4w, 6w go through GroupNorm(8);
+        // the image halves twice
+        if (d.channels <= 0 || d.base_width <= 0 || d.base_width % 8 || d.image_size <= 0 || d.image_size % 4 ||
+            d.t_embed < 2 || d.t_embed % 2 || d.timestep < 0)
+            return MLE_ERR_ARG;
     } else {
         return MLE_ERR_ARG;
     }
@@ -333,9 +399,9 @@ int mle_session_create(const mle_session_desc* desc, mle_session_t* out) {
     // parameters in graph order (the order ParameterUpdate visits them)
     {
         std::vector<AdamParameter*> ordered;
-        for (auto& l : S->linears) {
-            ordered.push_back(&l->W1);
-            ordered.push_back(&l->B1);
+        for (auto& wb : S->layer_params) {
+            ordered.push_back(wb.first);
+            ordered.push_back(wb.second);
         }
         S->params = ordered;
     }

@@ -17,7 +17,7 @@ import numpy as np
 
 from ._lib import MLEError, engine
 
-MLP, ENCODER, ENCDEC = 1, 2, 3
+MLP, ENCODER, ENCDEC, UNET = 1, 2, 3, 4
 KEYGRAD_REFERENCE, KEYGRAD_TRUE = 0, 1
 
 
@@ -31,6 +31,8 @@ class SessionDesc(ctypes.Structure):
         ("lr", ctypes.c_float), ("adamw", ctypes.c_int), ("clip_norm", ctypes.c_float),
         ("seed", ctypes.c_uint64),
         ("gemm_mode", ctypes.c_int),
+        ("channels", ctypes.c_int), ("image_size", ctypes.c_int), ("base_width", ctypes.c_int),
+        ("t_embed", ctypes.c_int), ("timestep", ctypes.c_int),
     ]
 
 
@@ -87,6 +89,13 @@ class Session:
     def encdec(cls, batch=256, seq_len=256, d_model=512, heads=8, ffn=2048, layers=6, vocab=8192, **kw):
         return cls(config=ENCDEC, batch=batch, seq_len=seq_len, d_model=d_model, heads=heads, ffn=ffn,
                    layers=layers, vocab=vocab, **kw)
+
+    @classmethod
+    def unet(cls, batch=32, channels=3, image_size=64, base_width=64, t_embed=256, timestep=500, **kw):
+        """DDPM noise prediction; inputs "x_t" (noised images) and
+        "noise" (the target), both [batch, channels, image_size, image_size]."""
+        return cls(config=UNET, batch=batch, channels=channels, image_size=image_size, base_width=base_width,
+                   t_embed=t_embed, timestep=timestep, **kw)
 
     # ---------------------------------------------------------------- step
     @property

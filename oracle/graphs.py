@@ -296,3 +296,164 @@ def encdec_step(params, tables, src, tgt_in, tgt_out, batch, seq, d_model, heads
     steps = steps or [1] * len(grads)
     clip, new_p, m, v = clip_and_update([p.ravel() for p in P], grads, steps, lr, clip_norm)
     return dict(loss=loss, grads=raw, clipped=grads, clip=clip, params=new_p, m=m, v=v)
+
+
+# ================================================================== U-Net
+def _conv(tape, x, dx, W, b, gW, gb, pad, stride):
+    y = o.conv2d_fwd(x, W, b, pad, stride)
+    dy = np.zeros_like(y)
+    N = x.shape[0]
+
+    def bwd():
+        gW[...] = o.conv2d_bwd_k(x, dy, W.shape, pad, stride)          # assigned, as GV2D
+        o.channel_bias_bwd(dy, None, gb.reshape(-1), N, W.shape[0], y.shape[2] * y.shape[3])
+        if dx is not None:
+            o.conv2d_bwd_x(dy, W, dx, pad, stride)
+
+    tape.add(bwd)
+    return y, dy
+
+
+def _convT(tape, x, dx, W, b, gW, gb, pad, stride):
+    y = o.convT2d_fwd(x, W, b, pad, stride)
+    dy = np.zeros_like(y)
+    N = x.shape[0]
+
+    def bwd():
+        gW[...] = o.convT2d_bwd_w(x, dy, W.shape, pad, stride)         # assigned, as GVT2D
+        o.channel_bias_bwd(dy, None, gb.reshape(-1), N, W.shape[0], y.shape[2] * y.shape[3])
+        dx[...] = o.convT2d_bwd_x(dy, W, x.shape, pad, stride)         # assigned, as CVT2D_GradInput
+
+    tape.add(bwd)
+    return y, dy
+
+
+def _groupnorm(tape, x, dx, groups=8):
+    N, C, Hh, Ww = x.shape
+    y, _, sq = o.groupnorm_fwd(x, N, C, groups, Hh, Ww)
+    y = y.reshape(x.shape)
+    dy = np.zeros_like(y)
+
+    def bwd():
+        o.groupnorm_bwd(y, dy, sq, dx, N, C, groups, Hh, Ww)
+
+    tape.add(bwd)
+    return y, dy
+
+
+def _silu(tape, x, dx):
+    y = o.act_fwd(2, x).reshape(x.shape)
+    dy = np.zeros_like(y)
+
+    def bwd():
+        o.act_bwd(2, x, dy, dx)
+
+    tape.add(bwd)
+    return y, dy
+
+
+def _broadcast_channel(tape, a, da, tv, dtv):
+    """Broadcast_Channel: y = a + tv[c]; the B gradient is reduced for the
+    first min(width, channels) channels only, as the reference's
+    Channel_Squeeze1D<<<width, ...>>> launch does (Engine/engine.cu:1435)."""
+    N, C, Hh, Ww = a.shape
+    y = o.channel_bias_fwd(a, tv.reshape(-1), N, C, Hh * Ww).reshape(a.shape)
+    dy = np.zeros_like(y)
+
+    def bwd():
+        np.add(da, dy, out=da)
+        red = min(Ww, C)
+        part = np.zeros(red, np.float32)
+        o.channel_bias_bwd(np.ascontiguousarray(dy[:, :red]), None, part, N, red, Hh * Ww)
+        dtv.reshape(-1)[:red] += part
+
+    tape.add(bwd)
+    return y, dy
+
+
+def _residual_block(tape, x, dx, t, dt, prm, grd, cin, cout, stride):
+    """ResidualBlock::forward (Engine/diffusion.cu:129-137); prm/grd hold
+    conv1 (W, b), conv2 (W, b), time Linear (W, b) and, when the shape
+    changes, the 1x1 skip convolution (W, b)."""
+    c1, dc1 = _conv(tape, x, dx, prm[0], prm[1], grd[0], grd[1], 1, stride)
+    g1, dg1 = _groupnorm(tape, c1, dc1)
+    s1, ds1 = _silu(tape, g1, dg1)
+    tv, dtv = _linear(tape, t, dt, prm[4], prm[5], grd[4], grd[5])
+    h, dh = _broadcast_channel(tape, s1, ds1, tv, dtv)
+    c2, dc2 = _conv(tape, h, dh, prm[2], prm[3], grd[2], grd[3], 1, 1)
+    g2, dg2 = _groupnorm(tape, c2, dc2)
+    if cin != cout or stride != 1:
+        skip, dskip = _conv(tape, x, dx, prm[6], prm[7], grd[6], grd[7], 0, stride)
+    else:
+        skip, dskip = x, dx
+    a, da = _add(tape, g2, dg2, skip, dskip)
+    return _silu(tape, a.reshape(g2.shape), da.reshape(g2.shape))
+
+
+def unet_step(params, x_t, noise, batch, channels, image_size, base_width, t_embed, timestep, lr=1e-3,
+              clip_norm=1.0, steps=None):
+    """One step of the UNET session graph on the oracle (U_NET::build_train,
+    Engine/diffusion.cu:271-294, with three levels)."""
+    N, C, S, w = batch, channels, image_size, base_width
+    th = t_embed // 2
+    shapes = [(t_embed, th), (th,), (th, th), (th,)]
+
+    def block_shapes(cin, cout, stride):
+        s = [(cout, cin, 3, 3), (cout,), (cout, cout, 3, 3), (cout,), (th, cout), (cout,)]
+        if cin != cout or stride != 1:
+            s += [(cout, cin, 1, 1), (cout,)]
+        return s
+
+    layout = [("Enc1", C, w, 1), ("Enc2", w, 2 * w, 2), ("Enc3", 2 * w, 4 * w, 2), ("B0", 4 * w, 4 * w, 1),
+              ("B1", 4 * w, 4 * w, 1)]
+    for _, ci, co, st in layout:
+        shapes += block_shapes(ci, co, st)
+    shapes += [(4 * w, 4 * w, 2, 2), (4 * w,)] + block_shapes(6 * w, 2 * w, 1)
+    shapes += [(2 * w, 2 * w, 2, 2), (2 * w,)] + block_shapes(3 * w, w, 1)
+    shapes += [(C, w, 1, 1), (C,)]
+    P = [p.reshape(s) for p, s in zip(params, shapes)]
+    G = [np.zeros_like(p) for p in P]
+    tape = _Tape()
+    temb = o.timestep_pe(timestep, t_embed).reshape(1, t_embed)
+    t0, dt0 = _linear(tape, temb, None, P[0], P[1], G[0], G[1])
+    a0, da0 = _silu(tape, t0, dt0)
+    t, dt = _linear(tape, a0, da0, P[2], P[3], G[2], G[3])
+    x = x_t.reshape(N, C, S, S).astype(np.float32)
+    dx = np.zeros_like(x)
+    k = 4
+    outs = []
+    cur, dcur = x, dx
+    for _, ci, co, st in layout:
+        n = 8 if (ci != co or st != 1) else 6
+        cur, dcur = _residual_block(tape, cur, dcur, t, dt, P[k:k + n], G[k:k + n], ci, co, st)
+        outs.append((cur, dcur))
+        k += n
+    e1, e2 = outs[0], outs[1]
+
+    def up_level(cur, dcur, skip, cin, cout, k):
+        u, du = _convT(tape, cur, dcur, P[k], P[k + 1], G[k], G[k + 1], 0, 2)
+        Nn, c1, Hh, Ww = u.shape
+        c2 = skip[0].shape[1]
+        cat = o.channel_concat(u, skip[0], Nn, c1, c2, Hh * Ww).reshape(Nn, c1 + c2, Hh, Ww)
+        dcat = np.zeros_like(cat)
+
+        def bwd():
+            o.channel_split(du, skip[1], dcat, Nn, c1, c2, Hh * Ww)
+
+        tape.add(bwd)
+        n = 8
+        y, dy = _residual_block(tape, cat, dcat, t, dt, P[k + 2:k + 2 + n], G[k + 2:k + 2 + n], cin, cout, 1)
+        return y, dy, k + 2 + n
+
+    cur, dcur, k = up_level(cur, dcur, e2, 6 * w, 2 * w, k)
+    cur, dcur, k = up_level(cur, dcur, e1, 3 * w, w, k)
+    y, dy = _conv(tape, cur, dcur, P[k], P[k + 1], G[k], G[k + 1], 0, 1)
+    target = noise.reshape(y.shape).astype(np.float32)
+    loss = o.mse_fwd(y, target)
+    o.mse_bwd(y, target, dy)
+    tape.backward()
+    grads = [g.ravel().copy() for g in G]
+    raw = [g.copy() for g in grads]
+    steps = steps or [1] * len(grads)
+    clip, new_p, m, v = clip_and_update([p.ravel() for p in P], grads, steps, lr, clip_norm)
+    return dict(loss=loss, grads=raw, clipped=grads, clip=clip, params=new_p, m=m, v=v)

@@ -30,24 +30,30 @@ def _session(**kw):
     return Session(**kw)
 
 
-def _check_step(s, ref, p0, lr, exact):
+def _check_step(s, ref, p0, lr, exact, rtol=RTOL_TC):
     n = len(s.param_names)
     gnorm = np.sqrt(sum(float(np.sum(np.asarray(g, np.float64) ** 2)) for g in ref["clipped"]))
     for i in range(n):
         g = s.read_param(i, 1)   # clipped gradient written back by the update
         r = ref["clipped"][i]
         if exact:
-            assert rel_err(g, r) <= 1e-4, (s.param_names[i], rel_err(g, r))
+            floor = np.linalg.norm(g - r) <= 1e-5 * gnorm
+            assert rel_err(g, r) <= 1e-4 or floor, (s.param_names[i], rel_err(g, r))
         else:
             floor = np.linalg.norm(g - r) <= 1e-4 * gnorm
-            assert norm_err(g, r) <= RTOL_TC or floor, (s.param_names[i], norm_err(g, r))
+            assert norm_err(g, r) <= rtol or floor, (s.param_names[i], norm_err(g, r))
         m = s.read_param(i, 2)
-        assert norm_err(m, ref["m"][i]) <= (1e-4 if exact else RTOL_TC) or \
+        assert norm_err(m, ref["m"][i]) <= (1e-4 if exact else rtol) or \
             np.linalg.norm(m - ref["m"][i]) <= 1e-4 * 0.1 * gnorm, s.param_names[i]
         w = s.read_param(i, 0)
         diff = np.abs((w - p0[i]) - (ref["params"][i] - p0[i]))
         assert np.max(diff) <= 2.05 * lr, s.param_names[i]
-        assert np.mean(diff > 0.05 * lr) <= (0.001 if exact else 0.02), (s.param_names[i], np.mean(diff > 0.05 * lr))
+        # a tensor whose exact gradient vanishes (a bias right before a
+        # GroupNorm of one channel per group, the query bias) moves by noise
+        # amplified to ~lr by Adam's normalisation: only the bound above holds
+        if np.linalg.norm(r) > 1e-4 * gnorm:
+            assert np.mean(diff > 0.05 * lr) <= (0.001 if exact else 0.02), \
+                (s.param_names[i], np.mean(diff > 0.05 * lr))
         assert s.param_step(i) == 2
 
 
@@ -138,6 +144,32 @@ def test_encdec_step_matches_oracle(cuda, rng, fused):
                              cfg["heads"], cfg["ffn"], cfg["layers"], cfg["vocab"], lr=lr)
     assert abs(loss - ref["loss"]) <= 1e-4 * abs(ref["loss"]), (loss, ref["loss"])
     _check_step(s, ref, p0, lr, exact=False)
+
+
+@pytest.mark.parametrize("gemm_mode", [1, 0], ids=["fp32", "tf32"])
+def test_unet_step_matches_oracle(cuda, rng, gemm_mode):
+    """configs[3] structure at a small size: ResidualBlocks (Conv2D,
+    GroupNorm(8), SiLU, time-MLP Broadcast_Channel, 1x1 skip), stride-2
+    downsampling, Conv2DT upsampling with CopyCrop skips, MSE, clip, AdamW.
+    fp32 GEMM mode: 1e-4 per tensor.  TF32: the error of 13 convolution +
+    GroupNorm layers compounds on the way back to the first convolution,
+    so the bound is 5e-3 per tensor there (2e-3 holds for the encoder)."""
+    from oracle import graphs
+    cfg = dict(batch=2, channels=3, image_size=16, base_width=8, t_embed=32, timestep=500)
+    lr = 1e-3
+    s = _session(config=4, lr=lr, clip_norm=1.0, seed=9, gemm_mode=gemm_mode, **cfg)
+    p0 = [(rng.standard_normal(n) * 0.1).astype(np.float32) for n in s.param_sizes]
+    for i, p in enumerate(p0):
+        s.write_param(i, p)
+    n_img = cfg["batch"] * cfg["channels"] * cfg["image_size"] ** 2
+    x_t = rng.standard_normal(n_img).astype(np.float32)
+    noise = rng.standard_normal(n_img).astype(np.float32)
+    s.inputs["x_t"][:] = x_t
+    s.inputs["noise"][:] = noise
+    loss = s.step()
+    ref = graphs.unet_step(p0, x_t, noise, lr=lr, **cfg)
+    assert abs(loss - ref["loss"]) <= 1e-4 * abs(ref["loss"]), (loss, ref["loss"])
+    _check_step(s, ref, p0, lr, exact=gemm_mode == 1, rtol=5e-3)
 
 
 def test_graph_replay_equals_eager(cuda, rng):
