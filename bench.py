@@ -298,6 +298,68 @@ def run_sweep(args):
                       "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
 
 
+# ------------------------------------------------------------ U-Net workload
+def run_unet(args):
+    """configs[3] (single GPU): DDPM noise-prediction step on 32 x 3 x 64 x
+    64 images, widths 64/128/256, time embedding 256.  x_t = sqrt(abar) x0
+    + sqrt(1 - abar) eps with x0, eps ~ N(0, 1) and the linear beta schedule
+    1e-4 .. 0.02 at the session's timestep; the step is zero_grad + forward
+    + backward + clip(1.0) + AdamW, replayed as a captured CUDA graph."""
+    import numpy as np
+    import torch
+
+    from ml_engine_b200.session import Session
+    dev = torch.device("cuda", 0)
+    B, C, S = 32, 3, 64
+    t = 500
+    betas = np.linspace(1e-4, 0.02, 1000)
+    abar = float(np.prod(1.0 - betas[: t + 1]))
+    s = Session.unet(batch=B, channels=C, image_size=S, base_width=64, t_embed=256, timestep=t, lr=1e-3, adamw=1,
+                     clip_norm=1.0, seed=4321)
+    rng = np.random.default_rng(7)
+    pool = []
+    for _ in range(4):
+        x0 = rng.standard_normal(B * C * S * S).astype(np.float32)
+        eps = rng.standard_normal(B * C * S * S).astype(np.float32)
+        pool.append(((np.sqrt(abar) * x0 + np.sqrt(1 - abar) * eps).astype(np.float32), eps))
+    stream = torch.cuda.ExternalStream(s.stream, device=dev)
+
+    def feed(i):
+        s.inputs["x_t"][:], s.inputs["noise"][:] = pool[i % len(pool)]
+
+    feed(0)
+    s.step()
+    s.capture()
+    for i in range(max(args.warmup, 3)):
+        feed(i)
+        s.step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        s.step(upload=False, read_loss=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for i in range(args.steps):
+        feed(i)
+        loss = s.step(upload=True, read_loss=True)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e2.elapsed_time(e3) / args.steps
+    print(json.dumps({"metric": "train images/s (fwd+bwd+AdamW), configs[3] U-Net", "value": B * 1e3 / ms,
+                      "unit": "images/s", "steps_per_s": 1e3 / ms, "ms_per_step": ms, "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "dtype": "f32 (tf32 tensor-core products)", "data": "synthetic",
+                      "config": {"workload": "configs[3]: U-Net 32x3x64x64, widths 64/128/256, t_embed 256",
+                                 "global_batch": B},
+                      "e2e": {"value": B * 1e3 / e2e_ms, "unit": "images/s", "ms_per_step": e2e_ms,
+                              "h2d_bytes_per_step": 2 * B * C * S * S * 4, "d2h_bytes_per_step": 4,
+                              "loss_last": loss}}), flush=True)
+    s.close()
+
+
 # ------------------------------------------------------------ native arm
 def run_native(args, rank, world, local_rank):
     import numpy as np
@@ -412,11 +474,16 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="configs[4] kernel sweep, one JSON line per case")
+    ap.add_argument("--config", default="encoder", choices=["encoder", "unet"],
+                    help="encoder: configs[1], the benchmark line; unet: configs[3] on one GPU")
     ap.add_argument("--roofline-only", action="store_true",
                     help="run only the roofline kernel pair (3 + 2 pairs; for a profiler capture)")
     args = ap.parse_args()
     if args.sweep:
         run_sweep(args)
+        return
+    if args.config == "unet":
+        run_unet(args)
         return
     if args.roofline_only:
         import torch

@@ -404,19 +404,22 @@ int mle_swap_dims(const float* in, float* out, int a, int b, int c, int mode, ml
 /* Convolute2D (Engine/engine.cu:3732-3817): weights [cout][cin][kh][kw],
  * x [batch][cin][h][w], y [batch][cout][OH][OW].
  *   forward : y = conv(x) (+ bias) (assigned, CV2D Engine/kernels.cu:985-1019);
- *             ws receives the im2col columns of x
- *             (mle_conv2d_workspace_floats floats) and must still hold them
- *             when the backward runs;
+ *             ws (mle_conv2d_workspace_floats floats) receives what the
+ *             backward reads of x (shifted copies of x for the stride-1
+ *             implicit GEMM, else its im2col columns) and must still hold
+ *             it when the backward runs;
  *   backward: dw = sum over the batch (assigned, GV2D :1021-1051), db +=
  *             channel sums (Channel_Squeeze1D :1734-1761), dx += (CV2D_GradInput
- *             :1053-1089); any of dx, dw, db may be NULL; ws is consumed. */
-int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int kh, int kw, int pad, int stride);
+ *             :1053-1089); x is the forward's input; any of dx, dw, db may be
+ *             NULL; ws is consumed. */
+int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad,
+                                    int stride);
 int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y, float* ws, int batch,
                    int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
                    mle_stream_t stream);
-int mle_conv2d_bwd(const float* wgt, const float* dy, float* dx, float* dw, float* db, float* ws,
-                   int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
-                   mle_stream_t stream);
+int mle_conv2d_bwd(const float* x, const float* wgt, const float* dy, float* dx, float* dw, float* db,
+                   float* ws, int batch, int cin, int h, int w, int cout, int kh, int kw, int pad,
+                   int stride, mle_stream_t stream);
 
 /* Convolute2DT (Engine/engine.cu:3828-3912): weights [cout][cin][kh][kw],
  * x [batch][cin][h][w], y [batch][cout][OH][OW] with OH from

@@ -746,7 +746,7 @@ graph Convolute2D::forward(const graph& X) {
     auto node = std::make_shared<NodeBackProp>(name, batch, out, outR, outC, 1);
     node->inputs = {X};
     GraphOperations::GB += (double)node->total * sizeof(float) / (1ULL << 30);
-    const int64_t wsn = mle_conv2d_workspace_floats(batch, inp, a, b, c, d, pad, stride);
+    const int64_t wsn = mle_conv2d_workspace_floats(batch, inp, a, b, out, c, d, pad, stride);
     float* ws = arena_alloc(ARENA_WS, wsn, name + " columns");
     NodeBackProp *nd = node.get(), *xp = X.get();
     AdamParameter *W = &W1, *B = &B1;
@@ -757,8 +757,8 @@ graph Convolute2D::forward(const graph& X) {
     };
     node->backward = [=]() {
         // dW assigned (GV2D), dB += (Channel_Squeeze1D), dX += (CV2D_GradInput)
-        check(mle_conv2d_bwd(W->output, nd->grad, xp->grad, W->grad, B->grad, ws, batch, ci, a, b, co, kh, kw, p, s,
-                             st()),
+        check(mle_conv2d_bwd(xp->output, W->output, nd->grad, xp->grad, W->grad, B->grad, ws, batch, ci, a, b, co, kh,
+                             kw, p, s, st()),
               "Weight + Bias + Input Gradient in " + nd->op_name);
     };
     conv_param_lambdas(node, W, B);

@@ -20,6 +20,8 @@
 // reference's order.
 #include <string.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemm.cuh"
 
@@ -80,6 +82,61 @@ __global__ void col2im_kernel(const float* __restrict__ cols, float* __restrict_
     }
 }
 
+// dst[b][n][c][y][x] = src[n][c][y][x + b + shift] (0 outside the source
+// row), b < KW, x < WD: the horizontally shifted copies an implicit-GEMM
+// convolution reads its taps from.  One thread per 4 consecutive x of one
+// row; WD % 4 == 0.
+__global__ void shift_copies_kernel(const float* __restrict__ src, float* __restrict__ dst, int rows, int WS, int WD,
+                                    int KW, int shift, int64_t copy_stride) {
+    pdl_entry();
+    const int q4 = WD >> 2;
+    const int64_t total = (int64_t)rows * q4;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        const int row = (int)(i / q4);
+        const int x0 = (int)(i - (int64_t)row * q4) * 4;
+        const float* s = src + (int64_t)row * WS;
+        float v[4 + 15];
+        const int lo = x0 + shift;
+#pragma unroll 4
+        for (int u = 0; u < KW + 3; ++u) {
+            const int xs = lo + u;
+            v[u] = (xs >= 0 && xs < WS) ? __ldg(s + xs) : 0.f;
+        }
+        float* d = dst + (int64_t)row * WD + x0;
+        for (int b = 0; b < KW; ++b)
+            *reinterpret_cast<float4*>(d + (int64_t)b * copy_stride) = make_float4(v[b], v[b + 1], v[b + 2], v[b + 3]);
+    }
+}
+
+// Weight layouts for the implicit GEMM (taps t = kh*KW + kw, T taps):
+//   mode 0: out[t][co][ld] = w[co][ci][t]          (0 for ci >= Cin)
+//   mode 1: out[t][ci][ld] = w[co][ci][T - 1 - t]  (0 for co >= Cout)
+//   mode 2: out[co][ci][t] = in[t][co][ci] (row pitch ld)  -- dW back to [Cout][Cin][KH][KW]
+__global__ void conv_weight_pack_kernel(const float* __restrict__ in, float* __restrict__ out, int Cout, int Cin,
+                                        int T, int ld, int mode, int64_t total) {
+    pdl_entry();
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        if (mode == 0) {
+            const int c = (int)(i % ld);
+            const int64_t r = i / ld;
+            const int co = (int)(r % Cout), t = (int)(r / Cout);
+            out[i] = c < Cin ? in[((int64_t)co * Cin + c) * T + t] : 0.f;
+        } else if (mode == 1) {
+            const int co = (int)(i % ld);
+            const int64_t r = i / ld;
+            const int ci = (int)(r % Cin), t = (int)(r / Cin);
+            out[i] = co < Cout ? in[((int64_t)co * Cin + ci) * T + (T - 1 - t)] : 0.f;
+        } else {
+            const int t = (int)(i % T);
+            const int64_t r = i / T;
+            const int ci = (int)(r % Cin), co = (int)(r / Cin);
+            out[i] = in[((int64_t)t * Cout + co) * ld + ci];
+        }
+    }
+}
+
 // out = in with two of its three dimensions exchanged:
 //   mode 0: [A][B][C] -> [B][A][C];  mode 1: [A][B][C] -> [A][C][B]
 __global__ void swap_dims_kernel(const float* __restrict__ in, float* __restrict__ out, int A, int B, int C, int mode,
@@ -112,6 +169,23 @@ int col2im(const float* cols, float* x, int n, int c, int h, int w, int kh, int 
     return launch_status();
 }
 
+int shift_copies(const float* src, float* dst, int rows, int ws, int wd, int kw, int shift, cudaStream_t st) {
+    const int64_t total = (int64_t)rows * (wd / 4);
+    if (total == 0) return MLE_OK;
+    launch_k(shift_copies_kernel, grid_for(total, kT), kT, 0, st, src, dst, rows, ws, wd, kw, shift,
+             (int64_t)rows * wd);
+    return launch_status();
+}
+
+int weight_pack(const float* in, float* out, int cout, int cin, int taps, int ld, int mode, cudaStream_t st) {
+    const int64_t total = mode == 0   ? (int64_t)taps * cout * ld
+                          : mode == 1 ? (int64_t)taps * cin * ld
+                                      : (int64_t)cout * cin * taps;
+    if (total == 0) return MLE_OK;
+    launch_k(conv_weight_pack_kernel, grid_for(total, kT), kT, 0, st, in, out, cout, cin, taps, ld, mode, total);
+    return launch_status();
+}
+
 int swap_dims(const float* in, float* out, int a, int b, int c, int mode, cudaStream_t st) {
     const int64_t total = (int64_t)a * b * c;
     if (total == 0) return MLE_OK;
@@ -121,6 +195,111 @@ int swap_dims(const float* in, float* out, int a, int b, int c, int mode, cudaSt
 
 bool conv_shape_ok(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride) {
     return batch > 0 && cin > 0 && h > 0 && w > 0 && cout > 0 && kh > 0 && kw > 0 && pad >= 0 && stride > 0;
+}
+
+int64_t r4(int64_t n) { return (n + 3) & ~int64_t(3); }
+
+// Implicit-GEMM plan of a stride-1 Convolute2D (ConvGemm, gemm.cuh):
+//   forward y = kind 1 over S = KW shifted copies of x (width OW), weights
+//               packed [tap][Cout][Cin4];
+//   dW        = kind 2 over the same S and dy, into [tap][Cout][Cin4], then
+//               unpacked to [Cout][Cin][KH][KW];
+//   dx       += kind 1 over KW shifted copies of dy (width W) with the taps
+//               flipped, weights packed [tap][Cin][Cout4], row offset KH-1-pad.
+// A 1x1 unpadded convolution reads x and dy in place.  The workspace holds
+// S (kept from the forward for the backward), the packed weights (also the
+// dW staging) and the copies of dy.
+struct ConvPlan {
+    int oh, ow, taps, cin4, cout4;
+    bool in_place;            // KW == 1 and pad == 0: no shifted copies
+    int64_t xs, wp, wd, dys;  // workspace offsets (floats)
+    int64_t floats;
+};
+
+ConvPlan conv_plan(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad) {
+    ConvPlan p;
+    p.oh = h + 2 * pad - kh + 1;
+    p.ow = w + 2 * pad - kw + 1;
+    p.taps = kh * kw;
+    p.cin4 = (int)r4(cin);
+    p.cout4 = (int)r4(cout);
+    p.in_place = kw == 1 && pad == 0;
+    const int64_t n_xs = p.in_place ? 0 : (int64_t)kw * batch * cin * h * p.ow;
+    const int64_t n_dys = p.in_place ? 0 : (int64_t)kw * batch * cout * p.oh * w;
+    p.xs = 0;
+    p.wp = r4(n_xs);
+    p.wd = p.wp + r4((int64_t)p.taps * cout * p.cin4);
+    p.dys = p.wd + r4((int64_t)p.taps * cin * p.cout4);
+    p.floats = p.dys + r4(n_dys);
+    return p;
+}
+
+ConvGemm conv_fwd_gemm(const ConvPlan& p, const float* x, const float* ws, float* y, int batch, int cin, int h,
+                       int cout, int kh, int kw, int pad) {
+    ConvGemm g;
+    memset(&g, 0, sizeof(g));
+    g.kind = 1;
+    g.A = ws + p.wp;
+    g.S = p.in_place ? x : ws + p.xs;
+    g.out = y;
+    g.M = cout;
+    g.C = cin;
+    g.HS = h;
+    g.WS = p.ow;
+    g.KH = kh;
+    g.KW = kw;
+    g.pad = pad;
+    g.nb = batch;
+    g.P = p.oh * p.ow;
+    g.lda = p.cin4;
+    return g;
+}
+
+ConvGemm conv_dw_gemm(const ConvPlan& p, const float* x, const float* dy, float* ws, int batch, int cin, int h,
+                      int cout, int kh, int kw, int pad) {
+    ConvGemm g = conv_fwd_gemm(p, x, ws, ws + p.wp, batch, cin, h, cout, kh, kw, pad);
+    g.kind = 2;
+    g.A = dy;
+    g.ldc = p.cin4;
+    return g;
+}
+
+ConvGemm conv_dx_gemm(const ConvPlan& p, const float* dy, float* ws, float* dx, int batch, int cin, int w,
+                      int cout, int kh, int kw, int pad) {
+    ConvGemm g;
+    memset(&g, 0, sizeof(g));
+    g.kind = 1;
+    g.A = ws + p.wd;
+    g.S = p.in_place ? dy : ws + p.dys;
+    g.out = dx;
+    g.M = cin;
+    g.C = cout;
+    g.HS = p.oh;
+    g.WS = w;
+    g.KH = kh;
+    g.KW = kw;
+    g.pad = kh - 1 - pad;
+    g.nb = batch;
+    g.P = (p.oh + kh - 1 - 2 * pad) * w;  // = h * w
+    g.lda = p.cout4;
+    g.accumulate = 1;
+    return g;
+}
+
+// The implicit path runs for stride 1 when all three products are supported
+// (tensor-core mode, widths whose 32-pixel blocks TMA can address).  The
+// choice depends only on the shape, the GEMM mode and x / ws, which the
+// forward and the backward share, so both take the same path; a gradient
+// pointer that TMA cannot address then fails the call.
+bool conv_implicit_ok(const float* x, float* ws, int batch, int cin, int h, int w, int cout, int kh, int kw, int pad,
+                      int stride) {
+    if (stride != 1 || kw - 1 - pad < 0 || kh - 1 - pad < 0) return false;
+    const ConvPlan p = conv_plan(batch, cin, h, w, cout, kh, kw, pad);
+    if (p.oh <= 0 || p.ow <= 0) return false;
+    const ConvGemm f = conv_fwd_gemm(p, x, ws, ws, batch, cin, h, cout, kh, kw, pad);
+    const ConvGemm d = conv_dx_gemm(p, p.in_place ? x : ws, ws, ws, batch, cin, w, cout, kh, kw, pad);
+    const ConvGemm g = conv_dw_gemm(p, x, ws, ws, batch, cin, h, cout, kh, kw, pad);
+    return conv_gemm_supported(f) && conv_gemm_supported(d) && conv_gemm_supported(g);
 }
 
 }  // namespace
@@ -158,10 +337,14 @@ int mle_swap_dims(const float* in, float* out, int a, int b, int c, int mode, ml
     return swap_dims(in, out, a, b, c, mode, as_stream(stream));
 }
 
-int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int kh, int kw, int pad, int stride) {
+int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride) {
     const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
-    if (batch <= 0 || cin <= 0 || oh <= 0 || ow <= 0) return -1;
-    return (int64_t)batch * cin * kh * kw * oh * ow;
+    if (batch <= 0 || cin <= 0 || cout <= 0 || kh <= 0 || kw <= 0 || oh <= 0 || ow <= 0) return -1;
+    // room for either path: the choice also depends on the GEMM mode and
+    // pointer alignment at call time
+    int64_t n = (int64_t)batch * cin * kh * kw * oh * ow;
+    if (stride == 1) n = std::max(n, conv_plan(batch, cin, h, w, cout, kh, kw, pad).floats);
+    return n;
 }
 
 int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y, float* ws, int batch, int cin,
@@ -171,30 +354,67 @@ int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y
     if (oh <= 0 || ow <= 0) return MLE_ERR_ARG;
     cudaStream_t st = as_stream(stream);
     const int64_t P = (int64_t)oh * ow, K = (int64_t)cin * kh * kw;
-    int s = im2col(x, ws, batch, cin, h, w, kh, kw, oh, ow, pad, stride, st);
-    if (s) return s;
-    // y[n][Cout][P] = W[Cout][K] * cols[n][K][P]
-    s = mle_gemm(wgt, ws, y, nullptr, batch, cout, P, K, K, P, P, 0, K * P, cout * P, 0, 0, 1.0f, 0.0f, stream);
+    int s;
+    if (conv_implicit_ok(x, ws, batch, cin, h, w, cout, kh, kw, pad, stride)) {
+        const ConvPlan p = conv_plan(batch, cin, h, w, cout, kh, kw, pad);
+        if (!p.in_place) {
+            s = shift_copies(x, ws + p.xs, batch * cin * h, w, p.ow, kw, -pad, st);
+            if (s) return s;
+        }
+        s = weight_pack(wgt, ws + p.wp, cout, cin, p.taps, p.cin4, 0, st);
+        if (s) return s;
+        s = run_conv_gemm(conv_fwd_gemm(p, x, ws, y, batch, cin, h, cout, kh, kw, pad), st);
+    } else {
+        s = im2col(x, ws, batch, cin, h, w, kh, kw, oh, ow, pad, stride, st);
+        if (s) return s;
+        // y[n][Cout][P] = W[Cout][K] * cols[n][K][P]
+        s = mle_gemm(wgt, ws, y, nullptr, batch, cout, P, K, K, P, P, 0, K * P, cout * P, 0, 0, 1.0f, 0.0f, stream);
+    }
     if (s || !bias) return s;
     return mle_channel_bias_fwd(y, bias, y, batch, cout, P, stream);
 }
 
-int mle_conv2d_bwd(const float* wgt, const float* dy, float* dx, float* dw, float* db, float* ws, int batch, int cin,
-                   int h, int w, int cout, int kh, int kw, int pad, int stride, mle_stream_t stream) {
-    if (!wgt || !dy || !ws || !conv_shape_ok(batch, cin, h, w, cout, kh, kw, pad, stride)) return MLE_ERR_ARG;
+int mle_conv2d_bwd(const float* x, const float* wgt, const float* dy, float* dx, float* dw, float* db, float* ws,
+                   int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
+                   mle_stream_t stream) {
+    if (!x || !wgt || !dy || !ws || !conv_shape_ok(batch, cin, h, w, cout, kh, kw, pad, stride)) return MLE_ERR_ARG;
     const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
     if (oh <= 0 || ow <= 0) return MLE_ERR_ARG;
     cudaStream_t st = as_stream(stream);
     const int64_t P = (int64_t)oh * ow, K = (int64_t)cin * kh * kw;
     int s;
+    if (db) {
+        s = mle_channel_bias_bwd(dy, nullptr, db, batch, cout, P, stream);
+        if (s) return s;
+    }
+    if (conv_implicit_ok(x, ws, batch, cin, h, w, cout, kh, kw, pad, stride)) {
+        const ConvPlan p = conv_plan(batch, cin, h, w, cout, kh, kw, pad);
+        if (dw) {
+            // dW staged as [tap][Cout][Cin4] (reduce-added over images and
+            // pixels), then assigned in the reference layout (as GV2D)
+            if (cudaMemsetAsync(ws + p.wp, 0, sizeof(float) * (size_t)p.taps * cout * p.cin4, st) != cudaSuccess)
+                return launch_status();
+            s = run_conv_gemm(conv_dw_gemm(p, x, dy, ws, batch, cin, h, cout, kh, kw, pad), st);
+            if (s) return s;
+            s = weight_pack(ws + p.wp, dw, cout, cin, p.taps, p.cin4, 2, st);
+            if (s) return s;
+        }
+        if (dx) {
+            if (!p.in_place) {
+                s = shift_copies(dy, ws + p.dys, batch * cout * oh, ow, w, kw, -(kw - 1 - pad), st);
+                if (s) return s;
+            }
+            s = weight_pack(wgt, ws + p.wd, cout, cin, p.taps, p.cout4, 1, st);
+            if (s) return s;
+            return run_conv_gemm(conv_dx_gemm(p, dy, ws, dx, batch, cin, w, cout, kh, kw, pad), st);
+        }
+        return MLE_OK;
+    }
     if (dw) {
+        // the forward left cols(x) in ws
         // dW[Cout][K] = sum_n dy[n][Cout][P] * cols[n][K][P]^T  (assigned, as GV2D)
         if (cudaMemsetAsync(dw, 0, sizeof(float) * (size_t)(cout * K), st) != cudaSuccess) return launch_status();
         s = mle_gemm(dy, ws, dw, nullptr, batch, cout, K, P, P, P, K, cout * P, K * P, 0, 0, 1, 1.0f, 1.0f, stream);
-        if (s) return s;
-    }
-    if (db) {
-        s = mle_channel_bias_bwd(dy, nullptr, db, batch, cout, P, stream);
         if (s) return s;
     }
     if (dx) {

@@ -21,7 +21,31 @@ struct GemmProblem {
     int mode;  // 0 assign, 1 +=, 2 atomic add
 };
 
+// Implicit-GEMM convolution at stride 1 over KW horizontally shifted
+// copies of an image, S[kw][n][c][y][x] = src[n][c][y][x + kw + shift]
+// (0 outside), so that every tap's operand tile is a TMA box of S, whose
+// image planes are addressed flattened: the tap moves the pixel index by
+// (kh - pad) whole rows, a multiple of 4 elements when WS % 4 == 0, and rows
+// above or below the image read as 0:
+//   kind 1: C[n][m][p] (= or +=) sum over taps t = (kh, kw) and channels c
+//           of A[t][m][c] * S[kw][n][c][oy + kh - pad][ox],  p = oy*WS + ox
+//   kind 2: C[t][m][c] += sum over images n and pixels p of
+//           A[n][m][p] * S[kw][n][c][oy + kh - pad][ox]
+struct ConvGemm {
+    int kind;
+    const float* A;  // kind 1: [KH*KW][M][lda]; kind 2: [nb][M][P]
+    const float* S;  // [KW][nb][C][HS][WS]
+    float* out;      // kind 1: [nb][M][P]; kind 2: [KH*KW][M][ldc]
+    int M, C, HS, WS, KH, KW, pad, nb;
+    int P;           // pixels per image of the output (kind 1) / of A (kind 2)
+    int64_t lda, ldc;
+    int accumulate;  // kind 1 only (kind 2 always adds)
+};
+
 int simt_gemm(const GemmProblem& p, cudaStream_t st);
+// false when the shapes or pointers rule out the tensor-core implicit path
+bool conv_gemm_supported(const ConvGemm& c);
+int run_conv_gemm(const ConvGemm& c, cudaStream_t st);
 int run_gemm(const GemmProblem& p, cudaStream_t st);
 int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st);
 

@@ -60,6 +60,14 @@ struct EpiParams {
     int vec;                          // C rows (and bias) 16-byte aligned
     int tma_epi;                      // C leaves through bulk tensor stores / reduce-adds (tmC)
     int c_has_b, c_has_c;             // C varies over batch / channel (tensor-map coordinates)
+    // implicit convolution (ConvGemm in gemm.cuh); 0 = plain GEMM.
+    //   1: k-block kb = (tap, channel block), tap = kb / cv_cblk; B boxes
+    //      come from the shifted copies at (p + (kh - pad)*cv_w, c, kw*nb + n)
+    //      with p the output pixel (rows of width cv_w, flattened)
+    //   2: tile column index = (tap, channel block of BN), tap = n / cv_cblk,
+    //      stored as the tile's channel index (C's third coordinate); k = pixel
+    int conv;
+    int cv_kw, cv_pad, cv_w, cv_cblk, cv_nb;
 };
 
 // Output tile `t` of the persistent walk: n fastest, then m, then (batch,
@@ -96,6 +104,10 @@ __device__ __forceinline__ Tile tile_at(const EpiParams& ep, int64_t t, int BN) 
     x.bidx = (int)(z / ep.channels);
     x.m0 = m * 128;
     x.n0 = n * BN;
+    if (ep.conv == 2) {
+        x.cidx = n / ep.cv_cblk;
+        x.n0 = (n - x.cidx * ep.cv_cblk) * BN;
+    }
     const int kb_total = (ep.K + 31) / 32;
     x.kb_begin = split * ep.kb_per_split;
     int kb_end = x.kb_begin + ep.kb_per_split;
@@ -363,19 +375,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint8_t* sb = sa + L::A_BYTES;
                     const int k0 = (x.kb_begin + i) * BK;
                     mbar_arrive_expect_tx(&full[s], (uint32_t)L::STAGE_BYTES);
-                    if (A_MN) {
-#pragma unroll
-                        for (int j = 0; j < BM / 32; ++j)
-                            tma_load_4d(tmA, &full[s], sa + j * 4096, x.m0 + 32 * j, k0, a_c, a_b);
-                    } else {
-                        tma_load_4d(tmA, &full[s], sa, k0, x.m0, a_c, a_b);
-                    }
-                    if (B_MN) {
+                    if (!A_MN && B_MN && ep.conv == 1) {
+                        // weights [tap][m][c]; the pixels of a tap are the output
+                        // pixels moved by whole rows in the flattened image plane
+                        const int kb = x.kb_begin + i;
+                        const int tap = kb / ep.cv_cblk, c0 = (kb - tap * ep.cv_cblk) * BK;
+                        const int kh = tap / ep.cv_kw, kw = tap - kh * ep.cv_kw;
+                        const int zc = kw * ep.cv_nb + x.bidx;
+                        const int dp = (kh - ep.cv_pad) * ep.cv_w;
+                        tma_load_4d(tmA, &full[s], sa, c0, x.m0, tap, 0);
 #pragma unroll
                         for (int j = 0; j < BN / 32; ++j)
-                            tma_load_4d(tmB, &full[s], sb + j * 4096, x.n0 + 32 * j, k0, b_c, b_b);
+                            tma_load_4d(tmB, &full[s], sb + j * 4096, x.n0 + 32 * j + dp, c0, zc, 0);
+                    } else if (!A_MN && !B_MN && ep.conv == 2) {
+                        // B rows = channels x.n0.. of tap x.cidx at pixels k0..k0+31
+                        const int kh = x.cidx / ep.cv_kw, kw = x.cidx - kh * ep.cv_kw;
+                        tma_load_4d(tmA, &full[s], sa, k0, x.m0, a_c, a_b);
+                        tma_load_4d(tmB, &full[s], sb, k0 + (kh - ep.cv_pad) * ep.cv_w, x.n0, kw * ep.cv_nb + x.bidx,
+                                    0);
                     } else {
-                        tma_load_4d(tmB, &full[s], sb, k0, x.n0, b_c, b_b);
+                        if (A_MN) {
+#pragma unroll
+                            for (int j = 0; j < BM / 32; ++j)
+                                tma_load_4d(tmA, &full[s], sa + j * 4096, x.m0 + 32 * j, k0, a_c, a_b);
+                        } else {
+                            tma_load_4d(tmA, &full[s], sa, k0, x.m0, a_c, a_b);
+                        }
+                        if (B_MN) {
+#pragma unroll
+                            for (int j = 0; j < BN / 32; ++j)
+                                tma_load_4d(tmB, &full[s], sb + j * 4096, x.n0 + 32 * j, k0, b_c, b_b);
+                        } else {
+                            tma_load_4d(tmB, &full[s], sb, k0, x.n0, b_c, b_b);
+                        }
                     }
                     issued[s] = true;
                     last_parity[s] = ph;
@@ -632,6 +664,24 @@ static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner
                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+// 4-D fp32 tensor map with explicit extents, element strides of dims 1..3
+// and box.
+static bool encode_map(CUtensorMap* map, const float* base, const int64_t dims[4], const int64_t strides[3],
+                       const int box[4], CUtensorMapSwizzle swizzle) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return false;
+    cuuint64_t d[4], st[3];
+    cuuint32_t b[4], e[4] = {1, 1, 1, 1};
+    for (int i = 0; i < 4; ++i) {
+        d[i] = (cuuint64_t)dims[i];
+        b[i] = (cuuint32_t)box[i];
+    }
+    for (int i = 0; i < 3; ++i) st[i] = (cuuint64_t)(strides[i] * 4);
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), d, st, b, e,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
@@ -927,6 +977,119 @@ int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st)
         grp.tile_start[i + 1] = grp.tile_start[i] + grp.ep[i].tiles;
     }
     return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st);
+}
+
+bool conv_gemm_supported(const ConvGemm& c) {
+    if (g_gemm_mode != MLE_GEMM_MODE_TF32 || tc::get_encode() == nullptr) return false;
+    if (c.kind != 1 && c.kind != 2) return false;
+    if (c.M <= 0 || c.C <= 0 || c.HS <= 0 || c.WS <= 0 || c.KH <= 0 || c.KW <= 0 || c.nb <= 0 || c.P <= 0)
+        return false;
+    // a tap moves the flattened pixel index by whole rows, which keeps TMA
+    // x coordinates at multiples of 4 elements (16 bytes)
+    if (c.WS & 3) return false;
+    if ((c.P & 3) || !aligned16(c.A) || !aligned16(c.S) || !aligned16(c.out)) return false;
+    if (c.kind == 1 && ((c.lda & 3) || c.lda < c.C)) return false;
+    if (c.kind == 2 && ((c.ldc & 3) || c.ldc < c.C)) return false;
+    return true;
+}
+
+int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
+    using namespace tc;
+    if (!conv_gemm_supported(c)) return MLE_ERR_ARG;
+    const int taps = c.KH * c.KW;
+    // tile choice on the equivalent plain products
+    GemmProblem q;
+    memset(&q, 0, sizeof(q));
+    q.M = c.M;
+    q.channels = 1;
+    q.alpha = 1.f;
+    if (c.kind == 1) {
+        q.N = c.P;
+        q.K = taps * ((c.C + BK - 1) / BK) * BK;
+        q.nbatch = c.nb;
+        q.ldc = c.P;
+        q.c_sb = (int64_t)c.M * c.P;
+        q.mode = c.accumulate ? EPI_ACCUM : EPI_ASSIGN;
+    } else {
+        q.N = c.C;
+        q.K = c.P;
+        q.nbatch = c.nb * taps;
+        q.ldc = c.ldc;
+        q.mode = EPI_ACCUM;
+    }
+    int BN, splits;
+    choose_tiles(&q, 1, BN, splits);
+    const int kb_total = (q.K + BK - 1) / BK;
+    const int kb_per_split = (kb_total + splits - 1) / splits;
+    splits = (kb_total + kb_per_split - 1) / kb_per_split;
+
+    GemmGroup grp;
+    memset(&grp, 0, sizeof(grp));
+    EpiParams& ep = grp.ep[0];
+    ep.C = c.out;
+    ep.alpha = 1.f;
+    ep.M = c.M;
+    ep.K = q.K;
+    ep.channels = 1;
+    ep.splits = splits;
+    ep.kb_per_split = kb_per_split;
+    ep.m_tiles = (c.M + BM - 1) / BM;
+    ep.conv = c.kind;
+    ep.cv_kw = c.KW;
+    ep.cv_pad = c.pad;
+    ep.cv_w = c.WS;
+    ep.cv_nb = c.nb;
+    // shifted copies as [KW*nb][C][HS*WS]: rows outside the image read as 0
+    const int64_t plane = (int64_t)c.HS * c.WS;
+    const int64_t s_dims[4] = {plane, c.C, (int64_t)c.KW * c.nb, 1};
+    const int64_t s_str[3] = {plane, plane * c.C, plane * c.C * c.KW * c.nb};
+    if (c.kind == 1) {
+        ep.N = c.P;
+        ep.ldc = c.P;
+        ep.c_stride_b = c.nb > 1 ? (int64_t)c.M * c.P : 0;
+        ep.cv_cblk = (c.C + BK - 1) / BK;
+        ep.n_tiles = (c.P + BN - 1) / BN;
+        ep.mode = splits > 1 ? EPI_ATOMIC : (c.accumulate ? EPI_ACCUM : EPI_ASSIGN);
+        const int64_t a_dims[4] = {c.lda, c.M, taps, 1};
+        const int64_t a_str[3] = {c.lda, (int64_t)c.M * c.lda, (int64_t)taps * c.M * c.lda};
+        const int a_box[4] = {BK, BM, 1, 1};
+        const int s_box[4] = {32, BK, 1, 1};
+        if (!encode_map(&grp.a[0], c.A, a_dims, a_str, a_box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode_map(&grp.b[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+            return MLE_ERR_ARG;
+        const int64_t c_dims[4] = {c.P, c.M, 1, c.nb};
+        const int64_t c_str[3] = {c.P, (int64_t)c.M * c.P, (int64_t)c.M * c.P};
+        const int c_box[4] = {32, 32, 1, 1};
+        ep.tma_epi = encode_map(&grp.c[0], c.out, c_dims, c_str, c_box, CU_TENSOR_MAP_SWIZZLE_128B) ? 1 : 0;
+        ep.c_has_b = c.nb > 1;
+    } else {
+        ep.N = c.C;
+        ep.ldc = c.ldc;
+        ep.c_stride_c = (int64_t)c.M * c.ldc;
+        ep.cv_cblk = (c.C + BN - 1) / BN;
+        ep.n_tiles = taps * ep.cv_cblk;
+        ep.mode = EPI_ATOMIC;
+        ep.a_has_b = c.nb > 1;
+        const int64_t a_dims[4] = {c.P, c.M, 1, c.nb};
+        const int64_t a_str[3] = {c.P, (int64_t)c.M * c.P, (int64_t)c.M * c.P};
+        const int a_box[4] = {BK, BM, 1, 1};
+        const int s_box[4] = {32, BN, 1, 1};
+        if (!encode_map(&grp.a[0], c.A, a_dims, a_str, a_box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode_map(&grp.b[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return MLE_ERR_ARG;
+        const int64_t c_dims[4] = {c.C, c.M, taps, 1};
+        const int64_t c_str[3] = {c.ldc, (int64_t)c.M * c.ldc, (int64_t)taps * c.M * c.ldc};
+        const int c_box[4] = {32, 32, 1, 1};
+        ep.tma_epi = encode_map(&grp.c[0], c.out, c_dims, c_str, c_box, CU_TENSOR_MAP_SWIZZLE_128B) ? 1 : 0;
+        ep.c_has_c = 1;
+    }
+    ep.vec = ((ep.ldc & 3) == 0) && aligned16(c.out);
+    ep.tiles = (int64_t)ep.m_tiles * ep.n_tiles * c.nb * splits;
+    grp.n = 1;
+    grp.tile_start[0] = 0;
+    grp.tile_start[1] = ep.tiles;
+    if (ep.tiles == 0) return MLE_OK;
+    return dispatch(grp, false, c.kind == 1, BN, st);
 }
 
 }  // namespace mle

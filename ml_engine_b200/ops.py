@@ -269,8 +269,8 @@ def convT_out_size(n, k, pad, stride):
 
 def conv2d_workspace(x, w, pad, stride):
     n, cin, h, wd = x.shape
-    _, _, kh, kw = w.shape
-    nf = kernels().mle_conv2d_workspace_floats(n, cin, h, wd, kh, kw, pad, stride)
+    cout, _, kh, kw = w.shape
+    nf = kernels().mle_conv2d_workspace_floats(n, cin, h, wd, cout, kh, kw, pad, stride)
     if nf < 0:
         raise MLEError("conv2d: kernel does not fit the input")
     return torch.empty(nf, device=x.device, dtype=torch.float32)
@@ -278,18 +278,19 @@ def conv2d_workspace(x, w, pad, stride):
 
 def conv2d_fwd(x, w, bias, y, ws, pad, stride):
     """x [N,Cin,H,W], w [Cout,Cin,KH,KW], y [N,Cout,OH,OW] (assigned);
-    ws keeps the im2col columns for conv2d_bwd."""
+    ws keeps what conv2d_bwd reads of x."""
     n, cin, h, wd = x.shape
     cout, _, kh, kw = w.shape
     _call("mle_conv2d_fwd", _p(x), _p(w), _p(bias), _p(y), _p(ws), n, cin, h, wd, cout, kh, kw, pad, stride, _s())
 
 
-def conv2d_bwd(w, dy, dx, dw, db, ws, xshape, pad, stride):
-    """dw assigned, db and dx accumulated; ws from conv2d_fwd (consumed)."""
-    n, cin, h, wd = xshape
+def conv2d_bwd(x, w, dy, dx, dw, db, ws, pad, stride):
+    """dw assigned, db and dx accumulated; x and ws as given to conv2d_fwd
+    (ws consumed)."""
+    n, cin, h, wd = x.shape
     cout, _, kh, kw = w.shape
-    _call("mle_conv2d_bwd", _p(w), _p(dy), _p(dx), _p(dw), _p(db), _p(ws), n, cin, h, wd, cout, kh, kw, pad, stride,
-          _s())
+    _call("mle_conv2d_bwd", _p(x), _p(w), _p(dy), _p(dx), _p(dw), _p(db), _p(ws), n, cin, h, wd, cout, kh, kw, pad,
+          stride, _s())
 
 
 def convT2d_workspace(x, w, pad, stride):

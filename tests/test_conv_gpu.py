@@ -12,10 +12,17 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 CONV = [  # N, Cin, H, W, Cout, K, pad, stride
-    (2, 3, 16, 16, 8, 3, 1, 1),      # first layer of a U-Net: K = 27 (CUDA-core GEMM)
-    (4, 16, 32, 32, 32, 3, 1, 1),    # 3x3, tensor cores
-    (2, 32, 17, 13, 16, 3, 1, 2),    # stride-2 downsampling, odd sizes
-    (2, 64, 8, 8, 32, 1, 0, 1),      # 1x1 skip projection
+    (2, 3, 16, 16, 8, 3, 1, 1),      # first layer of a U-Net: 3 channels, two rows per 32-pixel block
+    (4, 16, 32, 32, 32, 3, 1, 1),    # 3x3 implicit GEMM, one row per block
+    (2, 32, 17, 13, 16, 3, 1, 2),    # stride-2 downsampling, odd sizes (im2col)
+    (2, 64, 8, 8, 32, 1, 0, 1),      # 1x1 skip projection read in place
+    (2, 64, 64, 64, 64, 3, 1, 1),    # U-Net top level: 32 pixel tiles per image, half-height M tile
+    (2, 192, 16, 16, 160, 3, 1, 1),  # two M tiles, six channel blocks per tap
+    (2, 40, 12, 12, 24, 3, 1, 1),    # width 12: pixel blocks straddle rows
+    (2, 8, 10, 10, 8, 3, 1, 1),      # width 10: rows not 16-byte aligned, im2col
+    (3, 24, 8, 8, 3, 1, 0, 1),       # 3 output channels (the U-Net's output projection)
+    (2, 16, 4, 4, 16, 3, 1, 1),      # 16-pixel images: blocks run past the image
+    (2, 8, 32, 32, 16, 5, 2, 1),     # 5x5 taps
 ]
 CONVT = [  # N, Cin, H, W, Cout, K, pad, stride
     (2, 32, 8, 8, 16, 2, 0, 2),      # 2x2 stride-2 upsampling
@@ -60,7 +67,7 @@ def test_conv2d(cuda, rng, gemm_mode, case):
     ws = ops.conv2d_workspace(tx, tw, pad, stride)
     ops.conv2d_fwd(tx, tw, tb, y, ws, pad, stride)
     dx, dw, db = T(dx0, cuda), torch.full((Cout, Cin, K, K), 7.0, device=cuda), T(db0, cuda)
-    ops.conv2d_bwd(tw, T(dy, cuda), dx, dw, db, ws, x.shape, pad, stride)
+    ops.conv2d_bwd(tx, tw, T(dy, cuda), dx, dw, db, ws, pad, stride)
     tol = RTOL_TC if gemm_mode == 0 else 1e-5
     assert norm_err(H(y), orc.conv2d_fwd(x, w, b, pad, stride)) <= tol
     assert norm_err(H(dw), orc.conv2d_bwd_k(x, dy, w.shape, pad, stride)) <= tol      # assigned
