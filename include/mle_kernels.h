@@ -144,6 +144,12 @@ int mle_channel_bias_fwd(const float* x, const float* b, float* y, int batch, in
  * of Convolute2D/2DT backward (Engine/engine.cu:3768,3868). */
 int mle_channel_bias_bwd(const float* g, float* gx, float* gb, int batch, int channels,
                          int64_t spatial, mle_stream_t stream);
+/* The same sums for the first `first` channels only: Broadcast_Channel's
+ * backward launches Channel_Squeeze1D with one block per index of dim[3],
+ * so only channels [0, min(dim[3], C)) receive their sums
+ * (Engine/engine.cu:1435). */
+int mle_channel_bias_bwd_first(const float* g, float* gb, int batch, int channels, int first,
+                               int64_t spatial, mle_stream_t stream);
 
 /* Sinusoidal matrix positional encoding, y = x + PE (sin even / cos odd
  * columns).  Replaces MatPEncoding (Engine/kernels.cu:166-185). */

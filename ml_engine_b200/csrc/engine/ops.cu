@@ -215,17 +215,8 @@ graph GraphOperations::Broadcast_Channel(const graph& A, const graph& B) {
     node->backward = [=]() {
         check(mle_accumulate(nd->grad, ap->grad, nd->total, 1.0, st()), "Broadcast_Channel backward A");
         const int reduced = b < channels ? b : channels;
-        if (reduced == channels) {
-            check(mle_channel_bias_bwd(nd->grad, nullptr, bp->grad, batch, channels, (int64_t)a * b, st()),
-                  "Broadcast_Channel backward B");
-        } else {
-            // reduce only channels [0, reduced): view the tensor per sample as
-            // [reduced channels] + rest by running one sample at a time
-            for (int n = 0; n < batch; ++n)
-                check(mle_channel_bias_bwd(nd->grad + (int64_t)n * channels * a * b, nullptr, bp->grad, 1, reduced,
-                                           (int64_t)a * b, st()),
-                      "Broadcast_Channel backward B");
-        }
+        check(mle_channel_bias_bwd_first(nd->grad, bp->grad, batch, channels, reduced, (int64_t)a * b, st()),
+              "Broadcast_Channel backward B");
     };
     node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
     node->free = [nd]() { nd->clear(); };

@@ -71,6 +71,29 @@ inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// launch_k for kernels built of thread-block clusters of `cluster` CTAs
+// along x (gridDim.x a multiple of it).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kc(void (*kern)(KArgs...), dim3 grid, dim3 block, int cluster, cudaStream_t st,
+                             Args&&... args) {
+    prefer_max_shared(reinterpret_cast<const void*>(kern));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 inline unsigned grid_for(int64_t n, int per_block, int max_waves = 16) {
     int64_t blocks = (n + per_block - 1) / per_block;
     int64_t cap = (int64_t)kSMs * max_waves;

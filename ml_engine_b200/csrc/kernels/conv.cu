@@ -20,6 +20,8 @@
 // reference's order.
 #include <string.h>
 
+#include <stdint.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -30,55 +32,93 @@ namespace {
 
 constexpr int kT = 256;
 
-// cols[n][(c,kh,kw)][(oy,ox)]; one thread per column entry, (oy,ox) fastest
+constexpr int kRowThreads = 128;
+
+// cols[n][(c, kh, kw)][(oy, ox)]: blockIdx.y walks the column rows
+// (n, c, kh, kw), threads the output pixels of a row, Q consecutive ox each
+// (Q = 4 when OW % 4 == 0: one 16-byte store).  32-bit index arithmetic
+// within a row.
+template <int Q>
 __global__ void im2col_kernel(const float* __restrict__ x, float* __restrict__ cols, int C, int H, int W, int KH,
-                              int KW, int OH, int OW, int pad, int stride, int64_t total) {
+                              int KW, int OH, int OW, int pad, int stride, int rows) {
     pdl_entry();
-    const int64_t step = (int64_t)gridDim.x * blockDim.x;
-    const int64_t P = (int64_t)OH * OW, KK = (int64_t)KH * KW;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
-        const int64_t p = i % P;
-        int64_t r = i / P;
-        const int64_t k = r % (C * KK);
-        const int64_t n = r / (C * KK);
-        const int c = (int)(k / KK), kh = (int)((k % KK) / KW), kw = (int)(k % KW);
-        const int oy = (int)(p / OW), ox = (int)(p % OW);
-        const int iy = oy * stride - pad + kh, ix = ox * stride - pad + kw;
-        float v = 0.f;
-        if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = x[((n * C + c) * H + iy) * (int64_t)W + ix];
-        cols[i] = v;
+    const int P = OH * OW, per_row = P / Q;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= per_row) return;
+    const int p0 = j * Q, oy = p0 / OW, ox0 = p0 - oy * OW;
+    for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+        const int kw = row % KW;
+        int r = row / KW;
+        const int kh = r % KH;
+        r /= KH;  // n * C + c
+        const float* xp = x + (int64_t)r * H * W;
+        const int iy = oy * stride - pad + kh;
+        const bool row_in = iy >= 0 && iy < H;
+        float v[Q];
+#pragma unroll
+        for (int u = 0; u < Q; ++u) {
+            const int ix = (ox0 + u) * stride - pad + kw;
+            v[u] = (row_in && ix >= 0 && ix < W) ? __ldg(xp + (int64_t)iy * W + ix) : 0.f;
+        }
+        float* dst = cols + (int64_t)row * P + p0;
+        if constexpr (Q == 4) {
+            *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+            for (int u = 0; u < Q; ++u) dst[u] = v[u];
+        }
     }
 }
 
-// x[n][c][h][w] (=|+=) sum over the (kh, kw) taps that reach (h, w) of
-// cols[n][(c,kh,kw)][(oy,ox)], with h = oy*s - p + kh, w = ox*s - p + kw
+// x[n][c][h][w] (=|+=) sum over the taps (kh, kw) that reach (h, w) of
+// cols[n][(c,kh,kw)][(oy,ox)], h = oy*s - p + kh, w = ox*s - p + kw.
+// blockIdx.y walks the image rows (n, c, h), threads Q consecutive w each.
+template <int Q>
 __global__ void col2im_kernel(const float* __restrict__ cols, float* __restrict__ x, int C, int H, int W, int KH,
-                              int KW, int OH, int OW, int pad, int stride, int accumulate, int64_t total) {
+                              int KW, int OH, int OW, int pad, int stride, int accumulate, int rows) {
     pdl_entry();
-    const int64_t step = (int64_t)gridDim.x * blockDim.x;
-    const int64_t P = (int64_t)OH * OW, KK = (int64_t)KH * KW;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
-        const int w = (int)(i % W);
-        const int h = (int)((i / W) % H);
-        const int64_t nc = i / ((int64_t)H * W);
-        const int c = (int)(nc % C);
-        const int64_t n = nc / C;
-        const float* base = cols + (n * C + c) * KK * P;
-        float s = 0.f;
+    const int P = OH * OW, per_row = W / Q;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= per_row) return;
+    const int w0 = j * Q;
+    for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+        const int h = row % H;
+        const int nc = row / H;
+        const float* base = cols + (int64_t)nc * KH * KW * P;
+        float s[Q];
+#pragma unroll
+        for (int u = 0; u < Q; ++u) s[u] = 0.f;
         for (int kh = 0; kh < KH; ++kh) {
             const int ry = h + pad - kh;
             if (ry < 0 || ry % stride != 0) continue;
             const int oy = ry / stride;
             if (oy >= OH) continue;
             for (int kw = 0; kw < KW; ++kw) {
-                const int rx = w + pad - kw;
-                if (rx < 0 || rx % stride != 0) continue;
-                const int ox = rx / stride;
-                if (ox >= OW) continue;
-                s += base[((int64_t)kh * KW + kw) * P + (int64_t)oy * OW + ox];
+                const float* plane = base + (int64_t)(kh * KW + kw) * P + oy * OW;
+#pragma unroll
+                for (int u = 0; u < Q; ++u) {
+                    const int rx = w0 + u + pad - kw;
+                    if (rx < 0 || rx % stride != 0) continue;
+                    const int ox = rx / stride;
+                    if (ox < OW) s[u] += __ldg(plane + ox);
+                }
             }
         }
-        x[i] = accumulate ? x[i] + s : s;
+        float* dst = x + (int64_t)row * W + w0;
+        if constexpr (Q == 4) {
+            float4 o = make_float4(s[0], s[1], s[2], s[3]);
+            if (accumulate) {
+                const float4 a = *reinterpret_cast<const float4*>(dst);
+                o.x += a.x;
+                o.y += a.y;
+                o.z += a.z;
+                o.w += a.w;
+            }
+            *reinterpret_cast<float4*>(dst) = o;
+        } else {
+#pragma unroll
+            for (int u = 0; u < Q; ++u) dst[u] = accumulate ? dst[u] + s[u] : s[u];
+        }
     }
 }
 
@@ -154,18 +194,33 @@ __global__ void swap_dims_kernel(const float* __restrict__ in, float* __restrict
 
 int im2col(const float* x, float* cols, int n, int c, int h, int w, int kh, int kw, int oh, int ow, int pad,
            int stride, cudaStream_t st) {
-    const int64_t total = (int64_t)n * c * kh * kw * oh * ow;
-    if (total == 0) return MLE_OK;
-    launch_k(im2col_kernel, grid_for(total, kT), kT, 0, st, x, cols, c, h, w, kh, kw, oh, ow, pad, stride, total);
+    const int64_t rows = (int64_t)n * c * kh * kw;
+    if (rows == 0) return MLE_OK;
+    if (rows > INT32_MAX || (int64_t)oh * ow > INT32_MAX || (int64_t)h * w > INT32_MAX) return MLE_ERR_UNSUPPORTED;
+    const bool v4 = ow % 4 == 0 && aligned16(cols);
+    const int per_row = oh * ow / (v4 ? 4 : 1);
+    const dim3 grid((unsigned)((per_row + kRowThreads - 1) / kRowThreads), (unsigned)std::min<int64_t>(rows, 65535));
+    if (v4)
+        launch_k(im2col_kernel<4>, grid, kRowThreads, 0, st, x, cols, c, h, w, kh, kw, oh, ow, pad, stride, (int)rows);
+    else
+        launch_k(im2col_kernel<1>, grid, kRowThreads, 0, st, x, cols, c, h, w, kh, kw, oh, ow, pad, stride, (int)rows);
     return launch_status();
 }
 
 int col2im(const float* cols, float* x, int n, int c, int h, int w, int kh, int kw, int oh, int ow, int pad,
            int stride, int accumulate, cudaStream_t st) {
-    const int64_t total = (int64_t)n * c * h * w;
-    if (total == 0) return MLE_OK;
-    launch_k(col2im_kernel, grid_for(total, kT), kT, 0, st, cols, x, c, h, w, kh, kw, oh, ow, pad, stride, accumulate,
-             total);
+    const int64_t rows = (int64_t)n * c * h;
+    if (rows == 0) return MLE_OK;
+    if (rows > INT32_MAX || (int64_t)oh * ow > INT32_MAX) return MLE_ERR_UNSUPPORTED;
+    const bool v4 = w % 4 == 0 && aligned16(x);
+    const int per_row = w / (v4 ? 4 : 1);
+    const dim3 grid((unsigned)((per_row + kRowThreads - 1) / kRowThreads), (unsigned)std::min<int64_t>(rows, 65535));
+    if (v4)
+        launch_k(col2im_kernel<4>, grid, kRowThreads, 0, st, cols, x, c, h, w, kh, kw, oh, ow, pad, stride, accumulate,
+                 (int)rows);
+    else
+        launch_k(col2im_kernel<1>, grid, kRowThreads, 0, st, cols, x, c, h, w, kh, kw, oh, ow, pad, stride, accumulate,
+                 (int)rows);
     return launch_status();
 }
 
@@ -363,7 +418,9 @@ int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y
         }
         s = weight_pack(wgt, ws + p.wp, cout, cin, p.taps, p.cin4, 0, st);
         if (s) return s;
-        s = run_conv_gemm(conv_fwd_gemm(p, x, ws, y, batch, cin, h, cout, kh, kw, pad), st);
+        ConvGemm g = conv_fwd_gemm(p, x, ws, y, batch, cin, h, cout, kh, kw, pad);
+        g.bias = bias;  // added by the GEMM
+        return run_conv_gemm(g, st);
     } else {
         s = im2col(x, ws, batch, cin, h, w, kh, kw, oh, ow, pad, stride, st);
         if (s) return s;

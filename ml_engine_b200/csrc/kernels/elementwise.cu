@@ -341,9 +341,11 @@ __global__ void channel_bias_fwd_kernel(const float* __restrict__ x, const float
 }
 
 // One block per (channel, batch chunk): gb[c] += sum; optional gx += g.
+// blockIdx.x runs over the reduced channels (the first gridDim.x of
+// `channels`); float4 accesses when `vec` (spatial % 4 == 0, aligned).
 __global__ void channel_bias_bwd_kernel(const float* __restrict__ g, float* __restrict__ gx,
                                         float* __restrict__ gb, int batch, int channels, int64_t spatial,
-                                        int batch_per_block) {
+                                        int batch_per_block, int vec) {
     pdl_entry();
     __shared__ float scratch[32];
     const int c = blockIdx.x;
@@ -353,10 +355,27 @@ __global__ void channel_bias_bwd_kernel(const float* __restrict__ g, float* __re
     float s = 0.f;
     for (int n = n0; n < n1; ++n) {
         const int64_t base = ((int64_t)n * channels + c) * spatial;
-        for (int64_t k = threadIdx.x; k < spatial; k += blockDim.x) {
-            const float v = g[base + k];
-            s += v;
-            if (gx) gx[base + k] += v;
+        if (vec) {
+            const float4* g4 = reinterpret_cast<const float4*>(g + base);
+            float4* x4 = reinterpret_cast<float4*>(gx + base);
+            for (int64_t k = threadIdx.x; k < spatial / 4; k += blockDim.x) {
+                const float4 v = g4[k];
+                s += (v.x + v.y) + (v.z + v.w);
+                if (gx) {
+                    float4 o = x4[k];
+                    o.x += v.x;
+                    o.y += v.y;
+                    o.z += v.z;
+                    o.w += v.w;
+                    x4[k] = o;
+                }
+            }
+        } else {
+            for (int64_t k = threadIdx.x; k < spatial; k += blockDim.x) {
+                const float v = g[base + k];
+                s += v;
+                if (gx) gx[base + k] += v;
+            }
         }
     }
     s = block_sum(s, scratch);
@@ -712,17 +731,30 @@ int mle_channel_bias_fwd(const float* x, const float* b, float* y, int batch, in
     return launch_status();
 }
 
-int mle_channel_bias_bwd(const float* g, float* gx, float* gb, int batch, int channels, int64_t spatial,
-                         mle_stream_t stream) {
-    if (batch < 0 || channels <= 0 || spatial <= 0 || !g || !gb) return MLE_ERR_ARG;
-    if (batch == 0) return MLE_OK;
-    int chunks = (2 * kSMs + channels - 1) / channels;
+static int channel_sums(const float* g, float* gx, float* gb, int batch, int channels, int first, int64_t spatial,
+                        cudaStream_t st) {
+    if (batch == 0 || first == 0) return MLE_OK;
+    int chunks = (2 * kSMs + first - 1) / first;
     if (chunks > batch) chunks = batch;
     const int bpb = (batch + chunks - 1) / chunks;
     chunks = (batch + bpb - 1) / bpb;
-    dim3 grid((unsigned)channels, (unsigned)chunks);
-    launch_k(channel_bias_bwd_kernel, grid, kThreads, 0, as_stream(stream), g, gx, gb, batch, channels, spatial, bpb);
+    const int vec = (spatial % 4 == 0) && aligned16(g) && (gx == nullptr || aligned16(gx));
+    dim3 grid((unsigned)first, (unsigned)chunks);
+    launch_k(channel_bias_bwd_kernel, grid, kThreads, 0, st, g, gx, gb, batch, channels, spatial, bpb, vec);
     return launch_status();
+}
+
+int mle_channel_bias_bwd(const float* g, float* gx, float* gb, int batch, int channels, int64_t spatial,
+                         mle_stream_t stream) {
+    if (batch < 0 || channels <= 0 || spatial <= 0 || !g || !gb) return MLE_ERR_ARG;
+    return channel_sums(g, gx, gb, batch, channels, channels, spatial, as_stream(stream));
+}
+
+int mle_channel_bias_bwd_first(const float* g, float* gb, int batch, int channels, int first, int64_t spatial,
+                               mle_stream_t stream) {
+    if (batch < 0 || channels <= 0 || first < 0 || first > channels || spatial <= 0 || !g || !gb)
+        return MLE_ERR_ARG;
+    return channel_sums(g, nullptr, gb, batch, channels, first, spatial, as_stream(stream));
 }
 
 int mle_matpe_fwd(const float* x, float* y, int batch, int rows, int cols, int start_idx, mle_stream_t stream) {

@@ -40,6 +40,7 @@ struct ConvGemm {
     int P;           // pixels per image of the output (kind 1) / of A (kind 2)
     int64_t lda, ldc;
     int accumulate;  // kind 1 only (kind 2 always adds)
+    const float* bias;  // kind 1 only: added per output channel m (assigned output)
 };
 
 int simt_gemm(const GemmProblem& p, cudaStream_t st);

@@ -66,8 +66,12 @@ struct EpiParams {
     //      with p the output pixel (rows of width cv_w, flattened)
     //   2: tile column index = (tap, channel block of BN), tap = n / cv_cblk,
     //      stored as the tile's channel index (C's third coordinate); k = pixel
+    //   3: kind 1 with the roles exchanged: tile rows are output pixels
+    //      (A = the shifted copies, MN-major), tile columns output channels
+    //      (B = the packed weights), C written transposed (c_trans)
     int conv;
     int cv_kw, cv_pad, cv_w, cv_cblk, cv_nb;
+    int c_trans;                      // tile rows run along C's contiguous dimension (TMA epilogue only)
 };
 
 // Output tile `t` of the persistent walk: n fastest, then m, then (batch,
@@ -387,6 +391,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < BN / 32; ++j)
                             tma_load_4d(tmB, &full[s], sb + j * 4096, x.n0 + 32 * j + dp, c0, zc, 0);
+                    } else if (A_MN && !B_MN && ep.conv == 3) {
+                        const int kb = x.kb_begin + i;
+                        const int tap = kb / ep.cv_cblk, c0 = (kb - tap * ep.cv_cblk) * BK;
+                        const int kh = tap / ep.cv_kw, kw = tap - kh * ep.cv_kw;
+                        const int zc = kw * ep.cv_nb + x.bidx;
+                        const int dp = (kh - ep.cv_pad) * ep.cv_w;
+#pragma unroll
+                        for (int j = 0; j < BM / 32; ++j)
+                            tma_load_4d(tmA, &full[s], sa + j * 4096, x.m0 + 32 * j + dp, c0, zc, 0);
+                        tma_load_4d(tmB, &full[s], sb, c0, x.n0, tap, 0);
                     } else if (!A_MN && !B_MN && ep.conv == 2) {
                         // B rows = channels x.n0.. of tap x.cidx at pixels k0..k0+31
                         const int kh = x.cidx / ep.cv_kw, kw = x.cidx - kh * ep.cv_kw;
@@ -504,6 +518,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (blocks_out >= 2) {
                         if (lane == 0) bulk_wait_read<1>();
                         __syncwarp();
+                    }
+                    if (ep.c_trans) {
+                        // C stores the tile transposed: block row j (C row col0 + j)
+                        // holds the 32 tile rows, lane's word in chunk
+                        // (lane / 4) ^ (j % 8) (128-byte swizzle); the bias is per
+                        // tile column
+                        const bool add_bias = ep.bias && x.kb_begin == 0;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            float v = ep.alpha * __uint_as_float(r[j]);
+                            if (add_bias && col0 + j < ep.N) v += __ldg(ep.bias + col0 + j);
+                            blk[j * 32 + ((((lane >> 2) ^ (j & 7))) << 2) + (lane & 3)] = v;
+                        }
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            const int cz = ep.c_has_c ? x.cidx : 0, bz = ep.c_has_b ? x.bidx : 0;
+                            if (ep.mode == EPI_ASSIGN) tma_store_4d(tmC, blk, row0, col0, cz, bz);
+                            else tma_reduce_add_4d(tmC, blk, row0, col0, cz, bz);
+                            bulk_commit();
+                        }
+                        ++blocks_out;
+                        continue;
                     }
                     // row `lane` of the block: alpha * acc + bias, 16-byte chunk j
                     // stored at chunk j ^ (row % 8) (128-byte swizzle)
@@ -759,20 +796,21 @@ bool may_split(const GemmProblem& p) {
 // spread over the SMs in use, and splitting K adds one reduce-add of C per
 // split.  Its choices match the best measured (BN, splits) within ~5 % for
 // the transformer's backward GEMMs.
-void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits) {
+void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model_assign = false) {
     using namespace tc;
     BN = 64;
     splits = 1;
     // Assigned outputs never split (the memset and reduce-adds cost more
     // than they save, measured on B200); narrow tiles keep enough of them
-    // in flight for these small-K products.
+    // in flight for these small-K products.  `model_assign`: pick the width
+    // of an assigned (long-K) product with the fill model instead.
     bool any_assign = false;
     int max_n = 0;
     for (int i = 0; i < n; ++i) {
         any_assign = any_assign || ps[i].mode == EPI_ASSIGN;
         max_n = std::max(max_n, ps[i].N);
     }
-    if (any_assign) {
+    if (any_assign && !model_assign) {
         BN = max_n <= 256 ? 64 : 128;
         return;
     }
@@ -797,7 +835,7 @@ void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits) {
             cbytes += (double)p.M * p.N * sh.z * 4.0;
             if (p.mode == EPI_ASSIGN) assign_bytes += (double)p.M * p.N * sh.z * 4.0;
         }
-        const int max_split = split_ok ? std::max(1, kb_min / 4) : 1;
+        const int max_split = (split_ok && !any_assign) ? std::max(1, kb_min / 4) : 1;
         for (int sp = 1; sp <= max_split; sp = (sp < 4 ? sp + 1 : sp * 2)) {
             const int64_t work = units * sp;
             const double active = (double)std::min<int64_t>(work, kSMs);
@@ -993,10 +1031,97 @@ bool conv_gemm_supported(const ConvGemm& c) {
     return true;
 }
 
+// Kind 1 with output pixels as the tile rows (EpiParams::conv == 3): the
+// output channels become the tile columns, so a narrow channel count (64)
+// fills a 64-wide tile instead of half of a 128-row one, and the bias is
+// added in the epilogue.  Returns false (nothing launched) when TMA cannot
+// describe the transposed output.
+static bool run_conv_gemm_swapped(const ConvGemm& c, cudaStream_t st, int& status) {
+    using namespace tc;
+    const int taps = c.KH * c.KW;
+    const int cblk = (c.C + BK - 1) / BK;
+    GemmProblem q;
+    memset(&q, 0, sizeof(q));
+    q.M = c.P;
+    q.N = c.M;
+    q.K = taps * cblk * BK;
+    q.nbatch = c.nb;
+    q.channels = 1;
+    q.ldc = c.P;
+    q.alpha = 1.f;
+    q.mode = c.accumulate ? EPI_ACCUM : EPI_ASSIGN;
+    int BN, splits;
+    choose_tiles(&q, 1, BN, splits, true);
+    const int kb_total = taps * cblk;
+    const int kb_per_split = (kb_total + splits - 1) / splits;
+    splits = (kb_total + kb_per_split - 1) / kb_per_split;
+    GemmGroup grp;
+    memset(&grp, 0, sizeof(grp));
+    EpiParams& ep = grp.ep[0];
+    ep.C = c.out;
+    ep.bias = c.bias;
+    ep.alpha = 1.f;
+    ep.M = c.P;
+    ep.N = c.M;
+    ep.K = q.K;
+    ep.ldc = c.P;
+    ep.c_stride_b = c.nb > 1 ? (int64_t)c.M * c.P : 0;
+    ep.channels = 1;
+    ep.splits = splits;
+    ep.kb_per_split = kb_per_split;
+    ep.m_tiles = (c.P + BM - 1) / BM;
+    ep.n_tiles = (c.M + BN - 1) / BN;
+    ep.mode = splits > 1 ? EPI_ATOMIC : (c.accumulate ? EPI_ACCUM : EPI_ASSIGN);
+    ep.conv = 3;
+    ep.cv_kw = c.KW;
+    ep.cv_pad = c.pad;
+    ep.cv_w = c.WS;
+    ep.cv_nb = c.nb;
+    ep.cv_cblk = cblk;
+    ep.c_trans = 1;
+    ep.c_has_b = c.nb > 1;
+    ep.vec = aligned16(c.out) && (c.bias == nullptr || aligned16(c.bias));
+    const int64_t plane = (int64_t)c.HS * c.WS;
+    const int64_t s_dims[4] = {plane, c.C, (int64_t)c.KW * c.nb, 1};
+    const int64_t s_str[3] = {plane, plane * c.C, plane * c.C * c.KW * c.nb};
+    const int s_box[4] = {32, BK, 1, 1};
+    const int64_t w_dims[4] = {c.lda, c.M, taps, 1};
+    const int64_t w_str[3] = {c.lda, (int64_t)c.M * c.lda, (int64_t)taps * c.M * c.lda};
+    const int w_box[4] = {BK, BN, 1, 1};
+    const int64_t c_dims[4] = {c.P, c.M, 1, c.nb};
+    const int64_t c_str[3] = {c.P, (int64_t)c.M * c.P, (int64_t)c.M * c.P};
+    const int c_box[4] = {32, 32, 1, 1};
+    if (!encode_map(&grp.a[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+        !encode_map(&grp.b[0], c.A, w_dims, w_str, w_box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_map(&grp.c[0], c.out, c_dims, c_str, c_box, CU_TENSOR_MAP_SWIZZLE_128B))
+        return false;
+    ep.tma_epi = 1;
+    if (splits > 1 && !c.accumulate) {
+        // split partial products are reduce-added into a zeroed output
+        if (cudaMemsetAsync(c.out, 0, sizeof(float) * (size_t)c.nb * c.M * c.P, st) != cudaSuccess) {
+            status = launch_status();
+            return true;
+        }
+    }
+    ep.tiles = (int64_t)ep.m_tiles * ep.n_tiles * c.nb * splits;
+    grp.n = 1;
+    grp.tile_start[0] = 0;
+    grp.tile_start[1] = ep.tiles;
+    status = dispatch(grp, true, false, BN, st);
+    return true;
+}
+
 int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
     using namespace tc;
     if (!conv_gemm_supported(c)) return MLE_ERR_ARG;
     const int taps = c.KH * c.KW;
+    if (c.kind == 1) {
+        // pixel rows unless the padded tile area says otherwise
+        auto up = [](int64_t v, int64_t m) { return (v + m - 1) / m * m; };
+        const int64_t area_n = up(c.M, BM) * up(c.P, 64), area_t = up(c.P, BM) * up(c.M, 64);
+        int status = MLE_OK;
+        if (area_t <= area_n && run_conv_gemm_swapped(c, st, status)) return status;
+    }
     // tile choice on the equivalent plain products
     GemmProblem q;
     memset(&q, 0, sizeof(q));
@@ -1089,7 +1214,10 @@ int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
     grp.tile_start[0] = 0;
     grp.tile_start[1] = ep.tiles;
     if (ep.tiles == 0) return MLE_OK;
-    return dispatch(grp, false, c.kind == 1, BN, st);
+    const int s = dispatch(grp, false, c.kind == 1, BN, st);
+    if (s || c.kind != 1 || !c.bias) return s;
+    // the bias runs along the tile rows here: a separate pass
+    return mle_channel_bias_fwd(c.out, c.bias, c.out, c.nb, c.M, c.P, st);
 }
 
 }  // namespace mle

@@ -4,14 +4,19 @@
 // LayerNorm one segment of C*H*W per dim0 index (Engine/kernels.cu:541-572),
 // GroupNorm one segment of (C/G)*H*W per (sample, group)
 // (Engine/kernels.cu:607-639).  One kernel pair therefore serves both: a
-// warp owns a segment when it fits in registers (N <= 2048, N % 4 == 0),
-// otherwise a 256-thread block owns it.  gamma = 1 and beta = 0 are the
+// warp owns a segment when it fits in its registers (N <= 2048, N % 4 == 0),
+// a cluster of up to 8 CTAs when it fits in theirs (N <= 65536), otherwise
+// a 256-thread block streams it.  gamma = 1 and beta = 0 are the
 // reference's fixed constants.
 //
 // The reference computes the forward scale as rsqrtf((1/N)*sqdev + eps)
 // (LNorm/GNorm) and the backward scale as rsqrtf(sqdev/N + eps)
 // (LayerBackward/GroupBackward); both expressions are kept.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace mle {
 namespace {
@@ -161,6 +166,140 @@ __global__ void seg_norm_bwd_block(const float* __restrict__ y, const float* __r
     for (int i = threadIdx.x; i < N; i += blockDim.x) xs[i] += rstd * (1.0f * gs[i] - mg - ys[i] * mgy);
 }
 
+// --------------------------- cluster per segment ----------------------------
+// A segment too long for one warp is split over the CL CTAs of a thread-block
+// cluster (CTA `rank` owns floats [rank*slice, (rank+1)*slice)); each thread
+// keeps its V float4 in registers, so the input is read once and the output
+// written once.  The CTAs' partial sums meet in distributed shared memory and
+// every CTA adds them in rank order, so all of them see the same totals.
+// Statistics as the block path: mean first, then the squared deviations.
+template <int V>
+__global__ void __launch_bounds__(kBlock) seg_norm_fwd_cluster(const float* __restrict__ x, float* __restrict__ y,
+                                                               float* __restrict__ mean, float* __restrict__ sqdev,
+                                                               int N, int slice, float eps) {
+    pdl_entry();
+    cg::cluster_group cl = cg::this_cluster();
+    __shared__ float scratch[32];
+    __shared__ float part[2];
+    const int CL = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+    const int64_t seg = blockIdx.x / CL;
+    const int lo = rank * slice;
+    const int n = min(slice, N - lo);
+    const float4* xs = reinterpret_cast<const float4*>(x + seg * N + lo);
+    float4 v[V];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int e = (i * kBlock + threadIdx.x) * 4;
+        v[i] = e < n ? xs[e / 4] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+    s = block_sum(s, scratch);
+    if (threadIdx.x == 0) part[0] = s;
+    cl.sync();
+    float tot = 0.f;
+    for (int r = 0; r < CL; ++r) tot += *cl.map_shared_rank(&part[0], r);
+    const float mu = tot / N;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int e = (i * kBlock + threadIdx.x) * 4;
+        if (e < n) {
+            const float a = v[i].x - mu, b = v[i].y - mu, c = v[i].z - mu, d = v[i].w - mu;
+            q += (a * a + b * b) + (c * c + d * d);
+        }
+    }
+    q = block_sum(q, scratch);
+    if (threadIdx.x == 0) part[1] = q;
+    cl.sync();
+    float qt = 0.f;
+    for (int r = 0; r < CL; ++r) qt += *cl.map_shared_rank(&part[1], r);
+    const float scale = rsqrtf((1.0f / N) * qt + eps);
+    float4* ys = reinterpret_cast<float4*>(y + seg * N + lo);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int e = (i * kBlock + threadIdx.x) * 4;
+        if (e < n)
+            ys[e / 4] = make_float4((v[i].x - mu) * scale, (v[i].y - mu) * scale, (v[i].z - mu) * scale,
+                                    (v[i].w - mu) * scale);
+    }
+    if (rank == 0 && threadIdx.x == 0) {
+        if (mean) mean[seg] = mu;
+        sqdev[seg] = qt;
+    }
+    cl.sync();  // peers may still be reading part[]
+}
+
+template <int V>
+__global__ void __launch_bounds__(kBlock) seg_norm_bwd_cluster(const float* __restrict__ y,
+                                                               const float* __restrict__ gy,
+                                                               const float* __restrict__ sqdev,
+                                                               float* __restrict__ gx, int N, int slice, float eps) {
+    pdl_entry();
+    cg::cluster_group cl = cg::this_cluster();
+    __shared__ float scratch[32];
+    __shared__ float part[2];
+    const int CL = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+    const int64_t seg = blockIdx.x / CL;
+    const int lo = rank * slice;
+    const int n = min(slice, N - lo);
+    const float4* ys = reinterpret_cast<const float4*>(y + seg * N + lo);
+    const float4* gs = reinterpret_cast<const float4*>(gy + seg * N + lo);
+    float4 yv[V], gv[V];
+    float sg = 0.f, sgy = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int e = (i * kBlock + threadIdx.x) * 4;
+        if (e < n) {
+            yv[i] = ys[e / 4];
+            gv[i] = gs[e / 4];
+        } else {
+            yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            gv[i] = yv[i];
+        }
+        sg += (gv[i].x + gv[i].y) + (gv[i].z + gv[i].w);
+        sgy += (gv[i].x * yv[i].x + gv[i].y * yv[i].y) + (gv[i].z * yv[i].z + gv[i].w * yv[i].w);
+    }
+    sg = block_sum(sg, scratch);
+    sgy = block_sum(sgy, scratch);
+    if (threadIdx.x == 0) {
+        part[0] = sg;
+        part[1] = sgy;
+    }
+    cl.sync();
+    float tg = 0.f, tgy = 0.f;
+    for (int r = 0; r < CL; ++r) {
+        const float* pr = cl.map_shared_rank(part, r);
+        tg += pr[0];
+        tgy += pr[1];
+    }
+    const float rstd = rsqrtf(sqdev[seg] / N + eps);
+    const float mg = tg / N, mgy = tgy / N;
+    float4* xs = reinterpret_cast<float4*>(gx + seg * N + lo);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int e = (i * kBlock + threadIdx.x) * 4;
+        if (e < n) {
+            float4 o = xs[e / 4];
+            o.x += rstd * (1.0f * gv[i].x - mg - yv[i].x * mgy);
+            o.y += rstd * (1.0f * gv[i].y - mg - yv[i].y * mgy);
+            o.z += rstd * (1.0f * gv[i].z - mg - yv[i].z * mgy);
+            o.w += rstd * (1.0f * gv[i].w - mg - yv[i].w * mgy);
+            xs[e / 4] = o;
+        }
+    }
+    cl.sync();  // peers may still be reading part[]
+}
+
+// Cluster shape for a segment of N floats: CL CTAs (<= 8, the portable
+// cluster size) of V float4 per thread, V <= 8.  False if N is too long.
+bool cluster_shape(int N, int& CL, int& V) {
+    CL = 1;
+    while (CL < 8 && (int64_t)CL * 4096 < N) CL *= 2;
+    V = (N + CL * kBlock * 4 - 1) / (CL * kBlock * 4);
+    return V <= 8;
+}
+
 // LayerBackward with channels > 1 keeps the reference's index map: only the
 // first batch*row*col elements are updated and element idx uses the
 // statistics of sample idx/(row*col) (Engine/kernels.cu:849-862), while the
@@ -201,6 +340,13 @@ static int seg_norm_fwd(const float* x, float* y, float* mean, float* sqdev, int
         else if (N <= 512) launch_k(seg_norm_fwd_warp<4>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
         else if (N <= 1024) launch_k(seg_norm_fwd_warp<8>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
         else launch_k(seg_norm_fwd_warp<16>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
+    } else if (int CL, V; N % 4 == 0 && aligned16(x) && aligned16(y) && cluster_shape(N, CL, V)) {
+        const int slice = V * kBlock * 4;
+        const dim3 grid((unsigned)(segs * CL));
+        if (V <= 1) launch_kc(seg_norm_fwd_cluster<1>, grid, kBlock, CL, st, x, y, mean, sqdev, N, slice, eps);
+        else if (V <= 2) launch_kc(seg_norm_fwd_cluster<2>, grid, kBlock, CL, st, x, y, mean, sqdev, N, slice, eps);
+        else if (V <= 4) launch_kc(seg_norm_fwd_cluster<4>, grid, kBlock, CL, st, x, y, mean, sqdev, N, slice, eps);
+        else launch_kc(seg_norm_fwd_cluster<8>, grid, kBlock, CL, st, x, y, mean, sqdev, N, slice, eps);
     } else {
         launch_k(seg_norm_fwd_block, (unsigned)segs, kBlock, 0, st, x, y, mean, sqdev, N, eps);
     }
@@ -218,6 +364,13 @@ static int seg_norm_bwd(const float* y, const float* gy, const float* sqdev, flo
         else if (N <= 512) launch_k(seg_norm_bwd_warp<4>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
         else if (N <= 1024) launch_k(seg_norm_bwd_warp<8>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
         else launch_k(seg_norm_bwd_warp<16>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
+    } else if (int CL, V; N % 4 == 0 && aligned16(y) && aligned16(gy) && aligned16(gx) && cluster_shape(N, CL, V)) {
+        const int slice = V * kBlock * 4;
+        const dim3 grid((unsigned)(segs * CL));
+        if (V <= 1) launch_kc(seg_norm_bwd_cluster<1>, grid, kBlock, CL, st, y, gy, sqdev, gx, N, slice, eps);
+        else if (V <= 2) launch_kc(seg_norm_bwd_cluster<2>, grid, kBlock, CL, st, y, gy, sqdev, gx, N, slice, eps);
+        else if (V <= 4) launch_kc(seg_norm_bwd_cluster<4>, grid, kBlock, CL, st, y, gy, sqdev, gx, N, slice, eps);
+        else launch_kc(seg_norm_bwd_cluster<8>, grid, kBlock, CL, st, y, gy, sqdev, gx, N, slice, eps);
     } else {
         launch_k(seg_norm_bwd_block, (unsigned)segs, kBlock, 0, st, y, gy, sqdev, gx, N, eps);
     }

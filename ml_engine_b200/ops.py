@@ -88,6 +88,10 @@ def channel_bias_bwd(g, gx, gb, batch, channels, spatial):
     _call("mle_channel_bias_bwd", _p(g), _p(gx), _p(gb), batch, channels, spatial, _s())
 
 
+def channel_bias_bwd_first(g, gb, batch, channels, first, spatial):
+    _call("mle_channel_bias_bwd_first", _p(g), _p(gb), batch, channels, first, spatial, _s())
+
+
 def matpe_fwd(x, y, batch, rows, cols, start_idx=0):
     _call("mle_matpe_fwd", _p(x), _p(y), batch, rows, cols, start_idx, _s())
 

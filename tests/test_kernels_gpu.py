@@ -112,8 +112,9 @@ def test_bias_add_and_grad(cuda, ops, orc, rng, rows, cols):
     assert rel_err(H(db), orc.bias_grad(x, db0.copy())) <= 1e-5 * max(1, rows / 64)
 
 
-def test_channel_bias(cuda, ops, orc, rng):
-    B, C, S = 4, 6, 35
+@pytest.mark.parametrize("S", [35, 64])
+def test_channel_bias(cuda, ops, orc, rng, S):
+    B, C = 4, 6
     x = rng.standard_normal(B * C * S).astype(np.float32)
     b = rng.standard_normal(C).astype(np.float32)
     y = torch.empty(B * C * S, device=cuda)
@@ -127,6 +128,20 @@ def test_channel_bias(cuda, ops, orc, rng):
     orc.channel_bias_bwd(x, rgx, rgb, B, C, S)
     assert np.array_equal(H(gx), rgx)
     assert rel_err(H(gb), rgb) <= RTOL_EXACT
+
+
+def test_channel_bias_first(cuda, ops, orc, rng):
+    """Broadcast_Channel's reduction of the first min(dim[3], C) channels."""
+    B, C, first, S = 5, 12, 7, 16
+    g = rng.standard_normal(B * C * S).astype(np.float32)
+    gb0 = rng.standard_normal(C).astype(np.float32)
+    gb = T(gb0, cuda)
+    ops.channel_bias_bwd_first(T(g, cuda), gb, B, C, first, S)
+    want = gb0.copy()
+    want[:first] += g.reshape(B, C, S)[:, :first].sum(axis=(0, 2), dtype=np.float64).astype(np.float32)
+    got = H(gb)
+    assert np.array_equal(got[first:], gb0[first:])
+    assert rel_err(got, want) <= RTOL_EXACT
 
 
 @pytest.mark.parametrize("flag", [0, 1, 2, 3])
@@ -149,8 +164,12 @@ def test_matpe(cuda, ops, orc, rng):
 
 
 # -------------------------------------------------------------- normalisation
+# segment lengths for every path: warp (<= 2048), one CTA (4096), clusters of
+# 2 and 8 CTAs (8192, 60000 with a partial last CTA), streamed block (70000
+# and the unaligned 4099)
 @pytest.mark.parametrize("batch,channels,row,col", [(64, 1, 1, 256), (33, 1, 1, 1000), (7, 1, 4, 1024),
-                                                    (5, 1, 1, 8192), (4, 3, 5, 8)])
+                                                    (5, 1, 1, 8192), (3, 1, 1, 60000), (2, 1, 1, 70000),
+                                                    (3, 1, 1, 4099), (4, 3, 5, 8)])
 def test_layernorm(cuda, ops, orc, rng, batch, channels, row, col):
     n = batch * channels * row * col
     x = (rng.standard_normal(n) * 2 + 0.5).astype(np.float32)
@@ -166,7 +185,8 @@ def test_layernorm(cuda, ops, orc, rng, batch, channels, row, col):
     assert rel_err(H(gx), orc.layernorm_bwd(ry, gy, rsq, gx0.copy(), batch, channels, row, col)) <= RTOL_EXACT
 
 
-@pytest.mark.parametrize("batch,channels,groups,row,col", [(4, 64, 8, 16, 16), (2, 24, 8, 3, 5)])
+@pytest.mark.parametrize("batch,channels,groups,row,col", [(4, 64, 8, 16, 16), (2, 24, 8, 3, 5), (2, 64, 8, 64, 64),
+                                                           (3, 128, 8, 32, 32)])
 def test_groupnorm(cuda, ops, orc, rng, batch, channels, groups, row, col):
     n = batch * channels * row * col
     x = (rng.standard_normal(n) * 2 + 0.5).astype(np.float32)
