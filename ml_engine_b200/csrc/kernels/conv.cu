@@ -32,26 +32,25 @@ namespace {
 
 constexpr int kT = 256;
 
-constexpr int kRowThreads = 128;
+constexpr int kRowThreads = 256;
 
-// cols[n][(c, kh, kw)][(oy, ox)]: blockIdx.y walks the column rows
-// (n, c, kh, kw), threads the output pixels of a row, Q consecutive ox each
-// (Q = 4 when OW % 4 == 0: one 16-byte store).  32-bit index arithmetic
-// within a row.
+// cols[n][(c, kh, kw)][(oy, ox)]: one thread per Q consecutive ox of one
+// column row (Q = 4 when OW % 4 == 0: one 16-byte store).  The thread index
+// runs over (row, chunk) pairs; 32-bit index arithmetic (the host checks
+// that the chunk count fits).
 template <int Q>
 __global__ void im2col_kernel(const float* __restrict__ x, float* __restrict__ cols, int C, int H, int W, int KH,
-                              int KW, int OH, int OW, int pad, int stride, int rows) {
+                              int KW, int OH, int OW, int pad, int stride, unsigned chunks) {
     pdl_entry();
-    const int P = OH * OW, per_row = P / Q;
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= per_row) return;
-    const int p0 = j * Q, oy = p0 / OW, ox0 = p0 - oy * OW;
-    for (int row = blockIdx.y; row < rows; row += gridDim.y) {
-        const int kw = row % KW;
-        int r = row / KW;
-        const int kh = r % KH;
-        r /= KH;  // n * C + c
-        const float* xp = x + (int64_t)r * H * W;
+    const unsigned per_row = (unsigned)(OH * OW) / Q;
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += gridDim.x * blockDim.x) {
+        const unsigned row = i / per_row;
+        const int p0 = (int)(i - row * per_row) * Q;
+        const int oy = p0 / OW, ox0 = p0 - oy * OW;
+        const int kw = (int)(row % (unsigned)KW);
+        const unsigned r = row / (unsigned)KW;
+        const int kh = (int)(r % (unsigned)KH);
+        const float* xp = x + (int64_t)(r / (unsigned)KH) * H * W;  // plane n * C + c
         const int iy = oy * stride - pad + kh;
         const bool row_in = iy >= 0 && iy < H;
         float v[Q];
@@ -60,7 +59,7 @@ __global__ void im2col_kernel(const float* __restrict__ x, float* __restrict__ c
             const int ix = (ox0 + u) * stride - pad + kw;
             v[u] = (row_in && ix >= 0 && ix < W) ? __ldg(xp + (int64_t)iy * W + ix) : 0.f;
         }
-        float* dst = cols + (int64_t)row * P + p0;
+        float* dst = cols + (int64_t)i * Q;
         if constexpr (Q == 4) {
             *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
         } else {
@@ -71,19 +70,19 @@ __global__ void im2col_kernel(const float* __restrict__ x, float* __restrict__ c
 }
 
 // x[n][c][h][w] (=|+=) sum over the taps (kh, kw) that reach (h, w) of
-// cols[n][(c,kh,kw)][(oy,ox)], h = oy*s - p + kh, w = ox*s - p + kw.
-// blockIdx.y walks the image rows (n, c, h), threads Q consecutive w each.
+// cols[n][(c,kh,kw)][(oy,ox)], h = oy*s - p + kh, w = ox*s - p + kw.  One
+// thread per Q consecutive w of one image row (n, c, h).
 template <int Q>
 __global__ void col2im_kernel(const float* __restrict__ cols, float* __restrict__ x, int C, int H, int W, int KH,
-                              int KW, int OH, int OW, int pad, int stride, int accumulate, int rows) {
+                              int KW, int OH, int OW, int pad, int stride, int accumulate, unsigned chunks) {
     pdl_entry();
-    const int P = OH * OW, per_row = W / Q;
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= per_row) return;
-    const int w0 = j * Q;
-    for (int row = blockIdx.y; row < rows; row += gridDim.y) {
-        const int h = row % H;
-        const int nc = row / H;
+    const int P = OH * OW;
+    const unsigned per_row = (unsigned)W / Q;
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += gridDim.x * blockDim.x) {
+        const unsigned row = i / per_row;
+        const int w0 = (int)(i - row * per_row) * Q;
+        const int h = (int)(row % (unsigned)H);
+        const unsigned nc = row / (unsigned)H;
         const float* base = cols + (int64_t)nc * KH * KW * P;
         float s[Q];
 #pragma unroll
@@ -104,7 +103,7 @@ __global__ void col2im_kernel(const float* __restrict__ cols, float* __restrict_
                 }
             }
         }
-        float* dst = x + (int64_t)row * W + w0;
+        float* dst = x + (int64_t)i * Q;
         if constexpr (Q == 4) {
             float4 o = make_float4(s[0], s[1], s[2], s[3]);
             if (accumulate) {
@@ -194,33 +193,33 @@ __global__ void swap_dims_kernel(const float* __restrict__ in, float* __restrict
 
 int im2col(const float* x, float* cols, int n, int c, int h, int w, int kh, int kw, int oh, int ow, int pad,
            int stride, cudaStream_t st) {
-    const int64_t rows = (int64_t)n * c * kh * kw;
-    if (rows == 0) return MLE_OK;
-    if (rows > INT32_MAX || (int64_t)oh * ow > INT32_MAX || (int64_t)h * w > INT32_MAX) return MLE_ERR_UNSUPPORTED;
     const bool v4 = ow % 4 == 0 && aligned16(cols);
-    const int per_row = oh * ow / (v4 ? 4 : 1);
-    const dim3 grid((unsigned)((per_row + kRowThreads - 1) / kRowThreads), (unsigned)std::min<int64_t>(rows, 65535));
+    const int64_t chunks = (int64_t)n * c * kh * kw * oh * ow / (v4 ? 4 : 1);
+    if (chunks == 0) return MLE_OK;
+    if (chunks > INT32_MAX || (int64_t)h * w > INT32_MAX) return MLE_ERR_UNSUPPORTED;
+    const unsigned grid = grid_for(chunks, kRowThreads);
     if (v4)
-        launch_k(im2col_kernel<4>, grid, kRowThreads, 0, st, x, cols, c, h, w, kh, kw, oh, ow, pad, stride, (int)rows);
+        launch_k(im2col_kernel<4>, grid, kRowThreads, 0, st, x, cols, c, h, w, kh, kw, oh, ow, pad, stride,
+                 (unsigned)chunks);
     else
-        launch_k(im2col_kernel<1>, grid, kRowThreads, 0, st, x, cols, c, h, w, kh, kw, oh, ow, pad, stride, (int)rows);
+        launch_k(im2col_kernel<1>, grid, kRowThreads, 0, st, x, cols, c, h, w, kh, kw, oh, ow, pad, stride,
+                 (unsigned)chunks);
     return launch_status();
 }
 
 int col2im(const float* cols, float* x, int n, int c, int h, int w, int kh, int kw, int oh, int ow, int pad,
            int stride, int accumulate, cudaStream_t st) {
-    const int64_t rows = (int64_t)n * c * h;
-    if (rows == 0) return MLE_OK;
-    if (rows > INT32_MAX || (int64_t)oh * ow > INT32_MAX) return MLE_ERR_UNSUPPORTED;
     const bool v4 = w % 4 == 0 && aligned16(x);
-    const int per_row = w / (v4 ? 4 : 1);
-    const dim3 grid((unsigned)((per_row + kRowThreads - 1) / kRowThreads), (unsigned)std::min<int64_t>(rows, 65535));
+    const int64_t chunks = (int64_t)n * c * h * w / (v4 ? 4 : 1);
+    if (chunks == 0) return MLE_OK;
+    if (chunks > INT32_MAX || (int64_t)oh * ow > INT32_MAX) return MLE_ERR_UNSUPPORTED;
+    const unsigned grid = grid_for(chunks, kRowThreads);
     if (v4)
         launch_k(col2im_kernel<4>, grid, kRowThreads, 0, st, cols, x, c, h, w, kh, kw, oh, ow, pad, stride, accumulate,
-                 (int)rows);
+                 (unsigned)chunks);
     else
         launch_k(col2im_kernel<1>, grid, kRowThreads, 0, st, cols, x, c, h, w, kh, kw, oh, ow, pad, stride, accumulate,
-                 (int)rows);
+                 (unsigned)chunks);
     return launch_status();
 }
 

@@ -329,14 +329,25 @@ __global__ void bias_add_kernel(const float* __restrict__ x, const float* __rest
     }
 }
 
-// y[n,c,s] = x[n,c,s] + b[c]
+// y[n,c,s] = x[n,c,s] + b[c]; Q consecutive s per thread (Q = 4: 16-byte
+// accesses), 32-bit chunk index (the host checks the count)
+template <int Q>
 __global__ void channel_bias_fwd_kernel(const float* __restrict__ x, const float* __restrict__ b,
-                                        float* __restrict__ y, int channels, int64_t spatial, int64_t total) {
+                                        float* __restrict__ y, unsigned channels, unsigned per_plane,
+                                        unsigned chunks) {
     pdl_entry();
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-        const int c = (int)((i / spatial) % channels);
-        y[i] = x[i] + b[c];
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += gridDim.x * blockDim.x) {
+        const float bc = __ldg(b + (i / per_plane) % channels);
+        if constexpr (Q == 4) {
+            float4 v = reinterpret_cast<const float4*>(x)[i];
+            v.x += bc;
+            v.y += bc;
+            v.z += bc;
+            v.w += bc;
+            reinterpret_cast<float4*>(y)[i] = v;
+        } else {
+            y[i] = x[i] + bc;
+        }
     }
 }
 
@@ -501,30 +512,48 @@ __global__ void headify4_kernel(const float4* __restrict__ in, float4* __restric
     }
 }
 
+// Channel concatenation along dim1 and its adjoint: every (n, channel)
+// plane is a contiguous run of `spatial` floats, so a thread moves Q
+// consecutive floats of one plane (Q = 4: 16-byte accesses).  32-bit chunk
+// index (the host checks the count).
+template <int Q>
 __global__ void channel_concat_kernel(const float* __restrict__ a, const float* __restrict__ b,
-                                      float* __restrict__ c, int c1, int c2, int64_t spatial, int64_t total) {
+                                      float* __restrict__ c, int c1, int c2, unsigned per_plane, unsigned chunks) {
     pdl_entry();
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    const int cc = c1 + c2;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-        const int64_t n = i / ((int64_t)cc * spatial);
-        const int ch = (int)((i / spatial) % cc);
-        const int64_t s = i % spatial;
-        c[i] = (ch < c1) ? a[(n * c1 + ch) * spatial + s] : b[(n * c2 + (ch - c1)) * spatial + s];
+    const unsigned cc = (unsigned)(c1 + c2);
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += gridDim.x * blockDim.x) {
+        const unsigned pl = i / per_plane, j = i - pl * per_plane;
+        const unsigned n = pl / cc, ch = pl - n * cc;
+        const float* src = ch < (unsigned)c1 ? a + ((int64_t)n * c1 + ch) * per_plane * Q
+                                             : b + ((int64_t)n * c2 + (ch - c1)) * per_plane * Q;
+        if constexpr (Q == 4)
+            reinterpret_cast<float4*>(c)[i] = reinterpret_cast<const float4*>(src)[j];
+        else
+            c[i] = src[j];
     }
 }
 
+template <int Q>
 __global__ void channel_split_kernel(float* __restrict__ ga, float* __restrict__ gb, const float* __restrict__ gc,
-                                     int c1, int c2, int64_t spatial, int64_t total) {
+                                     int c1, int c2, unsigned per_plane, unsigned chunks) {
     pdl_entry();
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    const int cc = c1 + c2;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-        const int64_t n = i / ((int64_t)cc * spatial);
-        const int ch = (int)((i / spatial) % cc);
-        const int64_t s = i % spatial;
-        if (ch < c1) ga[(n * c1 + ch) * spatial + s] += gc[i];
-        else gb[(n * c2 + (ch - c1)) * spatial + s] += gc[i];
+    const unsigned cc = (unsigned)(c1 + c2);
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += gridDim.x * blockDim.x) {
+        const unsigned pl = i / per_plane, j = i - pl * per_plane;
+        const unsigned n = pl / cc, ch = pl - n * cc;
+        float* dst = ch < (unsigned)c1 ? ga + ((int64_t)n * c1 + ch) * per_plane * Q
+                                       : gb + ((int64_t)n * c2 + (ch - c1)) * per_plane * Q;
+        if constexpr (Q == 4) {
+            const float4 g = reinterpret_cast<const float4*>(gc)[i];
+            float4 o = reinterpret_cast<float4*>(dst)[j];
+            o.x += g.x;
+            o.y += g.y;
+            o.z += g.z;
+            o.w += g.w;
+            reinterpret_cast<float4*>(dst)[j] = o;
+        } else {
+            dst[j] += gc[i];
+        }
     }
 }
 
@@ -724,10 +753,17 @@ int mle_bias_grad(const float* g, float* bias_grad, int64_t rows, int64_t cols, 
 int mle_channel_bias_fwd(const float* x, const float* b, float* y, int batch, int channels, int64_t spatial,
                          mle_stream_t stream) {
     if (batch < 0 || channels <= 0 || spatial <= 0 || !x || !b || !y) return MLE_ERR_ARG;
-    const int64_t total = (int64_t)batch * channels * spatial;
-    if (total == 0) return MLE_OK;
-    launch_k(channel_bias_fwd_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), x, b, y, channels, spatial,
-                                                                                           total);
+    const int Q = (spatial % 4 == 0 && aligned16(x) && aligned16(y)) ? 4 : 1;
+    const int64_t chunks = (int64_t)batch * channels * spatial / Q;
+    if (chunks == 0) return MLE_OK;
+    if (chunks > INT32_MAX) return MLE_ERR_UNSUPPORTED;
+    const unsigned per = (unsigned)(spatial / Q), grid = grid_for(chunks, kThreads);
+    if (Q == 4)
+        launch_k(channel_bias_fwd_kernel<4>, grid, kThreads, 0, as_stream(stream), x, b, y, (unsigned)channels, per,
+                 (unsigned)chunks);
+    else
+        launch_k(channel_bias_fwd_kernel<1>, grid, kThreads, 0, as_stream(stream), x, b, y, (unsigned)channels, per,
+                 (unsigned)chunks);
     return launch_status();
 }
 
@@ -814,20 +850,34 @@ int mle_headify(const float* in, float* out, int batch, int heads, int seq, int 
 int mle_channel_concat(const float* a, const float* b, float* c, int batch, int c1, int c2, int64_t spatial,
                        mle_stream_t stream) {
     if (batch < 0 || c1 < 0 || c2 < 0 || spatial <= 0 || !a || !b || !c) return MLE_ERR_ARG;
-    const int64_t total = (int64_t)batch * (c1 + c2) * spatial;
-    if (total == 0) return MLE_OK;
-    launch_k(channel_concat_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), a, b, c, c1, c2, spatial,
-                                                                                         total);
+    const int Q = (spatial % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(c)) ? 4 : 1;
+    const int64_t chunks = (int64_t)batch * (c1 + c2) * spatial / Q;
+    if (chunks == 0) return MLE_OK;
+    if (chunks > INT32_MAX) return MLE_ERR_UNSUPPORTED;
+    const unsigned per = (unsigned)(spatial / Q), grid = grid_for(chunks, kThreads);
+    if (Q == 4)
+        launch_k(channel_concat_kernel<4>, grid, kThreads, 0, as_stream(stream), a, b, c, c1, c2, per,
+                 (unsigned)chunks);
+    else
+        launch_k(channel_concat_kernel<1>, grid, kThreads, 0, as_stream(stream), a, b, c, c1, c2, per,
+                 (unsigned)chunks);
     return launch_status();
 }
 
 int mle_channel_split(float* ga, float* gb, const float* gc, int batch, int c1, int c2, int64_t spatial,
                       mle_stream_t stream) {
     if (batch < 0 || c1 < 0 || c2 < 0 || spatial <= 0 || !ga || !gb || !gc) return MLE_ERR_ARG;
-    const int64_t total = (int64_t)batch * (c1 + c2) * spatial;
-    if (total == 0) return MLE_OK;
-    launch_k(channel_split_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), ga, gb, gc, c1, c2, spatial,
-                                                                                        total);
+    const int Q = (spatial % 4 == 0 && aligned16(ga) && aligned16(gb) && aligned16(gc)) ? 4 : 1;
+    const int64_t chunks = (int64_t)batch * (c1 + c2) * spatial / Q;
+    if (chunks == 0) return MLE_OK;
+    if (chunks > INT32_MAX) return MLE_ERR_UNSUPPORTED;
+    const unsigned per = (unsigned)(spatial / Q), grid = grid_for(chunks, kThreads);
+    if (Q == 4)
+        launch_k(channel_split_kernel<4>, grid, kThreads, 0, as_stream(stream), ga, gb, gc, c1, c2, per,
+                 (unsigned)chunks);
+    else
+        launch_k(channel_split_kernel<1>, grid, kThreads, 0, as_stream(stream), ga, gb, gc, c1, c2, per,
+                 (unsigned)chunks);
     return launch_status();
 }
 

@@ -1,9 +1,12 @@
 // CUDA-core GEMM for the shapes the TMA path cannot describe: row strides
 // that are not a multiple of 16 bytes, unaligned bases, or tiny N/M such as
 // the 10-way classifier of the MNIST MLP.  64x64 output tile per 256-thread
-// block, 4x4 outputs per thread, k-slices of 16 staged in shared memory.
+// block, 4x4 outputs per thread, k-slices of 16 staged in shared memory;
+// products of at most 8 rows take one warp per output instead.
 // Operand access follows the same GemmProblem description as the tensor-core
 // path (transposes, batch/channel strides, assign / += / atomic epilogue).
+#include <stdint.h>
+
 #include "gemm.cuh"
 
 namespace mle {
@@ -80,11 +83,50 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const GemmProblem p) {
     }
 }
 
+// Products with at most kSkinnyM rows (a [1, in] time embedding through a
+// Linear layer): one warp per output element, the lanes striding over k
+// and meeting in a butterfly sum.  blockIdx.z indexes (batch, channel).
+constexpr int kSkinnyM = 8;
+
+__global__ void __launch_bounds__(256) skinny_gemm_kernel(const GemmProblem p) {
+    pdl_entry();
+    const int z = blockIdx.z;
+    const int cidx = z % p.channels, bidx = z / p.channels;
+    const float* A = p.A + (int64_t)bidx * p.a_sb + (int64_t)cidx * p.a_sc;
+    const float* B = p.B + (int64_t)bidx * p.b_sb + (int64_t)cidx * p.b_sc;
+    float* C = p.C + (int64_t)bidx * p.c_sb + (int64_t)cidx * p.c_sc;
+    const int lane = threadIdx.x & 31;
+    const int64_t out = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (out >= (int64_t)p.M * p.N) return;
+    const int m = (int)(out / p.N), n = (int)(out - (int64_t)m * p.N);
+    float acc = 0.f;
+    for (int k = lane; k < p.K; k += 32) {
+        const float a = p.trans_a ? A[(int64_t)k * p.lda + m] : A[(int64_t)m * p.lda + k];
+        const float b = p.trans_b ? B[(int64_t)n * p.ldb + k] : B[(int64_t)k * p.ldb + n];
+        acc += a * b;
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        float v = p.alpha * acc;
+        if (p.bias) v += p.bias[n];
+        float* dst = C + (int64_t)m * p.ldc + n;
+        if (p.mode == 0) *dst = v;
+        else if (p.mode == 1) *dst += v;
+        else atomicAdd(dst, v);
+    }
+}
+
 }  // namespace
 
 int simt_gemm(const GemmProblem& p, cudaStream_t st) {
     const int64_t z = (int64_t)p.nbatch * p.channels;
     if (z > 65535) return MLE_ERR_UNSUPPORTED;
+    if (p.M <= kSkinnyM) {
+        const int64_t blocks = ((int64_t)p.M * p.N + 7) / 8;
+        if (blocks > INT32_MAX) return MLE_ERR_UNSUPPORTED;
+        launch_k(skinny_gemm_kernel, dim3((unsigned)blocks, 1, (unsigned)z), 256, 0, st, p);
+        return launch_status();
+    }
     dim3 grid((p.N + TN - 1) / TN, (p.M + TM - 1) / TM, (unsigned)z);
     if (grid.y > 65535) return MLE_ERR_UNSUPPORTED;
     launch_k(simt_gemm_kernel, grid, 256, 0, st, p);

@@ -144,6 +144,25 @@ def test_channel_bias_first(cuda, ops, orc, rng):
     assert rel_err(got, want) <= RTOL_EXACT
 
 
+@pytest.mark.parametrize("S", [35, 64])
+def test_channel_concat_split(cuda, ops, orc, rng, S):
+    """CopyCrop's channel concatenation and its gradient split."""
+    B, c1, c2 = 3, 5, 7
+    a = rng.standard_normal(B * c1 * S).astype(np.float32)
+    b = rng.standard_normal(B * c2 * S).astype(np.float32)
+    c = torch.empty(B * (c1 + c2) * S, device=cuda)
+    ops.channel_concat(T(a, cuda), T(b, cuda), c, B, c1, c2, S)
+    assert np.array_equal(H(c), orc.channel_concat(a, b, B, c1, c2, S))
+    gc = rng.standard_normal(B * (c1 + c2) * S).astype(np.float32)
+    ga0 = rng.standard_normal(B * c1 * S).astype(np.float32)
+    gb0 = rng.standard_normal(B * c2 * S).astype(np.float32)
+    ga, gb = T(ga0, cuda), T(gb0, cuda)
+    ops.channel_split(ga, gb, T(gc, cuda), B, c1, c2, S)
+    ra, rb = ga0.copy(), gb0.copy()
+    orc.channel_split(ra, rb, gc, B, c1, c2, S)
+    assert np.array_equal(H(ga), ra) and np.array_equal(H(gb), rb)
+
+
 @pytest.mark.parametrize("flag", [0, 1, 2, 3])
 def test_headify(cuda, ops, orc, rng, flag):
     B, Hh, S, D = 3, 4, 5, 8
@@ -254,7 +273,8 @@ def test_mse(cuda, ops, orc, rng):
 
 # ----------------------------------------------------------------------- GEMM
 GEMM_SHAPES = [(128, 128, 32), (256, 512, 384), (200, 130, 70), (64, 256, 784), (784, 256, 64), (1000, 96, 8),
-               (4096, 256, 256), (256, 256, 4096), (33, 1024, 129)]
+               (4096, 256, 256), (256, 256, 4096), (33, 1024, 129),
+               (1, 128, 256), (3, 64, 1000)]  # at most 8 rows: one warp per output
 
 
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
