@@ -360,6 +360,91 @@ def run_unet(args):
     s.close()
 
 
+# ------------------------------------------------------ encoder-decoder workload
+def run_encdec(args, rank, world, local_rank):
+    """6+6-layer encoder-decoder (d 512, 8 heads, FFN 2048,
+    seq 256, vocab 8192), global batch 256 split over the ranks (strong
+    scaling); token ids Zipf(s=1.1) over the vocabulary, next-token targets;
+    one step = zero_grad + forward + backward + bucketed NCCL allreduce +
+    clip(1.0) + AdamW, replayed as a captured CUDA graph."""
+    import numpy as np
+    import torch
+
+    from ml_engine_b200.session import Session
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    GB, S, V = 256, 256, 8192
+    if GB % world:
+        raise SystemExit(f"global batch {GB} does not split over {world} ranks")
+    B = GB // world
+    s = Session.encdec(batch=B, seq_len=S, d_model=512, heads=8, ffn=2048, layers=6, vocab=V, lr=1e-4, adamw=1,
+                       clip_norm=1.0, fused_attention=1, seed=2024)
+    if world > 1:
+        import torch.distributed as dist
+        uid = [Session.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        s.enable_dp(uid[0], rank, world, bucket_mb=32)
+    stream = torch.cuda.ExternalStream(s.stream, device=dev)
+    rng = np.random.default_rng(3000 + rank)
+    zipf = 1.0 / np.arange(1, V + 1) ** 1.1
+    zipf /= zipf.sum()
+    pool = []
+    for _ in range(4):
+        seq = rng.choice(V, size=(B, S + 1), p=zipf).astype(np.int32)
+        src = rng.choice(V, size=(B, S), p=zipf).astype(np.int32)
+        pool.append((src.ravel(), seq[:, :S].ravel().copy(), seq[:, 1:].ravel().copy()))
+
+    def feed(i):
+        s.inputs["src"][:], s.inputs["tgt_in"][:], s.inputs["tgt_out"][:] = pool[i % len(pool)]
+
+    feed(0)
+    s.step()
+    s.capture()
+    for i in range(max(args.warmup, 3)):
+        feed(i)
+        s.step()
+    import ctypes
+    kk, mm, cc = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    s._lib.call("mle_session_graph_counts", s._h, ctypes.addressof(kk), ctypes.addressof(mm), ctypes.addressof(cc))
+    smi_index = os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank] \
+        if "CUDA_VISIBLE_DEVICES" in os.environ else str(local_rank)
+    with ClockSampler(smi_index) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            s.step(upload=False, read_loss=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
+        barrier(world)
+        torch.cuda.synchronize()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        loss = None
+        for i in range(args.steps):
+            feed(i)
+            loss = s.step(upload=True, read_loss=True)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps, world, dev)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "train steps/s (fwd+bwd+AdamW), configs[2] encoder-decoder", "value": 1e3 / ms,
+            "unit": "steps/s", "tokens_per_s": GB * S * 1e3 / ms, "ms_per_step": ms, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "dtype": "f32 (tf32 tensor-core products)", "data": "synthetic (Zipf(1.1) token ids)",
+            "config": {"workload": "configs[2]: enc-dec 6+6, d 512, 8 heads, FFN 2048, seq 256, vocab 8192",
+                       "global_batch": GB, "per_rank_batch": B, "seq_len": S, "parallelism": f"dp{world}"},
+            "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": 3 * B * S * 4, "d2h_bytes_per_step": 4, "loss_last": loss},
+            "gpu_launches": kk.value * args.steps, "clocks": clocks.summary()}), flush=True)
+    s.close()
+
+
 # ------------------------------------------------------------ native arm
 def run_native(args, rank, world, local_rank):
     import numpy as np
@@ -474,8 +559,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="configs[4] kernel sweep, one JSON line per case")
-    ap.add_argument("--config", default="encoder", choices=["encoder", "unet"],
-                    help="encoder: configs[1], the benchmark line; unet: configs[3] on one GPU")
+    ap.add_argument("--config", default="encoder", choices=["encoder", "unet", "encdec"],
+                    help="encoder: configs[1], the benchmark line; unet: configs[3] on one GPU; "
+                         "encdec: configs[2], global batch 256 over the ranks")
     ap.add_argument("--roofline-only", action="store_true",
                     help="run only the roofline kernel pair (3 + 2 pairs; for a profiler capture)")
     args = ap.parse_args()
@@ -495,6 +581,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.config == "encdec":
+            run_encdec(args, rank, world, local_rank)
         else:
             run_native(args, rank, world, local_rank)
     finally:

@@ -378,6 +378,22 @@ int mle_attention_bwd(const float* Q, const float* K, const float* V, const floa
  * layout), 0 if they need the head-major composed path. */
 int mle_attention_fused_supported(int seq_q, int seq_k, int head_dim, int softmax_axis, int key_grad_mode);
 
+/* Which implementation mle_attention_fwd/bwd use for the column softmax on
+ * this host thread (no counterpart in the reference):
+ *   MLE_ATTN_PATH_AUTO  : tensor cores in TF32 GEMM mode for long sequences
+ *                         (Sq*Sk*hd >= 2^21, e.g. 256 x 256 x 64), the CUDA-
+ *                         core kernels in the reference's summation order
+ *                         otherwise and in FP32 GEMM mode;
+ *   MLE_ATTN_PATH_FUSED : always the CUDA-core kernels where they apply;
+ *   MLE_ATTN_PATH_TENSOR: tensor cores wherever the sizes allow (TF32 GEMM
+ *                         mode, Sq <= 256, Sq, Sk, hd multiples of 4; the
+ *                         reference key gradient also needs Sq == Sk, hd a
+ *                         multiple of 32 dividing Sk).
+ * The tensor-core backward writes its score gradients to `workspace`. */
+enum mle_attn_path { MLE_ATTN_PATH_AUTO = 0, MLE_ATTN_PATH_FUSED = 1, MLE_ATTN_PATH_TENSOR = 2 };
+int mle_set_attention_path(int path);
+int mle_get_attention_path(void);
+
 /* Positional table of MatPEncoding alone, table[r, c] = (float)sin/cos of
  * the angle for position r + start_idx (Engine/kernels.cu:166-185), and its
  * broadcast add y[b, i] = x[b, i] + table[i]: together bitwise equal to

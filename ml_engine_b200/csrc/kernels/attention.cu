@@ -19,6 +19,16 @@
 // and the gradients are read and written token-major ([B, S, H*hd], the
 // Linear layout) or head-major through strides, so no head copies are made.
 //
+// Tensor-core path (TF32 GEMM mode; chosen for long sequences, where the
+// CUDA-core kernels' serial sums dominate the step, or on request through
+// mle_set_attention_path): the two forward and four backward products run
+// on the tcgen05 GEMM, which reads Q, K, V, dO and writes O, dQ, dK, dV in
+// either layout through strides, P and the score gradients [B,H,Sq,Sk] in
+// between; the column softmax and its backward are column-block kernels
+// holding a column in registers.  The reference's key gradient (memory of
+// dScores read as [Sk,Sq], result laid out [hd,Sk] in the head's block) is
+// one GEMM whose output columns are split over rows of the head block.
+//
 // Other shapes run the composed path on the tensor-core GEMM (head-major).
 #include <float.h>
 
@@ -27,6 +37,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "gemm.cuh"
 
 namespace mle {
 namespace {
@@ -528,12 +539,215 @@ int dispatch_hd(int hd, F&& f) {
     }
 }
 
+// ------------------------------ tensor-core path -----------------------------
+thread_local int g_attn_path = MLE_ATTN_PATH_AUTO;
+constexpr int kTcMaxRows = 256;  // column softmax kernels keep a column in registers
+
+// Column softmax of each [rows, cols] matrix in place (the reference's type
+// 1, causal entries key > query zeroed after the max over the whole column,
+// as SoftMask does).  Block = 8 warps over (matrix, 32 columns); lane = the
+// column, warp w holds rows w, w+8, ...
+template <int R>
+__global__ void __launch_bounds__(256) col_softmax_regs(float* __restrict__ P, int rows, int cols, int causal,
+                                                        int mats) {
+    pdl_entry();
+    __shared__ float red[8][33];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    for (int mat = blockIdx.y; mat < mats; mat += gridDim.y) {
+        float* Pm = P + (int64_t)mat * rows * cols;
+        float v[R];
+        float m = -FLT_MAX;
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int r = warp + 8 * i;
+            v[i] = (r < rows && c < cols) ? Pm[(int64_t)r * cols + c] : -FLT_MAX;
+            m = fmaxf(m, v[i]);
+        }
+        red[warp][lane] = m;
+        __syncthreads();
+#pragma unroll
+        for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w][lane]);
+        __syncthreads();
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int r = warp + 8 * i;
+            const float e = (r < rows && c < cols && !(causal && c > r)) ? expf(v[i] - m) : 0.f;
+            v[i] = e;
+            sum += e;
+        }
+        red[warp][lane] = sum;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tot += red[w][lane];
+        __syncthreads();
+        if (tot < 1e-45f) tot = 1.0f;
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int r = warp + 8 * i;
+            if (r < rows && c < cols) Pm[(int64_t)r * cols + c] = v[i] / tot;
+        }
+    }
+}
+
+// G (dP on entry) becomes dS = P (dP - sum over the column of P dP).
+template <int R>
+__global__ void __launch_bounds__(256) col_softmax_bwd_regs(const float* __restrict__ P, float* __restrict__ G,
+                                                            int rows, int cols, int mats) {
+    pdl_entry();
+    __shared__ float red[8][33];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    for (int mat = blockIdx.y; mat < mats; mat += gridDim.y) {
+        const float* Pm = P + (int64_t)mat * rows * cols;
+        float* Gm = G + (int64_t)mat * rows * cols;
+        float pv[R], gv[R];
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int r = warp + 8 * i;
+            const bool in = r < rows && c < cols;
+            pv[i] = in ? Pm[(int64_t)r * cols + c] : 0.f;
+            gv[i] = in ? Gm[(int64_t)r * cols + c] : 0.f;
+            dot += pv[i] * gv[i];
+        }
+        red[warp][lane] = dot;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tot += red[w][lane];
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int r = warp + 8 * i;
+            if (r < rows && c < cols) Gm[(int64_t)r * cols + c] = pv[i] * (gv[i] - tot);
+        }
+    }
+}
+
+int tc_col_softmax(float* P, int64_t mats, int rows, int cols, int causal, cudaStream_t st) {
+    const dim3 grid((unsigned)((cols + 31) / 32), (unsigned)std::min<int64_t>(mats, 65535));
+    if (rows <= 64) launch_k(col_softmax_regs<8>, grid, 256, 0, st, P, rows, cols, causal, (int)mats);
+    else if (rows <= 128) launch_k(col_softmax_regs<16>, grid, 256, 0, st, P, rows, cols, causal, (int)mats);
+    else launch_k(col_softmax_regs<32>, grid, 256, 0, st, P, rows, cols, causal, (int)mats);
+    return launch_status();
+}
+
+int tc_col_softmax_bwd(const float* P, float* G, int64_t mats, int rows, int cols, cudaStream_t st) {
+    const dim3 grid((unsigned)((cols + 31) / 32), (unsigned)std::min<int64_t>(mats, 65535));
+    if (rows <= 64) launch_k(col_softmax_bwd_regs<8>, grid, 256, 0, st, P, G, rows, cols, (int)mats);
+    else if (rows <= 128) launch_k(col_softmax_bwd_regs<16>, grid, 256, 0, st, P, G, rows, cols, (int)mats);
+    else launch_k(col_softmax_bwd_regs<32>, grid, 256, 0, st, P, G, rows, cols, (int)mats);
+    return launch_status();
+}
+
+GemmProblem attn_gemm(const float* A, const float* B, float* C, int M, int N, int K, int64_t lda, int64_t ldb,
+                      int64_t ldc, int ta, int tb, int nb, int nh, int64_t a_sb, int64_t a_sh, int64_t b_sb,
+                      int64_t b_sh, int64_t c_sb, int64_t c_sh, float alpha, int mode) {
+    GemmProblem p;
+    memset(&p, 0, sizeof(p));
+    p.A = A;
+    p.B = B;
+    p.C = C;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.lda = lda;
+    p.ldb = ldb;
+    p.ldc = ldc;
+    p.trans_a = ta;
+    p.trans_b = tb;
+    p.nbatch = nb;
+    p.channels = nh;
+    p.a_sb = a_sb;
+    p.a_sc = a_sh;
+    p.b_sb = b_sb;
+    p.b_sc = b_sh;
+    p.c_sb = c_sb;
+    p.c_sc = c_sh;
+    p.alpha = alpha;
+    p.mode = mode;
+    return p;
+}
+
+// Whether the tensor-core path can run these sizes (GEMM operand strides in
+// whole 16-byte units, columns of at most kTcMaxRows rows for the softmax
+// kernels, the reference key gradient's head-block split in whole 32-column
+// blocks) and is the one to take.
+bool tc_attention_ok(int axis, int Sq, int Sk, int hd, int64_t BH, bool bwd, int key_mode) {
+    if (g_attn_path == MLE_ATTN_PATH_FUSED || mle_get_gemm_mode() != MLE_GEMM_MODE_TF32) return false;
+    if (axis != 1 || Sq > kTcMaxRows || hd % 4 || Sq % 4 || Sk % 4 || BH > INT32_MAX) return false;
+    if (bwd && key_mode == MLE_KEYGRAD_REFERENCE && !(Sq == Sk && hd % 32 == 0 && Sk % hd == 0)) return false;
+    if (g_attn_path == MLE_ATTN_PATH_TENSOR) return true;
+    // the CUDA-core kernels win below about 2M multiply-adds per head product
+    return (int64_t)Sq * Sk * hd >= (1ll << 21) || !fused_ok(axis, Sq, Sk, hd, 1, 1);
+}
+
+int tc_attention_fwd(const float* Q, const float* K, const float* V, float* P, float* O, int B, int H, int Sq, int Sk,
+                     int hd, float scale, int causal, int layout, cudaStream_t st) {
+    int64_t qb, qh, qs, kb, kh, ks;
+    strides_for(layout, H, Sq, hd, qb, qh, qs);
+    strides_for(layout, H, Sk, hd, kb, kh, ks);
+    const int64_t pb = (int64_t)H * Sq * Sk, ph = (int64_t)Sq * Sk;
+    // P = scale Q K^T, softmax over each column, O = P V
+    int s = run_gemm(attn_gemm(Q, K, P, Sq, Sk, hd, qs, ks, Sk, 0, 1, B, H, qb, qh, kb, kh, pb, ph, scale, 0), st);
+    if (s) return s;
+    s = tc_col_softmax(P, (int64_t)B * H, Sq, Sk, causal, st);
+    if (s) return s;
+    return run_gemm(attn_gemm(P, V, O, Sq, hd, Sk, Sk, ks, qs, 0, 0, B, H, pb, ph, kb, kh, qb, qh, 1.0f, 0), st);
+}
+
+int tc_attention_bwd(const float* Q, const float* K, const float* V, const float* P, const float* dO, float* dQ,
+                     float* dK, float* dV, float* dP_out, float* dS_out, float* W, int B, int H, int Sq, int Sk,
+                     int hd, float scale, int key_mode, int layout, cudaStream_t st) {
+    int64_t qb, qh, qs, kb, kh, ks;
+    strides_for(layout, H, Sq, hd, qb, qh, qs);
+    strides_for(layout, H, Sk, hd, kb, kh, ks);
+    const int64_t pb = (int64_t)H * Sq * Sk, ph = (int64_t)Sq * Sk, ns = (int64_t)B * pb;
+    // W = dO V^T (the softmax node's gradient)
+    int s = run_gemm(attn_gemm(dO, V, W, Sq, Sk, hd, qs, ks, Sk, 0, 1, B, H, qb, qh, kb, kh, pb, ph, 1.0f, 0), st);
+    if (s) return s;
+    if (dP_out && (s = mle_accumulate(W, dP_out, ns, 1.0, st)) != 0) return s;
+    // W = P (W - column sums of P W), the score gradient
+    s = tc_col_softmax_bwd(P, W, (int64_t)B * H, Sq, Sk, st);
+    if (s) return s;
+    if (dS_out && (s = mle_accumulate(W, dS_out, ns, 1.0, st)) != 0) return s;
+    // dV += P^T dO
+    s = run_gemm(attn_gemm(P, dO, dV, Sk, hd, Sq, Sk, qs, ks, 1, 0, B, H, pb, ph, qb, qh, kb, kh, 1.0f, 1), st);
+    if (s) return s;
+    // dQ += scale W K
+    s = run_gemm(attn_gemm(W, K, dQ, Sq, hd, Sk, Sk, ks, qs, 0, 0, B, H, pb, ph, kb, kh, qb, qh, scale, 1), st);
+    if (s) return s;
+    if (key_mode == MLE_KEYGRAD_TRUE)  // dK += scale W^T Q
+        return run_gemm(attn_gemm(W, Q, dK, Sk, hd, Sq, Sk, qs, ks, 1, 0, B, H, pb, ph, qb, qh, kb, kh, scale, 1),
+                        st);
+    // reference: the head block of dK receives scale * Q^T M^T as [hd, Sk],
+    // M = W's memory read as [Sk, Sq]; block element (d, i) lives at row
+    // d*(Sk/hd) + i/hd, column i % hd of the head in `layout`
+    GemmProblem g = attn_gemm(Q, W, dK, hd, Sk, Sq, qs, Sq, (int64_t)(Sk / hd) * ks, 1, 1, B, H, qb, qh, pb, ph, kb,
+                              kh, scale, 1);
+    g.c_split = hd;
+    g.c_split_ld = ks;
+    return run_gemm(g, st);
+}
+
 }  // namespace
 }  // namespace mle
 
 using namespace mle;
 
 extern "C" {
+
+int mle_set_attention_path(int path) {
+    if (path != MLE_ATTN_PATH_AUTO && path != MLE_ATTN_PATH_FUSED && path != MLE_ATTN_PATH_TENSOR)
+        return MLE_ERR_ARG;
+    g_attn_path = path;
+    return MLE_OK;
+}
+
+int mle_get_attention_path(void) { return g_attn_path; }
 
 int mle_attention_fused_supported(int seq_q, int seq_k, int head_dim, int softmax_axis, int key_grad_mode) {
     if (!fused_ok(softmax_axis, seq_q, seq_k, head_dim, 1, 1)) return 0;
@@ -555,6 +769,11 @@ int mle_attention_fwd(const float* Q, const float* K, const float* V, float* P, 
     if ((softmax_axis != 0 && softmax_axis != 1) || (layout != MLE_ATTN_HEAD_MAJOR && layout != MLE_ATTN_TOKEN_MAJOR))
         return MLE_ERR_ARG;
     cudaStream_t st = as_stream(stream);
+    if (tc_attention_ok(softmax_axis, seq_q, seq_k, head_dim, (int64_t)batch * heads, false, MLE_KEYGRAD_TRUE) &&
+        ptrs_aligned({Q, K, V, P, O})) {
+        const int s = tc_attention_fwd(Q, K, V, P, O, batch, heads, seq_q, seq_k, head_dim, scale, causal, layout, st);
+        if (s != MLE_ERR_UNSUPPORTED) return s;
+    }
     if (fused_ok(softmax_axis, seq_q, seq_k, head_dim, batch, heads) && ptrs_aligned({Q, K, V, O})) {
         AttnArgs a{};
         a.Q = Q;
@@ -593,6 +812,15 @@ int mle_attention_bwd(const float* Q, const float* K, const float* V, const floa
         return MLE_ERR_ARG;
     if (key_grad_mode != MLE_KEYGRAD_REFERENCE && key_grad_mode != MLE_KEYGRAD_TRUE) return MLE_ERR_ARG;
     cudaStream_t st = as_stream(stream);
+    // every check of the tensor-core path precedes its first write, so a
+    // refusal (MLE_ERR_UNSUPPORTED) leaves the gradients untouched
+    if (workspace &&
+        tc_attention_ok(softmax_axis, seq_q, seq_k, head_dim, (int64_t)batch * heads, true, key_grad_mode) &&
+        ptrs_aligned({Q, K, V, P, dO, dQ, dK, dV, workspace})) {
+        const int s = tc_attention_bwd(Q, K, V, P, dO, dQ, dK, dV, dP_out, dS_out, workspace, batch, heads, seq_q,
+                                       seq_k, head_dim, scale, key_grad_mode, layout, st);
+        if (s != MLE_ERR_UNSUPPORTED) return s;
+    }
     const bool ref_shape_ok = key_grad_mode == MLE_KEYGRAD_TRUE || seq_q == seq_k;
     if (fused_ok(softmax_axis, seq_q, seq_k, head_dim, batch, heads) && ref_shape_ok &&
         ptrs_aligned({Q, K, V, dO, dQ, dK, dV})) {

@@ -19,6 +19,10 @@ struct GemmProblem {
     int64_t a_sb, a_sc, b_sb, b_sc, c_sb, c_sc;  // element strides, 0 = broadcast
     float alpha;
     int mode;  // 0 assign, 1 +=, 2 atomic add
+    // > 0: C's column n lives at (n % c_split) + (n / c_split) * c_split_ld
+    // (tensor-core path only; c_split a multiple of 32 dividing N)
+    int c_split = 0;
+    int64_t c_split_ld = 0;
 };
 
 // Implicit-GEMM convolution at stride 1 over KW horizontally shifted

@@ -72,6 +72,7 @@ struct EpiParams {
     int conv;
     int cv_kw, cv_pad, cv_w, cv_cblk, cv_nb;
     int c_trans;                      // tile rows run along C's contiguous dimension (TMA epilogue only)
+    int c_split;                      // > 0: C's inner coordinate is split (x % c_split, x / c_split), 5-D map
 };
 
 // Output tile `t` of the persistent walk: n fastest, then m, then (batch,
@@ -210,6 +211,38 @@ __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const 
             reinterpret_cast<uint64_t>(map)),
         "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
+}
+
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3,
+                                             int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_5d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                                  int c3, int c4) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.5d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
+// One staged 32 x 32 block of C leaves: (inner, outer) are its C coordinates
+// along the contiguous and the row dimension.
+__device__ __forceinline__ void store_block(const CUtensorMap* map, const void* blk, const EpiParams& ep, int inner,
+                                            int outer, int cz, int bz) {
+    if (ep.c_split) {
+        const int lo = inner % ep.c_split, hi = inner / ep.c_split;
+        if (ep.mode == EPI_ASSIGN) tma_store_5d(map, blk, lo, hi, outer, cz, bz);
+        else tma_reduce_add_5d(map, blk, lo, hi, outer, cz, bz);
+    } else {
+        if (ep.mode == EPI_ASSIGN) tma_store_4d(map, blk, inner, outer, cz, bz);
+        else tma_reduce_add_4d(map, blk, inner, outer, cz, bz);
+    }
 }
 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -534,9 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         fence_async_smem();
                         __syncwarp();
                         if (lane == 0) {
-                            const int cz = ep.c_has_c ? x.cidx : 0, bz = ep.c_has_b ? x.bidx : 0;
-                            if (ep.mode == EPI_ASSIGN) tma_store_4d(tmC, blk, row0, col0, cz, bz);
-                            else tma_reduce_add_4d(tmC, blk, row0, col0, cz, bz);
+                            store_block(tmC, blk, ep, row0, col0, ep.c_has_c ? x.cidx : 0, ep.c_has_b ? x.bidx : 0);
                             bulk_commit();
                         }
                         ++blocks_out;
@@ -570,9 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        const int cz = ep.c_has_c ? x.cidx : 0, bz = ep.c_has_b ? x.bidx : 0;
-                        if (ep.mode == EPI_ASSIGN) tma_store_4d(tmC, blk, col0, row0, cz, bz);
-                        else tma_reduce_add_4d(tmC, blk, col0, row0, cz, bz);
+                        store_block(tmC, blk, ep, col0, row0, ep.c_has_c ? x.cidx : 0, ep.c_has_b ? x.bidx : 0);
                         bulk_commit();
                     }
                     ++blocks_out;
@@ -703,20 +732,20 @@ static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner
     return r == CUDA_SUCCESS;
 }
 
-// 4-D fp32 tensor map with explicit extents, element strides of dims 1..3
-// and box.
-static bool encode_map(CUtensorMap* map, const float* base, const int64_t dims[4], const int64_t strides[3],
-                       const int box[4], CUtensorMapSwizzle swizzle) {
+// fp32 tensor map of `rank` (4 or 5) dims with explicit extents, element
+// strides of dims 1.. and box.
+static bool encode_map(CUtensorMap* map, const float* base, const int64_t* dims, const int64_t* strides,
+                       const int* box, CUtensorMapSwizzle swizzle, int rank = 4) {
     EncodeTiledFn enc = get_encode();
-    if (!enc) return false;
-    cuuint64_t d[4], st[3];
-    cuuint32_t b[4], e[4] = {1, 1, 1, 1};
-    for (int i = 0; i < 4; ++i) {
+    if (!enc || rank < 1 || rank > 5) return false;
+    cuuint64_t d[5], st[4];
+    cuuint32_t b[5], e[5] = {1, 1, 1, 1, 1};
+    for (int i = 0; i < rank; ++i) {
         d[i] = (cuuint64_t)dims[i];
         b[i] = (cuuint32_t)box[i];
     }
-    for (int i = 0; i < 3; ++i) st[i] = (cuuint64_t)(strides[i] * 4);
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), d, st, b, e,
+    for (int i = 0; i + 1 < rank; ++i) st[i] = (cuuint64_t)(strides[i] * 4);
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<float*>(base), d, st, b, e,
                CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -914,6 +943,23 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
     ep.c_has_b = (ep.c_stride_b != 0);
     ep.c_has_c = (ep.c_stride_c != 0);
     ep.tma_epi = 0;
+    if (p.c_split) {
+        // 5-D map (n % c_split, n / c_split, m, channel, batch); only through TMA
+        if (p.c_split % 32 || p.N % p.c_split || !aligned16(p.C) || (p.ldc & 3) || (p.c_split_ld & 3) ||
+            (ep.c_stride_b & 3) || (ep.c_stride_c & 3) || (splits > 1 && p.mode == EPI_ASSIGN))
+            return MLE_OK;
+        const int64_t nc = ep.c_has_c ? p.channels : 1, nb = ep.c_has_b ? p.nbatch : 1;
+        const int64_t sc = ep.c_has_c ? ep.c_stride_c : (int64_t)p.ldc * p.M;
+        const int64_t sb = ep.c_has_b ? ep.c_stride_b : sc * nc;
+        const int64_t dims[5] = {p.c_split, p.N / p.c_split, p.M, nc, nb};
+        const int64_t str[4] = {p.c_split_ld, p.ldc, sc, sb};
+        const int box[5] = {32, 1, 32, 1, 1};
+        if (!encode_map(&grp.c[g], p.C, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B, 5)) return MLE_OK;
+        ep.tma_epi = 1;
+        ep.c_split = p.c_split;
+        ok = true;
+        return MLE_OK;
+    }
     if (aligned16(p.C) && (p.ldc & 3) == 0 && (ep.c_stride_b & 3) == 0 && (ep.c_stride_c & 3) == 0) {
         OperandView vc;
         vc.base = p.C;
@@ -961,7 +1007,7 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
         // empty reduction: assign writes alpha*0 (+bias); accumulate is a no-op
         if (p.mode != tc::EPI_ASSIGN) return MLE_OK;
     }
-    if (!tc_path(p)) return simt_gemm(p, st);
+    if (!tc_path(p)) return p.c_split ? MLE_ERR_UNSUPPORTED : simt_gemm(p, st);
     int BN, splits;
     choose_tiles(&p, 1, BN, splits);
     tc::GemmGroup grp;
@@ -969,7 +1015,7 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     bool ok = false;
     const int s = prepare(p, BN, splits, false, grp, 0, st, ok);
     if (s) return s;
-    if (!ok) return simt_gemm(p, st);
+    if (!ok) return p.c_split ? MLE_ERR_UNSUPPORTED : simt_gemm(p, st);
     grp.n = 1;
     grp.tile_start[0] = 0;
     grp.tile_start[1] = grp.ep[0].tiles;

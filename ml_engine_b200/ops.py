@@ -194,9 +194,9 @@ def attention_fwd(Q, K, V, P, O, batch, heads, seq_q, seq_k, head_dim, scale, ca
 
 def attention_bwd(Q, K, V, P, dO, dQ, dK, dV, dP, dS, batch, heads, seq_q, seq_k, head_dim, scale, causal=0,
                   softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE, layout=HEAD_MAJOR, workspace=None):
-    """workspace: batch*heads*seq_q*seq_k floats for the fused path; made
-    here when not given."""
-    if workspace is None and attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis, key_grad_mode):
+    """workspace: batch*heads*seq_q*seq_k floats for the fused and the
+    tensor-core paths; made here when not given."""
+    if workspace is None:
         workspace = torch.empty(batch * heads * seq_q * seq_k, device=Q.device, dtype=torch.float32)
     _call("mle_attention_bwd", _p(Q), _p(K), _p(V), _p(P), _p(dO), _p(dQ), _p(dK), _p(dV), _p(dP), _p(dS),
           _p(workspace), batch, heads, seq_q, seq_k, head_dim, scale, causal, softmax_axis, key_grad_mode, layout,
@@ -205,6 +205,27 @@ def attention_bwd(Q, K, V, P, dO, dQ, dK, dV, dP, dS, batch, heads, seq_q, seq_k
 
 def attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE):
     return bool(kernels().mle_attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis, key_grad_mode))
+
+
+ATTN_PATH_AUTO, ATTN_PATH_FUSED, ATTN_PATH_TENSOR = 0, 1, 2
+
+
+def set_attention_path(path):
+    """Attention implementation on this thread (mle_set_attention_path);
+    returns the previous one."""
+    old = kernels().mle_get_attention_path()
+    _call("mle_set_attention_path", path)
+    return old
+
+
+def attention_tensor_supported(seq_q, seq_k, head_dim, softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE,
+                               backward=True):
+    """Whether ATTN_PATH_TENSOR runs these sizes on the tensor cores (TF32
+    GEMM mode)."""
+    ok = softmax_axis == 1 and seq_q <= 256 and seq_q % 4 == 0 and seq_k % 4 == 0 and head_dim % 4 == 0
+    if backward and key_grad_mode == KEYGRAD_REFERENCE:
+        ok = ok and seq_q == seq_k and head_dim % 32 == 0 and seq_k % head_dim == 0
+    return ok
 
 
 def matpe_table(table, rows, cols, start_idx=0):

@@ -379,13 +379,30 @@ def test_linear_fwd_bwd(cuda, ops, orc, rng, rows, fin, fout):
 
 # ------------------------------------------------------------------ attention
 ATTN_CASES = [  # B, H, Sq, Sk, hd, axis, causal
-    (2, 8, 128, 128, 32, 1, 0),   # configs[1] shape per head: fused
-    (2, 4, 64, 64, 64, 1, 1),     # masked (SoftMask): fused
-    (1, 2, 256, 256, 64, 1, 1),   # configs[2] head shape: fused
-    (1, 2, 40, 72, 16, 1, 0),     # Sq != Sk: fused for the true key gradient, composed for the reference one
-    (2, 3, 37, 37, 32, 1, 1),     # ragged row and key blocks, masked: fused
+    (2, 8, 128, 128, 32, 1, 0),   # configs[1] shape per head
+    (2, 4, 64, 64, 64, 1, 1),     # masked (SoftMask)
+    (1, 2, 256, 256, 64, 1, 1),   # configs[2] head shape
+    (1, 2, 40, 72, 16, 1, 0),     # Sq != Sk: the reference key gradient needs the composed path
+    (2, 3, 37, 37, 32, 1, 1),     # ragged row and key blocks, masked: CUDA-core kernels only
     (1, 2, 40, 72, 16, 0, 0),     # row-wise softmax: composed (tensor cores)
 ]
+
+
+@pytest.fixture(params=["fused", "tensor"])
+def attn_path(request, ops):
+    """Runs each attention case with the CUDA-core kernels in the reference's
+    order (exact) and with the tensor-core path (TF32 tolerance) forced."""
+    old = ops.set_attention_path(ops.ATTN_PATH_FUSED if request.param == "fused" else ops.ATTN_PATH_TENSOR)
+    yield request.param
+    ops.set_attention_path(old)
+
+
+def _attn_tol(ops, path, Sq, Sk, D, axis, key_mode, backward):
+    """(tolerance, runs token-major) for the path the entry points take."""
+    fused = ops.attention_fused_supported(Sq, Sk, D, axis, key_mode if backward else 1)
+    if path == "tensor" and ops.attention_tensor_supported(Sq, Sk, D, axis, key_mode, backward):
+        return RTOL_TC, True
+    return (1e-5 if fused else RTOL_TC), fused
 
 
 def _attn_inputs(rng, B, Hh, Sq, Sk, D):
@@ -405,11 +422,11 @@ def _from_token_major(x, B, Hh, D):
 
 @pytest.mark.parametrize("layout", [0, 1])
 @pytest.mark.parametrize("case", ATTN_CASES)
-def test_attention_fwd(cuda, ops, orc, rng, case, layout):
+def test_attention_fwd(cuda, ops, orc, rng, case, layout, attn_path):
     B, Hh, Sq, Sk, D, axis, causal = case
-    fused = ops.attention_fused_supported(Sq, Sk, D, axis, 1)
-    if layout == 1 and not fused:
-        pytest.skip("token-major layout is served by the fused kernels only")
+    tol, token_major_ok = _attn_tol(ops, attn_path, Sq, Sk, D, axis, 1, False)
+    if layout == 1 and not token_major_ok:
+        pytest.skip("token-major layout needs the fused or the tensor-core path")
     Q, K, V, _ = _attn_inputs(rng, B, Hh, Sq, Sk, D)
     scale = float(1.0 / np.sqrt(D))
     conv = (lambda x: _to_token_major(x, B, Hh)) if layout else (lambda x: x)
@@ -420,7 +437,6 @@ def test_attention_fwd(cuda, ops, orc, rng, case, layout):
     S = orc.bcmm(1, Q, K, np.zeros((B * Hh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 0, 3, 3, 3)
     rP = orc.softmax_fwd(orc.scale_write(S, scale), B * Hh, Sq, Sk, axis, causal)
     rO = orc.bcmm(0, rP, V, np.zeros((B * Hh, Sq, D), np.float32), B, Hh, Sq, Sk, D, 0, 3, 3, 3)
-    tol = 1e-5 if fused else RTOL_TC
     o = H(O)
     if layout:
         o = _from_token_major(o, B, Hh, D)
@@ -431,11 +447,11 @@ def test_attention_fwd(cuda, ops, orc, rng, case, layout):
 @pytest.mark.parametrize("layout", [0, 1])
 @pytest.mark.parametrize("key_mode", [0, 1])
 @pytest.mark.parametrize("case", ATTN_CASES)
-def test_attention_bwd(cuda, ops, orc, rng, case, key_mode, layout):
+def test_attention_bwd(cuda, ops, orc, rng, case, key_mode, layout, attn_path):
     B, Hh, Sq, Sk, D, axis, causal = case
-    fused = ops.attention_fused_supported(Sq, Sk, D, axis, key_mode)
-    if layout == 1 and not fused:
-        pytest.skip("token-major layout is served by the fused kernels only")
+    tol, token_major_ok = _attn_tol(ops, attn_path, Sq, Sk, D, axis, key_mode, True)
+    if layout == 1 and not token_major_ok:
+        pytest.skip("token-major layout needs the fused or the tensor-core path")
     bh = B * Hh
     Q, K, V, dO = _attn_inputs(rng, B, Hh, Sq, Sk, D)
     scale = float(1.0 / np.sqrt(D))
@@ -458,7 +474,6 @@ def test_attention_bwd(cuda, ops, orc, rng, case, key_mode, layout):
         rdK = orc.bcmm(3, Q, rdS, np.zeros((bh, Sk, D), np.float32), B, Hh, D, Sq, Sk, 1, 3, 3, 3)
     else:              # the mathematical gradient dS^T Q
         rdK = orc.bcmm(2, rdS, Q, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
-    tol = 1e-5 if fused else RTOL_TC
     assert rel_err(H(dP), rdP) <= tol
     assert rel_err(H(dS), rdSc) <= tol
     assert rel_err(back(H(dV)) - dV0, rdV) <= tol

@@ -187,6 +187,7 @@ def test_fused_attention_bitwise_vs_reference_chain(cuda, ref, ops, rng, mask):
     P, O, dQ, dK (reference key gradient) and dV are bitwise equal."""
     B, Hh, S, D = 2, 4, 128, 32
     bh, n_s = B * Hh, B * Hh * S * S
+    old_path = ops.set_attention_path(ops.ATTN_PATH_FUSED)
     Q, K, V, dO = (rng.standard_normal((bh, S, D)).astype(np.float32) for _ in range(4))
     scale = float(np.float32(1.0 / np.sqrt(D)))  # GraphOperations::Scale holds a float
     tQ, tK, tV, tdO = (T(a, cuda) for a in (Q, K, V, dO))
@@ -215,5 +216,6 @@ def test_fused_attention_bitwise_vs_reference_chain(cuda, ref, ops, rng, mask):
     dQ, dK, dV = (torch.zeros(bh * S * D, device=cuda) for _ in range(3))
     dP, dS = torch.zeros(n_s, device=cuda), torch.zeros(n_s, device=cuda)
     ops.attention_bwd(tQ, tK, tV, P, tdO, dQ, dK, dV, dP, dS, B, Hh, S, S, D, scale, mask, 1, 0, 0)
+    ops.set_attention_path(old_path)
     for mine, theirs in ((dP, rdP), (dS, rdSc), (dV, rdV), (dQ, rdQ), (dK, rdK)):
         assert np.array_equal(H(mine), H(theirs))
