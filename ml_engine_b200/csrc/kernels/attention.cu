@@ -25,7 +25,7 @@
 // on the tcgen05 GEMM, which reads Q, K, V, dO and writes O, dQ, dK, dV in
 // either layout through strides, P and the score gradients [B,H,Sq,Sk] in
 // between; the column softmax and its backward are column-block kernels
-// holding a column in registers.  The reference's key gradient (memory of
+// that park a 32-column slab in shared memory between their passes.  The reference's key gradient (memory of
 // dScores read as [Sk,Sq], result laid out [hd,Sk] in the head's block) is
 // one GEMM whose output columns are split over rows of the head block.
 //
@@ -545,24 +545,27 @@ constexpr int kTcMaxRows = 256;  // column softmax kernels keep a column in regi
 
 // Column softmax of each [rows, cols] matrix in place (the reference's type
 // 1, causal entries key > query zeroed after the max over the whole column,
-// as SoftMask does).  Block = 8 warps over (matrix, 32 columns); lane = the
-// column, warp w holds rows w, w+8, ...
-template <int R>
-__global__ void __launch_bounds__(256) col_softmax_regs(float* __restrict__ P, int rows, int cols, int causal,
-                                                        int mats) {
+// as SoftMask does).  A 256-thread block owns (matrix, 32 columns): lane =
+// the column, warp w the rows w, w + 8, ...; each thread parks its values
+// in shared memory between the passes (rows x 32 floats per block), so
+// several blocks share an SM and their loads overlap.
+constexpr int kSmThreads = 256;
+
+__global__ void __launch_bounds__(kSmThreads) col_softmax_smem(float* __restrict__ P, int rows, int cols, int causal,
+                                                               int mats) {
     pdl_entry();
+    extern __shared__ float tile[];  // [rows][32]
     __shared__ float red[8][33];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
     for (int mat = blockIdx.y; mat < mats; mat += gridDim.y) {
-        float* Pm = P + (int64_t)mat * rows * cols;
-        float v[R];
+        float* Pm = P + (int64_t)mat * rows * cols + c;
         float m = -FLT_MAX;
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const int r = warp + 8 * i;
-            v[i] = (r < rows && c < cols) ? Pm[(int64_t)r * cols + c] : -FLT_MAX;
-            m = fmaxf(m, v[i]);
+#pragma unroll 4
+        for (int r = warp; r < rows; r += 8) {
+            const float v = c < cols ? Pm[(int64_t)r * cols] : -FLT_MAX;
+            tile[r * 32 + lane] = v;
+            m = fmaxf(m, v);
         }
         red[warp][lane] = m;
         __syncthreads();
@@ -570,11 +573,10 @@ __global__ void __launch_bounds__(256) col_softmax_regs(float* __restrict__ P, i
         for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w][lane]);
         __syncthreads();
         float sum = 0.f;
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const int r = warp + 8 * i;
-            const float e = (r < rows && c < cols && !(causal && c > r)) ? expf(v[i] - m) : 0.f;
-            v[i] = e;
+#pragma unroll 4
+        for (int r = warp; r < rows; r += 8) {
+            const float e = (c < cols && !(causal && c > r)) ? expf(tile[r * 32 + lane] - m) : 0.f;
+            tile[r * 32 + lane] = e;
             sum += e;
         }
         red[warp][lane] = sum;
@@ -584,34 +586,34 @@ __global__ void __launch_bounds__(256) col_softmax_regs(float* __restrict__ P, i
         for (int w = 0; w < 8; ++w) tot += red[w][lane];
         __syncthreads();
         if (tot < 1e-45f) tot = 1.0f;
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const int r = warp + 8 * i;
-            if (r < rows && c < cols) Pm[(int64_t)r * cols + c] = v[i] / tot;
+        if (c < cols) {
+#pragma unroll 4
+            for (int r = warp; r < rows; r += 8) Pm[(int64_t)r * cols] = tile[r * 32 + lane] / tot;
         }
     }
 }
 
 // G (dP on entry) becomes dS = P (dP - sum over the column of P dP).
-template <int R>
-__global__ void __launch_bounds__(256) col_softmax_bwd_regs(const float* __restrict__ P, float* __restrict__ G,
-                                                            int rows, int cols, int mats) {
+__global__ void __launch_bounds__(kSmThreads) col_softmax_bwd_smem(const float* __restrict__ P, float* __restrict__ G,
+                                                                   int rows, int cols, int mats) {
     pdl_entry();
+    extern __shared__ float tile[];  // [rows][32] of P, then [rows][32] of G
     __shared__ float red[8][33];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
+    float* tg = tile + rows * 32;
     for (int mat = blockIdx.y; mat < mats; mat += gridDim.y) {
-        const float* Pm = P + (int64_t)mat * rows * cols;
-        float* Gm = G + (int64_t)mat * rows * cols;
-        float pv[R], gv[R];
+        const float* Pm = P + (int64_t)mat * rows * cols + c;
+        float* Gm = G + (int64_t)mat * rows * cols + c;
         float dot = 0.f;
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const int r = warp + 8 * i;
-            const bool in = r < rows && c < cols;
-            pv[i] = in ? Pm[(int64_t)r * cols + c] : 0.f;
-            gv[i] = in ? Gm[(int64_t)r * cols + c] : 0.f;
-            dot += pv[i] * gv[i];
+        if (c < cols) {
+#pragma unroll 4
+            for (int r = warp; r < rows; r += 8) {
+                const float pv = Pm[(int64_t)r * cols], gv = Gm[(int64_t)r * cols];
+                tile[r * 32 + lane] = pv;
+                tg[r * 32 + lane] = gv;
+                dot += pv * gv;
+            }
         }
         red[warp][lane] = dot;
         __syncthreads();
@@ -619,27 +621,35 @@ __global__ void __launch_bounds__(256) col_softmax_bwd_regs(const float* __restr
 #pragma unroll
         for (int w = 0; w < 8; ++w) tot += red[w][lane];
         __syncthreads();
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const int r = warp + 8 * i;
-            if (r < rows && c < cols) Gm[(int64_t)r * cols + c] = pv[i] * (gv[i] - tot);
+        if (c < cols) {
+#pragma unroll 4
+            for (int r = warp; r < rows; r += 8) Gm[(int64_t)r * cols] = tile[r * 32 + lane] * (tg[r * 32 + lane] - tot);
         }
     }
 }
 
 int tc_col_softmax(float* P, int64_t mats, int rows, int cols, int causal, cudaStream_t st) {
     const dim3 grid((unsigned)((cols + 31) / 32), (unsigned)std::min<int64_t>(mats, 65535));
-    if (rows <= 64) launch_k(col_softmax_regs<8>, grid, 256, 0, st, P, rows, cols, causal, (int)mats);
-    else if (rows <= 128) launch_k(col_softmax_regs<16>, grid, 256, 0, st, P, rows, cols, causal, (int)mats);
-    else launch_k(col_softmax_regs<32>, grid, 256, 0, st, P, rows, cols, causal, (int)mats);
+    const size_t smem = (size_t)rows * 32 * sizeof(float);
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(col_softmax_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kTcMaxRows * 32 * 4);
+        configured = true;
+    }
+    launch_k(col_softmax_smem, grid, kSmThreads, smem, st, P, rows, cols, causal, (int)mats);
     return launch_status();
 }
 
 int tc_col_softmax_bwd(const float* P, float* G, int64_t mats, int rows, int cols, cudaStream_t st) {
     const dim3 grid((unsigned)((cols + 31) / 32), (unsigned)std::min<int64_t>(mats, 65535));
-    if (rows <= 64) launch_k(col_softmax_bwd_regs<8>, grid, 256, 0, st, P, G, rows, cols, (int)mats);
-    else if (rows <= 128) launch_k(col_softmax_bwd_regs<16>, grid, 256, 0, st, P, G, rows, cols, (int)mats);
-    else launch_k(col_softmax_bwd_regs<32>, grid, 256, 0, st, P, G, rows, cols, (int)mats);
+    const size_t smem = (size_t)2 * rows * 32 * sizeof(float);
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(col_softmax_bwd_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             2 * kTcMaxRows * 32 * 4);
+        configured = true;
+    }
+    launch_k(col_softmax_bwd_smem, grid, kSmThreads, smem, st, P, G, rows, cols, (int)mats);
     return launch_status();
 }
 
