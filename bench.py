@@ -562,9 +562,14 @@ def main():
     ap.add_argument("--config", default="encoder", choices=["encoder", "unet", "encdec"],
                     help="encoder: configs[1], the benchmark line; unet: configs[3] on one GPU; "
                          "encdec: configs[2], global batch 256 over the ranks")
+    ap.add_argument("--gemm-pairs", type=int, default=None, choices=[0, 1],
+                    help="run large products on CTA pairs (mle_set_gemm_pairs); default: the library's")
     ap.add_argument("--roofline-only", action="store_true",
                     help="run only the roofline kernel pair (3 + 2 pairs; for a profiler capture)")
     args = ap.parse_args()
+    if args.gemm_pairs is not None:
+        from ml_engine_b200._lib import kernels
+        kernels().call("mle_set_gemm_pairs", args.gemm_pairs)
     if args.sweep:
         run_sweep(args)
         return

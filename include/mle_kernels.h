@@ -271,6 +271,17 @@ enum mle_gemm_mode { MLE_GEMM_MODE_TF32 = 0, MLE_GEMM_MODE_FP32 = 1 };
 int mle_set_gemm_mode(int mode);
 int mle_get_gemm_mode(void);
 
+/* Whether the tensor-core GEMM may compute large products (at least two
+ * waves of 128 x 128 tiles) on CTA pairs: 2-CTA clusters whose 256 x 256
+ * tiles issue cta_group::2 MMAs, each SM staging half of the tile's B, so
+ * a pair fills shared memory with a third fewer bytes per FLOP.  Per host
+ * thread; no counterpart in the reference. */
+int mle_set_gemm_pairs(int enable);
+int mle_get_gemm_pairs(void);
+/* out3 = {tile width, split-K count, 1 if CTA pairs} of this thread's last
+ * single tensor-core product (diagnostics for tests and benchmarks). */
+int mle_gemm_last_choice(int* out3);
+
 /* Batched GEMM with the reference's broadcast flags.  Same argument meaning
  * as bcmm/bcmmABT/bcmmATB/bcmmT (Engine/kernels.cu:387-539): `backward`!=0
  * adds scale*product into C (the reference's atomicAdd), 0 assigns it.

@@ -97,7 +97,7 @@ __device__ __forceinline__ int group_of(const GemmGroup& G, int64_t t) {
     return g;
 }
 
-__device__ __forceinline__ Tile tile_at(const EpiParams& ep, int64_t t, int BN) {
+__device__ __forceinline__ Tile tile_at(const EpiParams& ep, int64_t t, int BN, int BMT = 128) {
     Tile x;
     const int n = (int)(t % ep.n_tiles);
     t /= ep.n_tiles;
@@ -107,7 +107,7 @@ __device__ __forceinline__ Tile tile_at(const EpiParams& ep, int64_t t, int BN) 
     z /= ep.splits;
     x.cidx = (int)(z % ep.channels);
     x.bidx = (int)(z / ep.channels);
-    x.m0 = m * 128;
+    x.m0 = m * BMT;
     x.n0 = n * BN;
     if (ep.conv == 2) {
         x.cidx = n / ep.cv_cblk;
@@ -298,6 +298,74 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
         : "memory");
 }
 
+// ------------------------- CTA pairs (cta_group::2) -------------------------
+// A pair of CTAs (a 2-CTA cluster) computes one 256-row tile: each CTA
+// stages its 128 rows of A and half of the tile's B columns at the same
+// shared-memory offsets; the even CTA issues 256 x BN MMAs that read both
+// CTAs' stages and write each CTA's 128 accumulator rows into its own TMEM.
+// Both CTAs' copies complete on the even CTA's full barrier; its commits
+// arrive on both CTAs' barriers; both epilogues release the accumulator on
+// the even CTA's barrier.  No load uses cluster multicast.
+
+// shared::cluster address of the same shared-memory offset in CTA 0 of the cluster
+__device__ __forceinline__ uint32_t rank0_addr(const void* p) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// tiled load whose completion is counted on an mbarrier of either CTA of the pair
+__device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_t bar_cluster, void* dst, int c0,
+                                                 int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+        "%5, %6}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accum) {
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}\n" ::"r"(
+            tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(z)
+        : "memory");
+}
+
+// arrives once on the barrier at this offset in both CTAs of the pair when
+// the issuing thread's MMAs retire
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -333,12 +401,17 @@ struct Smem {
 };
 
 // A_MN: A is stored MN-major ([K][M]); B_MN: B is stored MN-major ([K][N]).
-template <bool A_MN, bool B_MN, int BN, int STAGES>
+// PAIR: launched as 2-CTA clusters; a tile is 256 x BN (cta_group::2 MMAs),
+// each CTA staging 128 rows of A and BN/2 columns of B.
+template <bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ GemmGroup grp) {
-    using L = Smem<BN, STAGES>;
+    constexpr int BNC = PAIR ? BN / 2 : BN;  // B columns staged by this CTA
+    constexpr int BMT = PAIR ? 2 * BM : BM;  // tile rows
+    using L = Smem<BNC, STAGES>;
     static_assert(L::EPI_WARP_BYTES >= 32 * kEpiLd * 4, "staging");
-    constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+    static_assert(BNC % 32 == 0, "B staged in 32-column boxes");
+    constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators (this CTA's 128 rows x BN)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
@@ -359,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], kEpiWarps);
+            mbar_init(&tmem_empty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -372,15 +445,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if constexpr (PAIR) {
+            // collective over the same warp of both CTAs
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(tmem_slot)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(tmem_slot)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // the peer's barriers are initialised before any copy or commit reaches them
+    if constexpr (PAIR) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    const int rank = PAIR ? (int)cluster_rank() : 0;
+    const int64_t t_first = PAIR ? blockIdx.x / 2 : blockIdx.x;
+    const int64_t t_step = PAIR ? gridDim.x / 2 : gridDim.x;
     // everything above overlapped the previous kernel; its outputs are read
     // (and C written) only from here on
     pdl_wait();
@@ -395,12 +483,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+            for (int64_t t = t_first; ok && t < total_tiles; t += t_step) {
                 const int g = group_of(grp, t);
                 const EpiParams& ep = grp.ep[g];
                 const CUtensorMap* tmA = &grp.a[g];
                 const CUtensorMap* tmB = &grp.b[g];
-                const Tile x = tile_at(ep, t - grp.tile_start[g], BN);
+                const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
                 const int a_c = ep.a_has_c ? x.cidx : 0, a_b = ep.a_has_b ? x.bidx : 0;
                 const int b_c = ep.b_has_c ? x.cidx : 0, b_b = ep.b_has_b ? x.bidx : 0;
                 for (int i = 0; i < x.nkb; ++i) {
@@ -411,7 +499,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint8_t* sa = smem + s * L::STAGE_BYTES;
                     uint8_t* sb = sa + L::A_BYTES;
                     const int k0 = (x.kb_begin + i) * BK;
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)L::STAGE_BYTES);
+                    // this CTA's rows of A and columns of B
+                    const int mo = x.m0 + rank * BM, no = x.n0 + rank * BNC;
+                    // a pair's copies all complete on CTA 0's barrier, which
+                    // expects both CTAs' bytes
+                    const uint32_t bar = PAIR ? rank0_addr(&full[s]) : 0u;
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(PAIR ? 2 : 1) * L::STAGE_BYTES);
+                    auto load = [&](const CUtensorMap* map, void* dst, int c0, int c1, int c2, int c3) {
+                        if constexpr (PAIR) tma_load_4d_pair(map, bar, dst, c0, c1, c2, c3);
+                        else tma_load_4d(map, &full[s], dst, c0, c1, c2, c3);
+                    };
                     if (!A_MN && B_MN && ep.conv == 1) {
                         // weights [tap][m][c]; the pixels of a tap are the output
                         // pixels moved by whole rows in the flattened image plane
@@ -420,10 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int kh = tap / ep.cv_kw, kw = tap - kh * ep.cv_kw;
                         const int zc = kw * ep.cv_nb + x.bidx;
                         const int dp = (kh - ep.cv_pad) * ep.cv_w;
-                        tma_load_4d(tmA, &full[s], sa, c0, x.m0, tap, 0);
+                        load(tmA, sa, c0, mo, tap, 0);
 #pragma unroll
-                        for (int j = 0; j < BN / 32; ++j)
-                            tma_load_4d(tmB, &full[s], sb + j * 4096, x.n0 + 32 * j + dp, c0, zc, 0);
+                        for (int j = 0; j < BNC / 32; ++j) load(tmB, sb + j * 4096, no + 32 * j + dp, c0, zc, 0);
                     } else if (A_MN && !B_MN && ep.conv == 3) {
                         const int kb = x.kb_begin + i;
                         const int tap = kb / ep.cv_cblk, c0 = (kb - tap * ep.cv_cblk) * BK;
@@ -431,29 +527,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int zc = kw * ep.cv_nb + x.bidx;
                         const int dp = (kh - ep.cv_pad) * ep.cv_w;
 #pragma unroll
-                        for (int j = 0; j < BM / 32; ++j)
-                            tma_load_4d(tmA, &full[s], sa + j * 4096, x.m0 + 32 * j + dp, c0, zc, 0);
-                        tma_load_4d(tmB, &full[s], sb, c0, x.n0, tap, 0);
+                        for (int j = 0; j < BM / 32; ++j) load(tmA, sa + j * 4096, mo + 32 * j + dp, c0, zc, 0);
+                        load(tmB, sb, c0, no, tap, 0);
                     } else if (!A_MN && !B_MN && ep.conv == 2) {
-                        // B rows = channels x.n0.. of tap x.cidx at pixels k0..k0+31
+                        // B rows = channels no.. of tap x.cidx at pixels k0..k0+31
                         const int kh = x.cidx / ep.cv_kw, kw = x.cidx - kh * ep.cv_kw;
-                        tma_load_4d(tmA, &full[s], sa, k0, x.m0, a_c, a_b);
-                        tma_load_4d(tmB, &full[s], sb, k0 + (kh - ep.cv_pad) * ep.cv_w, x.n0, kw * ep.cv_nb + x.bidx,
-                                    0);
+                        load(tmA, sa, k0, mo, a_c, a_b);
+                        load(tmB, sb, k0 + (kh - ep.cv_pad) * ep.cv_w, no, kw * ep.cv_nb + x.bidx, 0);
                     } else {
                         if (A_MN) {
 #pragma unroll
-                            for (int j = 0; j < BM / 32; ++j)
-                                tma_load_4d(tmA, &full[s], sa + j * 4096, x.m0 + 32 * j, k0, a_c, a_b);
+                            for (int j = 0; j < BM / 32; ++j) load(tmA, sa + j * 4096, mo + 32 * j, k0, a_c, a_b);
                         } else {
-                            tma_load_4d(tmA, &full[s], sa, k0, x.m0, a_c, a_b);
+                            load(tmA, sa, k0, mo, a_c, a_b);
                         }
                         if (B_MN) {
 #pragma unroll
-                            for (int j = 0; j < BN / 32; ++j)
-                                tma_load_4d(tmB, &full[s], sb + j * 4096, x.n0 + 32 * j, k0, b_c, b_b);
+                            for (int j = 0; j < BNC / 32; ++j) load(tmB, sb + j * 4096, no + 32 * j, k0, b_c, b_b);
                         } else {
-                            tma_load_4d(tmB, &full[s], sb, k0, x.n0, b_c, b_b);
+                            load(tmB, sb, k0, no, b_c, b_b);
                         }
                     }
                     issued[s] = true;
@@ -464,26 +556,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            if (*abort_flag) {
+            // on abort, let issued copies land before the CTA leaves (in a
+            // pair they complete on CTA 0's barriers, which CTA 0 drains)
+            if (*abort_flag && rank == 0) {
                 for (int u = 0; u < STAGES; ++u)
                     if (issued[u]) drain_wait(&full[u], last_parity[u]);
             }
         }
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
             // ------------------------------- MMA issuer -------------------------------
+            // (in a pair only CTA 0 issues: 256 x BN MMAs over both CTAs' stages)
             // instruction descriptor: D=f32, A=B=tf32, transpose bits, N>>3, M>>4
             const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
                                    ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
-                                   ((uint32_t)(BM >> 4) << 24);
+                                   ((uint32_t)(BMT >> 4) << 24);
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
             int acc = 0;
-            for (int64_t t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++acc) {
+            for (int64_t t = t_first; ok && t < total_tiles; t += t_step, ++acc) {
                 const int g = group_of(grp, t);
-                const Tile x = tile_at(grp.ep[g], t - grp.tile_start[g], BN);
+                const Tile x = tile_at(grp.ep[g], t - grp.tile_start[g], BN, BMT);
                 const int buf = acc & 1;
                 const uint32_t use = (uint32_t)(acc >> 1);
                 if (!wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) break;
@@ -501,19 +596,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < BK / 8; ++kk) {
                         const uint64_t ad = A_MN ? mnmajor_desc(sa, kk) : kmajor_desc(sa, kk);
                         const uint64_t bd = B_MN ? mnmajor_desc(sb, kk) : kmajor_desc(sb, kk);
-                        mma_tf32(tmem_d, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                        if constexpr (PAIR) mma_tf32_pair(tmem_d, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                        else mma_tf32(tmem_d, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
                     }
-                    mma_commit(&empty[s]);
+                    if constexpr (PAIR) mma_commit_pair_both(&empty[s]);
+                    else mma_commit(&empty[s]);
                     if (++s == STAGES) {
                         s = 0;
                         ph ^= 1u;
                     }
                 }
                 if (!ok) break;
-                mma_commit(&tmem_full[buf]);  // arrives once every MMA of this tile retired
+                // arrives once every MMA of this tile retired
+                if constexpr (PAIR) mma_commit_pair_both(&tmem_full[buf]);
+                else mma_commit(&tmem_full[buf]);
             }
             // every MMA issued above retires before TMEM is released
-            mma_commit(drain);
+            if constexpr (PAIR) mma_commit_pair_local(drain);
+            else mma_commit(drain);
             drain_wait(drain, 0);
         }
         __syncwarp();
@@ -524,11 +624,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rsub = lane >> 3, c4 = (lane & 7) * 4;
         int acc = 0;
         uint32_t blocks_out = 0;  // bulk groups this warp committed
-        for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++acc) {
+        for (int64_t t = t_first; t < total_tiles; t += t_step, ++acc) {
             const int g = group_of(grp, t);
             const EpiParams& ep = grp.ep[g];
             const CUtensorMap* tmC = &grp.c[g];
-            const Tile x = tile_at(ep, t - grp.tile_start[g], BN);
+            const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
             const int buf = acc & 1;
             const uint32_t use = (uint32_t)(acc >> 1);
             // the tcgen05.ld below is warp-collective: leave the loop together
@@ -545,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + cc * 32), r);
                 if (!live) continue;
                 if (ep.tma_epi) {
-                    const int row0 = x.m0 + q * 32;
+                    const int row0 = x.m0 + rank * BM + q * 32;
                     if (row0 >= ep.M) continue;  // warp-uniform: this quarter lies below the matrix
                     float* blk = stage + (blocks_out & 1u) * 1024;
                     if (blocks_out >= 2) {
@@ -629,7 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 4
                 for (int it = 0; it < 8; ++it) {
                     const int rr = it * 4 + rsub;
-                    const int row = x.m0 + q * 32 + rr;
+                    const int row = x.m0 + rank * BM + q * 32 + rr;
                     if (row >= ep.M || col >= ep.N) continue;
                     float4 v = *reinterpret_cast<const float4*>(stage + rr * kEpiLd + c4);
                     v.x = ep.alpha * v.x + bv.x;
@@ -667,7 +767,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // this accumulator may be overwritten once every lane's loads retired
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+            if (lane == 0) {
+                if constexpr (PAIR) mbar_arrive_cluster(rank0_addr(&tmem_empty[buf]));
+                else mbar_arrive(&tmem_empty[buf]);
+            }
         }
         // bulk stores must finish reading shared memory (and land) before exit
         if (lane == 0) bulk_wait_all();
@@ -675,10 +778,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    // a pair leaves together: CTA 0's MMAs (drained above) read this CTA's
+    // stages and write its TMEM, and its epilogue arrivals target CTA 0
+    if constexpr (PAIR) cluster_sync_all();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
-                     : "memory");
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                         : "memory");
     }
 }
 
@@ -750,32 +860,63 @@ static bool encode_map(CUtensorMap* map, const float* base, const int64_t* dims,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool A_MN, bool B_MN, int BN, int STAGES>
+template <bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR = false>
 static int launch_tc(const GemmGroup& grp, cudaStream_t st) {
-    using L = Smem<BN, STAGES>;
+    using L = Smem<PAIR ? BN / 2 : BN, STAGES>;
     static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
     static_assert(sizeof(GemmGroup) <= 4000, "kernel parameter space");
-    auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, STAGES>;
+    auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, STAGES, PAIR>;
     static bool configured = false;
     if (!configured) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
             return launch_status();
         configured = true;
     }
-    // persistent: one CTA per SM (the shared-memory ring admits one); the
-    // prologue may overlap the previous kernel (programmatic dependent launch)
+    // persistent: one CTA (or CTA pair) per SM (pair); the shared-memory
+    // ring admits one per SM; the prologue may overlap the previous kernel
+    // (programmatic dependent launch)
     const int64_t tiles = grp.tile_start[grp.n];
-    const int grid = (int)(tiles < kSMs ? tiles : kSMs);
+    int64_t units = kSMs;
+    if constexpr (PAIR) {
+        // as many pairs as can be resident at once (clusters need both SMs of
+        // a pair free in one GPC)
+        static int max_pairs = 0;
+        if (max_pairs == 0) {
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3(kSMs);
+            q.blockDim = dim3(kThreads);
+            q.dynamicSmemBytes = L::TOTAL;
+            cudaLaunchAttribute qa[1];
+            qa[0].id = cudaLaunchAttributeClusterDimension;
+            qa[0].val.clusterDim.x = 2;
+            qa[0].val.clusterDim.y = 1;
+            qa[0].val.clusterDim.z = 1;
+            q.attrs = qa;
+            q.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n <= 0) {
+                cudaGetLastError();
+                n = kSMs / 2;
+            }
+            max_pairs = n < kSMs / 2 ? n : kSMs / 2;
+        }
+        units = max_pairs;
+    }
+    const int grid = (int)(tiles < units ? tiles : units) * (PAIR ? 2 : 1);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = L::TOTAL;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = PAIR ? 2 : 1;
     if (cudaLaunchKernelEx(&cfg, kern, grp) != cudaSuccess) return launch_status();
     return launch_status();
 }
@@ -794,6 +935,10 @@ static bool tc_eligible(const GemmProblem& p) {
 }
 
 static thread_local int g_gemm_mode = MLE_GEMM_MODE_TF32;
+// whether large plain products may run on CTA pairs (256-row tiles)
+static thread_local int g_gemm_pairs = 1;
+// tile width, split count and pair flag of this thread's last tensor-core launch
+static thread_local int g_last_choice[3] = {0, 0, 0};
 
 namespace {
 
@@ -825,20 +970,31 @@ bool may_split(const GemmProblem& p) {
 // spread over the SMs in use, and splitting K adds one reduce-add of C per
 // split.  Its choices match the best measured (BN, splits) within ~5 % for
 // the transformer's backward GEMMs.
-void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model_assign = false) {
+void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model_assign = false,
+                  bool* pair = nullptr) {
     using namespace tc;
     BN = 64;
     splits = 1;
+    if (pair) *pair = false;
     // Assigned outputs never split (the memset and reduce-adds cost more
     // than they save, measured on B200); narrow tiles keep enough of them
     // in flight for these small-K products.  `model_assign`: pick the width
-    // of an assigned (long-K) product with the fill model instead.
+    // of an assigned (long-K) product with the fill model instead, as for
+    // products of at least two waves of 128 x 128 tiles when CTA pairs are
+    // allowed (`pair` non-null).
     bool any_assign = false;
     int max_n = 0;
+    int64_t tiles128 = 0;
     for (int i = 0; i < n; ++i) {
         any_assign = any_assign || ps[i].mode == EPI_ASSIGN;
         max_n = std::max(max_n, ps[i].N);
+        const Shape sh = shape_of(ps[i]);
+        tiles128 += (int64_t)sh.m_tiles * ((ps[i].N + 127) / 128) * sh.z;
     }
+    // pairs only pay once there are at least a wave of 128 x 128 tiles (a
+    // 1024^3 product ran slower on them, 2048^3 and up faster, on B200)
+    if (tiles128 < kSMs) pair = nullptr;
+    if (pair && tiles128 >= 2 * kSMs) model_assign = true;
     if (any_assign && !model_assign) {
         BN = max_n <= 256 ? 64 : 128;
         return;
@@ -851,31 +1007,46 @@ void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model
         kb_min = std::min(kb_min, shape_of(ps[i]).kb_total);
         split_ok = split_ok && may_split(ps[i]);
     }
-    for (int cand : {256, 128, 64}) {
+    // Model: operand tiles reach shared memory at ~90 GB/s per SM and the
+    // tensor pipe retires ~5.5 TFLOP/s per SM (TF32); a CTA pair stages
+    // half of its 256 x BN tile's B per SM, so it fills less per FLOP.
+    struct Cand {
+        int bn;
+        bool pr;
+    };
+    const Cand cands[] = {{256, false}, {128, false}, {64, false}, {256, true}};
+    for (const Cand& c : cands) {
+        if (c.pr && !pair) continue;
+        const int cand = c.bn, bmt = c.pr ? 2 * BM : BM, per_unit = c.pr ? 2 : 1;
         if (cand > 64 && min_n < cand / 2 + 1) continue;
         int64_t units = 0;
-        double fill = 0, cbytes = 0, assign_bytes = 0;
+        double fill = 0, flops = 0, cbytes = 0, assign_bytes = 0;
         for (int i = 0; i < n; ++i) {
             const GemmProblem& p = ps[i];
             const Shape sh = shape_of(p);
-            const int64_t u = (int64_t)sh.m_tiles * ((p.N + cand - 1) / cand) * sh.z;
+            const int64_t mt = (p.M + bmt - 1) / bmt;
+            const int64_t u = mt * ((p.N + cand - 1) / cand) * sh.z;
             units += u;
-            fill += (double)u * (BM + cand) * (double)sh.kb_total * BK * 4.0;
+            fill += (double)u * (bmt + cand) * (double)sh.kb_total * BK * 4.0;
+            flops += 2.0 * (double)u * bmt * cand * (double)sh.kb_total * BK;
             cbytes += (double)p.M * p.N * sh.z * 4.0;
             if (p.mode == EPI_ASSIGN) assign_bytes += (double)p.M * p.N * sh.z * 4.0;
         }
         const int max_split = (split_ok && !any_assign) ? std::max(1, kb_min / 4) : 1;
+        const int64_t slots = kSMs / per_unit;
         for (int sp = 1; sp <= max_split; sp = (sp < 4 ? sp + 1 : sp * 2)) {
             const int64_t work = units * sp;
-            const double active = (double)std::min<int64_t>(work, kSMs);
-            double t = fill / (active * 90e9) + 0.3e-6 * (double)((work + kSMs - 1) / kSMs);
+            const double active = (double)std::min<int64_t>(work * per_unit, kSMs);
+            double t = std::max(fill / (active * 90e9), flops / (active * 5.5e12)) +
+                       0.3e-6 * (double)((work + slots - 1) / slots);
             if (sp > 1) t += (double)sp * cbytes / 3e12 + assign_bytes / 5e12;
             if (t < best * 0.98) {
                 best = t;
                 BN = cand;
                 splits = sp;
+                if (pair) *pair = c.pr;
             }
-            if (work >= kSMs) break;
+            if (work >= slots) break;
         }
     }
 }
@@ -884,12 +1055,14 @@ void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model
 // parameters); an assigned C that is split is zeroed first.  False if TMA
 // cannot describe an operand.
 int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc::GemmGroup& grp, int g,
-            cudaStream_t st, bool& ok) {
+            cudaStream_t st, bool& ok, bool pair = false) {
     using namespace tc;
     ok = false;
     const Shape sh = shape_of(p);
     const int n_tiles = (p.N + BN - 1) / BN;
-    const int64_t tiles = (int64_t)sh.m_tiles * n_tiles * sh.z;
+    const int m_tiles = pair ? (p.M + 2 * BM - 1) / (2 * BM) : sh.m_tiles;  // a pair's tile has 256 rows
+    const int bn_cta = pair ? BN / 2 : BN;                                   // B columns a CTA stages
+    const int64_t tiles = (int64_t)m_tiles * n_tiles * sh.z;
     const int kb_per_split = (sh.kb_total + splits_req - 1) / splits_req;
     const int splits = (sh.kb_total + kb_per_split - 1) / kb_per_split;
     EpiParams& ep = grp.ep[g];
@@ -909,7 +1082,7 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
     ep.a_has_c = (p.a_sc != 0 && p.channels > 1);
     ep.b_has_b = (p.b_sb != 0 && p.nbatch > 1);
     ep.b_has_c = (p.b_sc != 0 && p.channels > 1);
-    ep.m_tiles = sh.m_tiles;
+    ep.m_tiles = m_tiles;
     ep.n_tiles = n_tiles;
     ep.tiles = tiles * splits;
     ep.alpha = p.alpha;
@@ -938,7 +1111,7 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
     memset(&grp.b[g], 0, sizeof(CUtensorMap));
     memset(&grp.c[g], 0, sizeof(CUtensorMap));
     if (!encode_operand(&grp.a[g], va, 32, sh.A_MN ? BK : BM, sh.A_MN)) return MLE_OK;
-    if (!encode_operand(&grp.b[g], vb, 32, sh.B_MN ? BK : BN, sh.B_MN)) return MLE_OK;
+    if (!encode_operand(&grp.b[g], vb, 32, sh.B_MN ? BK : bn_cta, sh.B_MN)) return MLE_OK;
     // C through bulk tensor stores when its rows and strides allow TMA
     ep.c_has_b = (ep.c_stride_b != 0);
     ep.c_has_c = (ep.c_stride_c != 0);
@@ -981,9 +1154,15 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
     return MLE_OK;
 }
 
-int dispatch(const tc::GemmGroup& grp, bool A_MN, bool B_MN, int BN, cudaStream_t st) {
+int dispatch(const tc::GemmGroup& grp, bool A_MN, bool B_MN, int BN, cudaStream_t st, bool pair = false) {
     using namespace tc;
 #define MLE_TC(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST>(grp, st)
+#define MLE_TC2(AM, BMN) return launch_tc<AM, BMN, 256, 6, true>(grp, st)
+    if (pair) {  // 256 x 256 tiles on CTA pairs
+        if (A_MN) { if (B_MN) MLE_TC2(true, true); else MLE_TC2(true, false); }
+        else { if (B_MN) MLE_TC2(false, true); else MLE_TC2(false, false); }
+    }
+#undef MLE_TC2
     if (BN == 256) {
         if (A_MN) { if (B_MN) MLE_TC(true, true, 256, 4); else MLE_TC(true, false, 256, 4); }
         else { if (B_MN) MLE_TC(false, true, 256, 4); else MLE_TC(false, false, 256, 4); }
@@ -1009,18 +1188,22 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     }
     if (!tc_path(p)) return p.c_split ? MLE_ERR_UNSUPPORTED : simt_gemm(p, st);
     int BN, splits;
-    choose_tiles(&p, 1, BN, splits);
+    bool pair = false;
+    choose_tiles(&p, 1, BN, splits, false, g_gemm_pairs ? &pair : nullptr);
     tc::GemmGroup grp;
     memset(&grp, 0, sizeof(grp));
     bool ok = false;
-    const int s = prepare(p, BN, splits, false, grp, 0, st, ok);
+    const int s = prepare(p, BN, splits, false, grp, 0, st, ok, pair);
     if (s) return s;
     if (!ok) return p.c_split ? MLE_ERR_UNSUPPORTED : simt_gemm(p, st);
     grp.n = 1;
     grp.tile_start[0] = 0;
     grp.tile_start[1] = grp.ep[0].tiles;
     const Shape sh = shape_of(p);
-    return dispatch(grp, sh.A_MN, sh.B_MN, BN, st);
+    g_last_choice[0] = BN;
+    g_last_choice[1] = grp.ep[0].splits;
+    g_last_choice[2] = pair ? 1 : 0;
+    return dispatch(grp, sh.A_MN, sh.B_MN, BN, st, pair);
 }
 
 // Problems of one layout class in one persistent launch.  `shared_c`: all
@@ -1042,14 +1225,15 @@ int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st)
         return MLE_OK;
     }
     int BN, splits;
-    choose_tiles(ps, n, BN, splits);
+    bool pair = false;
+    choose_tiles(ps, n, BN, splits, false, g_gemm_pairs ? &pair : nullptr);
     tc::GemmGroup grp;
     memset(&grp, 0, sizeof(grp));
     grp.n = n;
     grp.tile_start[0] = 0;
     for (int i = 0; i < n; ++i) {
         bool ok = false;
-        const int s = prepare(ps[i], BN, splits, shared_c, grp, i, st, ok);
+        const int s = prepare(ps[i], BN, splits, shared_c, grp, i, st, ok, pair);
         if (s) return s;
         if (!ok) {  // an operand TMA cannot describe: separate launches
             for (int j = 0; j < n; ++j) {
@@ -1060,7 +1244,7 @@ int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st)
         }
         grp.tile_start[i + 1] = grp.tile_start[i] + grp.ep[i].tiles;
     }
-    return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st);
+    return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st, pair);
 }
 
 bool conv_gemm_supported(const ConvGemm& c) {
@@ -1279,6 +1463,20 @@ int mle_set_gemm_mode(int mode) {
 }
 
 int mle_get_gemm_mode(void) { return g_gemm_mode; }
+
+int mle_set_gemm_pairs(int enable) {
+    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    g_gemm_pairs = enable;
+    return MLE_OK;
+}
+
+int mle_get_gemm_pairs(void) { return g_gemm_pairs; }
+
+int mle_gemm_last_choice(int* out3) {
+    if (!out3) return MLE_ERR_ARG;
+    for (int i = 0; i < 3; ++i) out3[i] = g_last_choice[i];
+    return MLE_OK;
+}
 
 int mle_watchdog_read(int* out_flag, mle_stream_t stream) {
     if (!out_flag) return MLE_ERR_ARG;

@@ -4,6 +4,8 @@ oracle on seeded inputs, including ragged, unaligned and edge sizes.
 Tolerances (see conftest): 1e-5 for elementwise / reduction / Adam paths,
 2e-3 per tensor for the TF32 tensor-core GEMMs.
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -295,6 +297,36 @@ def test_gemm_tf32(cuda, ops, orc, rng, M, N, K, ta, tb, beta):
     assert err <= RTOL_TC, err
 
 
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+def test_gemm_cta_pairs(cuda, ops, rng, ta, tb, beta):
+    """Products large enough for 256 x 256 tiles on CTA pairs (cta_group::2
+    MMAs), with ragged edges in M, N and K, against float64 products."""
+    from ml_engine_b200._lib import kernels
+    M, N, K = 4000, 2000, 520
+    A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    C = T(C0, cuda)
+    k = kernels()
+    old = k.mle_get_gemm_pairs()
+    k.mle_set_gemm_pairs(1)
+    try:
+        ops.gemm(T(A, cuda), T(B, cuda), C, M, N, K, ta, tb, alpha=0.5, beta=beta)
+        got = H(C)
+        choice = (ctypes.c_int * 3)()
+        k.call("mle_gemm_last_choice", choice)
+    finally:
+        k.mle_set_gemm_pairs(old)
+    assert choice[2] == 1, list(choice)  # the product ran on CTA pairs
+    a64 = (A.T if ta else A).astype(np.float64)
+    b64 = (B.T if tb else B).astype(np.float64)
+    prod = a64 @ b64
+    ref = (C0.astype(np.float64) if beta else 0.0) + 0.5 * prod
+    err = np.max(np.abs(got - ref)) / np.max(np.abs(0.5 * prod))
+    assert err <= RTOL_TC, err
+
+
 def test_gemm_fallback_exact(cuda, ops, orc, rng):
     """N = 10 (MNIST logits) has a 40-byte row stride: CUDA-core path, fp32."""
     M, N, K = 64, 10, 256
@@ -575,13 +607,23 @@ def test_watchdog_clear(cuda, ops):
     assert ops.watchdog() == 0
 
 
-@pytest.mark.parametrize("n", [1, 2, 3])
-def test_linear_group_matches_separate_linears(cuda, ops, rng, n):
+@pytest.mark.parametrize("n,rows,pairs", [(1, 1024, 0), (2, 1024, 0), (3, 1024, 0), (3, 8192, 1)])
+def test_linear_group_matches_separate_linears(cuda, ops, rng, n, rows, pairs):
     """mle_linear_group_fwd/_bwd against n separate mle_linear_fwd/_bwd
-    calls (TF32 products; dX sums the n products with reduce-adds)."""
-    import ctypes
+    calls (TF32 products; dX sums the n products with reduce-adds); the
+    8192-row case is large enough for the group to run on CTA pairs."""
     from ml_engine_b200._lib import kernels
-    rows, din = 1024, 256
+    old_pairs = kernels().mle_get_gemm_pairs()
+    kernels().mle_set_gemm_pairs(pairs)
+    try:
+        _linear_group_case(cuda, ops, rng, n, rows)
+    finally:
+        kernels().mle_set_gemm_pairs(old_pairs)
+
+
+def _linear_group_case(cuda, ops, rng, n, rows):
+    from ml_engine_b200._lib import kernels
+    din = 256
     outs = [256, 128, 512][:n]
     X = T(rng.standard_normal((rows, din)).astype(np.float32), cuda)
     Ws = [T((rng.standard_normal((din, o)) * 0.05).astype(np.float32), cuda) for o in outs]
