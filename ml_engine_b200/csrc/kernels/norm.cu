@@ -4,7 +4,7 @@
 // LayerNorm one segment of C*H*W per dim0 index (Engine/kernels.cu:541-572),
 // GroupNorm one segment of (C/G)*H*W per (sample, group)
 // (Engine/kernels.cu:607-639).  One kernel pair therefore serves both: a
-// warp owns a segment when it fits in its registers (N <= 2048, N % 4 == 0),
+// warp owns a segment when it fits in its registers (N <= 1024, N % 4 == 0),
 // a cluster of up to 8 CTAs when it fits in theirs (N <= 65536), otherwise
 // a 256-thread block streams it.  gamma = 1 and beta = 0 are the
 // reference's fixed constants.
@@ -22,6 +22,9 @@ namespace mle {
 namespace {
 
 constexpr int kBlock = 256;
+// longest segment a warp holds (8 float4 per lane); longer ones go to a CTA
+// or a cluster (a 2048-float row ran at 59 % of HBM on one warp)
+constexpr int kWarpMaxN = 1024;
 
 // ----------------------------- warp per segment ---------------------------
 template <int V>  // V float4 per lane -> N <= 128 * V
@@ -332,14 +335,13 @@ __global__ void ln_bwd_channels_block(const float* __restrict__ y, const float* 
 static int seg_norm_fwd(const float* x, float* y, float* mean, float* sqdev, int64_t segs, int N, float eps,
                         cudaStream_t st) {
     if (segs == 0) return MLE_OK;
-    if (N % 4 == 0 && N <= 2048 && aligned16(x) && aligned16(y)) {
+    if (N % 4 == 0 && N <= kWarpMaxN && aligned16(x) && aligned16(y)) {
         const int wpb = 8;  // warps per block
         const unsigned grid = (unsigned)((segs + wpb - 1) / wpb);
         if (N <= 128) launch_k(seg_norm_fwd_warp<1>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
         else if (N <= 256) launch_k(seg_norm_fwd_warp<2>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
         else if (N <= 512) launch_k(seg_norm_fwd_warp<4>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
-        else if (N <= 1024) launch_k(seg_norm_fwd_warp<8>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
-        else launch_k(seg_norm_fwd_warp<16>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
+        else launch_k(seg_norm_fwd_warp<8>, grid, 32 * wpb, 0, st, x, y, mean, sqdev, segs, N, eps);
     } else if (int CL, V; N % 4 == 0 && aligned16(x) && aligned16(y) && cluster_shape(N, CL, V)) {
         const int slice = V * kBlock * 4;
         const dim3 grid((unsigned)(segs * CL));
@@ -356,14 +358,13 @@ static int seg_norm_fwd(const float* x, float* y, float* mean, float* sqdev, int
 static int seg_norm_bwd(const float* y, const float* gy, const float* sqdev, float* gx, int64_t segs, int N, float eps,
                         cudaStream_t st) {
     if (segs == 0) return MLE_OK;
-    if (N % 4 == 0 && N <= 2048 && aligned16(y) && aligned16(gy) && aligned16(gx)) {
+    if (N % 4 == 0 && N <= kWarpMaxN && aligned16(y) && aligned16(gy) && aligned16(gx)) {
         const int wpb = 8;
         const unsigned grid = (unsigned)((segs + wpb - 1) / wpb);
         if (N <= 128) launch_k(seg_norm_bwd_warp<1>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
         else if (N <= 256) launch_k(seg_norm_bwd_warp<2>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
         else if (N <= 512) launch_k(seg_norm_bwd_warp<4>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
-        else if (N <= 1024) launch_k(seg_norm_bwd_warp<8>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
-        else launch_k(seg_norm_bwd_warp<16>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
+        else launch_k(seg_norm_bwd_warp<8>, grid, 32 * wpb, 0, st, y, gy, sqdev, gx, segs, N, eps);
     } else if (int CL, V; N % 4 == 0 && aligned16(y) && aligned16(gy) && aligned16(gx) && cluster_shape(N, CL, V)) {
         const int slice = V * kBlock * 4;
         const dim3 grid((unsigned)(segs * CL));

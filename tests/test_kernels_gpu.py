@@ -185,11 +185,12 @@ def test_matpe(cuda, ops, orc, rng):
 
 
 # -------------------------------------------------------------- normalisation
-# segment lengths for every path: warp (<= 2048), one CTA (4096), clusters of
+# segment lengths for every path: warp (<= 1024), one CTA (2048, 4096), clusters of
 # 2 and 8 CTAs (8192, 60000 with a partial last CTA), streamed block (70000
 # and the unaligned 4099)
 @pytest.mark.parametrize("batch,channels,row,col", [(64, 1, 1, 256), (33, 1, 1, 1000), (7, 1, 4, 1024),
-                                                    (5, 1, 1, 8192), (3, 1, 1, 60000), (2, 1, 1, 70000),
+                                                    (6, 1, 1, 2048), (5, 1, 1, 8192), (3, 1, 1, 60000),
+                                                    (2, 1, 1, 70000),
                                                     (3, 1, 1, 4099), (4, 3, 5, 8)])
 def test_layernorm(cuda, ops, orc, rng, batch, channels, row, col):
     n = batch * channels * row * col
