@@ -201,7 +201,8 @@ def run_reference(args, rank, world):
 def roofline_pair(dev, stream, reps=50):
     """The projection layer's backward GEMMs (dX = dY W^T, dW = X^T dY),
     2 * 2 * 4096 * 256 * 4096 FLOP per pair, on `stream`: 3 untimed pairs,
-    then `reps` pairs between CUDA events.  Returns (ms per pair, FLOP)."""
+    then `reps` pairs, each between its own CUDA events after a 256 MB write
+    that evicts the operands from L2.  Returns (ms per pair, FLOP)."""
     import torch
 
     from ml_engine_b200 import ops
@@ -211,17 +212,19 @@ def roofline_pair(dev, stream, reps=50):
     W = torch.randn(K, N, device=dev, generator=g) * 0.02
     dY = torch.randn(M, N, device=dev, generator=g) * 1e-3
     dX, dW = torch.zeros(M, K, device=dev), torch.zeros(K, N, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > 126 MB L2
     with torch.cuda.stream(stream):
         for _ in range(3):
             ops.linear_bwd(X, W, dY, dX, dW, None, M, K, N)
         torch.cuda.synchronize()
-        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        k0.record(stream)
-        for _ in range(reps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for k0, k1 in evs:
+            flush.fill_(1.0)
+            k0.record(stream)
             ops.linear_bwd(X, W, dY, dX, dW, None, M, K, N)
-        k1.record(stream)
+            k1.record(stream)
         torch.cuda.synchronize()
-    return k0.elapsed_time(k1) / reps, 2 * 2.0 * M * K * N
+    return sum(k0.elapsed_time(k1) for k0, k1 in evs) / reps, 2 * 2.0 * M * K * N
 
 
 # ------------------------------------------------------------ kernel sweep
@@ -562,10 +565,10 @@ def main():
     ap.add_argument("--config", default="encoder", choices=["encoder", "unet", "encdec"],
                     help="encoder: configs[1], the benchmark line; unet: configs[3] on one GPU; "
                          "encdec: configs[2], global batch 256 over the ranks")
-    ap.add_argument("--gemm-pairs", type=int, default=None, choices=[0, 1],
+    ap.add_argument("--gemm-pairs", type=int, default=None, choices=[0, 1, 2],
                     help="run large products on CTA pairs (mle_set_gemm_pairs); default: the library's")
     ap.add_argument("--roofline-only", action="store_true",
-                    help="run only the roofline kernel pair (3 + 2 pairs; for a profiler capture)")
+                    help="run only the roofline kernel pair (3 untimed + 20 timed pairs)")
     args = ap.parse_args()
     if args.gemm_pairs is not None:
         from ml_engine_b200._lib import kernels
@@ -579,7 +582,7 @@ def main():
     if args.roofline_only:
         import torch
         dev = torch.device("cuda", 0)
-        ms, flops = roofline_pair(dev, torch.cuda.current_stream(dev), reps=2)
+        ms, flops = roofline_pair(dev, torch.cuda.current_stream(dev), reps=20)
         print(json.dumps({"roofline_pair_ms": ms, "flop": flops}))
         return
     world, rank, local_rank = init_ranks()

@@ -274,8 +274,10 @@ int mle_get_gemm_mode(void);
 /* Whether the tensor-core GEMM may compute large products (at least two
  * waves of 128 x 128 tiles) on CTA pairs: 2-CTA clusters whose 256 x 256
  * tiles issue cta_group::2 MMAs, each SM staging half of the tile's B, so
- * a pair fills shared memory with a third fewer bytes per FLOP.  Per host
- * thread; no counterpart in the reference. */
+ * a pair fills shared memory with a third fewer bytes per FLOP.  0 off,
+ * 1 (default) where the tile model prefers them, 2 wherever the shapes
+ * allow (a measurement aid).  Per host thread; no counterpart in the
+ * reference. */
 int mle_set_gemm_pairs(int enable);
 int mle_get_gemm_pairs(void);
 /* out3 = {tile width, split-K count, 1 if CTA pairs} of this thread's last

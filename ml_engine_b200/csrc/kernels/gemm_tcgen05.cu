@@ -971,7 +971,7 @@ bool may_split(const GemmProblem& p) {
 // split.  Its choices match the best measured (BN, splits) within ~5 % for
 // the transformer's backward GEMMs.
 void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model_assign = false,
-                  bool* pair = nullptr) {
+                  bool* pair = nullptr, bool only_pairs = false) {
     using namespace tc;
     BN = 64;
     splits = 1;
@@ -985,16 +985,19 @@ void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model
     bool any_assign = false;
     int max_n = 0;
     int64_t tiles128 = 0;
+    double flops = 0;
     for (int i = 0; i < n; ++i) {
         any_assign = any_assign || ps[i].mode == EPI_ASSIGN;
         max_n = std::max(max_n, ps[i].N);
         const Shape sh = shape_of(ps[i]);
         tiles128 += (int64_t)sh.m_tiles * ((ps[i].N + 127) / 128) * sh.z;
+        flops += 2.0 * ps[i].M * (double)ps[i].N * ps[i].K * sh.z;
     }
-    // pairs only pay once there are at least a wave of 128 x 128 tiles (a
-    // 1024^3 product ran slower on them, 2048^3 and up faster, on B200)
-    if (tiles128 < kSMs) pair = nullptr;
-    if (pair && tiles128 >= 2 * kSMs) model_assign = true;
+    // pairs only pay with at least a wave of 128 x 128 tiles or a long
+    // split-K product (measured on B200: 1024^3 ran slower on pairs, 2048^3
+    // and up, and 4096 x 4096 x 256 split over K, faster)
+    if (tiles128 < kSMs && flops < 4e9 && !only_pairs) pair = nullptr;
+    if (pair && (tiles128 >= 2 * kSMs || only_pairs)) model_assign = true;
     if (any_assign && !model_assign) {
         BN = max_n <= 256 ? 64 : 128;
         return;
@@ -1017,6 +1020,7 @@ void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model
     const Cand cands[] = {{256, false}, {128, false}, {64, false}, {256, true}};
     for (const Cand& c : cands) {
         if (c.pr && !pair) continue;
+        if (only_pairs && pair && !c.pr) continue;
         const int cand = c.bn, bmt = c.pr ? 2 * BM : BM, per_unit = c.pr ? 2 : 1;
         if (cand > 64 && min_n < cand / 2 + 1) continue;
         int64_t units = 0;
@@ -1189,7 +1193,7 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     if (!tc_path(p)) return p.c_split ? MLE_ERR_UNSUPPORTED : simt_gemm(p, st);
     int BN, splits;
     bool pair = false;
-    choose_tiles(&p, 1, BN, splits, false, g_gemm_pairs ? &pair : nullptr);
+    choose_tiles(&p, 1, BN, splits, false, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
     tc::GemmGroup grp;
     memset(&grp, 0, sizeof(grp));
     bool ok = false;
@@ -1226,7 +1230,7 @@ int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st)
     }
     int BN, splits;
     bool pair = false;
-    choose_tiles(ps, n, BN, splits, false, g_gemm_pairs ? &pair : nullptr);
+    choose_tiles(ps, n, BN, splits, false, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
     tc::GemmGroup grp;
     memset(&grp, 0, sizeof(grp));
     grp.n = n;
@@ -1465,7 +1469,7 @@ int mle_set_gemm_mode(int mode) {
 int mle_get_gemm_mode(void) { return g_gemm_mode; }
 
 int mle_set_gemm_pairs(int enable) {
-    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    if (enable < 0 || enable > 2) return MLE_ERR_ARG;
     g_gemm_pairs = enable;
     return MLE_OK;
 }
