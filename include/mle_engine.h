@@ -55,6 +55,11 @@ typedef struct mle_session_desc {
      * features for the timestep `timestep` (fixed when the graph is built,
      * as the reference's PositionalEncoding node captures it) */
     int channels, image_size, base_width, t_embed, timestep;
+    /* classifier targets: 0 = class indices fed straight to the index-label
+     * softmax cross-entropy; 1 = the reference's dense one-hot tensor built
+     * each step by OneHotEmbeddings.  Same loss and gradients, bit for bit;
+     * the input is the int32 class ids either way. */
+    int dense_targets;
 } mle_session_desc;
 
 /* Builds the graph and allocates everything the step needs. */
@@ -105,6 +110,16 @@ int mle_session_param_read(mle_session_t s, int i, int which, float* host);
 int mle_session_param_write(mle_session_t s, int i, int which, const float* host);
 /* Step counter t of parameter i, read from its device mirror. */
 int mle_session_param_step(mle_session_t s, int i, int* t);
+
+/* Checkpoint of every parameter (weights, Adam m and v) in build order as
+ * the reference's AdamParameter::save records (Engine/engine.cu:139-188),
+ * plus `<path>.t` with the Adam step of each parameter, which the reference
+ * does not save.  Under data parallelism only rank 0 writes.  Load checks
+ * every record's name and size first (MLE_ERR_ARG and nothing changed on a
+ * mismatch), then reads the records (Engine/engine.cu:190-268) and, when
+ * the sidecar is present, the steps. */
+int mle_session_save(mle_session_t s, const char* path);
+int mle_session_load(mle_session_t s, const char* path);
 
 /* Embedding tables (transformer configs; gather only, not trained). */
 int mle_session_embedding_count(mle_session_t s);

@@ -249,6 +249,20 @@ int mle_softmax_ce_fwd(const float* logits, const float* target, float* probs, f
 int mle_softmax_ce_bwd(const float* probs, const float* target, const float* upstream,
                        float* grad, float batch_div, int64_t n, mle_stream_t stream);
 
+/* The same two entry points with the target as one int32 class index per
+ * row instead of the dense one-hot tensor the reference builds with
+ * OneHotEmbeddings (no counterpart in the reference; SURVEY's index-label
+ * variant).  Loss, probs and grad equal the dense entry points' on the
+ * one-hot target of `labels`, bit for bit; a label outside [0, cols) is a
+ * row of zeros.  The forward needs cols % 4 == 0, cols <= 8192 and 16-byte
+ * aligned logits/probs/grad (else MLE_ERR_UNSUPPORTED). */
+int mle_softmax_ce_index_fwd(const float* logits, const int32_t* labels, float* probs, float* loss,
+                             float* grad, float batch_div, int64_t rows, int cols,
+                             mle_stream_t stream);
+int mle_softmax_ce_index_bwd(const float* probs, const int32_t* labels, const float* upstream,
+                             float* grad, float batch_div, int64_t rows, int cols,
+                             mle_stream_t stream);
+
 /* Mean squared error: *loss = sum (t-x)^2 / n (assigned);
  * backward gx += 2 (x-t)/n [* upstream[0]].  Replaces scalar_mse_kernel and
  * deriv_mse_kernel (Engine/kernels.cu:1808-1848). */

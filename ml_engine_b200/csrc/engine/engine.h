@@ -199,6 +199,10 @@ class GraphOperations {
 
     static graph MeanSquaredError(const graph& prediction, const graph& target, const bool last);
     static graph SoftMaxCrossEntropy(const graph& prediction, const graph& target, const bool last);
+    // Extension: the target as one int32 class index per row of `prediction`
+    // (device memory, rows = dim0*dim1*dim2), same loss and gradient as the
+    // dense one-hot target without building it.
+    static graph SoftMaxCrossEntropyIndex(const graph& prediction, const int32_t* labels, const bool last);
 
     static graph BMM(const graph& A, const graph& B);     // m x n, n x p = m x p
     static graph BMMABT(const graph& A, const graph& B);  // m x n, p x n = m x p

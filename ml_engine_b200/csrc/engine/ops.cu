@@ -338,6 +338,44 @@ graph GraphOperations::SoftMaxCrossEntropy(const graph& prediction, const graph&
     return node;
 }
 
+// SoftMaxCrossEntropy with index labels (extension): the same lambdas with
+// the one-hot target replaced by its class indices.
+graph GraphOperations::SoftMaxCrossEntropyIndex(const graph& prediction, const int32_t* labels, const bool last) {
+    const int batch = prediction->dim[0], channels = prediction->dim[1], c = prediction->dim[2],
+              d = prediction->dim[3];
+    auto node = std::make_shared<NodeBackProp>("SoftMaxCrossEntropy Loss", 1, 1, 1, 1, 1);
+    node->inputs = {prediction};
+    float* probs = arena_alloc(ARENA_ACT, prediction->total, "SoftMax");
+    GB += sizeof(float) / (double)(1ULL << 30);
+    NodeBackProp *nd = node.get(), *pp = prediction.get();
+    ext(nd).kind = OP_SMCE;
+    const long long rows = (long long)batch * channels * c;
+    auto grad_written = std::make_shared<bool>(false);
+    node->forward = [=]() {
+        *grad_written = false;
+        if (calculate_loss || !last) {
+            float* gout = last ? pp->grad : nullptr;
+            check(mle_softmax_ce_index_fwd(pp->output, labels, (g_keep_softmax || !last) ? probs : nullptr,
+                                           nd->output, gout, (float)batch, rows, d, st()),
+                  "SoftMaxCrossEntropy (index labels)");
+            *grad_written = (gout != nullptr);
+            if (last && g_loss_readback) {
+                check_cuda(cudaStreamSynchronize(stream()), "SMCE loss");
+                check_cuda(cudaMemcpy(&loss, nd->output, sizeof(float), cudaMemcpyDeviceToHost), "SMCE loss");
+            }
+        }
+    };
+    node->backward = [=]() {
+        if (*grad_written) return;
+        check(mle_softmax_ce_index_bwd(probs, labels, last ? nullptr : nd->grad, pp->grad, (float)batch, rows, d,
+                                       st()),
+              "derivative of CE in CE backward (index labels)");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->output, 1); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
 // --------------------------------------------- BMM family (:2196-2428)
 static int bcase(const graph& X) { return (X->dim[0] > 1) + 2 * (X->dim[1] > 1); }
 

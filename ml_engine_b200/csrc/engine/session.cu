@@ -19,6 +19,7 @@
 #include <string.h>
 
 #include <cstring>
+#include <fstream>
 #include <memory>
 #include <random>
 #include <string>
@@ -240,22 +241,32 @@ graph onehot_target(Session& S, const std::string& name, int rows_b, int rows_s,
     return node;
 }
 
+// Loss over a classifier's logits and the int32 class ids of input `name`
+// (rows_b x rows_s of them): the index-label softmax cross-entropy, or the
+// reference's dense one-hot target when the session asks for it.
+graph class_loss(Session& S, const graph& logits, const std::string& name, int rows_b, int rows_s, int classes) {
+    // (the index kernel takes rows of a multiple of 4 classes, up to 8192)
+    if (S.d.dense_targets || classes % 4 != 0 || classes > 8192)
+        return GraphOperations::SoftMaxCrossEntropy(logits, onehot_target(S, name, rows_b, rows_s, classes), true);
+    int32_t* keys = (int32_t*)arena_alloc_bytes(ARENA_WS, (int64_t)rows_b * rows_s * 4, name + " keys");
+    add_input(S, name, 1, (int64_t)rows_b * rows_s, keys);
+    return GraphOperations::SoftMaxCrossEntropyIndex(logits, keys, true);
+}
+
 void build(Session& S) {
     const mle_session_desc& d = S.d;
     if (d.config == MLE_CFG_MLP) {
         auto x = std::make_shared<NodeBackProp>("MNIST input", d.batch, 1, 1, d.in_features, 1);
         add_input(S, "x", 0, (int64_t)d.batch * d.in_features, x->output);
-        graph target = onehot_target(S, "labels", d.batch, 1, d.classes);
         Linear* l1 = new_linear(S, d.in_features, d.hidden, "Linear1");
         Linear* l2 = new_linear(S, d.hidden, d.classes, "Linear2");
         graph logits = l2->forward(GraphOperations::RELU(l1->forward(x)));
-        S.loss = GraphOperations::SoftMaxCrossEntropy(logits, target, true);
+        S.loss = class_loss(S, logits, "labels", d.batch, 1, d.classes);
     } else if (d.config == MLE_CFG_ENCODER) {
         graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tokens", d.vocab));
-        graph target = onehot_target(S, "targets", d.batch, d.seq_len, d.vocab);
         for (int l = 0; l < d.layers; ++l) x = encoder_block(S, x, d.seq_len, "Enc" + std::to_string(l));
         Linear* proj = new_linear(S, d.d_model, d.vocab, "Projection");
-        S.loss = GraphOperations::SoftMaxCrossEntropy(proj->forward(x), target, true);
+        S.loss = class_loss(S, proj->forward(x), "targets", d.batch, d.seq_len, d.vocab);
     } else if (d.config == MLE_CFG_UNET) {
         // U_NET::build_train (Engine/diffusion.cu:271-294) with three levels
         const int B = d.batch, C = d.channels, HW = d.image_size, w = d.base_width;
@@ -283,10 +294,9 @@ void build(Session& S) {
         graph e = GraphOperations::MatrixPositionalEncoding(token_input(S, "src", d.vocab));
         for (int l = 0; l < d.layers; ++l) e = encoder_block(S, e, d.seq_len, "Enc" + std::to_string(l));
         graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tgt_in", d.vocab));
-        graph target = onehot_target(S, "tgt_out", d.batch, d.seq_len, d.vocab);
         for (int l = 0; l < d.layers; ++l) x = decoder_block(S, x, e, d.seq_len, "Dec" + std::to_string(l));
         Linear* proj = new_linear(S, d.d_model, d.vocab, "Projection");
-        S.loss = GraphOperations::SoftMaxCrossEntropy(proj->forward(x), target, true);
+        S.loss = class_loss(S, proj->forward(x), "tgt_out", d.batch, d.seq_len, d.vocab);
     }
     S.go.nodes = topological_sort(S.loss);
 }
@@ -562,6 +572,78 @@ int mle_session_param_step(mle_session_t s, int i, int* t) {
     StreamScope sc(S->stream, S->d.gemm_mode);
     S->params[i]->sync_step();
     *t = S->params[i]->t;
+    return MLE_OK;
+}
+
+// Checkpoints: every parameter of the session in build order as the
+// reference's AdamParameter::save records (u32 name length, name, i32 count,
+// f32 weights, m, v; Engine/engine.cu:139-188), the file a use case gets
+// from calling save() on its layers in the same order.  The reference does
+// not save the Adam step t; `<path>.t` holds it (i32 count, then one i32 per
+// parameter) so a resumed run continues the bias corrections.  Under data
+// parallelism only rank 0 writes.  Loading checks every record's name and
+// size before touching a parameter.
+static bool read_record_header(std::ifstream& f, std::string& name, int& total) {
+    uint32_t len = 0;
+    if (!f.read(reinterpret_cast<char*>(&len), sizeof(len)) || len > (1u << 20)) return false;
+    name.assign(len, '\0');
+    if (len && !f.read(&name[0], len)) return false;
+    return (bool)f.read(reinterpret_cast<char*>(&total), sizeof(int));
+}
+
+int mle_session_save(mle_session_t s, const char* path) {
+    Session* S = as_session(s);
+    if (!S || !path) return MLE_ERR_ARG;
+    if (S->dp && S->dp->rank() != 0) return MLE_OK;
+    StreamScope sc(S->stream, S->d.gemm_mode);
+    if (cudaStreamSynchronize(S->stream) != cudaSuccess) return MLE_ERR_CUDA;
+    {
+        std::ofstream f(path, std::ios::binary | std::ios::trunc);
+        if (!f) return MLE_ERR_ARG;
+        for (AdamParameter* p : S->params) p->save(f);
+        if (!f) return MLE_ERR_ARG;
+    }
+    std::ofstream t(std::string(path) + ".t", std::ios::binary | std::ios::trunc);
+    if (!t) return MLE_ERR_ARG;
+    const int n = (int)S->params.size();
+    t.write(reinterpret_cast<const char*>(&n), sizeof(n));
+    for (AdamParameter* p : S->params) {
+        p->sync_step();
+        const int32_t v = p->t;
+        t.write(reinterpret_cast<const char*>(&v), sizeof(v));
+    }
+    return t ? MLE_OK : MLE_ERR_ARG;
+}
+
+int mle_session_load(mle_session_t s, const char* path) {
+    Session* S = as_session(s);
+    if (!S || !path) return MLE_ERR_ARG;
+    StreamScope sc(S->stream, S->d.gemm_mode);
+    {
+        // names and sizes first, so a mismatched file changes nothing
+        std::ifstream f(path, std::ios::binary);
+        if (!f) return MLE_ERR_ARG;
+        for (AdamParameter* p : S->params) {
+            std::string name;
+            int total = 0;
+            if (!read_record_header(f, name, total) || name != p->op_name || total != (int)p->total)
+                return MLE_ERR_ARG;
+            if (!f.seekg((std::streamoff)total * 3 * (std::streamoff)sizeof(float), std::ios::cur)) return MLE_ERR_ARG;
+        }
+    }
+    if (cudaStreamSynchronize(S->stream) != cudaSuccess) return MLE_ERR_CUDA;
+    std::ifstream f(path, std::ios::binary);
+    for (AdamParameter* p : S->params) p->load(f);
+    std::ifstream t(std::string(path) + ".t", std::ios::binary);
+    int n = 0;
+    if (t && t.read(reinterpret_cast<char*>(&n), sizeof(n)) && n == (int)S->params.size()) {
+        for (AdamParameter* p : S->params) {
+            int32_t v = 0;
+            if (!t.read(reinterpret_cast<char*>(&v), sizeof(v)) || v < 1) return MLE_ERR_ARG;
+            p->t = v;
+            if (cudaMemcpy(p->t_dev, &v, sizeof(v), cudaMemcpyHostToDevice) != cudaSuccess) return MLE_ERR_CUDA;
+        }
+    }
     return MLE_OK;
 }
 

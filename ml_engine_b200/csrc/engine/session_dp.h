@@ -40,6 +40,7 @@ class DataParallel {
     // reduction (before clip and update).
     void reduce_remaining(cudaStream_t compute);
     int world() const { return world_; }
+    int rank() const { return rank_; }
     int bucket_count() const { return (int)buckets_.size(); }
 
    private:

@@ -200,6 +200,57 @@ __global__ void smce_fwd_cached(const float* __restrict__ logits, const float* _
     if (threadIdx.x == 0) atomicAdd(loss, (float)(part / total));
 }
 
+// The same with the target given as one class index per row (the one-hot
+// row of the reference's dense target: 1 at `label`, 0 elsewhere; a label
+// outside [0, cols) is a row of zeros).  Each row's loss term and gradient
+// are those of the dense kernel on the one-hot target, bit for bit.
+template <int EPT>
+__global__ void smce_index_fwd_cached(const float* __restrict__ logits, const int32_t* __restrict__ labels,
+                                      float* __restrict__ probs, float* __restrict__ loss, float* __restrict__ grad,
+                                      float batch_div, int cols, double total) {
+    pdl_entry();
+    __shared__ float scratch[32];
+    __shared__ double dscratch[32];
+    const int64_t row = blockIdx.x;
+    const int label = labels[row];
+    float v[EPT];
+    load_row<EPT>(logits + row * cols, cols, v);
+    const float s = row_softmax_regs<EPT>(v, cols, 0, 0, scratch);
+    double part = 0.0;
+#pragma unroll
+    for (int k = 0; k < EPT / 4; ++k) {
+        const int c = (k * blockDim.x + threadIdx.x) * 4;
+        if (c < cols) {
+            float p[4], g[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                p[j] = v[4 * k + j] / s;
+                const float tt = (c + j == label) ? 1.0f : 0.0f;
+                if (tt != 0.0f) part += -(double)tt * log((double)p[j] + 1e-27);
+                g[j] = (p[j] + (-1.0f) * tt) / batch_div;
+            }
+            if (probs) *reinterpret_cast<float4*>(probs + row * cols + c) = make_float4(p[0], p[1], p[2], p[3]);
+            if (grad) *reinterpret_cast<float4*>(grad + row * cols + c) = make_float4(g[0], g[1], g[2], g[3]);
+        }
+    }
+    part = block_sum(part, dscratch);
+    if (threadIdx.x == 0) atomicAdd(loss, (float)(part / total));
+}
+
+__global__ void smce_index_bwd_kernel(const float* __restrict__ probs, const int32_t* __restrict__ labels,
+                                      const float* __restrict__ upstream, float* __restrict__ grad, float batch_div,
+                                      int cols, int64_t n) {
+    pdl_entry();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const int64_t row = i / cols;
+        const float tt = (int)(i - row * cols) == labels[row] ? 1.0f : 0.0f;
+        float g = probs[i] + (-1.0f) * tt;
+        if (upstream) g *= upstream[0];
+        grad[i] = g / batch_div;
+    }
+}
+
 __global__ void smce_fwd_generic(const float* __restrict__ logits, const float* __restrict__ target,
                                  float* __restrict__ probs, float* __restrict__ loss, float* __restrict__ grad,
                                  float batch_div, int cols, double total) {
@@ -339,9 +390,46 @@ int mle_softmax_ce_fwd(const float* logits, const float* target, float* probs, f
     else if (vec && cols <= 16 * kRowThreads)
         launch_k(smce_fwd_cached<16>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div,
                                                                    cols, total);
+    else if (vec && cols <= 32 * kRowThreads)  // two threads' share per thread of a 512-thread block
+        launch_k(smce_fwd_cached<16>, (unsigned)rows, 2 * kRowThreads, 0, st, logits, target, probs, loss, grad,
+                 batch_div, cols, total);
     else
         launch_k(smce_fwd_generic, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, cols,
                                                                  total);
+    return launch_status();
+}
+
+int mle_softmax_ce_index_fwd(const float* logits, const int32_t* labels, float* probs, float* loss, float* grad,
+                             float batch_div, int64_t rows, int cols, mle_stream_t stream) {
+    if (rows < 0 || cols <= 0 || !logits || !labels || !loss || batch_div == 0.0f) return MLE_ERR_ARG;
+    const bool vec = cols % 4 == 0 && aligned16(logits) && (!probs || aligned16(probs)) && (!grad || aligned16(grad));
+    if (!vec || cols > 32 * kRowThreads) return MLE_ERR_UNSUPPORTED;
+    cudaStream_t st = as_stream(stream);
+    if (cudaMemsetAsync(loss, 0, sizeof(float), st) != cudaSuccess) return launch_status();
+    if (rows == 0) return MLE_OK;
+    const double total = (double)rows * (double)cols;
+    if (cols <= 4 * kRowThreads)
+        launch_k(smce_index_fwd_cached<4>, (unsigned)rows, kRowThreads, 0, st, logits, labels, probs, loss, grad,
+                 batch_div, cols, total);
+    else if (cols <= 8 * kRowThreads)
+        launch_k(smce_index_fwd_cached<8>, (unsigned)rows, kRowThreads, 0, st, logits, labels, probs, loss, grad,
+                 batch_div, cols, total);
+    else if (cols <= 16 * kRowThreads)
+        launch_k(smce_index_fwd_cached<16>, (unsigned)rows, kRowThreads, 0, st, logits, labels, probs, loss, grad,
+                 batch_div, cols, total);
+    else
+        launch_k(smce_index_fwd_cached<16>, (unsigned)rows, 2 * kRowThreads, 0, st, logits, labels, probs, loss, grad,
+                 batch_div, cols, total);
+    return launch_status();
+}
+
+int mle_softmax_ce_index_bwd(const float* probs, const int32_t* labels, const float* upstream, float* grad,
+                             float batch_div, int64_t rows, int cols, mle_stream_t stream) {
+    if (rows < 0 || cols <= 0 || !probs || !labels || !grad || batch_div == 0.0f) return MLE_ERR_ARG;
+    const int64_t n = rows * cols;
+    if (n == 0) return MLE_OK;
+    launch_k(smce_index_bwd_kernel, grid_for(n, 256), 256, 0, as_stream(stream), probs, labels, upstream, grad,
+             batch_div, cols, n);
     return launch_status();
 }
 

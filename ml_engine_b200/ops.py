@@ -152,6 +152,16 @@ def softmax_ce_bwd(probs, target, grad, batch_div, upstream=None):
     _call("mle_softmax_ce_bwd", _p(probs), _p(target), _p(upstream), _p(grad), batch_div, probs.numel(), _s())
 
 
+def softmax_ce_index_fwd(logits, labels, probs, loss, grad, batch_div, rows, cols):
+    """labels: int32, one class index per row."""
+    _call("mle_softmax_ce_index_fwd", _p(logits), _p(labels), _p(probs), _p(loss), _p(grad), batch_div, rows, cols,
+          _s())
+
+
+def softmax_ce_index_bwd(probs, labels, grad, batch_div, rows, cols, upstream=None):
+    _call("mle_softmax_ce_index_bwd", _p(probs), _p(labels), _p(upstream), _p(grad), batch_div, rows, cols, _s())
+
+
 def mse_fwd(x, target, loss):
     _call("mle_mse_fwd", _p(x), _p(target), _p(loss), x.numel(), _s())
 

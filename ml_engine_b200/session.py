@@ -33,6 +33,7 @@ class SessionDesc(ctypes.Structure):
         ("gemm_mode", ctypes.c_int),
         ("channels", ctypes.c_int), ("image_size", ctypes.c_int), ("base_width", ctypes.c_int),
         ("t_embed", ctypes.c_int), ("timestep", ctypes.c_int),
+        ("dense_targets", ctypes.c_int),
     ]
 
 
@@ -132,6 +133,14 @@ class Session:
         t = ctypes.c_int()
         self._lib.call("mle_session_param_step", self._h, i, ctypes.addressof(t))
         return t.value
+
+    def save(self, path):
+        """Checkpoint in the reference's AdamParameter::save record format
+        (build order) plus `<path>.t` with the Adam steps."""
+        self._lib.call("mle_session_save", self._h, str(path).encode())
+
+    def load(self, path):
+        self._lib.call("mle_session_load", self._h, str(path).encode())
 
     def write_embedding(self, i, table):
         table = np.ascontiguousarray(table, np.float32).ravel()

@@ -241,7 +241,7 @@ def test_softmax(cuda, ops, orc, rng, axis, causal, bc, rows, cols):
     assert rel_err(H(gx), orc.softmax_bwd(ry, gy, gx0.copy(), bc, rows, cols, axis)) <= RTOL_EXACT
 
 
-@pytest.mark.parametrize("rows,cols", [(64, 10), (256, 4096), (3, 8192 + 4), (9, 1001)])
+@pytest.mark.parametrize("rows,cols", [(64, 10), (256, 4096), (3, 8192 + 4), (9, 1001), (40, 8192)])
 def test_softmax_cross_entropy(cuda, ops, orc, rng, rows, cols):
     logits = (rng.standard_normal((rows, cols)) * 2).astype(np.float32)
     labels = rng.integers(0, cols, rows)
@@ -259,6 +259,38 @@ def test_softmax_cross_entropy(cuda, ops, orc, rng, rows, cols):
     g2 = torch.empty(rows, cols, device=cuda)
     ops.softmax_ce_bwd(probs, T(target, cuda), g2, batch)
     assert rel_err(H(g2), orc.smce_bwd(rp, target, batch)) <= RTOL_EXACT
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 12), (256, 1024), (33, 4096), (40, 8192)])
+def test_softmax_cross_entropy_index_labels(cuda, ops, rng, rows, cols):
+    """The index-label entry points against the dense ones on the one-hot
+    target of the same labels: probs and gradients bit for bit, the loss up
+    to the order of its atomics (labels -1 and cols are rows of zeros)."""
+    logits = (rng.standard_normal((rows, cols)) * 2).astype(np.float32)
+    labels = rng.integers(0, cols, rows).astype(np.int32)
+    labels[0], labels[-1] = -1, cols
+    target = np.zeros((rows, cols), np.float32)
+    ok = (labels >= 0) & (labels < cols)
+    target[np.arange(rows)[ok], labels[ok]] = 1.0
+    tl, tt = T(logits, cuda), T(target, cuda)
+    out = {}
+    for kind in ("dense", "index"):
+        probs, grad = torch.empty(rows, cols, device=cuda), torch.empty(rows, cols, device=cuda)
+        loss, g2 = torch.empty(1, device=cuda), torch.empty(rows, cols, device=cuda)
+        up = torch.full((1,), 0.75, device=cuda)
+        if kind == "dense":
+            ops.softmax_ce_fwd(tl, tt, probs, loss, grad, 4.0, rows, cols)
+            ops.softmax_ce_bwd(probs, tt, g2, 4.0, upstream=up)
+        else:
+            lab = T(labels, cuda)
+            ops.softmax_ce_index_fwd(tl, lab, probs, loss, grad, 4.0, rows, cols)
+            ops.softmax_ce_index_bwd(probs, lab, g2, 4.0, rows, cols, upstream=up)
+        out[kind] = [H(t) for t in (probs, grad, g2, loss)]
+    for a, b in zip(out["dense"][:3], out["index"][:3]):
+        assert np.array_equal(a, b)
+    # the loss sums per-row terms with float atomics in either kernel
+    la, lb = float(out["dense"][3][0]), float(out["index"][3][0])
+    assert abs(la - lb) <= 1e-6 * abs(la)
 
 
 def test_mse(cuda, ops, orc, rng):

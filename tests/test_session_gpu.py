@@ -202,3 +202,101 @@ def test_loss_decreases_on_fixed_batch(cuda, rng):
     for _ in range(30):
         last = s.step()
     assert last < 0.5 * first
+
+
+def _read_reference_checkpoint(path):
+    """Records of the reference's AdamParameter::save (Engine/engine.cu:
+    139-188): u32 name length, name, i32 count, f32 weights, m, v."""
+    import struct
+    recs = []
+    with open(path, "rb") as f:
+        data = f.read()
+    off = 0
+    while off < len(data):
+        (n,) = struct.unpack_from("<I", data, off)
+        off += 4
+        name = data[off:off + n].decode()
+        off += n
+        (total,) = struct.unpack_from("<i", data, off)
+        off += 4
+        arrs = []
+        for _ in range(3):
+            arrs.append(np.frombuffer(data, np.float32, total, off).copy())
+            off += 4 * total
+        recs.append((name, arrs))
+    return recs
+
+
+def test_checkpoint_roundtrip_and_resume(cuda, rng, tmp_path):
+    """save() writes the reference's record format (checked field by field
+    against the session's parameters) and a step sidecar; a session with
+    other weights and moments that loads it holds the same state and
+    continues like the original."""
+    kw = dict(config=2, batch=2, seq_len=32, d_model=64, heads=4, ffn=128, layers=1, vocab=128, gemm_mode=1)
+    a = _session(seed=9, **kw)
+    tokens = rng.integers(0, 128, 64).astype(np.int32)
+    targets = rng.integers(0, 128, 64).astype(np.int32)
+    a.inputs["tokens"][:] = tokens
+    a.inputs["targets"][:] = targets
+    for _ in range(3):
+        a.step()
+    path = tmp_path / "ckpt.bin"
+    a.save(path)
+    recs = _read_reference_checkpoint(path)
+    assert [r[0] for r in recs] == list(a.param_names)
+    for i, (_, (w, m, v)) in enumerate(recs):
+        assert np.array_equal(w, a.read_param(i, 0))
+        assert np.array_equal(m, a.read_param(i, 2))
+        assert np.array_equal(v, a.read_param(i, 3))
+    steps = np.fromfile(str(path) + ".t", np.int32)
+    assert steps[0] == len(recs) and np.all(steps[1:] == 4)
+
+    # same seed for the (untrained, gather-only) embedding table; every
+    # parameter and moment overwritten before the load
+    b = _session(seed=9, **kw)
+    b.inputs["tokens"][:] = tokens
+    b.inputs["targets"][:] = targets
+    for i in range(len(recs)):
+        for which in (0, 2, 3):
+            b.write_param(i, rng.standard_normal(b.param_sizes[i]).astype(np.float32), which)
+    assert not np.array_equal(b.read_param(0), a.read_param(0))
+    b.load(path)
+    for i in range(len(recs)):
+        assert np.array_equal(b.read_param(i, 0), a.read_param(i, 0))
+        assert b.param_step(i) == 4
+    # the next step: equal up to the order of the bias-gradient atomics
+    la, lb = a.step(), b.step()
+    assert abs(la - lb) <= 1e-6 * abs(la)
+    for i in range(len(recs)):
+        assert norm_err(b.read_param(i, 0), a.read_param(i, 0)) <= 1e-6, a.param_names[i]
+        assert b.param_step(i) == 5
+
+
+def test_checkpoint_mismatch_changes_nothing(cuda, rng, tmp_path):
+    from ml_engine_b200._lib import MLEError
+    a = _session(config=2, batch=2, seq_len=16, d_model=32, heads=2, ffn=64, layers=1, vocab=64, seed=1)
+    path = tmp_path / "small.bin"
+    a.save(path)
+    b = _session(config=2, batch=2, seq_len=16, d_model=64, heads=2, ffn=64, layers=1, vocab=64, seed=2)
+    before = [b.read_param(i) for i in range(len(b.param_names))]
+    with pytest.raises(MLEError):
+        b.load(path)
+    for i, w in enumerate(before):
+        assert np.array_equal(b.read_param(i), w)
+
+
+def test_index_labels_match_dense_targets(cuda, rng):
+    """The session's index-label loss (default) against the reference's dense
+    one-hot target graph (dense_targets=1): same loss and parameters."""
+    kw = dict(config=2, batch=2, seq_len=32, d_model=64, heads=4, ffn=128, layers=1, vocab=128, seed=9, gemm_mode=1)
+    a, b = _session(dense_targets=1, **kw), _session(dense_targets=0, **kw)
+    tokens = rng.integers(0, 128, 64).astype(np.int32)
+    targets = rng.integers(0, 128, 64).astype(np.int32)
+    for s in (a, b):
+        s.inputs["tokens"][:] = tokens
+        s.inputs["targets"][:] = targets
+    for _ in range(2):
+        la, lb = a.step(), b.step()
+        assert abs(la - lb) <= 1e-6 * abs(la)
+    for i in range(len(a.param_names)):
+        assert norm_err(b.read_param(i), a.read_param(i)) <= 1e-6, a.param_names[i]
