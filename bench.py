@@ -567,12 +567,17 @@ def main():
                          "encdec: configs[2], global batch 256 over the ranks")
     ap.add_argument("--gemm-pairs", type=int, default=None, choices=[0, 1, 2],
                     help="run large products on CTA pairs (mle_set_gemm_pairs); default: the library's")
+    ap.add_argument("--attn-path", default=None, choices=["auto", "fused", "tensor"],
+                    help="attention implementation (mle_set_attention_path); default: the library's")
     ap.add_argument("--roofline-only", action="store_true",
                     help="run only the roofline kernel pair (3 untimed + 20 timed pairs)")
     args = ap.parse_args()
     if args.gemm_pairs is not None:
         from ml_engine_b200._lib import kernels
         kernels().call("mle_set_gemm_pairs", args.gemm_pairs)
+    if args.attn_path is not None:
+        from ml_engine_b200._lib import kernels
+        kernels().call("mle_set_attention_path", {"auto": 0, "fused": 1, "tensor": 2}[args.attn_path])
     if args.sweep:
         run_sweep(args)
         return

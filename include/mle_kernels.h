@@ -297,6 +297,12 @@ int mle_get_gemm_pairs(void);
 /* out3 = {tile width, split-K count, 1 if CTA pairs} of this thread's last
  * single tensor-core product (diagnostics for tests and benchmarks). */
 int mle_gemm_last_choice(int* out3);
+/* How the tensor-core GEMM writes assigned outputs on this host thread:
+ * 0 bulk tensor (TMA) stores of staged 32 x 32 blocks, 1 (default) the
+ * epilogue warps' own row-contiguous 16-byte stores, measured faster on
+ * B200 for every shape tried.  Accumulated outputs always use bulk tensor
+ * reduce-adds.  No counterpart in the reference. */
+int mle_set_gemm_store_path(int path);
 
 /* Batched GEMM with the reference's broadcast flags.  Same argument meaning
  * as bcmm/bcmmABT/bcmmATB/bcmmT (Engine/kernels.cu:387-539): `backward`!=0
@@ -407,10 +413,10 @@ int mle_attention_fused_supported(int seq_q, int seq_k, int head_dim, int softma
 
 /* Which implementation mle_attention_fwd/bwd use for the column softmax on
  * this host thread (no counterpart in the reference):
- *   MLE_ATTN_PATH_AUTO  : tensor cores in TF32 GEMM mode for long sequences
- *                         (Sq*Sk*hd >= 2^21, e.g. 256 x 256 x 64), the CUDA-
- *                         core kernels in the reference's summation order
- *                         otherwise and in FP32 GEMM mode;
+ *   MLE_ATTN_PATH_AUTO  : tensor cores in TF32 GEMM mode when the heads are
+ *                         not tiny (Sq*Sk*hd >= 2^18, e.g. 128 x 128 x 32),
+ *                         the CUDA-core kernels in the reference's summation
+ *                         order otherwise and in FP32 GEMM mode;
  *   MLE_ATTN_PATH_FUSED : always the CUDA-core kernels where they apply;
  *   MLE_ATTN_PATH_TENSOR: tensor cores wherever the sizes allow (TF32 GEMM
  *                         mode, Sq <= 256, Sq, Sk, hd multiples of 4; the

@@ -691,8 +691,10 @@ bool tc_attention_ok(int axis, int Sq, int Sk, int hd, int64_t BH, bool bwd, int
     if (axis != 1 || Sq > kTcMaxRows || hd % 4 || Sq % 4 || Sk % 4 || BH > INT32_MAX) return false;
     if (bwd && key_mode == MLE_KEYGRAD_REFERENCE && !(Sq == Sk && hd % 32 == 0 && Sk % hd == 0)) return false;
     if (g_attn_path == MLE_ATTN_PATH_TENSOR) return true;
-    // the CUDA-core kernels win below about 2M multiply-adds per head product
-    return (int64_t)Sq * Sk * hd >= (1ll << 21) || !fused_ok(axis, Sq, Sk, hd, 1, 1);
+    // the CUDA-core kernels win below about 256K multiply-adds per head
+    // product (measured: configs[1], 128 x 128 x 32, ran 10 % faster per
+    // step on the tensor-core path)
+    return (int64_t)Sq * Sk * hd >= (1ll << 18) || !fused_ok(axis, Sq, Sk, hd, 1, 1);
 }
 
 int tc_attention_fwd(const float* Q, const float* K, const float* V, float* P, float* O, int B, int H, int Sq, int Sk,

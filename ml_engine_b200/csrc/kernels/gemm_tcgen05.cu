@@ -485,7 +485,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int64_t t = t_first; ok && t < total_tiles; t += t_step) {
                 const int g = group_of(grp, t);
-                const EpiParams& ep = grp.ep[g];
+                // a register copy: a reference into the parameter space would be
+                // re-read after every shared-memory or global access
+                const EpiParams ep = grp.ep[g];
                 const CUtensorMap* tmA = &grp.a[g];
                 const CUtensorMap* tmB = &grp.b[g];
                 const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
@@ -578,7 +580,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int acc = 0;
             for (int64_t t = t_first; ok && t < total_tiles; t += t_step, ++acc) {
                 const int g = group_of(grp, t);
-                const Tile x = tile_at(grp.ep[g], t - grp.tile_start[g], BN, BMT);
+                const EpiParams ep = grp.ep[g];
+                const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
                 const int buf = acc & 1;
                 const uint32_t use = (uint32_t)(acc >> 1);
                 if (!wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) break;
@@ -626,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t blocks_out = 0;  // bulk groups this warp committed
         for (int64_t t = t_first; t < total_tiles; t += t_step, ++acc) {
             const int g = group_of(grp, t);
-            const EpiParams& ep = grp.ep[g];
+            const EpiParams ep = grp.ep[g];  // register copy (see the producer)
             const CUtensorMap* tmC = &grp.c[g];
             const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
             const int buf = acc & 1;
@@ -937,6 +940,9 @@ static bool tc_eligible(const GemmProblem& p) {
 static thread_local int g_gemm_mode = MLE_GEMM_MODE_TF32;
 // whether large plain products may run on CTA pairs (256-row tiles)
 static thread_local int g_gemm_pairs = 1;
+// how assigned (not accumulated) outputs leave the epilogue: 0 bulk tensor
+// stores, 1 the epilogue warps' own 16-byte stores
+static thread_local int g_store_path = 1;
 // tile width, split count and pair flag of this thread's last tensor-core launch
 static thread_local int g_last_choice[3] = {0, 0, 0};
 
@@ -1137,7 +1143,9 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
         ok = true;
         return MLE_OK;
     }
-    if (aligned16(p.C) && (p.ldc & 3) == 0 && (ep.c_stride_b & 3) == 0 && (ep.c_stride_c & 3) == 0) {
+    const bool assign_out = p.mode == EPI_ASSIGN && splits == 1 && !force_atomic;
+    if (aligned16(p.C) && (p.ldc & 3) == 0 && (ep.c_stride_b & 3) == 0 && (ep.c_stride_c & 3) == 0 &&
+        !(assign_out && g_store_path == 1)) {
         OperandView vc;
         vc.base = p.C;
         vc.inner = p.N;
@@ -1475,6 +1483,12 @@ int mle_set_gemm_pairs(int enable) {
 }
 
 int mle_get_gemm_pairs(void) { return g_gemm_pairs; }
+
+int mle_set_gemm_store_path(int path) {
+    if (path != 0 && path != 1) return MLE_ERR_ARG;
+    g_store_path = path;
+    return MLE_OK;
+}
 
 int mle_gemm_last_choice(int* out3) {
     if (!out3) return MLE_ERR_ARG;
