@@ -419,7 +419,7 @@ int mle_attention_fused_supported(int seq_q, int seq_k, int head_dim, int softma
  *                         order otherwise and in FP32 GEMM mode;
  *   MLE_ATTN_PATH_FUSED : always the CUDA-core kernels where they apply;
  *   MLE_ATTN_PATH_TENSOR: tensor cores wherever the sizes allow (TF32 GEMM
- *                         mode, Sq <= 256, Sq, Sk, hd multiples of 4; the
+ *                         mode, Sq, Sk, hd multiples of 4; the
  *                         reference key gradient also needs Sq == Sk, hd a
  *                         multiple of 32 dividing Sk).
  * The tensor-core backward writes its score gradients to `workspace`. */

@@ -24,8 +24,8 @@
 // mle_set_attention_path): the two forward and four backward products run
 // on the tcgen05 GEMM, which reads Q, K, V, dO and writes O, dQ, dK, dV in
 // either layout through strides, P and the score gradients [B,H,Sq,Sk] in
-// between; the column softmax and its backward are column-block kernels
-// that park a 32-column slab in shared memory between their passes.  The reference's key gradient (memory of
+// between; the column softmax and its backward are multi-pass column-block
+// kernels (max, sum, update; dot, update) with 16-byte accesses.  The reference's key gradient (memory of
 // dScores read as [Sk,Sq], result laid out [hd,Sk] in the head's block) is
 // one GEMM whose output columns are split over rows of the head block.
 //
@@ -541,115 +541,136 @@ int dispatch_hd(int hd, F&& f) {
 
 // ------------------------------ tensor-core path -----------------------------
 thread_local int g_attn_path = MLE_ATTN_PATH_AUTO;
-constexpr int kTcMaxRows = 256;  // column softmax kernels keep a column in registers
 
 // Column softmax of each [rows, cols] matrix in place (the reference's type
 // 1, causal entries key > query zeroed after the max over the whole column,
-// as SoftMask does).  A 256-thread block owns (matrix, 32 columns): lane =
-// the column, warp w the rows w, w + 8, ...; each thread parks its values
-// in shared memory between the passes (rows x 32 floats per block), so
-// several blocks share an SM and their loads overlap.
+// as SoftMask does).  A 256-thread block owns (matrix, 128 columns): lane l
+// holds columns 4l..4l+3 (16-byte accesses), warp w the rows w, w + 8, ...
+// Three passes over the block's rows, the later two served by L2: the
+// column max, the sum of the exponentials, the probabilities; the 8 warps'
+// partials merge in shared memory.  Every pass is a short dependency chain
+// per element, so the loads of several rows stay in flight.  cols % 4 == 0.
 constexpr int kSmThreads = 256;
 
-__global__ void __launch_bounds__(kSmThreads) col_softmax_smem(float* __restrict__ P, int rows, int cols, int causal,
-                                                               int mats) {
+__global__ void __launch_bounds__(kSmThreads) col_softmax_vec(float* __restrict__ P, int rows, int cols, int causal,
+                                                              int mats) {
     pdl_entry();
-    extern __shared__ float tile[];  // [rows][32]
-    __shared__ float red[8][33];
+    __shared__ float red[8][128 + 4];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int c = blockIdx.x * 32 + lane;
+    const int c0 = blockIdx.x * 128 + lane * 4;
+    const bool live = c0 < cols;
     for (int mat = blockIdx.y; mat < mats; mat += gridDim.y) {
-        float* Pm = P + (int64_t)mat * rows * cols + c;
-        float m = -FLT_MAX;
-#pragma unroll 4
-        for (int r = warp; r < rows; r += 8) {
-            const float v = c < cols ? Pm[(int64_t)r * cols] : -FLT_MAX;
-            tile[r * 32 + lane] = v;
-            m = fmaxf(m, v);
+        float* Pm = P + (int64_t)mat * rows * cols + c0;
+        float m[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
+        if (live) {
+#pragma unroll 8
+            for (int r = warp; r < rows; r += 8) {
+                const float4 v = *reinterpret_cast<const float4*>(Pm + (int64_t)r * cols);
+                m[0] = fmaxf(m[0], v.x);
+                m[1] = fmaxf(m[1], v.y);
+                m[2] = fmaxf(m[2], v.z);
+                m[3] = fmaxf(m[3], v.w);
+            }
         }
-        red[warp][lane] = m;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) red[warp][lane * 4 + j] = m[j];
         __syncthreads();
 #pragma unroll
-        for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w][lane]);
+        for (int j = 0; j < 4; ++j)
+            for (int w = 0; w < 8; ++w) m[j] = fmaxf(m[j], red[w][lane * 4 + j]);
         __syncthreads();
-        float sum = 0.f;
-#pragma unroll 4
-        for (int r = warp; r < rows; r += 8) {
-            const float e = (c < cols && !(causal && c > r)) ? expf(tile[r * 32 + lane] - m) : 0.f;
-            tile[r * 32 + lane] = e;
-            sum += e;
-        }
-        red[warp][lane] = sum;
-        __syncthreads();
-        float tot = 0.f;
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) {
+#pragma unroll 8
+            for (int r = warp; r < rows; r += 8) {
+                const float4 v4 = *reinterpret_cast<const float4*>(Pm + (int64_t)r * cols);
+                const float v[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-        for (int w = 0; w < 8; ++w) tot += red[w][lane];
+                for (int j = 0; j < 4; ++j) sum[j] += (causal && c0 + j > r) ? 0.f : expf(v[j] - m[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) red[warp][lane * 4 + j] = sum[j];
         __syncthreads();
-        if (tot < 1e-45f) tot = 1.0f;
-        if (c < cols) {
-#pragma unroll 4
-            for (int r = warp; r < rows; r += 8) Pm[(int64_t)r * cols] = tile[r * 32 + lane] / tot;
+        float inv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float t = 0.f;
+            for (int w = 0; w < 8; ++w) t += red[w][lane * 4 + j];
+            if (t < 1e-45f) t = 1.0f;
+            inv[j] = 1.0f / t;
+        }
+        __syncthreads();
+        if (live) {
+#pragma unroll 8
+            for (int r = warp; r < rows; r += 8) {
+                float4* p4 = reinterpret_cast<float4*>(Pm + (int64_t)r * cols);
+                const float4 v4 = *p4;
+                const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+                float o[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) o[j] = (causal && c0 + j > r) ? 0.f : expf(v[j] - m[j]) * inv[j];
+                *p4 = make_float4(o[0], o[1], o[2], o[3]);
+            }
         }
     }
 }
 
-// G (dP on entry) becomes dS = P (dP - sum over the column of P dP).
-__global__ void __launch_bounds__(kSmThreads) col_softmax_bwd_smem(const float* __restrict__ P, float* __restrict__ G,
-                                                                   int rows, int cols, int mats) {
+// G (dP on entry) becomes dS = P (dP - sum over the column of P dP); same
+// block shape, pass 1 the column dots, pass 2 the update.
+__global__ void __launch_bounds__(kSmThreads) col_softmax_bwd_vec(const float* __restrict__ P, float* __restrict__ G,
+                                                                  int rows, int cols, int mats) {
     pdl_entry();
-    extern __shared__ float tile[];  // [rows][32] of P, then [rows][32] of G
-    __shared__ float red[8][33];
+    __shared__ float red[8][128 + 4];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int c = blockIdx.x * 32 + lane;
-    float* tg = tile + rows * 32;
+    const int c0 = blockIdx.x * 128 + lane * 4;
+    const bool live = c0 < cols;
     for (int mat = blockIdx.y; mat < mats; mat += gridDim.y) {
-        const float* Pm = P + (int64_t)mat * rows * cols + c;
-        float* Gm = G + (int64_t)mat * rows * cols + c;
-        float dot = 0.f;
-        if (c < cols) {
-#pragma unroll 4
+        const float* Pm = P + (int64_t)mat * rows * cols + c0;
+        float* Gm = G + (int64_t)mat * rows * cols + c0;
+        float dot[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) {
+#pragma unroll 8
             for (int r = warp; r < rows; r += 8) {
-                const float pv = Pm[(int64_t)r * cols], gv = Gm[(int64_t)r * cols];
-                tile[r * 32 + lane] = pv;
-                tg[r * 32 + lane] = gv;
-                dot += pv * gv;
+                const float4 p = *reinterpret_cast<const float4*>(Pm + (int64_t)r * cols);
+                const float4 g = *reinterpret_cast<const float4*>(Gm + (int64_t)r * cols);
+                dot[0] += p.x * g.x;
+                dot[1] += p.y * g.y;
+                dot[2] += p.z * g.z;
+                dot[3] += p.w * g.w;
             }
         }
-        red[warp][lane] = dot;
-        __syncthreads();
-        float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) tot += red[w][lane];
+        for (int j = 0; j < 4; ++j) red[warp][lane * 4 + j] = dot[j];
         __syncthreads();
-        if (c < cols) {
-#pragma unroll 4
-            for (int r = warp; r < rows; r += 8) Gm[(int64_t)r * cols] = tile[r * 32 + lane] * (tg[r * 32 + lane] - tot);
+        float D[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            D[j] = 0.f;
+            for (int w = 0; w < 8; ++w) D[j] += red[w][lane * 4 + j];
+        }
+        __syncthreads();
+        if (live) {
+#pragma unroll 8
+            for (int r = warp; r < rows; r += 8) {
+                const float4 p = *reinterpret_cast<const float4*>(Pm + (int64_t)r * cols);
+                float4* g4 = reinterpret_cast<float4*>(Gm + (int64_t)r * cols);
+                const float4 g = *g4;
+                *g4 = make_float4(p.x * (g.x - D[0]), p.y * (g.y - D[1]), p.z * (g.z - D[2]), p.w * (g.w - D[3]));
+            }
         }
     }
 }
 
 int tc_col_softmax(float* P, int64_t mats, int rows, int cols, int causal, cudaStream_t st) {
-    const dim3 grid((unsigned)((cols + 31) / 32), (unsigned)std::min<int64_t>(mats, 65535));
-    const size_t smem = (size_t)rows * 32 * sizeof(float);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(col_softmax_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kTcMaxRows * 32 * 4);
-        configured = true;
-    }
-    launch_k(col_softmax_smem, grid, kSmThreads, smem, st, P, rows, cols, causal, (int)mats);
+    const dim3 grid((unsigned)((cols + 127) / 128), (unsigned)std::min<int64_t>(mats, 65535));
+    launch_k(col_softmax_vec, grid, kSmThreads, 0, st, P, rows, cols, causal, (int)mats);
     return launch_status();
 }
 
 int tc_col_softmax_bwd(const float* P, float* G, int64_t mats, int rows, int cols, cudaStream_t st) {
-    const dim3 grid((unsigned)((cols + 31) / 32), (unsigned)std::min<int64_t>(mats, 65535));
-    const size_t smem = (size_t)2 * rows * 32 * sizeof(float);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(col_softmax_bwd_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             2 * kTcMaxRows * 32 * 4);
-        configured = true;
-    }
-    launch_k(col_softmax_bwd_smem, grid, kSmThreads, smem, st, P, G, rows, cols, (int)mats);
+    const dim3 grid((unsigned)((cols + 127) / 128), (unsigned)std::min<int64_t>(mats, 65535));
+    launch_k(col_softmax_bwd_vec, grid, kSmThreads, 0, st, P, G, rows, cols, (int)mats);
     return launch_status();
 }
 
@@ -682,13 +703,12 @@ GemmProblem attn_gemm(const float* A, const float* B, float* C, int M, int N, in
     return p;
 }
 
-// Whether the tensor-core path can run these sizes (GEMM operand strides in
-// whole 16-byte units, columns of at most kTcMaxRows rows for the softmax
-// kernels, the reference key gradient's head-block split in whole 32-column
-// blocks) and is the one to take.
+// Whether the tensor-core path can run these sizes (GEMM operand strides and
+// softmax rows in whole 16-byte units, the reference key gradient's
+// head-block split in whole 32-column blocks) and is the one to take.
 bool tc_attention_ok(int axis, int Sq, int Sk, int hd, int64_t BH, bool bwd, int key_mode) {
     if (g_attn_path == MLE_ATTN_PATH_FUSED || mle_get_gemm_mode() != MLE_GEMM_MODE_TF32) return false;
-    if (axis != 1 || Sq > kTcMaxRows || hd % 4 || Sq % 4 || Sk % 4 || BH > INT32_MAX) return false;
+    if (axis != 1 || hd % 4 || Sq % 4 || Sk % 4 || BH > INT32_MAX) return false;
     if (bwd && key_mode == MLE_KEYGRAD_REFERENCE && !(Sq == Sk && hd % 32 == 0 && Sk % hd == 0)) return false;
     if (g_attn_path == MLE_ATTN_PATH_TENSOR) return true;
     // the CUDA-core kernels win below about 256K multiply-adds per head

@@ -232,7 +232,7 @@ def attention_tensor_supported(seq_q, seq_k, head_dim, softmax_axis=1, key_grad_
                                backward=True):
     """Whether ATTN_PATH_TENSOR runs these sizes on the tensor cores (TF32
     GEMM mode)."""
-    ok = softmax_axis == 1 and seq_q <= 256 and seq_q % 4 == 0 and seq_k % 4 == 0 and head_dim % 4 == 0
+    ok = softmax_axis == 1 and seq_q % 4 == 0 and seq_k % 4 == 0 and head_dim % 4 == 0
     if backward and key_grad_mode == KEYGRAD_REFERENCE:
         ok = ok and seq_q == seq_k and head_dim % 32 == 0 and seq_k % head_dim == 0
     return ok
