@@ -97,6 +97,17 @@ void release_all_arenas() {
 static int g_zero_depth = 0;
 static std::vector<std::pair<float*, int64_t>> g_zero_ranges;
 
+// Base of the arena chunk holding p (nullptr if none): ranges merge only
+// within one chunk, since two chunks that happen to be adjacent in the
+// address space are still separate allocations a memset may not span.
+static const char* chunk_base(const void* p) {
+    const char* c = static_cast<const char*>(p);
+    for (auto& v : g_arenas)
+        for (auto& ch : v)
+            if (c >= ch.base && c < ch.base + ch.size) return ch.base;
+    return nullptr;
+}
+
 static void flush_zero_ranges() {
     auto& r = g_zero_ranges;
     if (r.empty()) return;
@@ -112,7 +123,7 @@ static void flush_zero_ranges() {
         // merge if the next range starts inside or at most one alignment pad
         // (<= 256 bytes) after the current one: the pad bytes belong to no
         // buffer, so clearing them is harmless
-        if (p <= cur + len + 64) {
+        if (p <= cur + len + 64 && chunk_base(p) == chunk_base(cur)) {
             const int64_t end = std::max<int64_t>((p + n) - cur, len);
             len = end;
         } else {
