@@ -640,12 +640,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             float* Cbase = ep.C + (int64_t)x.bidx * ep.c_stride_b + (int64_t)x.cidx * ep.c_stride_c;
             const bool live = x.nkb > 0;
+            // the warp-store path's bias for this lane's 4 columns of block cc,
+            // loaded one block ahead so its latency hides behind the stores
+            const bool row_bias = ep.bias && x.kb_begin == 0 && !ep.tma_epi;  // split 0 adds the bias
+            auto bias4 = [&](int col) {
+                float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (!row_bias) return b;
+                if (ep.vec && col + 4 <= ep.N) return __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+                if (col < ep.N) b.x = __ldg(ep.bias + col);
+                if (col + 1 < ep.N) b.y = __ldg(ep.bias + col + 1);
+                if (col + 2 < ep.N) b.z = __ldg(ep.bias + col + 2);
+                if (col + 3 < ep.N) b.w = __ldg(ep.bias + col + 3);
+                return b;
+            };
+            float4 bias_next = bias4(x.n0 + c4);
 #pragma unroll 1
             for (int cc = 0; cc < BN / 32; ++cc) {
                 const int col0 = x.n0 + cc * 32;
                 if (col0 >= ep.N) break;  // warp-uniform
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + cc * 32), r);
+                const float4 bias_cur = bias_next;
+                if (cc + 1 < BN / 32) bias_next = bias4(col0 + 32 + c4);
                 if (!live) continue;
                 if (ep.tma_epi) {
                     const int row0 = x.m0 + rank * BM + q * 32;
@@ -718,23 +734,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 const int col = col0 + c4;
                 const bool vec = ep.vec && col + 4 <= ep.N;
-                float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (ep.bias && x.kb_begin == 0) {  // split 0 adds the bias
-                    if (vec) {
-                        bv = *reinterpret_cast<const float4*>(ep.bias + col);
-                    } else {
-                        if (col < ep.N) bv.x = ep.bias[col];
-                        if (col + 1 < ep.N) bv.y = ep.bias[col + 1];
-                        if (col + 2 < ep.N) bv.z = ep.bias[col + 2];
-                        if (col + 3 < ep.N) bv.w = ep.bias[col + 3];
-                    }
-                }
-#pragma unroll 4
+                const float4 bv = bias_cur;
+                // every staged value first, then the stores: a store through a
+                // generic pointer could alias the staging area, so loads after
+                // it would wait for it
+                float4 staged[8];
+#pragma unroll
+                for (int it = 0; it < 8; ++it)
+                    staged[it] = *reinterpret_cast<const float4*>(stage + (it * 4 + rsub) * kEpiLd + c4);
+#pragma unroll
                 for (int it = 0; it < 8; ++it) {
                     const int rr = it * 4 + rsub;
                     const int row = x.m0 + rank * BM + q * 32 + rr;
                     if (row >= ep.M || col >= ep.N) continue;
-                    float4 v = *reinterpret_cast<const float4*>(stage + rr * kEpiLd + c4);
+                    float4 v = staged[it];
                     v.x = ep.alpha * v.x + bv.x;
                     v.y = ep.alpha * v.y + bv.y;
                     v.z = ep.alpha * v.z + bv.z;
