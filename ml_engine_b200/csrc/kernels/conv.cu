@@ -84,23 +84,27 @@ __global__ void col2im_kernel(const float* __restrict__ cols, float* __restrict_
         const int h = (int)(row % (unsigned)H);
         const unsigned nc = row / (unsigned)H;
         const float* base = cols + (int64_t)nc * KH * KW * P;
+        // only taps congruent to h + pad (w + pad) modulo the stride reach
+        // (h, w): walk them in ascending order (the gather order of the
+        // reference) with the output coordinate stepping down by one
         float s[Q];
+        int kw0[Q], ox0[Q];
 #pragma unroll
-        for (int u = 0; u < Q; ++u) s[u] = 0.f;
-        for (int kh = 0; kh < KH; ++kh) {
-            const int ry = h + pad - kh;
-            if (ry < 0 || ry % stride != 0) continue;
-            const int oy = ry / stride;
+        for (int u = 0; u < Q; ++u) {
+            s[u] = 0.f;
+            kw0[u] = (w0 + u + pad) % stride;
+            ox0[u] = (w0 + u + pad - kw0[u]) / stride;
+        }
+        const int kh0 = (h + pad) % stride;
+        int oy = (h + pad - kh0) / stride;
+        for (int kh = kh0; kh < KH && oy >= 0; kh += stride, --oy) {
             if (oy >= OH) continue;
-            for (int kw = 0; kw < KW; ++kw) {
-                const float* plane = base + (int64_t)(kh * KW + kw) * P + oy * OW;
+            const float* rowp = base + (int64_t)kh * KW * P + (int64_t)oy * OW;
 #pragma unroll
-                for (int u = 0; u < Q; ++u) {
-                    const int rx = w0 + u + pad - kw;
-                    if (rx < 0 || rx % stride != 0) continue;
-                    const int ox = rx / stride;
-                    if (ox < OW) s[u] += __ldg(plane + ox);
-                }
+            for (int u = 0; u < Q; ++u) {
+                int ox = ox0[u];
+                for (int kw = kw0[u]; kw < KW && ox >= 0; kw += stride, --ox)
+                    if (ox < OW) s[u] += __ldg(rowp + (int64_t)kw * P + ox);
             }
         }
         float* dst = x + (int64_t)i * Q;

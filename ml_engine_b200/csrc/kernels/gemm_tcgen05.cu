@@ -1036,7 +1036,7 @@ void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model
         int bn;
         bool pr;
     };
-    const Cand cands[] = {{256, false}, {128, false}, {64, false}, {256, true}};
+    const Cand cands[] = {{256, false}, {128, false}, {64, false}, {256, true}, {128, true}, {64, true}};
     for (const Cand& c : cands) {
         if (c.pr && !pair) continue;
         if (only_pairs && pair && !c.pr) continue;
@@ -1182,10 +1182,18 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
 int dispatch(const tc::GemmGroup& grp, bool A_MN, bool B_MN, int BN, cudaStream_t st, bool pair = false) {
     using namespace tc;
 #define MLE_TC(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST>(grp, st)
-#define MLE_TC2(AM, BMN) return launch_tc<AM, BMN, 256, 6, true>(grp, st)
-    if (pair) {  // 256 x 256 tiles on CTA pairs
-        if (A_MN) { if (B_MN) MLE_TC2(true, true); else MLE_TC2(true, false); }
-        else { if (B_MN) MLE_TC2(false, true); else MLE_TC2(false, false); }
+#define MLE_TC2(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST, true>(grp, st)
+    if (pair) {  // 256 x BN tiles on CTA pairs, each CTA staging BN/2 columns of B
+        if (BN == 256) {
+            if (A_MN) { if (B_MN) MLE_TC2(true, true, 256, 6); else MLE_TC2(true, false, 256, 6); }
+            else { if (B_MN) MLE_TC2(false, true, 256, 6); else MLE_TC2(false, false, 256, 6); }
+        } else if (BN == 128) {
+            if (A_MN) { if (B_MN) MLE_TC2(true, true, 128, 7); else MLE_TC2(true, false, 128, 7); }
+            else { if (B_MN) MLE_TC2(false, true, 128, 7); else MLE_TC2(false, false, 128, 7); }
+        } else {
+            if (A_MN) { if (B_MN) MLE_TC2(true, true, 64, 8); else MLE_TC2(true, false, 64, 8); }
+            else { if (B_MN) MLE_TC2(false, true, 64, 8); else MLE_TC2(false, false, 64, 8); }
+        }
     }
 #undef MLE_TC2
     if (BN == 256) {
@@ -1306,7 +1314,8 @@ static bool run_conv_gemm_swapped(const ConvGemm& c, cudaStream_t st, int& statu
     q.alpha = 1.f;
     q.mode = c.accumulate ? EPI_ACCUM : EPI_ASSIGN;
     int BN, splits;
-    choose_tiles(&q, 1, BN, splits, true);
+    bool pair = false;
+    choose_tiles(&q, 1, BN, splits, true, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
     const int kb_total = taps * cblk;
     const int kb_per_split = (kb_total + splits - 1) / splits;
     splits = (kb_total + kb_per_split - 1) / kb_per_split;
@@ -1324,7 +1333,7 @@ static bool run_conv_gemm_swapped(const ConvGemm& c, cudaStream_t st, int& statu
     ep.channels = 1;
     ep.splits = splits;
     ep.kb_per_split = kb_per_split;
-    ep.m_tiles = (c.P + BM - 1) / BM;
+    ep.m_tiles = (c.P + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
     ep.n_tiles = (c.M + BN - 1) / BN;
     ep.mode = splits > 1 ? EPI_ATOMIC : (c.accumulate ? EPI_ACCUM : EPI_ASSIGN);
     ep.conv = 3;
@@ -1342,7 +1351,7 @@ static bool run_conv_gemm_swapped(const ConvGemm& c, cudaStream_t st, int& statu
     const int s_box[4] = {32, BK, 1, 1};
     const int64_t w_dims[4] = {c.lda, c.M, taps, 1};
     const int64_t w_str[3] = {c.lda, (int64_t)c.M * c.lda, (int64_t)taps * c.M * c.lda};
-    const int w_box[4] = {BK, BN, 1, 1};
+    const int w_box[4] = {BK, pair ? BN / 2 : BN, 1, 1};
     const int64_t c_dims[4] = {c.P, c.M, 1, c.nb};
     const int64_t c_str[3] = {c.P, (int64_t)c.M * c.P, (int64_t)c.M * c.P};
     const int c_box[4] = {32, 32, 1, 1};
@@ -1362,7 +1371,7 @@ static bool run_conv_gemm_swapped(const ConvGemm& c, cudaStream_t st, int& statu
     grp.n = 1;
     grp.tile_start[0] = 0;
     grp.tile_start[1] = ep.tiles;
-    status = dispatch(grp, true, false, BN, st);
+    status = dispatch(grp, true, false, BN, st, pair);
     return true;
 }
 
@@ -1398,7 +1407,8 @@ int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
         q.mode = EPI_ACCUM;
     }
     int BN, splits;
-    choose_tiles(&q, 1, BN, splits);
+    bool pair = false;
+    choose_tiles(&q, 1, BN, splits, false, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
     const int kb_total = (q.K + BK - 1) / BK;
     const int kb_per_split = (kb_total + splits - 1) / splits;
     splits = (kb_total + kb_per_split - 1) / kb_per_split;
@@ -1413,7 +1423,7 @@ int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
     ep.channels = 1;
     ep.splits = splits;
     ep.kb_per_split = kb_per_split;
-    ep.m_tiles = (c.M + BM - 1) / BM;
+    ep.m_tiles = (c.M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
     ep.conv = c.kind;
     ep.cv_kw = c.KW;
     ep.cv_pad = c.pad;
@@ -1453,7 +1463,7 @@ int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
         const int64_t a_dims[4] = {c.P, c.M, 1, c.nb};
         const int64_t a_str[3] = {c.P, (int64_t)c.M * c.P, (int64_t)c.M * c.P};
         const int a_box[4] = {BK, BM, 1, 1};
-        const int s_box[4] = {32, BN, 1, 1};
+        const int s_box[4] = {32, pair ? BN / 2 : BN, 1, 1};
         if (!encode_map(&grp.a[0], c.A, a_dims, a_str, a_box, CU_TENSOR_MAP_SWIZZLE_128B) ||
             !encode_map(&grp.b[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B))
             return MLE_ERR_ARG;
@@ -1469,7 +1479,7 @@ int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
     grp.tile_start[0] = 0;
     grp.tile_start[1] = ep.tiles;
     if (ep.tiles == 0) return MLE_OK;
-    const int s = dispatch(grp, false, c.kind == 1, BN, st);
+    const int s = dispatch(grp, false, c.kind == 1, BN, st, pair);
     if (s || c.kind != 1 || !c.bias) return s;
     // the bias runs along the tile rows here: a separate pass
     return mle_channel_bias_fwd(c.out, c.bias, c.out, c.nb, c.M, c.P, st);

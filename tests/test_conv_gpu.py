@@ -40,14 +40,19 @@ def H(t):
     return t.cpu().numpy()
 
 
-@pytest.fixture(params=[0, 1], ids=["tf32", "fp32"])
+@pytest.fixture(params=[(0, 1), (0, 2), (1, 1)], ids=["tf32", "tf32-pairs", "fp32"])
 def gemm_mode(request):
+    """GEMM mode and CTA-pair setting: the tile model's choice, or every
+    tensor-core product forced onto CTA pairs (256-row tiles)."""
     from ml_engine_b200._lib import kernels
     k = kernels()
-    old = k.mle_get_gemm_mode()
-    k.mle_set_gemm_mode(request.param)
-    yield request.param
+    old, old_pairs = k.mle_get_gemm_mode(), k.mle_get_gemm_pairs()
+    mode, pairs = request.param
+    k.mle_set_gemm_mode(mode)
+    k.mle_set_gemm_pairs(pairs)
+    yield mode
     k.mle_set_gemm_mode(old)
+    k.mle_set_gemm_pairs(old_pairs)
 
 
 @pytest.mark.parametrize("case", CONV)

@@ -332,18 +332,19 @@ def test_gemm_tf32(cuda, ops, orc, rng, M, N, K, ta, tb, beta):
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("beta", [0.0, 1.0])
-def test_gemm_cta_pairs(cuda, ops, rng, ta, tb, beta):
-    """Products large enough for 256 x 256 tiles on CTA pairs (cta_group::2
-    MMAs), with ragged edges in M, N and K, against float64 products."""
+@pytest.mark.parametrize("M,N,K,mode", [(4000, 2000, 520, 1), (1000, 100, 300, 2), (700, 200, 96, 2)])
+def test_gemm_cta_pairs(cuda, ops, rng, ta, tb, beta, M, N, K, mode):
+    """Products on CTA pairs (cta_group::2 MMAs, 256-row tiles) with ragged
+    edges in M, N and K, against float64 products: chosen by the tile model
+    for the large one, forced (mode 2) for 64- and 128-wide pair tiles."""
     from ml_engine_b200._lib import kernels
-    M, N, K = 4000, 2000, 520
     A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
     B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
     C0 = rng.standard_normal((M, N)).astype(np.float32)
     C = T(C0, cuda)
     k = kernels()
     old = k.mle_get_gemm_pairs()
-    k.mle_set_gemm_pairs(1)
+    k.mle_set_gemm_pairs(mode)
     try:
         ops.gemm(T(A, cuda), T(B, cuda), C, M, N, K, ta, tb, alpha=0.5, beta=beta)
         got = H(C)
