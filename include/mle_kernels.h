@@ -294,6 +294,14 @@ int mle_get_gemm_mode(void);
  * reference. */
 int mle_set_gemm_pairs(int enable);
 int mle_get_gemm_pairs(void);
+/* Element type of the tensor-core GEMM's operand loads: 0 fp32 (the MMA
+ * uses the TF32 part of each value: its low 13 mantissa bits are dropped),
+ * 1 (default) TF32 (tensor maps of TF32 element type: the copy engine
+ * rounds each fp32 value to the nearest TF32, ties to even, as it lands in
+ * shared memory).  Outputs and accumulation are fp32 either way.  Per host
+ * thread; no counterpart in the reference. */
+int mle_set_gemm_operand_rounding(int mode);
+int mle_get_gemm_operand_rounding(void);
 /* out3 = {tile width, split-K count, 1 if CTA pairs} of this thread's last
  * single tensor-core product (diagnostics for tests and benchmarks). */
 int mle_gemm_last_choice(int* out3);

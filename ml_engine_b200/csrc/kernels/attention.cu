@@ -24,8 +24,9 @@
 // mle_set_attention_path): the two forward and four backward products run
 // on the tcgen05 GEMM, which reads Q, K, V, dO and writes O, dQ, dK, dV in
 // either layout through strides, P and the score gradients [B,H,Sq,Sk] in
-// between; the column softmax and its backward are multi-pass column-block
-// kernels (max, sum, update; dot, update) with 16-byte accesses.  The reference's key gradient (memory of
+// between; the column softmax and its backward read each 32-column slab of
+// a matrix once into registers (columns up to 512 rows; longer ones take
+// multi-pass column-block kernels), 16-byte accesses.  The reference's key gradient (memory of
 // dScores read as [Sk,Sq], result laid out [hd,Sk] in the head's block) is
 // one GEMM whose output columns are split over rows of the head block.
 //
@@ -544,7 +545,8 @@ thread_local int g_attn_path = MLE_ATTN_PATH_AUTO;
 
 // Column softmax of each [rows, cols] matrix in place (the reference's type
 // 1, causal entries key > query zeroed after the max over the whole column,
-// as SoftMask does).  A 256-thread block owns (matrix, 128 columns): lane l
+// as SoftMask does), the form for columns of more than 512 rows (the
+// single-pass register kernels below take the rest).  A 256-thread block owns (matrix, 128 columns): lane l
 // holds columns 4l..4l+3 (16-byte accesses), warp w the rows w, w + 8, ...
 // Three passes over the block's rows, the later two served by L2: the
 // column max, the sum of the exponentials, the probabilities; the 8 warps'
@@ -662,15 +664,169 @@ __global__ void __launch_bounds__(kSmThreads) col_softmax_bwd_vec(const float* _
     }
 }
 
+// Single-pass forms for columns of at most 512 rows: a block of 8 * RG
+// threads owns (matrix, 32 columns); lane l = tid % 8 holds columns
+// 4l..4l+3, row group g = tid / 8 the rows g, g + RG, ... (RPT of them), all
+// in registers, so every element is read once and written once.  Each warp
+// load covers four full 128-byte rows.  The column partials merge across
+// the warp's four row groups with shuffles, then across warps in shared
+// memory.
+__device__ __forceinline__ float4 max4(float4 a, float4 b) {
+    return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
+}
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+    return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+__device__ __forceinline__ float4 shfl_xor4(float4 v, int m) {
+    return make_float4(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m),
+                       __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
+}
+
+template <int RG, int RPT>
+__global__ void __launch_bounds__(8 * RG) col_softmax_reg(float* __restrict__ P, int rows, int cols, int causal,
+                                                          int mats) {
+    pdl_entry();
+    constexpr int kWarps = RG / 4;
+    __shared__ float4 red[kWarps][8];
+    const int l = threadIdx.x & 7, g = threadIdx.x >> 3, warp = threadIdx.x >> 5;
+    const int c0 = blockIdx.x * 32 + l * 4;
+    const bool live = c0 < cols;
+    for (int mat = blockIdx.y; mat < mats; mat += gridDim.y) {
+        float* Pm = P + (int64_t)mat * rows * cols + c0;
+        float4 v[RPT];
+        float4 m = make_float4(-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX);
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const int r = g + i * RG;
+            if (live && r < rows) {
+                v[i] = *reinterpret_cast<const float4*>(Pm + (int64_t)r * cols);
+                m = max4(m, v[i]);
+            }
+        }
+        m = max4(m, shfl_xor4(m, 8));
+        m = max4(m, shfl_xor4(m, 16));
+        if ((threadIdx.x & 31) < 8) red[warp][l] = m;
+        __syncthreads();
+        m = red[0][l];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) m = max4(m, red[w][l]);
+        __syncthreads();
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const int r = g + i * RG;
+            if (live && r < rows) {
+                float4 e;
+                e.x = (causal && c0 + 0 > r) ? 0.f : expf(v[i].x - m.x);
+                e.y = (causal && c0 + 1 > r) ? 0.f : expf(v[i].y - m.y);
+                e.z = (causal && c0 + 2 > r) ? 0.f : expf(v[i].z - m.z);
+                e.w = (causal && c0 + 3 > r) ? 0.f : expf(v[i].w - m.w);
+                v[i] = e;
+                s = add4(s, e);
+            }
+        }
+        s = add4(s, shfl_xor4(s, 8));
+        s = add4(s, shfl_xor4(s, 16));
+        if ((threadIdx.x & 31) < 8) red[warp][l] = s;
+        __syncthreads();
+        s = red[0][l];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) s = add4(s, red[w][l]);
+        __syncthreads();
+        const float4 inv = make_float4(1.0f / (s.x < 1e-45f ? 1.0f : s.x), 1.0f / (s.y < 1e-45f ? 1.0f : s.y),
+                                       1.0f / (s.z < 1e-45f ? 1.0f : s.z), 1.0f / (s.w < 1e-45f ? 1.0f : s.w));
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const int r = g + i * RG;
+            if (live && r < rows)
+                *reinterpret_cast<float4*>(Pm + (int64_t)r * cols) =
+                    make_float4(v[i].x * inv.x, v[i].y * inv.y, v[i].z * inv.z, v[i].w * inv.w);
+        }
+    }
+}
+
+template <int RG, int RPT>
+__global__ void __launch_bounds__(8 * RG) col_softmax_bwd_reg(const float* __restrict__ P, float* __restrict__ G,
+                                                              int rows, int cols, int mats) {
+    pdl_entry();
+    constexpr int kWarps = RG / 4;
+    __shared__ float4 red[kWarps][8];
+    const int l = threadIdx.x & 7, g = threadIdx.x >> 3, warp = threadIdx.x >> 5;
+    const int c0 = blockIdx.x * 32 + l * 4;
+    const bool live = c0 < cols;
+    for (int mat = blockIdx.y; mat < mats; mat += gridDim.y) {
+        const float* Pm = P + (int64_t)mat * rows * cols + c0;
+        float* Gm = G + (int64_t)mat * rows * cols + c0;
+        float4 p[RPT], q[RPT];
+        float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const int r = g + i * RG;
+            if (live && r < rows) {
+                p[i] = *reinterpret_cast<const float4*>(Pm + (int64_t)r * cols);
+                q[i] = *reinterpret_cast<const float4*>(Gm + (int64_t)r * cols);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const int r = g + i * RG;
+            if (live && r < rows)
+                d = make_float4(d.x + p[i].x * q[i].x, d.y + p[i].y * q[i].y, d.z + p[i].z * q[i].z,
+                                d.w + p[i].w * q[i].w);
+        }
+        d = add4(d, shfl_xor4(d, 8));
+        d = add4(d, shfl_xor4(d, 16));
+        if ((threadIdx.x & 31) < 8) red[warp][l] = d;
+        __syncthreads();
+        d = red[0][l];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) d = add4(d, red[w][l]);
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const int r = g + i * RG;
+            if (live && r < rows)
+                *reinterpret_cast<float4*>(Gm + (int64_t)r * cols) =
+                    make_float4(p[i].x * (q[i].x - d.x), p[i].y * (q[i].y - d.y), p[i].z * (q[i].z - d.z),
+                                p[i].w * (q[i].w - d.w));
+        }
+    }
+}
+
+// Calls f(std::integral_constant<int, RG>, std::integral_constant<int, RPT>)
+// for the single-pass shape covering `rows`; false above 512 rows.
+template <typename F>
+bool col_shape(int rows, F&& f) {
+    using std::integral_constant;
+    if (rows <= 32) return f(integral_constant<int, 32>(), integral_constant<int, 1>()), true;
+    if (rows <= 64) return f(integral_constant<int, 32>(), integral_constant<int, 2>()), true;
+    if (rows <= 128) return f(integral_constant<int, 32>(), integral_constant<int, 4>()), true;
+    if (rows <= 256) return f(integral_constant<int, 32>(), integral_constant<int, 8>()), true;
+    if (rows <= 512) return f(integral_constant<int, 64>(), integral_constant<int, 8>()), true;
+    return false;
+}
+
 int tc_col_softmax(float* P, int64_t mats, int rows, int cols, int causal, cudaStream_t st) {
-    const dim3 grid((unsigned)((cols + 127) / 128), (unsigned)std::min<int64_t>(mats, 65535));
-    launch_k(col_softmax_vec, grid, kSmThreads, 0, st, P, rows, cols, causal, (int)mats);
+    const unsigned gy = (unsigned)std::min<int64_t>(mats, 65535);
+    const bool single = col_shape(rows, [&](auto rg, auto rpt) {
+        launch_k(col_softmax_reg<decltype(rg)::value, decltype(rpt)::value>, dim3((unsigned)((cols + 31) / 32), gy),
+                 8 * decltype(rg)::value, 0, st, P, rows, cols, causal, (int)mats);
+    });
+    if (!single)
+        launch_k(col_softmax_vec, dim3((unsigned)((cols + 127) / 128), gy), kSmThreads, 0, st, P, rows, cols, causal,
+                 (int)mats);
     return launch_status();
 }
 
 int tc_col_softmax_bwd(const float* P, float* G, int64_t mats, int rows, int cols, cudaStream_t st) {
-    const dim3 grid((unsigned)((cols + 127) / 128), (unsigned)std::min<int64_t>(mats, 65535));
-    launch_k(col_softmax_bwd_vec, grid, kSmThreads, 0, st, P, G, rows, cols, (int)mats);
+    const unsigned gy = (unsigned)std::min<int64_t>(mats, 65535);
+    const bool single = col_shape(rows, [&](auto rg, auto rpt) {
+        launch_k(col_softmax_bwd_reg<decltype(rg)::value, decltype(rpt)::value>,
+                 dim3((unsigned)((cols + 31) / 32), gy), 8 * decltype(rg)::value, 0, st, P, G, rows, cols, (int)mats);
+    });
+    if (!single)
+        launch_k(col_softmax_bwd_vec, dim3((unsigned)((cols + 127) / 128), gy), kSmThreads, 0, st, P, G, rows, cols,
+                 (int)mats);
     return launch_status();
 }
 

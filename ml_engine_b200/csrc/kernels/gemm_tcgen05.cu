@@ -840,7 +840,7 @@ struct OperandView {
 // K-major tiles use the 16-byte-atom 128-byte swizzle; MN-major tiles the
 // 32-byte-atom one, matching the UMMA layout types above.
 static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner, int box_outer,
-                           bool mn_major = false) {
+                           bool mn_major = false, CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return false;
     cuuint64_t dims[4] = {(cuuint64_t)v.inner, (cuuint64_t)v.outer, (cuuint64_t)v.nc, (cuuint64_t)v.nb};
@@ -851,7 +851,7 @@ static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner
     cuuint64_t strides[3] = {(cuuint64_t)(v.ld * 4), (cuuint64_t)(sc * 4), (cuuint64_t)(sb * 4)};
     cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(v.base), dims, strides, box, estr,
+    CUresult r = enc(map, dt, 4, const_cast<float*>(v.base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE,
                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -861,7 +861,8 @@ static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner
 // fp32 tensor map of `rank` (4 or 5) dims with explicit extents, element
 // strides of dims 1.. and box.
 static bool encode_map(CUtensorMap* map, const float* base, const int64_t* dims, const int64_t* strides,
-                       const int* box, CUtensorMapSwizzle swizzle, int rank = 4) {
+                       const int* box, CUtensorMapSwizzle swizzle, int rank = 4,
+                       CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32) {
     EncodeTiledFn enc = get_encode();
     if (!enc || rank < 1 || rank > 5) return false;
     cuuint64_t d[5], st[4];
@@ -871,7 +872,7 @@ static bool encode_map(CUtensorMap* map, const float* base, const int64_t* dims,
         b[i] = (cuuint32_t)box[i];
     }
     for (int i = 0; i + 1 < rank; ++i) st[i] = (cuuint64_t)(strides[i] * 4);
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<float*>(base), d, st, b, e,
+    return enc(map, dt, (cuuint32_t)rank, const_cast<float*>(base), d, st, b, e,
                CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -958,6 +959,16 @@ static thread_local int g_gemm_pairs = 1;
 static thread_local int g_store_path = 1;
 // tile width, split count and pair flag of this thread's last tensor-core launch
 static thread_local int g_last_choice[3] = {0, 0, 0};
+// Element type of the operand tensor maps: 0 fp32 (the MMA reads the TF32
+// part of each value: the low 13 mantissa bits are dropped, a truncation),
+// 1 TF32 (the copy engine rounds each fp32 value to the nearest TF32, ties
+// to even, as it loads; measured on B200).  Rounding halves the typical
+// product error at no cost, so it is the default.
+static thread_local int g_operand_round = 1;
+
+static CUtensorMapDataType operand_type() {
+    return g_operand_round ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+}
 
 namespace {
 
@@ -1133,8 +1144,8 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
     memset(&grp.a[g], 0, sizeof(CUtensorMap));
     memset(&grp.b[g], 0, sizeof(CUtensorMap));
     memset(&grp.c[g], 0, sizeof(CUtensorMap));
-    if (!encode_operand(&grp.a[g], va, 32, sh.A_MN ? BK : BM, sh.A_MN)) return MLE_OK;
-    if (!encode_operand(&grp.b[g], vb, 32, sh.B_MN ? BK : bn_cta, sh.B_MN)) return MLE_OK;
+    if (!encode_operand(&grp.a[g], va, 32, sh.A_MN ? BK : BM, sh.A_MN, operand_type())) return MLE_OK;
+    if (!encode_operand(&grp.b[g], vb, 32, sh.B_MN ? BK : bn_cta, sh.B_MN, operand_type())) return MLE_OK;
     // C through bulk tensor stores when its rows and strides allow TMA
     ep.c_has_b = (ep.c_stride_b != 0);
     ep.c_has_c = (ep.c_stride_c != 0);
@@ -1355,8 +1366,8 @@ static bool run_conv_gemm_swapped(const ConvGemm& c, cudaStream_t st, int& statu
     const int64_t c_dims[4] = {c.P, c.M, 1, c.nb};
     const int64_t c_str[3] = {c.P, (int64_t)c.M * c.P, (int64_t)c.M * c.P};
     const int c_box[4] = {32, 32, 1, 1};
-    if (!encode_map(&grp.a[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
-        !encode_map(&grp.b[0], c.A, w_dims, w_str, w_box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+    if (!encode_map(&grp.a[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, 4, operand_type()) ||
+        !encode_map(&grp.b[0], c.A, w_dims, w_str, w_box, CU_TENSOR_MAP_SWIZZLE_128B, 4, operand_type()) ||
         !encode_map(&grp.c[0], c.out, c_dims, c_str, c_box, CU_TENSOR_MAP_SWIZZLE_128B))
         return false;
     ep.tma_epi = 1;
@@ -1444,8 +1455,9 @@ int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
         const int64_t a_str[3] = {c.lda, (int64_t)c.M * c.lda, (int64_t)taps * c.M * c.lda};
         const int a_box[4] = {BK, BM, 1, 1};
         const int s_box[4] = {32, BK, 1, 1};
-        if (!encode_map(&grp.a[0], c.A, a_dims, a_str, a_box, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !encode_map(&grp.b[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+        if (!encode_map(&grp.a[0], c.A, a_dims, a_str, a_box, CU_TENSOR_MAP_SWIZZLE_128B, 4, operand_type()) ||
+            !encode_map(&grp.b[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, 4,
+                        operand_type()))
             return MLE_ERR_ARG;
         const int64_t c_dims[4] = {c.P, c.M, 1, c.nb};
         const int64_t c_str[3] = {c.P, (int64_t)c.M * c.P, (int64_t)c.M * c.P};
@@ -1464,8 +1476,8 @@ int run_conv_gemm(const ConvGemm& c, cudaStream_t st) {
         const int64_t a_str[3] = {c.P, (int64_t)c.M * c.P, (int64_t)c.M * c.P};
         const int a_box[4] = {BK, BM, 1, 1};
         const int s_box[4] = {32, pair ? BN / 2 : BN, 1, 1};
-        if (!encode_map(&grp.a[0], c.A, a_dims, a_str, a_box, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !encode_map(&grp.b[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B))
+        if (!encode_map(&grp.a[0], c.A, a_dims, a_str, a_box, CU_TENSOR_MAP_SWIZZLE_128B, 4, operand_type()) ||
+            !encode_map(&grp.b[0], c.S, s_dims, s_str, s_box, CU_TENSOR_MAP_SWIZZLE_128B, 4, operand_type()))
             return MLE_ERR_ARG;
         const int64_t c_dims[4] = {c.C, c.M, taps, 1};
         const int64_t c_str[3] = {c.ldc, (int64_t)c.M * c.ldc, (int64_t)taps * c.M * c.ldc};
@@ -1512,6 +1524,14 @@ int mle_set_gemm_store_path(int path) {
     g_store_path = path;
     return MLE_OK;
 }
+
+int mle_set_gemm_operand_rounding(int mode) {
+    if (mode != 0 && mode != 1) return MLE_ERR_ARG;
+    g_operand_round = mode;
+    return MLE_OK;
+}
+
+int mle_get_gemm_operand_rounding(void) { return g_operand_round; }
 
 int mle_gemm_last_choice(int* out3) {
     if (!out3) return MLE_ERR_ARG;

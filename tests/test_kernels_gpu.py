@@ -361,6 +361,41 @@ def test_gemm_cta_pairs(cuda, ops, rng, ta, tb, beta, M, N, K, mode):
     assert err <= RTOL_TC, err
 
 
+def _tf32(x, mode):
+    """fp32 -> TF32 (low 13 mantissa bits cleared): 'trunc' or nearest-even."""
+    b = x.astype(np.float32).view(np.uint32).astype(np.uint64)
+    if mode == "rne":
+        b = b + 0xFFF + ((b >> 13) & 1)
+    return (b & 0xFFFFE000).astype(np.uint32).view(np.float32)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 1)])
+@pytest.mark.parametrize("mode,emul", [(0, "trunc"), (1, "rne")])
+def test_gemm_operand_rounding(cuda, ops, rng, ta, tb, mode, emul):
+    """Operand loads of fp32 type leave the tensor core to drop the low 13
+    mantissa bits; TF32-typed tensor maps round to nearest, ties to even
+    (row 0 of A holds exact ties).  The product then equals the float64
+    product of the converted operands up to fp32 accumulation."""
+    from ml_engine_b200._lib import kernels
+    M, N, K = 256, 256, 512
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    A[0, :64] = (A[0, :64].view(np.uint32) & np.uint32(0xFFFFE000) | np.uint32(0x1000)).view(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    C = torch.zeros(M, N, device=cuda)
+    k = kernels()
+    old = k.mle_get_gemm_operand_rounding()
+    k.call("mle_set_gemm_operand_rounding", mode)
+    try:
+        ops.gemm(T(np.ascontiguousarray(A.T) if ta else A, cuda), T(np.ascontiguousarray(B.T) if tb else B, cuda),
+                 C, M, N, K, ta, tb)
+        got = H(C).astype(np.float64)
+    finally:
+        k.call("mle_set_gemm_operand_rounding", old)
+    ref = _tf32(A, emul).astype(np.float64) @ _tf32(B, emul).astype(np.float64)
+    assert np.max(np.abs(got - ref)) / np.max(np.abs(ref)) <= 2e-5
+    assert np.max(np.abs(got[0] - ref[0])) / np.max(np.abs(ref[0])) <= 2e-5
+
+
 def test_gemm_fallback_exact(cuda, ops, orc, rng):
     """N = 10 (MNIST logits) has a 40-byte row stride: CUDA-core path, fp32."""
     M, N, K = 64, 10, 256
@@ -451,6 +486,8 @@ ATTN_CASES = [  # B, H, Sq, Sk, hd, axis, causal
     (1, 2, 40, 72, 16, 1, 0),     # Sq != Sk: the reference key gradient needs the composed path
     (2, 3, 37, 37, 32, 1, 1),     # ragged row and key blocks, masked: CUDA-core kernels only
     (1, 2, 40, 72, 16, 0, 0),     # row-wise softmax: composed (tensor cores)
+    (1, 2, 272, 64, 32, 1, 1),    # tensor path: single-pass column softmax of 512-thread blocks, ragged rows
+    (1, 1, 544, 64, 16, 1, 0),    # tensor path: columns over 512 rows take the multi-pass kernels
 ]
 
 
