@@ -569,6 +569,8 @@ def main():
                     help="run large products on CTA pairs (mle_set_gemm_pairs); default: the library's")
     ap.add_argument("--attn-path", default=None, choices=["auto", "fused", "tensor"],
                     help="attention implementation (mle_set_attention_path); default: the library's")
+    ap.add_argument("--param-stream", type=int, default=None, choices=[0, 1],
+                    help="weight/bias gradients on a second stream (mle_set_param_grad_stream); default: on")
     ap.add_argument("--roofline-only", action="store_true",
                     help="run only the roofline kernel pair (3 untimed + 20 timed pairs)")
     args = ap.parse_args()
@@ -578,6 +580,9 @@ def main():
     if args.attn_path is not None:
         from ml_engine_b200._lib import kernels
         kernels().call("mle_set_attention_path", {"auto": 0, "fused": 1, "tensor": 2}[args.attn_path])
+    if args.param_stream is not None:
+        from ml_engine_b200._lib import engine
+        engine().call("mle_set_param_grad_stream", args.param_stream)
     if args.sweep:
         run_sweep(args)
         return

@@ -91,6 +91,15 @@ int mle_session_phase(mle_session_t s, int phase);
  * mle_session_step calls replay the one matching `upload`. */
 int mle_session_capture(mle_session_t s);
 
+/* Whether backward puts the Linear layers' weight and bias gradients on a
+ * second stream (forked from the compute stream where the layer's output
+ * gradient is complete, joined back at the end of the backward), so they
+ * run concurrently with the input-gradient chain.  1 (default) on, 0 all on
+ * the compute stream.  Process-wide; takes effect for steps issued (or
+ * captured) afterwards. */
+int mle_set_param_grad_stream(int enable);
+int mle_get_param_grad_stream(void);
+
 /* Kernel, memset and memcpy nodes of the captured device-resident step
  * (the launches one replay issues). */
 int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* copies);

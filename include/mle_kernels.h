@@ -339,7 +339,10 @@ int mle_linear_fwd(const float* X, const float* W, const float* bias, float* Y, 
                    int in_features, int out_features, mle_stream_t stream);
 
 /* Linear layer backward: dX += dY*W^T (if dX != NULL), dW += X^T*dY as one
- * GEMM with K = rows, dB += column sums of dY (if dB != NULL).  Replaces
+ * GEMM with K = rows (if dW != NULL), dB += column sums of dY (if dB !=
+ * NULL); X is read only for dW.  The parts may run on different streams as
+ * separate calls (input gradient on one, parameter gradients on another).
+ * Replaces
  * bcmmABT + bcmmATB + BCompress of the Linear backward lambda
  * (Engine/engine.cu:3550-3563) without its two device synchronisations. */
 int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, float* dW,
@@ -355,7 +358,8 @@ int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, f
  *   forward : Y_i = X W_i (+ b_i) (assigned), W_i [in, out_i];
  *   backward: dX += sum_i dY_i W_i^T (one launch, reduce-added), dW_i +=
  *             X^T dY_i (one launch), dB_i += column sums of dY_i;
- *             dX, bias and dB (or any dB[i]) may be NULL.
+ *             dX, dW (all weight gradients skipped), bias and dB (or any
+ *             dB[i]) may be NULL.
  * Pointer arrays are HOST arrays of n device pointers. */
 int mle_linear_group_fwd(const float* X, const float* const* W, const float* const* bias, float* const* Y,
                          int n, int64_t rows, int in_features, const int* out_features,
@@ -474,7 +478,9 @@ int mle_swap_dims(const float* in, float* out, int a, int b, int c, int mode, ml
  *   backward: dw = sum over the batch (assigned, GV2D :1021-1051), db +=
  *             channel sums (Channel_Squeeze1D :1734-1761), dx += (CV2D_GradInput
  *             :1053-1089); x is the forward's input; any of dx, dw, db may be
- *             NULL; ws is consumed. */
+ *             NULL.  The dx part and the dw/db part touch disjoint regions of
+ *             ws, so they may be issued as two calls on two streams (each
+ *             after the forward); either part may run once per forward. */
 int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad,
                                     int stride);
 int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y, float* ws, int batch,

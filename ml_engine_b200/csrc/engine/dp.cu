@@ -85,6 +85,7 @@ DataParallel::~DataParallel() {
     if (comm_stream_) cudaStreamSynchronize(comm_stream_);
     if (comm_ && nccl().ok) nccl().CommDestroy((ncclComm_t)comm_);
     for (cudaEvent_t e : ready_) cudaEventDestroy(e);
+    for (cudaEvent_t e : ready_param_) cudaEventDestroy(e);
     if (done_) cudaEventDestroy(done_);
     if (comm_stream_) cudaStreamDestroy(comm_stream_);
 }
@@ -110,7 +111,10 @@ int DataParallel::init(const uint8_t* id128, int rank, int world, const std::vec
     buckets_ = plan_buckets(grads, bucket_mb);
     members_.assign(buckets_.size(), 0);
     ready_.assign(buckets_.size(), nullptr);
+    ready_param_.assign(buckets_.size(), nullptr);
     for (auto& e : ready_)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return MLE_ERR_CUDA;
+    for (auto& e : ready_param_)
         if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return MLE_ERR_CUDA;
     for (auto& gr : grads) {
         if (gr.second <= 0) continue;
@@ -135,6 +139,11 @@ void DataParallel::begin_backward() {
 void DataParallel::issue(int b, cudaStream_t compute) {
     check_cuda(cudaEventRecord(ready_[b], compute), "dp bucket ready");
     check_cuda(cudaStreamWaitEvent(comm_stream_, ready_[b], 0), "dp bucket wait");
+    if (param_stream_pending()) {
+        // parameter gradients produced on the parameter-gradient stream
+        check_cuda(cudaEventRecord(ready_param_[b], param_stream()), "dp bucket ready");
+        check_cuda(cudaStreamWaitEvent(comm_stream_, ready_param_[b], 0), "dp bucket wait");
+    }
     const ncclResult_t r = nccl().AllReduce(buckets_[b].base, buckets_[b].base, (size_t)buckets_[b].count,
                                             ncclFloat32, ncclSum, (ncclComm_t)comm_, comm_stream_);
     if (r != ncclSuccess) {

@@ -27,6 +27,42 @@ cudaStream_t stream() { return g_stream; }
 void set_stream(cudaStream_t s) { g_stream = s; }
 void* st() { return (void*)g_stream; }
 
+static bool g_ps_enabled = true;
+static cudaStream_t g_ps = nullptr;
+static cudaEvent_t g_ps_fork = nullptr, g_ps_join = nullptr;
+static bool g_ps_pending = false;
+
+void init_param_stream() {
+    if (g_ps) return;
+    check_cuda(cudaStreamCreateWithFlags(&g_ps, cudaStreamNonBlocking), "param stream");
+    check_cuda(cudaEventCreateWithFlags(&g_ps_fork, cudaEventDisableTiming), "param stream");
+    check_cuda(cudaEventCreateWithFlags(&g_ps_join, cudaEventDisableTiming), "param stream");
+}
+
+cudaStream_t fork_param_stream() {
+    if (!g_ps_enabled) return g_stream;
+    init_param_stream();
+    check_cuda(cudaEventRecord(g_ps_fork, g_stream), "param stream fork");
+    check_cuda(cudaStreamWaitEvent(g_ps, g_ps_fork, 0), "param stream fork");
+    g_ps_pending = true;
+    return g_ps;
+}
+
+void join_param_stream() {
+    if (!g_ps_pending) return;
+    check_cuda(cudaEventRecord(g_ps_join, g_ps), "param stream join");
+    check_cuda(cudaStreamWaitEvent(g_stream, g_ps_join, 0), "param stream join");
+    g_ps_pending = false;
+}
+
+bool param_stream_pending() { return g_ps_pending; }
+cudaStream_t param_stream() { return g_ps; }
+void set_param_stream_enabled(bool on) {
+    join_param_stream();
+    g_ps_enabled = on;
+}
+bool param_stream_enabled() { return g_ps_enabled; }
+
 void check(int status, const str& what) {
     if (status != MLE_OK) {
         std::cerr << "Runtime error in " << what << ": " << mle_status_string(status)
@@ -608,12 +644,14 @@ void GraphOperations::backward(const graph& X, const bool show, const bool time,
         }
         if (on_backward_done) on_backward_done(it->get());
         if (time) {
+            join_param_stream();
             CheckError("After " + (*it)->op_name + " backward");
             auto t1 = std::chrono::high_resolution_clock::now();
             std::cout << "Time elapsed for " << (*it)->op_name << " backward: "
                       << std::chrono::duration<double, std::milli>(t1 - t0).count() << "ms \n";
         }
     }
+    join_param_stream();
 }
 
 void GraphOperations::zero_grad(const graph& X, const bool show) {

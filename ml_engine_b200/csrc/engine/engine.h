@@ -55,6 +55,23 @@ namespace mle {
 cudaStream_t stream();
 void set_stream(cudaStream_t s);
 
+// Parameter-gradient stream.  A backward lambda may put work that only
+// parameter gradients depend on (a Linear layer's weight and bias
+// gradients) on a second stream: fork_param_stream() makes that stream wait
+// for everything issued on the compute stream so far and returns it (the
+// compute stream itself when the feature is off), so the input-gradient
+// chain goes on without waiting for those products.  GraphOperations::
+// backward joins it back before returning (join_param_stream), so callers
+// see every gradient complete on the compute stream, and a CUDA-graph
+// capture of the backward holds both branches.
+void init_param_stream();            // creates the stream (outside a capture)
+cudaStream_t fork_param_stream();
+void join_param_stream();
+bool param_stream_pending();         // forked since the last join
+cudaStream_t param_stream();         // the second stream (nullptr before init)
+void set_param_stream_enabled(bool on);
+bool param_stream_enabled();
+
 // Maps a non-zero mle_status onto the reference's behaviour: print the
 // reason and exit(1) (Engine/debug.cu:15-25).
 void check(int status, const str& what);

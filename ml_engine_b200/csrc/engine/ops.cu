@@ -693,8 +693,12 @@ graph Linear::forward(const graph& X) {
     };
     node->backward = [=]() {
         const bool fused = ext(nd).bias_grad_fused;
-        check(mle_linear_bwd(xp->output, W->output, nd->grad, xp->grad, W->grad, (Bp && !fused) ? Bp->grad : nullptr,
-                             rows, n, p, st()),
+        // dW and dB on the parameter-gradient stream, concurrent with dX
+        void* ps = (void*)fork_param_stream();
+        check(mle_linear_bwd(nullptr, W->output, nd->grad, xp->grad, nullptr, nullptr, rows, n, p, st()),
+              "MatMul... in " + nd->op_name + " backward");
+        check(mle_linear_bwd(xp->output, W->output, nd->grad, nullptr, W->grad, (Bp && !fused) ? Bp->grad : nullptr,
+                             rows, n, p, ps),
               "MatMul... in " + nd->op_name + " backward");
     };
     node->free = [nd]() { nd->clear(); };
@@ -785,10 +789,17 @@ graph Convolute2D::forward(const graph& X) {
               "Forward Convolution in " + nd->op_name);
     };
     node->backward = [=]() {
-        // dW assigned (GV2D), dB += (Channel_Squeeze1D), dX += (CV2D_GradInput)
-        check(mle_conv2d_bwd(xp->output, W->output, nd->grad, xp->grad, W->grad, B->grad, ws, batch, ci, a, b, co, kh,
-                             kw, p, s, st()),
-              "Weight + Bias + Input Gradient in " + nd->op_name);
+        // dW assigned (GV2D) and dB += (Channel_Squeeze1D) on the parameter-
+        // gradient stream, dX += (CV2D_GradInput) on the compute stream;
+        // the two parts use disjoint workspace regions
+        void* ps = (void*)fork_param_stream();
+        if (xp->grad)
+            check(mle_conv2d_bwd(xp->output, W->output, nd->grad, xp->grad, nullptr, nullptr, ws, batch, ci, a, b, co,
+                                 kh, kw, p, s, st()),
+                  "Input Gradient in " + nd->op_name);
+        check(mle_conv2d_bwd(xp->output, W->output, nd->grad, nullptr, W->grad, B->grad, ws, batch, ci, a, b, co, kh,
+                             kw, p, s, ps),
+              "Weight + Bias Gradient in " + nd->op_name);
     };
     conv_param_lambdas(node, W, B);
     return node;
@@ -908,8 +919,13 @@ std::vector<graph> GraphOperations::LinearGroup(const graph& X, const std::vecto
             done.clear();
             if (++sh->backward_seen < sh->n) return;
             sh->backward_seen = 0;
-            check(mle_linear_group_bwd(xp->output, sh->W, sh->dY, xp->grad, sh->dW, sh->dB, sh->n, rows, in, sh->out,
+            // weight and bias gradients on the parameter-gradient stream
+            void* ps = (void*)fork_param_stream();
+            check(mle_linear_group_bwd(nullptr, sh->W, sh->dY, xp->grad, nullptr, nullptr, sh->n, rows, in, sh->out,
                                        st()),
+                  "Linear group backward");
+            check(mle_linear_group_bwd(xp->output, sh->W, sh->dY, nullptr, sh->dW, sh->dB, sh->n, rows, in, sh->out,
+                                       ps),
                   "Linear group backward");
             for (int j = 0; j < sh->n; ++j) {
                 done.push_back(sh->dW[j]);

@@ -398,6 +398,7 @@ int mle_session_create(const mle_session_desc* desc, mle_session_t* out) {
         delete S;
         return MLE_ERR_CUDA;
     }
+    mle::init_param_stream();  // before any capture of the step
     mle::set_seed(d.seed);
     mle::set_keep_softmax(false);
     mle::g_loss_readback = false;
@@ -666,6 +667,14 @@ int mle_session_device_bytes(mle_session_t s, int64_t* bytes) {
 }
 
 int mle_session_node_count(mle_session_t s) { return s ? (int)as_session(s)->go.nodes.size() : -1; }
+
+int mle_set_param_grad_stream(int enable) {
+    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    mle::set_param_stream_enabled(enable != 0);
+    return MLE_OK;
+}
+
+int mle_get_param_grad_stream(void) { return mle::param_stream_enabled() ? 1 : 0; }
 
 int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* copies) {
     Session* S = as_session(s);

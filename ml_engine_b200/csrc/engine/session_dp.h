@@ -32,9 +32,10 @@ class DataParallel {
              int bucket_mb, cudaStream_t compute);
     // Backward of one step starts: every bucket waits for all its tensors.
     void begin_backward();
-    // `grads` are complete once the work queued on `compute` so far has run:
-    // each bucket whose last tensor this was is summed over the ranks on the
-    // comm stream, overlapping the rest of the backward.
+    // `grads` are complete once the work queued on `compute` (and on the
+    // parameter-gradient stream, when forked) so far has run: each bucket
+    // whose last tensor this was is summed over the ranks on the comm
+    // stream, overlapping the rest of the backward.
     void grads_done(const std::vector<float*>& grads, cudaStream_t compute);
     // Sums the buckets not started yet and makes `compute` wait for every
     // reduction (before clip and update).
@@ -48,7 +49,7 @@ class DataParallel {
     std::vector<GradBucket> buckets_;
     std::vector<int> members_, pending_;
     std::vector<char> issued_;
-    std::vector<cudaEvent_t> ready_;
+    std::vector<cudaEvent_t> ready_, ready_param_;
     std::vector<std::pair<float*, int>> bucket_of_;  // grad pointer -> bucket, sorted
     void* comm_ = nullptr;
     cudaStream_t comm_stream_ = nullptr;

@@ -399,8 +399,10 @@ int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int cout, 
     const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
     if (batch <= 0 || cin <= 0 || cout <= 0 || kh <= 0 || kw <= 0 || oh <= 0 || ow <= 0) return -1;
     // room for either path: the choice also depends on the GEMM mode and
-    // pointer alignment at call time
-    int64_t n = (int64_t)batch * cin * kh * kw * oh * ow;
+    // pointer alignment at call time.  The column path keeps the forward's
+    // columns (read by dW) and the input gradient's columns apart, so the
+    // dx and dw/db parts of the backward may run concurrently.
+    int64_t n = 2 * (int64_t)batch * cin * kh * kw * oh * ow;
     if (stride == 1) n = std::max(n, conv_plan(batch, cin, h, w, cout, kh, kw, pad).floats);
     return n;
 }
@@ -478,10 +480,12 @@ int mle_conv2d_bwd(const float* x, const float* wgt, const float* dy, float* dx,
         if (s) return s;
     }
     if (dx) {
-        // the forward's columns are consumed: ws[n][K][P] = W^T * dy[n], then dx += col2im
-        s = mle_gemm(wgt, dy, ws, nullptr, batch, K, P, cout, K, P, P, 0, cout * P, K * P, 1, 0, 1.0f, 0.0f, stream);
+        // input-gradient columns after the forward's: dcols[n][K][P] = W^T * dy[n], then dx += col2im
+        float* dcols = ws + (int64_t)batch * K * P;
+        s = mle_gemm(wgt, dy, dcols, nullptr, batch, K, P, cout, K, P, P, 0, cout * P, K * P, 1, 0, 1.0f, 0.0f,
+                     stream);
         if (s) return s;
-        return col2im(ws, dx, batch, cin, h, w, kh, kw, oh, ow, pad, stride, 1, st);
+        return col2im(dcols, dx, batch, cin, h, w, kh, kw, oh, ow, pad, stride, 1, st);
     }
     return MLE_OK;
 }

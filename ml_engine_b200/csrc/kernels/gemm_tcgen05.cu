@@ -1630,7 +1630,7 @@ int mle_linear_group_fwd(const float* X, const float* const* W, const float* con
 int mle_linear_group_bwd(const float* X, const float* const* W, const float* const* dY, float* dX,
                          float* const* dW, float* const* dB, int n, int64_t rows, int in_features,
                          const int* out_features, mle_stream_t stream) {
-    if (!X || !W || !dY || !dW || !out_features || n <= 0 || n > tc::kMaxGroup || rows < 0 || in_features <= 0)
+    if ((dW && !X) || !W || !dY || !out_features || n <= 0 || n > tc::kMaxGroup || rows < 0 || in_features <= 0)
         return MLE_ERR_ARG;
     if (rows == 0) return MLE_OK;
     if (rows > 0x7fffffff) return MLE_ERR_UNSUPPORTED;
@@ -1648,13 +1648,15 @@ int mle_linear_group_bwd(const float* X, const float* const* W, const float* con
         if (s) return s;
     }
     // dW_i += X^T dY_i
-    for (int i = 0; i < n; ++i) {
-        if (!dW[i] || !dY[i]) return MLE_ERR_ARG;
-        ps[i] = linear_problem(X, dY[i], dW[i], nullptr, in_features, out_features[i], rows, in_features,
-                               out_features[i], out_features[i], 1, 0, tc::EPI_ACCUM);
+    if (dW) {
+        for (int i = 0; i < n; ++i) {
+            if (!dW[i] || !dY[i] || out_features[i] <= 0) return MLE_ERR_ARG;
+            ps[i] = linear_problem(X, dY[i], dW[i], nullptr, in_features, out_features[i], rows, in_features,
+                                   out_features[i], out_features[i], 1, 0, tc::EPI_ACCUM);
+        }
+        s = run_gemm_group(ps, n, false, st);
+        if (s) return s;
     }
-    s = run_gemm_group(ps, n, false, st);
-    if (s) return s;
     if (dB) {
         for (int i = 0; i < n; ++i) {
             if (!dB[i]) continue;
@@ -1751,7 +1753,7 @@ int mle_linear_fwd(const float* X, const float* W, const float* bias, float* Y, 
 
 int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, float* dW, float* dB, int64_t rows,
                    int in_features, int out_features, mle_stream_t stream) {
-    if (!X || !W || !dY || !dW || rows < 0 || in_features <= 0 || out_features <= 0) return MLE_ERR_ARG;
+    if ((dW && !X) || !W || !dY || rows < 0 || in_features <= 0 || out_features <= 0) return MLE_ERR_ARG;
     if (rows == 0) return MLE_OK;
     int s;
     if (dX) {
@@ -1761,9 +1763,11 @@ int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, f
         if (s) return s;
     }
     // dW[in, out] += X[rows, in]^T * dY[rows, out]
-    s = mle_gemm(X, dY, dW, nullptr, 1, in_features, out_features, rows, in_features, out_features, out_features, 0, 0,
-                 0, 1, 0, 1.0f, 1.0f, stream);
-    if (s) return s;
+    if (dW) {
+        s = mle_gemm(X, dY, dW, nullptr, 1, in_features, out_features, rows, in_features, out_features, out_features,
+                     0, 0, 0, 1, 0, 1.0f, 1.0f, stream);
+        if (s) return s;
+    }
     if (dB) return mle_bias_grad(dY, dB, rows, out_features, 1.0f, stream);
     return MLE_OK;
 }

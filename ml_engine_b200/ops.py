@@ -320,8 +320,9 @@ def conv2d_fwd(x, w, bias, y, ws, pad, stride):
 
 
 def conv2d_bwd(x, w, dy, dx, dw, db, ws, pad, stride):
-    """dw assigned, db and dx accumulated; x and ws as given to conv2d_fwd
-    (ws consumed)."""
+    """dw assigned, db and dx accumulated; x and ws as given to conv2d_fwd.
+    Any of dx, dw, db may be None; the dx part and the dw/db part may run as
+    two calls on two streams."""
     n, cin, h, wd = x.shape
     cout, _, kh, kw = w.shape
     _call("mle_conv2d_bwd", _p(x), _p(w), _p(dy), _p(dx), _p(dw), _p(db), _p(ws), n, cin, h, wd, cout, kh, kw, pad,

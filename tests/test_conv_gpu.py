@@ -82,6 +82,39 @@ def test_conv2d(cuda, rng, gemm_mode, case):
     assert norm_err(H(db), rdb) <= 1e-5
 
 
+@pytest.mark.parametrize("case", [CONV[1], CONV[2], CONV[3]], ids=["implicit", "columns", "in-place"])
+def test_conv2d_backward_parts_on_two_streams(cuda, rng, gemm_mode, case):
+    """The input-gradient part and the weight/bias part of the backward as
+    two calls on two concurrent streams (as the engine issues them) give
+    the single call's results: their workspace regions are disjoint."""
+    from ml_engine_b200 import ops
+    N, Cin, Hh, W, Cout, K, pad, stride = case
+    x = rng.standard_normal((N, Cin, Hh, W)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin, K, K)) * 0.2).astype(np.float32)
+    OH, OW = ops.conv_out_size(Hh, K, pad, stride), ops.conv_out_size(W, K, pad, stride)
+    dy = T(rng.standard_normal((N, Cout, OH, OW)).astype(np.float32), cuda)
+    tx, tw = T(x, cuda), T(w, cuda)
+    y = torch.empty(N, Cout, OH, OW, device=cuda)
+    ws = ops.conv2d_workspace(tx, tw, pad, stride)
+    ops.conv2d_fwd(tx, tw, T(np.zeros(Cout, np.float32), cuda), y, ws, pad, stride)
+    dx1, dw1, db1 = torch.zeros_like(tx), torch.zeros_like(tw), torch.zeros(Cout, device=cuda)
+    ops.conv2d_bwd(tx, tw, dy, dx1, dw1, db1, ws, pad, stride)
+    torch.cuda.synchronize()
+    dx2, dw2, db2 = torch.zeros_like(tx), torch.zeros_like(tw), torch.zeros(Cout, device=cuda)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    for _ in range(2):  # twice: the workspace stays valid for another backward
+        dx2.zero_(), db2.zero_()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(s1):
+            ops.conv2d_bwd(tx, tw, dy, dx2, None, None, ws, pad, stride)
+        with torch.cuda.stream(s2):
+            ops.conv2d_bwd(tx, tw, dy, None, dw2, db2, ws, pad, stride)
+        torch.cuda.synchronize()
+        # split-K reduce-adds and bias atomics may sum in another order
+        for got, want in ((dx2, dx1), (dw2, dw1), (db2, db1)):
+            assert norm_err(H(got), H(want)) <= 1e-6
+
+
 @pytest.mark.parametrize("case", CONVT)
 def test_convT2d(cuda, rng, gemm_mode, case):
     from ml_engine_b200 import ops
