@@ -571,6 +571,8 @@ def main():
                     help="attention implementation (mle_set_attention_path); default: the library's")
     ap.add_argument("--param-stream", type=int, default=None, choices=[0, 1],
                     help="weight/bias gradients on a second stream (mle_set_param_grad_stream); default: on")
+    ap.add_argument("--stage-kblocks", type=int, default=None, choices=[1, 2],
+                    help="GEMM k-blocks per pipeline stage (mle_set_gemm_stage_kblocks); default: the library's")
     ap.add_argument("--roofline-only", action="store_true",
                     help="run only the roofline kernel pair (3 untimed + 20 timed pairs)")
     args = ap.parse_args()
@@ -580,6 +582,9 @@ def main():
     if args.attn_path is not None:
         from ml_engine_b200._lib import kernels
         kernels().call("mle_set_attention_path", {"auto": 0, "fused": 1, "tensor": 2}[args.attn_path])
+    if args.stage_kblocks is not None:
+        from ml_engine_b200._lib import kernels
+        kernels().call("mle_set_gemm_stage_kblocks", args.stage_kblocks)
     if args.param_stream is not None:
         from ml_engine_b200._lib import engine
         engine().call("mle_set_param_grad_stream", args.param_stream)

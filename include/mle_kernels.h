@@ -294,6 +294,19 @@ int mle_get_gemm_mode(void);
  * reference. */
 int mle_set_gemm_pairs(int enable);
 int mle_get_gemm_pairs(void);
+/* k-blocks (32 fp32 of K) per pipeline stage of the tensor-core GEMM: 2
+ * (default) stages two k-blocks of each operand with ONE tiled copy, where
+ * both operands' contiguous extents (K for a K-major operand, M or N for
+ * an MN-major one) are multiples of 32, else one; 1 forces one k-block
+ * per stage.  A copy engine serves few large copies faster than many
+ * small ones (measured on B200: 30 B/clk per SM for 16 KB boxes, 47 for
+ * 32 KB, 59 for 64 KB).  mle_gemm_last_stage_kblocks() reports the value
+ * this thread's last product ran with (0 after an mle_gemm call that did
+ * not run on the tensor cores).  Per host thread; no counterpart in the
+ * reference. */
+int mle_set_gemm_stage_kblocks(int kblocks);
+int mle_get_gemm_stage_kblocks(void);
+int mle_gemm_last_stage_kblocks(void);
 /* Element type of the tensor-core GEMM's operand loads: 0 fp32 (the MMA
  * uses the TF32 part of each value: its low 13 mantissa bits are dropped),
  * 1 (default) TF32 (tensor maps of TF32 element type: the copy engine

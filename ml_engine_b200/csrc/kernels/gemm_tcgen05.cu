@@ -73,6 +73,11 @@ struct EpiParams {
     int cv_kw, cv_pad, cv_w, cv_cblk, cv_nb;
     int c_trans;                      // tile rows run along C's contiguous dimension (TMA epilogue only)
     int c_split;                      // > 0: C's inner coordinate is split (x % c_split, x / c_split), 5-D map
+    // operand maps of the split view (one copy per operand and stage): a
+    // K-major operand as (32 K, rows, K / 32, channel, batch), an MN-major
+    // one as (32 MN, K, MN / 32, channel, batch); else the plain 4-D view
+    // (MN-major tiles then arrive as one 32-column box each)
+    int a_split, b_split;
 };
 
 // Output tile `t` of the persistent walk: n fastest, then m, then (batch,
@@ -193,6 +198,15 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1, int c2,
+                                            int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
 // Epilogue stores: a 32 x 32 fp32 block staged in shared memory (128-byte
 // swizzle) leaves with one bulk tensor store, or a bulk tensor reduce-add
 // (C += block) for the accumulate and split-K modes.
@@ -277,15 +291,16 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_byte
     return d;
 }
 
-// Operand tile descriptors for k-step kk (8 tf32 of K) of a stage:
+// Operand tile descriptors for k-step kk (8 tf32 of K) of a k-block:
 //  K-major : rows of 128 B (32 K-values), 8-row swizzle atoms 1024 B apart;
 //            a k-step advances 32 B along the row.
-//  MN-major: per TMA box 32 K-rows x 128 B (32 MN-values), boxes 4096 B
-//            apart along MN (LBO); 32-byte-atom swizzle repeats every 4 rows
-//            (SBO = 512 B); a k-step advances 8 rows = 1024 B.
+//  MN-major: 32 K-rows x 128 B (32 MN-values) per k-block and 32-column
+//            chunk, chunks `lbo` bytes apart along MN (4096 B, or 4096 B
+//            per k-block of a stage); 32-byte-atom swizzle repeats every 4
+//            rows (SBO = 512 B); a k-step advances 8 rows = 1024 B.
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) { return make_sdesc(base + kk * 32, 16, 1024); }
-__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
-    return make_sdesc(base + kk * 1024, 4096, 512, kLayoutSW128Atom32);
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk, uint32_t lbo = 4096) {
+    return make_sdesc(base + kk * 1024, lbo, 512, kLayoutSW128Atom32);
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -332,6 +347,15 @@ __device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_
         "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
         "%5, %6}], [%2];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d_pair(const CUtensorMap* map, uint32_t bar_cluster, void* dst, int c0,
+                                                 int c1, int c2, int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+        "%5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
         : "memory");
 }
 
@@ -387,10 +411,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN, int STAGES>
+// A stage holds KPL k-blocks of A (and of B): K-major [kb][rows][32 K],
+// MN-major [32-column chunk][kb][32 K rows][32 MN].
+template <int BN, int STAGES, int KPL = 1>
 struct Smem {
-    static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
-    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int A_BYTES = KPL * BM * BK * 4;  // 16 KB per k-block
+    static constexpr int B_BYTES = KPL * BN * BK * 4;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
     static constexpr int EPI_WARP_BYTES = 2 * 32 * 32 * 4;  // two 4 KB blocks (>= 32 x kEpiLd floats)
@@ -403,12 +429,14 @@ struct Smem {
 // A_MN: A is stored MN-major ([K][M]); B_MN: B is stored MN-major ([K][N]).
 // PAIR: launched as 2-CTA clusters; a tile is 256 x BN (cta_group::2 MMAs),
 // each CTA staging 128 rows of A and BN/2 columns of B.
-template <bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR = false>
+// KPL: k-blocks per stage, each operand's stage arriving as one copy of
+// the split view (KPL = 2 only for operands that have one).
+template <bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR = false, int KPL = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ GemmGroup grp) {
     constexpr int BNC = PAIR ? BN / 2 : BN;  // B columns staged by this CTA
     constexpr int BMT = PAIR ? 2 * BM : BM;  // tile rows
-    using L = Smem<BNC, STAGES>;
+    using L = Smem<BNC, STAGES, KPL>;
     static_assert(L::EPI_WARP_BYTES >= 32 * kEpiLd * 4, "staging");
     static_assert(BNC % 32 == 0, "B staged in 32-column boxes");
     constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators (this CTA's 128 rows x BN)
@@ -493,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
                 const int a_c = ep.a_has_c ? x.cidx : 0, a_b = ep.a_has_b ? x.bidx : 0;
                 const int b_c = ep.b_has_c ? x.cidx : 0, b_b = ep.b_has_b ? x.bidx : 0;
-                for (int i = 0; i < x.nkb; ++i) {
+                for (int i = 0; i < x.nkb; i += KPL) {
                     if (!wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
                         ok = false;
                         break;
@@ -511,7 +539,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if constexpr (PAIR) tma_load_4d_pair(map, bar, dst, c0, c1, c2, c3);
                         else tma_load_4d(map, &full[s], dst, c0, c1, c2, c3);
                     };
-                    if (!A_MN && B_MN && ep.conv == 1) {
+                    auto load5 = [&](const CUtensorMap* map, void* dst, int c1, int c2, int c3, int c4) {
+                        if constexpr (PAIR) tma_load_5d_pair(map, bar, dst, 0, c1, c2, c3, c4);
+                        else tma_load_5d(map, &full[s], dst, 0, c1, c2, c3, c4);
+                    };
+                    if (KPL == 1 && !A_MN && B_MN && ep.conv == 1) {
                         // weights [tap][m][c]; the pixels of a tap are the output
                         // pixels moved by whole rows in the flattened image plane
                         const int kb = x.kb_begin + i;
@@ -522,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         load(tmA, sa, c0, mo, tap, 0);
 #pragma unroll
                         for (int j = 0; j < BNC / 32; ++j) load(tmB, sb + j * 4096, no + 32 * j + dp, c0, zc, 0);
-                    } else if (A_MN && !B_MN && ep.conv == 3) {
+                    } else if (KPL == 1 && A_MN && !B_MN && ep.conv == 3) {
                         const int kb = x.kb_begin + i;
                         const int tap = kb / ep.cv_cblk, c0 = (kb - tap * ep.cv_cblk) * BK;
                         const int kh = tap / ep.cv_kw, kw = tap - kh * ep.cv_kw;
@@ -531,19 +563,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < BM / 32; ++j) load(tmA, sa + j * 4096, mo + 32 * j + dp, c0, zc, 0);
                         load(tmB, sb, c0, no, tap, 0);
-                    } else if (!A_MN && !B_MN && ep.conv == 2) {
+                    } else if (KPL == 1 && !A_MN && !B_MN && ep.conv == 2) {
                         // B rows = channels no.. of tap x.cidx at pixels k0..k0+31
                         const int kh = x.cidx / ep.cv_kw, kw = x.cidx - kh * ep.cv_kw;
                         load(tmA, sa, k0, mo, a_c, a_b);
                         load(tmB, sb, k0 + (kh - ep.cv_pad) * ep.cv_w, no, kw * ep.cv_nb + x.bidx, 0);
                     } else {
-                        if (A_MN) {
+                        // split views: the stage's KPL k-blocks of all its
+                        // rows (K-major) or 32-column chunks (MN-major) in
+                        // one copy per operand
+                        if (ep.a_split) {
+                            if (A_MN) load5(tmA, sa, k0, mo >> 5, a_c, a_b);
+                            else load5(tmA, sa, mo, k0 >> 5, a_c, a_b);
+                        } else if (A_MN) {
 #pragma unroll
                             for (int j = 0; j < BM / 32; ++j) load(tmA, sa + j * 4096, mo + 32 * j, k0, a_c, a_b);
                         } else {
                             load(tmA, sa, k0, mo, a_c, a_b);
                         }
-                        if (B_MN) {
+                        if (ep.b_split) {
+                            if (B_MN) load5(tmB, sb, k0, no >> 5, b_c, b_b);
+                            else load5(tmB, sb, no, k0 >> 5, b_c, b_b);
+                        } else if (B_MN) {
 #pragma unroll
                             for (int j = 0; j < BNC / 32; ++j) load(tmB, sb + j * 4096, no + 32 * j, k0, b_c, b_b);
                         } else {
@@ -587,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
-                for (int i = 0; i < x.nkb; ++i) {
+                for (int i = 0; i < x.nkb; i += KPL) {
                     if (!wait_bounded(&full[s], ph, abort_flag)) {
                         ok = false;
                         break;
@@ -595,12 +636,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
                     const uint32_t sb = sa + L::A_BYTES;
+                    // the stage's last copy may reach past the tile's k-range
+                    const int nv = min(KPL, x.nkb - i);
+                    for (int kb = 0; kb < nv; ++kb) {
+                        const uint32_t ka = A_MN ? sa + kb * 4096 : sa + kb * (BM * BK * 4);
+                        const uint32_t kbb = B_MN ? sb + kb * 4096 : sb + kb * (BNC * BK * 4);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk) {
-                        const uint64_t ad = A_MN ? mnmajor_desc(sa, kk) : kmajor_desc(sa, kk);
-                        const uint64_t bd = B_MN ? mnmajor_desc(sb, kk) : kmajor_desc(sb, kk);
-                        if constexpr (PAIR) mma_tf32_pair(tmem_d, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                        else mma_tf32(tmem_d, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            const uint64_t ad = A_MN ? mnmajor_desc(ka, kk, KPL * 4096) : kmajor_desc(ka, kk);
+                            const uint64_t bd = B_MN ? mnmajor_desc(kbb, kk, KPL * 4096) : kmajor_desc(kbb, kk);
+                            const uint32_t accum = (i > 0 || kb > 0 || kk > 0) ? 1u : 0u;
+                            if constexpr (PAIR) mma_tf32_pair(tmem_d, ad, bd, idesc, accum);
+                            else mma_tf32(tmem_d, ad, bd, idesc, accum);
+                        }
                     }
                     if constexpr (PAIR) mma_commit_pair_both(&empty[s]);
                     else mma_commit(&empty[s]);
@@ -858,6 +906,28 @@ static bool encode_operand(CUtensorMap* map, const OperandView& v, int box_inner
     return r == CUDA_SUCCESS;
 }
 
+// Split view of an operand whose contiguous extent is a multiple of 32:
+// (32, outer, inner / 32, channel, batch), so one copy brings a stage.
+// K-major (inner = K): box (32, rows, kpl) lands as [kb][rows][32 K];
+// MN-major (inner = M or N): box (32, 32 * kpl, mn / 32) lands as
+// [32-column chunk][32 * kpl K rows][32 MN].
+static bool encode_operand_split(CUtensorMap* map, const OperandView& v, bool mn_major, int box_rows, int kpl,
+                                 CUtensorMapDataType dt) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc || v.inner % 32 != 0 || box_rows % 32 != 0) return false;
+    int64_t sc = v.sc, sb = v.sb;
+    if (v.nc == 1) sc = v.ld * v.outer;
+    if (v.nb == 1) sb = (v.nc == 1 ? v.ld * v.outer : sc * v.nc);
+    cuuint64_t dims[5] = {32, (cuuint64_t)v.outer, (cuuint64_t)(v.inner / 32), (cuuint64_t)v.nc, (cuuint64_t)v.nb};
+    cuuint64_t strides[4] = {(cuuint64_t)(v.ld * 4), 128, (cuuint64_t)(sc * 4), (cuuint64_t)(sb * 4)};
+    cuuint32_t box[5] = {32, (cuuint32_t)(mn_major ? 32 * kpl : box_rows), (cuuint32_t)(mn_major ? box_rows / 32 : kpl),
+                         1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return enc(map, dt, 5, const_cast<float*>(v.base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // fp32 tensor map of `rank` (4 or 5) dims with explicit extents, element
 // strides of dims 1.. and box.
 static bool encode_map(CUtensorMap* map, const float* base, const int64_t* dims, const int64_t* strides,
@@ -877,12 +947,12 @@ static bool encode_map(CUtensorMap* map, const float* base, const int64_t* dims,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR = false>
+template <bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR = false, int KPL = 1>
 static int launch_tc(const GemmGroup& grp, cudaStream_t st) {
-    using L = Smem<PAIR ? BN / 2 : BN, STAGES>;
+    using L = Smem<PAIR ? BN / 2 : BN, STAGES, KPL>;
     static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
     static_assert(sizeof(GemmGroup) <= 4000, "kernel parameter space");
-    auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, STAGES, PAIR>;
+    auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, STAGES, PAIR, KPL>;
     static bool configured = false;
     if (!configured) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
@@ -965,6 +1035,11 @@ static thread_local int g_last_choice[3] = {0, 0, 0};
 // to even, as it loads; measured on B200).  Rounding halves the typical
 // product error at no cost, so it is the default.
 static thread_local int g_operand_round = 1;
+
+// k-blocks per stage for products whose operands all have a split view
+// (1 forces one k-block per stage everywhere)
+static thread_local int g_stage_kblocks = 2;
+static thread_local int g_last_kpl = 1;
 
 static CUtensorMapDataType operand_type() {
     return g_operand_round ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -1089,7 +1164,7 @@ void choose_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool model
 // parameters); an assigned C that is split is zeroed first.  False if TMA
 // cannot describe an operand.
 int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc::GemmGroup& grp, int g,
-            cudaStream_t st, bool& ok, bool pair = false) {
+            cudaStream_t st, bool& ok, bool pair = false, int kpl = 1) {
     using namespace tc;
     ok = false;
     const Shape sh = shape_of(p);
@@ -1144,8 +1219,16 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
     memset(&grp.a[g], 0, sizeof(CUtensorMap));
     memset(&grp.b[g], 0, sizeof(CUtensorMap));
     memset(&grp.c[g], 0, sizeof(CUtensorMap));
-    if (!encode_operand(&grp.a[g], va, 32, sh.A_MN ? BK : BM, sh.A_MN, operand_type())) return MLE_OK;
-    if (!encode_operand(&grp.b[g], vb, 32, sh.B_MN ? BK : bn_cta, sh.B_MN, operand_type())) return MLE_OK;
+    // split views: always for MN-major operands that have one (one copy
+    // instead of one per 32 columns), for K-major ones when the stage holds
+    // several k-blocks (kpl > 1 needs both operands split)
+    ep.a_split = ((sh.A_MN || kpl > 1) && encode_operand_split(&grp.a[g], va, sh.A_MN, BM, kpl, operand_type())) ? 1 : 0;
+    ep.b_split =
+        ((sh.B_MN || kpl > 1) && encode_operand_split(&grp.b[g], vb, sh.B_MN, bn_cta, kpl, operand_type())) ? 1 : 0;
+    if (kpl > 1 && !(ep.a_split && ep.b_split)) return MLE_OK;
+    if (!ep.a_split && !encode_operand(&grp.a[g], va, 32, sh.A_MN ? BK : BM, sh.A_MN, operand_type())) return MLE_OK;
+    if (!ep.b_split && !encode_operand(&grp.b[g], vb, 32, sh.B_MN ? BK : bn_cta, sh.B_MN, operand_type()))
+        return MLE_OK;
     // C through bulk tensor stores when its rows and strides allow TMA
     ep.c_has_b = (ep.c_stride_b != 0);
     ep.c_has_c = (ep.c_stride_c != 0);
@@ -1190,8 +1273,25 @@ int prepare(const GemmProblem& p, int BN, int splits_req, bool force_atomic, tc:
     return MLE_OK;
 }
 
-int dispatch(const tc::GemmGroup& grp, bool A_MN, bool B_MN, int BN, cudaStream_t st, bool pair = false) {
+int dispatch(const tc::GemmGroup& grp, bool A_MN, bool B_MN, int BN, cudaStream_t st, bool pair = false,
+             int kpl = 1) {
     using namespace tc;
+    if (kpl == 2) {  // two k-blocks per stage: half as many stages in the same ring
+#define MLE_TCK(AM, BMN, BNV, ST, PR) return launch_tc<AM, BMN, BNV, ST, PR, 2>(grp, st)
+#define MLE_TCK4(BNV, ST, PR)                                                        \
+    if (A_MN) { if (B_MN) MLE_TCK(true, true, BNV, ST, PR); else MLE_TCK(true, false, BNV, ST, PR); } \
+    else { if (B_MN) MLE_TCK(false, true, BNV, ST, PR); else MLE_TCK(false, false, BNV, ST, PR); }
+        if (pair) {
+            if (BN == 256) { MLE_TCK4(256, 3, true) }
+            else if (BN == 128) { MLE_TCK4(128, 4, true) }
+            else { MLE_TCK4(64, 4, true) }
+        }
+        if (BN == 256) { MLE_TCK4(256, 2, false) }
+        else if (BN == 128) { MLE_TCK4(128, 3, false) }
+        else { MLE_TCK4(64, 4, false) }
+#undef MLE_TCK4
+#undef MLE_TCK
+    }
 #define MLE_TC(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST>(grp, st)
 #define MLE_TC2(AM, BMN, BNV, ST) return launch_tc<AM, BMN, BNV, ST, true>(grp, st)
     if (pair) {  // 256 x BN tiles on CTA pairs, each CTA staging BN/2 columns of B
@@ -1222,6 +1322,13 @@ int dispatch(const tc::GemmGroup& grp, bool A_MN, bool B_MN, int BN, cudaStream_
 
 bool tc_path(const GemmProblem& p) { return p.K > 0 && g_gemm_mode == MLE_GEMM_MODE_TF32 && tc_eligible(p); }
 
+// Both operands have a split view (contiguous extent a multiple of 32):
+// the product may stage two k-blocks per copy.
+bool split_ok(const GemmProblem& p) {
+    const Shape sh = shape_of(p);
+    return (sh.A_MN ? p.M % 32 == 0 : p.K % 32 == 0) && (sh.B_MN ? p.N % 32 == 0 : p.K % 32 == 0);
+}
+
 }  // namespace
 
 int run_gemm(const GemmProblem& p, cudaStream_t st) {
@@ -1237,8 +1344,15 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     tc::GemmGroup grp;
     memset(&grp, 0, sizeof(grp));
     bool ok = false;
-    const int s = prepare(p, BN, splits, false, grp, 0, st, ok, pair);
+    int kpl = (g_stage_kblocks == 2 && split_ok(p)) ? 2 : 1;
+    int s = prepare(p, BN, splits, false, grp, 0, st, ok, pair, kpl);
     if (s) return s;
+    if (!ok && kpl == 2) {
+        kpl = 1;
+        memset(&grp, 0, sizeof(grp));
+        s = prepare(p, BN, splits, false, grp, 0, st, ok, pair, kpl);
+        if (s) return s;
+    }
     if (!ok) return p.c_split ? MLE_ERR_UNSUPPORTED : simt_gemm(p, st);
     grp.n = 1;
     grp.tile_start[0] = 0;
@@ -1247,7 +1361,8 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     g_last_choice[0] = BN;
     g_last_choice[1] = grp.ep[0].splits;
     g_last_choice[2] = pair ? 1 : 0;
-    return dispatch(grp, sh.A_MN, sh.B_MN, BN, st, pair);
+    g_last_kpl = kpl;
+    return dispatch(grp, sh.A_MN, sh.B_MN, BN, st, pair, kpl);
 }
 
 // Problems of one layout class in one persistent launch.  `shared_c`: all
@@ -1272,23 +1387,34 @@ int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st)
     bool pair = false;
     choose_tiles(ps, n, BN, splits, false, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
     tc::GemmGroup grp;
-    memset(&grp, 0, sizeof(grp));
-    grp.n = n;
-    grp.tile_start[0] = 0;
-    for (int i = 0; i < n; ++i) {
-        bool ok = false;
-        const int s = prepare(ps[i], BN, splits, shared_c, grp, i, st, ok, pair);
-        if (s) return s;
-        if (!ok) {  // an operand TMA cannot describe: separate launches
-            for (int j = 0; j < n; ++j) {
-                const int s2 = run_gemm(ps[j], st);
-                if (s2) return s2;
-            }
-            return MLE_OK;
+    int kpl = g_stage_kblocks == 2 ? 2 : 1;
+    for (int i = 0; i < n; ++i) kpl = split_ok(ps[i]) ? kpl : 1;
+    for (;;) {
+        memset(&grp, 0, sizeof(grp));
+        grp.n = n;
+        grp.tile_start[0] = 0;
+        bool all_ok = true;
+        for (int i = 0; i < n && all_ok; ++i) {
+            bool ok = false;
+            const int s = prepare(ps[i], BN, splits, shared_c, grp, i, st, ok, pair, kpl);
+            if (s) return s;
+            all_ok = ok;
+            grp.tile_start[i + 1] = grp.tile_start[i] + grp.ep[i].tiles;
         }
-        grp.tile_start[i + 1] = grp.tile_start[i] + grp.ep[i].tiles;
+        if (all_ok) break;
+        if (kpl == 2) {  // a split view TMA cannot describe: one k-block per stage
+            kpl = 1;
+            continue;
+        }
+        // an operand TMA cannot describe: separate launches
+        for (int j = 0; j < n; ++j) {
+            const int s2 = run_gemm(ps[j], st);
+            if (s2) return s2;
+        }
+        return MLE_OK;
     }
-    return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st, pair);
+    g_last_kpl = kpl;
+    return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st, pair, kpl);
 }
 
 bool conv_gemm_supported(const ConvGemm& c) {
@@ -1525,6 +1651,16 @@ int mle_set_gemm_store_path(int path) {
     return MLE_OK;
 }
 
+int mle_set_gemm_stage_kblocks(int kblocks) {
+    if (kblocks != 1 && kblocks != 2) return MLE_ERR_ARG;
+    g_stage_kblocks = kblocks;
+    return MLE_OK;
+}
+
+int mle_get_gemm_stage_kblocks(void) { return g_stage_kblocks; }
+
+int mle_gemm_last_stage_kblocks(void) { return g_last_kpl; }
+
 int mle_set_gemm_operand_rounding(int mode) {
     if (mode != 0 && mode != 1) return MLE_ERR_ARG;
     g_operand_round = mode;
@@ -1558,6 +1694,7 @@ int mle_gemm(const float* A, const float* B, float* C, const float* bias, int ba
     if (!A || !B || !C || batch <= 0 || M < 0 || N < 0 || K < 0) return MLE_ERR_ARG;
     if (beta != 0.0f && beta != 1.0f) return MLE_ERR_UNSUPPORTED;
     if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return MLE_ERR_UNSUPPORTED;
+    g_last_kpl = 0;  // set again if the product runs on the tensor cores
     GemmProblem p;
     p.A = A;
     p.B = B;

@@ -309,18 +309,39 @@ def test_mse(cuda, ops, orc, rng):
 # ----------------------------------------------------------------------- GEMM
 GEMM_SHAPES = [(128, 128, 32), (256, 512, 384), (200, 130, 70), (64, 256, 784), (784, 256, 64), (1000, 96, 8),
                (4096, 256, 256), (256, 256, 4096), (33, 1024, 129),
-               (1, 128, 256), (3, 64, 1000)]  # at most 8 rows: one warp per output
+               (1, 128, 256), (3, 64, 1000),  # at most 8 rows: one warp per output
+               (512, 256, 480),               # 15 k-blocks: a stage of two k-blocks holds only the last one
+               (256, 256, 2080)]              # split-K ranges of an odd number of k-blocks
+
+
+@pytest.fixture(params=[2, 1], ids=["kpl2", "kpl1"])
+def stage_kblocks(request):
+    """Two k-blocks per GEMM stage where both operands have split views
+    (the default), or one everywhere."""
+    from ml_engine_b200._lib import kernels
+    k = kernels()
+    old = k.mle_get_gemm_stage_kblocks()
+    k.call("mle_set_gemm_stage_kblocks", request.param)
+    yield request.param
+    k.call("mle_set_gemm_stage_kblocks", old)
 
 
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("beta", [0.0, 1.0])
-def test_gemm_tf32(cuda, ops, orc, rng, M, N, K, ta, tb, beta):
+def test_gemm_tf32(cuda, ops, orc, rng, stage_kblocks, M, N, K, ta, tb, beta):
+    from ml_engine_b200._lib import kernels
     A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
     B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
     C0 = rng.standard_normal((M, N)).astype(np.float32)
     C = T(C0, cuda)
     ops.gemm(T(A, cuda), T(B, cuda), C, M, N, K, ta, tb, alpha=0.5, beta=beta)
+    kpl = kernels().mle_gemm_last_stage_kblocks()
+    if kpl:  # a tensor-core product: two k-blocks per stage iff both operands split
+        split = (M % 32 == 0 if ta else K % 32 == 0) and (K % 32 == 0 if tb else N % 32 == 0)
+        assert kpl == (2 if split and stage_kblocks == 2 else 1)
+    if (M, N, K) == (4096, 256, 256):
+        assert kpl == stage_kblocks
     ref = C0.copy() if beta else np.zeros_like(C0)
     prod = np.zeros((M, N), np.float32)
     orc.gemm(A, B, prod, M, N, K, ta, tb)
@@ -332,8 +353,9 @@ def test_gemm_tf32(cuda, ops, orc, rng, M, N, K, ta, tb, beta):
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("beta", [0.0, 1.0])
-@pytest.mark.parametrize("M,N,K,mode", [(4000, 2000, 520, 1), (1000, 100, 300, 2), (700, 200, 96, 2)])
-def test_gemm_cta_pairs(cuda, ops, rng, ta, tb, beta, M, N, K, mode):
+@pytest.mark.parametrize("M,N,K,mode", [(4000, 2000, 520, 1), (1000, 100, 300, 2), (700, 200, 96, 2),
+                                        (1024, 512, 544, 2), (512, 192, 96, 2)])
+def test_gemm_cta_pairs(cuda, ops, rng, stage_kblocks, ta, tb, beta, M, N, K, mode):
     """Products on CTA pairs (cta_group::2 MMAs, 256-row tiles) with ragged
     edges in M, N and K, against float64 products: chosen by the tile model
     for the large one, forced (mode 2) for 64- and 128-wide pair tiles."""
