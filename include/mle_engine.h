@@ -100,6 +100,16 @@ int mle_session_capture(mle_session_t s);
 int mle_set_param_grad_stream(int enable);
 int mle_get_param_grad_stream(void);
 
+/* First-writer assignment of activation gradients: when the first node to
+ * write a gradient in the backward walk overwrites all of it (the loss,
+ * an activation, or a Linear whose input gradient spans at least two waves
+ * of 128 x 128 tiles), zero_grad leaves that buffer alone and the writer
+ * assigns instead of adding, with bit-identical results.  1 (default) on,
+ * 0 every gradient cleared and accumulated.  Process-wide; decided when a
+ * backward pass starts, so it applies from the next zero_grad on. */
+int mle_set_grad_first_write(int enable);
+int mle_get_grad_first_write(void);
+
 /* Kernel, memset and memcpy nodes of the captured device-resident step
  * (the launches one replay issues). */
 int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* copies);

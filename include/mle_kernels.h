@@ -122,6 +122,12 @@ int mle_act_fwd(int kind, const float* x, float* y, int64_t n, mle_stream_t stre
  * consumer. */
 int mle_act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n,
                 float* bias_grad, int64_t rows, int64_t cols, mle_stream_t stream);
+/* The same with gx's previous contents taken as zero: gx is written, not
+ * read, and equals bit for bit what mle_act_bwd leaves in a cleared gx.
+ * For the first writer of a gradient buffer that is not cleared between
+ * steps. */
+int mle_act_bwd_assign(int kind, const float* x, const float* gy, float* gx, int64_t n,
+                       float* bias_grad, int64_t rows, int64_t cols, mle_stream_t stream);
 
 /* y[r, c] = x[r, c] + bias[c].  Replaces BCumAdd (Engine/kernels.cu:1586-1592)
  * as launched by Linear/Bias_Add forward.  y may alias x. */

@@ -172,8 +172,26 @@ static void flush_zero_ranges() {
     r.clear();
 }
 
+static std::unordered_set<const float*> g_preassigned;
+static bool g_first_write = true;
+
+void set_preassigned_grads(const std::vector<const float*>& grads) {
+    g_preassigned.clear();
+    if (g_first_write) g_preassigned.insert(grads.begin(), grads.end());
+}
+
+bool grad_preassigned(const float* grad) { return g_preassigned.count(grad) != 0; }
+
+void set_first_write_assign(bool on) {
+    g_first_write = on;
+    if (!on) g_preassigned.clear();
+}
+
+bool first_write_assign() { return g_first_write; }
+
 void zero_range(float* p, int64_t n) {
     if (!p || n <= 0) return;
+    if (g_preassigned.count(p)) return;  // its first writer in the backward assigns it
     if (g_zero_depth > 0) g_zero_ranges.push_back({p, n});
     else check_cuda(cudaMemsetAsync(p, 0, (size_t)n * sizeof(float), g_stream), "Zerograd");
 }

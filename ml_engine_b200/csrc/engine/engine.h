@@ -72,6 +72,13 @@ cudaStream_t param_stream();         // the second stream (nullptr before init)
 void set_param_stream_enabled(bool on);
 bool param_stream_enabled();
 
+// First-writer assignment: a gradient whose first writer in the backward
+// walk overwrites all of it (see prepare_fusions) is not cleared by
+// zero_grad, and that writer assigns instead of adding.  The results are
+// those of adding into a cleared buffer, bit for bit.  On by default.
+void set_first_write_assign(bool on);
+bool first_write_assign();
+
 // Maps a non-zero mle_status onto the reference's behaviour: print the
 // reason and exit(1) (Engine/debug.cu:15-25).
 void check(int status, const str& what);

@@ -48,6 +48,7 @@ struct NodeExt {
     float* fused_bias_target = nullptr;  // activation: bias grad to accumulate
     long long fused_rows = 0, fused_cols = 0;
     std::vector<float*> param_grads;     // parameter gradients complete once this node's backward ran
+    bool assign_input_grad = false;      // this node's backward writes (not adds to) its input's gradient
 };
 NodeExt& ext(const NodeBackProp* n);
 void forget_ext(const NodeBackProp* n);
@@ -55,6 +56,14 @@ void forget_ext(const NodeBackProp* n);
 // Decides the Linear -> activation bias-gradient fusion for a node list:
 // an activation whose input is a biased Linear output consumed by nothing
 // else adds that Linear's BCompress (column sums) to its own backward pass.
+// Also finds gradients whose first writer in the backward walk (the
+// consumer last in topological order) overwrites the whole buffer: a
+// loss node, an activation, or a Linear with a large input gradient.  That
+// writer assigns (assign_input_grad) and zero_grad leaves the buffer alone.
 void prepare_fusions(const graph_tree& nodes);
+
+// Gradient buffers zero_range skips (their first writer assigns them).
+void set_preassigned_grads(const std::vector<const float*>& grads);
+bool grad_preassigned(const float* grad);
 
 }  // namespace mle

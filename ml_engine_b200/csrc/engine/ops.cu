@@ -30,13 +30,43 @@ void forget_ext(const NodeBackProp* n) { ext_map().erase(n); }
 
 void prepare_fusions(const graph_tree& nodes) {
     std::unordered_map<const NodeBackProp*, int> consumers;
+    // the consumer of each node that runs first in the backward walk
+    std::unordered_map<const NodeBackProp*, const NodeBackProp*> first_writer;
     for (auto& n : nodes)
-        for (auto& in : n->inputs) consumers[in.get()]++;
+        for (auto& in : n->inputs) {
+            consumers[in.get()]++;
+            first_writer[in.get()] = n.get();
+        }
     for (auto& n : nodes) {
         NodeExt& e = ext(n.get());
         if (e.kind == OP_LINEAR) e.bias_grad_fused = false;
         if (e.kind == OP_ACTIVATION) e.fused_bias_target = nullptr;
+        e.assign_input_grad = false;
     }
+    // first writers that overwrite the whole input gradient: the loss
+    // (SoftMaxCrossEntropy assigns its prediction's gradient), an
+    // activation, and a Linear whose input gradient spans at least two
+    // waves of 128 x 128 tiles (its product then never splits K, so the
+    // assigned GEMM costs no memset of its own)
+    std::vector<const float*> pre;
+    if (first_write_assign()) {
+        for (auto& n : nodes) {
+            const NodeBackProp* x = n.get();
+            auto it = first_writer.find(x);
+            if (it == first_writer.end() || !x->grad) continue;
+            const NodeBackProp* w = it->second;
+            NodeExt& we = ext(w);
+            bool ok = false;
+            if (we.kind == OP_SMCE) ok = w->inputs.size() == 2 && w->inputs[0].get() == x && w->inputs[1].get() != x;
+            if (we.kind == OP_ACTIVATION) ok = w->inputs.size() == 1;
+            if (we.kind == OP_LINEAR)
+                ok = w->inputs.size() == 1 && (double)x->total >= 2.0 * 148 * 128.0 * 128.0;  // 148 SMs
+            if (!ok) continue;
+            if (we.kind != OP_SMCE) we.assign_input_grad = true;
+            pre.push_back(x->grad);
+        }
+    }
+    set_preassigned_grads(pre);
     for (auto& n : nodes) {
         NodeExt& e = ext(n.get());
         if (e.kind != OP_ACTIVATION || n->inputs.size() != 1) continue;
@@ -476,8 +506,9 @@ static graph act_node(const char* name, int kind, const graph& input) {
     node->forward = [=]() { check(mle_act_fwd(kind, ip->output, nd->output, nd->total, st()), str(name) + " forward"); };
     node->backward = [=]() {
         const NodeExt& e = ext(nd);
-        check(mle_act_bwd(kind, ip->output, nd->grad, ip->grad, nd->total, e.fused_bias_target, e.fused_rows,
-                          e.fused_cols, st()),
+        check((e.assign_input_grad ? mle_act_bwd_assign : mle_act_bwd)(kind, ip->output, nd->grad, ip->grad,
+                                                                        nd->total, e.fused_bias_target, e.fused_rows,
+                                                                        e.fused_cols, st()),
               str(name) + " backward");
     };
     node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
@@ -695,8 +726,13 @@ graph Linear::forward(const graph& X) {
         const bool fused = ext(nd).bias_grad_fused;
         // dW and dB on the parameter-gradient stream, concurrent with dX
         void* ps = (void*)fork_param_stream();
-        check(mle_linear_bwd(nullptr, W->output, nd->grad, xp->grad, nullptr, nullptr, rows, n, p, st()),
-              "MatMul... in " + nd->op_name + " backward");
+        if (ext(nd).assign_input_grad)  // first writer of dX: dX = dY W^T
+            check(mle_gemm(nd->grad, W->output, xp->grad, nullptr, 1, rows, n, p, p, p, n, 0, 0, 0, 0, 1, 1.0f, 0.0f,
+                           st()),
+                  "MatMul... in " + nd->op_name + " backward");
+        else
+            check(mle_linear_bwd(nullptr, W->output, nd->grad, xp->grad, nullptr, nullptr, rows, n, p, st()),
+                  "MatMul... in " + nd->op_name + " backward");
         check(mle_linear_bwd(xp->output, W->output, nd->grad, nullptr, W->grad, (Bp && !fused) ? Bp->grad : nullptr,
                              rows, n, p, ps),
               "MatMul... in " + nd->op_name + " backward");

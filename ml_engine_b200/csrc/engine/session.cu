@@ -676,6 +676,14 @@ int mle_set_param_grad_stream(int enable) {
 
 int mle_get_param_grad_stream(void) { return mle::param_stream_enabled() ? 1 : 0; }
 
+int mle_set_grad_first_write(int enable) {
+    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    mle::set_first_write_assign(enable != 0);
+    return MLE_OK;
+}
+
+int mle_get_grad_first_write(void) { return mle::first_write_assign() ? 1 : 0; }
+
 int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* copies) {
     Session* S = as_session(s);
     if (!S || !kernels || !memsets || !copies) return MLE_ERR_ARG;

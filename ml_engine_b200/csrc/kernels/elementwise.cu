@@ -195,7 +195,9 @@ __global__ void act_fwd_kernel(int kind, const float* __restrict__ x, float* __r
     for (int64_t j = tail + i0; j < n; j += stride) y[j] = act_forward(kind, x[j]);
 }
 
-template <bool VEC>
+// ASSIGN: gx's previous contents count as zero (not read): the result is
+// bitwise that of accumulating into a cleared buffer.
+template <bool VEC, bool ASSIGN = false>
 __global__ void act_bwd_kernel(int kind, const float* __restrict__ x, const float* __restrict__ gy,
                                float* __restrict__ gx, int64_t n) {
     pdl_entry();
@@ -209,7 +211,7 @@ __global__ void act_bwd_kernel(int kind, const float* __restrict__ x, const floa
         float4* o4 = reinterpret_cast<float4*>(gx);
         for (int64_t j = i0; j < n4; j += stride) {
             const float4 a = x4[j], g = g4[j];
-            float4 o = o4[j];
+            float4 o = ASSIGN ? make_float4(0.f, 0.f, 0.f, 0.f) : o4[j];
             o.x = act_backward(kind, a.x, g.x, o.x);
             o.y = act_backward(kind, a.y, g.y, o.y);
             o.z = act_backward(kind, a.z, g.z, o.z);
@@ -218,7 +220,7 @@ __global__ void act_bwd_kernel(int kind, const float* __restrict__ x, const floa
         }
         tail = n4 << 2;
     }
-    for (int64_t j = tail + i0; j < n; j += stride) gx[j] = act_backward(kind, x[j], gy[j], gx[j]);
+    for (int64_t j = tail + i0; j < n; j += stride) gx[j] = act_backward(kind, x[j], gy[j], ASSIGN ? 0.f : gx[j]);
 }
 
 // Column sums of a [rows, cols] matrix, optionally fused with the activation
@@ -230,7 +232,7 @@ __global__ void act_bwd_kernel(int kind, const float* __restrict__ x, const floa
 // most a few dozen atomics.
 constexpr int kColWarps = 8;
 
-template <bool ACT, bool VEC>
+template <bool ACT, bool VEC, bool ASSIGN = false>
 __global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __restrict__ x,
                                                      const float* __restrict__ gy, float* __restrict__ g,
                                                      float* __restrict__ out, int64_t rows, int64_t cols,
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __re
         for (int64_t r = r_begin + warp; r < r_end; r += kColWarps) {
             const int64_t idx = r * cols + c0;
             if constexpr (VEC) {
-                float4 o = *reinterpret_cast<float4*>(g + idx);
+                float4 o = (ACT && ASSIGN) ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<float4*>(g + idx);
                 if (ACT) {
                     const float4 a = *reinterpret_cast<const float4*>(x + idx);
                     const float4 d = *reinterpret_cast<const float4*>(gy + idx);
@@ -264,7 +266,7 @@ __global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __re
                 s[2] += o.z;
                 s[3] += o.w;
             } else {
-                float o = g[idx];
+                float o = (ACT && ASSIGN) ? 0.f : g[idx];
                 if (ACT) {
                     o = act_backward(kind, x[idx], gy[idx], o);
                     g[idx] = o;
@@ -701,27 +703,44 @@ int mle_act_fwd(int kind, const float* x, float* y, int64_t n, mle_stream_t stre
     return launch_status();
 }
 
-int mle_act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n, float* bias_grad, int64_t rows,
-                int64_t cols, mle_stream_t stream) {
+extern "C++" {
+namespace {
+template <bool ASSIGN>
+int act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n, float* bias_grad, int64_t rows,
+            int64_t cols, mle_stream_t stream) {
     if (kind < 0 || kind > MLE_ACT_SIGMOID || n < 0 || (n > 0 && (!x || !gy || !gx))) return MLE_ERR_ARG;
     if (n == 0) return MLE_OK;
     if (!bias_grad) {
         if (vec_ok(n, x, gy, gx))
-            launch_k(act_bwd_kernel<true>, grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream), kind, x, gy, gx, n);
+            launch_k(act_bwd_kernel<true, ASSIGN>, grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream), kind,
+                     x, gy, gx, n);
         else
-            launch_k(act_bwd_kernel<false>, grid_for(n, kThreads), kThreads, 0, as_stream(stream), kind, x, gy, gx, n);
+            launch_k(act_bwd_kernel<false, ASSIGN>, grid_for(n, kThreads), kThreads, 0, as_stream(stream), kind, x, gy,
+                     gx, n);
         return launch_status();
     }
     if (rows <= 0 || cols <= 0 || rows * cols != n) return MLE_ERR_ARG;
     const bool vec = (cols % 4 == 0) && vec_ok(n, x, gy, gx);
     const ColsumShape sh = colsum_shape(rows, cols, vec);
     if (vec)
-        launch_k(colsum_kernel<true, true>, sh.grid, 256, 0, as_stream(stream), kind, x, gy, gx, bias_grad, rows, cols,
-                                                                          sh.rpb, 1.0f);
+        launch_k(colsum_kernel<true, true, ASSIGN>, sh.grid, 256, 0, as_stream(stream), kind, x, gy, gx, bias_grad,
+                 rows, cols, sh.rpb, 1.0f);
     else
-        launch_k(colsum_kernel<true, false>, sh.grid, 256, 0, as_stream(stream), kind, x, gy, gx, bias_grad, rows, cols,
-                                                                           sh.rpb, 1.0f);
+        launch_k(colsum_kernel<true, false, ASSIGN>, sh.grid, 256, 0, as_stream(stream), kind, x, gy, gx, bias_grad,
+                 rows, cols, sh.rpb, 1.0f);
     return launch_status();
+}
+}  // namespace
+}  // extern "C++"
+
+int mle_act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n, float* bias_grad, int64_t rows,
+                int64_t cols, mle_stream_t stream) {
+    return act_bwd<false>(kind, x, gy, gx, n, bias_grad, rows, cols, stream);
+}
+
+int mle_act_bwd_assign(int kind, const float* x, const float* gy, float* gx, int64_t n, float* bias_grad,
+                       int64_t rows, int64_t cols, mle_stream_t stream) {
+    return act_bwd<true>(kind, x, gy, gx, n, bias_grad, rows, cols, stream);
 }
 
 int mle_bias_add_fwd(const float* x, const float* bias, float* y, int64_t rows, int64_t cols, mle_stream_t stream) {

@@ -101,6 +101,30 @@ def test_activation_bwd_fused_bias(cuda, ops, orc, rng, rows, cols):
     assert rel_err(H(db), ref_db) <= 1e-4  # column sums over up to 4096 rows, reordered
 
 
+@pytest.mark.parametrize("rows,cols", [(64, 256), (33, 10), (5, 1027)])
+@pytest.mark.parametrize("fused", [False, True])
+def test_activation_bwd_assign(cuda, ops, rng, rows, cols, fused):
+    """mle_act_bwd_assign never reads gx and leaves bit for bit what
+    mle_act_bwd leaves in a cleared gx (bias column sums included)."""
+    from ml_engine_b200._lib import kernels
+    k = kernels()
+    x = T((rng.standard_normal((rows, cols)) * 3).astype(np.float32), cuda)
+    g = T(rng.standard_normal((rows, cols)).astype(np.float32), cuda)
+    n = rows * cols
+    for kind in range(6):
+        want = torch.zeros(rows, cols, device=cuda)
+        got = torch.full((rows, cols), float("nan"), device=cuda)
+        db_w, db_g = torch.zeros(cols, device=cuda), torch.zeros(cols, device=cuda)
+        st = torch.cuda.current_stream().cuda_stream
+        k.call("mle_act_bwd", kind, x.data_ptr(), g.data_ptr(), want.data_ptr(), n,
+               db_w.data_ptr() if fused else None, rows if fused else 0, cols if fused else 0, st)
+        k.call("mle_act_bwd_assign", kind, x.data_ptr(), g.data_ptr(), got.data_ptr(), n,
+               db_g.data_ptr() if fused else None, rows if fused else 0, cols if fused else 0, st)
+        assert torch.equal(got, want), kind
+        if fused:
+            assert rel_err(H(db_g), H(db_w)) <= 1e-6, kind  # column-sum atomics in any order
+
+
 @pytest.mark.parametrize("rows,cols", [(64, 256), (1000, 10), (7, 4096)])
 def test_bias_add_and_grad(cuda, ops, orc, rng, rows, cols):
     x = rng.standard_normal((rows, cols)).astype(np.float32)

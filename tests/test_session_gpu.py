@@ -300,3 +300,44 @@ def test_index_labels_match_dense_targets(cuda, rng):
         assert abs(la - lb) <= 1e-6 * abs(la)
     for i in range(len(a.param_names)):
         assert norm_err(b.read_param(i), a.read_param(i)) <= 1e-6, a.param_names[i]
+
+
+def test_first_write_assign_matches_cleared_gradients(cuda, rng):
+    """First-writer assignment (gradients the first backward writer
+    overwrites are not cleared; the loss, activations and large-input
+    Linears assign) against every gradient cleared and accumulated, over an
+    eager step and two graph replays: the same losses and gradients.  A
+    gradient left uncleared but still accumulated would be off by a whole
+    step's gradient.  The learning rate is 0, so every step sees the same
+    weights: the gradients of both runs then differ only where split-K
+    reduce-adds and column-sum atomics reorder sums (with a moving model,
+    Adam amplifies that noise in near-degenerate tensors such as the query
+    weights).  The FFN width makes the second Linear's input gradient large
+    enough to be assigned."""
+    from ml_engine_b200._lib import engine
+    kw = dict(config=2, batch=16, seq_len=256, d_model=512, heads=8, ffn=2048, layers=1, vocab=512, seed=5, lr=0.0)
+    lib = engine()
+    old = lib.mle_get_grad_first_write()
+    tokens = rng.integers(0, 512, 16 * 256).astype(np.int32)
+    targets = rng.integers(0, 512, 16 * 256).astype(np.int32)
+    runs = {}
+    try:
+        for mode in (0, 1):
+            lib.call("mle_set_grad_first_write", mode)
+            s = _session(**kw)
+            s.inputs["tokens"][:] = tokens
+            s.inputs["targets"][:] = targets
+            losses = [s.step()]
+            s.capture()
+            losses += [s.step(), s.step()]
+            runs[mode] = (s, losses, [s.read_param(i, 1) for i in range(len(s.param_names))])
+    finally:
+        lib.call("mle_set_grad_first_write", old)
+    (a, la, ga), (b, lb, gb) = runs[0], runs[1]
+    for x, y in zip(la + lb, la[:1] * 6):  # the same weights every step: the same loss
+        assert abs(x - y) <= 1e-5 * abs(y), (la, lb)
+    gnorm = np.sqrt(sum(float(np.sum(np.asarray(g, np.float64) ** 2)) for g in ga))
+    for i in range(len(a.param_names)):
+        # the query bias's exact gradient is zero (column softmax): no relative scale
+        floor = np.linalg.norm(gb[i] - ga[i]) <= 1e-7 * gnorm
+        assert norm_err(gb[i], ga[i]) <= 1e-4 or floor, (a.param_names[i], norm_err(gb[i], ga[i]))
