@@ -57,7 +57,8 @@ void prepare_fusions(const graph_tree& nodes) {
             const NodeBackProp* w = it->second;
             NodeExt& we = ext(w);
             bool ok = false;
-            if (we.kind == OP_SMCE) ok = w->inputs.size() == 2 && w->inputs[0].get() == x && w->inputs[1].get() != x;
+            if (we.kind == OP_SMCE)  // {prediction, target} or {prediction} (index labels)
+                ok = w->inputs[0].get() == x && (w->inputs.size() == 1 || w->inputs[1].get() != x);
             if (we.kind == OP_ACTIVATION) ok = w->inputs.size() == 1;
             if (we.kind == OP_LINEAR)
                 ok = w->inputs.size() == 1 && (double)x->total >= 2.0 * 148 * 128.0 * 128.0;  // 148 SMs
