@@ -165,17 +165,23 @@ __global__ void softmax_row_bwd(const float* __restrict__ y, const float* __rest
 }
 
 // ------------------------- softmax cross-entropy ---------------------------
+// x / batch_div; binv = 1 / batch_div when that is exact (a power of two),
+// then the product is the same number, else 0 and the quotient is taken.
+__device__ __forceinline__ float div_batch(float x, float batch_div, float binv) {
+    return binv != 0.0f ? x * binv : x / batch_div;
+}
+
 template <int EPT>
 __global__ void smce_fwd_cached(const float* __restrict__ logits, const float* __restrict__ target,
                                 float* __restrict__ probs, float* __restrict__ loss, float* __restrict__ grad,
-                                float batch_div, int cols, double total) {
+                                float batch_div, float binv, int cols, double total) {
     pdl_entry();
     __shared__ float scratch[32];
     __shared__ double dscratch[32];
     const int64_t row = blockIdx.x;
     float v[EPT];
     load_row<EPT>(logits + row * cols, cols, v);
-    const float s = row_softmax_regs<EPT>(v, cols, 0, 0, scratch);
+    const float inv_s = 1.0f / row_softmax_regs<EPT>(v, cols, 0, 0, scratch);
     double part = 0.0;
 #pragma unroll
     for (int k = 0; k < EPT / 4; ++k) {
@@ -186,11 +192,11 @@ __global__ void smce_fwd_cached(const float* __restrict__ logits, const float* _
             float p[4], g[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                p[j] = v[4 * k + j] / s;
+                p[j] = v[4 * k + j] * inv_s;
                 // -t*log(p+1e-27) is -0 where t == 0, so skipping those terms
                 // leaves the double sum unchanged.
                 if (tt[j] != 0.0f) part += -(double)tt[j] * log((double)p[j] + 1e-27);
-                g[j] = (p[j] + (-1.0f) * tt[j]) / batch_div;
+                g[j] = div_batch(p[j] + (-1.0f) * tt[j], batch_div, binv);
             }
             if (probs) *reinterpret_cast<float4*>(probs + row * cols + c) = make_float4(p[0], p[1], p[2], p[3]);
             if (grad) *reinterpret_cast<float4*>(grad + row * cols + c) = make_float4(g[0], g[1], g[2], g[3]);
@@ -207,16 +213,14 @@ __global__ void smce_fwd_cached(const float* __restrict__ logits, const float* _
 template <int EPT>
 __global__ void smce_index_fwd_cached(const float* __restrict__ logits, const int32_t* __restrict__ labels,
                                       float* __restrict__ probs, float* __restrict__ loss, float* __restrict__ grad,
-                                      float batch_div, int cols, double total) {
+                                      float batch_div, float binv, int cols, double total) {
     pdl_entry();
     __shared__ float scratch[32];
-    __shared__ double dscratch[32];
     const int64_t row = blockIdx.x;
     const int label = labels[row];
     float v[EPT];
     load_row<EPT>(logits + row * cols, cols, v);
-    const float s = row_softmax_regs<EPT>(v, cols, 0, 0, scratch);
-    double part = 0.0;
+    const float inv_s = 1.0f / row_softmax_regs<EPT>(v, cols, 0, 0, scratch);
 #pragma unroll
     for (int k = 0; k < EPT / 4; ++k) {
         const int c = (k * blockDim.x + threadIdx.x) * 4;
@@ -224,22 +228,22 @@ __global__ void smce_index_fwd_cached(const float* __restrict__ logits, const in
             float p[4], g[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                p[j] = v[4 * k + j] / s;
+                p[j] = v[4 * k + j] * inv_s;
                 const float tt = (c + j == label) ? 1.0f : 0.0f;
-                if (tt != 0.0f) part += -(double)tt * log((double)p[j] + 1e-27);
-                g[j] = (p[j] + (-1.0f) * tt) / batch_div;
+                // the row's one loss term (the dense kernel's block sum of
+                // this term and zeros is this term), from the thread holding it
+                if (tt != 0.0f) atomicAdd(loss, (float)(-(double)tt * log((double)p[j] + 1e-27) / total));
+                g[j] = div_batch(p[j] + (-1.0f) * tt, batch_div, binv);
             }
             if (probs) *reinterpret_cast<float4*>(probs + row * cols + c) = make_float4(p[0], p[1], p[2], p[3]);
             if (grad) *reinterpret_cast<float4*>(grad + row * cols + c) = make_float4(g[0], g[1], g[2], g[3]);
         }
     }
-    part = block_sum(part, dscratch);
-    if (threadIdx.x == 0) atomicAdd(loss, (float)(part / total));
 }
 
 __global__ void smce_index_bwd_kernel(const float* __restrict__ probs, const int32_t* __restrict__ labels,
                                       const float* __restrict__ upstream, float* __restrict__ grad, float batch_div,
-                                      int cols, int64_t n) {
+                                      float binv, int cols, int64_t n) {
     pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -247,13 +251,13 @@ __global__ void smce_index_bwd_kernel(const float* __restrict__ probs, const int
         const float tt = (int)(i - row * cols) == labels[row] ? 1.0f : 0.0f;
         float g = probs[i] + (-1.0f) * tt;
         if (upstream) g *= upstream[0];
-        grad[i] = g / batch_div;
+        grad[i] = div_batch(g, batch_div, binv);
     }
 }
 
 __global__ void smce_fwd_generic(const float* __restrict__ logits, const float* __restrict__ target,
                                  float* __restrict__ probs, float* __restrict__ loss, float* __restrict__ grad,
-                                 float batch_div, int cols, double total) {
+                                 float batch_div, float binv, int cols, double total) {
     pdl_entry();
     __shared__ float scratch[32];
     __shared__ double dscratch[32];
@@ -276,12 +280,13 @@ __global__ void smce_fwd_generic(const float* __restrict__ logits, const float* 
     s = block_sum(s, scratch);
     if (s < 1e-45f) s = 1.0f;
     double part = 0.0;
+    const float inv_s = 1.0f / s;
     for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-        const float p = expf(xr[c] - m) / s;
+        const float p = expf(xr[c] - m) * inv_s;
         const float t = tr[c];
         if (t != 0.0f) part += -(double)t * log((double)p + 1e-27);
         if (probs) probs[row * cols + c] = p;
-        if (grad) grad[row * cols + c] = (p + (-1.0f) * t) / batch_div;
+        if (grad) grad[row * cols + c] = div_batch(p + (-1.0f) * t, batch_div, binv);
     }
     part = block_sum(part, dscratch);
     if (threadIdx.x == 0) atomicAdd(loss, (float)(part / total));
@@ -289,13 +294,13 @@ __global__ void smce_fwd_generic(const float* __restrict__ logits, const float* 
 
 __global__ void smce_bwd_kernel(const float* __restrict__ probs, const float* __restrict__ target,
                                 const float* __restrict__ upstream, float* __restrict__ grad, float batch_div,
-                                int64_t n) {
+                                float binv, int64_t n) {
     pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
         float g = probs[i] + (-1.0f) * target[i];
         if (upstream) g *= upstream[0];
-        grad[i] = g / batch_div;
+        grad[i] = div_batch(g, batch_div, binv);
     }
 }
 
@@ -372,6 +377,17 @@ int mle_softmax_bwd(const float* y, const float* gy, float* gx, int64_t bc, int 
     return launch_status();
 }
 
+}  // extern "C"
+
+// 1 / b when it is exact (b a power of two), else 0 (see div_batch)
+static float exact_inverse(float b) {
+    int e = 0;
+    const float m = frexpf(b, &e);
+    return (m == 0.5f || m == -0.5f) ? 1.0f / b : 0.0f;
+}
+
+extern "C" {
+
 int mle_softmax_ce_fwd(const float* logits, const float* target, float* probs, float* loss, float* grad,
                        float batch_div, int64_t rows, int cols, mle_stream_t stream) {
     if (rows < 0 || cols <= 0 || !logits || !target || !loss || batch_div == 0.0f) return MLE_ERR_ARG;
@@ -379,23 +395,22 @@ int mle_softmax_ce_fwd(const float* logits, const float* target, float* probs, f
     if (cudaMemsetAsync(loss, 0, sizeof(float), st) != cudaSuccess) return launch_status();
     if (rows == 0) return MLE_OK;
     const double total = (double)rows * (double)cols;
+    const float binv = exact_inverse(batch_div);
     const bool vec = cols % 4 == 0 && aligned16(logits) && aligned16(target) && (!probs || aligned16(probs)) &&
                      (!grad || aligned16(grad));
     if (vec && cols <= 4 * kRowThreads)
-        launch_k(smce_fwd_cached<4>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, cols,
-                                                                  total);
+        launch_k(smce_fwd_cached<4>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, binv, cols, total);
     else if (vec && cols <= 8 * kRowThreads)
-        launch_k(smce_fwd_cached<8>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, cols,
-                                                                  total);
+        launch_k(smce_fwd_cached<8>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, binv, cols, total);
     else if (vec && cols <= 16 * kRowThreads)
-        launch_k(smce_fwd_cached<16>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div,
-                                                                   cols, total);
+        launch_k(smce_fwd_cached<16>, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, binv,
+                 cols, total);
     else if (vec && cols <= 32 * kRowThreads)  // two threads' share per thread of a 512-thread block
         launch_k(smce_fwd_cached<16>, (unsigned)rows, 2 * kRowThreads, 0, st, logits, target, probs, loss, grad,
-                 batch_div, cols, total);
+                 batch_div, binv, cols, total);
     else
-        launch_k(smce_fwd_generic, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, cols,
-                                                                 total);
+        launch_k(smce_fwd_generic, (unsigned)rows, kRowThreads, 0, st, logits, target, probs, loss, grad, batch_div, binv, cols,
+                 total);
     return launch_status();
 }
 
@@ -408,18 +423,19 @@ int mle_softmax_ce_index_fwd(const float* logits, const int32_t* labels, float* 
     if (cudaMemsetAsync(loss, 0, sizeof(float), st) != cudaSuccess) return launch_status();
     if (rows == 0) return MLE_OK;
     const double total = (double)rows * (double)cols;
+    const float binv = exact_inverse(batch_div);
     if (cols <= 4 * kRowThreads)
         launch_k(smce_index_fwd_cached<4>, (unsigned)rows, kRowThreads, 0, st, logits, labels, probs, loss, grad,
-                 batch_div, cols, total);
+                 batch_div, binv, cols, total);
     else if (cols <= 8 * kRowThreads)
         launch_k(smce_index_fwd_cached<8>, (unsigned)rows, kRowThreads, 0, st, logits, labels, probs, loss, grad,
-                 batch_div, cols, total);
+                 batch_div, binv, cols, total);
     else if (cols <= 16 * kRowThreads)
         launch_k(smce_index_fwd_cached<16>, (unsigned)rows, kRowThreads, 0, st, logits, labels, probs, loss, grad,
-                 batch_div, cols, total);
+                 batch_div, binv, cols, total);
     else
         launch_k(smce_index_fwd_cached<16>, (unsigned)rows, 2 * kRowThreads, 0, st, logits, labels, probs, loss, grad,
-                 batch_div, cols, total);
+                 batch_div, binv, cols, total);
     return launch_status();
 }
 
@@ -429,7 +445,7 @@ int mle_softmax_ce_index_bwd(const float* probs, const int32_t* labels, const fl
     const int64_t n = rows * cols;
     if (n == 0) return MLE_OK;
     launch_k(smce_index_bwd_kernel, grid_for(n, 256), 256, 0, as_stream(stream), probs, labels, upstream, grad,
-             batch_div, cols, n);
+             batch_div, exact_inverse(batch_div), cols, n);
     return launch_status();
 }
 
@@ -437,7 +453,8 @@ int mle_softmax_ce_bwd(const float* probs, const float* target, const float* ups
                        int64_t n, mle_stream_t stream) {
     if (n < 0 || !probs || !target || !grad || batch_div == 0.0f) return MLE_ERR_ARG;
     if (n == 0) return MLE_OK;
-    launch_k(smce_bwd_kernel, grid_for(n, 256), 256, 0, as_stream(stream), probs, target, upstream, grad, batch_div, n);
+    launch_k(smce_bwd_kernel, grid_for(n, 256), 256, 0, as_stream(stream), probs, target, upstream, grad, batch_div,
+             exact_inverse(batch_div), n);
     return launch_status();
 }
 
