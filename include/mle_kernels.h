@@ -100,6 +100,11 @@ int mle_accumulate(const float* x, float* y, int64_t n, double scale, mle_stream
 /* ga += g; gb += g in one pass.  Replaces the two Accumulate launches of
  * GraphOperations::Add backward (Engine/engine.cu:1659-1667). */
 int mle_add_bwd(const float* g, float* ga, float* gb, int64_t n, mle_stream_t stream);
+/* The same with ga (assign_mask bit 0) and/or gb (bit 1) written instead of
+ * accumulated: bitwise what mle_add_bwd leaves in cleared buffers.  For the
+ * first writer of a gradient buffer that is not cleared between steps;
+ * ga == gb with an assign bit is MLE_ERR_ARG. */
+int mle_add_bwd_assign(const float* g, float* ga, float* gb, int64_t n, int assign_mask, mle_stream_t stream);
 
 /* y[i] = scale * x[i].  Replaces Scale_Write (Engine/kernels.cu:1677-1682),
  * the forward of Scale (Engine/engine.cu:2533-2538). */
@@ -437,6 +442,16 @@ int mle_attention_bwd(const float* Q, const float* K, const float* V, const floa
                       float* dS_out, float* workspace, int batch, int heads, int seq_q, int seq_k,
                       int head_dim, float scale, int causal, int softmax_axis, int key_grad_mode,
                       int layout, mle_stream_t stream);
+/* The same with dQ (assign_mask bit 0), dK (bit 1) and/or dV (bit 2)
+ * written instead of accumulated: the tensor-core path writes them with
+ * beta = 0 products, the other paths clear them and accumulate.  For the
+ * first writer of gradient buffers that are not cleared between steps;
+ * an assigned gradient may not alias another one (MLE_ERR_ARG). */
+int mle_attention_bwd_assign(const float* Q, const float* K, const float* V, const float* P,
+                             const float* dO, float* dQ, float* dK, float* dV, float* dP_out, float* dS_out,
+                             float* workspace, int batch, int heads, int seq_q, int seq_k, int head_dim,
+                             float scale, int causal, int softmax_axis, int key_grad_mode, int layout,
+                             int assign_mask, mle_stream_t stream);
 
 /* 1 if mle_attention_fwd/bwd take the fused path for these sizes (any
  * layout), 0 if they need the head-major composed path. */

@@ -38,6 +38,8 @@ enum OpKind {
     OP_LINEAR = 1,
     OP_ACTIVATION = 2,
     OP_SMCE = 3,
+    OP_ATTENTION = 4,  // ScaledDotAttention on the token-major kernels
+    OP_ADD = 5,
 };
 
 // Per-node fusion state decided by prepare_fusions() before a backward pass.
@@ -48,7 +50,7 @@ struct NodeExt {
     float* fused_bias_target = nullptr;  // activation: bias grad to accumulate
     long long fused_rows = 0, fused_cols = 0;
     std::vector<float*> param_grads;     // parameter gradients complete once this node's backward ran
-    bool assign_input_grad = false;      // this node's backward writes (not adds to) its input's gradient
+    int assign_inputs = 0;               // bit i: backward writes (not adds to) inputs[i]'s gradient
 };
 NodeExt& ext(const NodeBackProp* n);
 void forget_ext(const NodeBackProp* n);
@@ -58,8 +60,9 @@ void forget_ext(const NodeBackProp* n);
 // else adds that Linear's BCompress (column sums) to its own backward pass.
 // Also finds gradients whose first writer in the backward walk (the
 // consumer last in topological order) overwrites the whole buffer: a
-// loss node, an activation, or a Linear with a large input gradient.  That
-// writer assigns (assign_input_grad) and zero_grad leaves the buffer alone.
+// loss node, an activation, an Add, the token-major attention, or a Linear
+// with a large input gradient.  That writer assigns (assign_inputs) and
+// zero_grad leaves the buffer alone.
 void prepare_fusions(const graph_tree& nodes);
 
 // Gradient buffers zero_range skips (their first writer assigns them).

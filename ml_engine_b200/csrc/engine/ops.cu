@@ -41,13 +41,15 @@ void prepare_fusions(const graph_tree& nodes) {
         NodeExt& e = ext(n.get());
         if (e.kind == OP_LINEAR) e.bias_grad_fused = false;
         if (e.kind == OP_ACTIVATION) e.fused_bias_target = nullptr;
-        e.assign_input_grad = false;
+        e.assign_inputs = 0;
     }
     // first writers that overwrite the whole input gradient: the loss
     // (SoftMaxCrossEntropy assigns its prediction's gradient), an
-    // activation, and a Linear whose input gradient spans at least two
-    // waves of 128 x 128 tiles (its product then never splits K, so the
-    // assigned GEMM costs no memset of its own)
+    // activation, an Add, the token-major attention (dQ, dK, dV), and a
+    // Linear whose input gradient spans at least two waves of 128 x 128
+    // tiles (its product then never splits K, so the assigned GEMM costs no
+    // memset of its own).  The input must appear once among the writer's
+    // inputs.
     std::vector<const float*> pre;
     if (first_write_assign()) {
         for (auto& n : nodes) {
@@ -56,14 +58,21 @@ void prepare_fusions(const graph_tree& nodes) {
             if (it == first_writer.end() || !x->grad) continue;
             const NodeBackProp* w = it->second;
             NodeExt& we = ext(w);
+            int pos = -1, seen = 0;
+            for (size_t i = 0; i < w->inputs.size(); ++i)
+                if (w->inputs[i].get() == x) {
+                    pos = (int)i;
+                    ++seen;
+                }
+            if (seen != 1) continue;
             bool ok = false;
-            if (we.kind == OP_SMCE)  // {prediction, target} or {prediction} (index labels)
-                ok = w->inputs[0].get() == x && (w->inputs.size() == 1 || w->inputs[1].get() != x);
-            if (we.kind == OP_ACTIVATION) ok = w->inputs.size() == 1;
-            if (we.kind == OP_LINEAR)
-                ok = w->inputs.size() == 1 && (double)x->total >= 2.0 * 148 * 128.0 * 128.0;  // 148 SMs
+            if (we.kind == OP_SMCE) ok = pos == 0;  // {prediction, target} or {prediction} (index labels)
+            if (we.kind == OP_ACTIVATION) ok = pos == 0;
+            if (we.kind == OP_ADD) ok = pos <= 1;
+            if (we.kind == OP_ATTENTION) ok = pos <= 2;
+            if (we.kind == OP_LINEAR) ok = pos == 0 && (double)x->total >= 2.0 * 148 * 128.0 * 128.0;  // 148 SMs
             if (!ok) continue;
-            if (we.kind != OP_SMCE) we.assign_input_grad = true;
+            if (we.kind != OP_SMCE) we.assign_inputs |= 1 << pos;
             pre.push_back(x->grad);
         }
     }
@@ -262,6 +271,7 @@ graph GraphOperations::Add(const graph& A, const graph& B, const bool last) {
     node->inputs = {A, B};
     GB += (double)node->total * sizeof(float) / (1ULL << 30);
     NodeBackProp *nd = node.get(), *ap = A.get(), *bp = B.get();
+    ext(nd).kind = OP_ADD;
     node->forward = [=]() {
         check(mle_scale_add(ap->output, bp->output, nd->output, 1.0f, nd->total, st()), "Add forward");
         if (last && g_loss_readback) {
@@ -275,7 +285,8 @@ graph GraphOperations::Add(const graph& A, const graph& B, const bool last) {
             check(mle_accumulate(nd->grad, ap->grad, nd->total, 1.0, st()), "Add backward A");
             check(mle_accumulate(nd->grad, bp->grad, nd->total, 1.0, st()), "Add backward B");
         } else {
-            check(mle_add_bwd(nd->grad, ap->grad, bp->grad, nd->total, st()), "Add backward");
+            check(mle_add_bwd_assign(nd->grad, ap->grad, bp->grad, nd->total, ext(nd).assign_inputs & 3, st()),
+                  "Add backward");
         }
     };
     node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
@@ -507,7 +518,7 @@ static graph act_node(const char* name, int kind, const graph& input) {
     node->forward = [=]() { check(mle_act_fwd(kind, ip->output, nd->output, nd->total, st()), str(name) + " forward"); };
     node->backward = [=]() {
         const NodeExt& e = ext(nd);
-        check((e.assign_input_grad ? mle_act_bwd_assign : mle_act_bwd)(kind, ip->output, nd->grad, ip->grad,
+        check(((e.assign_inputs & 1) ? mle_act_bwd_assign : mle_act_bwd)(kind, ip->output, nd->grad, ip->grad,
                                                                         nd->total, e.fused_bias_target, e.fused_rows,
                                                                         e.fused_cols, st()),
               str(name) + " backward");
@@ -629,10 +640,11 @@ graph GraphOperations::ScaledDotAttention(const graph& Q, const graph& K, const 
                                     causal, axis, MLE_ATTN_TOKEN_MAJOR, st()),
                   "Attention forward");
         };
+        ext(nd).kind = OP_ATTENTION;
         node->backward = [=]() {
-            check(mle_attention_bwd(qp->output, kp->output, vp->output, P, nd->grad, qp->grad, kp->grad, vp->grad,
-                                    nullptr, nullptr, ws, B, heads, Sq, Sk, hd, scale, causal, axis, key_grad_mode,
-                                    MLE_ATTN_TOKEN_MAJOR, st()),
+            check(mle_attention_bwd_assign(qp->output, kp->output, vp->output, P, nd->grad, qp->grad, kp->grad,
+                                           vp->grad, nullptr, nullptr, ws, B, heads, Sq, Sk, hd, scale, causal, axis,
+                                           key_grad_mode, MLE_ATTN_TOKEN_MAJOR, ext(nd).assign_inputs & 7, st()),
                   "Attention backward");
         };
         node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
@@ -727,7 +739,7 @@ graph Linear::forward(const graph& X) {
         const bool fused = ext(nd).bias_grad_fused;
         // dW and dB on the parameter-gradient stream, concurrent with dX
         void* ps = (void*)fork_param_stream();
-        if (ext(nd).assign_input_grad)  // first writer of dX: dX = dY W^T
+        if (ext(nd).assign_inputs & 1)  // first writer of dX: dX = dY W^T
             check(mle_gemm(nd->grad, W->output, xp->grad, nullptr, 1, rows, n, p, p, p, n, 0, 0, 0, 0, 1, 1.0f, 0.0f,
                            st()),
                   "MatMul... in " + nd->op_name + " backward");

@@ -887,9 +887,11 @@ int tc_attention_fwd(const float* Q, const float* K, const float* V, float* P, f
     return run_gemm(attn_gemm(P, V, O, Sq, hd, Sk, Sk, ks, qs, 0, 0, B, H, pb, ph, kb, kh, qb, qh, 1.0f, 0), st);
 }
 
+// assign: bit 0 dQ, bit 1 dK, bit 2 dV written (not accumulated)
 int tc_attention_bwd(const float* Q, const float* K, const float* V, const float* P, const float* dO, float* dQ,
                      float* dK, float* dV, float* dP_out, float* dS_out, float* W, int B, int H, int Sq, int Sk,
-                     int hd, float scale, int key_mode, int layout, cudaStream_t st) {
+                     int hd, float scale, int key_mode, int layout, cudaStream_t st, int assign = 0) {
+    const int mq = (assign & 1) ? 0 : 1, mk = (assign & 2) ? 0 : 1, mv = (assign & 4) ? 0 : 1;
     int64_t qb, qh, qs, kb, kh, ks;
     strides_for(layout, H, Sq, hd, qb, qh, qs);
     strides_for(layout, H, Sk, hd, kb, kh, ks);
@@ -903,19 +905,19 @@ int tc_attention_bwd(const float* Q, const float* K, const float* V, const float
     if (s) return s;
     if (dS_out && (s = mle_accumulate(W, dS_out, ns, 1.0, st)) != 0) return s;
     // dV += P^T dO
-    s = run_gemm(attn_gemm(P, dO, dV, Sk, hd, Sq, Sk, qs, ks, 1, 0, B, H, pb, ph, qb, qh, kb, kh, 1.0f, 1), st);
+    s = run_gemm(attn_gemm(P, dO, dV, Sk, hd, Sq, Sk, qs, ks, 1, 0, B, H, pb, ph, qb, qh, kb, kh, 1.0f, mv), st);
     if (s) return s;
     // dQ += scale W K
-    s = run_gemm(attn_gemm(W, K, dQ, Sq, hd, Sk, Sk, ks, qs, 0, 0, B, H, pb, ph, kb, kh, qb, qh, scale, 1), st);
+    s = run_gemm(attn_gemm(W, K, dQ, Sq, hd, Sk, Sk, ks, qs, 0, 0, B, H, pb, ph, kb, kh, qb, qh, scale, mq), st);
     if (s) return s;
     if (key_mode == MLE_KEYGRAD_TRUE)  // dK += scale W^T Q
-        return run_gemm(attn_gemm(W, Q, dK, Sk, hd, Sq, Sk, qs, ks, 1, 0, B, H, pb, ph, qb, qh, kb, kh, scale, 1),
+        return run_gemm(attn_gemm(W, Q, dK, Sk, hd, Sq, Sk, qs, ks, 1, 0, B, H, pb, ph, qb, qh, kb, kh, scale, mk),
                         st);
     // reference: the head block of dK receives scale * Q^T M^T as [hd, Sk],
     // M = W's memory read as [Sk, Sq]; block element (d, i) lives at row
     // d*(Sk/hd) + i/hd, column i % hd of the head in `layout`
     GemmProblem g = attn_gemm(Q, W, dK, hd, Sk, Sq, qs, Sq, (int64_t)(Sk / hd) * ks, 1, 1, B, H, qb, qh, pb, ph, kb,
-                              kh, scale, 1);
+                              kh, scale, mk);
     g.c_split = hd;
     g.c_split_ld = ks;
     return run_gemm(g, st);
@@ -993,7 +995,18 @@ int mle_attention_bwd(const float* Q, const float* K, const float* V, const floa
                       float* dK, float* dV, float* dP_out, float* dS_out, float* workspace, int batch, int heads,
                       int seq_q, int seq_k, int head_dim, float scale, int causal, int softmax_axis,
                       int key_grad_mode, int layout, mle_stream_t stream) {
+    return mle_attention_bwd_assign(Q, K, V, P, dO, dQ, dK, dV, dP_out, dS_out, workspace, batch, heads, seq_q, seq_k,
+                                    head_dim, scale, causal, softmax_axis, key_grad_mode, layout, 0, stream);
+}
+
+int mle_attention_bwd_assign(const float* Q, const float* K, const float* V, const float* P, const float* dO,
+                             float* dQ, float* dK, float* dV, float* dP_out, float* dS_out, float* workspace,
+                             int batch, int heads, int seq_q, int seq_k, int head_dim, float scale, int causal,
+                             int softmax_axis, int key_grad_mode, int layout, int assign_mask, mle_stream_t stream) {
     (void)causal;  // P is exactly zero where the mask applied, so dS is too
+    if (assign_mask < 0 || assign_mask > 7) return MLE_ERR_ARG;
+    if ((dQ == dK && (assign_mask & 3)) || (dQ == dV && (assign_mask & 5)) || (dK == dV && (assign_mask & 6)))
+        return MLE_ERR_ARG;  // an assigned gradient may not also receive another one
     if (!Q || !K || !V || !P || !dO || !dQ || !dK || !dV) return MLE_ERR_ARG;
     if (batch <= 0 || heads <= 0 || seq_q <= 0 || seq_k <= 0 || head_dim <= 0) return MLE_ERR_ARG;
     if ((softmax_axis != 0 && softmax_axis != 1) || (layout != MLE_ATTN_HEAD_MAJOR && layout != MLE_ATTN_TOKEN_MAJOR))
@@ -1006,9 +1019,16 @@ int mle_attention_bwd(const float* Q, const float* K, const float* V, const floa
         tc_attention_ok(softmax_axis, seq_q, seq_k, head_dim, (int64_t)batch * heads, true, key_grad_mode) &&
         ptrs_aligned({Q, K, V, P, dO, dQ, dK, dV, workspace})) {
         const int s = tc_attention_bwd(Q, K, V, P, dO, dQ, dK, dV, dP_out, dS_out, workspace, batch, heads, seq_q,
-                                       seq_k, head_dim, scale, key_grad_mode, layout, st);
+                                       seq_k, head_dim, scale, key_grad_mode, layout, st, assign_mask);
         if (s != MLE_ERR_UNSUPPORTED) return s;
     }
+    // the other paths accumulate: assigned gradients start cleared
+    const size_t nq = sizeof(float) * (size_t)batch * heads * seq_q * head_dim;
+    const size_t nk = sizeof(float) * (size_t)batch * heads * seq_k * head_dim;
+    if (((assign_mask & 1) && cudaMemsetAsync(dQ, 0, nq, st) != cudaSuccess) ||
+        ((assign_mask & 2) && cudaMemsetAsync(dK, 0, nk, st) != cudaSuccess) ||
+        ((assign_mask & 4) && cudaMemsetAsync(dV, 0, nk, st) != cudaSuccess))
+        return launch_status();
     const bool ref_shape_ok = key_grad_mode == MLE_KEYGRAD_TRUE || seq_q == seq_k;
     if (fused_ok(softmax_axis, seq_q, seq_k, head_dim, batch, heads) && ref_shape_ok &&
         ptrs_aligned({Q, K, V, dO, dQ, dK, dV})) {

@@ -145,6 +145,39 @@ __global__ void map_kernel(const float* __restrict__ x, const float* __restrict_
     }
 }
 
+// AA / AB: ga / gb assigned (their previous contents count as zero: the
+// result is bitwise 0 + g, as accumulating into a cleared buffer).
+template <bool VEC, bool AA, bool AB>
+__global__ void add_bwd_kernel_t(const float* __restrict__ g, float* __restrict__ ga,
+                                 float* __restrict__ gb, int64_t n) {
+    pdl_entry();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    int64_t tail = 0;
+    if (VEC) {
+        const int64_t n4 = n >> 2;
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        float4* a4 = reinterpret_cast<float4*>(ga);
+        float4* b4 = reinterpret_cast<float4*>(gb);
+        for (int64_t j = i0; j < n4; j += stride) {
+            const float4 v = g4[j];
+            float4 a = AA ? z : a4[j];
+            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+            a4[j] = a;
+            float4 b = AB ? z : b4[j];
+            b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
+            b4[j] = b;
+        }
+        tail = n4 << 2;
+    }
+    for (int64_t j = tail + i0; j < n; j += stride) {
+        const float v = g[j];
+        ga[j] = (AA ? 0.f : ga[j]) + v;
+        gb[j] = (AB ? 0.f : gb[j]) + v;
+    }
+}
+
 template <bool VEC>
 __global__ void add_bwd_kernel(const float* __restrict__ g, float* __restrict__ ga,
                                float* __restrict__ gb, int64_t n) {
@@ -690,6 +723,28 @@ int mle_add_bwd(const float* g, float* ga, float* gb, int64_t n, mle_stream_t st
         launch_k(add_bwd_kernel<true>, grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream), g, ga, gb, n);
     else
         launch_k(add_bwd_kernel<false>, grid_for(n, kThreads), kThreads, 0, as_stream(stream), g, ga, gb, n);
+    return launch_status();
+}
+
+int mle_add_bwd_assign(const float* g, float* ga, float* gb, int64_t n, int assign_mask, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && (!g || !ga || !gb)) || assign_mask < 0 || assign_mask > 3) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    if (assign_mask == 0) return mle_add_bwd(g, ga, gb, n, stream);
+    if (ga == gb) return MLE_ERR_ARG;  // x + x accumulates twice into one buffer
+    const bool vec = vec_ok(n, g, ga, gb);
+    const unsigned grid = vec ? grid_for(n / 4 + 1, kThreads) : grid_for(n, kThreads);
+    cudaStream_t st = as_stream(stream);
+#define MLE_ADDB(V, A, B) launch_k(add_bwd_kernel_t<V, A, B>, grid, kThreads, 0, st, g, ga, gb, n)
+    if (vec) {
+        if (assign_mask == 1) MLE_ADDB(true, true, false);
+        else if (assign_mask == 2) MLE_ADDB(true, false, true);
+        else MLE_ADDB(true, true, true);
+    } else {
+        if (assign_mask == 1) MLE_ADDB(false, true, false);
+        else if (assign_mask == 2) MLE_ADDB(false, false, true);
+        else MLE_ADDB(false, true, true);
+    }
+#undef MLE_ADDB
     return launch_status();
 }
 

@@ -630,6 +630,53 @@ def test_attention_bwd(cuda, ops, orc, rng, case, key_mode, layout, attn_path):
     assert rel_err(back(H(dK)) - dK0, rdK) <= tol
 
 
+@pytest.mark.parametrize("case", [(2, 8, 128, 128, 32, 1, 0), (2, 4, 64, 64, 64, 1, 1)])
+@pytest.mark.parametrize("mask", [1, 2, 4, 7])
+def test_attention_bwd_assign(cuda, ops, rng, attn_path, case, mask):
+    """mle_attention_bwd_assign writes the gradients of its mask over
+    whatever they held and accumulates the others: the same results as
+    mle_attention_bwd into cleared buffers (the tensor-core products may
+    tile the beta = 0 form differently, hence the 1e-6)."""
+    from ml_engine_b200._lib import kernels
+    B, Hh, Sq, Sk, D, axis, causal = case
+    bh = B * Hh
+    Q, K, V, dO = (T(_to_token_major(x, B, Hh), cuda) for x in _attn_inputs(rng, B, Hh, Sq, Sk, D))
+    scale = float(1.0 / np.sqrt(D))
+    P = torch.empty(bh, Sq, Sk, device=cuda)
+    O = torch.empty_like(Q)
+    ops.attention_fwd(Q, K, V, P, O, B, Hh, Sq, Sk, D, scale, causal, axis, 1)
+    old = [T(rng.standard_normal(t.numel()).astype(np.float32).reshape(t.shape), cuda) for t in (Q, K, K)]
+    want = [torch.zeros_like(t) if mask >> i & 1 else t.clone() for i, t in enumerate(old)]
+    ws = torch.empty(bh * Sq * Sk, device=cuda)
+    st = torch.cuda.current_stream().cuda_stream
+    k = kernels()
+    p = [x.data_ptr() for x in (Q, K, V, P, dO)]
+    k.call("mle_attention_bwd", *p, *[t.data_ptr() for t in want], None, None, ws.data_ptr(), B, Hh, Sq, Sk, D,
+           ctypes.c_float(scale), causal, axis, 0, 1, st)
+    got = [t.clone() for t in old]
+    k.call("mle_attention_bwd_assign", *p, *[t.data_ptr() for t in got], None, None, ws.data_ptr(), B, Hh, Sq, Sk, D,
+           ctypes.c_float(scale), causal, axis, 0, 1, mask, st)
+    for i in range(3):
+        assert rel_err(H(got[i]), H(want[i])) <= 1e-6, i
+
+
+@pytest.mark.parametrize("mask", [0, 1, 2, 3])
+def test_add_bwd_assign(cuda, ops, rng, mask):
+    """Add backward with assigned outputs: bit for bit the accumulation
+    into cleared buffers; the others still accumulate."""
+    from ml_engine_b200._lib import kernels
+    for n in (4099, 1 << 16):
+        g = T(rng.standard_normal(n).astype(np.float32), cuda)
+        a0, b0 = (T(rng.standard_normal(n).astype(np.float32), cuda) for _ in range(2))
+        wa = torch.zeros_like(a0) if mask & 1 else a0.clone()
+        wb = torch.zeros_like(b0) if mask & 2 else b0.clone()
+        ops.add_bwd(g, wa, wb)
+        ga, gb = a0.clone(), b0.clone()
+        kernels().call("mle_add_bwd_assign", g.data_ptr(), ga.data_ptr(), gb.data_ptr(), n, mask,
+                       torch.cuda.current_stream().cuda_stream)
+        assert torch.equal(ga, wa) and torch.equal(gb, wb)
+
+
 def test_matpe_table_matches_direct(cuda, ops, rng):
     B, S, D = 3, 50, 64
     x = rng.standard_normal(B * S * D).astype(np.float32)
