@@ -326,6 +326,12 @@ int mle_gemm_last_stage_kblocks(void);
  * thread; no counterpart in the reference. */
 int mle_set_gemm_operand_rounding(int mode);
 int mle_get_gemm_operand_rounding(void);
+/* Forces the tile width (64, 128 or 256), the split-K count (1..64, as
+ * many as the k-blocks allow) and CTA pairs (0/1) of this thread's plain
+ * and grouped tensor-core products (convolutions keep the tile model);
+ * bn = 0 returns to the tile model.  A measurement aid for tuning the
+ * model; no counterpart in the reference. */
+int mle_set_gemm_tiles(int bn, int splits, int pair);
 /* out3 = {tile width, split-K count, 1 if CTA pairs} of this thread's last
  * single tensor-core product (diagnostics for tests and benchmarks). */
 int mle_gemm_last_choice(int* out3);

@@ -1040,6 +1040,21 @@ static thread_local int g_operand_round = 1;
 // (1 forces one k-block per stage everywhere)
 static thread_local int g_stage_kblocks = 2;
 static thread_local int g_last_kpl = 1;
+// forced (tile width, split-K count, CTA pair) for plain products; width 0:
+// the tile model decides
+static thread_local int g_force_tiles[3] = {0, 0, 0};
+
+// (after the tile model; split-K only where every problem may split, never
+// for split-column outputs)
+static bool may_split_all(const GemmProblem* ps, int n);
+static void apply_forced_tiles(const GemmProblem* ps, int n, int& BN, int& splits, bool& pair) {
+    if (g_force_tiles[0] == 0) return;
+    for (int i = 0; i < n; ++i)
+        if (ps[i].c_split) return;
+    BN = g_force_tiles[0];
+    splits = may_split_all(ps, n) ? g_force_tiles[1] : 1;
+    pair = g_force_tiles[2] != 0;
+}
 
 static CUtensorMapDataType operand_type() {
     return g_operand_round ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -1322,6 +1337,16 @@ int dispatch(const tc::GemmGroup& grp, bool A_MN, bool B_MN, int BN, cudaStream_
 
 bool tc_path(const GemmProblem& p) { return p.K > 0 && g_gemm_mode == MLE_GEMM_MODE_TF32 && tc_eligible(p); }
 
+}  // namespace
+
+static bool may_split_all(const GemmProblem* ps, int n) {
+    for (int i = 0; i < n; ++i)
+        if (!may_split(ps[i])) return false;
+    return true;
+}
+
+namespace {
+
 // Both operands have a split view (contiguous extent a multiple of 32):
 // the product may stage two k-blocks per copy.
 bool split_ok(const GemmProblem& p) {
@@ -1341,6 +1366,7 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     int BN, splits;
     bool pair = false;
     choose_tiles(&p, 1, BN, splits, false, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
+    apply_forced_tiles(&p, 1, BN, splits, pair);
     tc::GemmGroup grp;
     memset(&grp, 0, sizeof(grp));
     bool ok = false;
@@ -1386,6 +1412,7 @@ int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st)
     int BN, splits;
     bool pair = false;
     choose_tiles(ps, n, BN, splits, false, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
+    apply_forced_tiles(ps, n, BN, splits, pair);
     tc::GemmGroup grp;
     int kpl = g_stage_kblocks == 2 ? 2 : 1;
     for (int i = 0; i < n; ++i) kpl = split_ok(ps[i]) ? kpl : 1;
@@ -1648,6 +1675,19 @@ int mle_get_gemm_pairs(void) { return g_gemm_pairs; }
 int mle_set_gemm_store_path(int path) {
     if (path != 0 && path != 1) return MLE_ERR_ARG;
     g_store_path = path;
+    return MLE_OK;
+}
+
+int mle_set_gemm_tiles(int bn, int splits, int pair) {
+    if (bn == 0) {
+        g_force_tiles[0] = g_force_tiles[1] = g_force_tiles[2] = 0;
+        return MLE_OK;
+    }
+    if ((bn != 64 && bn != 128 && bn != 256) || splits < 1 || splits > 64 || (pair != 0 && pair != 1))
+        return MLE_ERR_ARG;
+    g_force_tiles[0] = bn;
+    g_force_tiles[1] = splits;
+    g_force_tiles[2] = pair;
     return MLE_OK;
 }
 

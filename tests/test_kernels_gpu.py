@@ -442,6 +442,31 @@ def test_gemm_operand_rounding(cuda, ops, rng, ta, tb, mode, emul):
     assert np.max(np.abs(got[0] - ref[0])) / np.max(np.abs(ref[0])) <= 2e-5
 
 
+@pytest.mark.parametrize("bn,splits,pair", [(64, 1, 0), (128, 2, 0), (256, 4, 1), (64, 3, 1)])
+def test_gemm_forced_tiles(cuda, ops, rng, bn, splits, pair):
+    """mle_set_gemm_tiles overrides the tile model (the product reports the
+    forced width, split count and pairing) and the result stays within the
+    TF32 tolerance; width 0 hands the choice back to the model."""
+    from ml_engine_b200._lib import kernels
+    k = kernels()
+    M, N, K = 1000, 384, 800
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    C = T(C0, cuda)
+    k.call("mle_set_gemm_tiles", bn, splits, pair)
+    try:
+        ops.gemm(T(A, cuda), T(B, cuda), C, M, N, K, 0, 0, alpha=1.0, beta=1.0)
+        got = H(C)
+        choice = (ctypes.c_int * 3)()
+        k.call("mle_gemm_last_choice", choice)
+    finally:
+        k.call("mle_set_gemm_tiles", 0, 0, 0)
+    assert list(choice) == [bn, splits, pair]
+    prod = A.astype(np.float64) @ B.astype(np.float64)
+    assert np.max(np.abs(got - C0 - prod)) / np.max(np.abs(prod)) <= RTOL_TC
+
+
 def test_gemm_fallback_exact(cuda, ops, orc, rng):
     """N = 10 (MNIST logits) has a 40-byte row stride: CUDA-core path, fp32."""
     M, N, K = 64, 10, 256
