@@ -529,6 +529,12 @@ int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y
 int mle_conv2d_bwd(const float* x, const float* wgt, const float* dy, float* dx, float* dw, float* db,
                    float* ws, int batch, int cin, int h, int w, int cout, int kh, int kw, int pad,
                    int stride, mle_stream_t stream);
+/* The same with dx written instead of accumulated when assign_dx is 1 (dx's
+ * previous contents are not read): for the first writer of an input
+ * gradient that is not cleared between steps. */
+int mle_conv2d_bwd_assign(const float* x, const float* wgt, const float* dy, float* dx, float* dw, float* db,
+                          float* ws, int batch, int cin, int h, int w, int cout, int kh, int kw, int pad,
+                          int stride, int assign_dx, mle_stream_t stream);
 
 /* Convolute2DT (Engine/engine.cu:3828-3912): weights [cout][cin][kh][kw],
  * x [batch][cin][h][w], y [batch][cout][OH][OW] with OH from

@@ -40,6 +40,7 @@ enum OpKind {
     OP_SMCE = 3,
     OP_ATTENTION = 4,  // ScaledDotAttention on the token-major kernels
     OP_ADD = 5,
+    OP_CONV = 6,       // Convolute2D
 };
 
 // Per-node fusion state decided by prepare_fusions() before a backward pass.
@@ -60,8 +61,8 @@ void forget_ext(const NodeBackProp* n);
 // else adds that Linear's BCompress (column sums) to its own backward pass.
 // Also finds gradients whose first writer in the backward walk (the
 // consumer last in topological order) overwrites the whole buffer: a
-// loss node, an activation, an Add, the token-major attention, or a Linear
-// with a large input gradient.  That writer assigns (assign_inputs) and
+// loss node, an activation, an Add, the token-major attention, a
+// Convolute2D, or a Linear with a large input gradient.  That writer assigns (assign_inputs) and
 // zero_grad leaves the buffer alone.
 void prepare_fusions(const graph_tree& nodes);
 

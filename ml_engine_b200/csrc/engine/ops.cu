@@ -45,8 +45,9 @@ void prepare_fusions(const graph_tree& nodes) {
     }
     // first writers that overwrite the whole input gradient: the loss
     // (SoftMaxCrossEntropy assigns its prediction's gradient), an
-    // activation, an Add, the token-major attention (dQ, dK, dV), and a
-    // Linear whose input gradient spans at least two waves of 128 x 128
+    // activation, an Add, the token-major attention (dQ, dK, dV), a
+    // Convolute2D (its input gradient), and a Linear whose input gradient
+    // spans at least two waves of 128 x 128
     // tiles (its product then never splits K, so the assigned GEMM costs no
     // memset of its own).  The input must appear once among the writer's
     // inputs.
@@ -70,6 +71,7 @@ void prepare_fusions(const graph_tree& nodes) {
             if (we.kind == OP_ACTIVATION) ok = pos == 0;
             if (we.kind == OP_ADD) ok = pos <= 1;
             if (we.kind == OP_ATTENTION) ok = pos <= 2;
+            if (we.kind == OP_CONV) ok = pos == 0;
             if (we.kind == OP_LINEAR) ok = pos == 0 && (double)x->total >= 2.0 * 148 * 128.0 * 128.0;  // 148 SMs
             if (!ok) continue;
             if (we.kind != OP_SMCE) we.assign_inputs |= 1 << pos;
@@ -831,6 +833,7 @@ graph Convolute2D::forward(const graph& X) {
     const int64_t wsn = mle_conv2d_workspace_floats(batch, inp, a, b, out, c, d, pad, stride);
     float* ws = arena_alloc(ARENA_WS, wsn, name + " columns");
     NodeBackProp *nd = node.get(), *xp = X.get();
+    ext(nd).kind = OP_CONV;
     AdamParameter *W = &W1, *B = &B1;
     const int ci = inp, co = out, kh = c, kw = d, p = pad, s = stride;
     node->forward = [=]() {
@@ -843,8 +846,8 @@ graph Convolute2D::forward(const graph& X) {
         // the two parts use disjoint workspace regions
         void* ps = (void*)fork_param_stream();
         if (xp->grad)
-            check(mle_conv2d_bwd(xp->output, W->output, nd->grad, xp->grad, nullptr, nullptr, ws, batch, ci, a, b, co,
-                                 kh, kw, p, s, st()),
+            check(mle_conv2d_bwd_assign(xp->output, W->output, nd->grad, xp->grad, nullptr, nullptr, ws, batch, ci, a,
+                                        b, co, kh, kw, p, s, ext(nd).assign_inputs & 1, st()),
                   "Input Gradient in " + nd->op_name);
         check(mle_conv2d_bwd(xp->output, W->output, nd->grad, nullptr, W->grad, B->grad, ws, batch, ci, a, b, co, kh,
                              kw, p, s, ps),

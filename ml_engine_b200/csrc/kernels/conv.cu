@@ -439,6 +439,13 @@ int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y
 int mle_conv2d_bwd(const float* x, const float* wgt, const float* dy, float* dx, float* dw, float* db, float* ws,
                    int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
                    mle_stream_t stream) {
+    return mle_conv2d_bwd_assign(x, wgt, dy, dx, dw, db, ws, batch, cin, h, w, cout, kh, kw, pad, stride, 0, stream);
+}
+
+int mle_conv2d_bwd_assign(const float* x, const float* wgt, const float* dy, float* dx, float* dw, float* db,
+                          float* ws, int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride,
+                          int assign_dx, mle_stream_t stream) {
+    if (assign_dx != 0 && assign_dx != 1) return MLE_ERR_ARG;
     if (!x || !wgt || !dy || !ws || !conv_shape_ok(batch, cin, h, w, cout, kh, kw, pad, stride)) return MLE_ERR_ARG;
     const int oh = mle_conv_out_size(h, kh, pad, stride), ow = mle_conv_out_size(w, kw, pad, stride);
     if (oh <= 0 || ow <= 0) return MLE_ERR_ARG;
@@ -468,7 +475,9 @@ int mle_conv2d_bwd(const float* x, const float* wgt, const float* dy, float* dx,
             }
             s = weight_pack(wgt, ws + p.wd, cout, cin, p.taps, p.cout4, 1, st);
             if (s) return s;
-            return run_conv_gemm(conv_dx_gemm(p, dy, ws, dx, batch, cin, w, cout, kh, kw, pad), st);
+            ConvGemm g = conv_dx_gemm(p, dy, ws, dx, batch, cin, w, cout, kh, kw, pad);
+            g.accumulate = assign_dx ? 0 : 1;
+            return run_conv_gemm(g, st);
         }
         return MLE_OK;
     }
@@ -485,7 +494,7 @@ int mle_conv2d_bwd(const float* x, const float* wgt, const float* dy, float* dx,
         s = mle_gemm(wgt, dy, dcols, nullptr, batch, K, P, cout, K, P, P, 0, cout * P, K * P, 1, 0, 1.0f, 0.0f,
                      stream);
         if (s) return s;
-        return col2im(dcols, dx, batch, cin, h, w, kh, kw, oh, ow, pad, stride, 1, st);
+        return col2im(dcols, dx, batch, cin, h, w, kh, kw, oh, ow, pad, stride, assign_dx ? 0 : 1, st);
     }
     return MLE_OK;
 }

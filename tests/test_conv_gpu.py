@@ -115,6 +115,31 @@ def test_conv2d_backward_parts_on_two_streams(cuda, rng, gemm_mode, case):
             assert norm_err(H(got), H(want)) <= 1e-6
 
 
+@pytest.mark.parametrize("case", [CONV[1], CONV[2], CONV[3], CONV[7]], ids=["implicit", "columns", "in-place",
+                                                                            "width10"])
+def test_conv2d_bwd_assign(cuda, rng, gemm_mode, case):
+    """mle_conv2d_bwd_assign with assign_dx = 1 writes dx over whatever it
+    held: the input gradient mle_conv2d_bwd accumulates into a cleared dx."""
+    from ml_engine_b200 import ops
+    from ml_engine_b200._lib import kernels
+    N, Cin, Hh, W, Cout, K, pad, stride = case
+    x = T(rng.standard_normal((N, Cin, Hh, W)).astype(np.float32), cuda)
+    w = T((rng.standard_normal((Cout, Cin, K, K)) * 0.2).astype(np.float32), cuda)
+    OH, OW = ops.conv_out_size(Hh, K, pad, stride), ops.conv_out_size(W, K, pad, stride)
+    dy = T(rng.standard_normal((N, Cout, OH, OW)).astype(np.float32), cuda)
+    y = torch.empty(N, Cout, OH, OW, device=cuda)
+    ws = ops.conv2d_workspace(x, w, pad, stride)
+    ops.conv2d_fwd(x, w, T(np.zeros(Cout, np.float32), cuda), y, ws, pad, stride)
+    want = torch.zeros_like(x)
+    ops.conv2d_bwd(x, w, dy, want, None, None, ws, pad, stride)
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        got = torch.full_like(x, float("nan"))
+        kernels().call("mle_conv2d_bwd_assign", x.data_ptr(), w.data_ptr(), dy.data_ptr(), got.data_ptr(), None, None,
+                       ws.data_ptr(), N, Cin, Hh, W, Cout, K, K, pad, stride, 1, st)
+        assert norm_err(H(got), H(want)) <= 1e-6
+
+
 @pytest.mark.parametrize("case", CONVT)
 def test_convT2d(cuda, rng, gemm_mode, case):
     from ml_engine_b200 import ops

@@ -302,6 +302,50 @@ def test_index_labels_match_dense_targets(cuda, rng):
         assert norm_err(b.read_param(i), a.read_param(i)) <= 1e-6, a.param_names[i]
 
 
+@pytest.mark.parametrize("gemm_mode", [0, 1], ids=["tf32", "fp32"])
+def test_first_write_assign_unet(cuda, rng, gemm_mode):
+    """First-writer assignment in the U-Net (convolutions write the
+    gradients of the activations they read; Adds, activations and the loss
+    as in the encoder) against every gradient cleared and accumulated: the
+    same losses and gradients over an eager step and two graph replays at
+    learning rate 0.  Each run is bitwise repeatable, but in TF32 mode an
+    assigned convolution product may tile differently from an accumulated
+    one, and the summation-order differences pass through thirteen
+    GroupNorm layers, so TF32 gets the TF32 tolerance.  An uncleared
+    gradient would be off by a whole step's gradient.  Tensors whose exact
+    gradient is zero (a bias before a GroupNorm of one channel per group)
+    are bounded absolutely."""
+    from ml_engine_b200._lib import engine
+    cfg = dict(config=4, batch=2, channels=3, image_size=16, base_width=8, t_embed=32, timestep=500, seed=9, lr=0.0,
+               gemm_mode=gemm_mode)
+    lib = engine()
+    old = lib.mle_get_grad_first_write()
+    n_img = 2 * 3 * 16 * 16
+    x_t = rng.standard_normal(n_img).astype(np.float32)
+    noise = rng.standard_normal(n_img).astype(np.float32)
+    runs = {}
+    try:
+        for mode in (0, 1):
+            lib.call("mle_set_grad_first_write", mode)
+            s = _session(**cfg)
+            s.inputs["x_t"][:] = x_t
+            s.inputs["noise"][:] = noise
+            losses = [s.step()]
+            s.capture()
+            losses += [s.step(), s.step()]
+            runs[mode] = (s, losses, [s.read_param(i, 1) for i in range(len(s.param_names))])
+    finally:
+        lib.call("mle_set_grad_first_write", old)
+    (a, la, ga), (b, lb, gb) = runs[0], runs[1]
+    for x, y in zip(la + lb, la[:1] * 6):
+        assert abs(x - y) <= 1e-5 * abs(y), (la, lb)
+    gnorm = np.sqrt(sum(float(np.sum(np.asarray(g, np.float64) ** 2)) for g in ga))
+    for i in range(len(a.param_names)):
+        floor = np.linalg.norm(gb[i] - ga[i]) <= 1e-6 * gnorm
+        tol = RTOL_TC if gemm_mode == 0 else 1e-4
+        assert norm_err(gb[i], ga[i]) <= tol or floor, (a.param_names[i], norm_err(gb[i], ga[i]))
+
+
 def test_first_write_assign_matches_cleared_gradients(cuda, rng):
     """First-writer assignment (gradients the first backward writer
     overwrites are not cleared; the loss, activations and large-input
