@@ -386,7 +386,7 @@ def run_encdec(args, rank, world, local_rank):
         import torch.distributed as dist
         uid = [Session.dp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-        s.enable_dp(uid[0], rank, world, bucket_mb=32)
+        s.enable_dp(uid[0], rank, world, bucket_mb=args.bucket_mb or 32)
     stream = torch.cuda.ExternalStream(s.stream, device=dev)
     rng = np.random.default_rng(3000 + rank)
     zipf = 1.0 / np.arange(1, V + 1) ** 1.1
@@ -464,7 +464,7 @@ def run_native(args, rank, world, local_rank):
         import torch.distributed as dist
         uid = [Session.dp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-        s.enable_dp(uid[0], rank, world, bucket_mb=32)
+        s.enable_dp(uid[0], rank, world, bucket_mb=args.bucket_mb or 4)
     stream = torch.cuda.ExternalStream(s.stream, device=dev)
 
     rng = np.random.default_rng(1000 + rank)
@@ -573,6 +573,10 @@ def main():
                     help="weight/bias gradients on a second stream (mle_set_param_grad_stream); default: on")
     ap.add_argument("--stage-kblocks", type=int, default=None, choices=[1, 2],
                     help="GEMM k-blocks per pipeline stage (mle_set_gemm_stage_kblocks); default: the library's")
+    ap.add_argument("--bucket-mb", type=int, default=None,
+                    help="data-parallel gradient bucket size in MiB (mle_session_enable_dp); default 4 for "
+                         "configs[1] (its 10.5 MB of gradients then reduce in a few buckets during the "
+                         "backward), 32 for configs[2]")
     ap.add_argument("--roofline-only", action="store_true",
                     help="run only the roofline kernel pair (3 untimed + 20 timed pairs)")
     args = ap.parse_args()
