@@ -172,8 +172,14 @@ static void flush_zero_ranges() {
     r.clear();
 }
 
+// Gradients whose first writer in the backward assigns them, for the graph
+// whose fusions were planned last.  zero_range consults the set only inside
+// GraphOperations::zero_grad, which plans its own graph first, so a graph
+// never skips a buffer on the strength of another graph's plan (two graphs
+// may share nodes, and one may assign a gradient the other accumulates).
 static std::unordered_set<const float*> g_preassigned;
 static bool g_first_write = true;
+static int g_skip_depth = 0;
 
 void set_preassigned_grads(const std::vector<const float*>& grads) {
     g_preassigned.clear();
@@ -191,7 +197,7 @@ bool first_write_assign() { return g_first_write; }
 
 void zero_range(float* p, int64_t n) {
     if (!p || n <= 0) return;
-    if (g_preassigned.count(p)) return;  // its first writer in the backward assigns it
+    if (g_skip_depth > 0 && g_preassigned.count(p)) return;  // its first writer in the backward assigns it
     if (g_zero_depth > 0) g_zero_ranges.push_back({p, n});
     else check_cuda(cudaMemsetAsync(p, 0, (size_t)n * sizeof(float), g_stream), "Zerograd");
 }
@@ -679,6 +685,13 @@ void GraphOperations::zero_grad(const graph& X, const bool show) {
                "sort \n");
         return;
     }
+    // the skip set must describe this graph: plan its fusions (the same plan
+    // backward() makes) before any gradient is left uncleared
+    prepare_fusions(nodes);
+    struct SkipScope {
+        SkipScope() { ++g_skip_depth; }
+        ~SkipScope() { --g_skip_depth; }
+    } skip;
     ZeroBatch zb;
     for (auto it = nodes.rbegin(); it != nodes.rend(); ++it) {
         if ((*it)->zero_grad) {
