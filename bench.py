@@ -2,29 +2,47 @@
 """Training-step benchmark of the ML_Engine hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+                    [--config encdec|encoder|mlp|unet] [--sweep]
 
-Workload: BASELINE configs[1] -- 2-layer pre-LN transformer encoder, batch 32
-x seq 128, d_model 256, 8 heads, FFN 1024 (GELU), vocab 4096, next-token
-softmax cross-entropy, AdamW with clipNorm 1.0 -- one step = zero_grad,
-forward, backward, clip, AdamW over one local batch (4096 tokens).  Under
-torchrun each rank runs one replica-parallel (data-parallel) session with its
-own batch; gradients are summed with NCCL (weak scaling).
+Default workload: BASELINE configs[2] -- 6+6-layer encoder-decoder, d_model
+512, 8 heads, FFN 2048 (GELU), seq 256, vocab 8192, global batch 256 split
+over the ranks (strong scaling), Zipf(1.1) token ids, next-token softmax
+cross-entropy, AdamW with clipNorm 1.0.  One step = zero_grad + forward +
+backward + bucketed NCCL all-reduce (N > 1) + clip + AdamW over the rank's
+batch, replayed as a captured CUDA graph.  `--config encoder` is configs[1]
+(batch 32 x seq 128 per rank, weak scaling), `--config mlp` configs[0],
+`--config unet` configs[3] (one GPU), `--sweep` the configs[4] kernels.
 
-Legs (all on the session's stream, CUDA events, max over ranks):
-  value  steps/s with the inputs resident in HBM (captured step replayed);
-  e2e    the same through the public API with host buffers: every step fills
-         the pinned host inputs with new token ids, uploads them, runs the
-         step and reads the loss back to the host;
-  roofline  the dominant kernel (the projection layer's backward GEMMs)
-         timed alone against the measured tensor peak;
-  cpu_baseline  the CPU oracle's step on a bounded sample (rank 0, N=1).
---impl reference times the reference's path on the host cores (the oracle
-port: the reference has no CPU implementation and its own CUDA graph cannot
-run its SoftMaxCrossEntropy node safely).
+Legs (CUDA events on the session's stream, max over ranks):
+  value     steps/s of the whole job, inputs resident in HBM;
+  e2e       the same through the public API with host buffers: every step
+            refills the pinned host inputs, uploads them, runs the step and
+            reads the loss back;
+  bwd_roofline  the backward phase alone (its own captured graph) against
+            the algorithmic backward work: tensor FLOP at TF32 plus the
+            elementwise/normalisation/softmax bytes at HBM bandwidth;
+  roofline  the dominant kernel, the tcgen05 TF32 GEMM, on every Linear
+            backward product (dX, dW) of the workload at the rank's token
+            count, each after an L2-evicting write;
+  ref_cuda  (N = 1, rank 0) the reference's OWN training step -- its
+            GraphOperations runtime, layer classes and CUDA kernels compiled
+            from its sources (oracle/_ref/librefstep.so) -- on configs[0],
+            configs[1] and configs[2] at 32 sequences, with this
+            implementation's step at the same shapes beside it;
+  cpu_baseline  (N = 1, rank 0) the C oracle's step on the host cores, on a
+            bounded sample.
+The baseline legs (ref_cuda, cpu_baseline, --impl reference) are the only
+code here that runs anything under oracle/; the measured path is the
+session ABI of libmle_engine.so.
+
+--impl reference times the reference's path on the host cores: the
+reference is CUDA-only, so its CPU arm is the oracle's C restatement of the
+same graph (oracle/mle_oracle.c + oracle/graphs.py), all host threads.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import subprocess
@@ -37,10 +55,29 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-CFG = dict(batch=32, seq_len=128, d_model=256, heads=8, ffn=1024, layers=2, vocab=4096)
-TOKENS_PER_STEP = CFG["batch"] * CFG["seq_len"]
 METRIC = "train steps/s (fwd+bwd+AdamW) at 1/2/4/8 B200; bwd % of roofline"
-WORKLOAD = "configs[1]: 2-layer pre-LN transformer encoder, batch 32 x seq 128, d256 h8 ffn1024 gelu, vocab 4096"
+
+WORKLOADS = {
+    "encdec": dict(
+        cfg=dict(seq_len=256, d_model=512, heads=8, ffn=2048, layers=6, vocab=8192),
+        global_batch=256, scaling="strong",
+        name="configs[2]: encoder-decoder 6+6, d 512, 8 heads, FFN 2048 GELU, seq 256, vocab 8192, "
+             "global batch 256 over the ranks"),
+    "encoder": dict(
+        cfg=dict(seq_len=128, d_model=256, heads=8, ffn=1024, layers=2, vocab=4096),
+        per_rank_batch=32, scaling="weak",
+        name="configs[1]: 2-layer pre-LN transformer encoder, batch 32 x seq 128 per rank, d256 h8 ffn1024 gelu, "
+             "vocab 4096"),
+    "mlp": dict(
+        cfg=dict(in_features=784, hidden=256, classes=10),
+        per_rank_batch=64, scaling="weak",
+        name="configs[0]: MLP 784-256(ReLU)-10, batch 64 per rank, softmax cross-entropy"),
+}
+L2_NOTE = {
+    "encdec": "no flush: a step moves ~10^2 GB through HBM (> 126 MB L2)",
+    "encoder": "no flush: a step moves ~1 GB through HBM (> 126 MB L2)",
+    "mlp": "no flush: the whole step (~2 MB) is L2-resident, as it is for the reference",
+}
 
 
 def load_peaks():
@@ -49,6 +86,70 @@ def load_peaks():
         d = json.loads(p.read_text())
         return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
     return 6650.0, 1590.0, "fallback"
+
+
+def local_batch(wl, world):
+    w = WORKLOADS[wl]
+    if "global_batch" in w:
+        if w["global_batch"] % world:
+            raise SystemExit(f"global batch {w['global_batch']} does not split over {world} ranks")
+        return w["global_batch"] // world
+    return w["per_rank_batch"]
+
+
+def config_dict(wl, world):
+    """The `config` object of both arms (identical by construction)."""
+    w = WORKLOADS[wl]
+    B = local_batch(wl, world)
+    d = {"workload": w["name"], "global_batch": B * world, "per_rank_batch": B, "parallelism": f"dp{world}",
+         "l2": L2_NOTE[wl]}
+    if "seq_len" in w["cfg"]:
+        d["seq_len"] = w["cfg"]["seq_len"]
+    return d
+
+
+def units_per_step(wl, B):
+    """(tokens or images per step for B sequences/images, unit name)."""
+    c = WORKLOADS[wl]["cfg"]
+    if wl == "mlp":
+        return B, "images/s"
+    return B * c["seq_len"], "tokens/s"
+
+
+# ------------------------------------------------------- algorithmic work
+def linear_shapes(wl):
+    """(in, out, count) of every Linear in the step's graph."""
+    c = WORKLOADS[wl]["cfg"]
+    if wl == "mlp":
+        return [(c["in_features"], c["hidden"], 1), (c["hidden"], c["classes"], 1)]
+    D, F, L, V = c["d_model"], c["ffn"], c["layers"], c["vocab"]
+    attn = 4 * L * (1 if wl == "encoder" else 3)   # enc self; dec self + cross
+    return [(D, D, attn), (D, F, L * (1 if wl == "encoder" else 2)), (F, D, L * (1 if wl == "encoder" else 2)),
+            (D, V, 1)]
+
+
+def backward_work(wl, B):
+    """Algorithmic backward work of one step on B sequences: tensor FLOP
+    (Linear dX and dW, 4 attention products per attention block) and the
+    bytes the non-GEMM backward ops must move (fp32, each tensor read or
+    written once): LayerNorm 16 B/elem, GELU 12, residual Add 12, column
+    softmax 12 B/score, loss gradient 8 B/logit.  The MLP's tiny
+    elementwise ops are left out."""
+    c = WORKLOADS[wl]["cfg"]
+    if wl == "mlp":
+        T = B
+        return sum(4.0 * T * i * o * n for i, o, n in linear_shapes(wl)), 0.0
+    S, D, H, F, L, V = c["seq_len"], c["d_model"], c["heads"], c["ffn"], c["layers"], c["vocab"]
+    T = B * S
+    flop = sum(4.0 * T * i * o * n for i, o, n in linear_shapes(wl))
+    blocks = L if wl == "encoder" else 3 * L
+    flop += blocks * 4 * 2.0 * B * H * S * S * (D // H)
+    lns = 2 * L if wl == "encoder" else 5 * L
+    adds = lns
+    ffns = L if wl == "encoder" else 2 * L
+    byts = 16.0 * lns * T * D + 12.0 * adds * T * D + 12.0 * ffns * T * F + 12.0 * blocks * B * H * S * S \
+        + 8.0 * T * V
+    return flop, byts
 
 
 # ------------------------------------------------------------------- clocks
@@ -67,7 +168,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", self.dev, f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -86,6 +187,7 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc:
+            time.sleep(0.15)   # the last sample of the timed region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -95,12 +197,18 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = sorted(float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit())
-        mx = max(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = sorted(v for v in (num(s[0]) for s in self.samples) if v is not None)
+        mxs = [v for v in (num(s[1]) for s in self.samples) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i].strip() == "Active"})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(self.samples)}
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(mxs) if mxs else None,
+                "reasons": reasons, "samples": len(self.samples)}
 
 
 # ------------------------------------------------------------ ranks
@@ -139,102 +247,325 @@ def init_ranks():
     return world, rank, local_rank
 
 
-# ------------------------------------------------------------ CPU baseline
-def cpu_sample(seconds=10.0, max_steps=None):
-    """The oracle's encoder step (OpenMP C restatement) on one sequence of
-    the 32-sequence batch; returns (full-config steps/s, cores, sample)."""
-    import numpy as np
+def smi_index(local_rank):
+    if "CUDA_VISIBLE_DEVICES" in os.environ:
+        return os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]
+    return str(local_rank)
 
-    from oracle import graphs
-    rng = np.random.default_rng(0)
-    D, F, V, L = CFG["d_model"], CFG["ffn"], CFG["vocab"], CFG["layers"]
+
+# ------------------------------------------------------------ inputs
+def input_pool(wl, B, seed, n=4):
+    """Seeded synthetic inputs per step: Zipf(1.1) token ids over the
+    vocabulary with next-token targets, uniform ids
+    (configs[1]), U[0,1) images with uniform labels."""
+    import numpy as np
+    c = WORKLOADS[wl]["cfg"]
+    rng = np.random.default_rng(seed)
+    pool = []
+    for _ in range(n):
+        if wl == "encdec":
+            V, S = c["vocab"], c["seq_len"]
+            zipf = 1.0 / np.arange(1, V + 1) ** 1.1
+            zipf /= zipf.sum()
+            seq = rng.choice(V, size=(B, S + 1), p=zipf).astype(np.int32)
+            src = rng.choice(V, size=(B, S), p=zipf).astype(np.int32)
+            pool.append({"src": src.ravel(), "tgt_in": seq[:, :S].ravel().copy(),
+                         "tgt_out": seq[:, 1:].ravel().copy()})
+        elif wl == "encoder":
+            V, S = c["vocab"], c["seq_len"]
+            pool.append({"tokens": rng.integers(0, V, B * S).astype(np.int32),
+                         "targets": rng.integers(0, V, B * S).astype(np.int32)})
+        else:
+            pool.append({"x": rng.random(B * c["in_features"], dtype=np.float32),
+                         "labels": rng.integers(0, c["classes"], B).astype(np.int32)})
+    return pool
+
+
+def make_session(wl, B, seed=2024, **kw):
+    from ml_engine_b200.session import Session
+    c = WORKLOADS[wl]["cfg"]
+    if wl == "encdec":
+        return Session.encdec(batch=B, **c, lr=1e-4, adamw=1, clip_norm=1.0, fused_attention=1, seed=seed, **kw)
+    if wl == "encoder":
+        return Session.encoder(batch=B, **c, lr=1e-3, adamw=1, clip_norm=1.0, fused_attention=1, seed=seed, **kw)
+    return Session.mlp(batch=B, **c, lr=1e-3, adamw=1, clip_norm=1.0, seed=seed, **kw)
+
+
+def feed(s, item):
+    for k, v in item.items():
+        s.inputs[k][:] = v
+
+
+def time_replays(s, stream, steps):
+    """ms per captured device-resident step (CUDA events on the stream)."""
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        s.step(upload=False, read_loss=False)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def time_phases(s, stream, steps):
+    """Mean ms of (forward incl. zero_grad, backward, all-reduce + clip +
+    update) over `steps` replays of the per-phase graphs."""
+    import torch
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    for ev in evs:
+        ev[0].record(stream)
+        s.phase_replay(0)
+        s.phase_replay(1)
+        ev[1].record(stream)
+        s.phase_replay(2)
+        ev[2].record(stream)
+        for ph in (3, 4, 5):
+            s.phase_replay(ph)
+        ev[3].record(stream)
+    torch.cuda.synchronize()
+    out = [0.0, 0.0, 0.0]
+    for ev in evs:
+        for i in range(3):
+            out[i] += ev[i].elapsed_time(ev[i + 1]) / steps
+    return out
+
+
+# ------------------------------------------------------------ roofline kernel
+def roofline_gemms(wl, B, dev, stream, reps=5):
+    """The tcgen05 TF32 GEMM on every Linear backward product of the step
+    at the rank's token count T (dX = dY W^T and dW = X^T dY, 4 T in out
+    FLOP per pair): per distinct shape, 2 untimed pairs, then `reps` pairs
+    each between its own CUDA events after a 256 MB write that evicts the
+    operands from L2.  Returns (per-shape rows, total FLOP, total ms), the
+    totals weighted by how often each shape occurs in one step."""
+    import torch
+
+    from ml_engine_b200 import ops
+    c = WORKLOADS[wl]["cfg"]
+    T = B * c.get("seq_len", 1)
+    g = torch.Generator(device=dev).manual_seed(0)
+    flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > 126 MB L2
+    rows, tot_flop, tot_ms = [], 0.0, 0.0
+    with torch.cuda.stream(stream):
+        for fin, fout, count in linear_shapes(wl):
+            X = torch.randn(T, fin, device=dev, generator=g)
+            W = torch.randn(fin, fout, device=dev, generator=g) * 0.02
+            dY = torch.randn(T, fout, device=dev, generator=g) * 1e-3
+            dX, dW = torch.zeros(T, fin, device=dev), torch.zeros(fin, fout, device=dev)
+            for _ in range(2):
+                ops.linear_bwd(X, W, dY, dX, dW, None, T, fin, fout)
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            for k0, k1 in evs:
+                flush.fill_(1.0)
+                k0.record(stream)
+                ops.linear_bwd(X, W, dY, dX, dW, None, T, fin, fout)
+                k1.record(stream)
+            torch.cuda.synchronize()
+            ms = sum(k0.elapsed_time(k1) for k0, k1 in evs) / reps
+            flop = 4.0 * T * fin * fout
+            rows.append({"shape": f"T{T} x {fin} -> {fout}", "per_step": count, "ms_per_pair": ms,
+                         "tflops": flop / (ms * 1e-3) / 1e12})
+            tot_flop += count * flop
+            tot_ms += count * ms
+            del X, W, dY, dX, dW
+    return rows, tot_flop, tot_ms
+
+
+def roofline_only(args):
+    """Only the roofline GEMM pairs (for ncu captures of the kernel)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    B = args.roofline_batch or local_batch(args.config, 1)
+    rows, flop, ms = roofline_gemms(args.config, B, dev, torch.cuda.current_stream(dev), reps=args.roofline_reps)
+    print(json.dumps({"rows": rows, "flop": flop, "ms": ms}))
+
+
+# ------------------------------------------------------------ reference CUDA
+REF_CASES = [
+    # name, workload, batch, timed steps
+    ("configs[0]", "mlp", 64, 30),
+    ("configs[1]", "encoder", 32, 10),
+    ("configs[2] at 32 sequences (one rank's share at 8 GPUs)", "encdec", 32, 2),
+]
+
+
+def ref_cuda_leg(dev):
+    """The reference's own step (librefstep.so) beside ours, same shapes."""
+    import numpy as np
+    import torch
+
+    from oracle import ref
+    if not ref.step_available():
+        return {"unavailable": "oracle/_ref/librefstep.so was not built (the reference source tree was absent "
+                               "at build time)"}
+    L = ref.step_lib()
+    out = {"what": "the reference's GraphOperations runtime, layer classes and CUDA kernels compiled from its "
+                   "sources (Engine/{engine,kernels,debug,transformer}.cu), graphs built through its API "
+                   "(oracle/ref_step.cu); one step = zero_grad, token gather, forward, backward, clip(1.0), "
+                   "AdamW, launched as the reference launches them (legacy stream, its own device syncs); "
+                   "CUDA events per phase", "cases": []}
+    for name, wl, B, steps in REF_CASES:
+        c = WORKLOADS[wl]["cfg"]
+        if wl == "mlp":
+            args_ = (1, B, c["in_features"], c["hidden"], c["classes"], 0, 0, 0, 0, 0, 0)
+        else:
+            args_ = (2 if wl == "encoder" else 3, B, 0, 0, 0, c["seq_len"], c["d_model"], c["heads"], c["ffn"],
+                     c["layers"], c["vocab"])
+        st = L.refstep_create(*args_)
+        if st != 0:
+            out["cases"].append({"case": name, "error": f"refstep_create: cuda error {st}"})
+            L.refstep_destroy()
+            continue
+        item = input_pool(wl, B, seed=77, n=1)[0]
+        for k, v in item.items():
+            L.refstep_input_write(k.encode(), v.ctypes.data, v.size)
+        ms = (ctypes.c_double * 4)()
+        st = L.refstep_time(1, steps, 1e-3, 1, 1.0, ms)
+        ref_ms = list(ms)
+        L.refstep_destroy()
+        torch.cuda.synchronize()
+        # this implementation at the same shape
+        s = make_session(wl, B)
+        stream = torch.cuda.ExternalStream(s.stream, device=dev)
+        feed(s, item)
+        s.step()
+        s.capture()
+        for _ in range(3):
+            s.step(upload=False, read_loss=False)
+        torch.cuda.synchronize()
+        ours = time_replays(s, stream, max(steps, 10))
+        s.capture_phases()
+        f_ms, b_ms, o_ms = time_phases(s, stream, max(3, min(steps, 10)))
+        s.close()
+        out["cases"].append({
+            "case": name, "batch": B, "status": st,
+            "ref_ms": {"forward": ref_ms[0], "backward": ref_ms[1], "clip_update": ref_ms[2], "step": ref_ms[3]},
+            "ours_ms": {"forward": f_ms, "backward": b_ms, "allreduce_clip_update": o_ms, "step": ours},
+            "speedup_step": ref_ms[3] / ours,
+            "speedup_bwd_plus_update": (ref_ms[1] + ref_ms[2]) / (b_ms + o_ms)})
+    return out
+
+
+# ------------------------------------------------------------ CPU baseline
+def _cpu_problem(wl, seed=0):
+    import numpy as np
+    c = WORKLOADS[wl]["cfg"]
+    rng = np.random.default_rng(seed)
+    if wl == "mlp":
+        sizes = [c["in_features"] * c["hidden"], c["hidden"], c["hidden"] * c["classes"], c["classes"]]
+        return [(rng.standard_normal(n) * 0.05).astype(np.float32) for n in sizes], None
+    D, F, V, L = c["d_model"], c["ffn"], c["vocab"], c["layers"]
     sizes = []
     for _ in range(L):
         sizes += [D * D, D] * 4 + [D * F, F, F * D, D]
+    if wl == "encdec":
+        for _ in range(L):
+            sizes += [D * D, D] * 8 + [D * F, F, F * D, D]
     sizes += [D * V, V]
     params = [(rng.standard_normal(n) * 0.02).astype(np.float32) for n in sizes]
-    table = (rng.standard_normal(V * D) * 0.02).astype(np.float32)
-    sb = 1
-    steps, t0 = 0, time.perf_counter()
-    while True:
-        tok = rng.integers(0, V, (sb, CFG["seq_len"])).astype(np.int32)
-        tgt = rng.integers(0, V, (sb, CFG["seq_len"])).astype(np.int32)
-        graphs.encoder_step(params, table, tok, tgt, sb, CFG["seq_len"], D, CFG["heads"], F, L, V)
-        steps += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or (max_steps and steps >= max_steps):
-            break
-    per_sample_step = el / steps
-    full_step = per_sample_step * CFG["batch"] / sb
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return 1.0 / full_step, cores, f"{steps} oracle steps of 1 of 32 sequences (128 tokens), scaled x32; {el:.1f}s"
+    tables = [(rng.standard_normal(V * D) * 0.02).astype(np.float32) for _ in range(2 if wl == "encdec" else 1)]
+    return params, tables
+
+
+def cpu_fwd_bwd(wl, params, tables, B, seed):
+    """One oracle forward + backward over B sequences/images (no update)."""
+    from oracle import graphs
+    c = WORKLOADS[wl]["cfg"]
+    item = input_pool(wl, B, seed=seed, n=1)[0]
+    if wl == "mlp":
+        return graphs.mlp_step(params, item["x"].reshape(B, -1), item["labels"], classes=c["classes"],
+                               update=False)
+    if wl == "encoder":
+        return graphs.encoder_step(params, tables[0], item["tokens"].reshape(B, -1), item["targets"].reshape(B, -1),
+                                   B, c["seq_len"], c["d_model"], c["heads"], c["ffn"], c["layers"], c["vocab"],
+                                   update=False)
+    return graphs.encdec_step(params, tables, item["src"].reshape(B, -1), item["tgt_in"].reshape(B, -1),
+                              item["tgt_out"].reshape(B, -1), B, c["seq_len"], c["d_model"], c["heads"], c["ffn"],
+                              c["layers"], c["vocab"], update=False)
+
+
+def cpu_sample_plan(wl, B_full):
+    """Sequences (images) per sampled step: the whole batch where the CPU
+    finishes it in seconds, one sequence of
+    configs[2] (a full configs[2] step is ~10^3 s on the host)."""
+    return 1 if wl == "encdec" else B_full
+
+
+def cpu_step_times(wl, B_full, n_steps, warm=1, params=None):
+    """Per sampled step: (estimated full-step seconds, sample seconds).  A
+    step's forward+backward is timed on the sample and scaled to the full
+    batch; the clip + AdamW over all parameters is timed once per step on
+    the gradients the sample produced (it does not scale with the batch)."""
+    from oracle import graphs
+    params_, tables = _cpu_problem(wl)
+    sb = cpu_sample_plan(wl, B_full)
+    times = []
+    for i in range(warm + n_steps):
+        t0 = time.perf_counter()
+        r = cpu_fwd_bwd(wl, params_, tables, sb, seed=500 + i)
+        t1 = time.perf_counter()
+        graphs.clip_and_update([p.ravel() for p in params_], r["grads"], [1] * len(params_), 1e-3, 1.0)
+        t2 = time.perf_counter()
+        if i >= warm:
+            times.append(((t1 - t0) * B_full / sb + (t2 - t1), t2 - t0))
+    return times, sb
+
+
+def cpu_cores():
+    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+
+
+def cpu_baseline_leg(wl, B_full, seconds):
+    times, sb = [], None
+    t0 = time.perf_counter()
+    while not times or time.perf_counter() - t0 < seconds:
+        tt, sb = cpu_step_times(wl, B_full, 1, warm=0 if times else 1)
+        times += tt
+    full = sum(t for t, _ in times) / len(times)
+    spent = sum(s for _, s in times)
+    unit = "sequences" if wl != "mlp" else "images"
+    return {"value": 1.0 / full, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
+            "sample": f"{len(times)} sampled steps: forward+backward on {sb} of {B_full} {unit} scaled x{B_full // sb}, "
+                      f"plus the clip + AdamW over all parameters once per step; {spent:.1f}s of host time"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    per_step = []
-    cores = None
-    sample = ""
-    for i in range(args.warmup + args.steps):
-        v, cores, sample = cpu_sample(seconds=0.0, max_steps=1)
-        if i >= args.warmup:
-            per_step.append(1.0 / v)
-    total = sum(per_step)
-    value = len(per_step) / total
+    wl = args.config
+    B = local_batch(wl, world)
+    n_gpu_b = B * world
+    # the reference arm runs the whole job's batch (all ranks' shares) on the host
+    times, sb = cpu_step_times(wl, n_gpu_b, args.steps, warm=min(args.warmup, 1))
+    full = sum(t for t, _ in times) / len(times)
+    value = 1.0 / full
+    unit = "sequences" if wl != "mlp" else "images"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(per_step),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": CFG["batch"] * world, "seq_len": CFG["seq_len"],
-                   "parallelism": f"dp{world}"},
-        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": cores, "kind": "port",
-                         "sample": "per step: " + sample},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * full,
+        "higher_is_better": True, "scaling": WORKLOADS[wl]["scaling"], "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_dict(wl, world),
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
+                         "sample": f"per step: forward+backward on {sb} of {n_gpu_b} {unit}, scaled "
+                                   f"x{n_gpu_b // sb}, plus the clip + AdamW over all parameters; "
+                                   f"{min(args.warmup, 1)} warm-up sample"},
         "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is CUDA-only; its CPU arm is the oracle's C restatement of the same graph "
-                "(oracle/mle_oracle.c + oracle/graphs.py) on the host cores",
+                "(oracle/mle_oracle.c + oracle/graphs.py, OpenMP) on the host cores",
     }
     print(json.dumps(line), flush=True)
-
-
-# ------------------------------------------------------------ roofline kernel
-def roofline_pair(dev, stream, reps=50):
-    """The projection layer's backward GEMMs (dX = dY W^T, dW = X^T dY),
-    2 * 2 * 4096 * 256 * 4096 FLOP per pair, on `stream`: 3 untimed pairs,
-    then `reps` pairs, each between its own CUDA events after a 256 MB write
-    that evicts the operands from L2.  Returns (ms per pair, FLOP)."""
-    import torch
-
-    from ml_engine_b200 import ops
-    M, K, N = TOKENS_PER_STEP, CFG["d_model"], CFG["vocab"]
-    g = torch.Generator(device=dev).manual_seed(0)
-    X = torch.randn(M, K, device=dev, generator=g)
-    W = torch.randn(K, N, device=dev, generator=g) * 0.02
-    dY = torch.randn(M, N, device=dev, generator=g) * 1e-3
-    dX, dW = torch.zeros(M, K, device=dev), torch.zeros(K, N, device=dev)
-    flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > 126 MB L2
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            ops.linear_bwd(X, W, dY, dX, dW, None, M, K, N)
-        torch.cuda.synchronize()
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-        for k0, k1 in evs:
-            flush.fill_(1.0)
-            k0.record(stream)
-            ops.linear_bwd(X, W, dY, dX, dW, None, M, K, N)
-            k1.record(stream)
-        torch.cuda.synchronize()
-    return sum(k0.elapsed_time(k1) for k0, k1 in evs) / reps, 2 * 2.0 * M * K * N
 
 
 # ------------------------------------------------------------ kernel sweep
 def run_sweep(args):
     """linear backward (dX = dY W^T, dW = X^T dY) at M=N=K = n,
-    LayerNorm backward over 65536 rows of width w, and the fused clip +
-    AdamW over 256 tensors totalling 1e8 parameters.  One JSON line per
-    case with achieved FLOP/s or bytes/s against the measured peaks (CUDA
-    events around `reps` launches, after warm-up; inputs larger than L2
-    except the two smallest GEMMs)."""
+    LayerNorm backward and LayerNorm + GELU backward over 65536 rows of
+    width w, and the fused clip + AdamW over 256 tensors totalling 1e8 and
+    1e9 parameters.  One JSON line per case with achieved FLOP/s or bytes/s
+    against the measured peaks (CUDA events around `reps` launches, after
+    warm-up; inputs larger than L2 except the two smallest GEMMs)."""
     import numpy as np
     import torch
 
@@ -276,29 +607,46 @@ def run_sweep(args):
         gbs = 16.0 * rows * w / (ms * 1e-3) / 1e9   # y, gy, gx read; gx written
         print(json.dumps({"sweep": "layernorm_bwd", "rows": rows, "width": w, "ms": ms, "gbs": gbs,
                           "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
-        del x, y, gy, gx
-    total, nt = 100_000_000, 256
-    sizes = np.random.default_rng(0).integers(1, 1000, nt).astype(np.float64)
-    sizes = np.maximum(1, (sizes / sizes.sum() * total).astype(np.int64))
-    params = []
-    for sz in sizes:
-        params.append(dict(w=torch.randn(int(sz), device=dev, generator=g) * 0.02,
-                           g=torch.randn(int(sz), device=dev, generator=g) * 1e-2,
-                           m=torch.zeros(int(sz), device=dev), v=torch.zeros(int(sz), device=dev),
-                           t=torch.ones(1, dtype=torch.int32, device=dev)))
-    ws = torch.zeros(1, dtype=torch.float64, device=dev)
-    views = ops.param_views(params)   # built once, as the engine's optimizer does
+        # LayerNorm + GELU backward: GELU(LN(x)) with the GELU backward
+        # writing the LayerNorm output's gradient (assign), then the
+        # LayerNorm backward: 12 + 16 B/elem
+        a = torch.empty_like(x)
+        ops.act_fwd(ops.GELU, y, a)
+        gh = torch.empty_like(x)
 
-    def clip_adam():
-        ws.zero_()
-        ops.grad_sumsq(views, ws)
-        ops.clip_finalize(ws, 1.0)
-        ops.adam_update(views, lr=1e-3, adamw=True, clip_ws=ws, write_back_grad=False)
-    ms = timed(clip_adam, 10)
-    nparam = int(sizes.sum())
-    gbs = 32.0 * nparam / (ms * 1e-3) / 1e9   # g read (norm); w, g, m, v read; w, m, v written
-    print(json.dumps({"sweep": "clip_adamw", "params": nparam, "tensors": nt, "ms": ms, "gbs": gbs,
-                      "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
+        def ln_gelu():
+            ops.act_bwd(ops.GELU, y, gy, gh, assign=True)
+            ops.layernorm_bwd(y, gh, sq, gx, rows, 1, 1, w)
+        ms = timed(ln_gelu, 20)
+        gbs = 28.0 * rows * w / (ms * 1e-3) / 1e9
+        print(json.dumps({"sweep": "layernorm_gelu_bwd", "rows": rows, "width": w, "ms": ms, "gbs": gbs,
+                          "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
+        del x, y, gy, gx, a, gh
+    for total in (100_000_000, 1_000_000_000):
+        nt = 256
+        sizes = np.random.default_rng(0).integers(1, 1000, nt).astype(np.float64)
+        sizes = np.maximum(1, (sizes / sizes.sum() * total).astype(np.int64))
+        params = []
+        for sz in sizes:
+            params.append(dict(w=torch.empty(int(sz), device=dev).normal_(0, 0.02, generator=g),
+                               g=torch.empty(int(sz), device=dev).normal_(0, 1e-2, generator=g),
+                               m=torch.zeros(int(sz), device=dev), v=torch.zeros(int(sz), device=dev),
+                               t=torch.ones(1, dtype=torch.int32, device=dev)))
+        ws = torch.zeros(1, dtype=torch.float64, device=dev)
+        views = ops.param_views(params)   # built once, as the engine's optimizer does
+
+        def clip_adam():
+            ws.zero_()
+            ops.grad_sumsq(views, ws)
+            ops.clip_finalize(ws, 1.0)
+            ops.adam_update(views, lr=1e-3, adamw=True, clip_ws=ws, write_back_grad=False)
+        ms = timed(clip_adam, 10 if total <= 100_000_000 else 3)
+        nparam = int(sizes.sum())
+        gbs = 32.0 * nparam / (ms * 1e-3) / 1e9   # g read (norm); w, g, m, v read; w, m, v written
+        print(json.dumps({"sweep": "clip_adamw", "params": nparam, "tensors": nt, "ms": ms, "gbs": gbs,
+                          "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
+        del params, views
+        torch.cuda.empty_cache()
 
 
 # ------------------------------------------------------------ U-Net workload
@@ -324,30 +672,21 @@ def run_unet(args):
     for _ in range(4):
         x0 = rng.standard_normal(B * C * S * S).astype(np.float32)
         eps = rng.standard_normal(B * C * S * S).astype(np.float32)
-        pool.append(((np.sqrt(abar) * x0 + np.sqrt(1 - abar) * eps).astype(np.float32), eps))
+        pool.append({"x_t": (np.sqrt(abar) * x0 + np.sqrt(1 - abar) * eps).astype(np.float32), "noise": eps})
     stream = torch.cuda.ExternalStream(s.stream, device=dev)
-
-    def feed(i):
-        s.inputs["x_t"][:], s.inputs["noise"][:] = pool[i % len(pool)]
-
-    feed(0)
+    feed(s, pool[0])
     s.step()
     s.capture()
     for i in range(max(args.warmup, 3)):
-        feed(i)
+        feed(s, pool[i % 4])
         s.step()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        s.step(upload=False, read_loss=False)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = time_replays(s, stream, args.steps)
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
+    loss = None
     for i in range(args.steps):
-        feed(i)
+        feed(s, pool[i % 4])
         loss = s.step(upload=True, read_loss=True)
     e3.record(stream)
     torch.cuda.synchronize()
@@ -363,154 +702,50 @@ def run_unet(args):
     s.close()
 
 
-# ------------------------------------------------------ encoder-decoder workload
-def run_encdec(args, rank, world, local_rank):
-    """6+6-layer encoder-decoder (d 512, 8 heads, FFN 2048,
-    seq 256, vocab 8192), global batch 256 split over the ranks (strong
-    scaling); token ids Zipf(s=1.1) over the vocabulary, next-token targets;
-    one step = zero_grad + forward + backward + bucketed NCCL allreduce +
-    clip(1.0) + AdamW, replayed as a captured CUDA graph."""
-    import numpy as np
-    import torch
-
-    from ml_engine_b200.session import Session
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    GB, S, V = 256, 256, 8192
-    if GB % world:
-        raise SystemExit(f"global batch {GB} does not split over {world} ranks")
-    B = GB // world
-    s = Session.encdec(batch=B, seq_len=S, d_model=512, heads=8, ffn=2048, layers=6, vocab=V, lr=1e-4, adamw=1,
-                       clip_norm=1.0, fused_attention=1, seed=2024)
-    if world > 1:
-        import torch.distributed as dist
-        uid = [Session.dp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        s.enable_dp(uid[0], rank, world, bucket_mb=args.bucket_mb or 32)
-    stream = torch.cuda.ExternalStream(s.stream, device=dev)
-    rng = np.random.default_rng(3000 + rank)
-    zipf = 1.0 / np.arange(1, V + 1) ** 1.1
-    zipf /= zipf.sum()
-    pool = []
-    for _ in range(4):
-        seq = rng.choice(V, size=(B, S + 1), p=zipf).astype(np.int32)
-        src = rng.choice(V, size=(B, S), p=zipf).astype(np.int32)
-        pool.append((src.ravel(), seq[:, :S].ravel().copy(), seq[:, 1:].ravel().copy()))
-
-    def feed(i):
-        s.inputs["src"][:], s.inputs["tgt_in"][:], s.inputs["tgt_out"][:] = pool[i % len(pool)]
-
-    feed(0)
-    s.step()
-    s.capture()
-    for i in range(max(args.warmup, 3)):
-        feed(i)
-        s.step()
-    import ctypes
-    kk, mm, cc = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
-    s._lib.call("mle_session_graph_counts", s._h, ctypes.addressof(kk), ctypes.addressof(mm), ctypes.addressof(cc))
-    smi_index = os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank] \
-        if "CUDA_VISIBLE_DEVICES" in os.environ else str(local_rank)
-    with ClockSampler(smi_index) as clocks:
-        barrier(world)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            s.step(upload=False, read_loss=False)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
-        barrier(world)
-        torch.cuda.synchronize()
-        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e2.record(stream)
-        loss = None
-        for i in range(args.steps):
-            feed(i)
-            loss = s.step(upload=True, read_loss=True)
-        e3.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps, world, dev)
-    if rank == 0:
-        print(json.dumps({
-            "metric": "train steps/s (fwd+bwd+AdamW), configs[2] encoder-decoder", "value": 1e3 / ms,
-            "unit": "steps/s", "tokens_per_s": GB * S * 1e3 / ms, "ms_per_step": ms, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
-            "dtype": "f32 (tf32 tensor-core products)", "data": "synthetic (Zipf(1.1) token ids)",
-            "config": {"workload": "configs[2]: enc-dec 6+6, d 512, 8 heads, FFN 2048, seq 256, vocab 8192",
-                       "global_batch": GB, "per_rank_batch": B, "seq_len": S, "parallelism": f"dp{world}"},
-            "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": 3 * B * S * 4, "d2h_bytes_per_step": 4, "loss_last": loss},
-            "gpu_launches": kk.value * args.steps, "clocks": clocks.summary()}), flush=True)
-    s.close()
-
-
 # ------------------------------------------------------------ native arm
 def run_native(args, rank, world, local_rank):
-    import numpy as np
     import torch
 
     from ml_engine_b200.session import Session
 
+    wl = args.config
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    hbm_peak, tf_peak, peak_kind = load_peaks()
-
-    s = Session.encoder(**CFG, lr=1e-3, adamw=1, clip_norm=1.0, fused_attention=1, seed=1234)
+    hbm_peak, bf16_peak, peak_kind = load_peaks()
+    tf32_peak = bf16_peak / 2
+    B = local_batch(wl, world)
+    s = make_session(wl, B, seed=2024)
     if world > 1:
         import torch.distributed as dist
         uid = [Session.dp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-        s.enable_dp(uid[0], rank, world, bucket_mb=args.bucket_mb or 4)
+        s.enable_dp(uid[0], rank, world, bucket_mb=args.bucket_mb)
     stream = torch.cuda.ExternalStream(s.stream, device=dev)
+    pool = input_pool(wl, B, seed=3000 + rank)
 
-    rng = np.random.default_rng(1000 + rank)
-    pool = [(rng.integers(0, CFG["vocab"], TOKENS_PER_STEP).astype(np.int32),
-             rng.integers(0, CFG["vocab"], TOKENS_PER_STEP).astype(np.int32)) for _ in range(16)]
-
-    def feed(i):
-        tok, tgt = pool[i % len(pool)]
-        s.inputs["tokens"][:] = tok
-        s.inputs["targets"][:] = tgt
-
-    feed(0)
+    feed(s, pool[0])
     s.step()                 # eager step: builds tensor maps, configures kernels
     s.capture()
     for i in range(max(args.warmup, 3)):
-        feed(i)
+        feed(s, pool[i % len(pool)])
         s.step()
-    kernels = memsets = copies = 0
-    import ctypes
     kk, mm, cc = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     s._lib.call("mle_session_graph_counts", s._h, ctypes.addressof(kk), ctypes.addressof(mm), ctypes.addressof(cc))
     kernels, memsets, copies = kk.value, mm.value, cc.value
 
-    smi_index = os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank] \
-        if "CUDA_VISIBLE_DEVICES" in os.environ else str(local_rank)
-    # ---------------------------------------------------------------- value
-    with ClockSampler(smi_index) as clocks:
+    with ClockSampler(smi_index(local_rank)) as clocks:
+        # ---------------------------------------------------------- value
         barrier(world)
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            s.step(upload=False, read_loss=False)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        dev_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
-
-        # ------------------------------------------------------------- e2e
+        dev_ms = max_over_ranks(time_replays(s, stream, args.steps), world, dev)
+        # ------------------------------------------------------------ e2e
         barrier(world)
         torch.cuda.synchronize()
         e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e2.record(stream)
         losses = []
         for i in range(args.steps):
-            feed(args.warmup + i)
+            feed(s, pool[(args.warmup + i) % len(pool)])
             losses.append(s.step(upload=True, read_loss=True))
         e3.record(stream)
         torch.cuda.synchronize()
@@ -518,67 +753,92 @@ def run_native(args, rank, world, local_rank):
         e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps, world, dev)
     clk = clocks.summary()
 
-    kern_ms, flops_pair = roofline_pair(dev, stream)
-    achieved_tf = flops_pair / (kern_ms * 1e-3) / 1e12
-    traffic = None
-    prof = ROOT / "profiles" / "traffic.json"
-    if prof.exists():
-        traffic = json.loads(prof.read_text()).get("proj_bwd_gemm_pair_bytes")
+    # ------------------------------------------------- backward vs roofline
+    s.capture_phases()
+    barrier(world)
+    f_ms, b_ms, o_ms = time_phases(s, stream, max(3, min(args.steps, 10)))
+    b_ms = max_over_ranks(b_ms, world, dev)
+    bflop, bbytes = backward_work(wl, B)
+    t_roof = bflop / (tf32_peak * 1e12) * 1e3 + bbytes / (hbm_peak * 1e9) * 1e3
+    bwd = {"ms": b_ms, "forward_ms": f_ms, "allreduce_clip_update_ms": o_ms, "algorithmic_tflop": bflop / 1e12,
+           "algorithmic_elementwise_gb": bbytes / 1e9, "achieved_tflops": bflop / (b_ms * 1e-3) / 1e12,
+           "roofline_ms": t_roof, "frac": t_roof / b_ms,
+           "tensor_frac_of_tf32": bflop / (b_ms * 1e-3) / 1e12 / tf32_peak,
+           "how": "backward phase replayed alone (its own captured graph, CUDA events); roofline time = "
+                  "algorithmic tensor FLOP at TF32 dense (half the measured bf16 peak) + algorithmic "
+                  "non-GEMM backward bytes at the measured HBM copy bandwidth"}
+    s.close()   # the remaining legs allocate their own buffers
+    torch.cuda.empty_cache()
 
-    value = world * 1e3 / dev_ms
+    units, unit_name = units_per_step(wl, B)
+    value = 1e3 / dev_ms
     line = {
         "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32 (tf32 tensor-core products)", "data": "synthetic",
-        "tokens_per_s": value * TOKENS_PER_STEP,
-        "config": {"workload": WORKLOAD, "global_batch": CFG["batch"] * world, "seq_len": CFG["seq_len"],
-                   "parallelism": f"dp{world}", "step": "zero_grad+fwd+bwd+clip(1.0)+AdamW, captured CUDA graph",
-                   "l2": "no flush: the step touches ~1 GB (> 126 MB L2) per iteration"},
-        "e2e": {"value": world * 1e3 / e2e_ms, "unit": "steps/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": 2 * TOKENS_PER_STEP * 4, "d2h_bytes_per_step": 4,
+        "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True,
+        "scaling": WORKLOADS[wl]["scaling"], "vs_baseline": None,
+        "dtype": "f32 (tf32 tensor-core products, fp32 accumulation)", "data": "synthetic (seeded)",
+        unit_name.replace("/", "_per_"): value * units * world,
+        "config": config_dict(wl, world),
+        "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(sum(v.nbytes for v in pool[0].values())), "d2h_bytes_per_step": 4,
                 "loss_last": losses[-1] if losses else None},
-        "roofline": {"bound": "tensor", "kernel": "tcgen05 tf32 GEMM pair of the projection backward (dX, dW)",
-                     "achieved": achieved_tf, "peak": tf_peak, "unit": "TFLOP/s", "frac": achieved_tf / tf_peak,
-                     "peak_kind": f"{peak_kind} bf16 dense (tf32 dense is half of it)",
-                     "frac_of_tf32": achieved_tf / (tf_peak / 2), "traffic": traffic, "ms_per_launch_pair": kern_ms},
+        "bwd_roofline": bwd,
         "gpu_launches": kernels * args.steps,
         "launches_per_step": {"kernels": kernels, "memsets": memsets, "copies": copies},
         "clocks": clk,
     }
+    if rank == 0 and not args.no_roofline:
+        rows, gflop, gms = roofline_gemms(wl, B, dev, torch.cuda.current_stream(dev))
+        achieved = gflop / (gms * 1e-3) / 1e12
+        traffic = None
+        prof = ROOT / "profiles" / "traffic.json"
+        if prof.exists():
+            tr = json.loads(prof.read_text()).get(wl)
+            if tr:
+                traffic = tr.get("bytes_per_launch")
+        line["roofline"] = {
+            "bound": "tensor", "kernel": "gemm_tf32_kernel (tcgen05 kind::tf32, TMA, TMEM): every Linear backward "
+                                         "product of the step (dX, dW) at the rank's token count",
+            "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s", "frac": achieved / bf16_peak,
+            "peak_kind": f"{peak_kind} bf16 dense burst (tf32 dense is half of it)",
+            "frac_of_tf32": achieved / tf32_peak, "traffic": traffic, "per_shape": rows}
+    if rank == 0 and world == 1 and not args.no_ref_cuda:
+        line["ref_cuda"] = ref_cuda_leg(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_sample(seconds=args.cpu_seconds)
-        line["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": cores, "kind": "port", "sample": sample}
+        line["cpu_baseline"] = cpu_baseline_leg(wl, B, args.cpu_seconds)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    s.close()
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--config", default="encdec", choices=["encdec", "encoder", "mlp", "unet"],
+                    help="encdec: configs[2], global batch 256 over the ranks (the benchmark line); encoder: "
+                         "configs[1] per rank; mlp: configs[0] per rank; unet: configs[3] on one GPU")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-cuda", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="configs[4] kernel sweep, one JSON line per case")
-    ap.add_argument("--config", default="encoder", choices=["encoder", "unet", "encdec"],
-                    help="encoder: configs[1], the benchmark line; unet: configs[3] on one GPU; "
-                         "encdec: configs[2], global batch 256 over the ranks")
     ap.add_argument("--gemm-pairs", type=int, default=None, choices=[0, 1, 2],
                     help="run large products on CTA pairs (mle_set_gemm_pairs); default: the library's")
     ap.add_argument("--attn-path", default=None, choices=["auto", "fused", "tensor"],
                     help="attention implementation (mle_set_attention_path); default: the library's")
     ap.add_argument("--param-stream", type=int, default=None, choices=[0, 1],
                     help="weight/bias gradients on a second stream (mle_set_param_grad_stream); default: on")
-    ap.add_argument("--stage-kblocks", type=int, default=None, choices=[1, 2],
-                    help="GEMM k-blocks per pipeline stage (mle_set_gemm_stage_kblocks); default: the library's")
-    ap.add_argument("--bucket-mb", type=int, default=None,
-                    help="data-parallel gradient bucket size in MiB (mle_session_enable_dp); default 4 for "
-                         "configs[1] (its 10.5 MB of gradients then reduce in a few buckets during the "
-                         "backward), 32 for configs[2]")
+    ap.add_argument("--bucket-mb", type=int, default=0,
+                    help="data-parallel gradient bucket size in MiB (mle_session_enable_dp); 0: the library's "
+                         "choice from the gradient total (mle_dp_auto_bucket_mb)")
     ap.add_argument("--roofline-only", action="store_true",
-                    help="run only the roofline kernel pair (3 untimed + 20 timed pairs)")
+                    help="run only the roofline GEMM pairs of --config (2 untimed + --roofline-reps timed pairs "
+                         "per shape)")
+    ap.add_argument("--roofline-batch", type=int, default=None,
+                    help="sequences for --roofline-only (default: the workload's per-rank batch at one GPU)")
+    ap.add_argument("--roofline-reps", type=int, default=5)
     args = ap.parse_args()
     if args.gemm_pairs is not None:
         from ml_engine_b200._lib import kernels
@@ -586,9 +846,6 @@ def main():
     if args.attn_path is not None:
         from ml_engine_b200._lib import kernels
         kernels().call("mle_set_attention_path", {"auto": 0, "fused": 1, "tensor": 2}[args.attn_path])
-    if args.stage_kblocks is not None:
-        from ml_engine_b200._lib import kernels
-        kernels().call("mle_set_gemm_stage_kblocks", args.stage_kblocks)
     if args.param_stream is not None:
         from ml_engine_b200._lib import engine
         engine().call("mle_set_param_grad_stream", args.param_stream)
@@ -599,17 +856,12 @@ def main():
         run_unet(args)
         return
     if args.roofline_only:
-        import torch
-        dev = torch.device("cuda", 0)
-        ms, flops = roofline_pair(dev, torch.cuda.current_stream(dev), reps=20)
-        print(json.dumps({"roofline_pair_ms": ms, "flop": flops}))
+        roofline_only(args)
         return
     world, rank, local_rank = init_ranks()
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
-        elif args.config == "encdec":
-            run_encdec(args, rank, world, local_rank)
         else:
             run_native(args, rank, world, local_rank)
     finally:

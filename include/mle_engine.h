@@ -110,6 +110,14 @@ int mle_get_param_grad_stream(void);
 int mle_set_grad_first_write(int enable);
 int mle_get_grad_first_write(void);
 
+/* Captures each phase of the step (the numbering of mle_session_phase,
+ * device resident: no upload, no loss download) as its own CUDA graph, so a
+ * caller can time phases on the device; mle_session_phase_replay(s, ph)
+ * launches phase ph's graph on the session stream.  Replaying phases 0..5 in
+ * order is one training step. */
+int mle_session_capture_phases(mle_session_t s);
+int mle_session_phase_replay(mle_session_t s, int phase);
+
 /* Kernel, memset and memcpy nodes of the captured device-resident step
  * (the launches one replay issues). */
 int mle_session_graph_counts(mle_session_t s, int* kernels, int* memsets, int* copies);
@@ -157,18 +165,29 @@ int mle_dp_unique_id(uint8_t* out128);
 
 /* Host-side bucket plan of data parallelism (what mle_session_enable_dp
  * uses): gradient tensors (device addresses and float counts) sorted by
- * address and merged while contiguous (gaps up to 64 floats bridged) within
- * bucket_mb MiB.  Writes up to max_out buckets (base address, float count)
- * and their number to *out_n; MLE_ERR_ARG if more than max_out are needed.
- * Touches no device. */
-int mle_dp_plan_buckets(const uint64_t* addrs, const int64_t* counts, int n, int bucket_mb,
+ * address and merged while contiguous (gaps up to 64 floats bridged), inside
+ * one allocation and within bucket_mb MiB (bucket_mb <= 0: the size
+ * mle_dp_auto_bucket_mb gives for the total).  `chunks` (nullable: all in
+ * one allocation) names the allocation each tensor lies in, by any id, such
+ * as its base address; tensors of different allocations never share a
+ * bucket, even when their addresses touch.  Writes up to max_out buckets
+ * (base address, float count) and their number to *out_n; MLE_ERR_ARG if
+ * more than max_out are needed.  Touches no device. */
+int mle_dp_plan_buckets(const uint64_t* addrs, const int64_t* counts, const uint64_t* chunks, int n, int bucket_mb,
                         uint64_t* out_base, int64_t* out_count, int max_out, int* out_n);
 
+/* The automatic bucket size for `total_floats` of gradients: the smallest
+ * power of two of MiB, from 1 to 32, that splits them into at most four
+ * buckets (configs[1]'s 10.5 MB -> 4 MiB, configs[2]'s 193 MB -> 32 MiB). */
+int mle_dp_auto_bucket_mb(int64_t total_floats);
+
 /* Joins a communicator of `world` ranks.  After backward, the parameter
- * gradients are summed over ranks in buckets of `bucket_mb` MiB on a second
- * stream, each bucket as soon as the backward pass has produced every
- * gradient in it, and the update averages them (scale 1/world) before the
- * clip norm and AdamW. */
+ * gradients are summed over ranks in buckets of `bucket_mb` MiB (<= 0:
+ * automatic, as above) on a second stream, each bucket as soon as the
+ * backward pass has produced every gradient in it, and the update averages
+ * them (scale 1/world) before the clip norm and AdamW.  A step whose
+ * all-reduce NCCL refuses returns MLE_ERR_CUDA without updating any
+ * parameter. */
 int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int world, int bucket_mb);
 
 #ifdef __cplusplus

@@ -37,7 +37,7 @@ enum mle_status {
     MLE_ERR_ARG = 1,          /* invalid size, pointer or flag */
     MLE_ERR_CUDA = 2,         /* a CUDA runtime call or launch failed */
     MLE_ERR_UNSUPPORTED = 3,  /* shape/flag combination not implemented */
-    MLE_ERR_TIMEOUT = 4       /* a bounded device-side wait gave up */
+    MLE_ERR_TIMEOUT = 4       /* a bounded wait gave up (a device-side wait, or the host waiting for other ranks) */
 };
 
 enum mle_activation {

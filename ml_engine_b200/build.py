@@ -83,9 +83,13 @@ def _build_lib(name: str, sources, includes, extra_compile=(), link_libs=(), rpa
         for j in jobs:
             j.result()
     out = LIB / f"lib{name}.so"
-    if out.exists() and not jobs and all(o.stat().st_mtime <= out.stat().st_mtime for o in objs):
+    if out.exists() and not jobs and all(o.stat().st_mtime <= out.stat().st_mtime for o in objs) and \
+            Path(__file__).stat().st_mtime <= out.stat().st_mtime:
         return out
-    cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(out), *map(str, objs), *link_libs]
+    # calls inside the library bind to its own functions, whatever else the
+    # process has loaded (the reference's runtime defines the same C++ names)
+    cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", "-Xlinker", "-Bsymbolic-functions", "-o", str(out),
+           *map(str, objs), *link_libs]
     if rpath_origin:
         cmd += ["-Xlinker", "-rpath,$ORIGIN"]
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -144,6 +144,8 @@ static const char* chunk_base(const void* p) {
     return nullptr;
 }
 
+const void* arena_chunk_of(const void* p) { return chunk_base(p); }
+
 static void flush_zero_ranges() {
     auto& r = g_zero_ranges;
     if (r.empty()) return;

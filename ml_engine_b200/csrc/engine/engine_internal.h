@@ -66,6 +66,9 @@ void forget_ext(const NodeBackProp* n);
 // zero_grad leaves the buffer alone.
 void prepare_fusions(const graph_tree& nodes);
 
+// Base of the arena chunk (one device allocation) holding p, or nullptr.
+const void* arena_chunk_of(const void* p);
+
 // Gradient buffers zero_range skips (their first writer assigns them).
 void set_preassigned_grads(const std::vector<const float*>& grads);
 bool grad_preassigned(const float* grad);

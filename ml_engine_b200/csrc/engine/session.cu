@@ -66,6 +66,8 @@ struct Session {
     // input upload and the loss download
     cudaGraph_t graph_[2] = {nullptr, nullptr};
     cudaGraphExec_t exec[2] = {nullptr, nullptr};
+    // one captured graph per phase (device resident), for timing phases
+    cudaGraphExec_t phase_exec[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     std::unique_ptr<DataParallel> dp;
     size_t param_first = 0;
 };
@@ -322,7 +324,9 @@ void init_params(Session& S) {
     }
 }
 
-void run_phase(Session& S, int phase) {
+// Runs one phase of the step; returns MLE_OK or the data-parallel
+// reduction's status (phase 3), after which the step must not update.
+int run_phase(Session& S, int phase) {
     switch (phase) {
         case 0:
             S.go.zero_grad();
@@ -336,7 +340,7 @@ void run_phase(Session& S, int phase) {
             S.go.backward();
             break;
         case 3:
-            if (S.dp) S.dp->reduce_remaining(stream());
+            if (S.dp) return S.dp->reduce_remaining(stream());
             break;
         case 4:
             if (S.d.clip_norm > 0) S.go.clip_grad_norm(S.d.clip_norm);
@@ -345,17 +349,22 @@ void run_phase(Session& S, int phase) {
             S.go.ParameterUpdate(nullptr, false, S.d.lr, S.d.adamw != 0);
             break;
     }
+    return MLE_OK;
 }
 
-void step_body(Session& S, int upload, int download) {
+int step_body(Session& S, int upload, int download) {
     if (upload)
         for (auto& in : S.inputs)
             check_cuda(cudaMemcpyAsync(in.dev, in.host, (size_t)in.numel * 4, cudaMemcpyHostToDevice, S.stream),
                        "input upload");
-    for (int ph = 0; ph <= 5; ++ph) run_phase(S, ph);
+    for (int ph = 0; ph <= 5; ++ph) {
+        const int st_ = run_phase(S, ph);
+        if (st_ != MLE_OK) return st_;  // gradients not reduced: leave the parameters as they are
+    }
     if (download)
         check_cuda(cudaMemcpyAsync(S.loss_host, S.loss->output, sizeof(float), cudaMemcpyDeviceToHost, S.stream),
                    "loss download");
+    return MLE_OK;
 }
 
 void drop_graphs(Session& S) {
@@ -364,6 +373,10 @@ void drop_graphs(Session& S) {
         if (S.graph_[i]) cudaGraphDestroy(S.graph_[i]);
         S.exec[i] = nullptr;
         S.graph_[i] = nullptr;
+    }
+    for (auto& e : S.phase_exec) {
+        if (e) cudaGraphExecDestroy(e);
+        e = nullptr;
     }
 }
 
@@ -473,7 +486,8 @@ int mle_session_step(mle_session_t s, int upload, float* loss_out) {
                                        S->stream),
                        "loss download");
     } else {
-        step_body(*S, upload, loss_out != nullptr || upload);
+        const int st_ = step_body(*S, upload, loss_out != nullptr || upload);
+        if (st_ != MLE_OK) return st_;
     }
     if (loss_out) {
         const cudaError_t e = cudaStreamSynchronize(S->stream);
@@ -491,7 +505,8 @@ int mle_session_phase(mle_session_t s, int phase) {
         for (auto& in : S->inputs)
             check_cuda(cudaMemcpyAsync(in.dev, in.host, (size_t)in.numel * 4, cudaMemcpyHostToDevice, S->stream),
                        "input upload");
-    run_phase(*S, phase);
+    const int st_ = run_phase(*S, phase);
+    if (st_ != MLE_OK) return st_;
     if (phase == 1)
         check_cuda(cudaMemcpyAsync(S->loss_host, S->loss->output, sizeof(float), cudaMemcpyDeviceToHost, S->stream),
                    "loss download");
@@ -508,13 +523,50 @@ int mle_session_capture(mle_session_t s) {
     for (int g = 0; g < 2; ++g) {
         e = cudaStreamBeginCapture(S->stream, cudaStreamCaptureModeThreadLocal);
         if (e != cudaSuccess) return status_of(e);
-        step_body(*S, g, g);
+        const int st_ = step_body(*S, g, g);
         e = cudaStreamEndCapture(S->stream, &S->graph_[g]);
+        if (st_ != MLE_OK) {
+            drop_graphs(*S);
+            return st_;
+        }
         if (e != cudaSuccess) return status_of(e);
         e = cudaGraphInstantiate(&S->exec[g], S->graph_[g], 0);
         if (e != cudaSuccess) return status_of(e);
     }
     return MLE_OK;
+}
+
+int mle_session_capture_phases(mle_session_t s) {
+    Session* S = as_session(s);
+    if (!S) return MLE_ERR_ARG;
+    StreamScope sc(S->stream, S->d.gemm_mode);
+    for (auto& e : S->phase_exec) {
+        if (e) cudaGraphExecDestroy(e);
+        e = nullptr;
+    }
+    cudaError_t e = cudaStreamSynchronize(S->stream);
+    if (e != cudaSuccess) return status_of(e);
+    for (int ph = 0; ph < 6; ++ph) {
+        e = cudaStreamBeginCapture(S->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return status_of(e);
+        const int st_ = run_phase(*S, ph);
+        cudaGraph_t g = nullptr;
+        e = cudaStreamEndCapture(S->stream, &g);
+        if (st_ != MLE_OK || e != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return st_ != MLE_OK ? st_ : status_of(e);
+        }
+        e = cudaGraphInstantiate(&S->phase_exec[ph], g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return status_of(e);
+    }
+    return MLE_OK;
+}
+
+int mle_session_phase_replay(mle_session_t s, int phase) {
+    Session* S = as_session(s);
+    if (!S || phase < 0 || phase > 5 || !S->phase_exec[phase]) return MLE_ERR_ARG;
+    return status_of(cudaGraphLaunch(S->phase_exec[phase], S->stream));
 }
 
 int mle_session_sync(mle_session_t s) {
@@ -723,8 +775,8 @@ int mle_session_graph_edges(mle_session_t s, int* edges, int* programmatic) {
 int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int world, int bucket_mb) {
     Session* S = as_session(s);
     if (!S || !id128 || world <= 0 || rank < 0 || rank >= world) return MLE_ERR_ARG;
-    std::vector<std::pair<float*, int64_t>> grads;
-    for (AdamParameter* p : S->params) grads.push_back({p->grad, p->total});
+    std::vector<GradSpan> grads;
+    for (AdamParameter* p : S->params) grads.push_back({p->grad, p->total, arena_chunk_of(p->grad)});
     std::unique_ptr<DataParallel> dp(new DataParallel());
     const int st_ = dp->init(id128, rank, world, grads, bucket_mb, S->stream);
     if (st_ != MLE_OK) return st_;

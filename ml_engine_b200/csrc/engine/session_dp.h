@@ -17,19 +17,35 @@ struct GradBucket {
     int64_t count;  // floats, from base
 };
 
-// Buckets over the parameter gradients: (pointer, element count) pairs are
-// sorted by address and merged while they are contiguous (a gap of at most
-// 64 floats -- one 256-byte arena pad, which belongs to no tensor -- is
-// bridged) and the bucket stays within bucket_mb MiB; a tensor larger than
-// that forms a bucket of its own.
-std::vector<GradBucket> plan_buckets(std::vector<std::pair<float*, int64_t>> grads, int bucket_mb);
+// One parameter gradient: its device address, float count and the
+// allocation (arena chunk) that holds it.
+struct GradSpan {
+    float* base;
+    int64_t count;
+    const void* chunk;
+};
+
+// Buckets over the parameter gradients: spans are sorted by address and
+// merged while they are contiguous (a gap of at most 64 floats -- one
+// 256-byte arena pad, which belongs to no tensor -- is bridged), lie in the
+// same allocation (one NCCL buffer may not span two cudaMalloc ranges that
+// happen to be adjacent) and the bucket stays within bucket_mb MiB; a tensor
+// larger than that forms a bucket of its own.  bucket_mb <= 0 picks the size
+// from the gradient total (auto_bucket_mb).
+std::vector<GradBucket> plan_buckets(std::vector<GradSpan> grads, int bucket_mb);
+
+// Bucket size for `total_floats` of gradients: the smallest power of two of
+// MiB that splits them into at most four buckets, between 1 and 32 MiB, so
+// that a model whose gradients fit one 32 MiB bucket still reduces its first
+// buckets while the backward runs.
+int auto_bucket_mb(int64_t total_floats);
 
 class DataParallel {
    public:
     DataParallel() = default;
     ~DataParallel();
-    int init(const uint8_t* id128, int rank, int world, const std::vector<std::pair<float*, int64_t>>& grads,
-             int bucket_mb, cudaStream_t compute);
+    int init(const uint8_t* id128, int rank, int world, const std::vector<GradSpan>& grads, int bucket_mb,
+             cudaStream_t compute);
     // Backward of one step starts: every bucket waits for all its tensors.
     void begin_backward();
     // `grads` are complete once the work queued on `compute` (and on the
@@ -38,9 +54,12 @@ class DataParallel {
     // stream, overlapping the rest of the backward.
     void grads_done(const std::vector<float*>& grads, cudaStream_t compute);
     // Sums the buckets not started yet and makes `compute` wait for every
-    // reduction (before clip and update).
-    void reduce_remaining(cudaStream_t compute);
+    // reduction (before clip and update).  Returns MLE_OK, or the status of
+    // the first all-reduce NCCL refused during this step (later buckets of
+    // that step are then not issued).
+    int reduce_remaining(cudaStream_t compute);
     int world() const { return world_; }
+    int bucket_mb() const { return bucket_mb_; }
     int rank() const { return rank_; }
     int bucket_count() const { return (int)buckets_.size(); }
 
@@ -54,7 +73,9 @@ class DataParallel {
     void* comm_ = nullptr;
     cudaStream_t comm_stream_ = nullptr;
     cudaEvent_t done_ = nullptr;
-    int rank_ = 0, world_ = 1;
+    int rank_ = 0, world_ = 1, bucket_mb_ = 0;
+    int error_ = 0;
+    bool nonblocking_ = false;  // communicator made with blocking = 0
 };
 
 int nccl_unique_id(uint8_t* out128);

@@ -661,7 +661,7 @@ const char* mle_status_string(int status) {
         case MLE_ERR_ARG: return "invalid argument";
         case MLE_ERR_CUDA: return "CUDA error";
         case MLE_ERR_UNSUPPORTED: return "unsupported shape or flag";
-        case MLE_ERR_TIMEOUT: return "device-side wait timed out";
+        case MLE_ERR_TIMEOUT: return "a bounded wait timed out";
         default: return "unknown status";
     }
 }

@@ -66,10 +66,12 @@ def act_fwd(kind, x, y):
     _call("mle_act_fwd", kind, _p(x), _p(y), x.numel(), _s())
 
 
-def act_bwd(kind, x, gy, gx, bias_grad=None):
+def act_bwd(kind, x, gy, gx, bias_grad=None, assign=False):
+    """gx += gy * f'(x) (assign=True: gx = ...; mle_act_bwd_assign)."""
     cols = bias_grad.numel() if bias_grad is not None else 0
     rows = x.numel() // cols if cols else 0
-    _call("mle_act_bwd", kind, _p(x), _p(gy), _p(gx), x.numel(), _p(bias_grad), rows, cols, _s())
+    _call("mle_act_bwd_assign" if assign else "mle_act_bwd", kind, _p(x), _p(gy), _p(gx), x.numel(), _p(bias_grad),
+          rows, cols, _s())
 
 
 def bias_add_fwd(x, bias, y):

@@ -114,6 +114,14 @@ class Session:
     def capture(self):
         self._lib.call("mle_session_capture", self._h)
 
+    def capture_phases(self):
+        """One CUDA graph per phase (0 zero_grad, 1 forward, 2 backward,
+        3 gradient all-reduce, 4 clip, 5 update), device resident."""
+        self._lib.call("mle_session_capture_phases", self._h)
+
+    def phase_replay(self, ph):
+        self._lib.call("mle_session_phase_replay", self._h, ph)
+
     def sync(self):
         self._lib.call("mle_session_sync", self._h)
 
@@ -164,7 +172,7 @@ class Session:
         engine().call("mle_dp_unique_id", ctypes.addressof(buf))
         return bytes(buf)
 
-    def enable_dp(self, uid: bytes, rank: int, world: int, bucket_mb: int = 32):
+    def enable_dp(self, uid: bytes, rank: int, world: int, bucket_mb: int = 0):
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
         self._lib.call("mle_session_enable_dp", self._h, ctypes.addressof(buf), rank, world, bucket_mb)
 

@@ -70,7 +70,7 @@ def clip_and_update(params, grads, steps, lr, clip_norm=1.0, adamw=True, moments
 
 
 # ============================================================== MLP (config 1)
-def mlp_step(params, x, labels, classes=10, lr=1e-3, clip_norm=1.0, steps=None):
+def mlp_step(params, x, labels, classes=10, lr=1e-3, clip_norm=1.0, steps=None, update=True):
     W1, b1, W2, b2 = [p.reshape(s) for p, s in zip(params, [(x.shape[1], -1), (-1,), (-1, classes), (-1,)])]
     B = x.shape[0]
     h = _lin_fwd(x, W1, b1)
@@ -86,6 +86,8 @@ def mlp_step(params, x, labels, classes=10, lr=1e-3, clip_norm=1.0, steps=None):
     gW1, gb1 = np.zeros_like(W1), np.zeros_like(b1)
     _lin_bwd(x, W1, dh, np.zeros_like(x), gW1, gb1)
     grads = [g.ravel().copy() for g in (gW1, gb1, gW2, gb2)]
+    if not update:
+        return dict(loss=loss, grads=grads)
     raw = [g.copy() for g in grads]
     steps = steps or [1] * 4
     clip, new_p, m, v = clip_and_update([p.ravel() for p in params], grads, steps, lr, clip_norm)
@@ -192,7 +194,7 @@ def _ffn(tape, h, dh, W1, b1, W2, b2, g):
     return f2, df2
 
 
-def encoder_step(params, table, tokens, targets, batch, seq, d_model, heads, ffn, layers, vocab, lr=1e-3,
+def encoder_step(params, table, tokens, targets, batch, seq, d_model, heads, ffn, layers, vocab, lr=1e-3, update=True,
                  clip_norm=1.0, steps=None):
     """One step of the ENCODER session graph on the oracle."""
     B, S, D, H = batch, seq, d_model, heads
@@ -228,13 +230,15 @@ def encoder_step(params, table, tokens, targets, batch, seq, d_model, heads, ffn
     dlogits[:] = o.smce_bwd(probs, target, float(B)).reshape(rows, vocab)
     tape.backward()
     grads = [g.ravel().copy() for g in G]
+    if not update:
+        return dict(loss=loss, grads=grads)
     raw = [g.copy() for g in grads]
     steps = steps or [1] * len(grads)
     clip, new_p, m, v = clip_and_update([p.ravel() for p in P], grads, steps, lr, clip_norm)
     return dict(loss=loss, grads=raw, clipped=grads, clip=clip, params=new_p, m=m, v=v)
 
 
-def encdec_step(params, tables, src, tgt_in, tgt_out, batch, seq, d_model, heads, ffn, layers, vocab, lr=1e-3,
+def encdec_step(params, tables, src, tgt_in, tgt_out, batch, seq, d_model, heads, ffn, layers, vocab, lr=1e-3, update=True,
                 clip_norm=1.0, steps=None):
     """One step of the ENCDEC session graph on the oracle: `layers` encoder
     blocks over the source, `layers` decoder blocks (pre-LN masked
@@ -292,6 +296,8 @@ def encdec_step(params, tables, src, tgt_in, tgt_out, batch, seq, d_model, heads
     dlogits[:] = o.smce_bwd(probs, target, float(B)).reshape(rows, vocab)
     tape.backward()
     grads = [g.ravel().copy() for g in G]
+    if not update:
+        return dict(loss=loss, grads=grads)
     raw = [g.copy() for g in grads]
     steps = steps or [1] * len(grads)
     clip, new_p, m, v = clip_and_update([p.ravel() for p in P], grads, steps, lr, clip_norm)
@@ -391,7 +397,7 @@ def _residual_block(tape, x, dx, t, dt, prm, grd, cin, cout, stride):
 
 
 def unet_step(params, x_t, noise, batch, channels, image_size, base_width, t_embed, timestep, lr=1e-3,
-              clip_norm=1.0, steps=None):
+              clip_norm=1.0, steps=None, update=True):
     """One step of the UNET session graph on the oracle (U_NET::build_train,
     Engine/diffusion.cu:271-294, with three levels)."""
     N, C, S, w = batch, channels, image_size, base_width
@@ -453,6 +459,8 @@ def unet_step(params, x_t, noise, batch, channels, image_size, base_width, t_emb
     o.mse_bwd(y, target, dy)
     tape.backward()
     grads = [g.ravel().copy() for g in G]
+    if not update:
+        return dict(loss=loss, grads=grads)
     raw = [g.copy() for g in grads]
     steps = steps or [1] * len(grads)
     clip, new_p, m, v = clip_and_update([p.ravel() for p in P], grads, steps, lr, clip_norm)

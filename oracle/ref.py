@@ -50,6 +50,43 @@ _SIGS = {
 }
 
 
+_STEP_SIGS = {
+    "refstep_create": (I, [I, I, I, I, I, I, I, I, I, I, I]),
+    "refstep_destroy": (I, []),
+    "refstep_param_count": (I, []),
+    "refstep_param_numel": (L, [I]),
+    "refstep_param_step": (I, [I]),
+    "refstep_param_write": (I, [I, I, P]),
+    "refstep_param_read": (I, [I, I, P]),
+    "refstep_embedding_count": (I, []),
+    "refstep_embedding_write": (I, [I, P, L]),
+    "refstep_input_write": (I, [ctypes.c_char_p, P, L]),
+    "refstep_step": (I, [F, I, F, P]),
+    "refstep_time": (I, [I, I, F, I, F, P]),
+    "refstep_graph_gb": (D, []),
+}
+_STEP = None
+
+
+def step_available() -> bool:
+    return (_HERE / "_ref" / "librefstep.so").exists()
+
+
+def step_lib():
+    """The reference's own runtime with the BASELINE graphs (ref_step.cu)."""
+    global _STEP
+    if _STEP is None:
+        so = _HERE / "_ref" / "librefstep.so"
+        if not so.exists():
+            raise RuntimeError("oracle/_ref/librefstep.so is not built (needs the reference source tree)")
+        _STEP = ctypes.CDLL(str(so))
+        for name, (res, args) in _STEP_SIGS.items():
+            fn = getattr(_STEP, name)
+            fn.restype = res
+            fn.argtypes = args
+    return _STEP
+
+
 def available() -> bool:
     return (_HERE / "_ref" / "libmle_ref.so").exists()
 

@@ -3,6 +3,7 @@ and export every entry point their headers declare; the header prototypes
 parse into complete ctypes signatures; the oracle agrees with numpy on the
 formulas it restates."""
 import ctypes
+import os
 from pathlib import Path
 
 import numpy as np
@@ -95,3 +96,40 @@ def test_oracle_adamw_matches_closed_form(rng):
     mh, vh = m_ref / (1 - 0.9 ** t), v_ref / (1 - 0.999 ** t)
     w_ref = w0 - lr * (mh / (np.sqrt(vh) + 1e-8) + 0.01 * w0)
     assert rel_err(w, w_ref) <= 1e-6
+
+
+def test_reference_runtime_never_binds_to_this_library():
+    """The reference's runtime (oracle/_ref/librefstep.so, the baseline the
+    bench and the parity tests run) defines the same C++ names as
+    libmle_engine.so (the drop-in API).  Loaded into one process, neither
+    library may call into the other: librefstep.so exports only its
+    refstep_* entry points and binds its own calls locally, and
+    libmle_engine.so binds its own functions at link time
+    (-Bsymbolic-functions).  Checked with the dynamic linker's binding trace,
+    every symbol bound at load (LD_BIND_NOW)."""
+    import subprocess
+    import sys
+    so = ROOT / "oracle" / "_ref" / "librefstep.so"
+    if not so.exists():
+        pytest.skip("oracle/_ref/librefstep.so not built")
+    code = ("import sys; sys.path.insert(0, sys.argv[1]);"
+            "from ml_engine_b200._lib import engine, kernels; engine(); kernels();"
+            "from oracle import ref; ref.step_lib(); ref.lib()")
+    env = dict(os.environ, LD_BIND_NOW="1", LD_DEBUG="bindings", CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run([sys.executable, "-c", code, str(ROOT)], capture_output=True, text=True, env=env,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    bad = []
+    for line in out.stderr.splitlines():
+        if "binding file" not in line:
+            continue
+        src, _, dst = line.partition(" to ")
+        ours_src = "libmle_engine" in src or "libmle_kernels" in src
+        ref_src = "librefstep" in src or "libmle_ref" in src
+        if (ref_src and ("libmle_engine" in dst or "libmle_kernels" in dst)) or \
+                (ours_src and ("librefstep" in dst or "libmle_ref" in dst)):
+            bad.append(line.strip())
+    assert not bad, bad[:5]
+    exported = subprocess.run(["nm", "-D", "--defined-only", str(so)], capture_output=True, text=True).stdout
+    names = [ln.split()[-1] for ln in exported.splitlines() if ln.strip()]
+    assert names and all(n.startswith("refstep_") for n in names), [n for n in names if not n.startswith("refstep_")][:5]

@@ -115,3 +115,41 @@ def test_two_rank_dp_equals_one_gpu_global_batch(cuda):
     # parameters: each AdamW step moves an element by at most ~lr
     for i, (a, b) in enumerate(zip(res[0][1], w_one)):
         assert np.max(np.abs(a - b)) <= 2.05 * CFG["lr"] * STEPS, i
+
+
+_MISSING_RANK = r"""
+import sys, time
+sys.path.insert(0, sys.argv[1])
+from ml_engine_b200.session import Session
+from ml_engine_b200._lib import MLEError
+s = Session(config=1, batch=8, in_features=16, hidden=8, classes=4, seed=1)
+uid = Session.dp_unique_id()
+t0 = time.time()
+try:
+    s.enable_dp(uid, 0, 2)          # rank 1 of 2 never joins
+    print("JOINED")
+except MLEError as e:
+    print("ERROR", time.time() - t0, e)
+s.step()                            # the session still trains on its own
+print("STEP OK")
+"""
+
+
+def test_dp_missing_rank_times_out_on_host(cuda):
+    """A communicator whose other rank never joins: the set-up gives up on
+    the host after MLE_DP_TIMEOUT_S (non-blocking NCCL initialisation,
+    ncclCommAbort) and returns MLE_ERR_TIMEOUT instead of waiting for good;
+    nothing was launched on the GPU for the communicator, and the session
+    stays usable.  One process on one GPU; NVLS off."""
+    import subprocess
+    env = dict(os.environ, MLE_DP_TIMEOUT_S="3", NCCL_NVLS_ENABLE="0", CUDA_VISIBLE_DEVICES="0")
+    out = subprocess.run([sys.executable, "-c", _MISSING_RANK, str(ROOT)], capture_output=True, text=True,
+                         timeout=120, env=env)
+    assert out.returncode == 0, out.stderr[-3000:]
+    lines = out.stdout.splitlines()
+    err = [x for x in lines if x.startswith("ERROR")]
+    assert err and "JOINED" not in lines, out.stdout + out.stderr[-2000:]
+    waited = float(err[0].split()[1])
+    assert 2.5 <= waited <= 60.0, waited
+    assert "timed out" in err[0] or "TIMEOUT" in err[0].upper() or "wait" in err[0], err[0]
+    assert "STEP OK" in lines

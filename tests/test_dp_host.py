@@ -15,15 +15,53 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 
 
-def _plan(addrs, counts, bucket_mb, max_out=64):
+def _plan(addrs, counts, bucket_mb, max_out=64, chunks=None):
     from ml_engine_b200._lib import engine
     lib = engine()
     n = len(addrs)
     a = (ctypes.c_uint64 * max(n, 1))(*addrs)
     c = (ctypes.c_int64 * max(n, 1))(*counts)
+    ch = None if chunks is None else (ctypes.c_uint64 * max(n, 1))(*chunks)
     ob, oc, on = (ctypes.c_uint64 * max_out)(), (ctypes.c_int64 * max_out)(), ctypes.c_int()
-    lib.call("mle_dp_plan_buckets", a, c, n, bucket_mb, ob, oc, max_out, ctypes.byref(on))
+    lib.call("mle_dp_plan_buckets", a, c, ch, n, bucket_mb, ob, oc, max_out, ctypes.byref(on))
     return [(ob[i], oc[i]) for i in range(on.value)]
+
+
+def test_plan_never_spans_two_allocations():
+    """Two arena chunks that happen to be adjacent in the address space are
+    still two cudaMalloc ranges: one NCCL buffer may not cover both."""
+    base = 1 << 32
+    chunk = 1 << 20                      # bytes per (toy) chunk
+    addrs = [base, base + chunk - 4096, base + chunk, base + chunk + 4096]
+    counts = [1024, 1024, 1024, 1024]    # 4 KiB each: they touch across the boundary
+    ids = [base, base, base + chunk, base + chunk]
+    b = _plan(addrs, counts, bucket_mb=32, chunks=ids)
+    assert len(b) == 3                   # [0] alone (gap), [1] alone (chunk end), [2]+[3] merged
+    for start, cnt in b:
+        end = start + 4 * cnt
+        assert (start < base + chunk) == (end <= base + chunk)
+    merged = _plan(addrs, counts, bucket_mb=32)          # no chunk ids: one allocation
+    assert len(merged) == 2
+
+
+def test_auto_bucket_size():
+    from ml_engine_b200._lib import engine
+    lib = engine()
+    mib = (1 << 20) // 4
+    assert lib.mle_dp_auto_bucket_mb(0) == 1
+    assert lib.mle_dp_auto_bucket_mb(2_630_000) == 4        # configs[1]: 10.5 MB -> 3 buckets
+    assert lib.mle_dp_auto_bucket_mb(48_200_000) == 32      # configs[2]: 193 MB -> 6 buckets
+    for total in (1, mib, 7 * mib, 100 * mib, 10_000 * mib):
+        mb = lib.mle_dp_auto_bucket_mb(total)
+        assert mb in (1, 2, 4, 8, 16, 32)
+        assert mb == 32 or total <= 4 * mb * mib             # at most four buckets below the cap
+        assert mb == 1 or total > 4 * (mb // 2) * mib        # the smallest such power of two
+    addrs, cur = [], 1 << 32
+    for _ in range(40):
+        addrs.append(cur)
+        cur += 256 * 1024 * 4
+    b = _plan(addrs, [256 * 1024] * 40, bucket_mb=0)        # 40 MiB -> 16 MiB buckets
+    assert len(b) == 3
 
 
 def test_plan_merges_contiguous_runs_within_cap():
@@ -95,7 +133,7 @@ def test_bench_reference_arm_prints_once_under_torchrun():
         pytest.skip("oracle not built")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(ROOT / "bench.py"),
-           "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0"]
+           "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0", "--config", "mlp"]
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="2")
     out = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
