@@ -790,18 +790,22 @@ def run_native(args, rank, world, local_rank):
     if rank == 0 and not args.no_roofline:
         rows, gflop, gms = roofline_gemms(wl, B, dev, torch.cuda.current_stream(dev))
         achieved = gflop / (gms * 1e-3) / 1e12
-        traffic = None
+        traffic = traffic_alg = None
         prof = ROOT / "profiles" / "traffic.json"
         if prof.exists():
             tr = json.loads(prof.read_text()).get(wl)
             if tr:
                 traffic = tr.get("bytes_per_launch")
+                traffic_alg = tr.get("algorithmic_bytes_per_launch")
         line["roofline"] = {
             "bound": "tensor", "kernel": "gemm_tf32_kernel (tcgen05 kind::tf32, TMA, TMEM): every Linear backward "
                                          "product of the step (dX, dW) at the rank's token count",
             "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s", "frac": achieved / bf16_peak,
             "peak_kind": f"{peak_kind} bf16 dense burst (tf32 dense is half of it)",
-            "frac_of_tf32": achieved / tf32_peak, "traffic": traffic, "per_shape": rows}
+            "frac_of_tf32": achieved / tf32_peak, "traffic": traffic,
+            "traffic_note": "DRAM bytes per launch from profiles/traffic.json (ncu capture at 1/8 of the tokens, "
+                            "scaled); algorithmic bytes per launch: " + (f"{traffic_alg:.4g}" if traffic_alg else "n/a"),
+            "per_shape": rows}
     if rank == 0 and world == 1 and not args.no_ref_cuda:
         line["ref_cuda"] = ref_cuda_leg(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
