@@ -60,6 +60,15 @@ typedef struct mle_session_desc {
      * each step by OneHotEmbeddings.  Same loss and gradients, bit for bit;
      * the input is the int32 class ids either way. */
     int dense_targets;
+    /* embedding training: > 0 runs TextualEmbedding::EmbeddingUpdate
+     * (Engine/transformer.cu:233-245) on the encoder-side token table
+     * ("tokens" / "src") after each backward pass, an SGD step of this
+     * learning rate (the reference's LLM::train uses LEARNING_RATE = 1e-4,
+     * Engine/transformer.cu:869); 0 keeps every table frozen.  Under data
+     * parallelism each rank scatters its rows into a dense [vocab, d_model]
+     * delta, the deltas are summed with the gradient buckets and applied
+     * with the same 1/world average, so every rank keeps the same table. */
+    float embed_lr;
 } mle_session_desc;
 
 /* Builds the graph and allocates everything the step needs. */
@@ -148,9 +157,11 @@ int mle_session_param_step(mle_session_t s, int i, int* t);
 int mle_session_save(mle_session_t s, const char* path);
 int mle_session_load(mle_session_t s, const char* path);
 
-/* Embedding tables (transformer configs; gather only, not trained). */
+/* Embedding tables (transformer configs, in input order; trained only when
+ * desc.embed_lr > 0, the encoder-side one). */
 int mle_session_embedding_count(mle_session_t s);
 int mle_session_embedding_write(mle_session_t s, int i, const float* host, int64_t numel);
+int mle_session_embedding_read(mle_session_t s, int i, float* host, int64_t numel);
 
 /* Total device bytes held by the session's arenas. */
 int mle_session_device_bytes(mle_session_t s, int64_t* bytes);

@@ -195,12 +195,44 @@ int mle_pad_crop(const float* x, float* y, int batch, int depth, int a, int b, i
                  mle_stream_t stream);
 
 /* Embedding gather out[i, :] = table[keys[i], :] (GatherEmbeddings,
- * Engine/kernels.cu:2279-2296); keys < 0 leave the row untouched.
+ * Engine/kernels.cu:2279-2296); a key < 0 (masked) gives a zero row.
  * one_hot writes out[i, keys[i]] = 1 into a zeroed [n, vocab] matrix
  * (OneHotEmbeddings, Engine/kernels.cu:1551-1560). */
 int mle_embedding_gather(const int32_t* keys, const float* table, float* out, int64_t n_keys,
                          int dim, mle_stream_t stream);
 int mle_one_hot(const int32_t* keys, float* out, int64_t n_keys, int vocab, mle_stream_t stream);
+
+/* z = x * y (accumulate = 0) or z += x * y (1), elementwise: mulKernel
+ * (Engine/kernels.cu:139-145) as Multiply's forward and backward launch it. */
+int mle_mul(const float* x, const float* y, float* z, int64_t n, int accumulate, mle_stream_t stream);
+
+/* *count (device) = the number of NaN elements of x.  The reference's ISNAN
+ * (Includes/kernels.h:381-391) traps the GPU on the first NaN; this counts
+ * them and leaves the decision to the host (isNan prints and exits). */
+int mle_count_nan(const float* x, int64_t n, unsigned long long* count, mle_stream_t stream);
+
+/* *out (device) = the first index of the largest of x[0..n) (ArgMax,
+ * Engine/kernels.cu:2353-2366, one block instead of one thread). */
+int mle_argmax(const float* x, int64_t n, int* out, mle_stream_t stream);
+
+/* x = mean + std * N(0,1) (kind 0) or mean + std * U[0,1) (kind 1) from a
+ * counter-based generator keyed by `seed` (Noise / GaussianNoise /
+ * UnifNoise, Engine/engine.cu:3936-3944; the reference draws from cuRAND, so
+ * the values differ and the distributions agree). */
+int mle_fill_noise(float* x, int64_t n, float mean, float stdv, int kind, uint64_t seed, mle_stream_t stream);
+
+/* Embedding SGD update: table[key, :] -= lr * grad[r, :] for each of the
+ * `rows` gradient rows (grad [rows, dim], rows = batch * row_len tokens),
+ * the key of token t of batch b read at keys[b * key_stride + t]; keys < 0
+ * (masked tokens) are skipped.  Replaces KeyUpdate (Engine/kernels.cu:
+ * 1536-1549) as TextualEmbedding::EmbeddingUpdate launches it
+ * (Engine/transformer.cu:233-245; key_stride = MAX_CONTEXT_LEN there).
+ * Rows that share a key all add their contribution (atomically, in no
+ * fixed order); the reference's KeyUpdate lets such rows race, so its
+ * result is defined only when every key of the batch is distinct, where the
+ * two agree bit for bit (one fp32 add per element). */
+int mle_embedding_update(const int32_t* keys, const float* grad, float* table, int64_t rows, int dim, int row_len,
+                         int key_stride, float lr, mle_stream_t stream);
 
 /* ------------------------------------------------------------------ */
 /* normalisation                                                        */

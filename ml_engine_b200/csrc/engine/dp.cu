@@ -136,6 +136,7 @@ DataParallel::~DataParallel() {
     }
     for (cudaEvent_t e : ready_) cudaEventDestroy(e);
     for (cudaEvent_t e : ready_param_) cudaEventDestroy(e);
+    for (cudaEvent_t e : dense_ready_) cudaEventDestroy(e);
     if (done_) cudaEventDestroy(done_);
     if (comm_stream_) cudaStreamDestroy(comm_stream_);
 }
@@ -240,9 +241,28 @@ void DataParallel::grads_done(const std::vector<float*>& grads, cudaStream_t com
     }
 }
 
+int DataParallel::add_dense(float* p, int64_t n) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return MLE_ERR_CUDA;
+    dense_.push_back({p, n});
+    dense_ready_.push_back(e);
+    return MLE_OK;
+}
+
 int DataParallel::reduce_remaining(cudaStream_t compute) {
     for (int b = 0; b < (int)buckets_.size(); ++b)
         if (!issued_[b]) issue(b, compute);
+    for (size_t i = 0; i < dense_.size() && error_ == MLE_OK; ++i) {
+        check_cuda(cudaEventRecord(dense_ready_[i], compute), "dp dense ready");
+        check_cuda(cudaStreamWaitEvent(comm_stream_, dense_ready_[i], 0), "dp dense wait");
+        ncclResult_t r = nccl().AllReduce(dense_[i].base, dense_[i].base, (size_t)dense_[i].count, ncclFloat32,
+                                          ncclSum, (ncclComm_t)comm_, comm_stream_);
+        if (nonblocking_ && r == ncclInProgress) r = wait_comm((ncclComm_t)comm_, dp_timeout_s());
+        if (r != ncclSuccess) {
+            fprintf(stderr, "mle: ncclAllReduce failed: %s\n", nccl().GetErrorString ? nccl().GetErrorString(r) : "?");
+            error_ = MLE_ERR_CUDA;
+        }
+    }
     check_cuda(cudaEventRecord(done_, comm_stream_), "dp done");
     check_cuda(cudaStreamWaitEvent(compute, done_, 0), "dp join");
     return error_;

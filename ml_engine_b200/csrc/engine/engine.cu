@@ -258,19 +258,11 @@ void CheckError(const str& reason) {
 }
 
 // The reference's isNan launches a kernel that __trap()s on NaN
-// (Includes/kernels.h:382-392).  Here the tensor is copied to the host and
-// checked there; on NaN the process prints and exits as CheckError would.
+// (Includes/kernels.h:382-392).  Here the NaNs are counted on the device and
+// the host decides: on any it prints and exits as CheckError would.
 static void host_nan_check(const float* p, long long n, const str& what) {
     if (!p || n <= 0) return;
-    std::vector<float> h((size_t)n);
-    check_cuda(cudaStreamSynchronize(g_stream), what);
-    check_cuda(cudaMemcpy(h.data(), p, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost), what);
-    for (long long i = 0; i < n; ++i)
-        if (h[(size_t)i] != h[(size_t)i]) {
-            printf("NaN at idx=%lld\n", i);
-            std::cerr << "Runtime error in " << what << " has nan value" << std::endl;
-            std::exit(1);
-        }
+    mle::nan_check(what, p, n);
 }
 
 static void print_head(const float* p, long long n, const str& name) {

@@ -30,18 +30,11 @@
 #include <utility>
 #include <vector>
 
+#include <type_traits>
+
+#include "debugging_utils.h"
+#include "kernels.h"
 #include "mle_kernels.h"
-
-using str = std::string;
-
-// Includes/debugging_utils.h:10-14 and Includes/kernels.h:7-8
-static constexpr float XAVIER = 6.0f;
-static constexpr bool ADAMW = true;
-static constexpr float NORM = 1.0f;
-static constexpr float LEARNING_RATE = 1e-4f;
-static constexpr bool SHOULDNORM = false;
-static constexpr int BLOCK_SIZE = 32;
-static constexpr int THREADSPERBLOCK = 512;
 
 struct NodeBackProp;
 struct AdamParameter;
@@ -111,8 +104,6 @@ double* clip_workspace();
 
 }  // namespace mle
 
-void CheckError(const str& reason);
-
 struct NodeBackProp {
     str op_name;
     graph_tree inputs;
@@ -167,6 +158,44 @@ void Zerograd(AdamParameter X);
 void Zerograd(graph X);
 graph_tree topological_sort(const graph& root);
 
+namespace mle {
+// Counts the NaNs of a device array on the compute stream and waits; on any
+// prints `what` and exits(1).  The reference's ISNAN kernel traps the GPU
+// instead (Includes/kernels.h:381-391), which this never does.
+void nan_check(const str& what, const float* x, long long n);
+}  // namespace mle
+
+// NaN checks (Includes/engine.h:20-29, Engine/engine.cu:328-348): type 0
+// the output, otherwise the gradient.
+template <typename numeric>
+void isNan(const str name, const numeric* X, const long long total) {
+    static_assert(std::is_same<numeric, float>::value, "isNan checks float tensors");
+    mle::nan_check(name + "   has nan value", X, total);
+}
+void isNan(graph X, const int type = 0);
+void isNan(AdamParameter X, const int type = 0);
+
+// Host prints of a node's output (type 0) or gradient: every element per
+// batch and channel, or the top-left 3 x 5 x 5 corner (Engine/engine.cu:
+// 350-474).
+void printGPU(const graph X, const int type = 0);
+void printGPU(AdamParameter X, const int type = 0);
+void printHeadGPU(const graph X, const int type = 0);
+void printHeadGPU(AdamParameter X, const int type = 0);
+
+// Index of the largest element of a [1, 1, 1, D] node (the first on ties),
+// or a sample from its k largest entries taken in proportion to their values
+// (Engine/engine.cu:564-646); the overloads with X use that int of device
+// memory as the result slot, the others a slot of their own.
+int ArgMaxToCPU(const graph& input, int* X);
+int TopKSampleToCPU(const graph& input, int* X, const int k);
+int ArgMaxToCPU(const graph& input);
+int TopKSampleToCPU(const graph& input, const int k);
+
+// Fills a node's output with Gaussian ("gaussian") or uniform ("uniform")
+// noise of the given mean and spread (Engine/engine.cu:3936-3944).
+void Noise(const graph& input, const float mean = 0.f, const float std = 1.f, const str type = "gaussian");
+
 class Linear;
 
 class GraphOperations {
@@ -220,6 +249,8 @@ class GraphOperations {
     static graph Broadcast_Channel(const graph& A, const graph& B);
     static graph Scale(const graph& input, const float scale, const bool last = false);
     static graph Add(const graph& A, const graph& B, const bool last = false);
+    static graph Subtract(const graph& A, const graph& B, const bool last = false);
+    static graph Multiply(const graph& A, const graph& B);
 
     static graph MeanSquaredError(const graph& prediction, const graph& target, const bool last);
     static graph SoftMaxCrossEntropy(const graph& prediction, const graph& target, const bool last);
@@ -271,6 +302,8 @@ class GraphOperations {
 };
 
 inline graph operator+(const graph& A, const graph& B) { return GraphOperations::Add(A, B); }
+inline graph operator-(const graph& A, const graph& B) { return GraphOperations::Subtract(A, B); }
+inline graph operator*(const graph& A, const graph& B) { return GraphOperations::Multiply(A, B); }
 
 class Linear {
    private:
@@ -316,4 +349,42 @@ class Convolute2DT {
     void save(std::ofstream& f) const;
     void load(std::ifstream& f);
     graph forward(const graph& X);
+};
+
+// TimeMLPBlock (Includes/engine.h:282-290, Engine/engine.cu:3914-3924):
+// Linear, SiLU, Linear.
+class TimeMLPBlock {
+   public:
+    Linear L0, L1;
+    TimeMLPBlock(const int t_embed_dim, const int t_hidden);
+    graph forward(const graph& X);
+    void save(std::ofstream& f) const;
+    void load(std::ifstream& f);
+};
+
+// Multi_Linear_Residual_Block (Includes/engine.h:292-319, Engine/engine.cu:
+// 3926-3934): an input Linear, `num_residuals` residual groups of `layers`
+// hidden Linears with the caller's activation, each group added back and
+// normalised with the caller's norm, and an output Linear.
+class Multi_Linear_Residual_Block {
+   public:
+    const int input_dim, output_dim, residuals, hidden_dim, layers;
+    std::vector<Linear*> sequence;
+    Multi_Linear_Residual_Block(const int input, const int output, const int num_residuals, const int layers,
+                                const int hidden_size);
+    template <typename ActFn, typename NormFn>
+    graph forward(const graph& X, ActFn activation, NormFn norm) {
+        graph H = sequence[0]->forward(X);
+        for (int r = 0; r < residuals; ++r) {
+            graph A = H;
+            for (int j = 0; j < layers; ++j) {
+                const int idx = r * layers + j + 1;
+                if (idx < residuals * layers) A = activation(sequence[idx]->forward(A));
+            }
+            H = norm(H + A);
+        }
+        return sequence[residuals * layers]->forward(H);
+    }
+    void save(std::ofstream& f) const;
+    void load(std::ifstream& f);
 };

@@ -296,6 +296,53 @@ graph GraphOperations::Add(const graph& A, const graph& B, const bool last) {
     return node;
 }
 
+// --------------------------------------------------------- Subtract (:1674-1718)
+// A - B; backward dA += g, dB += -g (the reference's Accumulate with scale
+// -1, in double as its kernel computes it).  With last, the upstream
+// gradient is 1 and the output is the loss.
+graph GraphOperations::Subtract(const graph& A, const graph& B, const bool last) {
+    for (int i = 0; i < 4; ++i)
+        if (A->dim[i] != B->dim[i]) dims_mismatch("Dimension mismatch in subtract", A, B);
+    auto node = std::make_shared<NodeBackProp>(" Subtract", A->dim[0], A->dim[1], A->dim[2], A->dim[3], 1);
+    node->inputs = {A, B};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *ap = A.get(), *bp = B.get();
+    node->forward = [=]() {
+        check(mle_scale_add(ap->output, bp->output, nd->output, -1.0f, nd->total, st()), "Subtract forward");
+        if (last && g_loss_readback) {
+            check_cuda(cudaStreamSynchronize(stream()), "Subtract loss");
+            check_cuda(cudaMemcpy(&loss, nd->output, sizeof(float), cudaMemcpyDeviceToHost), "Subtract loss");
+        }
+    };
+    node->backward = [=]() {
+        if (last) check(mle_fill(nd->grad, 1.0f, nd->total, st()), "Subtract backward fill");
+        check(mle_accumulate(nd->grad, ap->grad, nd->total, 1.0, st()), "Subtract backward - A grad");
+        check(mle_accumulate(nd->grad, bp->grad, nd->total, -1.0, st()), "Subtract backward - B grad");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
+// --------------------------------------------------------- Multiply (:1720-1763)
+// Elementwise A * B; backward dA += g * B, dB += g * A.
+graph GraphOperations::Multiply(const graph& A, const graph& B) {
+    for (int i = 0; i < 4; ++i)
+        if (A->dim[i] != B->dim[i]) dims_mismatch("Dimension mismatch in Multiply ", A, B);
+    auto node = std::make_shared<NodeBackProp>("Multiply", A->dim[0], A->dim[1], A->dim[2], A->dim[3], 1);
+    node->inputs = {A, B};
+    GB += (double)node->total * sizeof(float) / (1ULL << 30);
+    NodeBackProp *nd = node.get(), *ap = A.get(), *bp = B.get();
+    node->forward = [=]() { check(mle_mul(ap->output, bp->output, nd->output, nd->total, 0, st()), "Multiply forward"); };
+    node->backward = [=]() {
+        check(mle_mul(nd->grad, bp->output, ap->grad, nd->total, 1, st()), "Multiply backward - A grad");
+        check(mle_mul(nd->grad, ap->output, bp->grad, nd->total, 1, st()), "Multiply backward - B grad");
+    };
+    node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+    node->free = [nd]() { nd->clear(); };
+    return node;
+}
+
 // ------------------------------------------------------------ Scale (:2521-2549)
 graph GraphOperations::Scale(const graph& input, const float scale, const bool last) {
     auto node =

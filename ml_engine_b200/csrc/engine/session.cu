@@ -61,6 +61,16 @@ struct Session {
     std::vector<Input> inputs;
     std::vector<std::function<void()>> prep;
     std::vector<std::pair<float*, int64_t>> emb;
+    // token tables trained by the embedding SGD update (desc.embed_lr > 0)
+    struct EmbTrain {
+        int32_t* keys;
+        float* table;
+        NodeBackProp* node;   // gathered embeddings; its grad is the update's input
+        float* delta;         // data parallelism: this rank's [vocab, D] update
+        int64_t rows, table_n;
+        int dim, row_len;
+    };
+    std::vector<EmbTrain> emb_train;
     float* loss_host = nullptr;
     // captured steps: [0] device-resident (no host copies), [1] with the
     // input upload and the loss download
@@ -217,7 +227,11 @@ graph decoder_block(Session& S, graph x, const graph& enc, int Sq, const std::st
 }
 
 // token ids -> embedding node (gather) and target ids -> one-hot node
-graph token_input(Session& S, const std::string& name, int vocab) {
+// token ids -> gathered embeddings (TextualEmbedding::forward,
+// Engine/transformer.cu:176-192).  A trained table's node clears its
+// gradient with the step's zero_grad, as the reference's embedding node does
+// (DataLoading::forward, Engine/transformer.cu:547-548).
+graph token_input(Session& S, const std::string& name, int vocab, bool train = false) {
     const int B = S.d.batch, Sq = S.d.seq_len, D = S.d.d_model;
     auto node = std::make_shared<NodeBackProp>(name + " Embeddings", B, 1, Sq, D, 1);
     float* table = arena_alloc(ARENA_PARAM, (int64_t)vocab * D, name + " embedding table");
@@ -227,7 +241,33 @@ graph token_input(Session& S, const std::string& name, int vocab) {
     NodeBackProp* nd = node.get();
     const int64_t nk = (int64_t)B * Sq;
     S.prep.push_back([=]() { check(mle_embedding_gather(keys, table, nd->output, nk, D, st()), "GatherEmbeddings"); });
+    if (train) {
+        node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+        S.emb_train.push_back({keys, table, nd, nullptr, nk, (int64_t)vocab * D, D, Sq});
+    }
     return node;
+}
+
+// EmbeddingUpdate after the backward pass: straight into the table, or
+// (data parallelism) into this rank's delta, summed over the ranks with the
+// gradients and applied in the update phase.
+void embedding_scatter(Session& S) {
+    for (auto& e : S.emb_train) {
+        float* dst = e.table;
+        if (S.dp) {
+            check_cuda(cudaMemsetAsync(e.delta, 0, (size_t)e.table_n * 4, stream()), "embedding delta clear");
+            dst = e.delta;
+        }
+        check(mle_embedding_update(e.keys, e.node->grad, dst, e.rows, e.dim, e.row_len, e.row_len, S.d.embed_lr,
+                                   st()),
+              "EmbeddingUpdate");
+    }
+}
+
+void embedding_apply(Session& S) {
+    if (!S.dp) return;
+    for (auto& e : S.emb_train)
+        check(mle_accumulate(e.delta, e.table, e.table_n, 1.0 / S.dp->world(), st()), "EmbeddingUpdate (averaged)");
 }
 
 graph onehot_target(Session& S, const std::string& name, int rows_b, int rows_s, int classes) {
@@ -265,7 +305,7 @@ void build(Session& S) {
         graph logits = l2->forward(GraphOperations::RELU(l1->forward(x)));
         S.loss = class_loss(S, logits, "labels", d.batch, 1, d.classes);
     } else if (d.config == MLE_CFG_ENCODER) {
-        graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tokens", d.vocab));
+        graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tokens", d.vocab, d.embed_lr > 0));
         for (int l = 0; l < d.layers; ++l) x = encoder_block(S, x, d.seq_len, "Enc" + std::to_string(l));
         Linear* proj = new_linear(S, d.d_model, d.vocab, "Projection");
         S.loss = class_loss(S, proj->forward(x), "targets", d.batch, d.seq_len, d.vocab);
@@ -293,7 +333,7 @@ void build(Session& S) {
         graph y = new_conv(S, w, C, 1, 1, 0, "Output Convolution")->forward(d2);
         S.loss = GraphOperations::MeanSquaredError(y, target, true);
     } else if (d.config == MLE_CFG_ENCDEC) {
-        graph e = GraphOperations::MatrixPositionalEncoding(token_input(S, "src", d.vocab));
+        graph e = GraphOperations::MatrixPositionalEncoding(token_input(S, "src", d.vocab, d.embed_lr > 0));
         for (int l = 0; l < d.layers; ++l) e = encoder_block(S, e, d.seq_len, "Enc" + std::to_string(l));
         graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tgt_in", d.vocab));
         for (int l = 0; l < d.layers; ++l) x = decoder_block(S, x, e, d.seq_len, "Dec" + std::to_string(l));
@@ -338,6 +378,7 @@ int run_phase(Session& S, int phase) {
         case 2:
             if (S.dp) S.dp->begin_backward();
             S.go.backward();
+            embedding_scatter(S);
             break;
         case 3:
             if (S.dp) return S.dp->reduce_remaining(stream());
@@ -346,6 +387,7 @@ int run_phase(Session& S, int phase) {
             if (S.d.clip_norm > 0) S.go.clip_grad_norm(S.d.clip_norm);
             break;
         case 5:
+            embedding_apply(S);
             S.go.ParameterUpdate(nullptr, false, S.d.lr, S.d.adamw != 0);
             break;
     }
@@ -710,6 +752,14 @@ int mle_session_embedding_write(mle_session_t s, int i, const float* host, int64
     return status_of(e);
 }
 
+int mle_session_embedding_read(mle_session_t s, int i, float* host, int64_t numel) {
+    Session* S = as_session(s);
+    if (!S || i < 0 || i >= (int)S->emb.size() || !host || numel != S->emb[i].second) return MLE_ERR_ARG;
+    cudaError_t e = cudaStreamSynchronize(S->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(host, S->emb[i].first, (size_t)numel * 4, cudaMemcpyDeviceToHost);
+    return status_of(e);
+}
+
 int mle_session_device_bytes(mle_session_t s, int64_t* bytes) {
     if (!s || !bytes) return MLE_ERR_ARG;
     double gib = 0;
@@ -780,6 +830,10 @@ int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int w
     std::unique_ptr<DataParallel> dp(new DataParallel());
     const int st_ = dp->init(id128, rank, world, grads, bucket_mb, S->stream);
     if (st_ != MLE_OK) return st_;
+    for (auto& e : S->emb_train) {
+        if (!e.delta) e.delta = arena_alloc(ARENA_WS, e.table_n, "embedding delta");
+        if (dp->add_dense(e.delta, e.table_n) != MLE_OK) return MLE_ERR_CUDA;
+    }
     S->dp = std::move(dp);
     S->go.set_grad_prescale(1.0f / (float)world);
     DataParallel* d = S->dp.get();

@@ -58,6 +58,9 @@ class DataParallel {
     // the first all-reduce NCCL refused during this step (later buckets of
     // that step are then not issued).
     int reduce_remaining(cudaStream_t compute);
+    // A dense buffer summed over the ranks after the gradient buckets, in
+    // every step (the data-parallel embedding-table update).
+    int add_dense(float* p, int64_t n);
     int world() const { return world_; }
     int bucket_mb() const { return bucket_mb_; }
     int rank() const { return rank_; }
@@ -70,6 +73,8 @@ class DataParallel {
     std::vector<char> issued_;
     std::vector<cudaEvent_t> ready_, ready_param_;
     std::vector<std::pair<float*, int>> bucket_of_;  // grad pointer -> bucket, sorted
+    std::vector<GradBucket> dense_;
+    std::vector<cudaEvent_t> dense_ready_;
     void* comm_ = nullptr;
     cudaStream_t comm_stream_ = nullptr;
     cudaEvent_t done_ = nullptr;

@@ -102,13 +102,15 @@ __global__ void fill_kernel_scalar(float* __restrict__ x, float v, int64_t n) {
 }
 
 // op codes for the binary map kernel
-enum MapOp { OP_COPY = 0, OP_ACCUM = 1, OP_SCALE_WRITE = 2, OP_SCALE_ADD = 3 };
+enum MapOp { OP_COPY = 0, OP_ACCUM = 1, OP_SCALE_WRITE = 2, OP_SCALE_ADD = 3, OP_MUL = 4, OP_MUL_ACC = 5 };
 
 template <int OP>
 __device__ __forceinline__ float map1(float x, float y_old, float other, float fscale, double dscale) {
     if (OP == OP_COPY) return x;
     if (OP == OP_ACCUM) return (float)((double)y_old + dscale * (double)x);  // Y += scale*X in double
     if (OP == OP_SCALE_WRITE) return fscale * x;
+    if (OP == OP_MUL) return x * other;
+    if (OP == OP_MUL_ACC) return y_old + x * other;
     return x + fscale * other;  // OP_SCALE_ADD: z = x + scale*y
 }
 
@@ -127,8 +129,8 @@ __global__ void map_kernel(const float* __restrict__ x, const float* __restrict_
         for (int64_t j = i0; j < n4; j += stride) {
             const float4 a = x4[j];
             float4 yo = make_float4(0.f, 0.f, 0.f, 0.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (OP == OP_ACCUM) yo = y4[j];
-            if (OP == OP_SCALE_ADD) b = o4[j];
+            if (OP == OP_ACCUM || OP == OP_MUL_ACC) yo = y4[j];
+            if (OP == OP_SCALE_ADD || OP == OP_MUL || OP == OP_MUL_ACC) b = o4[j];
             float4 r;
             r.x = map1<OP>(a.x, yo.x, b.x, fscale, dscale);
             r.y = map1<OP>(a.y, yo.y, b.y, fscale, dscale);
@@ -139,8 +141,8 @@ __global__ void map_kernel(const float* __restrict__ x, const float* __restrict_
         tail = n4 << 2;
     }
     for (int64_t j = tail + i0; j < n; j += stride) {
-        const float yo = (OP == OP_ACCUM) ? y[j] : 0.f;
-        const float b = (OP == OP_SCALE_ADD) ? other[j] : 0.f;
+        const float yo = (OP == OP_ACCUM || OP == OP_MUL_ACC) ? y[j] : 0.f;
+        const float b = (OP == OP_SCALE_ADD || OP == OP_MUL || OP == OP_MUL_ACC) ? other[j] : 0.f;
         y[j] = map1<OP>(x[j], yo, b, fscale, dscale);
     }
 }
@@ -634,6 +636,107 @@ __global__ void gather_kernel(const int32_t* __restrict__ keys, const float* __r
     }
 }
 
+// table[keys[r], :] -= lr * grad[r, :] for every row r whose key is >= 0:
+// a quarter-warp per 16-byte chunk run of a row, vector atomics so repeated
+// keys accumulate every row's contribution (KeyUpdate,
+// Engine/kernels.cu:1536-1549, lets them race).
+__global__ void key_update_kernel(const int32_t* __restrict__ keys, const float* __restrict__ grad,
+                                  float* __restrict__ table, int64_t rows, int dim, int key_stride, int row_len,
+                                  float lr, int vec) {
+    pdl_entry();
+    const int per_row = vec ? dim / 4 : dim;
+    const int64_t total = rows * per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t r = i / per_row;
+        const int c = (int)(i - r * per_row);
+        // token r of batch r / row_len reads its key at the batch's stride
+        const int64_t b = r / row_len, t = r - b * row_len;
+        const int k = keys[b * key_stride + t];
+        if (k < 0) continue;
+        if (vec) {
+            const float4 g = *reinterpret_cast<const float4*>(grad + r * dim + 4 * c);
+            atomicAdd(reinterpret_cast<float4*>(table + (int64_t)k * dim + 4 * c),
+                      make_float4(-lr * g.x, -lr * g.y, -lr * g.z, -lr * g.w));
+        } else {
+            atomicAdd(table + (int64_t)k * dim + c, -lr * grad[r * dim + c]);
+        }
+    }
+}
+
+// Number of NaN elements (a block-local count, one atomic per block).
+__global__ void count_nan_kernel(const float* __restrict__ x, int64_t n, unsigned long long* __restrict__ count) {
+    unsigned long long c = 0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) c += (x[i] != x[i]);
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_down_sync(0xffffffffu, c, o);
+    __shared__ unsigned long long part[32];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long t = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+        if (t) atomicAdd(count, t);
+    }
+}
+
+// First index of the largest element (a strict > scan keeps the earliest of
+// equal maxima, NaNs never win): one block, per-thread strided scan, then a
+// shared-memory tree that prefers the lower index on ties.
+__global__ void argmax_kernel(const float* __restrict__ x, int64_t n, int* __restrict__ out) {
+    __shared__ float sv[1024];
+    __shared__ int64_t si[1024];
+    float best = -INFINITY;
+    int64_t bi = -1;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i];
+        if (bi < 0 || v > best) {
+            best = v;
+            bi = i;
+        }
+    }
+    sv[threadIdx.x] = best;
+    si[threadIdx.x] = bi;
+    __syncthreads();
+    for (int off = blockDim.x / 2; off > 0; off >>= 1) {
+        if ((int)threadIdx.x < off) {
+            const float ov = sv[threadIdx.x + off];
+            const int64_t oi = si[threadIdx.x + off];
+            const float mv = sv[threadIdx.x];
+            const int64_t mi = si[threadIdx.x];
+            const bool take = oi >= 0 && (mi < 0 || ov > mv || (ov == mv && oi < mi) || (mv != mv && ov == ov));
+            if (take) {
+                sv[threadIdx.x] = ov;
+                si[threadIdx.x] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *out = (int)(si[0] < 0 ? 0 : si[0]);
+}
+
+// Counter-based noise (not the reference's cuRAND stream: the values differ,
+// the distributions do not): splitmix64 of (seed, index) -> two uniforms;
+// kind 0 Gaussian (Box-Muller) mean + std * z, kind 1 uniform mean + std * u
+// with u in [0, 1) (GaussianNoise / UnifNoise, Engine/engine.cu:3936-3944).
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void noise_kernel(float* __restrict__ x, int64_t n, float mean, float stdv, int kind, uint64_t seed) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint64_t r = mix64(seed ^ mix64((uint64_t)i));
+        const float u1 = ((uint32_t)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);          // (0, 1)
+        const float u2 = ((uint32_t)(r & 0xFFFFFFu)) * (1.0f / 16777216.0f);            // [0, 1)
+        if (kind == 0) x[i] = mean + stdv * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+        else x[i] = mean + stdv * u2;
+    }
+}
+
 __global__ void one_hot_kernel(const int32_t* __restrict__ keys, float* __restrict__ out, int64_t n, int vocab) {
     pdl_entry();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -978,6 +1081,46 @@ int mle_embedding_gather(const int32_t* keys, const float* table, float* out, in
     const int64_t total = n_keys * dim;
     if (total == 0) return MLE_OK;
     launch_k(gather_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), keys, table, out, total, dim);
+    return launch_status();
+}
+
+int mle_embedding_update(const int32_t* keys, const float* grad, float* table, int64_t rows, int dim, int row_len,
+                         int key_stride, float lr, mle_stream_t stream) {
+    if (rows < 0 || dim <= 0 || row_len <= 0 || key_stride < row_len || !keys || !grad || !table) return MLE_ERR_ARG;
+    if (rows == 0) return MLE_OK;
+    const int vec = (dim % 4 == 0 && aligned16(grad) && aligned16(table)) ? 1 : 0;
+    const int64_t total = rows * (vec ? dim / 4 : dim);
+    launch_k(key_update_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), keys, grad, table, rows,
+             dim, key_stride, row_len, lr, vec);
+    return launch_status();
+}
+
+int mle_mul(const float* x, const float* y, float* z, int64_t n, int accumulate, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && (!x || !y || !z))) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    if (accumulate) MLE_MAP_LAUNCH(OP_MUL_ACC, x, y, z, n, 1.f, 1.0);
+    else MLE_MAP_LAUNCH(OP_MUL, x, y, z, n, 1.f, 1.0);
+    return launch_status();
+}
+
+int mle_count_nan(const float* x, int64_t n, unsigned long long* count, mle_stream_t stream) {
+    if (n < 0 || !count || (n > 0 && !x)) return MLE_ERR_ARG;
+    if (cudaMemsetAsync(count, 0, sizeof(unsigned long long), as_stream(stream)) != cudaSuccess) return MLE_ERR_CUDA;
+    if (n == 0) return MLE_OK;
+    count_nan_kernel<<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(x, n, count);
+    return launch_status();
+}
+
+int mle_argmax(const float* x, int64_t n, int* out, mle_stream_t stream) {
+    if (n <= 0 || !x || !out) return MLE_ERR_ARG;
+    argmax_kernel<<<1, 1024, 0, as_stream(stream)>>>(x, n, out);
+    return launch_status();
+}
+
+int mle_fill_noise(float* x, int64_t n, float mean, float stdv, int kind, uint64_t seed, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && !x) || (kind != 0 && kind != 1)) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    noise_kernel<<<grid_for(n, kThreads), kThreads, 0, as_stream(stream)>>>(x, n, mean, stdv, kind, seed);
     return launch_status();
 }
 

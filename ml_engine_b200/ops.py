@@ -118,6 +118,14 @@ def embedding_gather(keys, table, out):
     _call("mle_embedding_gather", _p(keys), _p(table), _p(out), keys.numel(), table.shape[-1], _s())
 
 
+def embedding_update(keys, grad, table, row_len, lr, key_stride=None):
+    """table[keys[b, t]] -= lr * grad[b * row_len + t] (int32 keys)."""
+    dim = table.shape[-1]
+    rows = grad.numel() // dim
+    _call("mle_embedding_update", _p(keys), _p(grad), _p(table), rows, dim, row_len,
+          key_stride if key_stride is not None else row_len, lr, _s())
+
+
 def one_hot(keys, out, vocab):
     _call("mle_one_hot", _p(keys), _p(out), keys.numel(), vocab, _s())
 

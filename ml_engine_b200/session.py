@@ -34,6 +34,7 @@ class SessionDesc(ctypes.Structure):
         ("channels", ctypes.c_int), ("image_size", ctypes.c_int), ("base_width", ctypes.c_int),
         ("t_embed", ctypes.c_int), ("timestep", ctypes.c_int),
         ("dense_targets", ctypes.c_int),
+        ("embed_lr", ctypes.c_float),
     ]
 
 
@@ -153,6 +154,12 @@ class Session:
     def write_embedding(self, i, table):
         table = np.ascontiguousarray(table, np.float32).ravel()
         self._lib.call("mle_session_embedding_write", self._h, i, table.ctypes.data, table.size)
+
+    def read_embedding(self, i):
+        n = self.desc.vocab * self.desc.d_model
+        out = np.empty(n, np.float32)
+        self._lib.call("mle_session_embedding_read", self._h, i, out.ctypes.data, n)
+        return out
 
     def device_bytes(self):
         b = ctypes.c_int64()

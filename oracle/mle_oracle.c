@@ -207,6 +207,23 @@ void oracle_embedding_gather(const int32_t* keys, const float* table, float* out
         for (int d = 0; d < dim; ++d) out[i * dim + d] = keys[i] < 0 ? 0.0f : table[(int64_t)keys[i] * dim + d];
 }
 
+/* KeyUpdate (Engine/kernels.cu:1536-1549): EmbedSpace[key * D + d] +=
+ * -lr * grad[i] for every gradient element whose token key is >= 0; token t
+ * of batch b reads its key at keys[b * max_clen + t].  Sequential, so rows
+ * sharing a key all contribute (in row order), which is what the kernel
+ * computes when its threads do not race. */
+void oracle_key_update(float* table, const float* grad, const int32_t* keys, int clen, int max_clen, int dim,
+                       float lr, int64_t total) {
+    for (int64_t i = 0; i < total; ++i) {
+        const int64_t b = i / ((int64_t)clen * dim);
+        const int64_t kr = i % ((int64_t)clen * dim);
+        const int64_t t = kr / dim, d = kr % dim;
+        const int key = keys[b * max_clen + t];
+        if (key < 0) continue;
+        table[(int64_t)key * dim + d] += -lr * grad[i];
+    }
+}
+
 void oracle_one_hot(const int32_t* keys, float* out, int64_t n_keys, int vocab) {
     for (int64_t i = 0; i < n_keys; ++i)
         if (keys[i] >= 0 && keys[i] < vocab) out[i * vocab + keys[i]] = 1.0f;

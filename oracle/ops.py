@@ -43,6 +43,7 @@ _SIGS = {
     "oracle_channel_split": (None, [P, P, P, I, I, I, L]),
     "oracle_embedding_gather": (None, [P, P, P, L, I]),
     "oracle_one_hot": (None, [P, P, L, I]),
+    "oracle_key_update": (None, [P, P, P, I, I, I, F, L]),
     "oracle_bcmm": (None, [I, P, P, P, I, I, I, I, I, I, I, I, I, F]),
     "oracle_gemm": (None, [P, P, P, L, L, L, I, I, I]),
     "oracle_layernorm_fwd": (None, [P, P, P, P, I, I, I, I, F]),
@@ -178,6 +179,13 @@ def embedding_gather(keys, table):
     out = np.empty((keys.size, table.shape[-1]), np.float32)
     lib().oracle_embedding_gather(_p(keys), _p(f32(table)), _p(out), keys.size, table.shape[-1])
     return out
+
+
+def key_update(table, grad, keys, clen, max_clen, lr):
+    """table (modified in place) -= lr * grad rows at their keys (KeyUpdate)."""
+    keys = np.ascontiguousarray(keys, np.int32)
+    lib().oracle_key_update(_p(table), _p(f32(grad)), _p(keys), clen, max_clen, table.shape[-1], lr, grad.size)
+    return table
 
 
 def one_hot(keys, vocab):

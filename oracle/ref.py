@@ -46,6 +46,7 @@ _SIGS = {
     "ref_convT2d_fwd": [P, P, P, P, I, I, I, I, I, I, I, I, I],
     "ref_convT2d_bwd_w": [P, P, P, I, I, I, I, I, I, I, I, I],
     "ref_convT2d_bwd_x": [P, P, P, I, I, I, I, I, I, I, I, I],
+    "ref_key_update": [P, P, P, I, I, I, F, L],
     "ref_sync": [],
 }
 
@@ -60,6 +61,8 @@ _STEP_SIGS = {
     "refstep_param_read": (I, [I, I, P]),
     "refstep_embedding_count": (I, []),
     "refstep_embedding_write": (I, [I, P, L]),
+    "refstep_embedding_read": (I, [I, P, L]),
+    "refstep_set_embed_update": (I, [I]),
     "refstep_input_write": (I, [ctypes.c_char_p, P, L]),
     "refstep_step": (I, [F, I, F, P]),
     "refstep_time": (I, [I, I, F, I, F, P]),

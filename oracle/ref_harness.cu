@@ -239,6 +239,15 @@ int ref_adam(float* w, const float* g, int n, int t, float* m, float* v, float b
     return (int)cudaGetLastError();
 }
 
+/* TextualEmbedding::EmbeddingUpdate (Engine/transformer.cu:233-245) on a
+ * [batch, 1, clen, dim] embedding node's gradient. */
+int ref_key_update(float* table, const float* grad, const int* keys, int clen, int max_clen, int dim, float lr,
+                   long long total) {
+    KeyUpdate<<<blocks(total, THREADSPERBLOCK), THREADSPERBLOCK>>>(table, grad, keys, clen, max_clen, dim, lr,
+                                                                   (unsigned long long)total);
+    return (int)cudaGetLastError();
+}
+
 int ref_sync(void) { return (int)cudaDeviceSynchronize(); }
 
 

@@ -74,6 +74,7 @@ struct RefModel {
     std::vector<TargetInput> targets;
     graph x_input;  // MLP input
     double* clip_ws = nullptr;
+    bool embed_update = false;  // TextualEmbedding::EmbeddingUpdate on the encoder-side tokens
     float* softmax = nullptr;
     float* softmax_arr = nullptr;
     float* max_arr = nullptr;
@@ -144,6 +145,13 @@ graph token_input(RefModel& M, const std::string& name) {
     cudaMemset(t.table, 0, (size_t)M.vocab * M.d_model * sizeof(float));
     cudaMalloc((void**)&t.keys, (size_t)M.batch * M.seq * sizeof(int));
     cudaMemset(t.keys, 0, (size_t)M.batch * M.seq * sizeof(int));
+    // the reference's embedding node clears its gradient with zero_grad
+    // (DataLoading::forward, Engine/transformer.cu:547-548)
+    NodeBackProp* nd = t.node.get();
+    t.node->zero_grad = [nd]() {
+        const int tpb = THREADSPERBLOCK;
+        fillKernel<<<(int)((nd->total + tpb - 1) / tpb), tpb>>>(nd->grad, 0.0f, (unsigned long long)nd->total);
+    };
     M.tokens.push_back(t);
     return t.node;
 }
@@ -238,6 +246,15 @@ void run_phase(RefModel& M, int phase, float lr, int adamw, float clip_norm) {
         M.go.forward(nullptr, true);
     } else if (phase == 1) {
         M.go.backward();
+        if (M.embed_update && !M.tokens.empty()) {
+            // embedder.EmbeddingUpdate(enc, "E") (Engine/transformer.cu:869,
+            // 233-245): KeyUpdate at LEARNING_RATE with the encoder-side keys
+            TokenInput& t = M.tokens[0];
+            const unsigned long long total = (unsigned long long)t.node->total;
+            const int tpb = THREADSPERBLOCK;
+            KeyUpdate<<<(int)((total + tpb - 1) / tpb), tpb>>>(t.table, t.node->grad, t.keys, M.seq, M.seq,
+                                                               M.d_model, LEARNING_RATE, total);
+        }
     } else {
         if (clip_norm > 0) clip(M, clip_norm);
         M.go.ParameterUpdate(nullptr, false, lr, adamw != 0);
@@ -325,6 +342,21 @@ int refstep_param_read(int i, int which, float* host) {
 }
 
 int refstep_embedding_count(void) { return g_model ? (int)g_model->tokens.size() : 0; }
+
+/* on != 0: every step runs the reference's embedding update on the
+ * encoder-side table after the backward pass. */
+int refstep_set_embed_update(int on) {
+    if (!g_model) return (int)cudaErrorInvalidValue;
+    g_model->embed_update = on != 0;
+    return 0;
+}
+
+int refstep_embedding_read(int i, float* host, long long numel) {
+    if (!g_model || i < 0 || i >= (int)g_model->tokens.size()) return (int)cudaErrorInvalidValue;
+    TokenInput& t = g_model->tokens[i];
+    if (numel != (long long)t.vocab * g_model->d_model) return (int)cudaErrorInvalidValue;
+    return (int)cudaMemcpy(host, t.table, (size_t)numel * sizeof(float), cudaMemcpyDeviceToHost);
+}
 
 int refstep_embedding_write(int i, const float* host, long long numel) {
     if (!g_model || i < 0 || i >= (int)g_model->tokens.size()) return (int)cudaErrorInvalidValue;

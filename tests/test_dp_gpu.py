@@ -35,7 +35,7 @@ def _problem():
     return params, table, toks, tgts
 
 
-def _run(session, params, table, toks, tgts, rows):
+def _run(session, params, table, toks, tgts, rows, embed=False):
     for i, p in enumerate(params):
         session.write_param(i, p)
     session.write_embedding(0, table)
@@ -47,10 +47,13 @@ def _run(session, params, table, toks, tgts, rows):
         if k == 0:
             session.capture()
     n = len(params)
-    return losses, [session.read_param(i, 0) for i in range(n)], [session.read_param(i, 1) for i in range(n)]
+    w = [session.read_param(i, 0) for i in range(n)]
+    if embed:   # the trained embedding table joins the compared tensors
+        w.append(session.read_embedding(0))
+    return losses, w, [session.read_param(i, 1) for i in range(n)]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, embed_lr=0.0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       NCCL_NVLS_ENABLE="0")
     sys.path.insert(0, str(ROOT))
@@ -59,18 +62,23 @@ def _worker(rank, world, port, q):
     dist.init_process_group("gloo", timeout=timedelta(seconds=60))   # carries the NCCL id only
     from ml_engine_b200.session import Session
     params, table, toks, tgts = _problem()
-    s = Session(batch=B // world, **CFG)
+    s = Session(batch=B // world, embed_lr=embed_lr, **CFG)
     uid = [Session.dp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     s.enable_dp(uid[0], rank, world)
-    losses, w, g = _run(s, params, table, toks, tgts, slice(rank * B // world, (rank + 1) * B // world))
+    losses, w, g = _run(s, params, table, toks, tgts, slice(rank * B // world, (rank + 1) * B // world),
+                        embed=embed_lr > 0)
     q.put((rank, losses, w, g))
     dist.barrier()
     s.close()
     dist.destroy_process_group()
 
 
-def test_two_rank_dp_equals_one_gpu_global_batch(cuda):
+@pytest.mark.parametrize("embed_lr", [0.0, 1e-3], ids=["frozen_table", "trained_table"])
+def test_two_rank_dp_equals_one_gpu_global_batch(cuda, embed_lr):
+    """With a trained table the ranks' embedding deltas are summed with the
+    gradient buckets and averaged, so the table moves as one GPU's with the
+    whole batch would (compared with the parameters below)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import socket as _s
@@ -80,7 +88,7 @@ def test_two_rank_dp_equals_one_gpu_global_batch(cuda):
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, embed_lr)) for r in range(2)]
     for p in procs:
         p.start()
     try:
@@ -96,8 +104,8 @@ def test_two_rank_dp_equals_one_gpu_global_batch(cuda):
     assert all(p.exitcode == 0 for p in procs)
     from ml_engine_b200.session import Session
     params, table, toks, tgts = _problem()
-    s = Session(batch=B, **CFG)
-    losses, w_one, g_one = _run(s, params, table, toks, tgts, slice(0, B))
+    s = Session(batch=B, embed_lr=embed_lr, **CFG)
+    losses, w_one, g_one = _run(s, params, table, toks, tgts, slice(0, B), embed=embed_lr > 0)
     s.close()
     # both ranks hold identical parameters and clipped gradients after every step
     for a, b in zip(res[0][1] + res[0][2], res[1][1] + res[1][2]):
@@ -115,6 +123,10 @@ def test_two_rank_dp_equals_one_gpu_global_batch(cuda):
     # parameters: each AdamW step moves an element by at most ~lr
     for i, (a, b) in enumerate(zip(res[0][1], w_one)):
         assert np.max(np.abs(a - b)) <= 2.05 * CFG["lr"] * STEPS, i
+    if embed_lr > 0:   # the table's total update over the steps, TF32 tolerance
+        moved_dp, moved_one = res[0][1][-1] - table, w_one[-1] - table
+        assert np.linalg.norm(moved_one) > 0
+        assert norm_err(moved_dp, moved_one) <= 2e-3, norm_err(moved_dp, moved_one)
 
 
 _MISSING_RANK = r"""

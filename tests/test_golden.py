@@ -135,3 +135,20 @@ def test_golden_conv():
         assert rel_err(orc.convT2d_fwd(x, w, b, pad, s), d[f"t{i}_y"]) <= RTOL_EXACT
         assert rel_err(orc.convT2d_bwd_w(x, dy, w.shape, pad, s), d[f"t{i}_gw"]) <= RTOL_EXACT
         assert rel_err(orc.convT2d_bwd_x(dy, w, x.shape, pad, s), d[f"t{i}_gx"]) <= RTOL_EXACT
+
+
+def test_oracle_key_update_is_a_scatter_add():
+    """The oracle's KeyUpdate restatement against numpy's unbuffered
+    scatter-add (np.add.at), repeated and masked keys included."""
+    from oracle import ops as orc
+    rng = np.random.default_rng(5)
+    batch, clen, max_clen, dim, vocab, lr = 3, 40, 48, 16, 25, 1e-2
+    keys = np.full((batch, max_clen), -1, np.int32)
+    keys[:, :clen] = rng.integers(-1, vocab, (batch, clen))
+    grad = rng.standard_normal((batch * clen, dim)).astype(np.float32)
+    table = rng.standard_normal((vocab, dim)).astype(np.float32)
+    got = orc.key_update(table.copy(), grad, keys, clen, max_clen, lr)
+    want = table.astype(np.float64).copy()
+    k = keys[:, :clen].ravel()
+    np.add.at(want, k[k >= 0], -lr * grad[k >= 0].astype(np.float64))
+    assert np.max(np.abs(got - want)) <= 1e-6 * np.max(np.abs(want))

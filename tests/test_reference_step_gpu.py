@@ -56,14 +56,21 @@ def _chk(st, what):
     assert st == 0, f"{what}: cuda error {st}"
 
 
-def _run_pair(L, kw, rargs, seed, lr=1e-3):
+def _run_pair(L, kw, rargs, seed, lr=1e-3, embed=False):
     """One step of our session and of the reference on identical state.
     Returns (session, p0, ours, ref, ref2): per-tensor clipped gradients and
-    weights, losses, and a second reference step from the same state."""
+    weights, losses, and a second reference step from the same state.  With
+    `embed`, both also train the encoder-side embedding table (token ids are
+    then distinct within the batch, the only case where the reference's
+    racing KeyUpdate is defined) and ours["emb"], ref["emb"] hold its update
+    (table after the step minus before)."""
     from ml_engine_b200.session import Session
     rng = np.random.default_rng(seed)
     s = Session(lr=lr, **kw)
     _chk(L.refstep_create(*rargs), "refstep_create")
+    if embed:
+        _chk(L.refstep_set_embed_update(1), "refstep_set_embed_update")
+    tab0 = None
     try:
         n = L.refstep_param_count()
         assert n == len(s.param_sizes)
@@ -84,8 +91,10 @@ def _run_pair(L, kw, rargs, seed, lr=1e-3):
                 tab = (rng.standard_normal(V * D) * 0.02).astype(np.float32)
                 s.write_embedding(e, tab)
                 _chk(L.refstep_embedding_write(e, tab.ctypes.data, tab.size), "embedding")
+                if e == 0:
+                    tab0 = tab
             for name, arr in s.inputs.items():
-                ids = rng.integers(0, V, arr.size).astype(np.int32)
+                ids = (rng.permutation(V)[: arr.size] if embed else rng.integers(0, V, arr.size)).astype(np.int32)
                 arr[:] = ids
                 _chk(L.refstep_input_write(name.encode(), ids.ctypes.data, ids.size), name)
         loss = s.step()
@@ -101,6 +110,11 @@ def _run_pair(L, kw, rargs, seed, lr=1e-3):
         rl = ctypes.c_float()
         _chk(L.refstep_step(lr, 1, 1.0, ctypes.addressof(rl)), "refstep_step")
         ref = dict(loss=rl.value, g=ref_state(1), w=ref_state(0))
+        if embed:
+            t1 = np.empty_like(tab0)
+            _chk(L.refstep_embedding_read(0, t1.ctypes.data, t1.size), "embedding read")
+            ref["emb"] = t1 - tab0
+            _chk(L.refstep_embedding_write(0, tab0.ctypes.data, tab0.size), "embedding")
         for i in range(n):   # the same state again: the reference's own spread
             z = np.zeros(s.param_sizes[i], np.float32)
             _chk(L.refstep_param_write(i, 0, p0[i].ctypes.data), "param")
@@ -111,6 +125,8 @@ def _run_pair(L, kw, rargs, seed, lr=1e-3):
     finally:
         _chk(L.refstep_destroy(), "refstep_destroy")
     ours = dict(loss=loss, g=[s.read_param(i, 1) for i in range(n)], w=[s.read_param(i, 0) for i in range(n)])
+    if embed:
+        ours["emb"] = s.read_embedding(0) - tab0
     return s, p0, ours, ref, ref2
 
 
@@ -177,4 +193,20 @@ def test_encdec_configs2_dims_step_equals_reference(cuda, gemm_mode):
     L = _ref()
     s, p0, ours, ref, ref2 = _run_pair(L, dict(ED, gemm_mode=gemm_mode), ED_REF, seed=23)
     _check(s, p0, ours, ref, ref2, exact=gemm_mode == 1, maxrel_tc=3e-3)
+    s.close()
+
+
+def test_encoder_embedding_update_equals_reference(cuda):
+    """configs[1] with the embedding table trained as the reference's
+    LLM::train does (EmbeddingUpdate at LEARNING_RATE = 1e-4 after the
+    backward pass, Engine/transformer.cu:869), fp32 products: the table's
+    update equals the reference's to the fp32 elementwise bound (its
+    gradient, the embedding node's, comes through the whole backward)."""
+    L = _ref()
+    s, p0, ours, ref, ref2 = _run_pair(L, dict(ENC, gemm_mode=1, embed_lr=1e-4), ENC_REF, seed=24, embed=True)
+    _check(s, p0, ours, ref, ref2, exact=True)
+    d_ours, d_ref = ours["emb"], ref["emb"]
+    assert np.count_nonzero(d_ref) > 0.9 * d_ref.size          # every vocabulary row was a token once
+    err = float(np.max(np.abs(d_ours - d_ref)) / np.max(np.abs(d_ref)))
+    assert err <= RTOL_EXACT, err
     s.close()
