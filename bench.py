@@ -764,7 +764,8 @@ def run_native(args, rank, world, local_rank):
            "algorithmic_elementwise_gb": bbytes / 1e9, "achieved_tflops": bflop / (b_ms * 1e-3) / 1e12,
            "roofline_ms": t_roof, "frac": t_roof / b_ms,
            "tensor_frac_of_tf32": bflop / (b_ms * 1e-3) / 1e12 / tf32_peak,
-           "how": "backward phase replayed alone (its own captured graph, CUDA events); roofline time = "
+           "how": "backward phase replayed alone (its own captured graph, CUDA events; with N > 1 the graph "
+                  "also holds the gradient all-reduce it starts); roofline time = "
                   "algorithmic tensor FLOP at TF32 dense (half the measured bf16 peak) + algorithmic "
                   "non-GEMM backward bytes at the measured HBM copy bandwidth"}
     s.close()   # the remaining legs allocate their own buffers
@@ -795,8 +796,11 @@ def run_native(args, rank, world, local_rank):
         if prof.exists():
             tr = json.loads(prof.read_text()).get(wl)
             if tr:
-                traffic = tr.get("bytes_per_launch")
-                traffic_alg = tr.get("algorithmic_bytes_per_launch")
+                # captured for the profile's token count; every operand but
+                # the weights grows with the tokens a rank processes
+                scale = B * WORKLOADS[wl]["cfg"].get("seq_len", 1) / tr.get("tokens", 1)
+                traffic = tr.get("bytes_per_launch") * scale
+                traffic_alg = tr.get("algorithmic_bytes_per_launch") * scale
         line["roofline"] = {
             "bound": "tensor", "kernel": "gemm_tf32_kernel (tcgen05 kind::tf32, TMA, TMEM): every Linear backward "
                                          "product of the step (dX, dW) at the rank's token count",

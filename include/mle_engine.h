@@ -123,7 +123,10 @@ int mle_get_grad_first_write(void);
  * device resident: no upload, no loss download) as its own CUDA graph, so a
  * caller can time phases on the device; mle_session_phase_replay(s, ph)
  * launches phase ph's graph on the session stream.  Replaying phases 0..5 in
- * order is one training step. */
+ * order is one training step.  Under data parallelism phase 2's graph also
+ * holds phase 3 (the bucket reductions the backward starts on the
+ * communication stream are joined there), and replaying phase 3 does
+ * nothing. */
 int mle_session_capture_phases(mle_session_t s);
 int mle_session_phase_replay(mle_session_t s, int phase);
 

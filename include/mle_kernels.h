@@ -221,18 +221,25 @@ int mle_argmax(const float* x, int64_t n, int* out, mle_stream_t stream);
  * the values differ and the distributions agree). */
 int mle_fill_noise(float* x, int64_t n, float mean, float stdv, int kind, uint64_t seed, mle_stream_t stream);
 
-/* Embedding SGD update: table[key, :] -= lr * grad[r, :] for each of the
- * `rows` gradient rows (grad [rows, dim], rows = batch * row_len tokens),
- * the key of token t of batch b read at keys[b * key_stride + t]; keys < 0
- * (masked tokens) are skipped.  Replaces KeyUpdate (Engine/kernels.cu:
+/* Embedding SGD update, the replacement of KeyUpdate (Engine/kernels.cu:
  * 1536-1549) as TextualEmbedding::EmbeddingUpdate launches it
- * (Engine/transformer.cu:233-245; key_stride = MAX_CONTEXT_LEN there).
- * Rows that share a key all add their contribution (atomically, in no
- * fixed order); the reference's KeyUpdate lets such rows race, so its
- * result is defined only when every key of the batch is distinct, where the
- * two agree bit for bit (one fp32 add per element). */
-int mle_embedding_update(const int32_t* keys, const float* grad, float* table, int64_t rows, int dim, int row_len,
-                         int key_stride, float lr, mle_stream_t stream);
+ * (Engine/transformer.cu:233-245; key_stride = MAX_CONTEXT_LEN there):
+ *   grad_scatter  gsum[key, :] += grad[r, :] for each of the `rows` gradient
+ *                 rows (grad [rows, dim], rows = batch * row_len tokens; the
+ *                 key of token t of batch b at keys[b * key_stride + t];
+ *                 keys < 0, masked tokens, skipped);
+ *   apply         table = fma(neg_lr, gsum, table) over n = vocab * dim;
+ *   update        both, with gsum (vocab * dim floats, caller-owned) cleared
+ *                 first: table[key] -= lr * (sum of its rows' gradients).
+ * For a key that occurs once this is the reference's own arithmetic (one
+ * fused multiply-add per element), bit for bit.  The reference adds repeated
+ * keys' rows without atomics, so they race and its result is undefined;
+ * here their gradients are summed first (atomically, in no fixed order). */
+int mle_embedding_grad_scatter(const int32_t* keys, const float* grad, float* gsum, int64_t rows, int dim,
+                               int row_len, int key_stride, mle_stream_t stream);
+int mle_embedding_apply(float* table, const float* gsum, int64_t n, float neg_lr, mle_stream_t stream);
+int mle_embedding_update(const int32_t* keys, const float* grad, float* table, float* gsum, int vocab, int64_t rows,
+                         int dim, int row_len, int key_stride, float lr, mle_stream_t stream);
 
 /* ------------------------------------------------------------------ */
 /* normalisation                                                        */

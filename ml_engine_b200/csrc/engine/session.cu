@@ -66,9 +66,9 @@ struct Session {
         int32_t* keys;
         float* table;
         NodeBackProp* node;   // gathered embeddings; its grad is the update's input
-        float* delta;         // data parallelism: this rank's [vocab, D] update
+        float* gsum;          // [vocab, D]: the step's gradient per table row
         int64_t rows, table_n;
-        int dim, row_len;
+        int dim, row_len, vocab;
     };
     std::vector<EmbTrain> emb_train;
     float* loss_host = nullptr;
@@ -243,31 +243,35 @@ graph token_input(Session& S, const std::string& name, int vocab, bool train = f
     S.prep.push_back([=]() { check(mle_embedding_gather(keys, table, nd->output, nk, D, st()), "GatherEmbeddings"); });
     if (train) {
         node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
-        S.emb_train.push_back({keys, table, nd, nullptr, nk, (int64_t)vocab * D, D, Sq});
+        float* gsum = arena_alloc(ARENA_WS, (int64_t)vocab * D, name + " embedding gradient");
+        S.emb_train.push_back({keys, table, nd, gsum, nk, (int64_t)vocab * D, D, Sq, vocab});
     }
     return node;
 }
 
-// EmbeddingUpdate after the backward pass: straight into the table, or
-// (data parallelism) into this rank's delta, summed over the ranks with the
-// gradients and applied in the update phase.
+// EmbeddingUpdate after the backward pass: the step's gradient rows summed
+// per table row; on one GPU applied at once, under data parallelism summed
+// over the ranks with the gradient buckets and applied in the update phase
+// with the 1/world average.
 void embedding_scatter(Session& S) {
     for (auto& e : S.emb_train) {
-        float* dst = e.table;
-        if (S.dp) {
-            check_cuda(cudaMemsetAsync(e.delta, 0, (size_t)e.table_n * 4, stream()), "embedding delta clear");
-            dst = e.delta;
+        if (!S.dp) {
+            check(mle_embedding_update(e.keys, e.node->grad, e.table, e.gsum, e.vocab, e.rows, e.dim, e.row_len,
+                                       e.row_len, S.d.embed_lr, st()),
+                  "EmbeddingUpdate");
+            continue;
         }
-        check(mle_embedding_update(e.keys, e.node->grad, dst, e.rows, e.dim, e.row_len, e.row_len, S.d.embed_lr,
-                                   st()),
-              "EmbeddingUpdate");
+        check_cuda(cudaMemsetAsync(e.gsum, 0, (size_t)e.table_n * 4, stream()), "embedding gradient clear");
+        check(mle_embedding_grad_scatter(e.keys, e.node->grad, e.gsum, e.rows, e.dim, e.row_len, e.row_len, st()),
+              "EmbeddingUpdate (scatter)");
     }
 }
 
 void embedding_apply(Session& S) {
     if (!S.dp) return;
     for (auto& e : S.emb_train)
-        check(mle_accumulate(e.delta, e.table, e.table_n, 1.0 / S.dp->world(), st()), "EmbeddingUpdate (averaged)");
+        check(mle_embedding_apply(e.table, e.gsum, e.table_n, -S.d.embed_lr / (float)S.dp->world(), st()),
+              "EmbeddingUpdate (averaged)");
 }
 
 graph onehot_target(Session& S, const std::string& name, int rows_b, int rows_s, int classes) {
@@ -589,9 +593,14 @@ int mle_session_capture_phases(mle_session_t s) {
     cudaError_t e = cudaStreamSynchronize(S->stream);
     if (e != cudaSuccess) return status_of(e);
     for (int ph = 0; ph < 6; ++ph) {
+        // under data parallelism the backward issues bucket reductions on
+        // the communication stream that only phase 3 joins: both phases
+        // go into phase 2's graph, and phase 3's is empty
+        if (ph == 3 && S->dp) continue;
         e = cudaStreamBeginCapture(S->stream, cudaStreamCaptureModeThreadLocal);
         if (e != cudaSuccess) return status_of(e);
-        const int st_ = run_phase(*S, ph);
+        int st_ = run_phase(*S, ph);
+        if (ph == 2 && S->dp && st_ == MLE_OK) st_ = run_phase(*S, 3);
         cudaGraph_t g = nullptr;
         e = cudaStreamEndCapture(S->stream, &g);
         if (st_ != MLE_OK || e != cudaSuccess) {
@@ -607,7 +616,9 @@ int mle_session_capture_phases(mle_session_t s) {
 
 int mle_session_phase_replay(mle_session_t s, int phase) {
     Session* S = as_session(s);
-    if (!S || phase < 0 || phase > 5 || !S->phase_exec[phase]) return MLE_ERR_ARG;
+    if (!S || phase < 0 || phase > 5) return MLE_ERR_ARG;
+    if (phase == 3 && S->dp && S->phase_exec[2]) return MLE_OK;  // captured with phase 2
+    if (!S->phase_exec[phase]) return MLE_ERR_ARG;
     return status_of(cudaGraphLaunch(S->phase_exec[phase], S->stream));
 }
 
@@ -830,10 +841,8 @@ int mle_session_enable_dp(mle_session_t s, const uint8_t* id128, int rank, int w
     std::unique_ptr<DataParallel> dp(new DataParallel());
     const int st_ = dp->init(id128, rank, world, grads, bucket_mb, S->stream);
     if (st_ != MLE_OK) return st_;
-    for (auto& e : S->emb_train) {
-        if (!e.delta) e.delta = arena_alloc(ARENA_WS, e.table_n, "embedding delta");
-        if (dp->add_dense(e.delta, e.table_n) != MLE_OK) return MLE_ERR_CUDA;
-    }
+    for (auto& e : S->emb_train)
+        if (dp->add_dense(e.gsum, e.table_n) != MLE_OK) return MLE_ERR_CUDA;
     S->dp = std::move(dp);
     S->go.set_grad_prescale(1.0f / (float)world);
     DataParallel* d = S->dp.get();

@@ -636,13 +636,12 @@ __global__ void gather_kernel(const int32_t* __restrict__ keys, const float* __r
     }
 }
 
-// table[keys[r], :] -= lr * grad[r, :] for every row r whose key is >= 0:
-// a quarter-warp per 16-byte chunk run of a row, vector atomics so repeated
-// keys accumulate every row's contribution (KeyUpdate,
-// Engine/kernels.cu:1536-1549, lets them race).
-__global__ void key_update_kernel(const int32_t* __restrict__ keys, const float* __restrict__ grad,
-                                  float* __restrict__ table, int64_t rows, int dim, int key_stride, int row_len,
-                                  float lr, int vec) {
+// gsum[keys[r], :] += grad[r, :] for every gradient row r whose key is >= 0
+// (token t of batch b reads its key at keys[b * key_stride + t]); rows that
+// share a key meet in atomic adds.
+__global__ void key_grad_scatter_kernel(const int32_t* __restrict__ keys, const float* __restrict__ grad,
+                                        float* __restrict__ gsum, int64_t rows, int dim, int key_stride, int row_len,
+                                        int vec) {
     pdl_entry();
     const int per_row = vec ? dim / 4 : dim;
     const int64_t total = rows * per_row;
@@ -650,18 +649,35 @@ __global__ void key_update_kernel(const int32_t* __restrict__ keys, const float*
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
         const int64_t r = i / per_row;
         const int c = (int)(i - r * per_row);
-        // token r of batch r / row_len reads its key at the batch's stride
         const int64_t b = r / row_len, t = r - b * row_len;
         const int k = keys[b * key_stride + t];
         if (k < 0) continue;
-        if (vec) {
-            const float4 g = *reinterpret_cast<const float4*>(grad + r * dim + 4 * c);
-            atomicAdd(reinterpret_cast<float4*>(table + (int64_t)k * dim + 4 * c),
-                      make_float4(-lr * g.x, -lr * g.y, -lr * g.z, -lr * g.w));
-        } else {
-            atomicAdd(table + (int64_t)k * dim + c, -lr * grad[r * dim + c]);
-        }
+        if (vec) atomicAdd(reinterpret_cast<float4*>(gsum + (int64_t)k * dim + 4 * c),
+                           *reinterpret_cast<const float4*>(grad + r * dim + 4 * c));
+        else atomicAdd(gsum + (int64_t)k * dim + c, grad[r * dim + c]);
     }
+}
+
+// table = fma(neg_lr, gsum, table): the reference's `EmbedSpace += -lr *
+// grad` is one fused multiply-add per element, so a table row whose key
+// occurred once gets exactly the reference's value.
+__global__ void key_apply_kernel(float* __restrict__ table, const float* __restrict__ gsum, int64_t n, float neg_lr) {
+    pdl_entry();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t n4 = n >> 2;
+    float4* t4 = reinterpret_cast<float4*>(table);
+    const float4* g4 = reinterpret_cast<const float4*>(gsum);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const float4 g = g4[i];
+        float4 t = t4[i];
+        t.x = __fmaf_rn(neg_lr, g.x, t.x);
+        t.y = __fmaf_rn(neg_lr, g.y, t.y);
+        t.z = __fmaf_rn(neg_lr, g.z, t.z);
+        t.w = __fmaf_rn(neg_lr, g.w, t.w);
+        t4[i] = t;
+    }
+    for (int64_t i = (n4 << 2) + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        table[i] = __fmaf_rn(neg_lr, gsum[i], table[i]);
 }
 
 // Number of NaN elements (a block-local count, one atomic per block).
@@ -1084,15 +1100,32 @@ int mle_embedding_gather(const int32_t* keys, const float* table, float* out, in
     return launch_status();
 }
 
-int mle_embedding_update(const int32_t* keys, const float* grad, float* table, int64_t rows, int dim, int row_len,
-                         int key_stride, float lr, mle_stream_t stream) {
-    if (rows < 0 || dim <= 0 || row_len <= 0 || key_stride < row_len || !keys || !grad || !table) return MLE_ERR_ARG;
+int mle_embedding_grad_scatter(const int32_t* keys, const float* grad, float* gsum, int64_t rows, int dim,
+                               int row_len, int key_stride, mle_stream_t stream) {
+    if (rows < 0 || dim <= 0 || row_len <= 0 || key_stride < row_len || !keys || !grad || !gsum) return MLE_ERR_ARG;
     if (rows == 0) return MLE_OK;
-    const int vec = (dim % 4 == 0 && aligned16(grad) && aligned16(table)) ? 1 : 0;
+    const int vec = (dim % 4 == 0 && aligned16(grad) && aligned16(gsum)) ? 1 : 0;
     const int64_t total = rows * (vec ? dim / 4 : dim);
-    launch_k(key_update_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), keys, grad, table, rows,
-             dim, key_stride, row_len, lr, vec);
+    launch_k(key_grad_scatter_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), keys, grad, gsum,
+             rows, dim, key_stride, row_len, vec);
     return launch_status();
+}
+
+int mle_embedding_apply(float* table, const float* gsum, int64_t n, float neg_lr, mle_stream_t stream) {
+    if (n < 0 || (n > 0 && (!table || !gsum)) || !aligned16(table) || !aligned16(gsum)) return MLE_ERR_ARG;
+    if (n == 0) return MLE_OK;
+    launch_k(key_apply_kernel, grid_for(n / 4 + 1, kThreads), kThreads, 0, as_stream(stream), table, gsum, n, neg_lr);
+    return launch_status();
+}
+
+int mle_embedding_update(const int32_t* keys, const float* grad, float* table, float* gsum, int vocab, int64_t rows,
+                         int dim, int row_len, int key_stride, float lr, mle_stream_t stream) {
+    if (vocab <= 0 || dim <= 0 || !gsum) return MLE_ERR_ARG;
+    const int64_t n = (int64_t)vocab * dim;
+    if (cudaMemsetAsync(gsum, 0, (size_t)n * sizeof(float), as_stream(stream)) != cudaSuccess) return MLE_ERR_CUDA;
+    int st = mle_embedding_grad_scatter(keys, grad, gsum, rows, dim, row_len, key_stride, stream);
+    if (st != MLE_OK) return st;
+    return mle_embedding_apply(table, gsum, n, -lr, stream);
 }
 
 int mle_mul(const float* x, const float* y, float* z, int64_t n, int accumulate, mle_stream_t stream) {

@@ -118,11 +118,14 @@ def embedding_gather(keys, table, out):
     _call("mle_embedding_gather", _p(keys), _p(table), _p(out), keys.numel(), table.shape[-1], _s())
 
 
-def embedding_update(keys, grad, table, row_len, lr, key_stride=None):
-    """table[keys[b, t]] -= lr * grad[b * row_len + t] (int32 keys)."""
-    dim = table.shape[-1]
+def embedding_update(keys, grad, table, row_len, lr, key_stride=None, gsum=None):
+    """table[k] -= lr * (sum of the grad rows whose key is k); int32 keys,
+    token t of batch b at keys[b * key_stride + t]."""
+    vocab, dim = table.shape[0], table.shape[-1]
     rows = grad.numel() // dim
-    _call("mle_embedding_update", _p(keys), _p(grad), _p(table), rows, dim, row_len,
+    if gsum is None:
+        gsum = torch.empty_like(table)
+    _call("mle_embedding_update", _p(keys), _p(grad), _p(table), _p(gsum), vocab, rows, dim, row_len,
           key_stride if key_stride is not None else row_len, lr, _s())
 
 

@@ -220,7 +220,8 @@ void oracle_key_update(float* table, const float* grad, const int32_t* keys, int
         const int64_t t = kr / dim, d = kr % dim;
         const int key = keys[b * max_clen + t];
         if (key < 0) continue;
-        table[(int64_t)key * dim + d] += -lr * grad[i];
+        /* the kernel's `+= -lr * grad` compiles to one fused multiply-add */
+        table[(int64_t)key * dim + d] = fmaf(-lr, grad[i], table[(int64_t)key * dim + d]);
     }
 }
 

@@ -62,7 +62,7 @@ _STEP_SIGS = {
     "refstep_embedding_count": (I, []),
     "refstep_embedding_write": (I, [I, P, L]),
     "refstep_embedding_read": (I, [I, P, L]),
-    "refstep_set_embed_update": (I, [I]),
+    "refstep_set_embed_update": (I, [I, F]),
     "refstep_input_write": (I, [ctypes.c_char_p, P, L]),
     "refstep_step": (I, [F, I, F, P]),
     "refstep_time": (I, [I, I, F, I, F, P]),

@@ -75,6 +75,7 @@ struct RefModel {
     graph x_input;  // MLP input
     double* clip_ws = nullptr;
     bool embed_update = false;  // TextualEmbedding::EmbeddingUpdate on the encoder-side tokens
+    float embed_lr = LEARNING_RATE;
     float* softmax = nullptr;
     float* softmax_arr = nullptr;
     float* max_arr = nullptr;
@@ -248,12 +249,13 @@ void run_phase(RefModel& M, int phase, float lr, int adamw, float clip_norm) {
         M.go.backward();
         if (M.embed_update && !M.tokens.empty()) {
             // embedder.EmbeddingUpdate(enc, "E") (Engine/transformer.cu:869,
-            // 233-245): KeyUpdate at LEARNING_RATE with the encoder-side keys
+            // 233-245): KeyUpdate with the encoder-side keys, at LEARNING_RATE
+            // unless the caller set another rate
             TokenInput& t = M.tokens[0];
             const unsigned long long total = (unsigned long long)t.node->total;
             const int tpb = THREADSPERBLOCK;
             KeyUpdate<<<(int)((total + tpb - 1) / tpb), tpb>>>(t.table, t.node->grad, t.keys, M.seq, M.seq,
-                                                               M.d_model, LEARNING_RATE, total);
+                                                               M.d_model, M.embed_lr, total);
         }
     } else {
         if (clip_norm > 0) clip(M, clip_norm);
@@ -344,10 +346,12 @@ int refstep_param_read(int i, int which, float* host) {
 int refstep_embedding_count(void) { return g_model ? (int)g_model->tokens.size() : 0; }
 
 /* on != 0: every step runs the reference's embedding update on the
- * encoder-side table after the backward pass. */
-int refstep_set_embed_update(int on) {
+ * encoder-side table after the backward pass, at rate lr (<= 0: the
+ * reference's LEARNING_RATE). */
+int refstep_set_embed_update(int on, float lr) {
     if (!g_model) return (int)cudaErrorInvalidValue;
     g_model->embed_update = on != 0;
+    g_model->embed_lr = lr > 0 ? lr : LEARNING_RATE;
     return 0;
 }
 

@@ -4,9 +4,9 @@ gather, against the reference's compiled kernel and the C oracle.
 
 The reference's KeyUpdate adds -lr * grad into the table without atomics, so
 two tokens with the same key race; its result is defined only for distinct
-keys, where ours must equal it bit for bit.  With repeated keys ours adds
-every contribution (atomically) and is compared with the oracle's
-sequential sum at the fp32 elementwise bound."""
+keys, where ours must equal it bit for bit (one fused multiply-add per
+element).  With repeated keys ours sums the rows' gradients first and is
+compared with the exact scatter-add at the fp32 elementwise bound."""
 import numpy as np
 import pytest
 
@@ -70,12 +70,15 @@ def test_embedding_update_sums_repeated_keys(cuda, ops, orc, rng):
     o_tab = T(table, cuda)
     ops.embedding_update(T(keys, cuda), T(grad, cuda), o_tab, rows, lr)
     torch.cuda.synchronize()
-    c_tab = orc.key_update(table.copy(), grad, keys, rows, rows, lr)
-    # the update itself (table - table0) to the fp32 reduction bound
-    assert rel_err(H(o_tab) - table, c_tab - table) <= RTOL_EXACT
     exact = table.astype(np.float64).copy()
     np.add.at(exact, keys[keys >= 0], -lr * grad[keys >= 0].astype(np.float64))
-    assert rel_err(c_tab - table, exact - table) <= RTOL_EXACT
+    # the update itself (table - table0) to the fp32 reduction bound: the
+    # rows of a key are summed, then applied with one fused multiply-add
+    assert rel_err(H(o_tab).astype(np.float64) - table, exact - table) <= RTOL_EXACT
+    # the oracle restates the reference's per-row chain (what it computes
+    # when its threads do not race): one rounding per row
+    c_tab = orc.key_update(table.copy(), grad, keys, rows, rows, lr)
+    assert rel_err(c_tab.astype(np.float64) - table, exact - table) <= 1e-4
 
 
 def test_embedding_gather_masked_rows_are_zero(cuda, ops, orc, rng):
