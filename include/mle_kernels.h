@@ -518,6 +518,16 @@ enum mle_attn_path { MLE_ATTN_PATH_AUTO = 0, MLE_ATTN_PATH_FUSED = 1, MLE_ATTN_P
 int mle_set_attention_path(int path);
 int mle_get_attention_path(void);
 
+/* On the tensor-core path (softmax axis 1): 1 (default) computes P =
+ * softmax(scale Q K^T) over each key column, and the score gradient
+ * P (dP - column sums of P dP) with dP = dO V^T, each in one kernel that
+ * holds one key per TMEM lane and all its queries in the lane's columns
+ * (Sq <= 256, head_dim 32, 64 or 128), so the scores and dP never reach
+ * HBM; 0 writes the product to HBM and runs the column softmax (or its
+ * backward) over it.  Process-wide per host thread. */
+int mle_set_attention_keys_kernel(int enable);
+int mle_get_attention_keys_kernel(void);
+
 /* Positional table of MatPEncoding alone, table[r, c] = (float)sin/cos of
  * the angle for position r + start_idx (Engine/kernels.cu:166-185), and its
  * broadcast add y[b, i] = x[b, i] + table[i]: together bitwise equal to

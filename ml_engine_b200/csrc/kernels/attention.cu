@@ -542,6 +542,10 @@ int dispatch_hd(int hd, F&& f) {
 
 // ------------------------------ tensor-core path -----------------------------
 thread_local int g_attn_path = MLE_ATTN_PATH_AUTO;
+// 1: the tensor-core path computes P (forward) and the score gradient
+// (backward) with the keys-on-lanes kernels of gemm_tcgen05.cu; 0: product
+// to HBM, then the column softmax (or its backward) in place
+thread_local int g_attn_keys = 1;
 
 // Column softmax of each [rows, cols] matrix in place (the reference's type
 // 1, causal entries key > query zeroed after the max over the whole column,
@@ -879,11 +883,19 @@ int tc_attention_fwd(const float* Q, const float* K, const float* V, float* P, f
     strides_for(layout, H, Sq, hd, qb, qh, qs);
     strides_for(layout, H, Sk, hd, kb, kh, ks);
     const int64_t pb = (int64_t)H * Sq * Sk, ph = (int64_t)Sq * Sk;
-    // P = scale Q K^T, softmax over each column, O = P V
-    int s = run_gemm(attn_gemm(Q, K, P, Sq, Sk, hd, qs, ks, Sk, 0, 1, B, H, qb, qh, kb, kh, pb, ph, scale, 0), st);
+    int s = MLE_ERR_UNSUPPORTED;
+    // P = softmax over each column of scale Q K^T: in one kernel with the
+    // keys on the TMEM lanes (the scores stay on chip), or as a product
+    // written to P and softmaxed in place
+    if (g_attn_keys && attn_keys_supported(Sq, Sk, hd, (int64_t)B * H))
+        s = run_attn_keys(0, K, Q, nullptr, P, B, H, Sq, Sk, hd, kb, kh, ks, qb, qh, qs, scale, causal, st);
+    if (s == MLE_ERR_UNSUPPORTED) {
+        s = run_gemm(attn_gemm(Q, K, P, Sq, Sk, hd, qs, ks, Sk, 0, 1, B, H, qb, qh, kb, kh, pb, ph, scale, 0), st);
+        if (s) return s;
+        s = tc_col_softmax(P, (int64_t)B * H, Sq, Sk, causal, st);
+    }
     if (s) return s;
-    s = tc_col_softmax(P, (int64_t)B * H, Sq, Sk, causal, st);
-    if (s) return s;
+    // O = P V
     return run_gemm(attn_gemm(P, V, O, Sq, hd, Sk, Sk, ks, qs, 0, 0, B, H, pb, ph, kb, kh, qb, qh, 1.0f, 0), st);
 }
 
@@ -896,12 +908,18 @@ int tc_attention_bwd(const float* Q, const float* K, const float* V, const float
     strides_for(layout, H, Sq, hd, qb, qh, qs);
     strides_for(layout, H, Sk, hd, kb, kh, ks);
     const int64_t pb = (int64_t)H * Sq * Sk, ph = (int64_t)Sq * Sk, ns = (int64_t)B * pb;
-    // W = dO V^T (the softmax node's gradient)
-    int s = run_gemm(attn_gemm(dO, V, W, Sq, Sk, hd, qs, ks, Sk, 0, 1, B, H, qb, qh, kb, kh, pb, ph, 1.0f, 0), st);
-    if (s) return s;
-    if (dP_out && (s = mle_accumulate(W, dP_out, ns, 1.0, st)) != 0) return s;
-    // W = P (W - column sums of P W), the score gradient
-    s = tc_col_softmax_bwd(P, W, (int64_t)B * H, Sq, Sk, st);
+    int s = MLE_ERR_UNSUPPORTED;
+    // W = P (dP - column sums of P dP), the score gradient, dP = dO V^T the
+    // softmax node's gradient: in one kernel with the keys on the TMEM lanes
+    // (dP stays on chip), or dP written to W and transformed in place
+    if (g_attn_keys && !dP_out && attn_keys_supported(Sq, Sk, hd, (int64_t)B * H))
+        s = run_attn_keys(1, V, dO, P, W, B, H, Sq, Sk, hd, kb, kh, ks, qb, qh, qs, 1.0f, 0, st);
+    if (s == MLE_ERR_UNSUPPORTED) {
+        s = run_gemm(attn_gemm(dO, V, W, Sq, Sk, hd, qs, ks, Sk, 0, 1, B, H, qb, qh, kb, kh, pb, ph, 1.0f, 0), st);
+        if (s) return s;
+        if (dP_out && (s = mle_accumulate(W, dP_out, ns, 1.0, st)) != 0) return s;
+        s = tc_col_softmax_bwd(P, W, (int64_t)B * H, Sq, Sk, st);
+    }
     if (s) return s;
     if (dS_out && (s = mle_accumulate(W, dS_out, ns, 1.0, st)) != 0) return s;
     // dV += P^T dO
@@ -938,6 +956,14 @@ int mle_set_attention_path(int path) {
 }
 
 int mle_get_attention_path(void) { return g_attn_path; }
+
+int mle_set_attention_keys_kernel(int enable) {
+    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    g_attn_keys = enable;
+    return MLE_OK;
+}
+
+int mle_get_attention_keys_kernel(void) { return g_attn_keys; }
 
 int mle_attention_fused_supported(int seq_q, int seq_k, int head_dim, int softmax_axis, int key_grad_mode) {
     if (!fused_ok(softmax_axis, seq_q, seq_k, head_dim, 1, 1)) return 0;

@@ -47,6 +47,19 @@ struct ConvGemm {
     const float* bias;  // kind 1 only: added per output channel m (assigned output)
 };
 
+// Attention scores with the column softmax on the tensor cores (keys on
+// the TMEM lanes, one CTA per batch, head and 128 keys; gemm_tcgen05.cu).
+// Operands are (hd, S, H, B) views with element strides (s, h, b) per
+// row, head and batch.  mode 0: out = column softmax of scale * Q K^T
+// (keys_src = K, rows_src = Q); mode 1: out = P (dP - column sums of P dP)
+// with dP = dO V^T (keys_src = V, rows_src = dO).  P and out are
+// [B, H, Sq, Sk].  MLE_ERR_UNSUPPORTED (nothing launched) outside Sq <= 256,
+// hd in {32, 64, 128}.
+bool attn_keys_supported(int Sq, int Sk, int hd, int64_t BH);
+int run_attn_keys(int mode, const float* keys_src, const float* rows_src, const float* P, float* out, int B, int H,
+                  int Sq, int Sk, int hd, int64_t key_b, int64_t key_h, int64_t key_s, int64_t row_b, int64_t row_h,
+                  int64_t row_s, float scale, int causal, cudaStream_t st);
+
 int simt_gemm(const GemmProblem& p, cudaStream_t st);
 // false when the shapes or pointers rule out the tensor-core implicit path
 bool conv_gemm_supported(const ConvGemm& c);

@@ -24,6 +24,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cfloat>
 #include <stdio.h>
 #include <string.h>
 
@@ -857,6 +858,235 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Attention scores with the column softmax, keys on the TMEM lanes.
+//
+// The reference normalises each key column of the scores over the queries
+// (SOFTMAX / SOFTMASK type 1, Engine/kernels.cu:2134-2235) and backs it up
+// with the per-column dot product (deriv_softmax, :2149-2181).  Computing
+// the transposed product S^T = K Q^T puts one key on each TMEM lane and all
+// its queries along the lane's columns, so each epilogue thread owns a
+// whole column: the max, the sum and the dot product are thread-local loops,
+// and the scores never reach HBM.  One CTA per (batch, head, block of 128
+// keys):
+//   MODE 0  S^T = scale * K_blk Q^T -> P[b,h,:,keys] = column softmax
+//           (causal: key > query contributes 0; the max runs over every
+//           query, as the reference's SoftMask takes it)
+//   MODE 1  dP^T = V_blk dO^T, then with P read back per column,
+//           dS = P (dP - sum_q P dP) -> out[b,h,:,keys]
+// Operands (HD columns of every row) arrive by TMA as K-major tiles (128-byte
+// swizzle, 32 floats per k-block); the product is tcgen05.mma kind::tf32,
+// M = 128 keys, N = SQ queries, into SQ TMEM columns.  Stores and the P
+// reads of MODE 1 run along the keys: a warp touches 32 consecutive floats
+// of one query row.
+struct AttnKeysParams {
+    CUtensorMap a_map;  // keys:    (HD, S_k, H, B) view of K (MODE 0) or V (MODE 1)
+    CUtensorMap b_map;  // queries: (HD, S_q, H, B) view of Q (MODE 0) or dO (MODE 1)
+    const float* P;     // MODE 1: probabilities [B, H, Sq, Sk]
+    float* out;         // P (MODE 0) or dS (MODE 1), [B, H, Sq, Sk]
+    int H, Sq, Sk, key_blocks;
+    float scale;
+    int causal;
+};
+
+template <int HD, int SQ>
+struct AttnKeysSmem {
+    static constexpr int KB = HD / 32;
+    static constexpr int A_BYTES = 128 * 128;  // one k-block of 128 key rows
+    static constexpr int B_BYTES = SQ * 128;   // one k-block of SQ query rows
+    static constexpr int B_OFFSET = KB * A_BYTES;
+    static constexpr int BAR_OFFSET = B_OFFSET + KB * B_BYTES;
+    static constexpr int TOTAL = BAR_OFFSET + 64 + 4 * 128 * 4 + 1024;  // barriers, TMEM slot, abort flag,
+                                                                        // per-key partials; alignment
+};
+
+// query groups per key: the warps that share a TMEM lane quarter split the
+// queries (4 for the softmax, whose registers allow 512 threads at two CTAs
+// per SM; 2 for the score gradient, which keeps two P chunks in registers)
+template <int MODE>
+constexpr int attn_keys_groups() {
+    return MODE == 0 ? 4 : 2;
+}
+
+template <int MODE, int HD, int SQ>
+__global__ void __launch_bounds__(128 * attn_keys_groups<MODE>(), 2)
+    attn_keys_kernel(const __grid_constant__ AttnKeysParams p) {
+    constexpr int QG = attn_keys_groups<MODE>();
+    using L = AttnKeysSmem<HD, SQ>;
+    constexpr int KB = L::KB;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
+    uint64_t* done = full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kblk = blockIdx.x % p.key_blocks;
+    const int bh = blockIdx.x / p.key_blocks;
+    const int h = bh % p.H, b = bh / p.H;
+    const int key0 = kblk * 128;
+
+    if (threadIdx.x == 0) {
+        mbar_init(full, 1);
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.a_map)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.b_map)) : "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)SQ)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // the previous kernel's outputs are read only from here on; the next
+    // kernel may be scheduled once every CTA of this grid holds its TMEM
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
+
+    bool mma_issued = false;
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(full, (uint32_t)(KB * (L::A_BYTES + L::B_BYTES)));
+#pragma unroll
+        for (int kk = 0; kk < KB; ++kk) {
+            tma_load_4d(&p.a_map, full, smem + kk * L::A_BYTES, 32 * kk, key0, h, b);
+            tma_load_4d(&p.b_map, full, smem + L::B_OFFSET + kk * L::B_BYTES, 32 * kk, 0, h, b);
+        }
+        if (wait_bounded(full, 0, abort_flag)) {
+            tc_fence_after();
+            // D = f32, A = B = tf32, both K-major, N = SQ, M = 128
+            const uint32_t idesc =
+                (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(SQ >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+#pragma unroll
+            for (int kk = 0; kk < KB; ++kk) {
+                const uint32_t sa = smem_u32(smem + kk * L::A_BYTES);
+                const uint32_t sb = smem_u32(smem + L::B_OFFSET + kk * L::B_BYTES);
+#pragma unroll
+                for (int k8 = 0; k8 < 4; ++k8)
+                    mma_tf32(tmem, kmajor_desc(sa, k8), kmajor_desc(sb, k8), idesc, (kk | k8) ? 1u : 0u);
+            }
+            mma_commit(done);
+            mma_issued = true;
+        } else {
+            drain_wait(full, 0);  // the copies land before the CTA leaves
+        }
+    }
+    // every thread takes the same branch: the epilogue exchanges per-key
+    // partials through shared memory between the two warps of a lane quarter
+    const bool issued = __syncthreads_or(mma_issued ? 1 : 0) != 0;
+    const bool ready = __syncthreads_and((issued && wait_bounded(done, 0, abort_flag)) ? 1 : 0) != 0;
+    if (ready) {
+        tc_fence_after();
+        // warp w reads TMEM lanes 32 (w % 4).. (its keys) and the columns of
+        // query group w / 4
+        constexpr int HALF = SQ / QG;  // queries per group
+        float* red = reinterpret_cast<float*>(smem + L::BAR_OFFSET + 64);  // [QG][128] partials
+        const int kl = (warp & 3) * 32 + lane, half = warp >> 2;
+        const int key = key0 + kl;
+        const bool live = key < p.Sk;
+        const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(half * HALF);
+        const int64_t base = (int64_t)bh * p.Sq * p.Sk + key;
+        const int q0 = half * HALF;
+        uint32_t r[32];
+        if (MODE == 0) {
+            float m = -FLT_MAX;
+            for (int c = 0; c < HALF / 32; ++c) {
+                tmem_ld32(taddr + (uint32_t)(c * 32), r);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (q0 + c * 32 + j < p.Sq) m = fmaxf(m, p.scale * __uint_as_float(r[j]));
+            }
+            red[half * 128 + kl] = m;
+            __syncthreads();
+            m = red[kl];
+#pragma unroll
+            for (int g = 1; g < QG; ++g) m = fmaxf(m, red[g * 128 + kl]);
+            __syncthreads();
+            float sum = 0.f;
+            for (int c = 0; c < HALF / 32; ++c) {
+                tmem_ld32(taddr + (uint32_t)(c * 32), r);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int q = q0 + c * 32 + j;
+                    if (q < p.Sq && !(p.causal && key > q)) sum += expf(p.scale * __uint_as_float(r[j]) - m);
+                }
+            }
+            red[half * 128 + kl] = sum;
+            __syncthreads();
+            sum = red[kl];
+#pragma unroll
+            for (int g = 1; g < QG; ++g) sum += red[g * 128 + kl];
+            const float inv = 1.0f / (sum < 1e-45f ? 1.0f : sum);
+            for (int c = 0; c < HALF / 32; ++c) {
+                tmem_ld32(taddr + (uint32_t)(c * 32), r);
+                if (live) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int q = q0 + c * 32 + j;
+                        const float e = (p.causal && key > q) ? 0.f : expf(p.scale * __uint_as_float(r[j]) - m);
+                        if (q < p.Sq) p.out[base + (int64_t)q * p.Sk] = e * inv;
+                    }
+                }
+            }
+        } else {
+            // P of this thread's key column, one chunk of 32 queries ahead:
+            // the loads of chunk c + 1 are in flight while chunk c's dP
+            // comes out of TMEM and is consumed
+            float pc[32], pn[32];
+            auto load_p = [&](float(&dst)[32], int c) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int q = q0 + c * 32 + j;
+                    dst[j] = (live && q < p.Sq) ? __ldg(p.P + base + (int64_t)q * p.Sk) : 0.f;
+                }
+            };
+            float d = 0.f;
+            load_p(pn, 0);
+            for (int c = 0; c < HALF / 32; ++c) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) pc[j] = pn[j];
+                if (c + 1 < HALF / 32) load_p(pn, c + 1);
+                tmem_ld32(taddr + (uint32_t)(c * 32), r);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) d += pc[j] * __uint_as_float(r[j]);
+            }
+            red[half * 128 + kl] = d;
+            __syncthreads();
+            d = red[kl];
+#pragma unroll
+            for (int g = 1; g < QG; ++g) d += red[g * 128 + kl];
+            load_p(pn, 0);
+            for (int c = 0; c < HALF / 32; ++c) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) pc[j] = pn[j];
+                if (c + 1 < HALF / 32) load_p(pn, c + 1);
+                tmem_ld32(taddr + (uint32_t)(c * 32), r);
+                if (live) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int q = q0 + c * 32 + j;
+                        if (q < p.Sq) p.out[base + (int64_t)q * p.Sk] = pc[j] * (__uint_as_float(r[j]) - d);
+                    }
+                }
+            }
+        }
+    } else if (threadIdx.x == 0 && mma_issued) {
+        drain_wait(done, 0);  // the MMAs retire before TMEM is released
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)SQ)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side: tensor maps through the driver entry point (no libcuda link)
 // ---------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1355,6 +1585,80 @@ bool split_ok(const GemmProblem& p) {
 }
 
 }  // namespace
+
+namespace {
+
+template <int MODE, int HD, int SQ>
+int launch_attn_keys(const tc::AttnKeysParams& prm, int64_t ctas, cudaStream_t st) {
+    using L = tc::AttnKeysSmem<HD, SQ>;
+    static_assert(2 * L::TOTAL <= 228 * 1024 || HD > 64, "two CTAs per SM");
+    auto kern = tc::attn_keys_kernel<MODE, HD, SQ>;
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) != cudaSuccess)
+            return launch_status();
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctas);
+    cfg.blockDim = dim3(128 * tc::attn_keys_groups<MODE>());
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, prm) != cudaSuccess) return launch_status();
+    return launch_status();
+}
+
+}  // namespace
+
+bool attn_keys_supported(int Sq, int Sk, int hd, int64_t BH) {
+    return Sq > 0 && Sq <= 256 && Sk > 0 && (hd == 32 || hd == 64 || hd == 128) &&
+           BH * ((Sk + 127) / 128) <= 0x7fffffff && tc::get_encode() != nullptr;
+}
+
+int run_attn_keys(int mode, const float* keys_src, const float* rows_src, const float* P, float* out, int B, int H,
+                  int Sq, int Sk, int hd, int64_t key_b, int64_t key_h, int64_t key_s, int64_t row_b, int64_t row_h,
+                  int64_t row_s, float scale, int causal, cudaStream_t st) {
+    if (!attn_keys_supported(Sq, Sk, hd, (int64_t)B * H)) return MLE_ERR_UNSUPPORTED;
+    tc::AttnKeysParams prm;
+    memset(&prm, 0, sizeof(prm));
+    const int SQ = Sq <= 128 ? 128 : 256;
+    const int64_t kd[4] = {hd, Sk, H, B}, ks[3] = {key_s, key_h, key_b};
+    const int64_t rd[4] = {hd, Sq, H, B}, rs[3] = {row_s, row_h, row_b};
+    const int kbox[4] = {32, 128, 1, 1}, rbox[4] = {32, SQ, 1, 1};
+    if (!tc::encode_map(&prm.a_map, keys_src, kd, ks, kbox, CU_TENSOR_MAP_SWIZZLE_128B, 4, operand_type()) ||
+        !tc::encode_map(&prm.b_map, rows_src, rd, rs, rbox, CU_TENSOR_MAP_SWIZZLE_128B, 4, operand_type()))
+        return MLE_ERR_UNSUPPORTED;
+    prm.P = P;
+    prm.out = out;
+    prm.H = H;
+    prm.Sq = Sq;
+    prm.Sk = Sk;
+    prm.key_blocks = (Sk + 127) / 128;
+    prm.scale = scale;
+    prm.causal = causal;
+    const int64_t ctas = (int64_t)B * H * prm.key_blocks;
+    auto go = [&](auto m, auto d, auto q) {
+        return launch_attn_keys<decltype(m)::value, decltype(d)::value, decltype(q)::value>(prm, ctas, st);
+    };
+    using std::integral_constant;
+#define MLE_AK(MO, HDV)                                                                                     \
+    if (mode == MO && hd == HDV)                                                                            \
+        return SQ == 128 ? go(integral_constant<int, MO>(), integral_constant<int, HDV>(), integral_constant<int, 128>()) \
+                         : go(integral_constant<int, MO>(), integral_constant<int, HDV>(), integral_constant<int, 256>());
+    MLE_AK(0, 32)
+    MLE_AK(0, 64)
+    MLE_AK(0, 128)
+    MLE_AK(1, 32)
+    MLE_AK(1, 64)
+    MLE_AK(1, 128)
+#undef MLE_AK
+    return MLE_ERR_UNSUPPORTED;
+}
 
 int run_gemm(const GemmProblem& p, cudaStream_t st) {
     if (p.M <= 0 || p.N <= 0 || p.nbatch <= 0 || p.channels <= 0) return MLE_OK;

@@ -839,3 +839,66 @@ def _linear_group_case(cuda, ops, rng, n, rows):
         assert norm_err(H(dWs[i]), H(dw)) <= RTOL_TC
         assert norm_err(H(dBs[i]), H(db)) <= 1e-6
     assert norm_err(H(dX) - dX0, H(rX) - dX0) <= RTOL_TC
+
+
+KEYS_CASES = [  # B, H, Sq, Sk, hd, causal: shapes the keys-on-lanes kernels take
+    (2, 8, 128, 128, 32, 0),   # configs[1] heads
+    (1, 4, 256, 256, 64, 1),   # configs[2] masked self-attention heads
+    (1, 4, 256, 256, 64, 0),   # configs[2] cross-attention heads (unmasked here)
+    (2, 3, 200, 136, 64, 1),   # ragged: queries below the 256-wide tile, a partial second key block
+    (1, 2, 96, 256, 128, 0),   # head_dim 128, queries below the 128-wide tile
+]
+
+
+@pytest.mark.parametrize("key_mode", [0, 1])
+@pytest.mark.parametrize("case", KEYS_CASES)
+def test_attention_keys_kernels(cuda, ops, orc, rng, case, key_mode):
+    """The tensor-core path with the keys-on-lanes kernels (P and the score
+    gradient computed with the scores / dP kept in TMEM, no dP or dS
+    output requested) against the C oracle's reference chain (TF32 bound)
+    and against the same path with the products written to HBM and
+    softmaxed in place (summation order only)."""
+    from ml_engine_b200._lib import kernels
+    B, Hh, Sq, Sk, D, causal = case
+    if key_mode == 0 and Sq != Sk:
+        pytest.skip("the reference key gradient is defined for Sq == Sk")
+    bh = B * Hh
+    Q, K, V, dO = _attn_inputs(rng, B, Hh, Sq, Sk, D)
+    scale = float(1.0 / np.sqrt(D))
+    tm = lambda x: T(_to_token_major(x, B, Hh), cuda)   # noqa: E731
+    back = lambda x: _from_token_major(H(x), B, Hh, D)   # noqa: E731
+    k = kernels()
+    old_path = ops.set_attention_path(ops.ATTN_PATH_TENSOR)
+    runs = {}
+    try:
+        for keys in (1, 0):
+            k.call("mle_set_attention_keys_kernel", keys)
+            P = torch.zeros(bh, Sq, Sk, device=cuda)
+            O = torch.zeros(B, Sq, Hh * D, device=cuda)
+            ops.attention_fwd(tm(Q), tm(K), tm(V), P, O, B, Hh, Sq, Sk, D, scale, causal, 1, 1)
+            dQ, dK, dV = (torch.zeros(B, s, Hh * D, device=cuda) for s in (Sq, Sk, Sk))
+            ops.attention_bwd(tm(Q), tm(K), tm(V), P, tm(dO), dQ, dK, dV, None, None, B, Hh, Sq, Sk, D, scale,
+                              causal, 1, key_mode, 1)
+            torch.cuda.synchronize()
+            runs[keys] = (H(P), back(O), back(dQ), back(dK), back(dV))
+    finally:
+        k.call("mle_set_attention_keys_kernel", 1)
+        ops.set_attention_path(old_path)
+    S = orc.bcmm(1, Q, K, np.zeros((bh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 0, 3, 3, 3)
+    rP = orc.softmax_fwd(orc.scale_write(S, scale), bh, Sq, Sk, 1, causal)
+    rO = orc.bcmm(0, rP, V, np.zeros((bh, Sq, D), np.float32), B, Hh, Sq, Sk, D, 0, 3, 3, 3)
+    rdP = orc.bcmm(1, dO, V, np.zeros((bh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 1, 3, 3, 3)
+    rdV = orc.bcmm(2, rP, dO, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
+    rdS = orc.accumulate(orc.softmax_bwd(rP, rdP, np.zeros_like(rP), bh, Sq, Sk, 1), np.zeros_like(rP), scale)
+    rdQ = orc.bcmm(0, rdS, K, np.zeros((bh, Sq, D), np.float32), B, Hh, Sq, Sk, D, 1, 3, 3, 3)
+    if key_mode == 0:
+        rdK = orc.bcmm(3, Q, rdS, np.zeros((bh, Sk, D), np.float32), B, Hh, D, Sq, Sk, 1, 3, 3, 3)
+    else:
+        rdK = orc.bcmm(2, rdS, Q, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
+    for name, got, want in zip("P O dQ dK dV".split(), runs[1], (rP, rO, rdQ, rdK, rdV)):
+        assert rel_err(got, want) <= RTOL_TC, (name, rel_err(got, want))
+    # the two paths differ in summation order only (the column sums, the
+    # dP product's tiling); the score gradient's cancellation p (dP - d)
+    # magnifies that in dQ and dK
+    for name, a, b in zip("P O dQ dK dV".split(), runs[1], runs[0]):
+        assert rel_err(a, b) <= 1e-3, (name, rel_err(a, b))
