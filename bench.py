@@ -88,7 +88,12 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+BATCH_OVERRIDE = None   # --batch: per-rank batch for profiling runs (not a bench line)
+
+
 def local_batch(wl, world):
+    if BATCH_OVERRIDE:
+        return BATCH_OVERRIDE
     w = WORKLOADS[wl]
     if "global_batch" in w:
         if w["global_batch"] % world:
@@ -847,7 +852,13 @@ def main():
     ap.add_argument("--roofline-batch", type=int, default=None,
                     help="sequences for --roofline-only (default: the workload's per-rank batch at one GPU)")
     ap.add_argument("--roofline-reps", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="profiling aid: this many sequences per rank instead of the workload's (the JSON line is "
+                         "then not the benchmark's)")
     args = ap.parse_args()
+    if args.batch:
+        global BATCH_OVERRIDE
+        BATCH_OVERRIDE = args.batch
     if args.gemm_pairs is not None:
         from ml_engine_b200._lib import kernels
         kernels().call("mle_set_gemm_pairs", args.gemm_pairs)

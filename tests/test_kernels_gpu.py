@@ -902,3 +902,34 @@ def test_attention_keys_kernels(cuda, ops, orc, rng, case, key_mode):
     # magnifies that in dQ and dK
     for name, a, b in zip("P O dQ dK dV".split(), runs[1], runs[0]):
         assert rel_err(a, b) <= 1e-3, (name, rel_err(a, b))
+
+
+@pytest.mark.parametrize("gemm_mode", [0, 1], ids=["tf32", "fp32"])
+def test_linear_bwd_long_reduction(cuda, ops, gemm_mode):
+    """configs[2]'s weight gradient on one GPU reduces over K = 65536 tokens
+    (dW = X^T dY, 512 x 512): against a float64 product of the same fp32
+    inputs (torch on the GPU; the C oracle would take minutes at this
+    size), per-tensor normwise within the TF32 bound and max-relative within
+    it too; fp32 mode (FMA chains of 65536 terms) within 1e-4."""
+    from ml_engine_b200._lib import kernels
+    rows, fin, fout = 65536, 512, 512
+    g = torch.Generator(device=cuda).manual_seed(3)
+    X = torch.randn(rows, fin, device=cuda, generator=g)
+    W = torch.randn(fin, fout, device=cuda, generator=g) * 0.02
+    dY = torch.randn(rows, fout, device=cuda, generator=g) * 1e-3
+    dX, dW = torch.zeros(rows, fin, device=cuda), torch.zeros(fin, fout, device=cuda)
+    k = kernels()
+    old = k.mle_get_gemm_mode()
+    try:
+        k.call("mle_set_gemm_mode", gemm_mode)
+        ops.linear_bwd(X, W, dY, dX, dW, None, rows, fin, fout)
+        torch.cuda.synchronize()
+    finally:
+        k.call("mle_set_gemm_mode", old)
+    rdW = (X.double().t() @ dY.double()).cpu().numpy()
+    rdX = (dY.double() @ W.double().t()).cpu().numpy()
+    for got, want in ((H(dW), rdW), (H(dX), rdX)):
+        if gemm_mode == 0:
+            assert norm_err(got, want) <= RTOL_TC and rel_err(got, want) <= RTOL_TC
+        else:   # fp32 FMA chains 65536 long
+            assert rel_err(got, want) <= 1e-4
