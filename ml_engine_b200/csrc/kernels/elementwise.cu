@@ -283,24 +283,44 @@ __global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __re
 #pragma unroll
     for (int k = 0; k < W; ++k) s[k] = 0.f;
     if (c0 < cols) {
-        for (int64_t r = r_begin + warp; r < r_end; r += kColWarps) {
-            const int64_t idx = r * cols + c0;
-            if constexpr (VEC) {
-                float4 o = (ACT && ASSIGN) ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<float4*>(g + idx);
-                if (ACT) {
-                    const float4 a = *reinterpret_cast<const float4*>(x + idx);
-                    const float4 d = *reinterpret_cast<const float4*>(gy + idx);
-                    o.x = act_backward(kind, a.x, d.x, o.x);
-                    o.y = act_backward(kind, a.y, d.y, o.y);
-                    o.z = act_backward(kind, a.z, d.z, o.z);
-                    o.w = act_backward(kind, a.w, d.w, o.w);
-                    *reinterpret_cast<float4*>(g + idx) = o;
+        if constexpr (VEC) {
+            // U rows per pass, their loads issued together (bytes in flight)
+            constexpr int U = 4;
+            for (int64_t r = r_begin + warp; r < r_end; r += U * kColWarps) {
+                float4 o[U], a[U], d[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t rr = r + (int64_t)u * kColWarps;
+                    const int64_t idx = rr * cols + c0;
+                    const bool in = rr < r_end;
+                    o[u] = (!in || (ACT && ASSIGN)) ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                                    : *reinterpret_cast<const float4*>(g + idx);
+                    if (ACT) {
+                        a[u] = in ? *reinterpret_cast<const float4*>(x + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        d[u] = in ? *reinterpret_cast<const float4*>(gy + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
                 }
-                s[0] += o.x;
-                s[1] += o.y;
-                s[2] += o.z;
-                s[3] += o.w;
-            } else {
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t rr = r + (int64_t)u * kColWarps;
+                    if (rr >= r_end) break;
+                    if (ACT) {
+                        o[u].x = act_backward(kind, a[u].x, d[u].x, o[u].x);
+                        o[u].y = act_backward(kind, a[u].y, d[u].y, o[u].y);
+                        o[u].z = act_backward(kind, a[u].z, d[u].z, o[u].z);
+                        o[u].w = act_backward(kind, a[u].w, d[u].w, o[u].w);
+                        *reinterpret_cast<float4*>(g + rr * cols + c0) = o[u];
+                    }
+                    s[0] += o[u].x;
+                    s[1] += o[u].y;
+                    s[2] += o[u].z;
+                    s[3] += o[u].w;
+                }
+            }
+        } else {
+          for (int64_t r = r_begin + warp; r < r_end; r += kColWarps) {
+            const int64_t idx = r * cols + c0;
+            {
                 float o = (ACT && ASSIGN) ? 0.f : g[idx];
                 if (ACT) {
                     o = act_backward(kind, x[idx], gy[idx], o);
@@ -308,6 +328,7 @@ __global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __re
                 }
                 s[0] += o;
             }
+          }
         }
     }
 #pragma unroll

@@ -864,10 +864,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // (SOFTMAX / SOFTMASK type 1, Engine/kernels.cu:2134-2235) and backs it up
 // with the per-column dot product (deriv_softmax, :2149-2181).  Computing
 // the transposed product S^T = K Q^T puts one key on each TMEM lane and all
-// its queries along the lane's columns, so each epilogue thread owns a
-// whole column: the max, the sum and the dot product are thread-local loops,
-// and the scores never reach HBM.  One CTA per (batch, head, block of 128
-// keys):
+// its queries along the lane's columns, so a column belongs to the QG warps
+// that read one TMEM lane quarter (each takes SQ / QG of the queries): the
+// max, the sum and the dot product are thread-local loops plus one exchange
+// of partials through shared memory, and the scores never reach HBM.  One
+// CTA of 4 * QG warps per (batch, head, block of 128 keys), two per SM (one
+// CTA's operand loads and products overlap the other's epilogue):
 //   MODE 0  S^T = scale * K_blk Q^T -> P[b,h,:,keys] = column softmax
 //           (causal: key > query contributes 0; the max runs over every
 //           query, as the reference's SoftMask takes it)
