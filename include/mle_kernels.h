@@ -301,10 +301,10 @@ int mle_softmax_ce_bwd(const float* probs, const float* target, const float* ups
 
 /* The same two entry points with the target as one int32 class index per
  * row instead of the dense one-hot tensor the reference builds with
- * OneHotEmbeddings (no counterpart in the reference; SURVEY's index-label
- * variant).  Loss, probs and grad equal the dense entry points' on the
- * one-hot target of `labels`, bit for bit; a label outside [0, cols) is a
- * row of zeros.  The forward needs cols % 4 == 0, cols <= 8192 and 16-byte
+ * OneHotEmbeddings (no counterpart in the reference: an index-label
+ * variant that skips building the one-hot tensor).  Loss, probs and grad
+ * equal the dense entry points' on the one-hot target of `labels`, bit for
+ * bit; a label outside [0, cols) is a row of zeros.  The forward needs cols % 4 == 0, cols <= 8192 and 16-byte
  * aligned logits/probs/grad (else MLE_ERR_UNSUPPORTED). */
 int mle_softmax_ce_index_fwd(const float* logits, const int32_t* labels, float* probs, float* loss,
                              float* grad, float batch_div, int64_t rows, int cols,
