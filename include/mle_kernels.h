@@ -528,6 +528,36 @@ int mle_get_attention_path(void);
 int mle_set_attention_keys_kernel(int enable);
 int mle_get_attention_keys_kernel(void);
 
+/* Attention with the column softmax (softmax axis 1) whose score matrices
+ * never reach HBM (no counterpart in the reference, whose MultiHeadAttention
+ * writes scale*QK^T, P, dP and dS as [B, H, Sq, Sk] tensors,
+ * Engine/transformer.cu:647-675).  The forward writes O and two numbers per
+ * key, stats = [column max m (B*H*Sk floats), inverse column sum 1/l
+ * (B*H*Sk floats)]; P = exp(scale QK^T - m) / l (0 where causal masks key >
+ * query) equals the P of mle_attention_fwd to rounding.  The backward
+ * recomputes P from Q, K and stats and writes dQ, dK, dV (bits of
+ * assign_mask as in mle_attention_bwd_assign), using dvec (B*H*Sk floats)
+ * as workspace for the per-key dot products sum_q P dP.  key_grad_mode as
+ * for mle_attention_bwd (the reference's BMMABT key gradient or the true
+ * one).  Tensor cores (TF32 GEMM mode) only: *_supported returns 1 for
+ * softmax_axis 1, seq_q <= 256, seq_k <= 512, head_dim 32 or 64 (the
+ * reference key gradient also needs seq_q == seq_k, seq_k % head_dim == 0)
+ * while mle_set_attention_flash(1) (the default) holds; otherwise the entry
+ * points return MLE_ERR_UNSUPPORTED with nothing written.  Pointers 16-byte
+ * aligned. */
+int mle_attention_flash_supported(int seq_q, int seq_k, int head_dim, int softmax_axis, int key_grad_mode);
+int mle_attention_flash_fwd(const float* Q, const float* K, const float* V, float* O, float* stats, int batch,
+                            int heads, int seq_q, int seq_k, int head_dim, float scale, int causal, int layout,
+                            mle_stream_t stream);
+int mle_attention_flash_bwd(const float* Q, const float* K, const float* V, const float* dO, const float* stats,
+                            float* dvec, float* dQ, float* dK, float* dV, int batch, int heads, int seq_q,
+                            int seq_k, int head_dim, float scale, int causal, int key_grad_mode, int layout,
+                            int assign_mask, mle_stream_t stream);
+/* 1 (default): graph attention nodes take the entry points above where
+ * they are supported; 0: mle_attention_fwd/bwd.  Per host thread. */
+int mle_set_attention_flash(int enable);
+int mle_get_attention_flash(void);
+
 /* Positional table of MatPEncoding alone, table[r, c] = (float)sin/cos of
  * the angle for position r + start_idx (Engine/kernels.cu:166-185), and its
  * broadcast add y[b, i] = x[b, i] + table[i]: together bitwise equal to

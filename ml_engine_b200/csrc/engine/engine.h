@@ -283,8 +283,9 @@ class GraphOperations {
     // (Headify x3, BMMABT, Scale, SOFTMAX/SOFTMASK type `axis`, BMM,
     // DeHeadify; Engine/transformer.cu:647-675) as one node over the flat
     // [B,1,S,H*hd] projections, forward on the tensor cores and backward
-    // through mle_attention_bwd.  key_grad_mode selects the reference's
-    // BMMABT key gradient (default) or the mathematical one.
+    // through mle_attention_flash_bwd (the scores never in HBM) where it
+    // applies, else mle_attention_bwd.  key_grad_mode selects the
+    // reference's BMMABT key gradient (default) or the mathematical one.
     static graph ScaledDotAttention(const graph& Q, const graph& K, const graph& V, const int heads, const float scale,
                                     const bool mask, const int axis = 1,
                                     const int key_grad_mode = MLE_KEYGRAD_REFERENCE);

@@ -679,6 +679,29 @@ graph GraphOperations::ScaledDotAttention(const graph& Q, const graph& K, const 
     const int64_t nq = (int64_t)B * Sq * D, nk = (int64_t)B * Sk * D, ns = (int64_t)B * heads * Sq * Sk;
     NodeBackProp *nd = node.get(), *qp = Q.get(), *kp = K.get(), *vp = V.get();
     const int causal = (mask && Sq > 1) ? 1 : 0;
+    if (mle_attention_flash_supported(Sq, Sk, hd, axis, key_grad_mode)) {
+        // the scores stay on chip: two numbers per key (column max and
+        // inverse sum) carry the softmax from the forward to the backward
+        const int64_t nkeys = (int64_t)B * heads * Sk;
+        float* stats = arena_alloc(ARENA_ACT, 2 * nkeys, "Attention column statistics");
+        float* dvec = arena_alloc(ARENA_WS, nkeys, "Attention column dots");
+        GB += (double)(3 * nkeys) * sizeof(float) / (1ULL << 30);
+        node->forward = [=]() {
+            check(mle_attention_flash_fwd(qp->output, kp->output, vp->output, nd->output, stats, B, heads, Sq, Sk,
+                                          hd, scale, causal, MLE_ATTN_TOKEN_MAJOR, st()),
+                  "Attention forward");
+        };
+        ext(nd).kind = OP_ATTENTION;
+        node->backward = [=]() {
+            check(mle_attention_flash_bwd(qp->output, kp->output, vp->output, nd->grad, stats, dvec, qp->grad,
+                                          kp->grad, vp->grad, B, heads, Sq, Sk, hd, scale, causal, key_grad_mode,
+                                          MLE_ATTN_TOKEN_MAJOR, ext(nd).assign_inputs & 7, st()),
+                  "Attention backward");
+        };
+        node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
+        node->free = [nd]() { nd->clear(); };
+        return node;
+    }
     if (mle_attention_fused_supported(Sq, Sk, hd, axis, key_grad_mode)) {
         // fused kernels read and write the Linear layout directly; only P is kept
         float* P = arena_alloc(ARENA_ACT, ns, "Attention P");

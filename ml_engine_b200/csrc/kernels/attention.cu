@@ -546,6 +546,8 @@ thread_local int g_attn_path = MLE_ATTN_PATH_AUTO;
 // (backward) with the keys-on-lanes kernels of gemm_tcgen05.cu; 0: product
 // to HBM, then the column softmax (or its backward) in place
 thread_local int g_attn_keys = 1;
+// 1: graph attention nodes use the flash entry points where supported
+thread_local int g_attn_flash = 1;
 
 // Column softmax of each [rows, cols] matrix in place (the reference's type
 // 1, causal entries key > query zeroed after the max over the whole column,
@@ -964,6 +966,55 @@ int mle_set_attention_keys_kernel(int enable) {
 }
 
 int mle_get_attention_keys_kernel(void) { return g_attn_keys; }
+
+int mle_set_attention_flash(int enable) {
+    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    g_attn_flash = enable;
+    return MLE_OK;
+}
+
+int mle_get_attention_flash(void) { return g_attn_flash; }
+
+int mle_attention_flash_supported(int seq_q, int seq_k, int head_dim, int softmax_axis, int key_grad_mode) {
+    if (!g_attn_flash || softmax_axis != 1 || mle_get_gemm_mode() != MLE_GEMM_MODE_TF32) return 0;
+    if (key_grad_mode != MLE_KEYGRAD_REFERENCE && key_grad_mode != MLE_KEYGRAD_TRUE) return 0;
+    return attn_flash_supported(seq_q, seq_k, head_dim, 1, key_grad_mode) ? 1 : 0;
+}
+
+int mle_attention_flash_fwd(const float* Q, const float* K, const float* V, float* O, float* stats, int batch,
+                            int heads, int seq_q, int seq_k, int head_dim, float scale, int causal, int layout,
+                            mle_stream_t stream) {
+    if (!Q || !K || !V || !O || !stats || batch <= 0 || heads <= 0) return MLE_ERR_ARG;
+    if (layout != MLE_ATTN_HEAD_MAJOR && layout != MLE_ATTN_TOKEN_MAJOR) return MLE_ERR_ARG;
+    if (!mle_attention_flash_supported(seq_q, seq_k, head_dim, 1, MLE_KEYGRAD_TRUE) ||
+        !ptrs_aligned({Q, K, V, O, stats}))
+        return MLE_ERR_UNSUPPORTED;
+    int64_t qb, qh, qs, kb, kh, ks;
+    strides_for(layout, heads, seq_q, head_dim, qb, qh, qs);
+    strides_for(layout, heads, seq_k, head_dim, kb, kh, ks);
+    return run_attn_flash_fwd(Q, K, V, O, stats, batch, heads, seq_q, seq_k, head_dim, qb, qh, qs, kb, kh, ks, scale,
+                              causal ? 1 : 0, as_stream(stream));
+}
+
+int mle_attention_flash_bwd(const float* Q, const float* K, const float* V, const float* dO, const float* stats,
+                            float* dvec, float* dQ, float* dK, float* dV, int batch, int heads, int seq_q,
+                            int seq_k, int head_dim, float scale, int causal, int key_grad_mode, int layout,
+                            int assign_mask, mle_stream_t stream) {
+    if (!Q || !K || !V || !dO || !stats || !dvec || !dQ || !dK || !dV || batch <= 0 || heads <= 0)
+        return MLE_ERR_ARG;
+    if (layout != MLE_ATTN_HEAD_MAJOR && layout != MLE_ATTN_TOKEN_MAJOR) return MLE_ERR_ARG;
+    if (assign_mask < 0 || assign_mask > 7) return MLE_ERR_ARG;
+    if ((dQ == dK && (assign_mask & 3)) || (dQ == dV && (assign_mask & 5)) || (dK == dV && (assign_mask & 6)))
+        return MLE_ERR_ARG;
+    if (!mle_attention_flash_supported(seq_q, seq_k, head_dim, 1, key_grad_mode) ||
+        !ptrs_aligned({Q, K, V, dO, stats, dvec, dQ, dK, dV}))
+        return MLE_ERR_UNSUPPORTED;
+    int64_t qb, qh, qs, kb, kh, ks;
+    strides_for(layout, heads, seq_q, head_dim, qb, qh, qs);
+    strides_for(layout, heads, seq_k, head_dim, kb, kh, ks);
+    return run_attn_flash_bwd(Q, K, V, dO, stats, dvec, dQ, dK, dV, batch, heads, seq_q, seq_k, head_dim, qb, qh, qs,
+                              kb, kh, ks, scale, causal ? 1 : 0, key_grad_mode, assign_mask, as_stream(stream));
+}
 
 int mle_attention_fused_supported(int seq_q, int seq_k, int head_dim, int softmax_axis, int key_grad_mode) {
     if (!fused_ok(softmax_axis, seq_q, seq_k, head_dim, 1, 1)) return 0;

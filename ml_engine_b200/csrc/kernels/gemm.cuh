@@ -53,12 +53,30 @@ struct ConvGemm {
 // row, head and batch.  mode 0: out = column softmax of scale * Q K^T
 // (keys_src = K, rows_src = Q); mode 1: out = P (dP - column sums of P dP)
 // with dP = dO V^T (keys_src = V, rows_src = dO).  P and out are
-// [B, H, Sq, Sk].  MLE_ERR_UNSUPPORTED (nothing launched) outside Sq <= 256,
-// hd in {32, 64, 128}.
+// [B, H, Sq, Sk]; mode 0 may leave out null and write only `stats` (column
+// max [B*H*Sk], then inverse column sum [B*H*Sk]).  MLE_ERR_UNSUPPORTED
+// (nothing launched) outside Sq <= 256, hd in {32, 64, 128}.
 bool attn_keys_supported(int Sq, int Sk, int hd, int64_t BH);
 int run_attn_keys(int mode, const float* keys_src, const float* rows_src, const float* P, float* out, int B, int H,
                   int Sq, int Sk, int hd, int64_t key_b, int64_t key_h, int64_t key_s, int64_t row_b, int64_t row_h,
-                  int64_t row_s, float scale, int causal, cudaStream_t st);
+                  int64_t row_s, float scale, int causal, cudaStream_t st, float* stats = nullptr);
+
+// Attention with the column softmax without the score matrices in HBM
+// (gemm_tcgen05.cu): the forward writes O and per-key statistics (column
+// max, inverse column sum: stats[2 * B*H*Sk]); the backward recomputes the
+// probabilities from them and writes dQ, dK, dV (dvec: B*H*Sk floats of
+// workspace holding sum_q P dP per key).  Operand and output strides as for
+// run_attn_keys; `assign` bit 0 dQ, bit 1 dK, bit 2 dV written rather than
+// accumulated.  MLE_ERR_UNSUPPORTED outside Sq <= 256, Sk <= 512,
+// hd in {32, 64} (and Sq == Sk, Sk % hd == 0 for the reference key gradient).
+bool attn_flash_supported(int Sq, int Sk, int hd, int64_t BH, int key_mode);
+int run_attn_flash_fwd(const float* Q, const float* K, const float* V, float* O, float* stats, int B, int H, int Sq,
+                       int Sk, int hd, int64_t qb, int64_t qh, int64_t qs, int64_t kb, int64_t kh, int64_t ks,
+                       float scale, int causal, cudaStream_t st);
+int run_attn_flash_bwd(const float* Q, const float* K, const float* V, const float* dO, const float* stats,
+                       float* dvec, float* dQ, float* dK, float* dV, int B, int H, int Sq, int Sk, int hd, int64_t qb,
+                       int64_t qh, int64_t qs, int64_t kb, int64_t kh, int64_t ks, float scale, int causal,
+                       int key_mode, int assign, cudaStream_t st);
 
 int simt_gemm(const GemmProblem& p, cudaStream_t st);
 // false when the shapes or pointers rule out the tensor-core implicit path
@@ -66,5 +84,9 @@ bool conv_gemm_supported(const ConvGemm& c);
 int run_conv_gemm(const ConvGemm& c, cudaStream_t st);
 int run_gemm(const GemmProblem& p, cudaStream_t st);
 int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st);
+// C (= or +=) sum_g A_g B_g as one product over the concatenated reduction
+// (problems sharing C, M, N, layouts, mode and alpha; unbatched, K_g % 64
+// == 0); otherwise the group launch above with C shared.
+int run_gemm_kcat(const GemmProblem* ps, int n, cudaStream_t st);
 
 }  // namespace mle

@@ -25,6 +25,7 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <type_traits>
 #include <stdio.h>
 #include <string.h>
 
@@ -95,11 +96,39 @@ struct GemmGroup {
     EpiParams ep[kMaxGroup];
     int64_t tile_start[kMaxGroup + 1];
     int n;
+    // kcat > 1: one product over the concatenated reduction of kcat problems
+    // that share C, M and N (sum_g A_g B_g); the tiles and the epilogue are
+    // problem 0's (ep[0].K = the summed K), k-block kb of a tile reads
+    // a[g], b[g] at k-block kb - kcat_kb[g] of segment g
+    int kcat;
+    int kcat_kb[kMaxGroup + 1];
+    // ilv: the problems share their (split, batch, channel, m) tile rows and
+    // walk them together, row-tile by row-tile, each problem's n-tiles in
+    // turn (ilv_n: prefix of the problems' n_tiles), so tiles that read the
+    // same rows of a shared A run back to back and find them in L2
+    int ilv;
+    int ilv_n[kMaxGroup + 1];
 };
 
 __device__ __forceinline__ int group_of(const GemmGroup& G, int64_t t) {
     int g = 0;
     while (g + 1 < G.n && t >= G.tile_start[g + 1]) ++g;
+    return g;
+}
+
+// Problem g of tile t and the tile's index within that problem.
+__device__ __forceinline__ int locate(const GemmGroup& G, int64_t t, int64_t& tl) {
+    if (G.ilv) {
+        const int64_t nsum = G.ilv_n[G.n];
+        const int64_t outer = t / nsum;
+        const int inner = (int)(t - outer * nsum);
+        int g = 0;
+        while (g + 1 < G.n && inner >= G.ilv_n[g + 1]) ++g;
+        tl = outer * (G.ilv_n[g + 1] - G.ilv_n[g]) + (inner - G.ilv_n[g]);
+        return g;
+    }
+    const int g = group_of(G, t);
+    tl = t - G.tile_start[g];
     return g;
 }
 
@@ -153,6 +182,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Non-blocking test of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity)
@@ -466,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int g = 0; g < grp.n; ++g) {
+        for (int g = 0; g < (grp.kcat > grp.n ? grp.kcat : grp.n); ++g) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&grp.a[g])) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&grp.b[g])) : "memory");
             if (grp.ep[g].tma_epi)
@@ -513,13 +555,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             for (int64_t t = t_first; ok && t < total_tiles; t += t_step) {
-                const int g = group_of(grp, t);
+                int64_t tl;
+                const int g = locate(grp, t, tl);
                 // a register copy: a reference into the parameter space would be
                 // re-read after every shared-memory or global access
                 const EpiParams ep = grp.ep[g];
                 const CUtensorMap* tmA = &grp.a[g];
                 const CUtensorMap* tmB = &grp.b[g];
-                const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
+                const Tile x = tile_at(ep, tl, BN, BMT);
                 const int a_c = ep.a_has_c ? x.cidx : 0, a_b = ep.a_has_b ? x.bidx : 0;
                 const int b_c = ep.b_has_c ? x.cidx : 0, b_b = ep.b_has_b ? x.bidx : 0;
                 for (int i = 0; i < x.nkb; i += KPL) {
@@ -570,26 +613,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                         load(tmA, sa, k0, mo, a_c, a_b);
                         load(tmB, sb, k0 + (kh - ep.cv_pad) * ep.cv_w, no, kw * ep.cv_nb + x.bidx, 0);
                     } else {
+                        // the segment of a concatenated reduction this
+                        // stage reads (a stage never straddles two)
+                        const CUtensorMap* mA = tmA;
+                        const CUtensorMap* mB = tmB;
+                        int kc = k0, asp = ep.a_split, bsp = ep.b_split;
+                        if (grp.kcat > 1) {
+                            const int kb = x.kb_begin + i;
+                            int gk = 0;
+                            while (gk + 1 < grp.kcat && kb >= grp.kcat_kb[gk + 1]) ++gk;
+                            mA = &grp.a[gk];
+                            mB = &grp.b[gk];
+                            kc = (kb - grp.kcat_kb[gk]) * BK;
+                            asp = grp.ep[gk].a_split;
+                            bsp = grp.ep[gk].b_split;
+                        }
                         // split views: the stage's KPL k-blocks of all its
                         // rows (K-major) or 32-column chunks (MN-major) in
                         // one copy per operand
-                        if (ep.a_split) {
-                            if (A_MN) load5(tmA, sa, k0, mo >> 5, a_c, a_b);
-                            else load5(tmA, sa, mo, k0 >> 5, a_c, a_b);
+                        if (asp) {
+                            if (A_MN) load5(mA, sa, kc, mo >> 5, a_c, a_b);
+                            else load5(mA, sa, mo, kc >> 5, a_c, a_b);
                         } else if (A_MN) {
 #pragma unroll
-                            for (int j = 0; j < BM / 32; ++j) load(tmA, sa + j * 4096, mo + 32 * j, k0, a_c, a_b);
+                            for (int j = 0; j < BM / 32; ++j) load(mA, sa + j * 4096, mo + 32 * j, kc, a_c, a_b);
                         } else {
-                            load(tmA, sa, k0, mo, a_c, a_b);
+                            load(mA, sa, kc, mo, a_c, a_b);
                         }
-                        if (ep.b_split) {
-                            if (B_MN) load5(tmB, sb, k0, no >> 5, b_c, b_b);
-                            else load5(tmB, sb, no, k0 >> 5, b_c, b_b);
+                        if (bsp) {
+                            if (B_MN) load5(mB, sb, kc, no >> 5, b_c, b_b);
+                            else load5(mB, sb, no, kc >> 5, b_c, b_b);
                         } else if (B_MN) {
 #pragma unroll
-                            for (int j = 0; j < BNC / 32; ++j) load(tmB, sb + j * 4096, no + 32 * j, k0, b_c, b_b);
+                            for (int j = 0; j < BNC / 32; ++j) load(mB, sb + j * 4096, no + 32 * j, kc, b_c, b_b);
                         } else {
-                            load(tmB, sb, k0, no, b_c, b_b);
+                            load(mB, sb, kc, no, b_c, b_b);
                         }
                     }
                     issued[s] = true;
@@ -621,9 +679,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             int acc = 0;
             for (int64_t t = t_first; ok && t < total_tiles; t += t_step, ++acc) {
-                const int g = group_of(grp, t);
+                int64_t tl;
+                const int g = locate(grp, t, tl);
                 const EpiParams ep = grp.ep[g];
-                const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
+                const Tile x = tile_at(ep, tl, BN, BMT);
                 const int buf = acc & 1;
                 const uint32_t use = (uint32_t)(acc >> 1);
                 if (!wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) break;
@@ -677,10 +736,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         int acc = 0;
         uint32_t blocks_out = 0;  // bulk groups this warp committed
         for (int64_t t = t_first; t < total_tiles; t += t_step, ++acc) {
-            const int g = group_of(grp, t);
+            int64_t tl;
+            const int g = locate(grp, t, tl);
             const EpiParams ep = grp.ep[g];  // register copy (see the producer)
             const CUtensorMap* tmC = &grp.c[g];
-            const Tile x = tile_at(ep, t - grp.tile_start[g], BN, BMT);
+            const Tile x = tile_at(ep, tl, BN, BMT);
             const int buf = acc & 1;
             const uint32_t use = (uint32_t)(acc >> 1);
             // the tcgen05.ld below is warp-collective: leave the loop together
@@ -884,11 +944,23 @@ struct AttnKeysParams {
     CUtensorMap a_map;  // keys:    (HD, S_k, H, B) view of K (MODE 0) or V (MODE 1)
     CUtensorMap b_map;  // queries: (HD, S_q, H, B) view of Q (MODE 0) or dO (MODE 1)
     const float* P;     // MODE 1: probabilities [B, H, Sq, Sk]
-    float* out;         // P (MODE 0) or dS (MODE 1), [B, H, Sq, Sk]
+    float* out;         // P (MODE 0; may be null) or dS (MODE 1), [B, H, Sq, Sk]
+    float* stats;       // MODE 0, optional: column max [B*H*Sk] then inverse column sum [B*H*Sk]
     int H, Sq, Sk, key_blocks;
     float scale;
     int causal;
 };
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x with the PTX approximate instruction (relative error around 2^-22,
+// far below the tf32 rounding the probabilities take before their
+// products; subnormal results flush to 0)
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 template <int HD, int SQ>
 struct AttnKeysSmem {
@@ -1008,13 +1080,15 @@ __global__ void __launch_bounds__(128 * attn_keys_groups<MODE>(), 2)
 #pragma unroll
             for (int g = 1; g < QG; ++g) m = fmaxf(m, red[g * 128 + kl]);
             __syncthreads();
+            // exp(scale s - m) = exp2(s c2 - m log2 e)
+            const float c2 = p.scale * kLog2e, m2 = m * kLog2e;
             float sum = 0.f;
             for (int c = 0; c < HALF / 32; ++c) {
                 tmem_ld32(taddr + (uint32_t)(c * 32), r);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int q = q0 + c * 32 + j;
-                    if (q < p.Sq && !(p.causal && key > q)) sum += expf(p.scale * __uint_as_float(r[j]) - m);
+                    if (q < p.Sq && !(p.causal && key > q)) sum += exp2_approx(fmaf(__uint_as_float(r[j]), c2, -m2));
                 }
             }
             red[half * 128 + kl] = sum;
@@ -1023,13 +1097,19 @@ __global__ void __launch_bounds__(128 * attn_keys_groups<MODE>(), 2)
 #pragma unroll
             for (int g = 1; g < QG; ++g) sum += red[g * 128 + kl];
             const float inv = 1.0f / (sum < 1e-45f ? 1.0f : sum);
-            for (int c = 0; c < HALF / 32; ++c) {
+            if (p.stats && live && half == 0) {
+                const int64_t nk = (int64_t)gridDim.x / p.key_blocks * p.Sk;  // B * H * Sk
+                p.stats[(int64_t)bh * p.Sk + key] = m;
+                p.stats[nk + (int64_t)bh * p.Sk + key] = inv;
+            }
+            for (int c = 0; p.out && c < HALF / 32; ++c) {
                 tmem_ld32(taddr + (uint32_t)(c * 32), r);
                 if (live) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int q = q0 + c * 32 + j;
-                        const float e = (p.causal && key > q) ? 0.f : expf(p.scale * __uint_as_float(r[j]) - m);
+                        const float e =
+                            (p.causal && key > q) ? 0.f : exp2_approx(fmaf(__uint_as_float(r[j]), c2, -m2));
                         if (q < p.Sq) p.out[base + (int64_t)q * p.Sk] = e * inv;
                     }
                 }
@@ -1624,8 +1704,9 @@ bool attn_keys_supported(int Sq, int Sk, int hd, int64_t BH) {
 
 int run_attn_keys(int mode, const float* keys_src, const float* rows_src, const float* P, float* out, int B, int H,
                   int Sq, int Sk, int hd, int64_t key_b, int64_t key_h, int64_t key_s, int64_t row_b, int64_t row_h,
-                  int64_t row_s, float scale, int causal, cudaStream_t st) {
+                  int64_t row_s, float scale, int causal, cudaStream_t st, float* stats) {
     if (!attn_keys_supported(Sq, Sk, hd, (int64_t)B * H)) return MLE_ERR_UNSUPPORTED;
+    if (mode == 0 && !out && !stats) return MLE_ERR_ARG;
     tc::AttnKeysParams prm;
     memset(&prm, 0, sizeof(prm));
     const int SQ = Sq <= 128 ? 128 : 256;
@@ -1637,6 +1718,7 @@ int run_attn_keys(int mode, const float* keys_src, const float* rows_src, const 
         return MLE_ERR_UNSUPPORTED;
     prm.P = P;
     prm.out = out;
+    prm.stats = mode == 0 ? stats : nullptr;
     prm.H = H;
     prm.Sq = Sq;
     prm.Sk = Sk;
@@ -1661,6 +1743,8 @@ int run_attn_keys(int mode, const float* keys_src, const float* rows_src, const 
 #undef MLE_AK
     return MLE_ERR_UNSUPPORTED;
 }
+
+#include "attention_flash.cuh"
 
 int run_gemm(const GemmProblem& p, cudaStream_t st) {
     if (p.M <= 0 || p.N <= 0 || p.nbatch <= 0 || p.channels <= 0) return MLE_OK;
@@ -1746,6 +1830,72 @@ int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st)
         }
         return MLE_OK;
     }
+    // problems reading the same A over the same tile rows walk them together
+    bool ilv = n > 1;
+    for (int i = 1; i < n && ilv; ++i)
+        ilv = ps[i].A == ps[0].A && ps[i].lda == ps[0].lda && grp.ep[i].m_tiles == grp.ep[0].m_tiles &&
+              grp.ep[i].splits == grp.ep[0].splits && grp.ep[i].kb_per_split == grp.ep[0].kb_per_split &&
+              ps[i].nbatch == ps[0].nbatch && ps[i].channels == ps[0].channels;
+    if (ilv) {
+        grp.ilv = 1;
+        grp.ilv_n[0] = 0;
+        for (int i = 0; i < n; ++i) grp.ilv_n[i + 1] = grp.ilv_n[i] + grp.ep[i].n_tiles;
+    }
+    g_last_kpl = kpl;
+    return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st, pair, kpl);
+}
+
+int run_gemm_kcat(const GemmProblem* ps, int n, cudaStream_t st) {
+    using namespace tc;
+    if (n <= 1) return n == 1 ? run_gemm(ps[0], st) : MLE_OK;
+    // one output, one launch, each A_g B_g product a segment of the
+    // reduction: C, M, N, layouts, mode and alpha shared, unbatched
+    bool ok = n <= kMaxGroup;
+    int64_t ksum = 0;
+    for (int i = 0; i < n && ok; ++i) {
+        const GemmProblem& p = ps[i];
+        ok = tc_path(p) && p.C == ps[0].C && p.M == ps[0].M && p.N == ps[0].N && p.ldc == ps[0].ldc &&
+             p.mode == ps[0].mode && p.alpha == ps[0].alpha && p.nbatch == 1 && p.channels == 1 && !p.bias &&
+             !p.c_split && p.mode != EPI_ATOMIC && p.K > 0 && p.K % 64 == 0 &&
+             shape_of(p).A_MN == shape_of(ps[0]).A_MN && shape_of(p).B_MN == shape_of(ps[0]).B_MN;
+        ksum += p.K;
+    }
+    if (!ok || ksum > 0x7fffffff) return run_gemm_group(ps, n, true, st);
+    GemmProblem whole = ps[0];
+    whole.K = (int)ksum;
+    int BN, splits;
+    bool pair = false;
+    choose_tiles(&whole, 1, BN, splits, false, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
+    apply_forced_tiles(&whole, 1, BN, splits, pair);
+    int kpl = g_stage_kblocks == 2 ? 2 : 1;
+    for (int i = 0; i < n; ++i) kpl = split_ok(ps[i]) ? kpl : 1;
+    tc::GemmGroup grp;
+    for (;;) {
+        memset(&grp, 0, sizeof(grp));
+        bool all_ok = true;
+        // every segment's operand maps; the tile walk and epilogue are ep[0]'s
+        for (int i = 0; i < n && all_ok; ++i) {
+            bool seg_ok = false;
+            const int s = prepare(ps[i], BN, 1, false, grp, i, st, seg_ok, pair, kpl);
+            if (s) return s;
+            all_ok = seg_ok;
+        }
+        if (all_ok) break;
+        if (kpl == 2) {
+            kpl = 1;
+            continue;
+        }
+        return run_gemm_group(ps, n, true, st);
+    }
+    grp.n = 1;
+    grp.kcat = n;
+    grp.kcat_kb[0] = 0;
+    for (int i = 0; i < n; ++i) grp.kcat_kb[i + 1] = grp.kcat_kb[i] + ps[i].K / BK;
+    grp.ep[0].K = (int)ksum;
+    grp.ep[0].splits = 1;
+    grp.ep[0].kb_per_split = grp.kcat_kb[n];
+    grp.tile_start[0] = 0;
+    grp.tile_start[1] = grp.ep[0].tiles;
     g_last_kpl = kpl;
     return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st, pair, kpl);
 }
@@ -2121,13 +2271,14 @@ int mle_linear_group_bwd(const float* X, const float* const* W, const float* con
     GemmProblem ps[tc::kMaxGroup];
     int s;
     if (dX) {
-        // dX += sum_i dY_i W_i^T: every product reduce-adds into dX
+        // dX += sum_i dY_i W_i^T: one product over the concatenated
+        // reduction (K = sum of out_features), dX read and written once
         for (int i = 0; i < n; ++i) {
             if (!W[i] || !dY[i] || out_features[i] <= 0) return MLE_ERR_ARG;
             ps[i] = linear_problem(dY[i], W[i], dX, nullptr, rows, in_features, out_features[i], out_features[i],
                                    out_features[i], in_features, 0, 1, tc::EPI_ACCUM);
         }
-        s = run_gemm_group(ps, n, true, st);
+        s = run_gemm_kcat(ps, n, st);
         if (s) return s;
     }
     // dW_i += X^T dY_i

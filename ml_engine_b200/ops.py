@@ -226,6 +226,29 @@ def attention_bwd(Q, K, V, P, dO, dQ, dK, dV, dP, dS, batch, heads, seq_q, seq_k
           _s())
 
 
+def attention_flash_fwd(Q, K, V, O, stats, batch, heads, seq_q, seq_k, head_dim, scale, causal=0,
+                        layout=HEAD_MAJOR):
+    """Column-softmax attention without the score matrices in HBM:
+    writes O and stats (2 * batch*heads*seq_k floats: column max, then
+    inverse column sum)."""
+    _call("mle_attention_flash_fwd", _p(Q), _p(K), _p(V), _p(O), _p(stats), batch, heads, seq_q, seq_k, head_dim,
+          scale, causal, layout, _s())
+
+
+def attention_flash_bwd(Q, K, V, dO, stats, dQ, dK, dV, batch, heads, seq_q, seq_k, head_dim, scale, causal=0,
+                        key_grad_mode=KEYGRAD_REFERENCE, layout=HEAD_MAJOR, assign_mask=0, dvec=None):
+    """Backward of attention_flash_fwd from its stats; dvec
+    (batch*heads*seq_k floats of workspace) is made here when not given."""
+    if dvec is None:
+        dvec = torch.empty(batch * heads * seq_k, device=Q.device, dtype=torch.float32)
+    _call("mle_attention_flash_bwd", _p(Q), _p(K), _p(V), _p(dO), _p(stats), _p(dvec), _p(dQ), _p(dK), _p(dV),
+          batch, heads, seq_q, seq_k, head_dim, scale, causal, key_grad_mode, layout, assign_mask, _s())
+
+
+def attention_flash_supported(seq_q, seq_k, head_dim, softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE):
+    return bool(kernels().mle_attention_flash_supported(seq_q, seq_k, head_dim, softmax_axis, key_grad_mode))
+
+
 def attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis=1, key_grad_mode=KEYGRAD_REFERENCE):
     return bool(kernels().mle_attention_fused_supported(seq_q, seq_k, head_dim, softmax_axis, key_grad_mode))
 

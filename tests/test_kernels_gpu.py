@@ -796,24 +796,29 @@ def test_watchdog_clear(cuda, ops):
     assert ops.watchdog() == 0
 
 
-@pytest.mark.parametrize("n,rows,pairs", [(1, 1024, 0), (2, 1024, 0), (3, 1024, 0), (3, 8192, 1)])
-def test_linear_group_matches_separate_linears(cuda, ops, rng, n, rows, pairs):
+@pytest.mark.parametrize("n,rows,pairs,outs", [(1, 1024, 0, None), (2, 1024, 0, None), (3, 1024, 0, None),
+                                                (3, 8192, 1, None), (3, 8192, 1, (512, 512, 512)),
+                                                (2, 1024, 0, (256, 96))])
+def test_linear_group_matches_separate_linears(cuda, ops, rng, n, rows, pairs, outs):
     """mle_linear_group_fwd/_bwd against n separate mle_linear_fwd/_bwd
-    calls (TF32 products; dX sums the n products with reduce-adds); the
-    8192-row case is large enough for the group to run on CTA pairs."""
+    calls (TF32 products; dX is one product over the concatenated
+    reduction when every out_features is a multiple of 64, else the n
+    products reduce-added); the 8192-row cases are large enough for the
+    group to run on CTA pairs (512 x 3: the query/key/value projections of
+    configs[2])."""
     from ml_engine_b200._lib import kernels
     old_pairs = kernels().mle_get_gemm_pairs()
     kernels().mle_set_gemm_pairs(pairs)
     try:
-        _linear_group_case(cuda, ops, rng, n, rows)
+        _linear_group_case(cuda, ops, rng, n, rows, outs)
     finally:
         kernels().mle_set_gemm_pairs(old_pairs)
 
 
-def _linear_group_case(cuda, ops, rng, n, rows):
+def _linear_group_case(cuda, ops, rng, n, rows, outs=None):
     from ml_engine_b200._lib import kernels
     din = 256
-    outs = [256, 128, 512][:n]
+    outs = list(outs) if outs else [256, 128, 512][:n]
     X = T(rng.standard_normal((rows, din)).astype(np.float32), cuda)
     Ws = [T((rng.standard_normal((din, o)) * 0.05).astype(np.float32), cuda) for o in outs]
     Bs = [T(rng.standard_normal(o).astype(np.float32), cuda) for o in outs]
@@ -901,6 +906,119 @@ def test_attention_keys_kernels(cuda, ops, orc, rng, case, key_mode):
     # dP product's tiling); the score gradient's cancellation p (dP - d)
     # magnifies that in dQ and dK
     for name, a, b in zip("P O dQ dK dV".split(), runs[1], runs[0]):
+        assert rel_err(a, b) <= 1e-3, (name, rel_err(a, b))
+
+
+FLASH_CASES = [  # B, H, Sq, Sk, hd, causal
+    (2, 8, 128, 128, 32, 0),   # configs[1] heads
+    (2, 8, 128, 128, 32, 1),
+    (1, 4, 256, 256, 64, 1),   # configs[2] masked self-attention heads
+    (1, 4, 256, 256, 64, 0),   # configs[2] cross-attention heads (unmasked)
+    (3, 2, 192, 192, 64, 1),   # a partial second block of queries and keys
+    (2, 3, 200, 136, 64, 1),   # ragged: Sq, Sk no multiple of the 64-wide chunk
+    (1, 2, 96, 448, 64, 0),    # queries below one block, seven key chunks
+    (12, 8, 256, 256, 64, 1),  # 192 units: persistent CTAs walk more than one
+    (40, 8, 128, 128, 32, 0),  # 320 units of configs[1]'s shape: up to three per CTA
+]
+
+
+def _flash_reference(orc, Q, K, V, dO, B, Hh, Sq, Sk, D, scale, causal, key_mode):
+    """The reference's chain on the C oracle: P, O, the column statistics,
+    dQ, dK (either key gradient), dV."""
+    bh = B * Hh
+    S = orc.scale_write(orc.bcmm(1, Q, K, np.zeros((bh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 0, 3, 3, 3), scale)
+    rP = orc.softmax_fwd(S, bh, Sq, Sk, 1, causal)
+    rO = orc.bcmm(0, rP, V, np.zeros((bh, Sq, D), np.float32), B, Hh, Sq, Sk, D, 0, 3, 3, 3)
+    rdP = orc.bcmm(1, dO, V, np.zeros((bh, Sq, Sk), np.float32), B, Hh, Sq, D, Sk, 1, 3, 3, 3)
+    rdV = orc.bcmm(2, rP, dO, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
+    rdS = orc.accumulate(orc.softmax_bwd(rP, rdP, np.zeros_like(rP), bh, Sq, Sk, 1), np.zeros_like(rP), scale)
+    rdQ = orc.bcmm(0, rdS, K, np.zeros((bh, Sq, D), np.float32), B, Hh, Sq, Sk, D, 1, 3, 3, 3)
+    if key_mode == 0:
+        rdK = orc.bcmm(3, Q, rdS, np.zeros((bh, Sk, D), np.float32), B, Hh, D, Sq, Sk, 1, 3, 3, 3)
+    else:
+        rdK = orc.bcmm(2, rdS, Q, np.zeros((bh, Sk, D), np.float32), B, Hh, Sk, Sq, D, 1, 3, 3, 3)
+    S3 = S.reshape(bh, Sq, Sk).astype(np.float64)
+    m = S3.max(axis=1)                                  # every query, masked ones included
+    e = np.exp(S3 - m[:, None, :])
+    if causal:
+        e = e * (np.arange(Sk)[None, None, :] <= np.arange(Sq)[None, :, None])
+    l = e.sum(axis=1)
+    return rO, rdQ, rdK, rdV, m, 1.0 / np.where(l < 1e-45, 1.0, l)
+
+
+@pytest.mark.parametrize("key_mode", [0, 1])
+@pytest.mark.parametrize("case", FLASH_CASES)
+def test_attention_flash(cuda, ops, orc, rng, case, key_mode):
+    """The flash entry points (scores, probabilities and score gradients
+    never in HBM; the backward recomputes P from the forward's column max
+    and inverse sum) against the C oracle's reference chain at the TF32
+    bound, in the token-major layout the graph nodes use, with dQ, dK, dV
+    accumulated onto existing values; the statistics against float64."""
+    B, Hh, Sq, Sk, D, causal = case
+    if key_mode == 0 and not (Sq == Sk and Sk % D == 0):
+        pytest.skip("the reference key gradient is defined for Sq == Sk, Sk % hd == 0")
+    assert ops.attention_flash_supported(Sq, Sk, D, 1, key_mode)
+    bh = B * Hh
+    Q, K, V, dO = _attn_inputs(rng, B, Hh, Sq, Sk, D)
+    scale = float(1.0 / np.sqrt(D))
+    tm = lambda x: T(_to_token_major(x, B, Hh), cuda)   # noqa: E731
+    back = lambda x: _from_token_major(H(x), B, Hh, D)   # noqa: E731
+    O = torch.full((B, Sq, Hh * D), float("nan"), device=cuda)
+    stats = torch.zeros(2 * bh * Sk, device=cuda)
+    ops.attention_flash_fwd(tm(Q), tm(K), tm(V), O, stats, B, Hh, Sq, Sk, D, scale, causal, 1)
+    pre = [rng.standard_normal((bh, s, D)).astype(np.float32) for s in (Sq, Sk, Sk)]
+    dQ, dK, dV = (tm(x) for x in pre)
+    ops.attention_flash_bwd(tm(Q), tm(K), tm(V), tm(dO), stats, dQ, dK, dV, B, Hh, Sq, Sk, D, scale, causal,
+                            key_mode, 1, 0)
+    rO, rdQ, rdK, rdV, rm, rinv = _flash_reference(orc, Q, K, V, dO, B, Hh, Sq, Sk, D, scale, causal, key_mode)
+    st = H(stats).reshape(2, bh, Sk)
+    assert rel_err(st[0], rm) <= RTOL_TC
+    assert rel_err(st[1], rinv) <= RTOL_TC
+    got = (back(O), back(dQ) - pre[0], back(dK) - pre[1], back(dV) - pre[2])
+    for name, a, r in zip("O dQ dK dV".split(), got, (rO, rdQ, rdK, rdV)):
+        assert np.isfinite(a).all(), name
+        assert norm_err(a, r) <= RTOL_TC, (name, norm_err(a, r))
+        assert rel_err(a, r) <= 2 * RTOL_TC, (name, rel_err(a, r))
+
+
+@pytest.mark.parametrize("case", [(2, 8, 128, 128, 32, 1), (1, 4, 256, 256, 64, 1)])
+def test_attention_flash_assign_and_layouts(cuda, ops, rng, case):
+    """assign_mask writes dQ, dK, dV instead of adding (the buffers' NaN
+    contents must vanish); the head-major layout gives the token-major
+    results; the flash path and the keys-on-lanes tensor-core path agree to
+    summation order."""
+    B, Hh, Sq, Sk, D, causal = case
+    bh = B * Hh
+    Q, K, V, dO = _attn_inputs(rng, B, Hh, Sq, Sk, D)
+    scale = float(1.0 / np.sqrt(D))
+    tm = lambda x: T(_to_token_major(x, B, Hh), cuda)   # noqa: E731
+    back = lambda x: _from_token_major(H(x), B, Hh, D)   # noqa: E731
+    outs = {}
+    for layout in (1, 0):
+        cv = tm if layout == 1 else (lambda x: T(x, cuda))                           # noqa: E731
+        bk = back if layout == 1 else H
+        O = torch.empty((B, Sq, Hh * D), device=cuda)
+        stats = torch.empty(2 * bh * Sk, device=cuda)
+        ops.attention_flash_fwd(cv(Q), cv(K), cv(V), O, stats, B, Hh, Sq, Sk, D, scale, causal, layout)
+        dQ, dK, dV = (torch.full((B, s, Hh * D), float("nan"), device=cuda) for s in (Sq, Sk, Sk))
+        ops.attention_flash_bwd(cv(Q), cv(K), cv(V), cv(dO), stats, dQ, dK, dV, B, Hh, Sq, Sk, D, scale, causal,
+                                0, layout, 7)
+        outs[layout] = [bk(x).reshape(bh, -1, D) for x in (O, dQ, dK, dV)]
+    for name, a, b in zip("O dQ dK dV".split(), outs[1], outs[0]):
+        assert np.isfinite(a).all(), name
+        assert np.array_equal(a, b), name
+    old_path = ops.set_attention_path(ops.ATTN_PATH_TENSOR)
+    try:
+        P = torch.zeros(bh, Sq, Sk, device=cuda)
+        O = torch.zeros(B, Sq, Hh * D, device=cuda)
+        ops.attention_fwd(tm(Q), tm(K), tm(V), P, O, B, Hh, Sq, Sk, D, scale, causal, 1, 1)
+        dQ, dK, dV = (torch.zeros(B, s, Hh * D, device=cuda) for s in (Sq, Sk, Sk))
+        ops.attention_bwd(tm(Q), tm(K), tm(V), P, tm(dO), dQ, dK, dV, None, None, B, Hh, Sq, Sk, D, scale,
+                          causal, 1, 0, 1)
+        ref = [back(x) for x in (O, dQ, dK, dV)]
+    finally:
+        ops.set_attention_path(old_path)
+    for name, a, b in zip("O dQ dK dV".split(), outs[1], ref):
         assert rel_err(a, b) <= 1e-3, (name, rel_err(a, b))
 
 
