@@ -34,8 +34,8 @@
 // TMA that runs on across units, so the next unit's copies overlap this
 // unit's work, warp 1 issues the MMAs (the next
 // chunk's scores before this chunk's accumulating product, so the tensor
-// cores run while the epilogue warps exponentiate), warps 2-9 own the TMEM
-// lane quarters (two warps each, one per half of a chunk's columns).  The
+// cores run while the epilogue warps exponentiate), warps 2-17 own the TMEM
+// lane quarters (four warps each, one per 16 of a chunk's 64 columns).  The
 // accumulators stay in TMEM until a unit's last chunk, in two sets that
 // alternate between units, so a unit's stores overlap the next one's
 // products.
@@ -44,8 +44,12 @@ namespace tc {
 constexpr int FA_FWD = 0, FA_BWD_KEYS = 1, FA_BWD_ROWS = 2;
 constexpr int FA_CH = 64;         // chunk: keys (FWD, BWD_ROWS) or queries (BWD_KEYS)
 constexpr int FA_SKMAX = 512;     // keys whose statistics a CTA stages in shared memory
-constexpr int FA_EPI_WARPS = 8;  // two per TMEM lane quarter
-constexpr int FA_THREADS = 64 + 32 * FA_EPI_WARPS;  // producer, MMA issuer, epilogue warps
+constexpr int FA_EPI_WARPS = 16;                     // four per TMEM lane quarter
+constexpr int FA_QW = FA_EPI_WARPS / 4;              // warps sharing a lane quarter
+constexpr int FA_COLS = FA_CH / FA_QW;               // a chunk's columns per warp
+constexpr int FA_EPI_THREADS = 32 * FA_EPI_WARPS;
+constexpr int FA_THREADS = 64 + FA_EPI_THREADS;      // producer, MMA issuer, epilogue warps
+static_assert(FA_COLS == 16, "the epilogue moves 16 TMEM columns per access");
 
 struct FlashParams {
     CUtensorMap fix[2];  // per-CTA operands, 128 rows, K-major
@@ -76,8 +80,8 @@ struct FlashSmem {
     static constexpr int STAT = RING + NS * SLOT;
     // per key (FWD, BWD_ROWS): {m log2 e - log2(1/l), d}
     static constexpr int NSTAT = KIND == FA_BWD_KEYS ? 0 : FA_SKMAX * 8;
-    static constexpr int RED = STAT + NSTAT;  // column-dot partials: [unit parity][column half][128]
-    static constexpr int BAR = RED + 2 * 2 * 128 * 4;
+    static constexpr int RED = STAT + NSTAT;  // column-dot partials: [unit parity][column group][128]
+    static constexpr int BAR = RED + 2 * FA_QW * 128 * 4;
     // full[NS], empty[NS], fixed_full, fixed_empty, s_full[2], epi_done[2],
     // acc_done[2], acc_free[2], drain
     static constexpr int NBARS = 2 * NS + 11;
@@ -111,6 +115,25 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
         "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
         "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
 
@@ -336,6 +359,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
                         next_issued = true;
                     }
                     if (mbar_test_wait(&epi_done[g & 1u], (g >> 1) & 1u)) return true;
+                    // leave the issue slots to the epilogue warps sharing this scheduler
+                    __nanosleep(64);
                     if ((k & 127u) == 127u) {
                         if (*abort_flag) return false;
                         const uint64_t now = gtimer();
@@ -433,14 +458,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
         }
         __syncwarp();
     } else {
-        // ------------------------- epilogue warps 2-9 -------------------------
-        // two warps per TMEM lane quarter, each taking 32 of a chunk's 64
-        // columns (and 32 of an accumulator row's HD columns).  Every warp
+        // ------------------------- epilogue warps 2-17 ------------------------
+        // four warps per TMEM lane quarter, each taking 16 of a chunk's 64
+        // columns (and 16 of an accumulator row's HD columns).  Every warp
         // walks every unit and chunk and reaches the same named barriers, also
         // after a timed-out wait (it then skips the work), so none waits for
         // a warp that left.
         const int quarter = warp & 3;
-        const int ch = (warp - 2) >> 2;     // column half
+        const int ch = (warp - 2) >> 2;     // column group
         const int r = quarter * 32 + lane;  // TMEM lane = row of the 128-row block
         const uint32_t lanes = tmem + ((uint32_t)(quarter * 32) << 16);
         const int et = threadIdx.x - 64;
@@ -449,8 +474,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
         // a unit's per-key statistics are read from global memory one unit
         // ahead (its loads in flight while the previous unit runs): BWD_KEYS
         // the thread's key, else keys et and et + 256 of the head
-        static_assert(FA_SKMAX <= 2 * FA_EPI_WARPS * 32, "statistics per thread");
-        float pf[6] = {0.f, 1.f, 0.f, 0.f, 1.f, 0.f};
+        constexpr int NPF = (FA_SKMAX + FA_EPI_THREADS - 1) / FA_EPI_THREADS;  // keys per thread
+        float pf[3 * NPF];
+#pragma unroll
+        for (int i = 0; i < NPF; ++i) {
+            pf[3 * i] = 0.f;
+            pf[3 * i + 1] = 1.f;
+            pf[3 * i + 2] = 0.f;
+        }
         auto fetch = [&](int64_t u) {
             if (u >= units) return;
             int b, h, row0;
@@ -464,8 +495,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
                 }
             } else {
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int k = et + i * FA_EPI_WARPS * 32;
+                for (int i = 0; i < NPF; ++i) {
+                    const int k = et + i * FA_EPI_THREADS;
                     if (k < Sk) {
                         pf[3 * i] = stats[bh * Sk + k];
                         pf[3 * i + 1] = stats[nk + bh * Sk + k];
@@ -482,29 +513,31 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
             int b, h, row0;
             int64_t bh;
             coords(u, b, h, row0, bh);
-            float cur[6];
+            float cur[3 * NPF];
 #pragma unroll
-            for (int i = 0; i < 6; ++i) cur[i] = pf[i];
+            for (int i = 0; i < 3 * NPF; ++i) cur[i] = pf[i];
             fetch(u + gridDim.x);
             if (KIND != FA_BWD_KEYS) {
                 // the previous unit's statistics are no longer read
-                asm volatile("bar.sync 1, %0;" ::"n"(FA_EPI_WARPS * 32) : "memory");
+                asm volatile("bar.sync 1, %0;" ::"n"(FA_EPI_THREADS) : "memory");
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int k = et + i * FA_EPI_WARPS * 32;
+                for (int i = 0; i < NPF; ++i) {
+                    const int k = et + i * FA_EPI_THREADS;
                     if (k < Sk) kst[k] = make_float2(cur[3 * i] * kLog2e - log2f(cur[3 * i + 1]), cur[3 * i + 2]);
                 }
-                asm volatile("bar.sync 1, %0;" ::"n"(FA_EPI_WARPS * 32) : "memory");
+                asm volatile("bar.sync 1, %0;" ::"n"(FA_EPI_THREADS) : "memory");
             }
             const int key_r = row0 + r;  // BWD_KEYS: this thread's key; else its query
             float kmm = 0.f, dsum = 0.f;
             if (KIND == FA_BWD_KEYS && key_r < Sk) kmm = cur[0] * kLog2e - log2f(cur[1]);
-            // the column dot over every query: this warp's half plus its partner's
-            float* rd = red + (it & 1) * 256;
+            // the column dot over every query: the partial sums of the four column groups
+            float* rd = red + (it & 1) * FA_QW * 128;
             auto combine_dsum = [&]() {
                 rd[ch * 128 + r] = dsum;
-                asm volatile("bar.sync 2, %0;" ::"n"(FA_EPI_WARPS * 32) : "memory");
-                dsum = rd[r] + rd[128 + r];
+                asm volatile("bar.sync 2, %0;" ::"n"(FA_EPI_THREADS) : "memory");
+                dsum = 0.f;
+#pragma unroll
+                for (int w = 0; w < FA_QW; ++w) dsum += rd[w * 128 + r];
             };
             int cb, nc;
             unit_chunks(row0, cb, nc);
@@ -518,18 +551,18 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
                 tc_fence_after();
                 const int c = cb + v % nc;
                 const bool pass2 = v >= nc;
-                const uint32_t col = (uint32_t)(ch * 32);
+                const uint32_t col = (uint32_t)(ch * FA_COLS);
                 const int i0 = c * FA_CH + (int)col;  // first key (FWD, BWD_ROWS) or query (BWD_KEYS) of the columns
-                uint32_t sr[32], pr[32], o[32];
-                tmem_ld32(lanes + L::SB0 + bb * FA_CH + col, sr);
-                if (KIND != FA_FWD) tmem_ld32(lanes + L::PB0 + bb * FA_CH + col, pr);
+                uint32_t sr[FA_COLS], pr[FA_COLS], o[FA_COLS];
+                tmem_ld16(lanes + L::SB0 + bb * FA_CH + col, sr);
+                if (KIND != FA_FWD) tmem_ld16(lanes + L::PB0 + bb * FA_CH + col, pr);
                 bool all_live;
-                if (KIND == FA_BWD_KEYS) all_live = key_r < Sk && i0 + 32 <= Sq && !(causal && key_r > i0);
-                else all_live = key_r < Sq && i0 + 32 <= Sk && !(causal && i0 + 31 > key_r);
+                if (KIND == FA_BWD_KEYS) all_live = key_r < Sk && i0 + FA_COLS <= Sq && !(causal && key_r > i0);
+                else all_live = key_r < Sq && i0 + FA_COLS <= Sk && !(causal && i0 + FA_COLS - 1 > key_r);
                 auto body = [&](auto checked) {
                     constexpr bool CHECK = decltype(checked)::value;
 #pragma unroll
-                    for (int jh = 0; jh < 32; jh += 16) {
+                    for (int jh = 0; jh < FA_COLS; jh += 16) {
                     // 16 columns' statistics first: independent shared loads
                     float cmm[16], cd[16];
                     if (KIND != FA_BWD_KEYS) {
@@ -573,7 +606,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
                 else body(std::true_type());
                 // P (or P^T) replaces S; dS (or dS^T) replaces dP
                 const bool to_s = KIND == FA_FWD || (KIND == FA_BWD_KEYS && !pass2);
-                tmem_st32(lanes + (to_s ? L::SB0 : L::PB0) + bb * FA_CH + col, o);
+                tmem_st16(lanes + (to_s ? L::SB0 : L::PB0) + bb * FA_CH + col, o);
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
@@ -583,18 +616,18 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
             if (KIND == FA_BWD_KEYS && !two_pass) combine_dsum();
             const int ab = it & 1;
             ok = __all_sync(0xffffffffu, ok && wait_bounded(&acc_done[ab], (uint32_t)(it >> 1) & 1u, abort_flag));
-            if (ok && ch < HD / 32) {
+            if (ok && ch < HD / 16) {
                 tc_fence_after();
-                const uint32_t cc = (uint32_t)(ch * 32);  // this warp's 32 accumulator columns
+                const uint32_t cc = (uint32_t)(ch * 16);  // this warp's 16 accumulator columns
                 const uint32_t acc0 = L::ACC_BASE + (uint32_t)ab * L::ACC_STRIDE, acc1 = acc0 + HD;
-                // 32 accumulated floats of one row leave per thread
+                // 16 accumulated floats of one row leave per thread
                 auto store_row = [&](uint32_t acc_col, float* dst, bool live, int accum) {
-                    uint32_t a[32];
-                    tmem_ld32(lanes + acc_col + cc, a);
+                    uint32_t a[16];
+                    tmem_ld16(lanes + acc_col + cc, a);
                     if (!live) return;
                     float4* d4 = reinterpret_cast<float4*>(dst + cc);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
+                    for (int j = 0; j < 4; ++j) {
                         float4 x = make_float4(__uint_as_float(a[4 * j]), __uint_as_float(a[4 * j + 1]),
                                                __uint_as_float(a[4 * j + 2]), __uint_as_float(a[4 * j + 3]));
                         if (accum) {
@@ -628,11 +661,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1) attn_flash_kernel(const __grid_
                         // consecutive floats of one row
                         float* base = out1 + (int64_t)b * o1b + (int64_t)h * o1h;
                         const int per = Sk / HD;
-                        uint32_t a[32];
-                        tmem_ld32(lanes + acc1 + cc, a);
+                        uint32_t a[16];
+                        tmem_ld16(lanes + acc1 + cc, a);
                         if (row < Sq) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) {
+                            for (int j = 0; j < 16; ++j) {
                                 const int d = (int)cc + j;
                                 float* dst = base + (int64_t)(d * per + row / HD) * o1s + (row % HD);
                                 const float x = __uint_as_float(a[j]);
