@@ -137,9 +137,11 @@ def backward_work(wl, B):
     """Algorithmic backward work of one step on B sequences: tensor FLOP
     (Linear dX and dW, 4 attention products per attention block) and the
     bytes the non-GEMM backward ops must move (fp32, each tensor read or
-    written once): LayerNorm 16 B/elem, GELU 12, residual Add 12, column
-    softmax 12 B/score, loss gradient 8 B/logit.  The MLP's tiny
-    elementwise ops are left out."""
+    written once): LayerNorm 16 B/elem, GELU 12, residual Add 12, loss
+    gradient 8 B/logit.  The attention's score matrices need not reach HBM
+    (the flash kernels keep them on chip), so they add no bytes; its
+    recomputed score products are not counted as work either.  The MLP's
+    tiny elementwise ops are left out."""
     c = WORKLOADS[wl]["cfg"]
     if wl == "mlp":
         T = B
@@ -152,8 +154,7 @@ def backward_work(wl, B):
     lns = 2 * L if wl == "encoder" else 5 * L
     adds = lns
     ffns = L if wl == "encoder" else 2 * L
-    byts = 16.0 * lns * T * D + 12.0 * adds * T * D + 12.0 * ffns * T * F + 12.0 * blocks * B * H * S * S \
-        + 8.0 * T * V
+    byts = 16.0 * lns * T * D + 12.0 * adds * T * D + 12.0 * ffns * T * F + 8.0 * T * V
     return flop, byts
 
 
@@ -564,6 +565,77 @@ def run_reference(args, rank, world):
 
 
 # ------------------------------------------------------------ kernel sweep
+def run_attention(args):
+    """The attention block of configs[2] (8 heads of 64, seq 256, token-major
+    [B, S, 512] projections; B = the rank's 256 sequences, or --batch),
+    masked (decoder self-attention) and unmasked (encoder, cross), on both
+    tensor-core paths: the keys-on-lanes kernels writing P and the score
+    gradient to HBM beside tcgen05 GEMMs, and the flash kernels (scores on
+    chip, P recomputed from per-key statistics).  Forward and backward
+    (reference key gradient, gradients assigned) timed apart with CUDA
+    events over `--steps` launches after `--warmup`; one JSON line per
+    case, with the algorithmic FLOP of the 2 + 4 products and the bytes the
+    flash path must move (Q, K, V, O forward; Q, K, V, dO read and dQ, dK,
+    dV written backward)."""
+    import torch
+
+    from ml_engine_b200 import ops
+    from ml_engine_b200._lib import kernels
+    dev = torch.device("cuda", 0)
+    hbm_peak, bf16_peak, kind = load_peaks()
+    B = args.batch or 256
+    H, S, D = 8, 256, 64
+    g = torch.Generator(device=dev).manual_seed(0)
+    Q, K, V, dO = (torch.randn(B, S, H * D, device=dev, generator=g) for _ in range(4))
+    O = torch.empty(B, S, H * D, device=dev)
+    dQ, dK, dV = (torch.empty(B, S, H * D, device=dev) for _ in range(3))
+    stats = torch.empty(2 * B * H * S, device=dev)
+    dvec = torch.empty(B * H * S, device=dev)
+    P = torch.empty(B * H, S, S, device=dev)
+    ws = torch.empty(B * H * S * S, device=dev)
+    scale = 1.0 / 8.0
+    old = ops.set_attention_path(ops.ATTN_PATH_TENSOR)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    flop_f, flop_b = 2 * 2.0 * B * H * S * S * D, 4 * 2.0 * B * H * S * S * D
+    bytes_f, bytes_b = 4.0 * 4 * B * S * H * D, 7 * 4.0 * B * S * H * D
+    try:
+        for causal in (1, 0):
+            paths = {
+                "keys": (lambda: ops.attention_fwd(Q, K, V, P, O, B, H, S, S, D, scale, causal, 1, 1),
+                         lambda: kernels().call("mle_attention_bwd_assign", Q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                                P.data_ptr(), dO.data_ptr(), dQ.data_ptr(), dK.data_ptr(),
+                                                dV.data_ptr(), None, None, ws.data_ptr(), B, H, S, S, D, scale,
+                                                causal, 1, 0, 1, 7, torch.cuda.current_stream().cuda_stream)),
+                "flash": (lambda: ops.attention_flash_fwd(Q, K, V, O, stats, B, H, S, S, D, scale, causal, 1),
+                          lambda: ops.attention_flash_bwd(Q, K, V, dO, stats, dQ, dK, dV, B, H, S, S, D, scale,
+                                                          causal, 0, 1, 7, dvec)),
+            }
+            for name, (fwd, bwd) in paths.items():
+                fwd()
+                f_ms, b_ms = timed(fwd), timed(bwd)
+                print(json.dumps({"attention": name, "batch": B, "heads": H, "seq": S, "head_dim": D,
+                                  "causal": causal, "fwd_ms": f_ms, "bwd_ms": b_ms,
+                                  "fwd_tflops": flop_f / (f_ms * 1e-3) / 1e12,
+                                  "bwd_tflops": flop_b / (b_ms * 1e-3) / 1e12,
+                                  "flash_bytes_fwd_gb": bytes_f / 1e9, "flash_bytes_bwd_gb": bytes_b / 1e9,
+                                  "tf32_peak_tflops": bf16_peak / 2, "hbm_peak_gbs": hbm_peak,
+                                  "peak_kind": kind}), flush=True)
+    finally:
+        ops.set_attention_path(old)
+
+
 def run_sweep(args):
     """linear backward (dX = dY W^T, dW = X^T dY) at M=N=K = n,
     LayerNorm backward and LayerNorm + GELU backward over 65536 rows of
@@ -837,6 +909,8 @@ def main():
     ap.add_argument("--no-ref-cuda", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="configs[4] kernel sweep, one JSON line per case")
+    ap.add_argument("--attention", action="store_true",
+                    help="configs[2]'s attention block on both tensor-core paths, one JSON line per case")
     ap.add_argument("--gemm-pairs", type=int, default=None, choices=[0, 1, 2],
                     help="run large products on CTA pairs (mle_set_gemm_pairs); default: the library's")
     ap.add_argument("--attn-path", default=None, choices=["auto", "fused", "tensor"],
@@ -870,6 +944,9 @@ def main():
         engine().call("mle_set_param_grad_stream", args.param_stream)
     if args.sweep:
         run_sweep(args)
+        return
+    if args.attention:
+        run_attention(args)
         return
     if args.config == "unet":
         run_unet(args)
