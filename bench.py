@@ -675,6 +675,22 @@ def run_sweep(args):
                           "frac_of_bf16": tf / bf16_peak, "peak_kind": kind}), flush=True)
         del X, W, dY, dX, dW
     rows = 65536
+    # bias gradient (column sums) and the GELU backward fused with it, at
+    # configs[2]'s token count: 4 B/elem read, and 12 B/elem (x, dy read; dx written)
+    for w in (512, 2048):
+        dy = torch.randn(rows * w, device=dev, generator=g)
+        db = torch.zeros(w, device=dev)
+        ms = timed(lambda: ops.bias_grad(dy, db), 20)
+        gbs = 4.0 * rows * w / (ms * 1e-3) / 1e9
+        print(json.dumps({"sweep": "bias_grad", "rows": rows, "width": w, "ms": ms, "gbs": gbs,
+                          "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
+        x = torch.randn(rows * w, device=dev, generator=g)
+        dx = torch.empty_like(x)
+        ms = timed(lambda: ops.act_bwd(ops.GELU, x, dy, dx, bias_grad=db, assign=True), 20)
+        gbs = 12.0 * rows * w / (ms * 1e-3) / 1e9
+        print(json.dumps({"sweep": "gelu_bwd_bias_grad", "rows": rows, "width": w, "ms": ms, "gbs": gbs,
+                          "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
+        del dy, db, x, dx
     for w in (1024, 2048, 4096, 8192):
         x = torch.randn(rows * w, device=dev, generator=g)
         y, mean, sq = torch.empty_like(x), torch.empty(rows, device=dev), torch.empty(rows, device=dev)

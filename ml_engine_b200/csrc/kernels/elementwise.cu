@@ -284,8 +284,9 @@ __global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __re
     for (int k = 0; k < W; ++k) s[k] = 0.f;
     if (c0 < cols) {
         if constexpr (VEC) {
-            // U rows per pass, their loads issued together (bytes in flight)
-            constexpr int U = 4;
+            // U rows per pass, their loads issued together (bytes in flight:
+            // the plain column sum reads one tensor, the fused one two)
+            constexpr int U = ACT ? 4 : 8;
             for (int64_t r = r_begin + warp; r < r_end; r += U * kColWarps) {
                 float4 o[U], a[U], d[U];
 #pragma unroll
@@ -345,17 +346,19 @@ __global__ void __launch_bounds__(256) colsum_kernel(int kind, const float* __re
     }
 }
 
-// Launch shape for colsum_kernel: column strips x row chunks, about two
-// waves of blocks, each chunk at least 32 rows.
+// Launch shape for colsum_kernel: column strips x row chunks, each chunk at
+// least 32 rows; about four waves of blocks for the plain column sum and
+// eight for the one fused with an activation backward (all resident: the
+// warps per SM keep enough loads in flight; measured on B200).
 struct ColsumShape {
     dim3 grid;
     int64_t rpb;
 };
 
-inline ColsumShape colsum_shape(int64_t rows, int64_t cols, bool vec) {
+inline ColsumShape colsum_shape(int64_t rows, int64_t cols, bool vec, bool act = false) {
     const int64_t strip = vec ? 128 : 32;
     const int64_t col_blocks = (cols + strip - 1) / strip;
-    int64_t row_blocks = (2 * kSMs + col_blocks - 1) / col_blocks;
+    int64_t row_blocks = ((act ? 8 : 4) * kSMs + col_blocks - 1) / col_blocks;
     const int64_t max_rb = (rows + 31) / 32;
     if (row_blocks > max_rb) row_blocks = max_rb;
     if (row_blocks < 1) row_blocks = 1;
@@ -916,7 +919,7 @@ int act_bwd(int kind, const float* x, const float* gy, float* gx, int64_t n, flo
     }
     if (rows <= 0 || cols <= 0 || rows * cols != n) return MLE_ERR_ARG;
     const bool vec = (cols % 4 == 0) && vec_ok(n, x, gy, gx);
-    const ColsumShape sh = colsum_shape(rows, cols, vec);
+    const ColsumShape sh = colsum_shape(rows, cols, vec, true);
     if (vec)
         launch_k(colsum_kernel<true, true, ASSIGN>, sh.grid, 256, 0, as_stream(stream), kind, x, gy, gx, bias_grad,
                  rows, cols, sh.rpb, 1.0f);
