@@ -933,6 +933,8 @@ def main():
                     help="attention implementation (mle_set_attention_path); default: the library's")
     ap.add_argument("--param-stream", type=int, default=None, choices=[0, 1],
                     help="weight/bias gradients on a second stream (mle_set_param_grad_stream); default: on")
+    ap.add_argument("--gemm-store-path", type=int, default=None, choices=[0, 1],
+                    help="assigned GEMM outputs through TMA bulk stores (0) or warp stores (1; the library default)")
     ap.add_argument("--bucket-mb", type=int, default=0,
                     help="data-parallel gradient bucket size in MiB (mle_session_enable_dp); 0: the library's "
                          "choice from the gradient total (mle_dp_auto_bucket_mb)")
@@ -955,6 +957,9 @@ def main():
     if args.attn_path is not None:
         from ml_engine_b200._lib import kernels
         kernels().call("mle_set_attention_path", {"auto": 0, "fused": 1, "tensor": 2}[args.attn_path])
+    if args.gemm_store_path is not None:
+        from ml_engine_b200._lib import kernels
+        kernels().call("mle_set_gemm_store_path", args.gemm_store_path)
     if args.param_stream is not None:
         from ml_engine_b200._lib import engine
         engine().call("mle_set_param_grad_stream", args.param_stream)
