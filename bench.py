@@ -738,7 +738,13 @@ def run_sweep(args):
         gbs = 32.0 * nparam / (ms * 1e-3) / 1e9   # g read (norm); w, g, m, v read; w, m, v written
         print(json.dumps({"sweep": "clip_adamw", "params": nparam, "tensors": nt, "ms": ms, "gbs": gbs,
                           "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
-        del params, views
+        fws = ops.clip_adam_workspace(views)   # the one-launch form the engine takes by default
+        ms = timed(lambda: ops.clip_adam(fws, lr=1e-3, max_norm=1.0, adamw=True, write_back_grad=False),
+                   10 if total <= 100_000_000 else 3)
+        gbs = 32.0 * nparam / (ms * 1e-3) / 1e9
+        print(json.dumps({"sweep": "clip_adamw_one_launch", "params": nparam, "tensors": nt, "ms": ms, "gbs": gbs,
+                          "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
+        del params, views, fws
         torch.cuda.empty_cache()
 
 
@@ -935,6 +941,9 @@ def main():
                     help="weight/bias gradients on a second stream (mle_set_param_grad_stream); default: on")
     ap.add_argument("--gemm-store-path", type=int, default=None, choices=[0, 1],
                     help="assigned GEMM outputs through TMA bulk stores (0) or warp stores (1; the library default)")
+    ap.add_argument("--fused-optimizer", type=int, default=None, choices=[0, 1],
+                    help="norm, clip and AdamW as one cooperative launch (1, the library default) or as the "
+                         "sum-of-squares, finalize and update launches (0) (mle_set_fused_optimizer)")
     ap.add_argument("--bucket-mb", type=int, default=0,
                     help="data-parallel gradient bucket size in MiB (mle_session_enable_dp); 0: the library's "
                          "choice from the gradient total (mle_dp_auto_bucket_mb)")
@@ -963,6 +972,9 @@ def main():
     if args.param_stream is not None:
         from ml_engine_b200._lib import engine
         engine().call("mle_set_param_grad_stream", args.param_stream)
+    if args.fused_optimizer is not None:
+        from ml_engine_b200._lib import engine
+        engine().call("mle_set_fused_optimizer", args.fused_optimizer)
     if args.sweep:
         run_sweep(args)
         return

@@ -119,6 +119,22 @@ int mle_get_param_grad_stream(void);
 int mle_set_grad_first_write(int enable);
 int mle_get_grad_first_write(void);
 
+/* One launch for the optimizer: when ParameterUpdate covers exactly the
+ * parameters clip_grad_norm collected (each once, one learning rate and one
+ * rule), the gradient norm, the clip, Adam/AdamW and the step counters run
+ * as the single cooperative kernel of mle_clip_adam_run instead of the
+ * sum-of-squares, finalize and update launches; clip_grad_norm then only
+ * records max_norm, and the norm is taken of the gradients as they are when
+ * the update runs.  The norm's summation order differs (per-block partials
+ * in block order), so the clip coefficient agrees to rounding; the
+ * per-element update is the same arithmetic.  The tensor table is copied to
+ * the device by the first such update outside stream capture; an update
+ * captured before that takes the separate launches.  1 (default) on, 0 the
+ * separate launches.  Process-wide; takes effect at the next
+ * clip_grad_norm. */
+int mle_set_fused_optimizer(int enable);
+int mle_get_fused_optimizer(void);
+
 /* Captures each phase of the step (the numbering of mle_session_phase,
  * device resident: no upload, no loss download) as its own CUDA graph, so a
  * caller can time phases on the device; mle_session_phase_replay(s, ph)

@@ -676,6 +676,41 @@ int mle_adam_update(const mle_param_view* params, int n_tensors, const double* c
                     float pre_scale, float lr, int adamw, int write_back_grad,
                     mle_stream_t stream);
 
+/* Norm, clip and update as ONE launch.  Replaces, together, the per-tensor
+ * SumSquared launches, Sqrt_Scale, the SP launches and the AdamWUpdate loop
+ * of GraphOperations::accumulate / clipNorm / ParameterUpdate
+ * (Engine/engine.cu:283-302, 3362-3384; Engine/kernels.cu:1486-1534,
+ * 1763-1773).  A cooperative kernel (every block resident) gives each block
+ * a contiguous range of 4096-element chunks over all tensors; each block
+ * sums g^2 over its range into the workspace, passes a grid barrier, adds
+ * all partials in block order (times pre_scale^2) and forms
+ * c = max(||g||, max_norm)/max_norm (max_norm <= 0: no clip and no barrier;
+ * a NaN norm stays NaN); it then walks its range again, backwards, applying
+ * g' = g * pre_scale / (float)c and the same per-element Adam/AdamW
+ * arithmetic as mle_adam_update.  The last block to finish adds 1 to every
+ * tensor's t.  g' is written back when write_back_grad != 0.
+ *
+ * Workspace: mle_clip_adam_ws_bytes(n) bytes of device memory, 16-byte
+ * aligned, owned by the caller.  mle_clip_adam_prepare copies the tensor
+ * table and zeroed counters into it (stream ordered; MLE_ERR_UNSUPPORTED
+ * while the stream is being captured, since the table is a host array);
+ * every later run reuses it with no further copy or memset, so runs of a
+ * prepared workspace may be replayed inside a CUDA graph.  Runs on one
+ * workspace must not overlap on the device.  The grid barrier waits at most
+ * two seconds; a wait that gives up sets a status word and ends the kernel
+ * early (the update then incomplete), and every later run returns at once
+ * until the workspace is prepared again.  mle_clip_adam_status reads the
+ * word (synchronizing the stream) and returns MLE_ERR_TIMEOUT when it is
+ * set.  The clip coefficient's summation order differs from
+ * mle_grad_sumsq's (per-block partials instead of atomics), so it agrees to
+ * rounding; with no clip the result is bit-identical to mle_adam_update. */
+int64_t mle_clip_adam_ws_bytes(int n_tensors);
+int mle_clip_adam_prepare(const mle_param_view* params, int n_tensors, void* ws, int64_t ws_bytes,
+                          mle_stream_t stream);
+int mle_clip_adam_run(void* ws, float max_norm, float pre_scale, float lr, int adamw, int write_back_grad,
+                      mle_stream_t stream);
+int mle_clip_adam_status(void* ws, int* out_status, mle_stream_t stream);
+
 /* No counterpart in the reference: a gradient-norm clip that needs no
  * workspace from the caller.  It computes what mle_grad_sumsq (scale 1),
  * mle_clip_finalize and mle_clip_apply compute together -- g /= c with

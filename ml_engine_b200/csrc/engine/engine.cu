@@ -567,7 +567,25 @@ void GraphOperations::collect_params(std::vector<AdamParameter*>& out) {
     out = c.sumsq;
 }
 
+static bool g_fused_optimizer = true;
+
+extern "C" int mle_set_fused_optimizer(int enable) {
+    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    g_fused_optimizer = enable != 0;
+    return MLE_OK;
+}
+
+extern "C" int mle_get_fused_optimizer(void) { return g_fused_optimizer ? 1 : 0; }
+
 void GraphOperations::clip_grad_norm(const float max_norm) {
+    if (g_fused_optimizer) {
+        // the norm is taken by the next ParameterUpdate's single launch, or
+        // by flush_deferred_clip() where that update cannot take it
+        clip_max_norm_ = max_norm;
+        clip_deferred_ = true;
+        clip_pending_ = true;
+        return;
+    }
     double* ws = clip_workspace();
     check_cuda(cudaMemsetAsync(ws, 0, sizeof(double), g_stream), "clip workspace");
     std::vector<AdamParameter*> ps;
@@ -577,7 +595,61 @@ void GraphOperations::clip_grad_norm(const float max_norm) {
     clip_pending_ = true;
 }
 
+void GraphOperations::flush_deferred_clip() {
+    if (!clip_deferred_) return;
+    clip_deferred_ = false;
+    double* ws = clip_workspace();
+    check_cuda(cudaMemsetAsync(ws, 0, sizeof(double), g_stream), "clip workspace");
+    std::vector<AdamParameter*> ps;
+    collect_params(ps);
+    for (auto& r : rounds_of(ps)) launch_sumsq(r, ws, (double)grad_prescale_);
+    check(mle_clip_finalize(ws, (double)clip_max_norm_, st()), "clip finalize");
+}
+
+// One launch for the norm, the clip, the update and the step counters, when
+// the update covers exactly the clipped parameters, each once, with one
+// learning rate and rule.  False (nothing launched) when it does not apply.
+bool GraphOperations::fused_update(const std::vector<AdamParameter*>& ps, float lr, bool adamw) {
+    if (!g_fused_optimizer || ps.empty()) return false;
+    std::unordered_set<AdamParameter*> seen(ps.begin(), ps.end());
+    if (seen.size() != ps.size()) return false;
+    if (clip_deferred_) {
+        std::vector<AdamParameter*> cl;
+        collect_params(cl);
+        if (cl.size() != ps.size()) return false;
+        for (auto* p : cl)
+            if (!seen.count(p)) return false;
+    } else if (clip_pending_) {
+        return false;  // a coefficient computed by the separate launches
+    }
+    std::vector<mle_param_view> v;
+    v.reserve(ps.size());
+    for (auto* p : ps) v.push_back(view_of(p));
+    const bool same = v.size() == fused_views_.size() &&
+                      memcmp(v.data(), fused_views_.data(), v.size() * sizeof(mle_param_view)) == 0;
+    if (!same) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        check_cuda(cudaStreamIsCapturing(g_stream, &cap), "capture status");
+        if (cap != cudaStreamCaptureStatusNone) return false;  // the table is copied from the host
+        const int64_t need = mle_clip_adam_ws_bytes((int)v.size());
+        if (need > fused_ws_bytes_) {
+            fused_ws_ = arena_alloc_bytes(ARENA_WS, need, "optimizer table");
+            fused_ws_bytes_ = need;
+        }
+        check(mle_clip_adam_prepare(v.data(), (int)v.size(), fused_ws_, fused_ws_bytes_, st()), "optimizer table");
+        fused_views_ = v;
+    }
+    const float max_norm = clip_deferred_ ? clip_max_norm_ : 0.0f;
+    const bool wb = clip_deferred_ || grad_prescale_ != 1.0f;
+    check(mle_clip_adam_run(fused_ws_, max_norm, grad_prescale_, lr, adamw ? 1 : 0, wb ? 1 : 0, st()),
+          "norm + clip + AdamWUpdate (one launch)");
+    clip_deferred_ = false;
+    clip_pending_ = false;
+    return true;
+}
+
 void GraphOperations::apply_clip() {
+    flush_deferred_clip();
     if (!clip_pending_) return;
     clipNorm(clip_workspace());
     clip_pending_ = false;
@@ -598,6 +670,14 @@ void GraphOperations::ParameterUpdate(const graph& X, const bool show, const flo
     // group by (lr, adamw); repeated parameters go to later rounds
     std::map<std::pair<float, bool>, std::vector<AdamParameter*>> groups;
     for (auto& u : c.update) groups[{u.lr, u.adamw}].push_back(u.p);
+    if (groups.size() == 1 && fused_update(groups.begin()->second, groups.begin()->first.first,
+                                           groups.begin()->first.second)) {
+        if (show)
+            for (auto& node : nodes)
+                if (node->updateParams) print_head(node->output, node->total, node->op_name);
+        return;
+    }
+    flush_deferred_clip();
     const double* clip = clip_pending_ ? clip_workspace() : nullptr;
     for (auto& g : groups) {
         for (auto& r : rounds_of(g.second)) {

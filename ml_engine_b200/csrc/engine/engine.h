@@ -299,6 +299,15 @@ class GraphOperations {
    private:
     float grad_prescale_ = 1.0f;
     bool clip_pending_ = false;
+    // clip_grad_norm left to the update's single launch (norm, clip,
+    // Adam/AdamW, step counters), whose tensor table lives in fused_ws_
+    bool clip_deferred_ = false;
+    float clip_max_norm_ = 0.0f;
+    void* fused_ws_ = nullptr;
+    int64_t fused_ws_bytes_ = 0;
+    std::vector<mle_param_view> fused_views_;
+    void flush_deferred_clip();
+    bool fused_update(const std::vector<AdamParameter*>& ps, float lr, bool adamw);
     void collect_params(std::vector<AdamParameter*>& out);
 };
 

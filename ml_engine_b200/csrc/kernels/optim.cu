@@ -17,7 +17,11 @@
 // and the clip divides by (float)norm as SP does.
 #include <math.h>
 
+#include <algorithm>
+#include <cstddef>
+#include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 
@@ -210,6 +214,305 @@ int64_t build_table(TensorTable& tt, const mle_param_view* params, int first, in
     return blocks;
 }
 
+// ---------------------- norm + clip + update in one launch ----------------------
+// A cooperative grid (every block resident) splits the kFusedUnit-element
+// units of all tensors into one contiguous range per block (blocks beyond
+// the unit count return at once) and walks it twice: forwards for the
+// per-block sum of squares, then, after one grid barrier, backwards for the
+// update, so that the gradients the first walk read last are still in L2
+// when the second walk starts.  After the barrier every block adds the
+// partials in block order (the same coefficient in every block, and the same
+// from run to run for a given grid).  The last block to finish the update (a
+// counter, no waiting) increments the step counters and re-arms the counters
+// for the next launch, so a run needs no memset.  The tensor table sits in
+// the caller's device workspace: the count of tensors is not bounded by the
+// kernel's parameter space.  A unit is two float4 of each array per thread,
+// so that small models still spread over many SMs.
+constexpr int kFusedUnit = kThreads * 8;  // 2048 elements
+constexpr int kFusedMaxBlocks = 148 * 8;
+constexpr int kFusedMinBlocksPerSM = 3;   // <= 80 registers a thread
+
+struct FusedWs {
+    int n;           // tensors      } one 16-byte load at kernel entry
+    int status;      // 1: the barrier timed out; later launches return at once
+    int64_t units;   // kFusedUnit-element units over all tensors
+    unsigned bar;    // arrivals at the grid barrier of the current launch
+    unsigned done;   // blocks that finished the current launch
+    double partial[kFusedMaxBlocks];
+};
+static_assert(offsetof(FusedWs, n) == 0 && offsetof(FusedWs, status) == 4 && offsetof(FusedWs, units) == 8,
+              "header read as one int4");
+
+__host__ __device__ inline size_t fused_table_offset() { return (sizeof(FusedWs) + 255) & ~size_t(255); }
+__host__ __device__ inline int64_t* fused_unit_start(void* ws) {
+    return reinterpret_cast<int64_t*>(static_cast<char*>(ws) + fused_table_offset());
+}
+__host__ __device__ inline size_t fused_views_offset(int n) {
+    return (fused_table_offset() + sizeof(int64_t) * (size_t)(n + 1) + 255) & ~size_t(255);
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Every active block arrives once (a reduction, no round trip) and polls
+// the counter.  True when all `active` arrivals came within two seconds and
+// no block gave up; otherwise the status word is set and the caller returns.
+// The counter is re-armed by the launch's last block.
+__device__ bool fused_grid_barrier(FusedWs* ws, unsigned active) {
+    __shared__ int ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(&ws->bar, 1u);
+        volatile unsigned* bar = &ws->bar;
+        volatile int* status = &ws->status;
+        const uint64_t t0 = global_ns();
+        ok = 1;
+        for (;;) {
+            if (*bar >= active) break;
+            if (*status) {
+                ok = 0;
+                break;
+            }
+            if (global_ns() - t0 > 2000000000ull) {
+                atomicOr(&ws->status, 1);
+                ok = 0;
+                break;
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+__device__ __forceinline__ int fused_find(const int64_t* us, int n, int64_t c) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (us[mid] <= c) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+template <bool ADAMW>
+__device__ __forceinline__ void bias_corrections(const mle_param_view& P, double* bc) {
+    const int t = *P.t;
+    if (ADAMW) {
+        bc[0] = 1.0 - pow(P.b1, t);  // pow(float, int) as in AdamWUpdate
+        bc[1] = 1.0 - pow(P.b2, t);
+    } else {
+        bc[0] = 1.0 - powf(P.b1, (float)t);
+        bc[1] = 1.0 - powf(P.b2, (float)t);
+    }
+}
+
+__device__ __forceinline__ double sumsq4(double acc, const float4& x) {
+    acc += (double)x.x * (double)x.x;
+    acc += (double)x.y * (double)x.y;
+    acc += (double)x.z * (double)x.z;
+    acc += (double)x.w * (double)x.w;
+    return acc;
+}
+
+// g' = g * pre_scale / clip, then the element update, for four elements
+template <bool ADAMW, bool CLIP, bool PRESCALE>
+__device__ __forceinline__ void adam1(float& g, float& w, float& m, float& v, const mle_param_view& P,
+                                      float pre_scale, float clip_f, float lr, double bc1, double bc2) {
+    if (PRESCALE) g = g * pre_scale;
+    if (CLIP) g /= clip_f;
+    adam_elem<ADAMW>(w, m, v, g, P.b1, P.b2, P.eps, P.weight_decay, lr, bc1, bc2);
+}
+
+template <bool ADAMW, bool CLIP, bool PRESCALE>
+__device__ __forceinline__ void adam4(float4& g4, float4& w4, float4& m4, float4& v4, const mle_param_view& P,
+                                      float pre_scale, float clip_f, float lr, double bc1, double bc2) {
+    adam1<ADAMW, CLIP, PRESCALE>(g4.x, w4.x, m4.x, v4.x, P, pre_scale, clip_f, lr, bc1, bc2);
+    adam1<ADAMW, CLIP, PRESCALE>(g4.y, w4.y, m4.y, v4.y, P, pre_scale, clip_f, lr, bc1, bc2);
+    adam1<ADAMW, CLIP, PRESCALE>(g4.z, w4.z, m4.z, v4.z, P, pre_scale, clip_f, lr, bc1, bc2);
+    adam1<ADAMW, CLIP, PRESCALE>(g4.w, w4.w, m4.w, v4.w, P, pre_scale, clip_f, lr, bc1, bc2);
+}
+
+template <bool ADAMW, bool CLIP, bool PRESCALE>
+__global__ void __launch_bounds__(kThreads, kFusedMinBlocksPerSM)
+    fused_clip_adam_kernel(void* wsv, float pre_scale, float lr, double max_norm, int write_back) {
+    FusedWs* ws = static_cast<FusedWs*>(wsv);
+    __shared__ double scratch[32];
+    __shared__ double bc[2];
+    __shared__ int last;
+    const int4 hdr = __ldcg(static_cast<const int4*>(wsv));  // n, status, units
+    if (hdr.y) return;  // a failed launch: nothing runs until the table is prepared again
+    const int n = hdr.x;
+    const int64_t units = (int64_t)(((uint64_t)(unsigned)hdr.w << 32) | (uint64_t)(unsigned)hdr.z);
+    // blocks beyond the unit count have nothing to do and take no part
+    const unsigned active = units < (int64_t)gridDim.x ? (unsigned)units : gridDim.x;
+    if (blockIdx.x >= active) return;
+    const int64_t* us = fused_unit_start(wsv);
+    const mle_param_view* views =
+        reinterpret_cast<const mle_param_view*>(static_cast<char*>(wsv) + fused_views_offset(n));
+    const int64_t per = units / active, rem = units % active;
+    const int64_t c0 = (int64_t)blockIdx.x * per + (blockIdx.x < rem ? blockIdx.x : rem);
+    const int64_t c1 = c0 + per + (blockIdx.x < rem ? 1 : 0);  // c1 > c0
+    const int tid4 = threadIdx.x * 4;
+    // The first tensor the update visits: its bias corrections are taken by
+    // a thread of the second warp while the first walk runs.  The table is
+    // read only where a walk crosses into another tensor; the data loads
+    // bypass L1 so that the table stays there.
+    int ti = fused_find(us, n, c1 - 1);
+    if (threadIdx.x == 32) bias_corrections<ADAMW>(views[ti], bc);
+    float clip_f = 1.0f;
+    if (CLIP) {
+        double acc = 0.0;
+        int tf = fused_find(us, n, c0);
+        int64_t t_begin = us[tf], t_end = us[tf + 1];
+        const float* g = views[tf].g;
+        int64_t len = views[tf].n;
+        for (int64_t c = c0; c < c1;) {
+            if (c >= t_end) {
+                do {
+                    ++tf;
+                    t_begin = t_end;
+                    t_end = us[tf + 1];
+                } while (c >= t_end);
+                g = views[tf].g;
+                len = views[tf].n;
+            }
+            const int64_t begin = (c - t_begin) * kFusedUnit;
+            const int64_t left = len - begin;
+            if (left >= 2 * kFusedUnit && c + 1 < c1 && aligned16(g)) {
+                // two whole units of one tensor: four float4 in flight
+                float4 x[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    x[j] = __ldcg(reinterpret_cast<const float4*>(g + begin + j * kThreads * 4 + tid4));
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc = sumsq4(acc, x[j]);
+                c += 2;
+                continue;
+            }
+            const int64_t end = left < kFusedUnit ? len : begin + kFusedUnit;
+            if (aligned16(g)) {
+                const int64_t ve = begin + ((end - begin) & ~int64_t(3));
+                for (int64_t i = begin + tid4; i < ve; i += kThreads * 4)
+                    acc = sumsq4(acc, __ldcg(reinterpret_cast<const float4*>(g + i)));
+                for (int64_t i = ve + threadIdx.x; i < end; i += kThreads) acc += (double)g[i] * (double)g[i];
+            } else {
+                for (int64_t i = begin + threadIdx.x; i < end; i += kThreads) acc += (double)g[i] * (double)g[i];
+            }
+            ++c;
+        }
+        acc = block_sum(acc, scratch);
+        if (threadIdx.x == 0) ws->partial[blockIdx.x] = acc;
+        if (!fused_grid_barrier(ws, active)) return;
+        double tot = 0.0;
+        for (int i = threadIdx.x; i < (int)active; i += kThreads) tot += __ldcg(&ws->partial[i]);
+        tot = block_sum(tot, scratch) * ((double)pre_scale * (double)pre_scale);
+        // Sqrt_Scale with a max norm; a NaN sum stays NaN
+        double coef = tot;
+        if (tot == tot) {
+            const double curr = sqrt(tot);
+            coef = (curr > max_norm) ? curr / max_norm : 1.0;
+        }
+        clip_f = (float)coef;
+    } else {
+        __syncthreads();  // bc of the first tensor
+    }
+    const bool wb = (CLIP || PRESCALE) && write_back;
+    mle_param_view P = views[ti];
+    int64_t t_begin = us[ti];
+    double bc1 = bc[0], bc2 = bc[1];
+    for (int64_t c = c1 - 1; c >= c0; --c) {
+        if (c < t_begin) {  // block-uniform: the next tensor and its bias corrections
+            do {
+                --ti;
+                t_begin = us[ti];
+            } while (c < t_begin);
+            P = views[ti];
+            __syncthreads();
+            if (threadIdx.x == 0) bias_corrections<ADAMW>(P, bc);
+            __syncthreads();
+            bc1 = bc[0];
+            bc2 = bc[1];
+        }
+        const int64_t begin = (c - t_begin) * kFusedUnit;
+        const int64_t end = begin + kFusedUnit < P.n ? begin + kFusedUnit : P.n;
+        float* __restrict__ W = P.w;
+        float* __restrict__ G = P.g;
+        float* __restrict__ M = P.m;
+        float* __restrict__ V = P.v;
+        const bool vec = aligned16(W) && aligned16(G) && aligned16(M) && aligned16(V);
+        if (vec && end - begin == kFusedUnit) {
+            // a whole unit: every load of the thread in flight before the arithmetic
+            float4 g4[2], w4[2], m4[2], v4[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int64_t i = begin + u * kThreads * 4 + tid4;
+                g4[u] = __ldcg(reinterpret_cast<const float4*>(G + i));
+                w4[u] = __ldcg(reinterpret_cast<const float4*>(W + i));
+                m4[u] = __ldcg(reinterpret_cast<const float4*>(M + i));
+                v4[u] = __ldcg(reinterpret_cast<const float4*>(V + i));
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int64_t i = begin + u * kThreads * 4 + tid4;
+                adam4<ADAMW, CLIP, PRESCALE>(g4[u], w4[u], m4[u], v4[u], P, pre_scale, clip_f, lr, bc1, bc2);
+                *reinterpret_cast<float4*>(W + i) = w4[u];
+                *reinterpret_cast<float4*>(M + i) = m4[u];
+                *reinterpret_cast<float4*>(V + i) = v4[u];
+                if (wb) *reinterpret_cast<float4*>(G + i) = g4[u];
+            }
+            continue;
+        }
+        int64_t tail = begin;
+        if (vec) {
+            const int64_t ve = begin + ((end - begin) & ~int64_t(3));
+            for (int64_t i = begin + tid4; i < ve; i += kThreads * 4) {
+                float4 g4 = __ldcg(reinterpret_cast<const float4*>(G + i));
+                float4 w4 = __ldcg(reinterpret_cast<const float4*>(W + i));
+                float4 m4 = __ldcg(reinterpret_cast<const float4*>(M + i));
+                float4 v4 = __ldcg(reinterpret_cast<const float4*>(V + i));
+                adam4<ADAMW, CLIP, PRESCALE>(g4, w4, m4, v4, P, pre_scale, clip_f, lr, bc1, bc2);
+                *reinterpret_cast<float4*>(W + i) = w4;
+                *reinterpret_cast<float4*>(M + i) = m4;
+                *reinterpret_cast<float4*>(V + i) = v4;
+                if (wb) *reinterpret_cast<float4*>(G + i) = g4;
+            }
+            tail = ve;
+        }
+        for (int64_t i = tail + threadIdx.x; i < end; i += kThreads) {
+            float g = G[i];
+            if (PRESCALE) g = g * pre_scale;
+            if (CLIP) g /= clip_f;
+            float w = W[i], m = M[i], v = V[i];
+            adam_elem<ADAMW>(w, m, v, g, P.b1, P.b2, P.eps, P.weight_decay, lr, bc1, bc2);
+            W[i] = w;
+            M[i] = m;
+            V[i] = v;
+            if (wb) G[i] = g;
+        }
+    }
+    // The last block to get here increments every step counter (every block
+    // read the counters it needed before arriving) and re-arms the counters.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(&ws->done, 1u) == active - 1;
+        if (last) __threadfence();
+    }
+    __syncthreads();
+    if (last) {
+        for (int i = threadIdx.x; i < n; i += kThreads) *views[i].t += 1;
+        if (threadIdx.x == 0) {
+            ws->bar = 0;
+            ws->done = 0;
+        }
+    }
+}
+
 // ------------------------- clip without a caller workspace -------------------------
 // Scratch of mle_clip_grad_norm_static: slots [0, blocks) hold the per-block
 // sums of squares of one call, slot MLE_CLIP_STATIC_MAX_BLOCKS the clip
@@ -320,6 +623,100 @@ int mle_clip_apply(const mle_param_view* params, int n_tensors, const double* no
         if (s) return s;
     }
     return MLE_OK;
+}
+
+int64_t mle_clip_adam_ws_bytes(int n_tensors) {
+    if (n_tensors < 0) return -1;
+    return (int64_t)(fused_views_offset(n_tensors) + sizeof(mle_param_view) * (size_t)n_tensors);
+}
+
+int mle_clip_adam_prepare(const mle_param_view* params, int n_tensors, void* ws, int64_t ws_bytes,
+                          mle_stream_t stream) {
+    if (n_tensors <= 0 || !params || !ws || ws_bytes < mle_clip_adam_ws_bytes(n_tensors)) return MLE_ERR_ARG;
+    if (!aligned16(ws)) return MLE_ERR_ARG;
+    cudaStream_t st = as_stream(stream);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return launch_status();
+    if (cap != cudaStreamCaptureStatusNone) return MLE_ERR_UNSUPPORTED;  // a copy of a host table
+    std::vector<FusedWs> hbuf((size_t)(mle_clip_adam_ws_bytes(n_tensors) + sizeof(FusedWs) - 1) / sizeof(FusedWs));
+    memset(static_cast<void*>(hbuf.data()), 0, hbuf.size() * sizeof(FusedWs));
+    char* buf = reinterpret_cast<char*>(hbuf.data());
+    FusedWs* hdr = hbuf.data();
+    int64_t* us = fused_unit_start(buf);
+    mle_param_view* views = reinterpret_cast<mle_param_view*>(buf + fused_views_offset(n_tensors));
+    int64_t units = 0;
+    for (int i = 0; i < n_tensors; ++i) {
+        const mle_param_view& p = params[i];
+        if (p.n < 0 || !p.t || (p.n > 0 && (!p.w || !p.g || !p.m || !p.v))) return MLE_ERR_ARG;
+        views[i] = p;
+        us[i] = units;
+        units += p.n > 0 ? (p.n + kFusedUnit - 1) / kFusedUnit : 1;  // an empty tensor owns one idle unit
+    }
+    us[n_tensors] = units;
+    hdr->n = n_tensors;
+    hdr->units = units;  // status and the counters start at zero
+    // pageable source: the runtime has taken its copy of `buf` when this returns
+    if (cudaMemcpyAsync(ws, buf, (size_t)mle_clip_adam_ws_bytes(n_tensors), cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return launch_status();
+    return launch_status();
+}
+
+int mle_clip_adam_run(void* ws, float max_norm, float pre_scale, float lr, int adamw, int write_back_grad,
+                      mle_stream_t stream) {
+    if (!ws || !aligned16(ws) || (adamw != 0 && adamw != 1))
+        return MLE_ERR_ARG;
+    cudaStream_t st = as_stream(stream);
+    const bool clip = max_norm > 0.0f;
+    const bool pres = pre_scale != 1.0f;
+    auto go = [&](auto kern) -> int {
+        static int grid = 0;  // one per instantiation: resident blocks on every SM
+        if (grid == 0) {
+            int per_sm = 0, dev = 0, sms = 0;
+            if (cudaGetDevice(&dev) != cudaSuccess ||
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0) != cudaSuccess)
+                return launch_status();
+            grid = std::min(per_sm * sms, kFusedMaxBlocks);
+            if (grid <= 0) return MLE_ERR_UNSUPPORTED;
+        }
+        // the counters were zeroed by prepare and are re-armed by each launch's last block
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kern, ws, pre_scale, lr, (double)max_norm, write_back_grad) != cudaSuccess)
+            return launch_status();
+        return launch_status();
+    };
+#define MLE_FCA(A, C, P) \
+    if (adamw == A && clip == C && pres == P) return go(fused_clip_adam_kernel<A, C, P>);
+    MLE_FCA(1, true, true)
+    MLE_FCA(1, true, false)
+    MLE_FCA(1, false, true)
+    MLE_FCA(1, false, false)
+    MLE_FCA(0, true, true)
+    MLE_FCA(0, true, false)
+    MLE_FCA(0, false, true)
+    MLE_FCA(0, false, false)
+#undef MLE_FCA
+    return MLE_ERR_ARG;
+}
+
+int mle_clip_adam_status(void* ws, int* out_status, mle_stream_t stream) {
+    if (!ws || !out_status) return MLE_ERR_ARG;
+    FusedWs* w = static_cast<FusedWs*>(ws);
+    int v = 0;
+    cudaStream_t st = as_stream(stream);
+    if (cudaMemcpyAsync(&v, &w->status, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return launch_status();
+    *out_status = v;
+    return v ? MLE_ERR_TIMEOUT : MLE_OK;
 }
 
 int mle_adam_update(const mle_param_view* params, int n_tensors, const double* clip_ws, float pre_scale, float lr,

@@ -323,6 +323,32 @@ def adam_update(params, lr, adamw=True, clip_ws=None, pre_scale=1.0, write_back_
           int(adamw), int(write_back_grad), _s())
 
 
+def clip_adam_workspace(params):
+    """Device workspace of the one-launch norm + clip + update for this
+    parameter list, its tensor table filled (stream ordered)."""
+    views = _views(params)
+    nbytes = kernels().mle_clip_adam_ws_bytes(len(views))
+    if nbytes <= 0:
+        raise MLEError("mle_clip_adam_ws_bytes: no tensors")
+    ws = torch.zeros((nbytes + 7) // 8, dtype=torch.float64, device="cuda")
+    _call("mle_clip_adam_prepare", ctypes.cast(views, ctypes.c_void_p), len(views), _p(ws), ws.numel() * 8, _s())
+    return ws
+
+
+def clip_adam(ws, lr, max_norm=1.0, pre_scale=1.0, adamw=True, write_back_grad=True):
+    """One launch: the gradient norm over every tensor of the workspace's
+    table, the Sqrt_Scale clip with max_norm (<= 0: none), Adam/AdamW and
+    t += 1."""
+    _call("mle_clip_adam_run", _p(ws), max_norm, pre_scale, lr, int(adamw), int(write_back_grad), _s())
+
+
+def clip_adam_status(ws):
+    """The workspace's barrier status (0: every barrier met in time)."""
+    out = ctypes.c_int(0)
+    kernels().mle_clip_adam_status(_p(ws), ctypes.addressof(out), _s())
+    return out.value
+
+
 def watchdog():
     flag = ctypes.c_int(0)
     _call("mle_watchdog_read", ctypes.addressof(flag), _s())

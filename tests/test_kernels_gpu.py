@@ -757,6 +757,77 @@ def test_clip_adam_multi_tensor(cuda, ops, orc, rng, adamw, clip):
         assert int(H(p["t"])[0]) == 4
 
 
+def _clone_params(ps):
+    return [{k: x.clone() for k, x in p.items()} for p in ps]
+
+
+@pytest.mark.parametrize("adamw", [True, False])
+@pytest.mark.parametrize("clip", [True, False])
+@pytest.mark.parametrize("pre_scale", [1.0, 0.25])
+def test_fused_clip_adam_matches_separate_launches(cuda, ops, orc, rng, adamw, clip, pre_scale):
+    """The one-launch norm + clip + update (cooperative kernel, table in
+    device memory) against the sum-of-squares, finalize and update launches
+    over 130 tensors (more than one launch table of the separate path), two
+    steps through the same workspace.  Without a clip the arithmetic is the
+    same element by element: bit-identical.  With one, the norm's partial
+    sums are added in another order, so the coefficient agrees to rounding,
+    and the first step is also checked against the oracle."""
+    sizes = [784 * 256, 256, 2560, 10, 1, 5000, 4096 * 3 + 1] + [int(x) for x in rng.integers(1, 3000, 123)]
+    if clip:
+        sizes[0] = 1 << 20  # a norm well above max_norm
+    ps, host = _make_params(rng, sizes, cuda)
+    ref = _clone_params(ps)
+    ws = ops.clip_adam_workspace(ops.param_views(ps))
+    max_norm = 1.0 if clip else 0.0
+    for step in range(2):
+        ops.clip_adam(ws, lr=1e-3, max_norm=max_norm, pre_scale=pre_scale, adamw=adamw)
+        cw = torch.zeros(1, dtype=torch.float64, device=cuda)
+        if clip:
+            ops.grad_sumsq(ref, cw, scale=pre_scale)
+            ops.clip_finalize(cw, max_norm)
+        ops.adam_update(ref, lr=1e-3, adamw=adamw, clip_ws=cw if clip else None, pre_scale=pre_scale)
+        if step == 0 and clip:
+            acc = np.zeros(1, np.float64)
+            for h in host:
+                orc.sumsq(acc, (h["g"] * np.float32(pre_scale)).astype(np.float32))
+            orc.clip_finalize(acc)
+            for p, h in list(zip(ps, host))[:9]:
+                g = (h["g"] * np.float32(pre_scale)).astype(np.float32)
+                orc.clip_apply(g, acc)
+                w, m, v = h["w"].copy(), h["m"].copy(), h["v"].copy()
+                orc.adam(w, g, m, v, 3, 1e-3, adamw)
+                for k, want in (("g", g), ("w", w), ("m", m), ("v", v)):
+                    assert rel_err(H(p[k]), want) <= RTOL_EXACT, k
+    assert ops.clip_adam_status(ws) == 0
+    for p, r in zip(ps, ref):
+        assert int(H(p["t"])[0]) == 5 and int(H(r["t"])[0]) == 5
+        for k in ("w", "m", "v", "g"):
+            if not clip:
+                assert torch.equal(p[k], r[k]), k
+            else:
+                assert rel_err(H(p[k]), H(r[k])) <= RTOL_EXACT, k
+
+
+def test_fused_clip_adam_nan_norm_and_errors(cuda, ops, rng):
+    """A NaN in one gradient makes the coefficient NaN and every tensor's
+    weights NaN, as with the separate launches; a short workspace and a
+    null one are refused."""
+    from ml_engine_b200 import MLEError
+    ps, _ = _make_params(rng, [1000, 33, 4097], cuda)
+    ps[1]["g"][5] = float("nan")
+    ws = ops.clip_adam_workspace(ps)
+    ops.clip_adam(ws, lr=1e-3, max_norm=1.0)
+    assert ops.clip_adam_status(ws) == 0
+    for p in ps:
+        assert torch.isnan(p["w"]).all()
+    views = ops.param_views(ps)
+    st = torch.cuda.current_stream().cuda_stream
+    with pytest.raises(MLEError):
+        ops.kernels().call("mle_clip_adam_prepare", ctypes.cast(views, ctypes.c_void_p), 3, ws.data_ptr(), 64, st)
+    with pytest.raises(MLEError):
+        ops.kernels().call("mle_clip_adam_run", None, 1.0, 1.0, 1e-3, 1, 1, st)
+
+
 def test_clip_apply_and_nan(cuda, ops, orc, rng):
     ps, host = _make_params(rng, [1000, 33], cuda)
     ws = torch.zeros(1, dtype=torch.float64, device=cuda)

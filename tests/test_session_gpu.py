@@ -414,3 +414,49 @@ def test_first_write_assign_matches_cleared_gradients(cuda, rng):
         # the query bias's exact gradient is zero (column softmax): no relative scale
         floor = np.linalg.norm(gb[i] - ga[i]) <= 1e-7 * gnorm
         assert norm_err(gb[i], ga[i]) <= 1e-4 or floor, (a.param_names[i], norm_err(gb[i], ga[i]))
+
+
+def test_fused_optimizer_matches_separate_launches(cuda, rng):
+    """The single cooperative norm + clip + AdamW launch that ParameterUpdate
+    takes by default, against the sum-of-squares, finalize and update
+    launches, over an eager step and two graph replays: the same losses,
+    clipped gradients, moments and step counters, and fewer kernel nodes in
+    the captured step.  The learning rate is 0 so both runs see the same
+    weights; their gradients then differ only by the backward's reordered
+    sums, and the clip coefficient by the norm's summation order."""
+    import ctypes
+    from ml_engine_b200._lib import engine
+    kw = dict(config=2, batch=16, seq_len=256, d_model=512, heads=8, ffn=2048, layers=1, vocab=512, seed=5, lr=0.0)
+    lib = engine()
+    old = lib.mle_get_fused_optimizer()
+    tokens = rng.integers(0, 512, 16 * 256).astype(np.int32)
+    targets = rng.integers(0, 512, 16 * 256).astype(np.int32)
+    runs = {}
+    try:
+        for mode in (0, 1):
+            lib.call("mle_set_fused_optimizer", mode)
+            s = _session(**kw)
+            s.inputs["tokens"][:] = tokens
+            s.inputs["targets"][:] = targets
+            losses = [s.step()]
+            s.capture()
+            losses += [s.step(), s.step()]
+            kk, mm, cc = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+            s._lib.call("mle_session_graph_counts", s._h, ctypes.addressof(kk), ctypes.addressof(mm),
+                        ctypes.addressof(cc))
+            state = [[s.read_param(i, w) for w in (1, 2, 3)] for i in range(len(s.param_names))]
+            steps = [s.param_step(i) for i in range(len(s.param_names))]
+            runs[mode] = (s, losses, state, steps, kk.value)
+    finally:
+        lib.call("mle_set_fused_optimizer", old)
+    (a, la, sa, ta, ka), (b, lb, sb, tb, kb) = runs[0], runs[1]
+    assert ta == tb
+    assert kb < ka, (ka, kb)
+    for x, y in zip(la + lb, la[:1] * 6):
+        assert abs(x - y) <= 1e-5 * abs(y), (la, lb)
+    for which in range(3):
+        gnorm = np.sqrt(sum(float(np.sum(np.asarray(st[which], np.float64) ** 2)) for st in sa))
+        for i in range(len(a.param_names)):
+            x, y = sb[i][which], sa[i][which]
+            floor = np.linalg.norm(x - y) <= 1e-7 * gnorm
+            assert norm_err(x, y) <= 1e-4 or floor, (a.param_names[i], which, norm_err(x, y))
