@@ -664,7 +664,8 @@ def run_sweep(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps
 
-    for n in (512, 1024, 2048, 4096, 8192):
+    legs = set(args.sweep_only.split(",")) if args.sweep_only else {"linear", "colsum", "layernorm", "optimizer"}
+    for n in ((512, 1024, 2048, 4096, 8192) if "linear" in legs else ()):
         X = torch.randn(n, n, device=dev, generator=g)
         W = torch.randn(n, n, device=dev, generator=g)
         dY = torch.randn(n, n, device=dev, generator=g)
@@ -677,7 +678,7 @@ def run_sweep(args):
     rows = 65536
     # bias gradient (column sums) and the GELU backward fused with it, at
     # configs[2]'s token count: 4 B/elem read, and 12 B/elem (x, dy read; dx written)
-    for w in (512, 2048):
+    for w in ((512, 2048) if "colsum" in legs else ()):
         dy = torch.randn(rows * w, device=dev, generator=g)
         db = torch.zeros(w, device=dev)
         ms = timed(lambda: ops.bias_grad(dy, db), 20)
@@ -691,7 +692,7 @@ def run_sweep(args):
         print(json.dumps({"sweep": "gelu_bwd_bias_grad", "rows": rows, "width": w, "ms": ms, "gbs": gbs,
                           "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
         del dy, db, x, dx
-    for w in (1024, 2048, 4096, 8192):
+    for w in ((1024, 2048, 4096, 8192) if "layernorm" in legs else ()):
         x = torch.randn(rows * w, device=dev, generator=g)
         y, mean, sq = torch.empty_like(x), torch.empty(rows, device=dev), torch.empty(rows, device=dev)
         ops.layernorm_fwd(x, y, mean, sq, rows, 1, 1, w)
@@ -715,7 +716,8 @@ def run_sweep(args):
         print(json.dumps({"sweep": "layernorm_gelu_bwd", "rows": rows, "width": w, "ms": ms, "gbs": gbs,
                           "frac_of_hbm": gbs / hbm_peak, "peak_kind": kind}), flush=True)
         del x, y, gy, gx, a, gh
-    for total in (100_000_000, 1_000_000_000):
+    totals = [int(float(x)) for x in args.sweep_optimizer_params.split(",")] if "optimizer" in legs else []
+    for total in totals:
         nt = 256
         sizes = np.random.default_rng(0).integers(1, 1000, nt).astype(np.float64)
         sizes = np.maximum(1, (sizes / sizes.sum() * total).astype(np.int64))
@@ -931,6 +933,10 @@ def main():
     ap.add_argument("--no-ref-cuda", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="configs[4] kernel sweep, one JSON line per case")
+    ap.add_argument("--sweep-only", default=None,
+                    help="comma list of sweep legs to run: linear, colsum, layernorm, optimizer (default: all)")
+    ap.add_argument("--sweep-optimizer-params", default="1e8,1e9",
+                    help="parameter totals of the optimizer legs (comma list)")
     ap.add_argument("--attention", action="store_true",
                     help="configs[2]'s attention block on both tensor-core paths, one JSON line per case")
     ap.add_argument("--gemm-pairs", type=int, default=None, choices=[0, 1, 2],
