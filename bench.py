@@ -950,6 +950,9 @@ def main():
     ap.add_argument("--fused-optimizer", type=int, default=None, choices=[0, 1],
                     help="norm, clip and AdamW as one cooperative launch (1, the library default) or as the "
                          "sum-of-squares, finalize and update launches (0) (mle_set_fused_optimizer)")
+    ap.add_argument("--gemm-column-sums", type=int, default=None, choices=[0, 1],
+                    help="Linear bias gradients from the dW product's epilogue (1, the library default) or a "
+                         "separate column-sum launch (0) (mle_set_gemm_column_sums)")
     ap.add_argument("--bucket-mb", type=int, default=0,
                     help="data-parallel gradient bucket size in MiB (mle_session_enable_dp); 0: the library's "
                          "choice from the gradient total (mle_dp_auto_bucket_mb)")
@@ -978,6 +981,9 @@ def main():
     if args.param_stream is not None:
         from ml_engine_b200._lib import engine
         engine().call("mle_set_param_grad_stream", args.param_stream)
+    if args.gemm_column_sums is not None:
+        from ml_engine_b200._lib import kernels
+        kernels().call("mle_set_gemm_column_sums", args.gemm_column_sums)
     if args.fused_optimizer is not None:
         from ml_engine_b200._lib import engine
         engine().call("mle_set_fused_optimizer", args.fused_optimizer)

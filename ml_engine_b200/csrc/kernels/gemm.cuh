@@ -23,6 +23,11 @@ struct GemmProblem {
     // (tensor-core path only; c_split a multiple of 32 dividing N)
     int c_split = 0;
     int64_t c_split_ld = 0;
+    // non-null: also colsum[n] += sum_k B[k][n] (B stored [K][N] with
+    // ldb == N, one product).  The tensor-core path sums B's tiles in shared
+    // memory while they pass through (a Linear's bias gradient beside its
+    // weight gradient); where it cannot, a column-sum launch follows.
+    float* colsum = nullptr;
 };
 
 // Implicit-GEMM convolution at stride 1 over KW horizontally shifted

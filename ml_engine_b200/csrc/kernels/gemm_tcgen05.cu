@@ -80,6 +80,10 @@ struct EpiParams {
     // one as (32 MN, K, MN / 32, channel, batch); else the plain 4-D view
     // (MN-major tiles then arrive as one 32-column box each)
     int a_split, b_split;
+    // non-null: colsum[n] += sum over this tile's k-range of B[k][n], taken
+    // by the epilogue warps from B's stages in shared memory (tiles of the
+    // first row-tile only; MN-major B, single CTAs)
+    float* colsum;
 };
 
 // Output tile `t` of the persistent walk: n fastest, then m, then (batch,
@@ -108,6 +112,9 @@ struct GemmGroup {
     // same rows of a shared A run back to back and find them in L2
     int ilv;
     int ilv_n[kMaxGroup + 1];
+    // some problem sums B's columns: the epilogue warps follow every stage
+    // (and release it) as the MMA issuer does
+    int colsum;
 };
 
 __device__ __forceinline__ int group_of(const GemmGroup& G, int64_t t) {
@@ -497,9 +504,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t total_tiles = grp.tile_start[grp.n];
 
     if (threadIdx.x == 0) {
+        // a stage is released by the MMA commit, and by each epilogue warp
+        // too when they sum B's columns
+        const bool follow = !PAIR && B_MN && grp.colsum;
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], follow ? 1 + kEpiWarps : 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
@@ -735,6 +745,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rsub = lane >> 3, c4 = (lane & 7) * 4;
         int acc = 0;
         uint32_t blocks_out = 0;  // bulk groups this warp committed
+        int es = 0;               // the stage ring as the MMA issuer walks it (column sums)
+        uint32_t eph = 0;
         for (int64_t t = t_first; t < total_tiles; t += t_step, ++acc) {
             int64_t tl;
             const int g = locate(grp, t, tl);
@@ -743,6 +755,59 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Tile x = tile_at(ep, tl, BN, BMT);
             const int buf = acc & 1;
             const uint32_t use = (uint32_t)(acc >> 1);
+            if constexpr (!PAIR && B_MN) {
+                if (grp.colsum) {
+                    // B's columns summed over the tile's k-range while its stages
+                    // pass: 32-column chunk ch of a stage holds KPL k-blocks of 32
+                    // rows of 128 bytes (one k each), swizzled in 32-byte units
+                    // (the MN-major 128-byte swizzle with 32-byte atoms): unit j of
+                    // row r sits at j ^ (r % 4); lane l sums column ch * 32 + l.
+                    // Every stage is released here (its empty barrier expects these
+                    // warps), summed or not.
+                    constexpr int kCh = (BNC / 32 + kEpiWarps - 1) / kEpiWarps;
+                    const bool sum_here = ep.colsum != nullptr && x.m0 == 0;
+                    const int e = warp - 2;
+                    float cs[kCh];
+#pragma unroll
+                    for (int u = 0; u < kCh; ++u) cs[u] = 0.0f;
+                    bool ok = true;
+                    for (int i = 0; i < x.nkb; i += KPL) {
+                        ok = __all_sync(0xffffffffu, wait_bounded(&full[es], eph, abort_flag));
+                        if (!ok) break;
+                        if (sum_here) {
+                            const uint8_t* sb = smem + es * L::STAGE_BYTES + L::A_BYTES;
+                            const int nv = min(KPL, x.nkb - i);
+#pragma unroll
+                            for (int u = 0; u < kCh; ++u) {
+                                const int ch = e + u * kEpiWarps;
+                                if (ch >= BNC / 32) break;
+                                for (int kb = 0; kb < nv; ++kb) {
+                                    const uint8_t* blk = sb + ch * (KPL * 4096) + kb * 4096 + (lane & 7) * 4;
+#pragma unroll 8
+                                    for (int r = 0; r < 32; ++r)
+                                        cs[u] += *reinterpret_cast<const float*>(
+                                            blk + r * 128 + ((((lane >> 3) ^ (r & 3))) << 5));
+                                }
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[es]);
+                        if (++es == STAGES) {
+                            es = 0;
+                            eph ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    if (sum_here && x.nkb > 0) {
+#pragma unroll
+                        for (int u = 0; u < kCh; ++u) {
+                            const int ch = e + u * kEpiWarps;
+                            const int col = x.n0 + ch * 32 + lane;
+                            if (ch < BNC / 32 && col < ep.N) atomicAdd(ep.colsum + col, cs[u]);
+                        }
+                    }
+                }
+            }
             // the tcgen05.ld below is warp-collective: leave the loop together
             const bool ready = wait_bounded(&tmem_full[buf], use & 1u, abort_flag);
             if (!__all_sync(0xffffffffu, ready)) break;
@@ -1347,6 +1412,7 @@ static thread_local int g_last_choice[3] = {0, 0, 0};
 // to even, as it loads; measured on B200).  Rounding halves the typical
 // product error at no cost, so it is the default.
 static thread_local int g_operand_round = 1;
+static thread_local int g_fuse_colsum = 1;  // column sums beside a product taken in its epilogue warps
 
 // k-blocks per stage for products whose operands all have a split view
 // (1 forces one k-block per stage everywhere)
@@ -1746,13 +1812,53 @@ int run_attn_keys(int mode, const float* keys_src, const float* rows_src, const 
 
 #include "attention_flash.cuh"
 
+// Column sums of B requested beside a product (GemmProblem::colsum): those
+// the launch takes in its epilogue warps are attached to the group; the rest
+// follow as column-sum launches (finish_colsums).
+static bool colsum_fusable(const GemmProblem& p, bool pair) {
+    return g_fuse_colsum && p.colsum && !pair && !p.trans_b && p.nbatch == 1 && p.channels == 1 && p.ldb == p.N;
+}
+
+static int column_sums(const GemmProblem& p, cudaStream_t st) {
+    if (!p.colsum || p.K <= 0) return MLE_OK;
+    if (p.trans_b || p.ldb != p.N || p.nbatch != 1 || p.channels != 1) return MLE_ERR_UNSUPPORTED;
+    return mle_bias_grad(p.B, p.colsum, p.K, p.N, 1.0f, reinterpret_cast<mle_stream_t>(st));
+}
+
+static void attach_colsums(const GemmProblem* ps, int n, tc::GemmGroup& grp, bool pair, bool* post) {
+    for (int i = 0; i < n; ++i) {
+        post[i] = false;
+        if (!ps[i].colsum) continue;
+        if (colsum_fusable(ps[i], pair) && grp.kcat <= 1 && grp.ep[i].conv == 0) {
+            grp.ep[i].colsum = ps[i].colsum;
+            grp.colsum = 1;
+        } else {
+            post[i] = true;
+        }
+    }
+}
+
+static int finish_colsums(const GemmProblem* ps, int n, const bool* post, cudaStream_t st) {
+    for (int i = 0; i < n; ++i)
+        if (post[i]) {
+            const int s = column_sums(ps[i], st);
+            if (s) return s;
+        }
+    return MLE_OK;
+}
+
 int run_gemm(const GemmProblem& p, cudaStream_t st) {
     if (p.M <= 0 || p.N <= 0 || p.nbatch <= 0 || p.channels <= 0) return MLE_OK;
+    if (p.colsum && (p.trans_b || p.ldb != p.N || p.nbatch != 1 || p.channels != 1)) return MLE_ERR_UNSUPPORTED;
     if (p.K <= 0) {
         // empty reduction: assign writes alpha*0 (+bias); accumulate is a no-op
         if (p.mode != tc::EPI_ASSIGN) return MLE_OK;
     }
-    if (!tc_path(p)) return p.c_split ? MLE_ERR_UNSUPPORTED : simt_gemm(p, st);
+    if (!tc_path(p)) {
+        if (p.c_split) return MLE_ERR_UNSUPPORTED;
+        const int s = simt_gemm(p, st);
+        return s ? s : column_sums(p, st);
+    }
     int BN, splits;
     bool pair = false;
     choose_tiles(&p, 1, BN, splits, false, g_gemm_pairs ? &pair : nullptr, g_gemm_pairs == 2);
@@ -1769,7 +1875,11 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
         s = prepare(p, BN, splits, false, grp, 0, st, ok, pair, kpl);
         if (s) return s;
     }
-    if (!ok) return p.c_split ? MLE_ERR_UNSUPPORTED : simt_gemm(p, st);
+    if (!ok) {
+        if (p.c_split) return MLE_ERR_UNSUPPORTED;
+        const int s2 = simt_gemm(p, st);
+        return s2 ? s2 : column_sums(p, st);
+    }
     grp.n = 1;
     grp.tile_start[0] = 0;
     grp.tile_start[1] = grp.ep[0].tiles;
@@ -1778,7 +1888,10 @@ int run_gemm(const GemmProblem& p, cudaStream_t st) {
     g_last_choice[1] = grp.ep[0].splits;
     g_last_choice[2] = pair ? 1 : 0;
     g_last_kpl = kpl;
-    return dispatch(grp, sh.A_MN, sh.B_MN, BN, st, pair, kpl);
+    bool post[1];
+    attach_colsums(&p, 1, grp, pair, post);
+    s = dispatch(grp, sh.A_MN, sh.B_MN, BN, st, pair, kpl);
+    return s ? s : finish_colsums(&p, 1, post, st);
 }
 
 // Problems of one layout class in one persistent launch.  `shared_c`: all
@@ -1842,7 +1955,10 @@ int run_gemm_group(const GemmProblem* ps, int n, bool shared_c, cudaStream_t st)
         for (int i = 0; i < n; ++i) grp.ilv_n[i + 1] = grp.ilv_n[i] + grp.ep[i].n_tiles;
     }
     g_last_kpl = kpl;
-    return dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st, pair, kpl);
+    bool post[tc::kMaxGroup];
+    attach_colsums(ps, n, grp, pair, post);
+    const int s = dispatch(grp, shape_of(ps[0]).A_MN, shape_of(ps[0]).B_MN, BN, st, pair, kpl);
+    return s ? s : finish_colsums(ps, n, post, st);
 }
 
 int run_gemm_kcat(const GemmProblem* ps, int n, cudaStream_t st) {
@@ -1856,7 +1972,7 @@ int run_gemm_kcat(const GemmProblem* ps, int n, cudaStream_t st) {
         const GemmProblem& p = ps[i];
         ok = tc_path(p) && p.C == ps[0].C && p.M == ps[0].M && p.N == ps[0].N && p.ldc == ps[0].ldc &&
              p.mode == ps[0].mode && p.alpha == ps[0].alpha && p.nbatch == 1 && p.channels == 1 && !p.bias &&
-             !p.c_split && p.mode != EPI_ATOMIC && p.K > 0 && p.K % 64 == 0 &&
+             !p.c_split && !p.colsum && p.mode != EPI_ATOMIC && p.K > 0 && p.K % 64 == 0 &&
              shape_of(p).A_MN == shape_of(ps[0]).A_MN && shape_of(p).B_MN == shape_of(ps[0]).B_MN;
         ksum += p.K;
     }
@@ -2165,6 +2281,14 @@ int mle_set_gemm_operand_rounding(int mode) {
 
 int mle_get_gemm_operand_rounding(void) { return g_operand_round; }
 
+int mle_set_gemm_column_sums(int enable) {
+    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    g_fuse_colsum = enable;
+    return MLE_OK;
+}
+
+int mle_get_gemm_column_sums(void) { return g_fuse_colsum; }
+
 int mle_gemm_last_choice(int* out3) {
     if (!out3) return MLE_ERR_ARG;
     for (int i = 0; i < 3; ++i) out3[i] = g_last_choice[i];
@@ -2287,9 +2411,9 @@ int mle_linear_group_bwd(const float* X, const float* const* W, const float* con
             if (!dW[i] || !dY[i] || out_features[i] <= 0) return MLE_ERR_ARG;
             ps[i] = linear_problem(X, dY[i], dW[i], nullptr, in_features, out_features[i], rows, in_features,
                                    out_features[i], out_features[i], 1, 0, tc::EPI_ACCUM);
+            ps[i].colsum = dB ? dB[i] : nullptr;
         }
-        s = run_gemm_group(ps, n, false, st);
-        if (s) return s;
+        return run_gemm_group(ps, n, false, st);
     }
     if (dB) {
         for (int i = 0; i < n; ++i) {
@@ -2396,11 +2520,15 @@ int mle_linear_bwd(const float* X, const float* W, const float* dY, float* dX, f
                      0, 0, 0, 1, 1.0f, 1.0f, stream);
         if (s) return s;
     }
-    // dW[in, out] += X[rows, in]^T * dY[rows, out]
+    // dW[in, out] += X[rows, in]^T * dY[rows, out], with dB[out] += the
+    // column sums of dY taken from the same product's dY tiles
     if (dW) {
-        s = mle_gemm(X, dY, dW, nullptr, 1, in_features, out_features, rows, in_features, out_features, out_features,
-                     0, 0, 0, 1, 0, 1.0f, 1.0f, stream);
-        if (s) return s;
+        if (rows > 0x7fffffffLL) return MLE_ERR_UNSUPPORTED;
+        GemmProblem q = linear_problem(X, dY, dW, nullptr, in_features, out_features, (int)rows, in_features,
+                                       out_features, out_features, 1, 0, tc::EPI_ACCUM);
+        q.colsum = dB;
+        g_last_kpl = 0;  // set again if the product runs on the tensor cores
+        return run_gemm(q, as_stream(stream));
     }
     if (dB) return mle_bias_grad(dY, dB, rows, out_features, 1.0f, stream);
     return MLE_OK;
