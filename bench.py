@@ -950,6 +950,12 @@ def main():
     ap.add_argument("--fused-optimizer", type=int, default=None, choices=[0, 1],
                     help="norm, clip and AdamW as one cooperative launch (1, the library default) or as the "
                          "sum-of-squares, finalize and update launches (0) (mle_set_fused_optimizer)")
+    ap.add_argument("--attn-flash", type=int, default=None, choices=[0, 1],
+                    help="flash attention kernels where they apply (1, the library default) or the keys-on-lanes "
+                         "path (0) (mle_set_attention_flash)")
+    ap.add_argument("--add-norm-fusion", type=int, default=None, choices=[0, 1],
+                    help="forward residual Add + LayerNorm as one pass (1, the library default) or two launches (0) "
+                         "(mle_set_add_norm_fusion)")
     ap.add_argument("--gemm-column-sums", type=int, default=None, choices=[0, 1],
                     help="Linear bias gradients from the dW product's epilogue (1, the library default) or a "
                          "separate column-sum launch (0) (mle_set_gemm_column_sums)")
@@ -981,6 +987,12 @@ def main():
     if args.param_stream is not None:
         from ml_engine_b200._lib import engine
         engine().call("mle_set_param_grad_stream", args.param_stream)
+    if args.attn_flash is not None:
+        from ml_engine_b200._lib import kernels
+        kernels().call("mle_set_attention_flash", args.attn_flash)
+    if args.add_norm_fusion is not None:
+        from ml_engine_b200._lib import engine
+        engine().call("mle_set_add_norm_fusion", args.add_norm_fusion)
     if args.gemm_column_sums is not None:
         from ml_engine_b200._lib import kernels
         kernels().call("mle_set_gemm_column_sums", args.gemm_column_sums)

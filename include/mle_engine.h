@@ -135,6 +135,14 @@ int mle_get_grad_first_write(void);
 int mle_set_fused_optimizer(int enable);
 int mle_get_fused_optimizer(void);
 
+/* Forward: a residual Add whose sum a LayerNorm reads runs as one pass that
+ * writes the sum and the norm's output and statistics
+ * (mle_add_layernorm_fwd), the norm's own launch dropped; both outputs are
+ * bitwise those of the two launches.  1 (default) on, 0 off.
+ * Process-wide; decided when a forward pass starts. */
+int mle_set_add_norm_fusion(int enable);
+int mle_get_add_norm_fusion(void);
+
 /* Captures each phase of the step (the numbering of mle_session_phase,
  * device resident: no upload, no loss download) as its own CUDA graph, so a
  * caller can time phases on the device; mle_session_phase_replay(s, ph)

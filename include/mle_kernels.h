@@ -252,6 +252,16 @@ int mle_embedding_update(const int32_t* keys, const float* grad, float* table, f
 int mle_layernorm_fwd(const float* x, float* y, float* mean, float* sqdev, int batch,
                       int channels, int row, int col, float eps, mle_stream_t stream);
 
+/* The residual Add and the LayerNorm that reads its sum, in one pass:
+ * xr = x + r (GraphOperations::Add forward, Engine/engine.cu:1650-1655, as
+ * ScaleAdd with scale 1) and then mle_layernorm_fwd of xr into y, mean and
+ * sqdev -- both outputs bitwise those of the two launches.  Segments of up
+ * to 1024 elements (a multiple of 4) with 16-byte aligned x, r, xr and y;
+ * other shapes return MLE_ERR_UNSUPPORTED with nothing written (the caller
+ * then launches the two apart). */
+int mle_add_layernorm_fwd(const float* x, const float* r, float* xr, float* y, float* mean, float* sqdev, int batch,
+                          int channels, int row, int col, float eps, mle_stream_t stream);
+
 /* LayerNorm backward gx += rstd*(gy - sum(gy)/N - y*sum(gy*y)/N), with the
  * reference's index map (only the first batch*row*col elements, correct for
  * channels == 1).  Replaces Scale_Write+mulKernel+2xLayerMean+LayerBackward

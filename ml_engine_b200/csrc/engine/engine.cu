@@ -568,6 +568,16 @@ void GraphOperations::collect_params(std::vector<AdamParameter*>& out) {
 }
 
 static bool g_fused_optimizer = true;
+static bool g_add_norm_fusion = true;
+bool mle::add_norm_fusion() { return g_add_norm_fusion; }
+
+extern "C" int mle_set_add_norm_fusion(int enable) {
+    if (enable != 0 && enable != 1) return MLE_ERR_ARG;
+    g_add_norm_fusion = enable != 0;
+    return MLE_OK;
+}
+
+extern "C" int mle_get_add_norm_fusion(void) { return g_add_norm_fusion ? 1 : 0; }
 
 extern "C" int mle_set_fused_optimizer(int enable) {
     if (enable != 0 && enable != 1) return MLE_ERR_ARG;
@@ -703,6 +713,7 @@ void GraphOperations::forward(const graph& X, const bool calc_loss, const bool s
                "sort \n");
         return;
     }
+    prepare_fusions(nodes);  // the forward's Add + LayerNorm passes (and the backward's plan)
     for (auto& node : nodes) {
         auto t0 = std::chrono::high_resolution_clock::now();
         if (time) CheckError("Before " + node->op_name + " forward");

@@ -41,6 +41,7 @@ enum OpKind {
     OP_ATTENTION = 4,  // ScaledDotAttention on the token-major kernels
     OP_ADD = 5,
     OP_CONV = 6,       // Convolute2D
+    OP_LAYERNORM = 7,
 };
 
 // Per-node fusion state decided by prepare_fusions() before a backward pass.
@@ -52,6 +53,14 @@ struct NodeExt {
     long long fused_rows = 0, fused_cols = 0;
     std::vector<float*> param_grads;     // parameter gradients complete once this node's backward ran
     int assign_inputs = 0;               // bit i: backward writes (not adds to) inputs[i]'s gradient
+    // forward: an Add whose sum feeds a LayerNorm computes both in one pass
+    const NodeBackProp* fused_norm = nullptr;  // Add: the LayerNorm it also produces
+    bool add_is_loss = false;                  // Add: the loss sum (read back; not fused)
+    bool norm_done = false;                    // LayerNorm: its Add wrote its output this forward
+    float* ln_mean = nullptr;                  // LayerNorm: its statistics buffers and shape
+    float* ln_sq = nullptr;
+    int ln_dims[4] = {0, 0, 0, 0};
+    float ln_eps = 0.0f;
 };
 NodeExt& ext(const NodeBackProp* n);
 void forget_ext(const NodeBackProp* n);
@@ -65,6 +74,10 @@ void forget_ext(const NodeBackProp* n);
 // Convolute2D, or a Linear with a large input gradient.  That writer assigns (assign_inputs) and
 // zero_grad leaves the buffer alone.
 void prepare_fusions(const graph_tree& nodes);
+
+// Whether forward fuses a residual Add with the LayerNorm that reads it
+// (mle_set_add_norm_fusion).
+bool add_norm_fusion();
 
 // Base of the arena chunk (one device allocation) holding p, or nullptr.
 const void* arena_chunk_of(const void* p);

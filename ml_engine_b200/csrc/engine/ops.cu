@@ -42,6 +42,20 @@ void prepare_fusions(const graph_tree& nodes) {
         if (e.kind == OP_LINEAR) e.bias_grad_fused = false;
         if (e.kind == OP_ACTIVATION) e.fused_bias_target = nullptr;
         e.assign_inputs = 0;
+        e.fused_norm = nullptr;
+        e.norm_done = false;
+    }
+    // a residual Add whose sum a LayerNorm reads writes the norm's output in
+    // the same pass (the norm's forward then has nothing left to do)
+    if (add_norm_fusion()) {
+        for (auto& n : nodes) {
+            const NodeExt& le = ext(n.get());
+            if (le.kind != OP_LAYERNORM || n->inputs.size() != 1) continue;
+            const NodeBackProp* a = n->inputs[0].get();
+            NodeExt& ae = ext(a);
+            if (ae.kind != OP_ADD || ae.add_is_loss || ae.fused_norm) continue;
+            ae.fused_norm = n.get();
+        }
     }
     // first writers that overwrite the whole input gradient: the loss
     // (SoftMaxCrossEntropy assigns its prediction's gradient), an
@@ -274,7 +288,19 @@ graph GraphOperations::Add(const graph& A, const graph& B, const bool last) {
     GB += (double)node->total * sizeof(float) / (1ULL << 30);
     NodeBackProp *nd = node.get(), *ap = A.get(), *bp = B.get();
     ext(nd).kind = OP_ADD;
+    ext(nd).add_is_loss = last;
     node->forward = [=]() {
+        if (const NodeBackProp* ln = ext(nd).fused_norm) {
+            NodeExt& le = ext(ln);
+            const int s = mle_add_layernorm_fwd(ap->output, bp->output, nd->output, ln->output, le.ln_mean, le.ln_sq,
+                                                le.ln_dims[0], le.ln_dims[1], le.ln_dims[2], le.ln_dims[3], le.ln_eps,
+                                                st());
+            if (s != MLE_ERR_UNSUPPORTED) {
+                check(s, "Add + LayerNorm forward");
+                le.norm_done = true;
+                return;
+            }
+        }
         check(mle_scale_add(ap->output, bp->output, nd->output, 1.0f, nd->total, st()), "Add forward");
         if (last && g_loss_readback) {
             check_cuda(cudaStreamSynchronize(stream()), "Add loss");
@@ -623,7 +649,20 @@ graph GraphOperations::LayerNorm(const graph& X) {
     GB += (double)(node->total + 2 * a) * sizeof(float) / (1ULL << 30);
     node->inputs = {X};
     NodeBackProp *nd = node.get(), *xp = X.get();
+    NodeExt& ne = ext(nd);
+    ne.kind = OP_LAYERNORM;
+    ne.ln_mean = mean;
+    ne.ln_sq = sq;
+    ne.ln_dims[0] = a;
+    ne.ln_dims[1] = b;
+    ne.ln_dims[2] = c;
+    ne.ln_dims[3] = d;
+    ne.ln_eps = eps;
     node->forward = [=]() {
+        if (ext(nd).norm_done) {  // written by the Add it reads (one pass)
+            ext(nd).norm_done = false;
+            return;
+        }
         check(mle_layernorm_fwd(xp->output, nd->output, mean, sq, a, b, c, d, eps, st()), "LayerNorm forward");
     };
     node->backward = [=]() {

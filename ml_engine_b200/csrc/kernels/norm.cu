@@ -27,10 +27,14 @@ constexpr int kBlock = 256;
 constexpr int kWarpMaxN = 1024;
 
 // ----------------------------- warp per segment ---------------------------
-template <int V>  // V float4 per lane -> N <= 128 * V
-__global__ void seg_norm_fwd_warp(const float* __restrict__ x, float* __restrict__ y, float* __restrict__ mean,
-                                  float* __restrict__ sqdev, int64_t segs, int N, float eps) {
-    pdl_entry();
+// RESID: the segment is x + r (the residual Add that feeds the norm), which
+// is also written to xr; the sum is the Add's own x + 1.0f * r, so both
+// outputs are bitwise those of the Add and the norm launched apart.
+template <int V, bool RESID>  // V float4 per lane -> N <= 128 * V
+__device__ __forceinline__ void norm_fwd_warp(const float* __restrict__ x, const float* __restrict__ r,
+                                              float* __restrict__ xr, float* __restrict__ y,
+                                              float* __restrict__ mean, float* __restrict__ sqdev, int64_t segs,
+                                              int N, float eps) {
     const int lane = threadIdx.x & 31;
     const int64_t seg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (seg >= segs) return;
@@ -42,6 +46,14 @@ __global__ void seg_norm_fwd_warp(const float* __restrict__ x, float* __restrict
         const int c = lane + 32 * i;
         if (c * 4 < N) {
             v[i] = xs[c];
+            if constexpr (RESID) {
+                const float4 w = reinterpret_cast<const float4*>(r + seg * N)[c];
+                v[i].x = v[i].x + 1.0f * w.x;
+                v[i].y = v[i].y + 1.0f * w.y;
+                v[i].z = v[i].z + 1.0f * w.z;
+                v[i].w = v[i].w + 1.0f * w.w;
+                reinterpret_cast<float4*>(xr + seg * N)[c] = v[i];
+            }
             s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
         } else {
             v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -77,6 +89,21 @@ __global__ void seg_norm_fwd_warp(const float* __restrict__ x, float* __restrict
         if (mean) mean[seg] = mu;
         sqdev[seg] = q;
     }
+}
+
+template <int V>
+__global__ void seg_norm_fwd_warp(const float* __restrict__ x, float* __restrict__ y, float* __restrict__ mean,
+                                  float* __restrict__ sqdev, int64_t segs, int N, float eps) {
+    pdl_entry();
+    norm_fwd_warp<V, false>(x, nullptr, nullptr, y, mean, sqdev, segs, N, eps);
+}
+
+template <int V>
+__global__ void add_norm_fwd_warp(const float* __restrict__ x, const float* __restrict__ r, float* __restrict__ xr,
+                                  float* __restrict__ y, float* __restrict__ mean, float* __restrict__ sqdev,
+                                  int64_t segs, int N, float eps) {
+    pdl_entry();
+    norm_fwd_warp<V, true>(x, r, xr, y, mean, sqdev, segs, N, eps);
 }
 
 template <int V>
@@ -390,6 +417,25 @@ int mle_layernorm_fwd(const float* x, float* y, float* mean, float* sqdev, int b
     const int64_t N = (int64_t)channels * row * col;
     if (N > (1ll << 30)) return MLE_ERR_UNSUPPORTED;
     return seg_norm_fwd(x, y, mean, sqdev, batch, (int)N, eps, as_stream(stream));
+}
+
+int mle_add_layernorm_fwd(const float* x, const float* r, float* xr, float* y, float* mean, float* sqdev, int batch,
+                          int channels, int row, int col, float eps, mle_stream_t stream) {
+    if (batch < 0 || channels <= 0 || row <= 0 || col <= 0 || !x || !r || !xr || !y || !sqdev) return MLE_ERR_ARG;
+    const int64_t N = (int64_t)channels * row * col;
+    if (N % 4 != 0 || N > kWarpMaxN || !aligned16(x) || !aligned16(r) || !aligned16(xr) || !aligned16(y))
+        return MLE_ERR_UNSUPPORTED;
+    if (batch == 0) return MLE_OK;
+    const int wpb = 8;  // warps per block, one segment each
+    const unsigned grid = (unsigned)((batch + wpb - 1) / wpb);
+    const int n = (int)N;
+    cudaStream_t st = as_stream(stream);
+    const int64_t segs = batch;
+    if (N <= 128) launch_k(add_norm_fwd_warp<1>, grid, 32 * wpb, 0, st, x, r, xr, y, mean, sqdev, segs, n, eps);
+    else if (N <= 256) launch_k(add_norm_fwd_warp<2>, grid, 32 * wpb, 0, st, x, r, xr, y, mean, sqdev, segs, n, eps);
+    else if (N <= 512) launch_k(add_norm_fwd_warp<4>, grid, 32 * wpb, 0, st, x, r, xr, y, mean, sqdev, segs, n, eps);
+    else launch_k(add_norm_fwd_warp<8>, grid, 32 * wpb, 0, st, x, r, xr, y, mean, sqdev, segs, n, eps);
+    return launch_status();
 }
 
 int mle_layernorm_bwd(const float* y, const float* gy, const float* sqdev, float* gx, int batch, int channels, int row,

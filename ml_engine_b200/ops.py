@@ -137,6 +137,12 @@ def layernorm_fwd(x, y, mean, sqdev, batch, channels, row, col, eps=1e-5):
     _call("mle_layernorm_fwd", _p(x), _p(y), _p(mean), _p(sqdev), batch, channels, row, col, eps, _s())
 
 
+def add_layernorm_fwd(x, r, xr, y, mean, sqdev, batch, channels, row, col, eps=1e-5):
+    """xr = x + r and the LayerNorm of xr, in one pass."""
+    _call("mle_add_layernorm_fwd", _p(x), _p(r), _p(xr), _p(y), _p(mean), _p(sqdev), batch, channels, row, col, eps,
+          _s())
+
+
 def layernorm_bwd(y, gy, sqdev, gx, batch, channels, row, col, eps=1e-5):
     _call("mle_layernorm_bwd", _p(y), _p(gy), _p(sqdev), _p(gx), batch, channels, row, col, eps, _s())
 

@@ -231,6 +231,34 @@ def test_layernorm(cuda, ops, orc, rng, batch, channels, row, col):
     assert rel_err(H(gx), orc.layernorm_bwd(ry, gy, rsq, gx0.copy(), batch, channels, row, col)) <= RTOL_EXACT
 
 
+@pytest.mark.parametrize("batch,channels,row,col", [(4096, 1, 1, 256), (8192, 1, 1, 512), (33, 1, 1, 1000),
+                                                    (7, 1, 4, 32), (5, 1, 1, 100), (3, 1, 1, 2048)])
+def test_add_layernorm_matches_two_launches(cuda, ops, rng, batch, channels, row, col):
+    """The residual Add and its LayerNorm in one pass against mle_scale_add
+    followed by mle_layernorm_fwd: the sum, the normalised output and the
+    statistics bit for bit; segments the one-pass kernel does not take
+    (over 1024 elements) are refused with nothing written."""
+    from ml_engine_b200 import MLEError
+    n = batch * channels * row * col
+    x = T((rng.standard_normal(n) * 2 + 0.5).astype(np.float32), cuda)
+    r = T(rng.standard_normal(n).astype(np.float32), cuda)
+    xr, y = torch.full((n,), 7.0, device=cuda), torch.full((n,), 7.0, device=cuda)
+    mean, sq = torch.zeros(batch, device=cuda), torch.zeros(batch, device=cuda)
+    seg = channels * row * col
+    if seg > 1024:
+        with pytest.raises(MLEError):
+            ops.add_layernorm_fwd(x, r, xr, y, mean, sq, batch, channels, row, col)
+        assert torch.all(xr == 7.0) and torch.all(y == 7.0)
+        return
+    ops.add_layernorm_fwd(x, r, xr, y, mean, sq, batch, channels, row, col)
+    rxr, ry = torch.empty(n, device=cuda), torch.empty(n, device=cuda)
+    rmean, rsq = torch.zeros(batch, device=cuda), torch.zeros(batch, device=cuda)
+    ops.scale_add(x, r, rxr, 1.0)
+    ops.layernorm_fwd(rxr, ry, rmean, rsq, batch, channels, row, col)
+    assert torch.equal(xr, rxr) and torch.equal(y, ry)
+    assert torch.equal(mean, rmean) and torch.equal(sq, rsq)
+
+
 @pytest.mark.parametrize("batch,channels,groups,row,col", [(4, 64, 8, 16, 16), (2, 24, 8, 3, 5), (2, 64, 8, 64, 64),
                                                            (3, 128, 8, 32, 32)])
 def test_groupnorm(cuda, ops, orc, rng, batch, channels, groups, row, col):

@@ -460,3 +460,43 @@ def test_fused_optimizer_matches_separate_launches(cuda, rng):
             x, y = sb[i][which], sa[i][which]
             floor = np.linalg.norm(x - y) <= 1e-7 * gnorm
             assert norm_err(x, y) <= 1e-4 or floor, (a.param_names[i], which, norm_err(x, y))
+
+
+def test_add_norm_fusion_matches_separate_launches(cuda, rng):
+    """The forward's residual Add + LayerNorm passes against the Add and the
+    norm launched apart, on the pre-LN encoder: the same loss and gradients
+    up to the step's own run-to-run spread (its loss and gradient sums use
+    atomics, so even repeated steps of one run differ in the last bits; the
+    pass itself is checked bit for bit against the two launches in the
+    kernel tests), and fewer kernels in the captured step."""
+    import ctypes
+    from ml_engine_b200._lib import engine
+    kw = dict(config=2, batch=16, seq_len=256, d_model=512, heads=8, ffn=2048, layers=1, vocab=512, seed=5, lr=0.0)
+    lib = engine()
+    old = lib.mle_get_add_norm_fusion()
+    tokens = rng.integers(0, 512, 16 * 256).astype(np.int32)
+    targets = rng.integers(0, 512, 16 * 256).astype(np.int32)
+    runs = {}
+    try:
+        for mode in (0, 1):
+            lib.call("mle_set_add_norm_fusion", mode)
+            s = _session(**kw)
+            s.inputs["tokens"][:] = tokens
+            s.inputs["targets"][:] = targets
+            losses = [s.step()]
+            s.capture()
+            losses += [s.step(), s.step()]
+            kk, mm, cc = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+            s._lib.call("mle_session_graph_counts", s._h, ctypes.addressof(kk), ctypes.addressof(mm),
+                        ctypes.addressof(cc))
+            runs[mode] = (s, losses, [s.read_param(i, 1) for i in range(len(s.param_names))], kk.value)
+    finally:
+        lib.call("mle_set_add_norm_fusion", old)
+    (a, la, ga, ka), (b, lb, gb, kb) = runs[0], runs[1]
+    assert kb < ka, (ka, kb)
+    for x, y in zip(la + lb, la[:1] * 6):
+        assert abs(x - y) <= 1e-5 * abs(y), (la, lb)
+    gnorm = np.sqrt(sum(float(np.sum(np.asarray(g, np.float64) ** 2)) for g in ga))
+    for i in range(len(a.param_names)):
+        floor = np.linalg.norm(gb[i] - ga[i]) <= 1e-7 * gnorm
+        assert norm_err(gb[i], ga[i]) <= 1e-4 or floor, (a.param_names[i], norm_err(gb[i], ga[i]))
