@@ -378,10 +378,10 @@ int mle_get_gemm_operand_rounding(void);
 /* Where a Linear's bias gradient comes from when its weight gradient is
  * taken too (mle_linear_bwd, mle_linear_group_bwd with dW and dB): 1
  * (default) the epilogue warps of the dW product sum dY's columns from the
- * dY tiles as they pass through shared memory (single-CTA tiles; CTA-pair
- * launches keep the separate column sum), so dB uses the operand values the
- * product uses -- TF32-rounded under operand rounding 1, the fp32 values
- * under 0; 0 a separate column-sum launch of the fp32 dY (BCompress,
+ * dY tiles as they pass through shared memory (in a CTA pair each CTA the
+ * columns it staged), so dB uses the operand values the product uses --
+ * TF32-rounded under operand rounding 1, the fp32 values under 0; 0 a
+ * separate column-sum launch of the fp32 dY (BCompress,
  * Engine/kernels.cu:1562-1584).  Per host thread. */
 int mle_set_gemm_column_sums(int enable);
 int mle_get_gemm_column_sums(void);

@@ -82,7 +82,7 @@ struct EpiParams {
     int a_split, b_split;
     // non-null: colsum[n] += sum over this tile's k-range of B[k][n], taken
     // by the epilogue warps from B's stages in shared memory (tiles of the
-    // first row-tile only; MN-major B, single CTAs)
+    // first row-tile only; MN-major B; in a pair each CTA its own columns)
     float* colsum;
 };
 
@@ -471,8 +471,8 @@ struct Smem {
     static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
     static constexpr int EPI_WARP_BYTES = 2 * 32 * 32 * 4;  // two 4 KB blocks (>= 32 x kEpiLd floats)
     static constexpr int BAR_OFFSET = EPI_OFFSET + kEpiWarps * EPI_WARP_BYTES;
-    // full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], drain
-    static constexpr int N_BARS = 2 * STAGES + 5;
+    // full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], drain, consumed[STAGES]
+    static constexpr int N_BARS = 3 * STAGES + 5;
     static constexpr int TOTAL = BAR_OFFSET + N_BARS * 8 + 16 + 1024;  // + TMEM slot, abort flag, alignment
 };
 
@@ -497,7 +497,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tmem_full = empty + STAGES;
     uint64_t* tmem_empty = tmem_full + 2;
     uint64_t* drain = tmem_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* consumed = drain + 1;  // a stage's MMAs retired (column sums read it then)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(consumed + STAGES);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -505,11 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         // a stage is released by the MMA commit, and by each epilogue warp
-        // too when they sum B's columns
-        const bool follow = !PAIR && B_MN && grp.colsum;
+        // too when they sum B's columns (after the commit on consumed[s])
+        const bool follow = B_MN && grp.colsum;
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], follow ? 1 + kEpiWarps : 1);
+            mbar_init(&consumed[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
@@ -722,6 +724,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if constexpr (PAIR) mma_commit_pair_both(&empty[s]);
                     else mma_commit(&empty[s]);
+                    if (B_MN && grp.colsum) {
+                        if constexpr (PAIR) mma_commit_pair_both(&consumed[s]);
+                        else mma_commit(&consumed[s]);
+                    }
                     if (++s == STAGES) {
                         s = 0;
                         ph ^= 1u;
@@ -755,15 +761,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Tile x = tile_at(ep, tl, BN, BMT);
             const int buf = acc & 1;
             const uint32_t use = (uint32_t)(acc >> 1);
-            if constexpr (!PAIR && B_MN) {
+            if constexpr (B_MN) {
                 if (grp.colsum) {
                     // B's columns summed over the tile's k-range while its stages
                     // pass: 32-column chunk ch of a stage holds KPL k-blocks of 32
                     // rows of 128 bytes (one k each), swizzled in 32-byte units
                     // (the MN-major 128-byte swizzle with 32-byte atoms): unit j of
                     // row r sits at j ^ (r % 4); lane l sums column ch * 32 + l.
-                    // Every stage is released here (its empty barrier expects these
-                    // warps), summed or not.
+                    // A stage is read once its MMAs retired (consumed[s], which the
+                    // MMA issuer commits in both CTAs of a pair, each summing the
+                    // columns it staged) and released here (its empty barrier
+                    // expects these warps), summed or not.
                     constexpr int kCh = (BNC / 32 + kEpiWarps - 1) / kEpiWarps;
                     const bool sum_here = ep.colsum != nullptr && x.m0 == 0;
                     const int e = warp - 2;
@@ -772,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int u = 0; u < kCh; ++u) cs[u] = 0.0f;
                     bool ok = true;
                     for (int i = 0; i < x.nkb; i += KPL) {
-                        ok = __all_sync(0xffffffffu, wait_bounded(&full[es], eph, abort_flag));
+                        ok = __all_sync(0xffffffffu, wait_bounded(&consumed[es], eph, abort_flag));
                         if (!ok) break;
                         if (sum_here) {
                             const uint8_t* sb = smem + es * L::STAGE_BYTES + L::A_BYTES;
@@ -802,7 +810,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int u = 0; u < kCh; ++u) {
                             const int ch = e + u * kEpiWarps;
-                            const int col = x.n0 + ch * 32 + lane;
+                            const int col = x.n0 + rank * BNC + ch * 32 + lane;
                             if (ch < BNC / 32 && col < ep.N) atomicAdd(ep.colsum + col, cs[u]);
                         }
                     }
@@ -1815,8 +1823,8 @@ int run_attn_keys(int mode, const float* keys_src, const float* rows_src, const 
 // Column sums of B requested beside a product (GemmProblem::colsum): those
 // the launch takes in its epilogue warps are attached to the group; the rest
 // follow as column-sum launches (finish_colsums).
-static bool colsum_fusable(const GemmProblem& p, bool pair) {
-    return g_fuse_colsum && p.colsum && !pair && !p.trans_b && p.nbatch == 1 && p.channels == 1 && p.ldb == p.N;
+static bool colsum_fusable(const GemmProblem& p, bool) {
+    return g_fuse_colsum && p.colsum && !p.trans_b && p.nbatch == 1 && p.channels == 1 && p.ldb == p.N;
 }
 
 static int column_sums(const GemmProblem& p, cudaStream_t st) {
