@@ -200,6 +200,13 @@ int mle_pad_crop(const float* x, float* y, int batch, int depth, int a, int b, i
  * (OneHotEmbeddings, Engine/kernels.cu:1551-1560). */
 int mle_embedding_gather(const int32_t* keys, const float* table, float* out, int64_t n_keys,
                          int dim, mle_stream_t stream);
+/* The gather followed by the positional table's broadcast add
+ * (MatrixPositionalEncoding forward, Engine/engine.cu:1272-1290, over the
+ * gathered rows): out[i, :] = table[keys[i], :] + pe[i % seq, :], bitwise
+ * mle_embedding_gather then mle_rows_add_table.  dim a multiple of 4 and
+ * 16-byte aligned table, pe and out (else MLE_ERR_UNSUPPORTED). */
+int mle_embedding_gather_add(const int32_t* keys, const float* table, const float* pe, float* out, int64_t n_keys,
+                             int dim, int seq, mle_stream_t stream);
 int mle_one_hot(const int32_t* keys, float* out, int64_t n_keys, int vocab, mle_stream_t stream);
 
 /* z = x * y (accumulate = 0) or z += x * y (1), elementwise: mulKernel

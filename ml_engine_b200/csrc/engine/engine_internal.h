@@ -61,6 +61,11 @@ struct NodeExt {
     float* ln_sq = nullptr;
     int ln_dims[4] = {0, 0, 0, 0};
     float ln_eps = 0.0f;
+    // MatrixPositionalEncoding: its table; output written by the gather
+    // that feeds it (pe_fed), its forward then idle
+    const float* pe_table = nullptr;
+    bool pe_fed = false;
+    bool grad_unused = false;  // nothing reads this node's gradient (a frozen input)
 };
 NodeExt& ext(const NodeBackProp* n);
 void forget_ext(const NodeBackProp* n);

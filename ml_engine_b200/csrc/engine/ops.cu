@@ -215,10 +215,15 @@ graph GraphOperations::MatrixPositionalEncoding(const graph& X, const int start_
     float* table = arena_alloc(ARENA_ACT, (int64_t)rows * cols, "MatPE table");
     check(mle_matpe_table(table, rows, cols, start_idx, st()), "MatPE table");
     const int64_t row_elems = (int64_t)rows * cols;
+    ext(nd).pe_table = table;
     node->forward = [=]() {
+        if (ext(nd).pe_fed) return;  // the gather feeding it added the table
         check(mle_rows_add_table(xp->output, table, nd->output, batch, row_elems, st()), "MatPE");
     };
-    node->backward = [=]() { check(mle_accumulate(nd->grad, xp->grad, nd->total, 1.0, st()), "MatPE backward"); };
+    node->backward = [=]() {
+        if (ext(xp).grad_unused) return;  // a frozen input: its gradient has no reader
+        check(mle_accumulate(nd->grad, xp->grad, nd->total, 1.0, st()), "MatPE backward");
+    };
     node->zero_grad = [nd]() { zero_range(nd->grad, nd->total); };
     node->free = [nd]() { nd->clear(); };
     return node;

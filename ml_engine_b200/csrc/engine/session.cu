@@ -61,6 +61,7 @@ struct Session {
     std::vector<Input> inputs;
     std::vector<std::function<void()>> prep;
     std::vector<std::pair<float*, int64_t>> emb;
+    std::vector<int32_t*> emb_keys;  // the token ids each table gathers with (same order as emb)
     // token tables trained by the embedding SGD update (desc.embed_lr > 0)
     struct EmbTrain {
         int32_t* keys;
@@ -238,6 +239,7 @@ graph token_input(Session& S, const std::string& name, int vocab, bool train = f
     S.emb.push_back({table, (int64_t)vocab * D});
     int32_t* keys = (int32_t*)arena_alloc_bytes(ARENA_WS, (int64_t)B * Sq * 4, name + " keys");
     add_input(S, name, 1, (int64_t)B * Sq, keys);
+    S.emb_keys.push_back(keys);
     NodeBackProp* nd = node.get();
     const int64_t nk = (int64_t)B * Sq;
     S.prep.push_back([=]() { check(mle_embedding_gather(keys, table, nd->output, nk, D, st()), "GatherEmbeddings"); });
@@ -247,6 +249,34 @@ graph token_input(Session& S, const std::string& name, int vocab, bool train = f
         S.emb_train.push_back({keys, table, nd, gsum, nk, (int64_t)vocab * D, D, Sq, vocab});
     }
     return node;
+}
+
+// token ids -> gathered embeddings -> MatrixPositionalEncoding, the gather
+// and the positional add as one pass writing the positional node's output
+// (the embedding node's own output then has no reader); a frozen table's
+// node has no gradient reader either, so the positional backward skips it.
+graph token_input_pe(Session& S, const std::string& name, int vocab, bool train = false) {
+    graph e = token_input(S, name, vocab, train);
+    graph pe = GraphOperations::MatrixPositionalEncoding(e);
+    if (!train) ext(e.get()).grad_unused = true;
+    const int Sq = S.d.seq_len, D = S.d.d_model;
+    const int32_t* keys = S.emb_keys.back();
+    const float* table = S.emb.back().first;
+    NodeBackProp* pn = pe.get();
+    const float* pet = ext(pn).pe_table;
+    const int64_t nk = (int64_t)S.d.batch * Sq;
+    auto gather = S.prep.back();
+    S.prep.back() = [=]() {
+        const int s = mle_embedding_gather_add(keys, table, pet, pn->output, nk, D, Sq, st());
+        if (s == MLE_ERR_UNSUPPORTED) {  // the two launches
+            ext(pn).pe_fed = false;
+            gather();
+            return;
+        }
+        check(s, "GatherEmbeddings + MatPE");
+        ext(pn).pe_fed = true;
+    };
+    return pe;
 }
 
 // EmbeddingUpdate after the backward pass: the step's gradient rows summed
@@ -309,7 +339,7 @@ void build(Session& S) {
         graph logits = l2->forward(GraphOperations::RELU(l1->forward(x)));
         S.loss = class_loss(S, logits, "labels", d.batch, 1, d.classes);
     } else if (d.config == MLE_CFG_ENCODER) {
-        graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tokens", d.vocab, d.embed_lr > 0));
+        graph x = token_input_pe(S, "tokens", d.vocab, d.embed_lr > 0);
         for (int l = 0; l < d.layers; ++l) x = encoder_block(S, x, d.seq_len, "Enc" + std::to_string(l));
         Linear* proj = new_linear(S, d.d_model, d.vocab, "Projection");
         S.loss = class_loss(S, proj->forward(x), "targets", d.batch, d.seq_len, d.vocab);
@@ -337,9 +367,9 @@ void build(Session& S) {
         graph y = new_conv(S, w, C, 1, 1, 0, "Output Convolution")->forward(d2);
         S.loss = GraphOperations::MeanSquaredError(y, target, true);
     } else if (d.config == MLE_CFG_ENCDEC) {
-        graph e = GraphOperations::MatrixPositionalEncoding(token_input(S, "src", d.vocab, d.embed_lr > 0));
+        graph e = token_input_pe(S, "src", d.vocab, d.embed_lr > 0);
         for (int l = 0; l < d.layers; ++l) e = encoder_block(S, e, d.seq_len, "Enc" + std::to_string(l));
-        graph x = GraphOperations::MatrixPositionalEncoding(token_input(S, "tgt_in", d.vocab));
+        graph x = token_input_pe(S, "tgt_in", d.vocab);
         for (int l = 0; l < d.layers; ++l) x = decoder_block(S, x, e, d.seq_len, "Dec" + std::to_string(l));
         Linear* proj = new_linear(S, d.d_model, d.vocab, "Projection");
         S.loss = class_loss(S, proj->forward(x), "tgt_out", d.batch, d.seq_len, d.vocab);

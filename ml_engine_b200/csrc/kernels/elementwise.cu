@@ -660,6 +660,24 @@ __global__ void gather_kernel(const int32_t* __restrict__ keys, const float* __r
     }
 }
 
+// out[r, :] = table[keys[r], :] (0 for a key < 0) + pe[r % seq, :]: the
+// gather and the positional table's add in one pass, four floats a thread
+__global__ void gather_add_kernel(const int32_t* __restrict__ keys, const float* __restrict__ table,
+                                  const float* __restrict__ pe, float* __restrict__ out, int64_t total4, int dim4,
+                                  int seq) {
+    pdl_entry();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += stride) {
+        const int64_t row = i / dim4;
+        const int c = (int)(i - row * dim4);
+        const int k = keys[row];
+        const float4 e = (k < 0) ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                 : reinterpret_cast<const float4*>(table)[(int64_t)k * dim4 + c];
+        const float4 q = reinterpret_cast<const float4*>(pe)[(row % seq) * dim4 + c];
+        reinterpret_cast<float4*>(out)[i] = make_float4(e.x + q.x, e.y + q.y, e.z + q.z, e.w + q.w);
+    }
+}
+
 // gsum[keys[r], :] += grad[r, :] for every gradient row r whose key is >= 0
 // (token t of batch b reads its key at keys[b * key_stride + t]); rows that
 // share a key meet in atomic adds.
@@ -1121,6 +1139,17 @@ int mle_embedding_gather(const int32_t* keys, const float* table, float* out, in
     const int64_t total = n_keys * dim;
     if (total == 0) return MLE_OK;
     launch_k(gather_kernel, grid_for(total, kThreads), kThreads, 0, as_stream(stream), keys, table, out, total, dim);
+    return launch_status();
+}
+
+int mle_embedding_gather_add(const int32_t* keys, const float* table, const float* pe, float* out, int64_t n_keys,
+                             int dim, int seq, mle_stream_t stream) {
+    if (n_keys < 0 || dim <= 0 || seq <= 0 || !keys || !table || !pe || !out) return MLE_ERR_ARG;
+    if (dim % 4 != 0 || !aligned16(table) || !aligned16(pe) || !aligned16(out)) return MLE_ERR_UNSUPPORTED;
+    if (n_keys == 0) return MLE_OK;
+    const int64_t total4 = n_keys * (dim / 4);
+    launch_k(gather_add_kernel, grid_for(total4, kThreads), kThreads, 0, as_stream(stream), keys, table, pe, out,
+             total4, dim / 4, seq);
     return launch_status();
 }
 

@@ -90,3 +90,25 @@ def test_embedding_gather_masked_rows_are_zero(cuda, ops, orc, rng):
     torch.cuda.synchronize()
     assert np.array_equal(H(out), orc.embedding_gather(keys, table))
     assert not H(out)[[3, 50, 299]].any()
+
+
+@pytest.mark.parametrize("batch,seq,dim", [(32, 128, 256), (3, 37, 64), (2, 256, 512)])
+def test_gather_with_positional_add_matches_two_launches(cuda, ops, rng, batch, seq, dim):
+    """The gather and the positional table's add in one pass (what the
+    sessions run for token inputs) against mle_embedding_gather followed by
+    mle_rows_add_table: bit for bit, masked keys included."""
+    from ml_engine_b200._lib import kernels
+    keys = rng.integers(0, 500, batch * seq).astype(np.int32)
+    keys[::17] = -1
+    table = T(rng.standard_normal((500, dim)).astype(np.float32), cuda)
+    pe = torch.empty(seq * dim, device=cuda)
+    ops.matpe_table(pe, seq, dim)
+    k = T(keys, cuda)
+    out = torch.full((batch * seq, dim), 7.0, device=cuda)
+    kernels().call("mle_embedding_gather_add", k.data_ptr(), table.data_ptr(), pe.data_ptr(), out.data_ptr(),
+                   batch * seq, dim, seq, torch.cuda.current_stream().cuda_stream)
+    g = torch.empty(batch * seq, dim, device=cuda)
+    ops.embedding_gather(k, table, g)
+    ref = torch.empty_like(g)
+    ops.rows_add_table(g, pe, ref, batch)
+    assert torch.equal(out, ref)
