@@ -308,7 +308,7 @@ NodeBackProp::NodeBackProp(str name, int batch, int d1, int d2, int d3, int allo
         output = nullptr;
         grad = nullptr;
     }
-    forget_ext(this);
+    node_born(this);
 }
 
 NodeBackProp::~NodeBackProp() { forget_ext(this); }

@@ -69,6 +69,7 @@ struct NodeExt {
 };
 NodeExt& ext(const NodeBackProp* n);
 void forget_ext(const NodeBackProp* n);
+void node_born(const NodeBackProp* n);
 
 // Decides the Linear -> activation bias-gradient fusion for a node list:
 // an activation whose input is a biased Linear output consumed by nothing

@@ -10,6 +10,7 @@
 #include <stdio.h>
 
 #include <unordered_map>
+#include <unordered_set>
 
 #include "engine.h"
 #include "engine_internal.h"
@@ -26,7 +27,20 @@ static std::unordered_map<const NodeBackProp*, NodeExt>& ext_map() {
     return *m;
 }
 NodeExt& ext(const NodeBackProp* n) { return ext_map()[n]; }
-void forget_ext(const NodeBackProp* n) { ext_map().erase(n); }
+
+// Every live node, so that a plan can see consumers outside its own graph.
+static std::unordered_set<const NodeBackProp*>& live_nodes() {
+    static auto* s = new std::unordered_set<const NodeBackProp*>();
+    return *s;
+}
+void node_born(const NodeBackProp* n) {
+    ext_map().erase(n);
+    live_nodes().insert(n);
+}
+void forget_ext(const NodeBackProp* n) {
+    ext_map().erase(n);
+    live_nodes().erase(n);
+}
 
 void prepare_fusions(const graph_tree& nodes) {
     std::unordered_map<const NodeBackProp*, int> consumers;
@@ -37,6 +51,12 @@ void prepare_fusions(const graph_tree& nodes) {
             consumers[in.get()]++;
             first_writer[in.get()] = n.get();
         }
+    // consumers anywhere: a node that another graph also reads may have its
+    // gradient written by that graph's backward between this graph's
+    // zero_grad and its first writer, so it is cleared and accumulated
+    std::unordered_map<const NodeBackProp*, int> all_consumers;
+    for (const NodeBackProp* n : live_nodes())
+        for (auto& in : n->inputs) all_consumers[in.get()]++;
     for (auto& n : nodes) {
         NodeExt& e = ext(n.get());
         if (e.kind == OP_LINEAR) e.bias_grad_fused = false;
@@ -71,6 +91,7 @@ void prepare_fusions(const graph_tree& nodes) {
             const NodeBackProp* x = n.get();
             auto it = first_writer.find(x);
             if (it == first_writer.end() || !x->grad) continue;
+            if (all_consumers[x] != consumers[x]) continue;  // shared with another graph
             const NodeBackProp* w = it->second;
             NodeExt& we = ext(w);
             int pos = -1, seen = 0;

@@ -37,3 +37,34 @@ def test_reference_style_program_trains(tmp_path):
     r = subprocess.run([str(out)], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "usecase ok" in r.stdout
+
+
+TWO = ROOT / "tests" / "cpp" / "two_graphs.cu"
+
+
+def test_two_graph_program_compiles_and_links(tmp_path):
+    sys.path.insert(0, str(ROOT / "tests" / "cpp"))
+    import build as cppbuild
+    out = tmp_path / "two_graphs"
+    cppbuild.build(TWO, out)
+    assert out.exists()
+
+
+@pytest.mark.gpu
+def test_shared_node_gradient_is_cleared_and_accumulated_across_graphs(tmp_path):
+    """Two GraphOperations share a node; graph A's first writer of its
+    gradient is an activation (which may assign), graph B's a Scale (which
+    adds).  Both zero_grads run, then B's backward, then A's: the node's
+    gradient must be the sum of both contributions (tests/cpp/two_graphs.cu),
+    so neither graph may leave a gradient uncleared that another graph's
+    backward writes."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    sys.path.insert(0, str(ROOT / "tests" / "cpp"))
+    import build as cppbuild
+    out = tmp_path / "two_graphs"
+    cppbuild.build(TWO, out)
+    r = subprocess.run([str(out)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "two graphs ok" in r.stdout
