@@ -520,10 +520,15 @@ def cpu_step_times(wl, B_full, n_steps, warm=1, params=None):
 
 
 def cpu_cores():
-    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    """Every host core for the oracle's loops (a launcher such as torchrun
+    pins OMP_NUM_THREADS to 1 per rank; the CPU arm runs on rank 0 alone);
+    returns the thread count in force."""
+    from oracle import ops as orc
+    return orc.set_threads(os.cpu_count() or 1)
 
 
 def cpu_baseline_leg(wl, B_full, seconds):
+    cores = cpu_cores()
     times, sb = [], None
     t0 = time.perf_counter()
     while not times or time.perf_counter() - t0 < seconds:
@@ -532,7 +537,7 @@ def cpu_baseline_leg(wl, B_full, seconds):
     full = sum(t for t, _ in times) / len(times)
     spent = sum(s for _, s in times)
     unit = "sequences" if wl != "mlp" else "images"
-    return {"value": 1.0 / full, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
+    return {"value": 1.0 / full, "unit": "steps/s", "cores": cores, "kind": "port",
             "sample": f"{len(times)} sampled steps: forward+backward on {sb} of {B_full} {unit} scaled x{B_full // sb}, "
                       f"plus the clip + AdamW over all parameters once per step; {spent:.1f}s of host time"}
 
@@ -544,6 +549,7 @@ def run_reference(args, rank, world):
     B = local_batch(wl, world)
     n_gpu_b = B * world
     # the reference arm runs the whole job's batch (all ranks' shares) on the host
+    cores = cpu_cores()
     times, sb = cpu_step_times(wl, n_gpu_b, args.steps, warm=min(args.warmup, 1))
     full = sum(t for t, _ in times) / len(times)
     value = 1.0 / full
@@ -553,7 +559,7 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * full,
         "higher_is_better": True, "scaling": WORKLOADS[wl]["scaling"], "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": config_dict(wl, world),
-        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": cores, "kind": "port",
                          "sample": f"per step: forward+backward on {sb} of {n_gpu_b} {unit}, scaled "
                                    f"x{n_gpu_b // sb}, plus the clip + AdamW over all parameters; "
                                    f"{min(args.warmup, 1)} warm-up sample"},

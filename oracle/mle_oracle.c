@@ -19,7 +19,24 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* Threads of the parallel loops below: n > 0 sets it for the calling
+ * thread's later regions (a launcher may have pinned OMP_NUM_THREADS to 1);
+ * returns the count in force. */
+int oracle_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}
 
 #define ORACLE_PI 3.14159265359f
 
@@ -269,9 +286,13 @@ void oracle_bcmm(int variant, const float* A, const float* B, float* C, int batc
 /* Plain row-major GEMM used by the Linear layer oracles: C (=|+=) op(A) op(B) */
 void oracle_gemm(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int trans_a, int trans_b,
                  int accumulate) {
-#pragma omp parallel for schedule(static)
+#pragma omp parallel
+    {
+    /* one row of double accumulators per thread, on the heap: a row of a
+     * wide product does not fit a thread's stack */
+    double* acc = (double*)malloc(sizeof(double) * (size_t)(N > 0 ? N : 1));
+#pragma omp for schedule(static)
     for (int64_t r = 0; r < M; ++r) {
-        double* acc = (double*)__builtin_alloca(sizeof(double) * (size_t)N);
         for (int64_t col = 0; col < N; ++col) acc[col] = 0.0;
         for (int64_t k = 0; k < K; ++k) {
             const double av = trans_a ? A[k * M + r] : A[r * K + k];
@@ -287,6 +308,8 @@ void oracle_gemm(const float* A, const float* B, float* C, int64_t M, int64_t N,
             if (accumulate) C[r * N + col] += (float)acc[col];
             else C[r * N + col] = (float)acc[col];
         }
+    }
+    free(acc);
     }
 }
 

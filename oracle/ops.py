@@ -201,6 +201,11 @@ def bcmm(variant, A, B, C, batch, channels, m, n, p, backward, A_case, B_case, C
     return C
 
 
+def set_threads(n):
+    """OpenMP threads of the oracle's loops (n <= 0: query); returns the count."""
+    return int(lib().oracle_set_threads(int(n)))
+
+
 def gemm(A, B, C, M, N, K, trans_a=0, trans_b=0, accumulate=False):
     lib().oracle_gemm(_p(f32(A)), _p(f32(B)), _p(C), M, N, K, trans_a, trans_b, int(accumulate))
     return C
