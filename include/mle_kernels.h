@@ -614,6 +614,23 @@ int mle_col2im(const float* cols, float* x, int batch, int channels, int h, int 
  * [a][b][c] -> [b][a][c], mode 1 [a][b][c] -> [a][c][b]. */
 int mle_swap_dims(const float* in, float* out, int a, int b, int c, int mode, mle_stream_t stream);
 
+/* Stride-2 convolutions (mle_conv2d_fwd / _bwd) in tensor-core mode as the
+ * stride-1 implicit GEMM over the input's polyphase sub-images -- phase
+ * (py, px) = x[2Y + py][2X + px] becomes a block of channels, each tap
+ * (kh, kw) a tap of a kernel of ceil-half size with top/left padding only
+ * -- with a one-pass phase split (and a phase merge of dx); the weights are
+ * expanded to and dW folded back from that kernel.  2: always; 1: where
+ * that kernel has no empty taps (1x1 and 2x2 kernels: a pure re-layout; a
+ * 3x3 kernel runs 16 products per output for 9); 0 (default): never
+ * (im2col + GEMM + col2im, which measured faster on the U-Net step: 5.07 ms
+ * against 5.11 ms with 1 and 5.24 ms with 2).  Shapes the implicit path
+ * cannot take fall
+ * back to im2col.  Per host thread; the forward and the backward of one
+ * convolution must see the same setting (they share the workspace layout).
+ * No counterpart in the reference. */
+int mle_set_conv_phase(int enable);
+int mle_get_conv_phase(void);
+
 /* Convolute2D (Engine/engine.cu:3732-3817): weights [cout][cin][kh][kw],
  * x [batch][cin][h][w], y [batch][cout][OH][OW].
  *   forward : y = conv(x) (+ bias) (assigned, CV2D Engine/kernels.cu:985-1019);

@@ -180,6 +180,124 @@ __global__ void conv_weight_pack_kernel(const float* __restrict__ in, float* __r
     }
 }
 
+// ------------------------------------------------------------ stride 2
+// A stride-2 convolution is a stride-1 convolution over the polyphase
+// sub-images of its input: phase (py, px) holds x[2Y + py][2X + px], and a
+// tap (kh, kw) with kh - pad = 2a + py, kw - pad = 2b + px reads phase
+// (py, px) at (oy + a, ox + b).  The phases in use (those some tap reads)
+// become the channels of one image, c' = phase * Cin + ci, and the taps
+// collapse onto a KH2 x KW2 kernel whose top/left padding is -min a.
+struct PhaseGeom {
+    int h2, w2;        // phase image size
+    int py0, npy;      // rows phases in use: py0 .. py0 + npy - 1
+    int px0, npx;
+    int k2, pad2;      // virtual square kernel and its top/left padding
+    int oh, ow;        // the stride-2 output size
+    int nph() const { return npy * npx; }
+};
+
+__host__ __device__ inline int floor_half(int a) { return a >= 0 ? a / 2 : -((1 - a) / 2); }
+
+// false where the virtual kernel is not square with one padding
+bool phase_geom(int h, int w, int kh, int kw, int pad, PhaseGeom& g) {
+    auto axis = [&](int k, int& p0, int& np, int& k2, int& pad2) {
+        const int amin = floor_half(-pad), amax = floor_half(k - 1 - pad);
+        k2 = amax - amin + 1;
+        pad2 = -amin;
+        const int r0 = ((-pad) % 2 + 2) % 2;  // phase of tap 0
+        np = k > 1 ? 2 : 1;
+        p0 = np == 2 ? 0 : r0;
+    };
+    int k2h, p2h, k2w, p2w;
+    axis(kh, g.py0, g.npy, k2h, p2h);
+    axis(kw, g.px0, g.npx, k2w, p2w);
+    if (k2h != k2w || p2h != p2w) return false;
+    g.k2 = k2h;
+    g.pad2 = p2h;
+    g.h2 = (h + 1) / 2;
+    g.w2 = (w + 1) / 2;
+    g.oh = (h + 2 * pad - kh) / 2 + 1;
+    g.ow = (w + 2 * pad - kw) / 2 + 1;
+    return g.oh > 0 && g.ow > 0;
+}
+
+// P[n][(iy * npx + ix) * C + c][Y][X] = x[n][c][2Y + py0 + iy][2X + px0 + ix] (0 outside)
+__global__ void phase_split_kernel(const float* __restrict__ x, float* __restrict__ P, int C, int H, int W, int H2,
+                                   int W2, int py0, int npy, int px0, int npx, int64_t total) {
+    pdl_entry();
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        const int X = (int)(i % W2);
+        int64_t r = i / W2;
+        const int Y = (int)(r % H2);
+        r /= H2;
+        const int cp = (int)(r % ((int64_t)npy * npx * C));
+        const int64_t n = r / ((int64_t)npy * npx * C);
+        const int ph = cp / C, c = cp - ph * C;
+        const int y = 2 * Y + py0 + ph / npx, xx = 2 * X + px0 + ph % npx;
+        P[i] = (y < H && xx < W) ? x[((n * C + c) * H + y) * W + xx] : 0.f;
+    }
+}
+
+// dx[n][c][y][x] (= or +=) dP[n][phase(y, x) * C + c][y / 2][x / 2]; a
+// pixel of an unused phase receives nothing (0 when assigned)
+__global__ void phase_merge_kernel(const float* __restrict__ dP, float* __restrict__ dx, int C, int H, int W, int H2,
+                                   int W2, int py0, int npy, int px0, int npx, int accumulate, int64_t total) {
+    pdl_entry();
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        const int xx = (int)(i % W);
+        int64_t r = i / W;
+        const int y = (int)(r % H);
+        r /= H;
+        const int c = (int)(r % C);
+        const int64_t n = r / C;
+        const int iy = (y & 1) - py0, ix = (xx & 1) - px0;
+        float v = 0.f;
+        if (iy >= 0 && iy < npy && ix >= 0 && ix < npx)
+            v = dP[((n * npy * npx + iy * npx + ix) * C + c) * (int64_t)H2 * W2 + (int64_t)(y >> 1) * W2 + (xx >> 1)];
+        dx[i] = accumulate ? dx[i] + v : v;
+    }
+}
+
+// mode 0 (expand): W2[co][(iy*npx+ix)*Cin + ci][th][tw] = W[co][ci][kh][kw],
+//   kh = 2 (th - pad2) + py0 + iy + pad (0 where kh or kw falls outside);
+// mode 1 (contract): W[co][ci][kh][kw] = W2[co][c'][th][tw] for the one
+//   virtual tap each real tap maps to (assigned)
+__global__ void phase_weights_kernel(const float* __restrict__ in, float* __restrict__ out, int Cout, int Cin, int KH,
+                                     int KW, int pad, int k2, int pad2, int py0, int npy, int px0, int npx, int mode,
+                                     int64_t total) {
+    pdl_entry();
+    const int nph = npy * npx;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+        if (mode == 0) {
+            const int tw = (int)(i % k2);
+            int64_t r = i / k2;
+            const int th = (int)(r % k2);
+            r /= k2;
+            const int cp = (int)(r % ((int64_t)nph * Cin));
+            const int co = (int)(r / ((int64_t)nph * Cin));
+            const int ph = cp / Cin, ci = cp - ph * Cin;
+            const int kh = 2 * (th - pad2) + py0 + ph / npx + pad, kw = 2 * (tw - pad2) + px0 + ph % npx + pad;
+            out[i] = (kh >= 0 && kh < KH && kw >= 0 && kw < KW) ? in[(((int64_t)co * Cin + ci) * KH + kh) * KW + kw]
+                                                                 : 0.f;
+        } else {
+            const int kw = (int)(i % KW);
+            int64_t r = i / KW;
+            const int kh = (int)(r % KH);
+            r /= KH;
+            const int ci = (int)(r % Cin);
+            const int co = (int)(r / Cin);
+            const int ah = floor_half(kh - pad), aw = floor_half(kw - pad);
+            const int py = kh - pad - 2 * ah, px = kw - pad - 2 * aw;
+            const int ph = (py - py0) * npx + (px - px0);
+            const int th = ah + pad2, tw = aw + pad2;
+            out[i] = in[((((int64_t)co * nph + ph) * Cin + ci) * k2 + th) * k2 + tw];
+        }
+    }
+}
+
 // out = in with two of its three dimensions exchanged:
 //   mode 0: [A][B][C] -> [B][A][C];  mode 1: [A][B][C] -> [A][C][B]
 __global__ void swap_dims_kernel(const float* __restrict__ in, float* __restrict__ out, int A, int B, int C, int mode,
@@ -268,16 +386,19 @@ int64_t r4(int64_t n) { return (n + 3) & ~int64_t(3); }
 // S (kept from the forward for the backward), the packed weights (also the
 // dW staging) and the copies of dy.
 struct ConvPlan {
-    int oh, ow, taps, cin4, cout4;
+    int h, oh, ow, taps, cin4, cout4;
     bool in_place;            // KW == 1 and pad == 0: no shifted copies
     int64_t xs, wp, wd, dys;  // workspace offsets (floats)
     int64_t floats;
 };
 
-ConvPlan conv_plan(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad) {
+// oh, ow >= 0: an output smaller than the padded one (the stride-2 phase
+// form, whose padding is top/left only)
+ConvPlan conv_plan(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int oh = -1, int ow = -1) {
     ConvPlan p;
-    p.oh = h + 2 * pad - kh + 1;
-    p.ow = w + 2 * pad - kw + 1;
+    p.h = h;
+    p.oh = oh >= 0 ? oh : h + 2 * pad - kh + 1;
+    p.ow = ow >= 0 ? ow : w + 2 * pad - kw + 1;
     p.taps = kh * kw;
     p.cin4 = (int)r4(cin);
     p.cout4 = (int)r4(cout);
@@ -338,7 +459,7 @@ ConvGemm conv_dx_gemm(const ConvPlan& p, const float* dy, float* ws, float* dx, 
     g.KW = kw;
     g.pad = kh - 1 - pad;
     g.nb = batch;
-    g.P = (p.oh + kh - 1 - 2 * pad) * w;  // = h * w
+    g.P = p.h * w;
     g.lda = p.cout4;
     g.accumulate = 1;
     return g;
@@ -360,12 +481,94 @@ bool conv_implicit_ok(const float* x, float* ws, int batch, int cin, int h, int 
     return conv_gemm_supported(f) && conv_gemm_supported(d) && conv_gemm_supported(g);
 }
 
+// Plan of the stride-2 phase form: the stride-1 plan over the phase image
+// (nph * Cin channels of h2 x w2, a k2 x k2 kernel, top/left padding pad2,
+// the stride-2 output size), plus the phase image (dP in the backward), the
+// expanded weights and the expanded dW.
+struct PhasePlan {
+    PhaseGeom g;
+    ConvPlan p;
+    int cin2;
+    int64_t pP, pdP, pWe, pWd, floats;
+};
+
+bool phase_plan(int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, PhasePlan& q) {
+    if (!phase_geom(h, w, kh, kw, pad, q.g)) return false;
+    const PhaseGeom& g = q.g;
+    if (g.k2 - 1 - g.pad2 < 0) return false;
+    q.cin2 = g.nph() * cin;
+    q.p = conv_plan(batch, q.cin2, g.h2, g.w2, cout, g.k2, g.k2, g.pad2, g.oh, g.ow);
+    const int64_t nw = (int64_t)cout * q.cin2 * g.k2 * g.k2;
+    q.pP = q.p.floats;
+    // dP apart from the phase image: dW may read the image (in place) while dx runs
+    q.pdP = q.pP + r4((int64_t)batch * q.cin2 * g.h2 * g.w2);
+    q.pWe = q.pdP + r4((int64_t)batch * q.cin2 * g.h2 * g.w2);
+    q.pWd = q.pWe + r4(nw);
+    q.floats = q.pWd + r4(nw);
+    return true;
+}
+
+// The phase form runs for stride 2 when its three products are supported,
+// on the same conditions as the stride-1 implicit path (the forward and the
+// backward make the same choice).
+// stride 2 through the phase form: 0 never (im2col, the default: it
+// measured faster on the U-Net step), 1 where the phase kernel has no empty
+// taps (phases x taps of the phase kernel = the real taps: 1x1 and 2x2
+// kernels; a 3x3 kernel at pad 1 runs 16 products per output for 9), 2
+// always
+static thread_local int g_conv_phase = 0;
+
+bool phase_implicit_ok(float* ws, int batch, int cin, int h, int w, int cout, int kh, int kw, int pad, int stride) {
+    PhasePlan q;
+    if (!g_conv_phase || stride != 2 || !phase_plan(batch, cin, h, w, cout, kh, kw, pad, q)) return false;
+    if (g_conv_phase == 1 && q.g.nph() * q.g.k2 * q.g.k2 != kh * kw) return false;
+    const ConvPlan& p = q.p;
+    const PhaseGeom& g = q.g;
+    const float* P = ws + q.pP;
+    const ConvGemm f = conv_fwd_gemm(p, P, ws, ws, batch, q.cin2, g.h2, cout, g.k2, g.k2, g.pad2);
+    const ConvGemm d = conv_dx_gemm(p, p.in_place ? P : ws, ws, ws + q.pdP, batch, q.cin2, g.w2, cout, g.k2, g.k2,
+                                    g.pad2);
+    const ConvGemm gw = conv_dw_gemm(p, P, ws, ws, batch, q.cin2, g.h2, cout, g.k2, g.k2, g.pad2);
+    return conv_gemm_supported(f) && conv_gemm_supported(d) && conv_gemm_supported(gw);
+}
+
+int phase_split(const float* x, float* P, int n, int c, int h, int w, const PhaseGeom& g, cudaStream_t st) {
+    const int64_t total = (int64_t)n * g.nph() * c * g.h2 * g.w2;
+    launch_k(phase_split_kernel, grid_for(total, kT), kT, 0, st, x, P, c, h, w, g.h2, g.w2, g.py0, g.npy, g.px0,
+             g.npx, total);
+    return launch_status();
+}
+
+int phase_merge(const float* dP, float* dx, int n, int c, int h, int w, const PhaseGeom& g, int accumulate,
+                cudaStream_t st) {
+    const int64_t total = (int64_t)n * c * h * w;
+    launch_k(phase_merge_kernel, grid_for(total, kT), kT, 0, st, dP, dx, c, h, w, g.h2, g.w2, g.py0, g.npy, g.px0,
+             g.npx, accumulate, total);
+    return launch_status();
+}
+
+int phase_weights(const float* in, float* out, int cout, int cin, int kh, int kw, int pad, const PhaseGeom& g,
+                  int mode, cudaStream_t st) {
+    const int64_t total = mode == 0 ? (int64_t)cout * g.nph() * cin * g.k2 * g.k2 : (int64_t)cout * cin * kh * kw;
+    launch_k(phase_weights_kernel, grid_for(total, kT), kT, 0, st, in, out, cout, cin, kh, kw, pad, g.k2, g.pad2,
+             g.py0, g.npy, g.px0, g.npx, mode, total);
+    return launch_status();
+}
+
 }  // namespace
 }  // namespace mle
 
 using namespace mle;
 
 extern "C" {
+
+int mle_set_conv_phase(int enable) {
+    if (enable < 0 || enable > 2) return MLE_ERR_ARG;
+    g_conv_phase = enable;
+    return MLE_OK;
+}
+
+int mle_get_conv_phase(void) { return g_conv_phase; }
 
 int mle_conv_out_size(int in, int k, int pad, int stride) {
     if (stride <= 0 || in + 2 * pad < k) return -1;
@@ -404,6 +607,8 @@ int64_t mle_conv2d_workspace_floats(int batch, int cin, int h, int w, int cout, 
     // dx and dw/db parts of the backward may run concurrently.
     int64_t n = 2 * (int64_t)batch * cin * kh * kw * oh * ow;
     if (stride == 1) n = std::max(n, conv_plan(batch, cin, h, w, cout, kh, kw, pad).floats);
+    PhasePlan q;
+    if (stride == 2 && phase_plan(batch, cin, h, w, cout, kh, kw, pad, q)) n = std::max(n, q.floats);
     return n;
 }
 
@@ -415,6 +620,27 @@ int mle_conv2d_fwd(const float* x, const float* wgt, const float* bias, float* y
     cudaStream_t st = as_stream(stream);
     const int64_t P = (int64_t)oh * ow, K = (int64_t)cin * kh * kw;
     int s;
+    if (phase_implicit_ok(ws, batch, cin, h, w, cout, kh, kw, pad, stride)) {
+        // stride 2: the stride-1 implicit GEMM over the phase image
+        PhasePlan q;
+        phase_plan(batch, cin, h, w, cout, kh, kw, pad, q);
+        const ConvPlan& p = q.p;
+        const PhaseGeom& g = q.g;
+        float* Pimg = ws + q.pP;
+        s = phase_split(x, Pimg, batch, cin, h, w, g, st);
+        if (s) return s;
+        if (!p.in_place) {
+            s = shift_copies(Pimg, ws + p.xs, batch * q.cin2 * g.h2, g.w2, p.ow, g.k2, -g.pad2, st);
+            if (s) return s;
+        }
+        s = phase_weights(wgt, ws + q.pWe, cout, cin, kh, kw, pad, g, 0, st);
+        if (s) return s;
+        s = weight_pack(ws + q.pWe, ws + p.wp, cout, q.cin2, p.taps, p.cin4, 0, st);
+        if (s) return s;
+        ConvGemm gm = conv_fwd_gemm(p, Pimg, ws, y, batch, q.cin2, g.h2, cout, g.k2, g.k2, g.pad2);
+        gm.bias = bias;
+        return run_conv_gemm(gm, st);
+    }
     if (conv_implicit_ok(x, ws, batch, cin, h, w, cout, kh, kw, pad, stride)) {
         const ConvPlan p = conv_plan(batch, cin, h, w, cout, kh, kw, pad);
         if (!p.in_place) {
@@ -455,6 +681,44 @@ int mle_conv2d_bwd_assign(const float* x, const float* wgt, const float* dy, flo
     if (db) {
         s = mle_channel_bias_bwd(dy, nullptr, db, batch, cout, P, stream);
         if (s) return s;
+    }
+    if (phase_implicit_ok(ws, batch, cin, h, w, cout, kh, kw, pad, stride)) {
+        PhasePlan q;
+        phase_plan(batch, cin, h, w, cout, kh, kw, pad, q);
+        const ConvPlan& p = q.p;
+        const PhaseGeom& g = q.g;
+        float* Pimg = ws + q.pP;  // the forward's phase image
+        float* dP = ws + q.pdP;
+        const int taps2 = p.taps;
+        if (dw) {
+            // dW' over the forward's shifted phase copies (or the phase image
+            // itself), staged [tap][Cout][Cin2_4], unpacked to the expanded
+            // layout, then folded back onto the real taps (assigned)
+            if (cudaMemsetAsync(ws + p.wp, 0, sizeof(float) * (size_t)taps2 * cout * p.cin4, st) != cudaSuccess)
+                return launch_status();
+            s = run_conv_gemm(conv_dw_gemm(p, Pimg, dy, ws, batch, q.cin2, g.h2, cout, g.k2, g.k2, g.pad2), st);
+            if (s) return s;
+            s = weight_pack(ws + p.wp, ws + q.pWd, cout, q.cin2, taps2, p.cin4, 2, st);
+            if (s) return s;
+            s = phase_weights(ws + q.pWd, dw, cout, cin, kh, kw, pad, g, 1, st);
+            if (s) return s;
+        }
+        if (dx) {
+            if (!p.in_place) {
+                s = shift_copies(dy, ws + p.dys, batch * cout * p.oh, p.ow, g.w2, g.k2, -(g.k2 - 1 - g.pad2), st);
+                if (s) return s;
+            }
+            s = phase_weights(wgt, ws + q.pWe, cout, cin, kh, kw, pad, g, 0, st);
+            if (s) return s;
+            s = weight_pack(ws + q.pWe, ws + p.wd, cout, q.cin2, taps2, p.cout4, 1, st);
+            if (s) return s;
+            ConvGemm gm = conv_dx_gemm(p, dy, ws, dP, batch, q.cin2, g.w2, cout, g.k2, g.k2, g.pad2);
+            gm.accumulate = 0;
+            s = run_conv_gemm(gm, st);
+            if (s) return s;
+            return phase_merge(dP, dx, batch, cin, h, w, g, assign_dx ? 0 : 1, st);
+        }
+        return MLE_OK;
     }
     if (conv_implicit_ok(x, ws, batch, cin, h, w, cout, kh, kw, pad, stride)) {
         const ConvPlan p = conv_plan(batch, cin, h, w, cout, kh, kw, pad);

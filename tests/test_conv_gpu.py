@@ -15,6 +15,10 @@ CONV = [  # N, Cin, H, W, Cout, K, pad, stride
     (2, 3, 16, 16, 8, 3, 1, 1),      # first layer of a U-Net: 3 channels, two rows per 32-pixel block
     (4, 16, 32, 32, 32, 3, 1, 1),    # 3x3 implicit GEMM, one row per block
     (2, 32, 17, 13, 16, 3, 1, 2),    # stride-2 downsampling, odd sizes (im2col)
+    (2, 16, 64, 64, 32, 3, 1, 2),    # U-Net downsampling: the stride-1 implicit GEMM over the 4 phase images
+    (2, 32, 16, 16, 64, 1, 0, 2),    # strided 1x1 skip projection: one phase image, read in place
+    (2, 8, 15, 15, 16, 3, 1, 2),     # odd input, phases of 8 x 8
+    (1, 8, 32, 32, 32, 4, 1, 2),     # 4x4 taps: a 3x3 kernel per phase
     (2, 64, 8, 8, 32, 1, 0, 1),      # 1x1 skip projection read in place
     (2, 64, 64, 64, 64, 3, 1, 1),    # U-Net top level: 32 pixel tiles per image, half-height M tile
     (2, 192, 16, 16, 160, 3, 1, 1),  # two M tiles, six channel blocks per tap
@@ -53,6 +57,43 @@ def gemm_mode(request):
     yield mode
     k.mle_set_gemm_mode(old)
     k.mle_set_gemm_pairs(old_pairs)
+
+
+@pytest.mark.parametrize("case", [c for c in CONV if c[7] == 2])
+def test_conv2d_stride2_phase_form_matches_im2col(cuda, rng, case):
+    """The stride-2 phase form (stride-1 implicit GEMM over the polyphase
+    sub-images) against im2col + GEMM + col2im on the same inputs, TF32
+    mode: both products take the same TF32-rounded operand values, so y, dx
+    and dW differ only by fp32 summation order (and a shape the phase form
+    cannot take runs im2col both times).  Every case has at least 16 output
+    channels: narrower im2col products run on the fp32 CUDA-core GEMM."""
+    from ml_engine_b200 import ops
+    from ml_engine_b200._lib import kernels
+    k = kernels()
+    old_mode, old_phase = k.mle_get_gemm_mode(), k.mle_get_conv_phase()
+    N, Cin, Hh, W, Cout, K, pad, stride = case
+    x = T(rng.standard_normal((N, Cin, Hh, W)).astype(np.float32), cuda)
+    w = T((rng.standard_normal((Cout, Cin, K, K)) * 0.2).astype(np.float32), cuda)
+    b = T(rng.standard_normal(Cout).astype(np.float32), cuda)
+    OH, OW = ops.conv_out_size(Hh, K, pad, stride), ops.conv_out_size(W, K, pad, stride)
+    dy = T(rng.standard_normal((N, Cout, OH, OW)).astype(np.float32), cuda)
+    dx0 = T(rng.standard_normal((N, Cin, Hh, W)).astype(np.float32), cuda)
+    out = {}
+    try:
+        k.mle_set_gemm_mode(0)
+        for phase in (2, 0):  # forced for every stride-2 shape, then im2col
+            k.call("mle_set_conv_phase", phase)
+            y = torch.empty(N, Cout, OH, OW, device=cuda)
+            ws = ops.conv2d_workspace(x, w, pad, stride)
+            ops.conv2d_fwd(x, w, b, y, ws, pad, stride)
+            dx, dw, db = dx0.clone(), torch.zeros(Cout, Cin, K, K, device=cuda), torch.zeros(Cout, device=cuda)
+            ops.conv2d_bwd(x, w, dy, dx, dw, db, ws, pad, stride)
+            out[phase] = (H(y), H(dx), H(dw))
+    finally:
+        k.mle_set_gemm_mode(old_mode)
+        k.call("mle_set_conv_phase", old_phase)
+    for a, r, name in zip(out[2], out[0], ("y", "dx", "dW")):
+        assert norm_err(a, r) <= 1e-5, (name, norm_err(a, r))
 
 
 @pytest.mark.parametrize("case", CONV)
