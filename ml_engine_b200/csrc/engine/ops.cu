@@ -119,7 +119,9 @@ void prepare_fusions(const graph_tree& nodes) {
         if (e.kind != OP_ACTIVATION || n->inputs.size() != 1) continue;
         const NodeBackProp* L = n->inputs[0].get();
         NodeExt& le = ext(L);
-        if (le.kind == OP_LINEAR && le.linear_bias_grad && consumers[L] == 1) {
+        // (not when the Linear's weight-gradient product sums its dY's columns
+        // itself: the activation backward then stays a plain elementwise pass)
+        if (le.kind == OP_LINEAR && le.linear_bias_grad && consumers[L] == 1 && !mle_get_gemm_column_sums()) {
             e.fused_bias_target = le.linear_bias_grad;
             e.fused_rows = L->total / L->dim[3];
             e.fused_cols = L->dim[3];
