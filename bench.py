@@ -680,6 +680,14 @@ def run_sweep(args):
         tf = 4.0 * n ** 3 / (ms * 1e-3) / 1e12
         print(json.dumps({"sweep": "linear_bwd", "n": n, "ms": ms, "tflops": tf, "frac_of_tf32": tf / tf32_peak,
                           "frac_of_bf16": tf / bf16_peak, "peak_kind": kind}), flush=True)
+        if n >= 2048:
+            # with the bias gradient: summed by the dW product's epilogue warps
+            # (or a separate column-sum launch under --gemm-column-sums 0)
+            dB = torch.zeros(n, device=dev)
+            ms_b = timed(lambda: ops.linear_bwd(X, W, dY, dX, dW, dB, n, n, n), 20 if n >= 4096 else 100)
+            print(json.dumps({"sweep": "linear_bwd_bias", "n": n, "ms": ms_b, "ms_without_bias": ms,
+                              "bias_cost_us": 1e3 * (ms_b - ms), "peak_kind": kind}), flush=True)
+            del dB
         del X, W, dY, dX, dW
     rows = 65536
     # bias gradient (column sums) and the GELU backward fused with it, at

@@ -386,12 +386,19 @@ int mle_get_gemm_operand_rounding(void);
  * taken too (mle_linear_bwd, mle_linear_group_bwd with dW and dB): 1
  * (default) the epilogue warps of the dW product sum dY's columns from the
  * dY tiles as they pass through shared memory (in a CTA pair each CTA the
- * columns it staged), so dB uses the operand values the product uses --
+ * columns it staged; launches of at most one tile per CTA, else a separate
+ * column sum follows), so dB uses the operand values the product uses --
  * TF32-rounded under operand rounding 1, the fp32 values under 0; 0 a
  * separate column-sum launch of the fp32 dY (BCompress,
  * Engine/kernels.cu:1562-1584).  Per host thread. */
 int mle_set_gemm_column_sums(int enable);
 int mle_get_gemm_column_sums(void);
+/* 1 when the calling thread's last product took its column sums in its
+ * epilogue warps, 0 when a separate column-sum launch followed (or none was
+ * asked for).  The epilogue takes them only for launches of at most one
+ * tile per CTA: a CTA with several tiles would lose the overlap of one
+ * tile's epilogue with the next tile's mainloop. */
+int mle_gemm_last_column_sums(void);
 /* Forces the tile width (64, 128 or 256), the split-K count (1..64, as
  * many as the k-blocks allow) and CTA pairs (0/1) of this thread's plain
  * and grouped tensor-core products (convolutions keep the tile model);

@@ -617,7 +617,7 @@ def test_linear_bwd_bias_from_weight_product(cuda, ops, orc, rng, stage_kblocks,
         orc.gemm(X, dY, rdw, fin, fout, rows, 1, 0)
         ch = (ctypes.c_int * 3)()
         k.mle_gemm_last_choice(ch)
-        fused = k.mle_gemm_last_stage_kblocks() > 0  # the product ran on the tensor cores
+        fused = k.mle_gemm_last_column_sums() == 1  # summed by the product's epilogue warps
         rdb = orc.bias_grad(_tf32_rne(dY) if fused and rounding else dY, dB0.copy())
         assert rel_err(H(dW), rdw) <= RTOL_TC
         assert rel_err(H(dB), rdb) <= 1e-5
@@ -990,8 +990,9 @@ def _linear_group_case(cuda, ops, rng, n, rows, outs=None):
         dw, db = torch.zeros(din, o, device=cuda), torch.zeros(o, device=cuda)
         ops.linear_bwd(X, Ws[i], dYs[i], rX, dw, db, rows, din, o)
         assert norm_err(H(dWs[i]), H(dw)) <= RTOL_TC
-        # both bias gradients come from their dW products' TF32-rounded dY tiles
-        assert norm_err(H(dBs[i]), H(db)) <= 1e-5
+        # the bias gradients come from the dW products' TF32-rounded dY tiles,
+        # or from a separate fp32 column sum where a launch has more tiles than CTAs
+        assert norm_err(H(dBs[i]), H(db)) <= 1e-3
     assert norm_err(H(dX) - dX0, H(rX) - dX0) <= RTOL_TC
 
 
