@@ -152,3 +152,25 @@ def test_oracle_key_update_is_a_scatter_add():
     k = keys[:, :clen].ravel()
     np.add.at(want, k[k >= 0], -lr * grad[k >= 0].astype(np.float64))
     assert np.max(np.abs(got - want)) <= 1e-6 * np.max(np.abs(want))
+
+
+def test_oracle_gemm_one_thread_wide_product():
+    """The oracle's GEMM on one OpenMP thread (what a launcher that pins
+    OMP_NUM_THREADS to 1 gives the CPU arms) over a product whose rows of
+    double accumulators would not fit a thread's stack many times over:
+    finite and equal to numpy, and the thread count restored after."""
+    from oracle import ops as orc
+    rng = np.random.default_rng(3)
+    M, N, K = 3072, 4096, 3
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    C = np.zeros((M, N), np.float32)
+    old = orc.set_threads(0)
+    try:
+        assert orc.set_threads(1) == 1
+        orc.gemm(A, B, C, M, N, K)
+    finally:
+        assert orc.set_threads(old) == old
+    ref = A.astype(np.float64) @ B.astype(np.float64)
+    assert np.all(np.isfinite(C))
+    assert np.max(np.abs(C - ref)) <= 1e-6 * np.max(np.abs(ref))
