@@ -134,9 +134,12 @@ def test_bench_reference_arm_prints_once_under_torchrun():
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(ROOT / "bench.py"),
            "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0", "--config", "mlp"]
-    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="2")
+    # torchrun's own setting: one OpenMP thread per rank; the CPU arm must
+    # still run the oracle on every host core
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
     out = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
     lines = [json.loads(x) for x in out.stdout.splitlines() if x.startswith("{")]
     assert len(lines) == 1
     assert lines[0]["impl"] == "reference" and lines[0]["n_gpus"] == 2 and lines[0]["value"] > 0
+    assert lines[0]["cpu_baseline"]["cores"] == (os.cpu_count() or 1)
